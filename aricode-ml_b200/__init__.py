@@ -9,6 +9,6 @@ import sys as _sys
 
 _sys.modules.setdefault("aricode_ml_b200", _sys.modules[__name__])
 
-from . import arch, blob, pack  # noqa: E402,F401
+from . import arch, blob, pack, runtime, synth  # noqa: E402,F401
 
-__all__ = ["arch", "blob", "pack"]
+__all__ = ["arch", "blob", "pack", "runtime", "synth"]

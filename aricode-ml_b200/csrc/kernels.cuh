@@ -1,0 +1,378 @@
+// kernels.cuh — small kernels of the decode path and the launch helpers shared by
+// the runtime (runtime.cu) and the kernel-level C ABI (capi.cu).
+#pragma once
+#include <cuda_runtime.h>
+
+#include "attn.cuh"
+#include "b2_common.cuh"
+#include "gemv.cuh"
+
+namespace b2 {
+
+// ------------------------------------------------------------------ embedding
+// Token selection + embedding row for one decode step (aricode_pack.py:2205-2284):
+// tok = prompt[t] while t < prompt_len, else the previous step's argmax;
+// x = f32(q[tok]) * scale[tok] (+ learned position row t).
+struct EmbedParams {
+    const void* emb;        // [vocab][ld] int8 or f32
+    int emb_i8;
+    const float* emb_s;     // per-row scales (int8)
+    long long ld;
+    const float* pos_tab;   // [max_pos][d] or nullptr
+    int max_pos;
+    int d, vocab, max_seq;
+    const int* prompt;      // device prompt ids
+    StepState* st;
+    float* x;               // residual stream [d]
+};
+
+static __global__ void embed_kernel(const __grid_constant__ EmbedParams p) {
+    __shared__ int s_tok, s_pos, s_ok;
+    pdl_launch_dependents();
+    pdl_wait();
+    if (threadIdx.x == 0) {
+        StepState* st = p.st;
+        int ok = 0;
+        if (st->active) {
+            const int t = st->step;
+            if (t >= p.max_seq || (p.pos_tab && t >= p.max_pos)) {
+                atomicCAS(&st->err, 0, (int)B2_DEV_ERR_KV_OVERFLOW);
+                st->active = 0;
+            } else {
+                const int tok = t < st->prompt_len ? p.prompt[t] : st->next_tok;
+                if (tok < 0 || tok >= p.vocab) {
+                    atomicCAS(&st->err, 0, (int)B2_DEV_ERR_BAD_TOKEN);
+                    st->active = 0;
+                } else {
+                    st->pos = t;
+                    st->step = t + 1;
+                    s_tok = tok;
+                    s_pos = t;
+                    ok = 1;
+                }
+            }
+        }
+        s_ok = ok;
+    }
+    __syncthreads();
+    if (!s_ok) return;
+    const int tok = s_tok, pos = s_pos;
+    for (int i = threadIdx.x; i < p.d; i += blockDim.x) {
+        float v;
+        if (p.emb_i8) {
+            const int8_t q = reinterpret_cast<const int8_t*>(p.emb)[(size_t)tok * p.ld + i];
+            v = fmul((float)q, p.emb_s[tok]);
+        } else {
+            v = reinterpret_cast<const float*>(p.emb)[(size_t)tok * p.ld + i];
+        }
+        if (p.pos_tab) v = fadd(v, p.pos_tab[(size_t)pos * p.d + i]);
+        p.x[i] = v;
+    }
+}
+
+// (re)start a decode sequence on the device without a host round trip
+static __global__ void set_state_kernel(StepState* st, int step, int prompt_len, int max_new,
+                                        int next_tok, int eos) {
+    pdl_wait();
+    st->step = step;
+    st->pos = step;
+    st->prompt_len = prompt_len;
+    st->max_new = max_new;
+    st->next_tok = next_tok;
+    st->n_out = 0;
+    st->active = 1;
+    st->eos = eos;
+    st->err = 0;
+}
+
+// ------------------------------------------------------------------ standalone ops
+// 256-thread block; same reduction pattern as the GEMV prologue / oracle reduce256
+__device__ __forceinline__ float block_reduce256(float part, float* red) {
+    const float w = butterfly32(part);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = w;
+    __syncthreads();
+    const float tot = fadd(fadd(fadd(red[0], red[1]), fadd(red[2], red[3])),
+                           fadd(fadd(red[4], red[5]), fadd(red[6], red[7])));
+    __syncthreads();
+    return tot;
+}
+
+static __global__ void __launch_bounds__(256) rmsnorm_kernel(const float* x, const float* g, float* y,
+                                                      int d, float eps) {
+    __shared__ float red[8];
+    float a = 0.0f;
+    for (int i = threadIdx.x; i < d; i += 256) a = ffma(x[i], x[i], a);
+    const float ms = fdiv(block_reduce256(a, red), (float)d);
+    const float inv = fdiv(1.0f, __fsqrt_rn(fadd(ms, eps)));
+    for (int i = threadIdx.x; i < d; i += 256) y[i] = fmul(fmul(x[i], inv), g[i]);
+}
+
+static __global__ void __launch_bounds__(256) layernorm_kernel(const float* x, const float* g,
+                                                        const float* b, float* y, int d,
+                                                        float eps) {
+    __shared__ float red[8];
+    float a = 0.0f;
+    for (int i = threadIdx.x; i < d; i += 256) a = fadd(a, x[i]);
+    const float mean = fdiv(block_reduce256(a, red), (float)d);
+    a = 0.0f;
+    for (int i = threadIdx.x; i < d; i += 256) { const float dx = fsub(x[i], mean); a = ffma(dx, dx, a); }
+    const float var = fdiv(block_reduce256(a, red), (float)d);
+    const float inv = fdiv(1.0f, __fsqrt_rn(fadd(var, eps)));
+    for (int i = threadIdx.x; i < d; i += 256) {
+        const float t = fmul(fsub(x[i], mean), inv);
+        y[i] = (float)dadd(dmul((double)t, (double)g[i]), (double)b[i]);
+    }
+}
+
+static __global__ void rope_kernel(float* v, const float* table, int pos, int dh, int n_pairs) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n_pairs) return;
+    const int vec = i / (dh / 2), pr = i % (dh / 2);
+    float* pv = v + (size_t)vec * dh + 2 * pr;
+    const float c = table[(size_t)pos * dh + 2 * pr], s = table[(size_t)pos * dh + 2 * pr + 1];
+    const float x0 = pv[0], x1 = pv[1];
+    pv[0] = fsub(fmul(x0, c), fmul(x1, s));
+    pv[1] = fadd(fmul(x0, s), fmul(x1, c));
+}
+
+static __global__ void __launch_bounds__(1024) argmax_kernel(const float* v, long long n, int* out) {
+    __shared__ float sv[32];
+    __shared__ int si[32], sh[32];
+    float bv = 0.0f; int bi = 0x7fffffff; bool have = false;
+    for (long long i = threadIdx.x; i < n; i += blockDim.x) {
+        const float x = v[i];
+        if (!have || amax_better(x, (int)i, bv, bi)) { bv = x; bi = (int)i; have = true; }
+    }
+    for (int s = 16; s >= 1; s >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, s);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, s);
+        const int oh = __shfl_xor_sync(0xffffffffu, (int)have, s);
+        if (oh && (!have || amax_better(ov, oi, bv, bi))) { bv = ov; bi = oi; have = true; }
+    }
+    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) { sv[w] = bv; si[w] = bi; sh[w] = have; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float cv = 0.0f; int ci = 0; bool ch = false;
+        for (int k = 0; k < (int)(blockDim.x >> 5); ++k)
+            if (sh[k] && (!ch || amax_better(sv[k], si[k], cv, ci))) { cv = sv[k]; ci = si[k]; ch = true; }
+        const float v0 = v[0];
+        out[0] = (v0 != v0 || !ch) ? 0 : ci;
+    }
+}
+
+static __global__ void silu_mul_kernel(const float* g, const float* u, float* h, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) h[i] = fmul(silu_f(g[i]), u[i]);
+}
+
+static __global__ void gelu_kernel(const float* x, float* y, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) y[i] = gelu_f(x[i]);
+}
+
+// per-row int8 quantiser, numpy float32 semantics (aricode_pack.py:3356-3379): warp per row
+static __global__ void quantize_rows_kernel(const float* W, long long m, long long n, int8_t* q,
+                                     long long ldq, float* scale) {
+    const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= m) return;
+    const float* w = W + row * n;
+    float mx = 0.0f;
+    for (long long c = lane; c < n; c += 32) mx = fmaxf(mx, fabsf(w[c]));
+    for (int s = 16; s >= 1; s >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, s));
+    const float sc = fdiv(mx, 127.0f);
+    const float safe = sc > 0.0f ? sc : 1.0f;
+    int8_t* qr = q + row * ldq;
+    for (long long c = lane; c < ldq; c += 32) {
+        if (c < n) {
+            float v = rintf(fdiv(w[c], safe));
+            v = fminf(fmaxf(v, -128.0f), 127.0f);
+            qr[c] = (int8_t)(int)v;
+        } else {
+            qr[c] = 0;
+        }
+    }
+    if (lane == 0) scale[row] = sc;
+}
+
+// synthetic weights: splitmix64 key -> four 16-bit uniforms -> centred sum * std/std_sum
+// (identical to oracle b2o_synth_value)
+__device__ __forceinline__ float synth_value(unsigned long long seed, unsigned long long tid,
+                                             unsigned long long idx, float stdv) {
+    unsigned long long z = seed * 0xD1B54A32D192ED03ull + tid * 0xA0761D6478BD642Full + idx;
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    z = z ^ (z >> 31);
+    const int s = (int)(z & 0xFFFF) + (int)((z >> 16) & 0xFFFF) + (int)((z >> 32) & 0xFFFF) +
+                  (int)(z >> 48) - 131070;
+    const float c = fmul(stdv, 0x1.bb67aep-16f);
+    return fmul((float)s, c);
+}
+
+static __global__ void synth_quant_kernel(unsigned long long seed, unsigned long long tid, long long n,
+                                   float stdv, long long r0, long long r1, long long c0,
+                                   long long c1, int8_t* q, long long ldq, float* scale) {
+    const long long row = r0 + (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= r1) return;
+    float mx = 0.0f;
+    for (long long c = lane; c < n; c += 32)
+        mx = fmaxf(mx, fabsf(synth_value(seed, tid, (unsigned long long)(row * n + c), stdv)));
+    for (int s = 16; s >= 1; s >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, s));
+    const float sc = fdiv(mx, 127.0f);
+    const float safe = sc > 0.0f ? sc : 1.0f;
+    int8_t* qr = q + (row - r0) * ldq;
+    const long long w = c1 - c0;
+    for (long long c = lane; c < ldq; c += 32) {
+        if (c < w) {
+            float v = rintf(fdiv(synth_value(seed, tid, (unsigned long long)(row * n + c0 + c), stdv), safe));
+            v = fminf(fmaxf(v, -128.0f), 127.0f);
+            qr[c] = (int8_t)(int)v;
+        } else {
+            qr[c] = 0;
+        }
+    }
+    if (lane == 0) scale[row - r0] = sc;
+}
+
+static __global__ void synth_fill_kernel(unsigned long long seed, unsigned long long tid, long long m,
+                                  long long n, long long ld, float stdv, float* out) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= m * ld) return;
+    const long long r = i / ld, c = i % ld;
+    out[i] = c < n ? synth_value(seed, tid, (unsigned long long)(r * n + c), stdv) : 0.0f;
+}
+
+static __global__ void fill_kernel(float* out, long long n, float v) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = v;
+}
+
+// ------------------------------------------------------------------ launch helpers
+inline cudaLaunchAttribute pdl_attr(bool pdl) {
+    cudaLaunchAttribute a;
+    a.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    a.val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    return a;
+}
+
+template <typename K, typename P>
+inline cudaError_t launch_ex(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                             bool pdl, const P& params) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1] = {pdl_attr(pdl)};
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, params);
+}
+
+constexpr size_t kGemvSmemBudget = 110 * 1024;
+constexpr size_t kGemvStageTarget = 16 * 1024;
+
+struct GemvShape {
+    int R;
+    bool paired;
+    int grid;
+    int nstages;
+    size_t smem;
+};
+
+template <int R>
+inline long long host_total_groups(const GemvParams& p) {
+    long long t = 0;
+    const int nseg = p.paired ? 1 : p.nseg;
+    for (int s = 0; s < nseg; ++s) t += (p.rows[s] + R - 1) / R;
+    return t;
+}
+
+inline long long host_groups(const GemvParams& p, int R) {
+    long long t = 0;
+    const int nseg = p.paired ? 1 : p.nseg;
+    for (int s = 0; s < nseg; ++s) t += (p.rows[s] + R - 1) / R;
+    return t;
+}
+
+// rows per group: largest power of two <= 8 keeping a stage near 16 KB
+inline GemvShape gemv_shape(const GemvParams& p, int esz, int min_r, int grid_cap) {
+    GemvShape sh{};
+    sh.paired = p.paired != 0;
+    const size_t row_bytes = (size_t)p.ld * esz * (sh.paired ? 2 : 1);
+    int R = 8;
+    while (R > min_r && (size_t)R * row_bytes > kGemvStageTarget) R >>= 1;
+    if (sh.paired && R > 4) R = 4;
+    sh.R = R;
+    const long long G = host_groups(p, R);
+    sh.grid = (int)(G < grid_cap ? G : grid_cap);
+    if (sh.grid < 1) sh.grid = 1;
+    const size_t stage = (size_t)R * row_bytes;
+    const size_t xs = ((size_t)p.ld * 4 + 127) & ~(size_t)127;
+    size_t budget = kGemvSmemBudget;
+    if (budget < 1024 + xs + 2 * stage) budget = 1024 + xs + 2 * stage;
+    long long ns = (long long)((budget - 1024 - xs) / stage);
+    const long long per_cta = (G + sh.grid - 1) / sh.grid;
+    if (ns > per_cta) ns = per_cta;
+    if (ns < 2) ns = 2;
+    if (ns > kGemvMaxStages) ns = kGemvMaxStages;
+    sh.nstages = (int)ns;
+    sh.smem = 1024 + xs + (size_t)ns * stage;
+    return sh;
+}
+
+template <typename WT, int R, bool PAIRED>
+inline cudaError_t launch_gemv_t(GemvParams p, const GemvShape& sh, cudaStream_t s, bool pdl) {
+    p.nstages = sh.nstages;
+    auto k = gemv_kernel<WT, R, PAIRED>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sh.smem);
+    if (e != cudaSuccess) return e;
+    return launch_ex(k, dim3(sh.grid), dim3(kGemvThreads), sh.smem, s, pdl, p);
+}
+
+// weights int8 (w_i8) or f32; returns the shape used through *out_shape
+inline cudaError_t launch_gemv(const GemvParams& p, bool w_i8, cudaStream_t s, bool pdl,
+                               int grid_cap, int min_r = 1, GemvShape* out_shape = nullptr) {
+    const GemvShape sh = gemv_shape(p, w_i8 ? 1 : 4, min_r, grid_cap);
+    if (out_shape) *out_shape = sh;
+    if (w_i8) {
+        if (sh.paired) {
+            switch (sh.R) {
+                case 1: return launch_gemv_t<int8_t, 1, true>(p, sh, s, pdl);
+                case 2: return launch_gemv_t<int8_t, 2, true>(p, sh, s, pdl);
+                default: return launch_gemv_t<int8_t, 4, true>(p, sh, s, pdl);
+            }
+        }
+        switch (sh.R) {
+            case 1: return launch_gemv_t<int8_t, 1, false>(p, sh, s, pdl);
+            case 2: return launch_gemv_t<int8_t, 2, false>(p, sh, s, pdl);
+            case 4: return launch_gemv_t<int8_t, 4, false>(p, sh, s, pdl);
+            default: return launch_gemv_t<int8_t, 8, false>(p, sh, s, pdl);
+        }
+    }
+    if (sh.paired) return cudaErrorInvalidValue;
+    switch (sh.R) {
+        case 1: return launch_gemv_t<float, 1, false>(p, sh, s, pdl);
+        case 2: return launch_gemv_t<float, 2, false>(p, sh, s, pdl);
+        case 4: return launch_gemv_t<float, 4, false>(p, sh, s, pdl);
+        default: return launch_gemv_t<float, 8, false>(p, sh, s, pdl);
+    }
+}
+
+inline cudaError_t launch_attn(const AttnParams& p, cudaStream_t s, bool pdl) {
+    const int G = p.H / p.KVH;
+    const size_t smem = attn_smem_bytes(G, p.dh, p.nsplit_max);
+    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+    return launch_ex(attn_decode_kernel, dim3(p.nsplit_max, p.KVH), dim3(kAttnThreads), smem, s, pdl, p);
+}
+
+inline cudaError_t launch_embed(const EmbedParams& p, cudaStream_t s, bool pdl) {
+    return launch_ex(embed_kernel, dim3(1), dim3(256), 0, s, pdl, p);
+}
+
+}  // namespace b2

@@ -1,0 +1,968 @@
+// runtime.cu — model context, blob loader, launch plan, CUDA-graph decode loop and
+// the C ABI of include/b2dec.h.
+//
+// One context = one model on one device. Weights live in one arena (one H2D copy
+// of the blob's data region), the KV cache in another, activations and scratch in
+// a third. The per-token step (embedding, every sub-block, LM head) is captured
+// once into two CUDA graphs — with and without the LM head — whose kernels are
+// chained by programmatic dependent launch. The decode state (position, next
+// token, generated ids, EOS/limit flag, error word) lives on the device, so a
+// whole generation is a sequence of graph launches with no host round trips.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <functional>
+#include <map>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/b2dec.h"
+#include "json.h"
+#include "kernels.cuh"
+
+using namespace b2;
+
+namespace {
+
+thread_local std::string g_last_create_error;
+
+struct DevMat {
+    const void* w = nullptr;
+    const float* s = nullptr;
+    int rows = 0, cols = 0;
+    int ld = 0;
+    bool i8 = false;
+};
+
+struct NormRef {
+    int kind = NORM_RMS;
+    const float* g = nullptr;
+    const float* b = nullptr;
+};
+
+struct Block {
+    bool attn = false;
+    NormRef norm;
+    // attention
+    bool rope = false;
+    int H = 0, KVH = 0, dh = 0;
+    DevMat q, k, v, o;
+    const float* bias[4] = {nullptr, nullptr, nullptr, nullptr};
+    float* K = nullptr;
+    float* V = nullptr;
+    // feed-forward
+    bool swiglu = false;
+    int d_ffn = 0;
+    DevMat w1, w3, w2;
+    const float* b1 = nullptr;
+    const float* b2 = nullptr;
+};
+
+struct TensorInfo {
+    int dtype = 0;          // 1 int8, 2 f32
+    long long rows = 0, cols = 0, ld = 0;
+    size_t off = 0, nbytes = 0;
+    bool two_d = false;
+};
+
+uint64_t fnv1a64(const std::string& s) {
+    uint64_t h = 0xcbf29ce484222325ull;
+    for (unsigned char c : s) { h ^= c; h *= 0x100000001b3ull; }
+    return h;
+}
+
+// blob checksum (same as blob.checksum in Python)
+uint64_t checksum_words(const unsigned char* p, size_t n, uint64_t first_word) {
+    uint64_t tot = 0;
+    const size_t nw = n / 8;
+    for (size_t i = 0; i < nw; ++i) {
+        uint64_t w;
+        std::memcpy(&w, p + 8 * i, 8);
+        tot += (w ^ ((first_word + i) * 0x9E3779B97F4A7C15ull)) * 0xBF58476D1CE4E5B9ull;
+    }
+    if (n % 8) {
+        uint64_t w = 0;
+        std::memcpy(&w, p + 8 * nw, n % 8);
+        tot += (w ^ ((first_word + nw) * 0x9E3779B97F4A7C15ull)) * 0xBF58476D1CE4E5B9ull;
+    }
+    return tot;
+}
+
+struct Err : std::runtime_error {
+    int code;
+    Err(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+#define CK(expr)                                                                              \
+    do {                                                                                      \
+        cudaError_t _e = (expr);                                                              \
+        if (_e != cudaSuccess)                                                                \
+            throw Err(B2_E_CUDA, std::string(#expr) + ": " + cudaGetErrorString(_e));         \
+    } while (0)
+
+}  // namespace
+
+struct b2_ctx {
+    int device = 0;
+    int sm_count = 148;
+    cudaStream_t stream = nullptr;
+    bool own_stream = false;
+    std::string err;
+
+    int vocab = 0, d = 0, max_seq = 0, max_pos = 0, token_bytes = 4;
+    float eps = 1e-5f;
+    DevMat emb;
+    const float* pos_tab = nullptr;
+    NormRef fnorm;
+    DevMat lm;
+    const float* lm_b = nullptr;
+    std::vector<Block> blocks;
+    int rope_dh = 0;
+    double rope_theta = 0.0;
+
+    void* d_weights = nullptr;
+    size_t weight_bytes = 0;
+    std::map<std::string, TensorInfo> tensors;
+    void* d_kv = nullptr;
+    size_t kv_bytes = 0, kv_bytes_per_pos = 0;
+    void* d_work = nullptr;
+    size_t work_bytes = 0;
+
+    float* rope_tab = nullptr;
+    float* x = nullptr;
+    float* q = nullptr;
+    float* att = nullptr;
+    float* f = nullptr;
+    float* logits = nullptr;
+    float* attn_part = nullptr;
+    unsigned* attn_cnt = nullptr;
+    int attn_nsplit_max = 1;
+    float* amax_val = nullptr;
+    int* amax_idx = nullptr;
+    int* amax_v0nan = nullptr;
+    unsigned* amax_cnt = nullptr;
+    StepState* st = nullptr;
+    int* prompt = nullptr;
+    int* out_ids = nullptr;
+    StepState* h_st = nullptr;     // pinned mirror
+
+    cudaGraphExec_t g_prefill = nullptr, g_decode = nullptr;
+    int kernels_prefill = 0, kernels_decode = 0;
+    bool pdl = true;               // programmatic dependent launch between kernels
+    int host_step = 0;
+
+    ~b2_ctx() {
+        if (device >= 0) cudaSetDevice(device);
+        if (g_prefill) cudaGraphExecDestroy(g_prefill);
+        if (g_decode) cudaGraphExecDestroy(g_decode);
+        if (d_weights) cudaFree(d_weights);
+        if (d_kv) cudaFree(d_kv);
+        if (d_work) cudaFree(d_work);
+        if (h_st) cudaFreeHost(h_st);
+        if (own_stream && stream) cudaStreamDestroy(stream);
+    }
+
+    // ------------------------------------------------------------ tensors
+    const TensorInfo& tinfo(const std::string& name) const {
+        auto it = tensors.find(name);
+        if (it == tensors.end()) throw Err(B2_E_FORMAT, "blob has no tensor '" + name + "'");
+        return it->second;
+    }
+    const float* vec(const b2json::Value& v, long long expect) const {
+        if (v.is_null()) return nullptr;
+        const TensorInfo& t = tinfo(v.as_str());
+        if (t.dtype != 2 || t.two_d || t.cols != expect)
+            throw Err(B2_E_FORMAT, "tensor '" + v.str + "' must be f32 [" + std::to_string(expect) + "]");
+        return reinterpret_cast<const float*>(static_cast<char*>(d_weights) + t.off);
+    }
+    DevMat mat(const std::string& name, long long rows, long long cols) const {
+        const TensorInfo& t = tinfo(name);
+        if (!t.two_d || t.rows != rows || t.cols != cols)
+            throw Err(B2_E_FORMAT, "tensor '" + name + "' must be [" + std::to_string(rows) + ", " +
+                                       std::to_string(cols) + "]");
+        DevMat m;
+        m.w = static_cast<char*>(d_weights) + t.off;
+        m.rows = (int)rows;
+        m.cols = (int)cols;
+        m.ld = (int)t.ld;
+        m.i8 = t.dtype == 1;
+        if (m.i8) {
+            if (t.ld % 16) throw Err(B2_E_FORMAT, "int8 tensor '" + name + "' row stride not 16-aligned");
+            b2json::Value sname;
+            sname.kind = b2json::Value::String;
+            sname.str = name + "_scales";
+            m.s = vec(sname, rows);
+        } else if (t.ld % 4) {
+            throw Err(B2_E_FORMAT, "f32 tensor '" + name + "' row stride not 4-aligned");
+        }
+        if ((reinterpret_cast<uintptr_t>(m.w) & 15) != 0)
+            throw Err(B2_E_FORMAT, "tensor '" + name + "' not 16-byte aligned");
+        return m;
+    }
+    NormRef norm_of(const b2json::Value& n) const {
+        NormRef r;
+        const std::string& kind = n["kind"].as_str("norm.kind");
+        if (kind == "rms") r.kind = NORM_RMS;
+        else if (kind == "ln") r.kind = NORM_LN;
+        else throw Err(B2_E_FORMAT, "unknown norm kind " + kind);
+        r.g = vec(n["g"], d);
+        if (r.kind == NORM_LN) r.b = vec(n["b"], d);
+        return r;
+    }
+};
+
+namespace {
+
+// ------------------------------------------------------------------ plan -> tensor shapes
+struct Need {
+    std::string name;
+    int dtype;            // 1 int8 (+ _scales), 2 f32
+    long long rows, cols; // cols = 0: 1-D of length rows
+    int init;             // synthetic: 0 random, 1 ones, 2 zeros
+};
+
+std::vector<Need> plan_needs(const b2json::Value& plan) {
+    std::vector<Need> out;
+    const long long d = plan["d_model"].as_int("d_model"), vocab = plan["vocab"].as_int("vocab");
+    auto norm = [&](const b2json::Value& n) {
+        out.push_back({n["g"].as_str(), 2, d, 0, 1});
+        if (n["kind"].as_str() == "ln") out.push_back({n["b"].as_str(), 2, d, 0, 2});
+    };
+    out.push_back({plan["embedding"].as_str(), 1, vocab, d, 0});
+    if (plan.has("pos_embedding"))
+        out.push_back({plan["pos_embedding"].as_str(), 2, plan["max_pos"].as_int(), d, 0});
+    const b2json::Value& blocks = plan["blocks"];
+    for (size_t i = 0; i < blocks.size(); ++i) {
+        const b2json::Value& b = blocks[i];
+        norm(b["norm"]);
+        if (b["type"].as_str() == "attn") {
+            const long long H = b["n_heads"].as_int(), KVH = b["n_kv_heads"].as_int(),
+                            dh = b["d_head"].as_int();
+            const int dt = b["dtype"].as_str() == "i8" ? 1 : 2;
+            out.push_back({b["q"].as_str(), dt, H * dh, d, 0});
+            out.push_back({b["k"].as_str(), dt, KVH * dh, d, 0});
+            out.push_back({b["v"].as_str(), dt, KVH * dh, d, 0});
+            out.push_back({b["o"].as_str(), dt, d, H * dh, 0});
+            if (b.has("bias")) {
+                const b2json::Value& bs = b["bias"];
+                out.push_back({bs["q"].as_str(), 2, H * dh, 0, 0});
+                out.push_back({bs["k"].as_str(), 2, KVH * dh, 0, 0});
+                out.push_back({bs["v"].as_str(), 2, KVH * dh, 0, 0});
+                out.push_back({bs["o"].as_str(), 2, d, 0, 0});
+            }
+        } else if (b["kind"].as_str() == "swiglu") {
+            const long long ffn = b["d_ffn"].as_int();
+            out.push_back({b["gate"].as_str(), 1, ffn, d, 0});
+            out.push_back({b["up"].as_str(), 1, ffn, d, 0});
+            out.push_back({b["down"].as_str(), 1, d, ffn, 0});
+        } else {
+            const long long ffn = b["d_ffn"].as_int();
+            out.push_back({b["fc1"].as_str(), 1, ffn, d, 0});
+            out.push_back({b["fc1_b"].as_str(), 2, ffn, 0, 0});
+            out.push_back({b["fc2"].as_str(), 1, d, ffn, 0});
+            out.push_back({b["fc2_b"].as_str(), 2, d, 0, 0});
+        }
+    }
+    norm(plan["final_norm"]);
+    out.push_back({plan["lm_head"]["W"].as_str(), 1, vocab, d, 0});
+    out.push_back({plan["lm_head"]["b"].as_str(), 2, vocab, 0, 2});
+    return out;
+}
+
+long long pad_ld(long long cols, int dtype) { return dtype == 1 ? (cols + 15) / 16 * 16 : (cols + 3) / 4 * 4; }
+
+// ------------------------------------------------------------------ model assembly
+void setup_device(b2_ctx* c, int device) {
+    int ndev = 0;
+    CK(cudaGetDeviceCount(&ndev));
+    if (device < 0 || device >= ndev) throw Err(B2_E_INVALID, "device index out of range");
+    c->device = device;
+    CK(cudaSetDevice(device));
+    cudaDeviceProp prop;
+    CK(cudaGetDeviceProperties(&prop, device));
+    if (prop.major < 10) throw Err(B2_E_UNSUPPORTED, "this library is built for sm_100a (B200)");
+    c->sm_count = prop.multiProcessorCount;
+    CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+    c->own_stream = true;
+}
+
+void assemble(b2_ctx* c, const b2json::Value& plan) {
+    if (plan["format"].is_null() || plan["format"].as_str() != "b200-decode-plan")
+        throw Err(B2_E_FORMAT, "not a b200 decode plan");
+    c->vocab = (int)plan["vocab"].as_int();
+    c->d = (int)plan["d_model"].as_int();
+    c->max_seq = (int)plan["max_seq"].as_int();
+    c->token_bytes = plan.has("token_bytes") ? (int)plan["token_bytes"].as_int() : 4;
+    c->eps = plan.has("eps") ? (float)plan["eps"].as_num() : 1e-5f;
+    c->max_pos = plan.has("max_pos") ? (int)plan["max_pos"].as_int() : 0;
+    if (c->d <= 0 || c->vocab <= 0 || c->max_seq <= 0) throw Err(B2_E_FORMAT, "bad plan dimensions");
+    c->emb = c->mat(plan["embedding"].as_str(), c->vocab, c->d);
+    if (plan.has("pos_embedding")) {
+        c->pos_tab = static_cast<const float*>(c->mat(plan["pos_embedding"].as_str(), c->max_pos, c->d).w);
+        if (c->mat(plan["pos_embedding"].as_str(), c->max_pos, c->d).ld != c->d)
+            throw Err(B2_E_FORMAT, "positional embedding rows must be unpadded");
+    }
+    const b2json::Value& blocks = plan["blocks"];
+    size_t kv_total = 0;
+    for (size_t i = 0; i < blocks.size(); ++i) {
+        const b2json::Value& b = blocks[i];
+        Block B;
+        B.norm = c->norm_of(b["norm"]);
+        if (b["type"].as_str() == "attn") {
+            B.attn = true;
+            B.rope = b["rope"].as_bool();
+            B.H = (int)b["n_heads"].as_int();
+            B.KVH = (int)b["n_kv_heads"].as_int();
+            B.dh = (int)b["d_head"].as_int();
+            if (B.H <= 0 || B.KVH <= 0 || B.H % B.KVH || B.dh <= 0 || B.dh > 256)
+                throw Err(B2_E_UNSUPPORTED, "attention heads/head_dim not supported");
+            if (B.rope && (B.dh % 2)) throw Err(B2_E_FORMAT, "RoPE needs an even head_dim");
+            const int qd = B.H * B.dh, kd = B.KVH * B.dh;
+            B.q = c->mat(b["q"].as_str(), qd, c->d);
+            B.k = c->mat(b["k"].as_str(), kd, c->d);
+            B.v = c->mat(b["v"].as_str(), kd, c->d);
+            B.o = c->mat(b["o"].as_str(), c->d, qd);
+            if (B.q.i8 != B.k.i8 || B.q.i8 != B.v.i8 || B.q.i8 != B.o.i8)
+                throw Err(B2_E_FORMAT, "attention projections must share one dtype");
+            if (b.has("bias")) {
+                const b2json::Value& bs = b["bias"];
+                B.bias[0] = c->vec(bs["q"], qd);
+                B.bias[1] = c->vec(bs["k"], kd);
+                B.bias[2] = c->vec(bs["v"], kd);
+                B.bias[3] = c->vec(bs["o"], c->d);
+            }
+            if (B.rope) {
+                const double th = b["theta"].as_num("theta");
+                if (c->rope_dh && (c->rope_dh != B.dh || c->rope_theta != th))
+                    throw Err(B2_E_UNSUPPORTED, "RoPE sub-blocks must share head_dim and theta");
+                c->rope_dh = B.dh;
+                c->rope_theta = th;
+            }
+            kv_total += 2ull * B.KVH * c->max_seq * B.dh;
+        } else {
+            B.d_ffn = (int)b["d_ffn"].as_int();
+            if (b["kind"].as_str() == "swiglu") {
+                B.swiglu = true;
+                B.w1 = c->mat(b["gate"].as_str(), B.d_ffn, c->d);
+                B.w3 = c->mat(b["up"].as_str(), B.d_ffn, c->d);
+                B.w2 = c->mat(b["down"].as_str(), c->d, B.d_ffn);
+                if (!B.w1.i8 || !B.w3.i8 || !B.w2.i8)
+                    throw Err(B2_E_UNSUPPORTED, "swiglu_ffn weights must be int8 (--quantize int8)");
+            } else {
+                B.w1 = c->mat(b["fc1"].as_str(), B.d_ffn, c->d);
+                B.w2 = c->mat(b["fc2"].as_str(), c->d, B.d_ffn);
+                B.b1 = c->vec(b["fc1_b"], B.d_ffn);
+                B.b2 = c->vec(b["fc2_b"], c->d);
+                if (!B.w1.i8 || !B.w2.i8)
+                    throw Err(B2_E_UNSUPPORTED, "linear weights must be int8 (--quantize int8)");
+            }
+        }
+        c->blocks.push_back(B);
+    }
+    c->fnorm = c->norm_of(plan["final_norm"]);
+    c->lm = c->mat(plan["lm_head"]["W"].as_str(), c->vocab, c->d);
+    c->lm_b = c->vec(plan["lm_head"]["b"], c->vocab);
+    if (!c->lm.i8 || !c->emb.i8) throw Err(B2_E_UNSUPPORTED, "embedding and LM head must be int8");
+
+    // ---- KV cache arena
+    c->kv_bytes = kv_total * sizeof(float);
+    c->kv_bytes_per_pos = c->kv_bytes / (size_t)c->max_seq;
+    if (c->kv_bytes) {
+        if (cudaMalloc(&c->d_kv, c->kv_bytes) != cudaSuccess) throw Err(B2_E_OOM, "KV cache allocation failed");
+        CK(cudaMemsetAsync(c->d_kv, 0, c->kv_bytes, c->stream));
+    }
+    float* kvp = static_cast<float*>(c->d_kv);
+    for (Block& B : c->blocks) {
+        if (!B.attn) continue;
+        const size_t e = (size_t)B.KVH * c->max_seq * B.dh;
+        B.K = kvp; kvp += e;
+        B.V = kvp; kvp += e;
+    }
+
+    // ---- activations + scratch arena
+    int max_q = 1, max_ffn = 1, max_H = 1, max_KVH = 1, max_dh = 1;
+    for (const Block& B : c->blocks) {
+        if (B.attn) {
+            max_q = std::max(max_q, B.H * B.dh);
+            max_H = std::max(max_H, B.H);
+            max_KVH = std::max(max_KVH, B.KVH);
+            max_dh = std::max(max_dh, B.dh);
+        } else {
+            max_ffn = std::max(max_ffn, B.d_ffn);
+        }
+    }
+    c->attn_nsplit_max = (c->max_seq + kAttnChunk - 1) / kAttnChunk;
+    std::vector<std::pair<void**, size_t>> plan_mem;
+    auto al = [](size_t n) { return (n + 255) & ~(size_t)255; };
+    size_t off = 0;
+    std::vector<size_t> offs;
+    auto add = [&](size_t bytes) { offs.push_back(off); off += al(bytes); return offs.size() - 1; };
+    const size_t i_rope = add(c->rope_dh ? (size_t)c->max_seq * c->rope_dh * 4 : 16);
+    const size_t i_x = add((size_t)c->d * 4);
+    const size_t i_q = add((size_t)max_q * 4);
+    const size_t i_att = add((size_t)max_q * 4);
+    const size_t i_f = add((size_t)max_ffn * 4);
+    const size_t i_logits = add((size_t)c->vocab * 4);
+    const size_t i_part = add((size_t)max_H * c->attn_nsplit_max * (max_dh + 2) * 4);
+    const size_t i_acnt = add((size_t)max_KVH * 4);
+    const size_t i_aval = add((size_t)c->sm_count * 4);
+    const size_t i_aidx = add((size_t)c->sm_count * 4);
+    const size_t i_anan = add(4);
+    const size_t i_amcnt = add(4);
+    const size_t i_st = add(sizeof(StepState));
+    const size_t i_prompt = add((size_t)c->max_seq * 4);
+    const size_t i_out = add((size_t)c->max_seq * 4);
+    c->work_bytes = off;
+    if (cudaMalloc(&c->d_work, c->work_bytes) != cudaSuccess) throw Err(B2_E_OOM, "workspace allocation failed");
+    CK(cudaMemsetAsync(c->d_work, 0, c->work_bytes, c->stream));
+    char* w = static_cast<char*>(c->d_work);
+    c->rope_tab = reinterpret_cast<float*>(w + offs[i_rope]);
+    c->x = reinterpret_cast<float*>(w + offs[i_x]);
+    c->q = reinterpret_cast<float*>(w + offs[i_q]);
+    c->att = reinterpret_cast<float*>(w + offs[i_att]);
+    c->f = reinterpret_cast<float*>(w + offs[i_f]);
+    c->logits = reinterpret_cast<float*>(w + offs[i_logits]);
+    c->attn_part = reinterpret_cast<float*>(w + offs[i_part]);
+    c->attn_cnt = reinterpret_cast<unsigned*>(w + offs[i_acnt]);
+    c->amax_val = reinterpret_cast<float*>(w + offs[i_aval]);
+    c->amax_idx = reinterpret_cast<int*>(w + offs[i_aidx]);
+    c->amax_v0nan = reinterpret_cast<int*>(w + offs[i_anan]);
+    c->amax_cnt = reinterpret_cast<unsigned*>(w + offs[i_amcnt]);
+    c->st = reinterpret_cast<StepState*>(w + offs[i_st]);
+    c->prompt = reinterpret_cast<int*>(w + offs[i_prompt]);
+    c->out_ids = reinterpret_cast<int*>(w + offs[i_out]);
+
+    // RoPE table in f64 via libm, stored f32 (rope_alloc_f32, rope_f32.ari:34-55)
+    if (c->rope_dh) {
+        std::vector<float> tab((size_t)c->max_seq * c->rope_dh);
+        const double log_theta = std::log(c->rope_theta);
+        const int half = c->rope_dh / 2;
+        for (int pos = 0; pos < c->max_seq; ++pos)
+            for (int i = 0; i < half; ++i) {
+                const double exponent = 0.0 - 2.0 * (double)i / (double)c->rope_dh;
+                const double freq = std::exp(exponent * log_theta);
+                const double angle = (double)pos * freq;
+                tab[(size_t)pos * c->rope_dh + 2 * i] = (float)std::cos(angle);
+                tab[(size_t)pos * c->rope_dh + 2 * i + 1] = (float)std::sin(angle);
+            }
+        CK(cudaMemcpyAsync(c->rope_tab, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice, c->stream));
+        CK(cudaStreamSynchronize(c->stream));
+    }
+    CK(cudaMallocHost(&c->h_st, sizeof(StepState)));
+    std::memset(c->h_st, 0, sizeof(StepState));
+}
+
+// ------------------------------------------------------------------ one step's launches
+int enqueue_step(b2_ctx* c, bool with_head, cudaStream_t s) {
+    int n = 0;
+    const bool pdl = c->pdl;
+    EmbedParams ep{};
+    ep.emb = c->emb.w; ep.emb_i8 = c->emb.i8; ep.emb_s = c->emb.s; ep.ld = c->emb.ld;
+    ep.pos_tab = c->pos_tab; ep.max_pos = c->max_pos;
+    ep.d = c->d; ep.vocab = c->vocab; ep.max_seq = c->max_seq;
+    ep.prompt = c->prompt; ep.st = c->st; ep.x = c->x;
+    CK(launch_embed(ep, s, pdl)); ++n;
+
+    for (const Block& B : c->blocks) {
+        GemvParams p{};
+        p.st = c->st;
+        p.err = &c->st->err;
+        p.eps = c->eps;
+        p.norm = B.norm.kind;
+        p.ng = B.norm.g;
+        p.nb = B.norm.b;
+        p.x = c->x;
+        p.n = c->d;
+        if (B.attn) {
+            // Q/K/V projections + RoPE + scale + KV append
+            p.W[0] = B.q.w; p.W[1] = B.k.w; p.W[2] = B.v.w;
+            p.S[0] = B.q.s; p.S[1] = B.k.s; p.S[2] = B.v.s;
+            p.bias[0] = B.bias[0]; p.bias[1] = B.bias[1]; p.bias[2] = B.bias[2];
+            p.rows[0] = B.q.rows; p.rows[1] = B.k.rows; p.rows[2] = B.v.rows;
+            p.nseg = 3; p.ld = B.q.ld;
+            p.epi = EPI_QKV;
+            p.rope = B.rope;
+            p.rope_tab = c->rope_tab;
+            p.dh = B.dh;
+            p.qscale = (float)(1.0 / std::sqrt((double)B.dh));
+            p.qout = c->q;
+            p.kcache = B.K; p.vcache = B.V;
+            p.max_seq = c->max_seq;
+            CK(launch_gemv(p, B.q.i8, s, pdl, c->sm_count, B.rope ? 2 : 1)); ++n;
+
+            AttnParams a{};
+            a.q = c->q; a.K = B.K; a.V = B.V; a.out = c->att;
+            a.part = c->attn_part; a.counters = c->attn_cnt;
+            a.H = B.H; a.KVH = B.KVH; a.dh = B.dh; a.max_seq = c->max_seq;
+            a.nsplit_max = c->attn_nsplit_max;
+            a.st = c->st; a.err = &c->st->err;
+            CK(launch_attn(a, s, pdl)); ++n;
+
+            GemvParams o{};
+            o.st = c->st; o.err = &c->st->err;
+            o.W[0] = B.o.w; o.S[0] = B.o.s; o.bias[0] = B.bias[3];
+            o.rows[0] = B.o.rows; o.nseg = 1; o.ld = B.o.ld;
+            o.x = c->att; o.n = B.o.cols; o.norm = NORM_NONE;
+            o.epi = EPI_RESID; o.y = c->x; o.resid = c->x;
+            CK(launch_gemv(o, B.o.i8, s, pdl, c->sm_count)); ++n;
+        } else if (B.swiglu) {
+            p.W[0] = B.w1.w; p.W[1] = B.w3.w;
+            p.S[0] = B.w1.s; p.S[1] = B.w3.s;
+            p.rows[0] = B.d_ffn; p.rows[1] = B.d_ffn;
+            p.nseg = 2; p.paired = 1; p.ld = B.w1.ld;
+            p.epi = EPI_SWIGLU; p.y = c->f;
+            CK(launch_gemv(p, true, s, pdl, c->sm_count)); ++n;
+
+            GemvParams dn{};
+            dn.st = c->st; dn.err = &c->st->err;
+            dn.W[0] = B.w2.w; dn.S[0] = B.w2.s;
+            dn.rows[0] = c->d; dn.nseg = 1; dn.ld = B.w2.ld;
+            dn.x = c->f; dn.n = B.d_ffn; dn.norm = NORM_NONE;
+            dn.epi = EPI_RESID; dn.y = c->x; dn.resid = c->x;
+            CK(launch_gemv(dn, true, s, pdl, c->sm_count)); ++n;
+        } else {
+            p.W[0] = B.w1.w; p.S[0] = B.w1.s; p.bias[0] = B.b1;
+            p.rows[0] = B.d_ffn; p.nseg = 1; p.ld = B.w1.ld;
+            p.epi = EPI_GELU; p.y = c->f;
+            CK(launch_gemv(p, true, s, pdl, c->sm_count)); ++n;
+
+            GemvParams f2{};
+            f2.st = c->st; f2.err = &c->st->err;
+            f2.W[0] = B.w2.w; f2.S[0] = B.w2.s; f2.bias[0] = B.b2;
+            f2.rows[0] = c->d; f2.nseg = 1; f2.ld = B.w2.ld;
+            f2.x = c->f; f2.n = B.d_ffn; f2.norm = NORM_NONE;
+            f2.epi = EPI_RESID; f2.y = c->x; f2.resid = c->x;
+            CK(launch_gemv(f2, true, s, pdl, c->sm_count)); ++n;
+        }
+    }
+    if (with_head) {
+        GemvParams h{};
+        h.st = c->st; h.err = &c->st->err;
+        h.W[0] = c->lm.w; h.S[0] = c->lm.s; h.bias[0] = c->lm_b;
+        h.rows[0] = c->vocab; h.nseg = 1; h.ld = c->lm.ld;
+        h.x = c->x; h.n = c->d;
+        h.norm = c->fnorm.kind; h.ng = c->fnorm.g; h.nb = c->fnorm.b; h.eps = c->eps;
+        h.epi = EPI_ARGMAX; h.y = c->logits;
+        h.amax_val = c->amax_val; h.amax_idx = c->amax_idx; h.amax_v0nan = c->amax_v0nan;
+        h.amax_count = c->amax_cnt; h.out_ids = c->out_ids;
+        CK(launch_gemv(h, true, s, pdl, c->sm_count)); ++n;
+    }
+    return n;
+}
+
+void capture_graphs_once(b2_ctx* c);
+
+void capture_graphs(b2_ctx* c) {
+    const char* env = std::getenv("B2_NO_PDL");
+    c->pdl = !(env && env[0] == '1');
+    try {
+        capture_graphs_once(c);
+    } catch (const Err&) {
+        if (!c->pdl) throw;
+        cudaGetLastError();            // clear, then capture without PDL edges
+        c->pdl = false;
+        capture_graphs_once(c);
+    }
+}
+
+void capture_graphs_once(b2_ctx* c) {
+    if (c->g_prefill) { cudaGraphExecDestroy(c->g_prefill); c->g_prefill = nullptr; }
+    if (c->g_decode) { cudaGraphExecDestroy(c->g_decode); c->g_decode = nullptr; }
+    for (int head = 0; head < 2; ++head) {
+        cudaGraph_t g = nullptr;
+        CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+        int n = 0;
+        try {
+            n = enqueue_step(c, head == 1, c->stream);
+        } catch (...) {
+            cudaStreamEndCapture(c->stream, &g);
+            if (g) cudaGraphDestroy(g);
+            throw;
+        }
+        CK(cudaStreamEndCapture(c->stream, &g));
+        cudaGraphExec_t ex = nullptr;
+        const cudaError_t e = cudaGraphInstantiate(&ex, g, 0);
+        cudaGraphDestroy(g);
+        CK(e);
+        if (head) { c->g_decode = ex; c->kernels_decode = n; }
+        else { c->g_prefill = ex; c->kernels_prefill = n; }
+    }
+}
+
+void upload_state(b2_ctx* c, int step, int prompt_len, int max_new, int next_tok, int eos) {
+    StepState& h = *c->h_st;
+    std::memset(&h, 0, sizeof(h));
+    h.step = step;
+    h.pos = step;
+    h.prompt_len = prompt_len;
+    h.max_new = max_new;
+    h.next_tok = next_tok;
+    h.n_out = 0;
+    h.active = 1;
+    h.eos = eos;
+    h.err = 0;
+    CK(cudaMemcpyAsync(c->st, c->h_st, sizeof(StepState), cudaMemcpyHostToDevice, c->stream));
+}
+
+int fetch_state(b2_ctx* c) {
+    CK(cudaMemcpyAsync(c->h_st, c->st, sizeof(StepState), cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    c->host_step = c->h_st->step;
+    if (c->h_st->err == B2_DEV_ERR_KV_OVERFLOW) throw Err(B2_E_KV_OVERFLOW, "KV cache overflow on the device");
+    if (c->h_st->err == B2_DEV_ERR_BAD_TOKEN) throw Err(B2_E_INVALID, "token id outside the vocabulary");
+    if (c->h_st->err) throw Err(B2_E_DEVICE, "device wait timed out (error word " +
+                                                 std::to_string(c->h_st->err) + ")");
+    return B2_OK;
+}
+
+void load_blob(b2_ctx* c, const char* path, std::string* embedded_plan) {
+    FILE* f = std::fopen(path, "rb");
+    if (!f) throw Err(B2_E_IO, std::string("cannot open blob ") + path);
+    struct Closer { FILE* f; ~Closer() { std::fclose(f); } } closer{f};
+    unsigned char hdr[64];
+    if (std::fread(hdr, 1, 64, f) != 64 || std::memcmp(hdr, "B2DBLOB1", 8) != 0)
+        throw Err(B2_E_FORMAT, "not a b200 decode blob");
+    uint32_t ver, ntens, plan_len;
+    uint64_t table_off, data_off, data_bytes, csum, plan_off;
+    std::memcpy(&ver, hdr + 8, 4);
+    std::memcpy(&ntens, hdr + 12, 4);
+    std::memcpy(&table_off, hdr + 16, 8);
+    std::memcpy(&data_off, hdr + 24, 8);
+    std::memcpy(&data_bytes, hdr + 32, 8);
+    std::memcpy(&csum, hdr + 40, 8);
+    std::memcpy(&plan_len, hdr + 48, 4);
+    std::memcpy(&plan_off, hdr + 56, 8);
+    if (ver != 1) throw Err(B2_E_FORMAT, "unsupported blob version");
+    std::vector<unsigned char> table((size_t)ntens * 128);
+    if (std::fseek(f, (long)table_off, SEEK_SET) || std::fread(table.data(), 1, table.size(), f) != table.size())
+        throw Err(B2_E_FORMAT, "truncated tensor table");
+    embedded_plan->resize(plan_len);
+    if (std::fseek(f, (long)plan_off, SEEK_SET) ||
+        std::fread(&(*embedded_plan)[0], 1, plan_len, f) != plan_len)
+        throw Err(B2_E_FORMAT, "truncated plan");
+    for (uint32_t i = 0; i < ntens; ++i) {
+        const unsigned char* e = table.data() + 128 * (size_t)i;
+        char name[65] = {0};
+        std::memcpy(name, e, 64);
+        TensorInfo t;
+        uint32_t dtype, ndim;
+        uint64_t s0, s1, ld, off, nb;
+        std::memcpy(&dtype, e + 64, 4);
+        std::memcpy(&ndim, e + 68, 4);
+        std::memcpy(&s0, e + 72, 8);
+        std::memcpy(&s1, e + 80, 8);
+        std::memcpy(&ld, e + 88, 8);
+        std::memcpy(&off, e + 96, 8);
+        std::memcpy(&nb, e + 104, 8);
+        t.dtype = (int)dtype;
+        t.two_d = ndim == 2;
+        t.rows = (long long)(t.two_d ? s0 : 1);
+        t.cols = (long long)(t.two_d ? s1 : s0);
+        t.ld = (long long)ld;
+        t.off = (size_t)off;
+        t.nbytes = (size_t)nb;
+        if ((dtype != 1 && dtype != 2) || off + nb > data_bytes)
+            throw Err(B2_E_FORMAT, std::string("bad table entry for ") + name);
+        c->tensors[name] = t;
+    }
+    if (cudaMalloc(&c->d_weights, data_bytes) != cudaSuccess) throw Err(B2_E_OOM, "weight allocation failed");
+    c->weight_bytes = data_bytes;
+    // stream the data region through two pinned buffers; checksum on the host as it passes
+    const size_t chunk = 64ull << 20;
+    unsigned char* pin[2] = {nullptr, nullptr};
+    CK(cudaMallocHost(&pin[0], chunk));
+    CK(cudaMallocHost(&pin[1], chunk));
+    struct PinFree { unsigned char** p; ~PinFree() { cudaFreeHost(p[0]); cudaFreeHost(p[1]); } } pf{pin};
+    cudaEvent_t ev[2];
+    CK(cudaEventCreateWithFlags(&ev[0], cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&ev[1], cudaEventDisableTiming));
+    struct EvFree { cudaEvent_t* e; ~EvFree() { cudaEventDestroy(e[0]); cudaEventDestroy(e[1]); } } ef{ev};
+    if (std::fseek(f, (long)data_off, SEEK_SET)) throw Err(B2_E_FORMAT, "truncated data region");
+    uint64_t sum = 0;
+    size_t done = 0;
+    int k = 0;
+    bool used[2] = {false, false};
+    while (done < data_bytes) {
+        const size_t n = std::min(chunk, (size_t)data_bytes - done);
+        if (used[k]) CK(cudaEventSynchronize(ev[k]));
+        if (std::fread(pin[k], 1, n, f) != n) throw Err(B2_E_FORMAT, "truncated data region");
+        sum += checksum_words(pin[k], n, done / 8);
+        CK(cudaMemcpyAsync(static_cast<char*>(c->d_weights) + done, pin[k], n, cudaMemcpyHostToDevice, c->stream));
+        CK(cudaEventRecord(ev[k], c->stream));
+        used[k] = true;
+        done += n;
+        k ^= 1;
+    }
+    CK(cudaStreamSynchronize(c->stream));
+    if (sum != csum) throw Err(B2_E_FORMAT, "blob checksum mismatch");
+}
+
+void synth_weights(b2_ctx* c, const b2json::Value& plan, uint64_t seed, float stdv) {
+    std::vector<Need> needs = plan_needs(plan);
+    size_t off = 0;
+    auto al = [](size_t n) { return (n + 255) & ~(size_t)255; };
+    for (const Need& nd : needs) {
+        if (c->tensors.count(nd.name)) continue;
+        TensorInfo t;
+        t.dtype = nd.dtype;
+        t.two_d = nd.cols > 0;
+        t.rows = t.two_d ? nd.rows : 1;
+        t.cols = t.two_d ? nd.cols : nd.rows;
+        t.ld = t.two_d ? pad_ld(nd.cols, nd.dtype) : t.cols;
+        t.nbytes = (size_t)t.rows * t.ld * (nd.dtype == 1 ? 1 : 4);
+        t.off = off;
+        off = al(off + t.nbytes);
+        c->tensors[nd.name] = t;
+        if (nd.dtype == 1) {
+            TensorInfo s;
+            s.dtype = 2; s.two_d = false; s.rows = 1; s.cols = nd.rows; s.ld = nd.rows;
+            s.nbytes = (size_t)nd.rows * 4;
+            s.off = off;
+            off = al(off + s.nbytes);
+            c->tensors[nd.name + "_scales"] = s;
+        }
+    }
+    if (cudaMalloc(&c->d_weights, off) != cudaSuccess) throw Err(B2_E_OOM, "weight allocation failed");
+    c->weight_bytes = off;
+    char* base = static_cast<char*>(c->d_weights);
+    for (const Need& nd : needs) {
+        const TensorInfo& t = c->tensors[nd.name];
+        const uint64_t tid = fnv1a64(nd.name);
+        if (nd.dtype == 1) {
+            const TensorInfo& s = c->tensors[nd.name + "_scales"];
+            const long long rows = t.rows;
+            synth_quant_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, c->stream>>>(
+                seed, tid, t.cols, stdv, 0, rows, 0, t.cols, reinterpret_cast<int8_t*>(base + t.off), t.ld,
+                reinterpret_cast<float*>(base + s.off));
+        } else if (nd.init == 0) {
+            const long long tot = t.rows * t.ld;
+            synth_fill_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, c->stream>>>(
+                seed, tid, t.rows, t.cols, t.ld, stdv, reinterpret_cast<float*>(base + t.off));
+        } else {
+            const long long tot = t.rows * t.ld;
+            fill_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, c->stream>>>(
+                reinterpret_cast<float*>(base + t.off), tot, nd.init == 1 ? 1.0f : 0.0f);
+        }
+        CK(cudaGetLastError());
+    }
+    CK(cudaStreamSynchronize(c->stream));
+}
+
+int fail(b2_ctx* c, const Err& e) {
+    if (c) c->err = e.what();
+    else g_last_create_error = e.what();
+    return e.code;
+}
+
+template <typename F>
+int guarded(b2_ctx* c, F&& f) {
+    if (!c) return B2_E_INVALID;
+    try {
+        cudaSetDevice(c->device);
+        return f();
+    } catch (const Err& e) {
+        return fail(c, e);
+    } catch (const std::exception& e) {
+        c->err = e.what();
+        return B2_E_FORMAT;
+    }
+}
+
+int create_common(b2_ctx** out, int device, const std::function<void(b2_ctx*)>& body) {
+    if (!out) return B2_E_INVALID;
+    *out = nullptr;
+    auto c = std::make_unique<b2_ctx>();
+    c->device = -1;
+    try {
+        setup_device(c.get(), device);
+        body(c.get());
+        capture_graphs(c.get());
+        upload_state(c.get(), 0, 0, 0, 0, -1);
+        CK(cudaStreamSynchronize(c->stream));
+    } catch (const Err& e) {
+        g_last_create_error = e.what();
+        return e.code;
+    } catch (const std::exception& e) {
+        g_last_create_error = e.what();
+        return B2_E_FORMAT;
+    }
+    *out = c.release();
+    return B2_OK;
+}
+
+}  // namespace
+
+// ===================================================================== C ABI
+extern "C" {
+
+int b2_create(const char* blob_path, const char* plan_json, int device, b2_ctx** out) {
+    if (!blob_path) return B2_E_INVALID;
+    return create_common(out, device, [&](b2_ctx* c) {
+        std::string embedded;
+        load_blob(c, blob_path, &embedded);
+        const b2json::Value plan = b2json::parse(plan_json ? std::string(plan_json) : embedded);
+        assemble(c, plan);
+    });
+}
+
+int b2_create_synthetic(const char* plan_json, uint64_t seed, float stdv, int device, b2_ctx** out) {
+    if (!plan_json) return B2_E_INVALID;
+    return create_common(out, device, [&](b2_ctx* c) {
+        const b2json::Value plan = b2json::parse(plan_json);
+        synth_weights(c, plan, seed, stdv);
+        assemble(c, plan);
+    });
+}
+
+int b2_destroy(b2_ctx* ctx) {
+    if (!ctx) return B2_E_INVALID;
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    delete ctx;
+    return B2_OK;
+}
+
+int b2_reset(b2_ctx* ctx) {
+    return guarded(ctx, [&] {
+        upload_state(ctx, 0, 0, 0, 0, -1);
+        CK(cudaStreamSynchronize(ctx->stream));
+        ctx->host_step = 0;
+        return B2_OK;
+    });
+}
+
+int b2_step(b2_ctx* ctx, const int32_t* tok, int n_seq, int32_t* next_tok, float* logits) {
+    return guarded(ctx, [&] {
+        if (!tok || n_seq != 1) return n_seq == 1 ? B2_E_INVALID : B2_E_UNSUPPORTED;
+        if (ctx->host_step >= ctx->max_seq) throw Err(B2_E_KV_OVERFLOW, "position reached max_seq");
+        if (tok[0] < 0 || tok[0] >= ctx->vocab) throw Err(B2_E_INVALID, "token id outside the vocabulary");
+        const int t = ctx->host_step;
+        CK(cudaMemcpyAsync(ctx->prompt + t, tok, 4, cudaMemcpyHostToDevice, ctx->stream));
+        upload_state(ctx, t, t + 1, 1 << 30, 0, -1);
+        CK(cudaGraphLaunch(ctx->g_decode, ctx->stream));
+        if (logits)
+            CK(cudaMemcpyAsync(logits, ctx->logits, (size_t)ctx->vocab * 4, cudaMemcpyDeviceToHost, ctx->stream));
+        fetch_state(ctx);
+        if (next_tok) next_tok[0] = ctx->h_st->next_tok;
+        return B2_OK;
+    });
+}
+
+int b2_prefill(b2_ctx* ctx, const int32_t* toks, int n) {
+    return guarded(ctx, [&] {
+        if (n < 0 || (n > 0 && !toks)) return B2_E_INVALID;
+        if (ctx->host_step + n > ctx->max_seq) throw Err(B2_E_KV_OVERFLOW, "prefill passes max_seq");
+        for (int i = 0; i < n; ++i)
+            if (toks[i] < 0 || toks[i] >= ctx->vocab) throw Err(B2_E_INVALID, "token id outside the vocabulary");
+        const int t = ctx->host_step;
+        if (n) CK(cudaMemcpyAsync(ctx->prompt + t, toks, (size_t)n * 4, cudaMemcpyHostToDevice, ctx->stream));
+        upload_state(ctx, t, t + n, 1 << 30, 0, -1);
+        for (int i = 0; i < n; ++i) CK(cudaGraphLaunch(ctx->g_prefill, ctx->stream));
+        fetch_state(ctx);
+        return B2_OK;
+    });
+}
+
+int b2_generate(b2_ctx* ctx, const int32_t* prompt, int n_prompt, int max_new, int32_t eos,
+                int32_t* out_ids, int* n_out) {
+    return guarded(ctx, [&] {
+        if (n_out) *n_out = 0;
+        if (!prompt || n_prompt <= 0 || max_new < 0 || (max_new > 0 && !out_ids)) return B2_E_INVALID;
+        if (max_new == 0) return B2_OK;
+        for (int i = 0; i < n_prompt; ++i)
+            if (prompt[i] < 0 || prompt[i] >= ctx->vocab) throw Err(B2_E_INVALID, "token id outside the vocabulary");
+        const int np = std::min(n_prompt, ctx->max_seq);
+        CK(cudaMemcpyAsync(ctx->prompt, prompt, (size_t)np * 4, cudaMemcpyHostToDevice, ctx->stream));
+        upload_state(ctx, 0, n_prompt, max_new, 0, eos);
+        const long long total = (long long)n_prompt + max_new - 1;
+        const int steps = (int)std::min<long long>(total, ctx->max_seq);
+        for (int t = 0; t < steps; ++t)
+            CK(cudaGraphLaunch(t < n_prompt - 1 ? ctx->g_prefill : ctx->g_decode, ctx->stream));
+        CK(cudaMemcpyAsync(out_ids, ctx->out_ids, (size_t)max_new * 4, cudaMemcpyDeviceToHost, ctx->stream));
+        fetch_state(ctx);
+        if (n_out) *n_out = ctx->h_st->n_out;
+        if (total > ctx->max_seq) throw Err(B2_E_KV_OVERFLOW, "generation passes max_seq");
+        return B2_OK;
+    });
+}
+
+int b2_set_position(b2_ctx* ctx, int pos, int32_t next_tok) {
+    return guarded(ctx, [&] {
+        if (pos < 0 || pos > ctx->max_seq || next_tok < 0 || next_tok >= ctx->vocab) return B2_E_INVALID;
+        // enqueued on the stream (no host synchronisation): one tiny kernel
+        set_state_kernel<<<1, 1, 0, ctx->stream>>>(ctx->st, pos, pos, 1 << 30, next_tok, -1);
+        CK(cudaGetLastError());
+        ctx->host_step = pos;
+        return B2_OK;
+    });
+}
+
+int b2_decode_async(b2_ctx* ctx, int n_steps) {
+    return guarded(ctx, [&] {
+        if (n_steps < 0) return B2_E_INVALID;
+        if (ctx->host_step + n_steps > ctx->max_seq) throw Err(B2_E_KV_OVERFLOW, "decode passes max_seq");
+        for (int i = 0; i < n_steps; ++i) CK(cudaGraphLaunch(ctx->g_decode, ctx->stream));
+        ctx->host_step += n_steps;
+        return B2_OK;
+    });
+}
+
+int b2_sync(b2_ctx* ctx) {
+    return guarded(ctx, [&] { return fetch_state(ctx); });
+}
+
+int b2_read_output(b2_ctx* ctx, int32_t* ids, int max_ids, int* n_ids) {
+    return guarded(ctx, [&] {
+        fetch_state(ctx);
+        const int n = std::min(max_ids, ctx->h_st->n_out);
+        if (n > 0) {
+            CK(cudaMemcpyAsync(ids, ctx->out_ids, (size_t)n * 4, cudaMemcpyDeviceToHost, ctx->stream));
+            CK(cudaStreamSynchronize(ctx->stream));
+        }
+        if (n_ids) *n_ids = n;
+        return B2_OK;
+    });
+}
+
+int b2_set_stream(b2_ctx* ctx, void* stream) {
+    return guarded(ctx, [&] {
+        CK(cudaStreamSynchronize(ctx->stream));
+        if (ctx->own_stream) CK(cudaStreamDestroy(ctx->stream));
+        ctx->stream = static_cast<cudaStream_t>(stream);
+        ctx->own_stream = false;
+        capture_graphs(ctx);
+        return B2_OK;
+    });
+}
+
+int b2_query(b2_ctx* ctx, const char* key, double* value) {
+    if (!ctx || !key || !value) return B2_E_INVALID;
+    const std::string k(key);
+    if (k == "weight_bytes") *value = (double)ctx->weight_bytes;
+    else if (k == "kv_bytes_per_pos") *value = (double)ctx->kv_bytes_per_pos;
+    else if (k == "kernels_per_step") *value = ctx->kernels_decode;
+    else if (k == "kernels_per_prefill_step") *value = ctx->kernels_prefill;
+    else if (k == "max_seq") *value = ctx->max_seq;
+    else if (k == "vocab") *value = ctx->vocab;
+    else if (k == "position") *value = ctx->host_step;
+    else if (k == "n_out") *value = ctx->h_st->n_out;
+    else if (k == "device_err") *value = ctx->h_st->err;
+    else if (k == "sm_count") *value = ctx->sm_count;
+    else if (k == "pdl") *value = ctx->pdl ? 1 : 0;
+    else return B2_E_INVALID;
+    return B2_OK;
+}
+
+int b2_last_error(b2_ctx* ctx, char* buf, int len) {
+    if (!buf || len <= 0) return B2_E_INVALID;
+    const std::string& m = ctx ? ctx->err : g_last_create_error;
+    std::snprintf(buf, (size_t)len, "%s", m.c_str());
+    return B2_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,332 @@
+#!/usr/bin/env python3
+"""Decode benchmark: Llama-2-7B-shaped int8 model, prompt 512 + 256 greedy tokens, batch 1.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+One step = decoding the 256 new tokens after the 512-token prompt (positions
+512..767) with every input already in HBM; the KV cache of the prompt is filled
+once before timing and every step rewinds to position 512, so all steps do the
+same work. value = generated tokens per second over all GPUs (N independent
+replicas when N > 1). e2e = the same metric through the public C ABI call
+b2_generate (prompt from pinned host memory, prefill + decode, ids back to
+pinned host memory). The roofline object is the int8 GEMV timed alone on the
+model's FFN shape. `--impl reference` times the CPU restatement of the
+reference decode path (oracle/) on the host cores.
+
+Weights: random N(0, 0.02)-like synthetic weights of the Llama-2-7B architecture
+(counter-based generator, identical on GPU and host); prompt ids uniform random.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "Llama-2-7B int8 decode tok/s (b=1) at 1/2/4/8 B200; i8 GEMV % HBM peak"
+CONFIG = "llama2-7b"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    p.add_argument("--config", default=CONFIG)
+    p.add_argument("--layers", type=int, default=None, help="(testing only) fewer layers")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=15.0)
+    return p.parse_args()
+
+
+def env_rank():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)),
+            int(os.environ.get("WORLD_SIZE", 1)))
+
+
+def measured_peaks():
+    try:
+        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text()), "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region (median SM clock, throttle reasons)."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu)], stdout=self.tmp, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.tmp.flush()
+        rows = []
+        for line in open(self.tmp.name).read().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.tmp.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return None
+        sm = [num(r[1]) for r in rows if num(r[1])]
+        reasons = set()
+        for r in rows:
+            for name, v in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
+                                "sw_power_cap"), r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": num(rows[0][2]), "power_w_max": max(num(r[3]) or 0 for r in rows),
+                "samples": len(rows), "reasons": sorted(reasons)}
+
+
+def cpu_baseline(pkg, plan, seconds, threads=None):
+    """The oracle (CPU restatement of the reference decode path) on the host cores:
+    decode steps at positions 512.. over a synthetic KV prefix, as many as fit in
+    `seconds` (at least 2)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle as O
+    threads = threads or os.cpu_count() or 1
+    O.set_threads(threads)
+    t0 = time.time()
+    om = O.OracleModel(plan, O.synth_tensors(plan, seed=0), threads=threads)
+    setup_s = time.time() - t0
+    P = pkg.synth.CONFIGS[CONFIG]["prompt"] if plan["max_seq"] > 512 else plan["max_seq"] // 2
+    om.fill_kv(P, seed=1)
+    tok = 1
+    n = 0
+    t0 = time.time()
+    while n < 2 or (time.time() - t0 < seconds and om.count < plan["max_seq"]):
+        tok, _ = om.step(tok)
+        n += 1
+    dt = time.time() - t0
+    return {"value": n / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{n} greedy decode tokens at positions {P}..{P + n - 1} of the same "
+                      f"synthetic model (KV prefix synthetic), {threads} host threads; "
+                      f"weight generation {setup_s:.1f} s untimed"}
+
+
+def run_reference(args):
+    rank, _, world = env_rank()
+    if rank != 0:
+        return 0
+    pkg = importlib.import_module("aricode-ml_b200")
+    plan = pkg.synth.config_plan(args.config, n_layers=args.layers)
+    cb = cpu_baseline(pkg, plan, seconds=max(args.cpu_seconds, 10.0))
+    line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tokens/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000.0 * 256 / cb["value"], "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": workload_config(args, plan),
+            "cpu_baseline": cb,
+            "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def workload_config(args, plan):
+    c = pkg_configs()[args.config]
+    return {"workload": f"{args.config} int8 (per-row scales) decode, prompt {c['prompt']} + "
+                        f"{c['new']} greedy tokens, batch 1",
+            "layers": plan["n_layers"], "d_model": plan["d_model"], "vocab": plan["vocab"],
+            "prompt_tokens": c["prompt"], "decode_tokens": c["new"], "batch": 1,
+            "parallelism": "replicas" if args.gpus > 1 else "single",
+            "l2": "weights (6.6 GB) exceed L2 (126 MB); no flush needed"}
+
+
+def pkg_configs():
+    return importlib.import_module("aricode-ml_b200").synth.CONFIGS
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    import numpy as np
+    import torch
+    rank, local_rank, world = env_rank()
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    pkg = importlib.import_module("aricode-ml_b200")
+    rt = pkg.runtime
+    c = pkg.synth.CONFIGS[args.config]
+    plan = pkg.synth.config_plan(args.config, n_layers=args.layers)
+    P, NEW = c["prompt"], c["new"]
+
+    dec = rt.Decoder.synthetic(plan, seed=0, device=local_rank)
+    stream = torch.cuda.current_stream()
+    dec.set_stream(stream.cuda_stream)
+    prompt = np.random.default_rng(1).integers(0, plan["vocab"], P).astype(np.int32)
+
+    # prefill once (untimed), remember the first generated token
+    dec.reset()
+    t0 = time.time()
+    dec.prefill(prompt[:-1].tolist())
+    first, _ = dec.step(int(prompt[-1]))
+    prefill_s = time.time() - t0
+
+    def one_step():
+        dec.set_position(P, first)
+        dec.decode_async(NEW - 1)
+
+    for _ in range(args.warmup):
+        one_step()
+    torch.cuda.synchronize()
+    ids_warm = dec.read_output(NEW)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = Clocks(local_rank)
+    clocks.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        one_step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    if dist:
+        dist.barrier()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    ids = dec.read_output(NEW)
+    assert ids == ids_warm, "decode is not deterministic across steps"
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    toks = NEW - 1
+    value = world * toks / (ms / 1000.0)
+    kps = int(dec.query("kernels_per_step"))
+    launches = args.steps * (toks * kps + 1)
+
+    # ---- whole-step roofline: algorithmic bytes per token / time per token
+    peaks, peak_kind = measured_peaks()
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    bytes_tok = sum(pkg.synth.bytes_per_token(plan, P + i) for i in range(1, NEW)) / toks
+    step_gbs = bytes_tok / (ms / 1000.0 / toks) / 1e9
+
+    # ---- dominant kernel: int8 GEMV on the FFN shape, one launch per layer's weights
+    gemv = time_gemv(torch, rt, plan, stream)
+
+    # ---- e2e through b2_generate with pinned host buffers
+    e2e = time_e2e(torch, dec, prompt, NEW, stream, world)
+
+    out = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": workload_config(args, plan),
+        "roofline": {"bound": "hbm", "achieved": gemv["gbs"], "peak": hbm, "unit": "GB/s",
+                     "frac": gemv["gbs"] / hbm, "traffic": None,
+                     "kernel": gemv["kernel"], "bytes_per_launch": gemv["bytes"],
+                     "us_per_launch": gemv["us"], "peak_kind": f"{peak_kind} hbm_gbs"},
+        "step_roofline": {"bound": "hbm", "bytes_per_token": bytes_tok, "achieved": step_gbs,
+                          "peak": hbm, "unit": "GB/s", "frac": step_gbs / hbm},
+        "e2e": e2e, "gpu_launches": launches, "clocks": clk,
+        "decode_ms_per_token": ms / toks, "prefill_s_untimed": prefill_s,
+        "tokens_head": ids[:8],
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(pkg, plan, args.cpu_seconds)
+    dec.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    return 0
+
+
+def time_gemv(torch, rt, plan, stream, reps=3):
+    """int8 GEMV alone on the FFN gate shape [d_ffn, d_model], cycling over one
+    weight matrix per layer so every launch streams from HBM."""
+    blk = next(b for b in plan["blocks"] if b["type"] == "ffn")
+    m, n = blk["d_ffn"], plan["d_model"]
+    L = max(2, plan["n_layers"])
+    Ws = [torch.randint(-128, 128, (m, n), dtype=torch.int8, device="cuda") for _ in range(L)]
+    s = torch.rand(m, device="cuda") * 1e-3
+    x = torch.randn(n, device="cuda")
+    y = torch.empty(m, device="cuda")
+    for W in Ws:
+        rt.gemv_i8(W, s, x, y=y, stream=stream.cuda_stream)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        for W in Ws:
+            rt.gemv_i8(W, s, x, y=y, stream=stream.cuda_stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1000.0 / (reps * L)
+    nbytes = m * n + 4 * m + 4 * n + 4 * m
+    del Ws
+    return {"kernel": f"gemv_i8 {m}x{n}", "us": us, "bytes": nbytes, "gbs": nbytes / (us * 1e-6) / 1e9}
+
+
+def time_e2e(torch, dec, prompt, new, stream, world, reps=2):
+    import ctypes
+    import numpy as np
+    rt = importlib.import_module("aricode-ml_b200").runtime
+    P = len(prompt)
+    hp = torch.from_numpy(prompt).pin_memory()
+    ho = torch.empty(new, dtype=torch.int32).pin_memory()
+    p_ptr = ctypes.cast(hp.data_ptr(), ctypes.POINTER(ctypes.c_int32))
+    o_ptr = ctypes.cast(ho.data_ptr(), ctypes.POINTER(ctypes.c_int32))
+    n = ctypes.c_int(0)
+    rt.check(rt.lib().b2_generate(dec._ctx, p_ptr, P, new, -1, o_ptr, ctypes.byref(n)), dec._ctx)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(reps):
+        rt.check(rt.lib().b2_generate(dec._ctx, p_ptr, P, new, -1, o_ptr, ctypes.byref(n)),
+                 dec._ctx)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    return {"value": world * new / (ms / 1000.0), "unit": "tokens/s",
+            "h2d_bytes_per_step": 4 * P + 64, "d2h_bytes_per_step": 4 * new + 64,
+            "ms_per_generate": ms, "includes": "token-at-a-time prefill of the prompt"}
+
+
+if __name__ == "__main__":
+    sys.exit(main())

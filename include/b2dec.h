@@ -1,0 +1,169 @@
+/*
+ * b2dec.h — C ABI of the B200 decode library (libb2dec.so).
+ *
+ * Plain pointers and sizes only. Every function returns an int status (B2_OK or a
+ * negative B2_E_* code) and never aborts the process. The library is built for
+ * sm_100a; device pointers below are CUDA global-memory addresses on the device
+ * the call runs on, `stream` is a cudaStream_t (NULL = the legacy default stream).
+ *
+ * Reference = AriCodeLabs/aricode-ml. The reference has no native library of its
+ * own: its packer (tools/aricode_pack.py) emits `.ari` source whose decode loop
+ * calls builtins of the external `aric` compiler. The model-level calls below
+ * replace the packed binary's main() (gen_decoder_main, aricode_pack.py:2068-2344,
+ * driven by tools/run_decoder.py); the kernel-level calls replace the builtins and
+ * .ari step functions listed beside them.
+ */
+#ifndef B2DEC_H
+#define B2DEC_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    B2_OK = 0,
+    B2_E_INVALID = -1,      /* bad argument / shape */
+    B2_E_IO = -2,           /* blob file unreadable */
+    B2_E_FORMAT = -3,       /* blob or plan malformed, checksum mismatch */
+    B2_E_CUDA = -4,         /* CUDA runtime error (see b2_last_error) */
+    B2_E_OOM = -5,          /* device allocation failed */
+    B2_E_KV_OVERFLOW = -6,  /* position >= max_seq (reference: step returns -1) */
+    B2_E_UNSUPPORTED = -7,
+    B2_E_DEVICE = -8,       /* device-side error word set (timeout, bad token id) */
+    B2_E_COMM = -9          /* tensor-parallel exchange failed */
+};
+
+typedef struct b2_ctx b2_ctx;
+
+/* ---------------------------------------------------------------- model level */
+
+/* Load a packed model (<out>.b2blob from `python -m aricode-ml_b200.pack
+ * --target b200`) onto `device`: weights, KV cache and workspaces are allocated
+ * once; the per-token step is captured into CUDA graphs. plan_json NULL uses the
+ * plan embedded in the blob.
+ * Replaces: the packed binary's start-up — weight load gen_load
+ * (aricode_pack.py:1476-1611) and state allocation gen_scratch (:1222-1466). */
+int b2_create(const char* blob_path, const char* plan_json, int device, b2_ctx** out);
+
+/* Same, with weights synthesised on the device from (seed, std): int8 weights are
+ * drawn per tensor from a counter-based generator and quantised per row exactly
+ * like the packer; norm gains 1, norm/linear biases 0. No reference counterpart
+ * (the reference always packs a checkpoint); used for models too large to stage
+ * through a host checkpoint. */
+int b2_create_synthetic(const char* plan_json, uint64_t seed, float stdv, int device,
+                        b2_ctx** out);
+
+int b2_destroy(b2_ctx* ctx);
+
+/* Forget the sequence: position 0, no generated ids (KV contents need no zeroing:
+ * positions >= count are never read).
+ * Replaces: attn_gqa_kv_reset_i8 (attention_gqa_kv_i8.ari:82-92),
+ * attn_mh_kv_reset_f32 (attention_mh_kv_f32.ari:78-87). */
+int b2_reset(b2_ctx* ctx);
+
+/* One token through the model (n_seq must be 1): next_tok = greedy argmax of the
+ * logits; logits (vocab floats, host) optional. Returns B2_E_KV_OVERFLOW, writing
+ * nothing, when the position has reached max_seq.
+ * Replaces: one iteration of the decoder loop (aricode_pack.py:2203-2324). */
+int b2_step(b2_ctx* ctx, const int32_t* tok, int n_seq, int32_t* next_tok, float* logits);
+
+/* Feed n tokens without evaluating the LM head (results-equivalent to n steps;
+ * the reference evaluates and discards the head on every prompt token). */
+int b2_prefill(b2_ctx* ctx, const int32_t* toks, int n);
+
+/* Whole greedy generation from host buffers: total = n_prompt + max_new - 1 steps,
+ * ids emitted for t >= n_prompt - 1, stop before emitting `eos` (eos < 0: none).
+ * out_ids holds max_new entries. Returns B2_E_KV_OVERFLOW (with *n_out ids) when
+ * the steps would pass max_seq.
+ * Replaces: gen_decoder_main (aricode_pack.py:2068-2344) + run_decoder.py:62-151. */
+int b2_generate(b2_ctx* ctx, const int32_t* prompt, int n_prompt, int max_new, int32_t eos,
+                int32_t* out_ids, int* n_out);
+
+/* Device-resident decode loop pieces (no host round trips; for benchmarks and
+ * streaming hosts): rewind the position (KV rows < pos are kept; next_tok is the
+ * token fed at pos), then enqueue n decode steps whose argmax feeds the next
+ * step. Both only enqueue work on the context's stream. */
+int b2_set_position(b2_ctx* ctx, int pos, int32_t next_tok);
+int b2_decode_async(b2_ctx* ctx, int n_steps);
+int b2_sync(b2_ctx* ctx);
+int b2_read_output(b2_ctx* ctx, int32_t* ids, int max_ids, int* n_ids);
+
+/* Run the model's kernels on `stream` (cudaStream_t) instead of the private
+ * stream; graphs are re-captured. */
+int b2_set_stream(b2_ctx* ctx, void* stream);
+
+/* Numeric properties: "weight_bytes", "kv_bytes_per_pos", "kernels_per_step",
+ * "max_seq", "vocab", "position", "n_out", "device_err", "sm_count". */
+int b2_query(b2_ctx* ctx, const char* key, double* value);
+
+/* Last error message of ctx (or of the last failed create when ctx is NULL). */
+int b2_last_error(b2_ctx* ctx, char* buf, int len);
+
+/* ---------------------------------------------------------------- kernel level
+ * Device pointers in and out; nothing is allocated and nothing synchronises. */
+
+/* y[j] = scale[j] * sum_k W[j,k] x[k] (+ bias[j]), W int8 row-major with row
+ * stride ld (ld % 16 == 0, zero padding past n), f32 accumulation.
+ * Replaces: arr_i8_matvec_f32_perrow + arr_f32_add_scaled
+ * (aricode_pack.py:183-184; attention_gqa_kv_i8.ari:149-151, :191). */
+int b2_gemv_i8_rowscale(const int8_t* W, int64_t ld, const float* scale, const float* x,
+                        const float* bias, float* y, int m, int n, void* stream);
+
+/* y = W x + bias (bias NULL adds 0), W f32 with row stride ld (ld % 4 == 0).
+ * Replaces: arr_f32_matvec (attention_kv_f32.ari:122-140, attention_mh_kv_f32.ari:150). */
+int b2_gemv_f32(const float* W, int64_t ld, const float* x, const float* bias, float* y,
+                int m, int n, void* stream);
+
+/* Replaces: rmsnorm_affine_f32 (aricode_pack.py:585-607). */
+int b2_rmsnorm(const float* x, const float* g, float* y, int d, float eps, void* stream);
+
+/* Replaces: layernorm_affine_f32 (aricode_pack.py:503-521). */
+int b2_layernorm(const float* x, const float* g, const float* b, float* y, int d, float eps,
+                 void* stream);
+
+/* Rotate n_vec consecutive d_head-wide vectors in place with table row pos.
+ * Replaces: rope_apply_f32 / arr_f32_rope_apply_pairs (rope_f32.ari:69-72). */
+int b2_rope_apply(float* v, const float* table, int pos, int d_head, int n_vec, void* stream);
+
+/* Decode attention for one step: q [n_heads*d_head] (rotated, pre-scaled),
+ * K/V caches [n_kv_heads][max_seq][d_head], n valid keys, inactive tail = -60.
+ * workspace: b2_attn_decode_workspace() bytes of device memory, zero-filled
+ * before the first call (the kernel leaves it zero again).
+ * Replaces: _gqa_score_head_i8 (attention_gqa_kv_i8.ari:97-117) /
+ * the scoring half of attn_kv_step_f32 (attention_kv_f32.ari:134-162). */
+size_t b2_attn_decode_workspace(int n_heads, int n_kv_heads, int d_head, int max_seq);
+int b2_attn_decode(const float* q, const float* K, const float* V, float* out, int n_heads,
+                   int n_kv_heads, int d_head, int n, int max_seq, void* workspace,
+                   size_t workspace_bytes, void* stream);
+
+/* out[0] = first index of the maximum (NaN never wins; logits[0] NaN -> 0).
+ * Replaces: sample_greedy_f32 (sampling_f32.ari:10-24). */
+int b2_argmax(const float* v, int64_t n, int32_t* out, void* stream);
+
+/* h[i] = silu(g[i]) * u[i] (silu in f64, narrowed). Replaces: silu_mul_f32
+ * (aricode_pack.py:626-632). */
+int b2_silu_mul(const float* g, const float* u, float* h, int n, void* stream);
+
+/* y[i] = tanh-GELU(x[i]) in f64. Replaces: gelu_f32 (aricode_pack.py:539-572). */
+int b2_gelu(const float* x, float* y, int n, void* stream);
+
+/* Per-row symmetric int8: scale = max|row|/127, q = clip(rint(row/scale)).
+ * Replaces: the packer's per-row quantiser (aricode_pack.py:3356-3379). */
+int b2_quantize_rows(const float* W, int64_t m, int64_t n, int8_t* q, int64_t ldq,
+                     float* scale, void* stream);
+
+/* Synthetic weights: rows [r0,r1) x cols [c0,c1) of an m x n tensor quantised per
+ * FULL row. No reference counterpart (synthetic-checkpoint generator). */
+int b2_synth_quant_rows(uint64_t seed, uint64_t tensor_id, int64_t n, float stdv, int64_t r0,
+                        int64_t r1, int64_t c0, int64_t c1, int8_t* q, int64_t ldq,
+                        float* scale, void* stream);
+int b2_synth_fill_f32(uint64_t seed, uint64_t tensor_id, int64_t m, int64_t n, float stdv,
+                      float* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -106,6 +106,7 @@ def _declare(L):
     L.b2o_step.argtypes = [C.POINTER(Model), C.POINTER(State), C.c_int32, f32p, C.c_int]
     L.b2o_generate.restype = C.c_int
     L.b2o_generate.argtypes = [C.POINTER(Model), C.POINTER(State), i32p, C.c_int, C.c_int, i32p]
+    L.b2o_state_fill_kv.argtypes = [C.POINTER(Model), C.POINTER(State), C.c_int, C.c_uint64]
     L.b2o_set_threads.argtypes = [C.c_int]
     L.b2o_get_threads.restype = C.c_int
 
@@ -314,6 +315,10 @@ class OracleModel:
     def reset(self):
         lib().b2o_state_reset(C.byref(self.model), C.byref(self.state))
 
+    def fill_kv(self, count, seed=0):
+        """Synthetic KV rows [0, count) and position = count (benchmark sampling)."""
+        lib().b2o_state_fill_kv(C.byref(self.model), C.byref(self.state), int(count), int(seed))
+
     def step(self, tok, want_logits=True):
         """Returns (next_id, logits) — next_id -1 on KV overflow."""
         set_threads(self.threads)
@@ -331,3 +336,28 @@ class OracleModel:
         if n < 0:
             raise OverflowError("KV cache overflow" if n == -1 else "bad token id")
         return out[:n].tolist()
+
+
+def synth_tensors(plan, seed=0, stdv=0.02):
+    """Host copy of a synthetic model (same generator as b2_create_synthetic)."""
+    import importlib
+    import sys
+    root = str(HERE.parent)
+    if root not in sys.path:
+        sys.path.insert(0, root)
+    pkg = importlib.import_module("aricode-ml_b200")
+    from_name = pkg.runtime.fnv1a64
+    out = {}
+    for name, dt, shape, init in pkg.synth.tensor_specs(plan):
+        tid = from_name(name)
+        if dt == "i8":
+            q, s = synth_quant(seed, tid, shape[0], shape[1], stdv)
+            out[name] = q
+            out[name + "_scales"] = s
+        elif init == "rand":
+            m, n = (shape if len(shape) == 2 else (1, shape[0]))
+            a = synth_f32(seed, tid, m, n, stdv)
+            out[name] = a if len(shape) == 2 else a[0]
+        else:
+            out[name] = np.full(shape, 1.0 if init == "ones" else 0.0, np.float32)
+    return out

@@ -554,6 +554,22 @@ void b2o_state_reset(const b2o_model* m, b2o_state* s) {
     s->count = 0;
 }
 
+void b2o_state_fill_kv(const b2o_model* m, b2o_state* s, int count, uint64_t seed) {
+    if (count > m->max_seq) count = m->max_seq;
+    for (int b = 0; b < m->n_blocks; ++b) {
+        const b2o_block* B = &m->blocks[b];
+        if (B->type != B2O_SB_ATTN) continue;
+        for (int kh = 0; kh < B->n_kv_heads; ++kh)
+            for (int pos = 0; pos < count; ++pos)
+                for (int i = 0; i < B->d_head; ++i) {
+                    const int64_t at = ((int64_t)kh * m->max_seq + pos) * B->d_head + i;
+                    s->K[B->kv_slot][at] = b2o_synth_value(seed, 0xC0DE0000ull + 2 * b, (uint64_t)at, 1.0f);
+                    s->V[B->kv_slot][at] = b2o_synth_value(seed, 0xC0DE0001ull + 2 * b, (uint64_t)at, 1.0f);
+                }
+    }
+    s->count = count;
+}
+
 /* projection with the reference's bias rule: int8 weights add a bias only when
  * the op has one (emit_linear, aricode_pack.py:182-185); f32 weights always add
  * one (arr_f32_matvec takes W,x,b and the ops without a bias pass a zero-filled

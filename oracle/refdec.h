@@ -139,6 +139,10 @@ typedef struct {
 int  b2o_state_init(const b2o_model* m, b2o_state* s);
 void b2o_state_free(b2o_state* s);
 void b2o_state_reset(const b2o_model* m, b2o_state* s);
+/* Benchmark helper: fill KV rows [0, count) of every attention sub-block with
+ * synthetic values (unit std) and set the position to count, so a decode sample
+ * can start mid-sequence without a CPU prefill. */
+void b2o_state_fill_kv(const b2o_model* m, b2o_state* s, int count, uint64_t seed);
 /* One token through the whole model: returns argmax id (want_logits=1) or 0,
  * -1 on KV overflow (nothing written), -2 on a bad token id. */
 int32_t b2o_step(const b2o_model* m, b2o_state* s, int32_t tok, float* logits, int want_logits);

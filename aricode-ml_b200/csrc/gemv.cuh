@@ -13,7 +13,8 @@
 // Data movement: rows of W are contiguous in HBM, so a group of R rows is one
 // contiguous block. One producer lane streams groups into a shared-memory ring
 // with 1-D bulk async copies (TMA engine, mbarrier completion); 8 consumer warps
-// each own whole groups. The producer starts before griddepcontrol.wait, so under
+// each own whole groups: group j -> warp j % 8, slot j % NS with NS a multiple
+// of 8, so every slot belongs to one warp and its barrier phases stay in order. The producer starts before griddepcontrol.wait, so under
 // programmatic dependent launch the ring fills with this kernel's weights while
 // the previous kernel is still running.
 //
@@ -32,7 +33,7 @@ enum NormKind : int { NORM_NONE = 0, NORM_RMS = 1, NORM_LN = 2 };
 
 constexpr int kGemvConsumerWarps = 8;
 constexpr int kGemvThreads = (kGemvConsumerWarps + 1) * 32;
-constexpr int kGemvMaxStages = 32;
+constexpr int kGemvMaxStages = 32;     // multiple of kGemvConsumerWarps
 
 struct GemvParams {
     const void* W[3];          // up to 3 segments sharing n and ld (Q, K, V)
@@ -153,6 +154,10 @@ gemv_kernel(const __grid_constant__ GemvParams p) {
     const long long g1 = (long long)(blockIdx.x + 1) * G / gridDim.x;
     const int nloc = (int)(g1 - g0);
 
+    if (NS <= 0 || NS > kGemvMaxStages || NS % kGemvConsumerWarps != 0) {   // uniform per grid
+        if (tid == 0) set_err(p.err, B2_DEV_ERR_TIMEOUT);
+        return;
+    }
     if (tid == 0) {
         for (int s = 0; s < NS; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
         fence_mbar_init();

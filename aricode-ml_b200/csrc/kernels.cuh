@@ -298,29 +298,39 @@ inline long long host_groups(const GemvParams& p, int R) {
     return t;
 }
 
-// rows per group: largest power of two <= 8 keeping a stage near 16 KB
+// Ring geometry. The ring depth is a multiple of the 8 consumer warps: group j
+// goes to warp j % 8 and slot j % NS, so each slot is only ever consumed by one
+// warp and its mbarrier phases advance strictly in order (a warp never waits for
+// round r+1 of a slot whose round r is still pending, which parity waits cannot
+// tell apart). Rows per group: the largest power of two <= 8 whose stage keeps 8
+// stages inside the shared-memory budget.
 inline GemvShape gemv_shape(const GemvParams& p, int esz, int min_r, int grid_cap) {
     GemvShape sh{};
     sh.paired = p.paired != 0;
     const size_t row_bytes = (size_t)p.ld * esz * (sh.paired ? 2 : 1);
+    const size_t xs = ((size_t)p.ld * 4 + 127) & ~(size_t)127;
+    const size_t fixed = 1024 + xs;
+    const size_t per_stage_cap = kGemvSmemBudget > fixed + 8 * row_bytes * min_r
+                                     ? (kGemvSmemBudget - fixed) / 8 : row_bytes * min_r;
+    size_t cap = per_stage_cap < kGemvStageTarget ? per_stage_cap : kGemvStageTarget;
     int R = 8;
-    while (R > min_r && (size_t)R * row_bytes > kGemvStageTarget) R >>= 1;
+    while (R > min_r && (size_t)R * row_bytes > cap) R >>= 1;
     if (sh.paired && R > 4) R = 4;
     sh.R = R;
     const long long G = host_groups(p, R);
     sh.grid = (int)(G < grid_cap ? G : grid_cap);
     if (sh.grid < 1) sh.grid = 1;
     const size_t stage = (size_t)R * row_bytes;
-    const size_t xs = ((size_t)p.ld * 4 + 127) & ~(size_t)127;
     size_t budget = kGemvSmemBudget;
-    if (budget < 1024 + xs + 2 * stage) budget = 1024 + xs + 2 * stage;
-    long long ns = (long long)((budget - 1024 - xs) / stage);
+    if (budget < fixed + 8 * stage) budget = fixed + 8 * stage;
+    long long ns = (long long)((budget - fixed) / stage) / 8 * 8;
     const long long per_cta = (G + sh.grid - 1) / sh.grid;
-    if (ns > per_cta) ns = per_cta;
-    if (ns < 2) ns = 2;
+    const long long need = (per_cta + 7) / 8 * 8;
+    if (ns > need) ns = need;
+    if (ns < 8) ns = 8;
     if (ns > kGemvMaxStages) ns = kGemvMaxStages;
     sh.nstages = (int)ns;
-    sh.smem = 1024 + xs + (size_t)ns * stage;
+    sh.smem = fixed + (size_t)ns * stage;
     return sh;
 }
 

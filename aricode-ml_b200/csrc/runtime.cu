@@ -110,7 +110,8 @@ struct Err : std::runtime_error {
 struct b2_ctx {
     int device = 0;
     int sm_count = 148;
-    cudaStream_t stream = nullptr;
+    cudaStream_t stream = nullptr;       // launches and copies
+    cudaStream_t cap_stream = nullptr;   // private stream the graphs are captured on
     bool own_stream = false;
     std::string err;
 
@@ -165,6 +166,7 @@ struct b2_ctx {
         if (d_work) cudaFree(d_work);
         if (h_st) cudaFreeHost(h_st);
         if (own_stream && stream) cudaStreamDestroy(stream);
+        if (cap_stream) cudaStreamDestroy(cap_stream);
     }
 
     // ------------------------------------------------------------ tensors
@@ -288,6 +290,7 @@ void setup_device(b2_ctx* c, int device) {
     if (prop.major < 10) throw Err(B2_E_UNSUPPORTED, "this library is built for sm_100a (B200)");
     c->sm_count = prop.multiProcessorCount;
     CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+    CK(cudaStreamCreateWithFlags(&c->cap_stream, cudaStreamNonBlocking));
     c->own_stream = true;
 }
 
@@ -575,16 +578,16 @@ void capture_graphs_once(b2_ctx* c) {
     if (c->g_decode) { cudaGraphExecDestroy(c->g_decode); c->g_decode = nullptr; }
     for (int head = 0; head < 2; ++head) {
         cudaGraph_t g = nullptr;
-        CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+        CK(cudaStreamBeginCapture(c->cap_stream, cudaStreamCaptureModeThreadLocal));
         int n = 0;
         try {
-            n = enqueue_step(c, head == 1, c->stream);
+            n = enqueue_step(c, head == 1, c->cap_stream);
         } catch (...) {
-            cudaStreamEndCapture(c->stream, &g);
+            cudaStreamEndCapture(c->cap_stream, &g);
             if (g) cudaGraphDestroy(g);
             throw;
         }
-        CK(cudaStreamEndCapture(c->stream, &g));
+        CK(cudaStreamEndCapture(c->cap_stream, &g));
         cudaGraphExec_t ex = nullptr;
         const cudaError_t e = cudaGraphInstantiate(&ex, g, 0);
         cudaGraphDestroy(g);
@@ -931,11 +934,11 @@ int b2_read_output(b2_ctx* ctx, int32_t* ids, int max_ids, int* n_ids) {
 
 int b2_set_stream(b2_ctx* ctx, void* stream) {
     return guarded(ctx, [&] {
+        // graphs were captured on the private capture stream and launch on any stream
         CK(cudaStreamSynchronize(ctx->stream));
         if (ctx->own_stream) CK(cudaStreamDestroy(ctx->stream));
         ctx->stream = static_cast<cudaStream_t>(stream);
         ctx->own_stream = false;
-        capture_graphs(ctx);
         return B2_OK;
     });
 }

@@ -194,7 +194,8 @@ def main():
     P, NEW = c["prompt"], c["new"]
 
     dec = rt.Decoder.synthetic(plan, seed=0, device=local_rank)
-    stream = torch.cuda.current_stream()
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     dec.set_stream(stream.cuda_stream)
     prompt = np.random.default_rng(1).integers(0, plan["vocab"], P).astype(np.int32)
 

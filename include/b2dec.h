@@ -91,8 +91,9 @@ int b2_decode_async(b2_ctx* ctx, int n_steps);
 int b2_sync(b2_ctx* ctx);
 int b2_read_output(b2_ctx* ctx, int32_t* ids, int max_ids, int* n_ids);
 
-/* Run the model's kernels on `stream` (cudaStream_t) instead of the private
- * stream; graphs are re-captured. */
+/* Launch the model's graphs and copies on `stream` (cudaStream_t, NULL = legacy
+ * default stream) instead of the context's private stream, e.g. to time them
+ * with the caller's events. The context does not take ownership. */
 int b2_set_stream(b2_ctx* ctx, void* stream);
 
 /* Numeric properties: "weight_bytes", "kv_bytes_per_pos", "kernels_per_step",

@@ -16,7 +16,7 @@ from pathlib import Path
 PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libb2dec.so"
-SOURCES = ["runtime.cu", "capi.cu"]
+SOURCES = ["runtime.cu", "capi.cu", "noalloc.cu"]
 HEADERS = ["b2_common.cuh", "gemv.cuh", "attn.cuh", "kernels.cuh", "json.h"]
 
 NVCC_FLAGS = [

@@ -800,6 +800,9 @@ int create_common(b2_ctx** out, int device, const std::function<void(b2_ctx*)>& 
 
 }  // namespace
 
+// message for b2_last_error(NULL, ...) from the context-free entry points
+void b2_internal_set_error(const std::string& msg) { g_last_create_error = msg; }
+
 // ===================================================================== C ABI
 extern "C" {
 

@@ -75,6 +75,8 @@ def _declare(L):
     L.b2_attn_decode_workspace.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int]
     L.b2_attn_decode.argtypes = [vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, vp,
                                  C.c_size_t, vp]
+    L.b2_attn_decode_static.argtypes = [vp, vp, vp, vp, C.c_int, C.c_int, C.c_int, C.c_int,
+                                        C.c_int, vp]
     L.b2_argmax.argtypes = [vp, C.c_int64, vp, vp]
     L.b2_silu_mul.argtypes = [vp, vp, vp, C.c_int, vp]
     L.b2_gelu.argtypes = [vp, vp, C.c_int, vp]
@@ -268,6 +270,16 @@ def attn_decode(q, K, V, n_heads, n_kv_heads, d_head, n, max_seq, workspace=None
     check(lib().b2_attn_decode(_ptr(q), _ptr(K), _ptr(V), _ptr(out), n_heads, n_kv_heads, d_head,
                                int(n), int(max_seq), _ptr(workspace), workspace.numel(),
                                _stream(stream)))
+    return out
+
+
+def attn_decode_static(q, K, V, n_heads, n_kv_heads, d_head, n, max_seq, stream=None):
+    """b2_attn_decode with the library's fixed device scratch (no workspace, no
+    allocation inside the call; the output tensor is the caller's)."""
+    import torch
+    out = torch.empty(n_heads * d_head, dtype=torch.float32, device=q.device)
+    check(lib().b2_attn_decode_static(_ptr(q), _ptr(K), _ptr(V), _ptr(out), n_heads, n_kv_heads,
+                                      d_head, int(n), int(max_seq), _stream(stream)))
     return out
 
 

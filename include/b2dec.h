@@ -140,6 +140,21 @@ int b2_attn_decode(const float* q, const float* K, const float* V, float* out, i
                    int n_kv_heads, int d_head, int n, int max_seq, void* workspace,
                    size_t workspace_bytes, void* stream);
 
+/* b2_attn_decode without a workspace argument, for callers that cannot allocate
+ * device memory (a host framework that owns the device's memory and forbids
+ * library cudaMalloc calls, or an FFI binding with no device allocator). No
+ * counterpart in the reference. Its scratch is a fixed device array of
+ * B2_ATTN_STATIC_SCRATCH_BYTES that every GPU loading the library holds until
+ * exit; problems needing more scratch than that (n_heads * ceil(max_seq/64) *
+ * (d_head+2) * 4 + n_kv_heads * 4 bytes) return B2_E_INVALID, with the reason in
+ * b2_last_error(NULL, ...). The first call on a device looks the array up on that
+ * device, so make it before any stream capture. All calls share the array: calls
+ * that overlap on the GPU race. Allocates nothing. */
+#define B2_ATTN_STATIC_SCRATCH_BYTES (4u << 20)
+int b2_attn_decode_static(const float* q, const float* K, const float* V, float* out,
+                          int n_heads, int n_kv_heads, int d_head, int n, int max_seq,
+                          void* stream);
+
 /* out[0] = first index of the maximum (NaN never wins; logits[0] NaN -> 0).
  * Replaces: sample_greedy_f32 (sampling_f32.ari:10-24). */
 int b2_argmax(const float* v, int64_t n, int32_t* out, void* stream);

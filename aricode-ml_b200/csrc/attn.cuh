@@ -40,13 +40,30 @@ inline size_t attn_scratch_bytes(int H, int KVH, int dh, int max_seq) {
 }
 
 inline size_t attn_smem_bytes(int G, int dh, int nsplit_max) {
-    return ((size_t)G * dh + (size_t)G * kAttnChunk + 2 * (size_t)G +
-            (size_t)G * nsplit_max + (size_t)G + 8) * sizeof(float);
+    return 64 + 2 * (size_t)kAttnChunk * dh * sizeof(float) +
+           ((size_t)G * dh + (size_t)G * kAttnChunk + 2 * (size_t)G + (size_t)G * nsplit_max +
+            (size_t)G + 8) * sizeof(float);
 }
 
+// K/V rows of one split are contiguous ([kv_head][max_seq][dh] layout): two bulk
+// copies bring the split's keys and values into shared memory (dh % 4 == 0).
 static __global__ void __launch_bounds__(kAttnThreads)
 attn_decode_kernel(const __grid_constant__ AttnParams p) {
-    extern __shared__ __align__(16) float sm[];
+    extern __shared__ __align__(128) unsigned char asmem[];
+    uint64_t* bar = reinterpret_cast<uint64_t*>(asmem);
+    const int G = p.H / p.KVH, dh = p.dh;
+    float* Ks = reinterpret_cast<float*>(asmem + 64);         // [64][dh]
+    float* Vs = Ks + kAttnChunk * dh;                          // [64][dh]
+    float* qs = Vs + kAttnChunk * dh;                          // [G][dh]
+    float* sc = qs + G * dh;                                   // [G][64] scores, then exp
+    float* mpart = sc + G * kAttnChunk;                        // [G]
+    float* lpart = mpart + G;                                  // [G]
+    float* wsm = lpart + G;                                    // [G][nsplit_max]
+    float* Lsm = wsm + G * p.nsplit_max;                       // [G]
+    __shared__ int last;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) { mbar_init(bar, 1); fence_mbar_init(); }
+    __syncthreads();
     pdl_launch_dependents();
     pdl_wait();
     const bool active = p.st ? (*(volatile int*)&p.st->active != 0) : true;
@@ -55,29 +72,28 @@ attn_decode_kernel(const __grid_constant__ AttnParams p) {
     const int s = blockIdx.x, kvh = blockIdx.y;
     const int nsplit = (n + kAttnChunk - 1) / kAttnChunk;
     if (s >= nsplit) return;
-    const int G = p.H / p.KVH, dh = p.dh;
     const int j0 = s * kAttnChunk;
     const int len = min(kAttnChunk, n - j0);
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-
-    float* qs = sm;                           // [G][dh]
-    float* sc = qs + G * dh;                  // [G][64]  scores, then exp
-    float* mpart = sc + G * kAttnChunk;       // [G]
-    float* lpart = mpart + G;                 // [G]
-    float* wsm = lpart + G;                   // [G][nsplit_max] combine weights
-    float* Lsm = wsm + G * p.nsplit_max;      // [G]
-    __shared__ int last;
-
-    const int h0 = kvh * G;
-    for (int i = tid; i < G * dh; i += kAttnThreads) qs[i] = p.q[(size_t)h0 * dh + i];
-    __syncthreads();
-
     const float* Kh = p.K + (size_t)kvh * p.max_seq * dh;
     const float* Vh = p.V + (size_t)kvh * p.max_seq * dh;
+    if (tid == 0) {
+        const uint32_t bytes = (uint32_t)len * dh * 4;
+        mbar_arrive_expect_tx(bar, 2 * bytes);
+        bulk_g2s(Ks, Kh + (size_t)j0 * dh, bytes, bar);
+        bulk_g2s(Vs, Vh + (size_t)j0 * dh, bytes, bar);
+    }
+    const int h0 = kvh * G;
+    for (int i = tid; i < G * dh; i += kAttnThreads) qs[i] = p.q[(size_t)h0 * dh + i];
+    if (!mbar_wait_bounded(bar, 0)) {
+        set_err(p.err, B2_DEV_ERR_TIMEOUT);
+        mbar_wait_bounded(bar, 0);                 // last bounded wait for the copies in flight
+        return;
+    }
+    __syncthreads();
 
     // scores: warp per key, 32-lane dot over dh (lane L: d = L, L+32, ...)
     for (int jj = warp; jj < len; jj += kAttnThreads / 32) {
-        const float* kr = Kh + (size_t)(j0 + jj) * dh;
+        const float* kr = Ks + jj * dh;
         float kv[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -126,10 +142,9 @@ attn_decode_kernel(const __grid_constant__ AttnParams p) {
     const int stride = dh + 2;
     for (int it = tid; it < G * dh; it += kAttnThreads) {
         const int g = it / dh, d = it % dh;
-        const float* vcol = Vh + (size_t)j0 * dh + d;
         const float* e = sc + g * kAttnChunk;
         float a = 0.0f;
-        for (int jj = 0; jj < len; ++jj) a = ffma(e[jj], vcol[(size_t)jj * dh], a);
+        for (int jj = 0; jj < len; ++jj) a = ffma(e[jj], Vs[jj * dh + d], a);
         float* pp = p.part + ((size_t)(h0 + g) * p.nsplit_max + s) * stride;
         pp[d] = a;
         if (d == 0) { pp[dh] = mpart[g]; pp[dh + 1] = lpart[g]; }

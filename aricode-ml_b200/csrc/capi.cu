@@ -71,7 +71,8 @@ size_t b2_attn_decode_workspace(int n_heads, int n_kv_heads, int d_head, int max
 int b2_attn_decode(const float* q, const float* K, const float* V, float* out, int n_heads, int n_kv_heads,
                    int d_head, int n, int max_seq, void* workspace, size_t workspace_bytes, void* stream) {
     if (!q || !K || !V || !out || !workspace || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads ||
-        d_head <= 0 || d_head > 256 || n <= 0 || n > max_seq)
+        d_head <= 0 || d_head > 256 || d_head % 4 || n <= 0 || n > max_seq ||
+        (reinterpret_cast<uintptr_t>(K) & 15) || (reinterpret_cast<uintptr_t>(V) & 15))
         return B2_E_INVALID;
     if (workspace_bytes < attn_scratch_bytes(n_heads, n_kv_heads, d_head, max_seq)) return B2_E_INVALID;
     AttnParams a{};

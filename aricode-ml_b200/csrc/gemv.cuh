@@ -3,25 +3,28 @@
 // Replaces the reference's arr_i8_matvec_f32_perrow / arr_f32_matvec builtins
 // (call sites tools/aricode_pack.py:183, :1789-1808, attention_gqa_kv_i8.ari:149-151,
 // :191, attention_kv_f32.ari:122-140) and fuses what runs around them:
-//   prologue : input vector -> shared memory, optionally RMSNorm / LayerNorm
+//   prologue : input vector, optionally RMSNorm / LayerNorm
 //              (rmsnorm_affine_f32 aricode_pack.py:585-607, layernorm_affine_f32 :503-521)
 //   epilogue : per-row scale, bias (emit_linear :182-185), residual add (:2015-2018),
 //              RoPE + 1/sqrt(d_head) + KV-cache append (attention_gqa_kv_i8.ari:154-182),
 //              SiLU*up (silu_mul_f32 :626-632), GELU (gelu_f32 :539-572),
 //              greedy argmax over the logits (sample_greedy_f32, sampling_f32.ari:10-24).
 //
-// Data movement: rows of W are contiguous in HBM, so a group of R rows is one
-// contiguous block. One producer lane streams groups into a shared-memory ring
-// with 1-D bulk async copies (TMA engine, mbarrier completion); 8 consumer warps
-// each own whole groups: group j -> warp j % 8, slot j % NS with NS a multiple
-// of 8, so every slot belongs to one warp and its barrier phases stay in order. The producer starts before griddepcontrol.wait, so under
-// programmatic dependent launch the ring fills with this kernel's weights while
-// the previous kernel is still running.
+// Data movement: each CTA owns a balanced, contiguous range of rows. Consecutive
+// rows are contiguous in HBM, so a stage of R whole rows (~16 KB) is ONE 1-D bulk
+// async copy (TMA engine, mbarrier completion) into a shared-memory ring; a
+// producer warp keeps the ring full. Its copies start before griddepcontrol.wait:
+// under programmatic dependent launch the weights stream in while the previous
+// kernel is still finishing.
 //
-// Arithmetic order (identical to oracle/refdec.c b2o_dot_i8 / b2o_dot_f32): lane L
-// owns 16-byte blocks L, L+32, ...; four accumulators take element t of a block
-// into a[t & 3] by fused multiply-add; lane partial (a0+a1)+(a2+a3); XOR
-// butterfly 16,8,4,2,1.
+// Compute: two groups of 8 consumer warps take alternate stages. Within a group
+// the 256 threads split every row: thread s owns the 16-byte blocks s, s+256, ...
+// (its slice of x lives in registers, normalised once), so a stage is read once
+// from shared memory, conflict-free. Per row: four accumulators a[t & 3] updated
+// by fused multiply-adds (issued as packed f32x2 pairs: two independent IEEE
+// round-to-nearest operations, the same results as scalar ones), slot partial
+// (a0+a1)+(a2+a3), warp butterfly, then the 8 warp sums
+// ((W0+W1)+(W2+W3))+((W4+W5)+(W6+W7)) — oracle/refdec.c b2o_dot_i8 / b2o_dot_f32.
 #pragma once
 #include "b2_common.cuh"
 
@@ -31,9 +34,12 @@ enum EpiKind : int { EPI_STORE = 0, EPI_RESID = 1, EPI_QKV = 2, EPI_SWIGLU = 3, 
                      EPI_ARGMAX = 5 };
 enum NormKind : int { NORM_NONE = 0, NORM_RMS = 1, NORM_LN = 2 };
 
-constexpr int kGemvConsumerWarps = 8;
-constexpr int kGemvThreads = (kGemvConsumerWarps + 1) * 32;
-constexpr int kGemvMaxStages = 32;     // multiple of kGemvConsumerWarps
+constexpr int kGemvGroupWarps = 8;                                 // warps per consumer group
+constexpr int kGemvGroups = 2;                                     // groups on alternate stages
+constexpr int kGemvConsumerWarps = kGemvGroupWarps * kGemvGroups;
+constexpr int kGemvConsumerThreads = kGemvConsumerWarps * 32;
+constexpr int kGemvThreads = kGemvConsumerThreads + 32;            // + producer warp
+constexpr int kGemvMaxStages = 32;                                 // multiple of kGemvGroups
 
 struct GemvParams {
     const void* W[3];          // up to 3 segments sharing n and ld (Q, K, V)
@@ -41,10 +47,12 @@ struct GemvParams {
     const float* bias[3];      // optional per-row bias
     int rows[3];
     int nseg;
-    int paired;                // 1: each group takes R rows of segment 0 and of segment 1
+    int paired;                // 1: every stage carries R rows of segment 0 and of segment 1
     int n;                     // logical input length
     int ld;                    // row stride in elements (16-byte multiple)
-    int nstages;               // ring depth
+    int nstages;               // ring depth (multiple of kGemvGroups)
+    int stage_rows;            // rows per stage (R)
+    int ring_offset;           // byte offset of the ring in shared memory
     const float* x;            // input vector [n]
     int norm;
     const float* ng;
@@ -83,116 +91,171 @@ __device__ __forceinline__ bool amax_better(float va, int ia, float vb, int ib) 
     return ia < ib;
 }
 
-struct GroupInfo { int seg, row0, nrows; };
-
-template <int R>
-__device__ __forceinline__ GroupInfo group_info(const GemvParams& p, long long g) {
-    GroupInfo gi{0, 0, 0};
-    const int nseg = p.paired ? 1 : p.nseg;
-    for (int s = 0; s < nseg; ++s) {
-        const long long ng = (p.rows[s] + R - 1) / R;
-        if (g < ng) {
-            gi.seg = s;
-            gi.row0 = (int)(g * R);
-            gi.nrows = min(R, p.rows[s] - gi.row0);
-            return gi;
-        }
-        g -= ng;
-    }
-    return gi;
+// 4 int8 of u (xor 0x80 applied) against x: (a0,a1) += (w0,w1)*(x0,x1),
+// (a2,a3) += (w2,w3)*(x2,x3); w = (2^23 + 128 + b) - (2^23 + 128), exact.
+__device__ __forceinline__ void fma_word2(float2& a01, float2& a23, uint32_t u, float2 x01, float2 x23) {
+    const float2 c = make_float2(-8388736.0f, -8388736.0f);
+    float2 w01 = make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440u)),
+                             __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7441u)));
+    float2 w23 = make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7442u)),
+                             __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7443u)));
+    w01 = __fadd2_rn(w01, c);
+    w23 = __fadd2_rn(w23, c);
+    a01 = __ffma2_rn(w01, x01, a01);
+    a23 = __ffma2_rn(w23, x23, a23);
 }
 
-template <int R>
-__device__ __forceinline__ long long total_groups(const GemvParams& p) {
-    long long t = 0;
-    const int nseg = p.paired ? 1 : p.nseg;
-    for (int s = 0; s < nseg; ++s) t += (p.rows[s] + R - 1) / R;
-    return t;
+__device__ __forceinline__ void consumer_bar() {
+    asm volatile("bar.sync 1, %0;" ::"r"(kGemvConsumerThreads) : "memory");
 }
 
-// 4 int8 (xor 0x80 applied) x 4 floats into a[0..3]
-__device__ __forceinline__ void fma_word(float* a, uint32_t u, const float4& xv) {
-    a[0] = ffma(i8_to_f(u, 0), xv.x, a[0]);
-    a[1] = ffma(i8_to_f(u, 1), xv.y, a[1]);
-    a[2] = ffma(i8_to_f(u, 2), xv.z, a[2]);
-    a[3] = ffma(i8_to_f(u, 3), xv.w, a[3]);
-}
-
-// Reduction over the consumer threads' 256 partials (thread t < 256 holds partial t):
-// warp butterfly, then ((W0+W1)+(W2+W3)) + ((W4+W5)+(W6+W7)). Same as reduce256().
+// Reduction over 256 partials held by consumer threads 0..255 (the others pass
+// zeros and take part only in the barriers): warp butterfly, then
+// ((W0+W1)+(W2+W3)) + ((W4+W5)+(W6+W7)). Same as the oracle's reduce256().
 __device__ __forceinline__ float consumer_reduce256(float part, float* red, int tid) {
     const float w = butterfly32(part);
     if ((tid & 31) == 0 && tid < 256) red[tid >> 5] = w;
-    asm volatile("bar.sync 1, %0;" ::"r"(kGemvConsumerWarps * 32) : "memory");
+    consumer_bar();
     const float tot = fadd(fadd(fadd(red[0], red[1]), fadd(red[2], red[3])),
                            fadd(fadd(red[4], red[5]), fadd(red[6], red[7])));
-    asm volatile("bar.sync 1, %0;" ::"r"(kGemvConsumerWarps * 32) : "memory");
+    consumer_bar();
     return tot;
 }
 
-template <typename WT, int R, bool PAIRED>
+__device__ __forceinline__ float tree8(const float* w) {
+    return fadd(fadd(fadd(w[0], w[1]), fadd(w[2], w[3])), fadd(fadd(w[4], w[5]), fadd(w[6], w[7])));
+}
+
+__device__ __forceinline__ void seg_of(const GemvParams& p, int row, int& seg, int& local) {
+    seg = 0;
+    local = row;
+    while (seg < p.nseg - 1 && local >= p.rows[seg]) { local -= p.rows[seg]; ++seg; }
+}
+
+__device__ __forceinline__ int total_rows(const GemvParams& p) {
+    if (p.paired) return p.rows[0];
+    int t = 0;
+    for (int s = 0; s < p.nseg; ++s) t += p.rows[s];
+    return t;
+}
+
+// rows [r0, r1) of CTA b: balanced in units of `unit` rows (2 keeps RoPE pairs together)
+__device__ __forceinline__ void cta_rows(int total, int unit, int& r0, int& r1) {
+    const long long units = (total + unit - 1) / unit;
+    const long long u0 = (long long)blockIdx.x * units / gridDim.x;
+    const long long u1 = (long long)(blockIdx.x + 1) * units / gridDim.x;
+    r0 = (int)(u0 * unit);
+    r1 = (int)(u1 * unit < (long long)total ? u1 * unit : (long long)total);
+}
+
+// Stage walk shared by producer and consumers: from logical row `cur`, the next
+// stage takes up to R rows that stay inside one segment.
+struct StageRows { int seg, local, nr; };
+__device__ __forceinline__ StageRows next_stage(const GemvParams& p, int cur, int r1, int R) {
+    StageRows st;
+    if (p.paired) { st.seg = 0; st.local = cur; st.nr = min(R, r1 - cur); return st; }
+    seg_of(p, cur, st.seg, st.local);
+    st.nr = min(min(R, r1 - cur), p.rows[st.seg] - st.local);
+    return st;
+}
+
+// Exchange butterfly over the 32 lanes for N row partials at once (N a power of
+// two <= 32). At stride s the lane keeps half of its rows and trades the other
+// half with lane ^ s; each kept sum is own + partner, exactly the operands the
+// plain butterfly (v <- v + shfl_xor(v, s)) adds for that row, so the row totals
+// are bit-identical to per-row butterflies while N rows cost about N + 4 shuffles.
+// On return v[0] holds row (lane >> (5 - log2 N)); the 32/N lanes sharing those
+// high bits hold the same total.
+template <int N>
+__device__ __forceinline__ void exchange_butterfly(float (&v)[N], int lane) {
+    int cnt = N;
+#pragma unroll
+    for (int s = 16; s >= 1; s >>= 1) {
+        if (cnt > 1) {
+            const bool upper = (lane & s) != 0;
+            const int h = cnt / 2;
+#pragma unroll
+            for (int i = 0; i < (N > 1 ? N / 2 : 1); ++i) {
+                if (i < h) {
+                    const float send = upper ? v[i] : v[h + i];
+                    const float keep = upper ? v[h + i] : v[i];
+                    v[i] = fadd(keep, __shfl_xor_sync(0xffffffffu, send, s));
+                }
+            }
+            cnt = h;
+        } else {
+            v[0] = fadd(v[0], __shfl_xor_sync(0xffffffffu, v[0], s));
+        }
+    }
+}
+
+template <int N> struct Log2 { static constexpr int v = 1 + Log2<N / 2>::v; };
+template <> struct Log2<1> { static constexpr int v = 0; };
+
+template <typename WT, int KMAX, int RS, bool PAIRED>
 __global__ void __launch_bounds__(kGemvThreads, 1)
 gemv_kernel(const __grid_constant__ GemvParams p) {
-    constexpr int RT = PAIRED ? R * 2 : R;          // rows held per group
     constexpr int ESZ = (int)sizeof(WT);
+    constexpr int EPB = 16 / ESZ;                                // elements per 16-byte block
+    constexpr int NM = PAIRED ? 2 : 1;                           // matrices per stage
+    constexpr int NR = RS * NM;                                  // rows reduced together
+    constexpr int LG = Log2<NR>::v;
     extern __shared__ __align__(128) unsigned char smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + kGemvMaxStages;
-    float* red = reinterpret_cast<float*>(empty + kGemvMaxStages);        // 64 floats
-    float* xs = reinterpret_cast<float*>(smem + 1024);
+    float* red = reinterpret_cast<float*>(empty + kGemvMaxStages);      // 8 floats
+    float* part = reinterpret_cast<float*>(smem + 1024);                 // [rows_cta][NM][8]
     const int ld = p.ld;
-    const int rows_per_stage = RT;
-    const uint32_t seg_bytes = (uint32_t)R * ld * ESZ;
-    const uint32_t stage_bytes = (uint32_t)rows_per_stage * ld * ESZ;
-    unsigned char* ring = smem + 1024 + (((size_t)ld * 4 + 127) & ~(size_t)127);
+    const uint32_t row_bytes = (uint32_t)ld * ESZ;
+    const uint32_t stage_bytes = (uint32_t)RS * row_bytes * NM;
+    unsigned char* ring = smem + p.ring_offset;
     const int NS = p.nstages;
+    const int nblk = (int)(row_bytes >> 4);
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
-    const long long G = total_groups<R>(p);
-    const long long g0 = (long long)blockIdx.x * G / gridDim.x;
-    const long long g1 = (long long)(blockIdx.x + 1) * G / gridDim.x;
-    const int nloc = (int)(g1 - g0);
+    int r0, r1;
+    cta_rows(total_rows(p), p.rope ? 2 : 1, r0, r1);
 
-    if (NS <= 0 || NS > kGemvMaxStages || NS % kGemvConsumerWarps != 0) {   // uniform per grid
-        if (tid == 0) set_err(p.err, B2_DEV_ERR_TIMEOUT);
+    if (NS < 2 * kGemvGroups || NS > kGemvMaxStages || NS % kGemvGroups || p.stage_rows != RS) {
+        if (tid == 0) set_err(p.err, B2_DEV_ERR_TIMEOUT);     // uniform per grid
         return;
     }
     if (tid == 0) {
-        for (int s = 0; s < NS; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kGemvGroupWarps);
+        }
         fence_mbar_init();
     }
     __syncthreads();
     pdl_launch_dependents();
 
     if (warp == kGemvConsumerWarps) {
-        // ---------------- producer: stream this CTA's groups into the ring
+        // ---------------- producer: one bulk copy (two when paired) per stage
         if (lane == 0) {
             int issued = 0;
-            for (int j = 0; j < nloc; ++j) {
-                const int slot = j % NS;
-                const int round = j / NS;
+            bool ok = true;
+            int cur = r0;
+            for (int j = 0; cur < r1; ++j) {
+                const StageRows sr = next_stage(p, cur, r1, RS);
+                const int slot = j % NS, round = j / NS;
                 if (round > 0 && !mbar_wait_bounded(&empty[slot], (uint32_t)((round - 1) & 1))) {
-                    set_err(p.err, B2_DEV_ERR_TIMEOUT);
+                    ok = false;
                     break;
                 }
-                const GroupInfo gi = group_info<R>(p, g0 + j);
-                const uint32_t bytes = (uint32_t)gi.nrows * ld * ESZ;
+                const uint32_t bytes = (uint32_t)sr.nr * row_bytes;
                 unsigned char* dst = ring + (size_t)slot * stage_bytes;
-                const unsigned char* src0 =
-                    reinterpret_cast<const unsigned char*>(p.W[gi.seg]) + (size_t)gi.row0 * ld * ESZ;
-                if constexpr (PAIRED) {
-                    const unsigned char* src1 =
-                        reinterpret_cast<const unsigned char*>(p.W[1]) + (size_t)gi.row0 * ld * ESZ;
-                    mbar_arrive_expect_tx(&full[slot], 2 * bytes);
-                    bulk_g2s(dst, src0, bytes, &full[slot]);
-                    bulk_g2s(dst + seg_bytes, src1, bytes, &full[slot]);
-                } else {
-                    mbar_arrive_expect_tx(&full[slot], bytes);
-                    bulk_g2s(dst, src0, bytes, &full[slot]);
-                }
+                mbar_arrive_expect_tx(&full[slot], bytes * NM);
+                bulk_g2s(dst, reinterpret_cast<const unsigned char*>(p.W[sr.seg]) +
+                                  (size_t)sr.local * row_bytes, bytes, &full[slot]);
+                if constexpr (PAIRED)
+                    bulk_g2s(dst + (size_t)RS * row_bytes, reinterpret_cast<const unsigned char*>(p.W[1]) +
+                                                               (size_t)sr.local * row_bytes, bytes, &full[slot]);
                 ++issued;
+                cur += sr.nr;
             }
+            if (!ok) set_err(p.err, B2_DEV_ERR_TIMEOUT);
             // drain: no copy may still be in flight when the CTA exits
             for (int j = max(0, issued - NS); j < issued; ++j)
                 if (!mbar_wait_bounded(&full[j % NS], (uint32_t)((j / NS) & 1))) {
@@ -203,167 +266,176 @@ gemv_kernel(const __grid_constant__ GemvParams p) {
         return;
     }
 
-    // ---------------- consumers
+    // ---------------- consumers: group g takes stages j with j % kGemvGroups == g
+    const int group = warp / kGemvGroupWarps;
+    const int gwarp = warp % kGemvGroupWarps;
+    const int slotid = tid % 256;                                // this thread's block slot
     pdl_wait();
     const bool active = p.st ? (*(volatile int*)&p.st->active != 0) : true;
     const int pos = p.st ? *(volatile int*)&p.st->pos : p.pos_fixed;
     const int n = p.n;
 
-    // prologue: x (optionally normalised) into shared memory, zero-padded to ld
-    if (p.norm == NORM_NONE) {
-        for (int i = tid; i < ld; i += kGemvConsumerWarps * 32) xs[i] = i < n ? p.x[i] : 0.0f;
-    } else if (p.norm == NORM_RMS) {
+    // prologue: this thread's slice of x (blocks slot, slot+256, ...), normalised
+    float scale_a = 1.0f, shift_m = 0.0f;
+    if (p.norm == NORM_RMS) {
         float a = 0.0f;
         if (tid < 256)
             for (int i = tid; i < n; i += 256) { const float v = p.x[i]; a = ffma(v, v, a); }
         const float tot = consumer_reduce256(a, red, tid);
         const float ms = fdiv(tot, (float)n);
-        const float inv = fdiv(1.0f, __fsqrt_rn(fadd(ms, p.eps)));
-        for (int i = tid; i < ld; i += kGemvConsumerWarps * 32)
-            xs[i] = i < n ? fmul(fmul(p.x[i], inv), p.ng[i]) : 0.0f;
-    } else {
+        scale_a = fdiv(1.0f, __fsqrt_rn(fadd(ms, p.eps)));
+    } else if (p.norm == NORM_LN) {
         float a = 0.0f;
         if (tid < 256)
             for (int i = tid; i < n; i += 256) a = fadd(a, p.x[i]);
-        const float mean = fdiv(consumer_reduce256(a, red, tid), (float)n);
+        shift_m = fdiv(consumer_reduce256(a, red, tid), (float)n);
         a = 0.0f;
         if (tid < 256)
-            for (int i = tid; i < n; i += 256) { const float dx = fsub(p.x[i], mean); a = ffma(dx, dx, a); }
+            for (int i = tid; i < n; i += 256) { const float dx = fsub(p.x[i], shift_m); a = ffma(dx, dx, a); }
         const float var = fdiv(consumer_reduce256(a, red, tid), (float)n);
-        const float inv = fdiv(1.0f, __fsqrt_rn(fadd(var, p.eps)));
-        for (int i = tid; i < ld; i += kGemvConsumerWarps * 32) {
-            if (i < n) {
-                const float t = fmul(fsub(p.x[i], mean), inv);
-                xs[i] = (float)dadd(dmul((double)t, (double)p.ng[i]), (double)p.nb[i]);
-            } else {
-                xs[i] = 0.0f;
+        scale_a = fdiv(1.0f, __fsqrt_rn(fadd(var, p.eps)));
+    }
+    const int K = (nblk + 255) / 256;
+    float2 xr[KMAX][EPB / 2];
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k) {
+        const int b = slotid + 256 * k;
+#pragma unroll
+        for (int t = 0; t < EPB; ++t) {
+            const int i = b * EPB + t;
+            float v = 0.0f;
+            if (k < K && b < nblk && i < n) {
+                const float xv = p.x[i];
+                if (p.norm == NORM_RMS) v = fmul(fmul(xv, scale_a), p.ng[i]);
+                else if (p.norm == NORM_LN)
+                    v = (float)dadd(dmul((double)fmul(fsub(xv, shift_m), scale_a), (double)p.ng[i]),
+                                    (double)p.nb[i]);
+                else v = xv;
             }
+            if (t & 1) xr[k][t / 2].y = v;
+            else xr[k][t / 2].x = v;
         }
     }
-    asm volatile("bar.sync 1, %0;" ::"r"(kGemvConsumerWarps * 32) : "memory");
 
+    // stream the stages: all rows of a stage at once, then one exchange butterfly
+    int cur = r0;
+    for (int j = 0; cur < r1; ++j) {
+        const StageRows sr = next_stage(p, cur, r1, RS);
+        if (j % kGemvGroups == group) {
+            const int slot = j % NS;
+            if (!mbar_wait_bounded(&full[slot], (uint32_t)((j / NS) & 1))) {
+                set_err(p.err, B2_DEV_ERR_TIMEOUT);
+                break;
+            }
+            const unsigned char* stage = ring + (size_t)slot * stage_bytes;
+            if (active) {
+                float2 a01[NR], a23[NR];
+#pragma unroll
+                for (int r = 0; r < NR; ++r) a01[r] = a23[r] = make_float2(0.0f, 0.0f);
+#pragma unroll
+                for (int k = 0; k < KMAX; ++k) {
+                    const int b = slotid + 256 * k;
+                    if (k < K && b < nblk) {
+#pragma unroll
+                        for (int r = 0; r < NR; ++r) {
+                            // rows past sr.nr read stale (in-bounds) stage bytes; never stored
+                            const unsigned char* row = stage + (size_t)r * row_bytes + 16 * b;
+                            if constexpr (ESZ == 1) {
+                                const uint4 w = lds128(row);
+                                fma_word2(a01[r], a23[r], w.x ^ 0x80808080u, xr[k][0], xr[k][1]);
+                                fma_word2(a01[r], a23[r], w.y ^ 0x80808080u, xr[k][2], xr[k][3]);
+                                fma_word2(a01[r], a23[r], w.z ^ 0x80808080u, xr[k][4], xr[k][5]);
+                                fma_word2(a01[r], a23[r], w.w ^ 0x80808080u, xr[k][6], xr[k][7]);
+                            } else {
+                                const float4 w = lds128f(row);
+                                a01[r] = __ffma2_rn(make_float2(w.x, w.y), xr[k][0], a01[r]);
+                                a23[r] = __ffma2_rn(make_float2(w.z, w.w), xr[k][1], a23[r]);
+                            }
+                        }
+                    }
+                }
+                float v[NR];
+#pragma unroll
+                for (int r = 0; r < NR; ++r)
+                    v[r] = fadd(fadd(a01[r].x, a01[r].y), fadd(a23[r].x, a23[r].y));
+                exchange_butterfly<NR>(v, lane);
+                if ((lane & ((32 >> LG) - 1)) == 0) {
+                    const int rr = lane >> (5 - LG);             // stage row (m * RS + r)
+                    const int m = rr / RS, r = rr % RS;
+                    if (r < sr.nr) part[((cur - r0 + r) * NM + m) * 8 + gwarp] = v[0];
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+        cur += sr.nr;
+    }
+    consumer_bar();
+    if (!active) return;
+
+    // ---------------- epilogue: thread per row (per row pair with RoPE)
     float best_v = 0.0f;
     int best_i = 0x7fffffff;
     bool have_best = false;
-    bool ok = true;
-
-    for (int j = warp; j < nloc; j += kGemvConsumerWarps) {
-        const int slot = j % NS;
-        if (!mbar_wait_bounded(&full[slot], (uint32_t)((j / NS) & 1))) {
-            set_err(p.err, B2_DEV_ERR_TIMEOUT);
-            ok = false;
-            break;
-        }
-        const GroupInfo gi = group_info<R>(p, g0 + j);
-        const unsigned char* stage = ring + (size_t)slot * stage_bytes;
-        float acc[RT][4];
-#pragma unroll
-        for (int r = 0; r < RT; ++r) acc[r][0] = acc[r][1] = acc[r][2] = acc[r][3] = 0.0f;
-        if (active) {
-            if constexpr (ESZ == 1) {
-                const int nblk = ld >> 4;
-                for (int b = lane; b < nblk; b += 32) {
-                    const float4 x0 = lds128f(xs + 16 * b);
-                    const float4 x1 = lds128f(xs + 16 * b + 4);
-                    const float4 x2 = lds128f(xs + 16 * b + 8);
-                    const float4 x3 = lds128f(xs + 16 * b + 12);
-#pragma unroll
-                    for (int r = 0; r < RT; ++r) {
-                        const uint4 w = lds128(stage + (size_t)r * ld + 16 * b);
-                        fma_word(acc[r], w.x ^ 0x80808080u, x0);
-                        fma_word(acc[r], w.y ^ 0x80808080u, x1);
-                        fma_word(acc[r], w.z ^ 0x80808080u, x2);
-                        fma_word(acc[r], w.w ^ 0x80808080u, x3);
-                    }
-                }
-            } else {
-                const int nblk = ld >> 2;
-                for (int b = lane; b < nblk; b += 32) {
-                    const float4 xv = lds128f(xs + 4 * b);
-#pragma unroll
-                    for (int r = 0; r < RT; ++r) {
-                        const float4 w = lds128f(stage + ((size_t)r * ld + 4 * b) * 4);
-                        acc[r][0] = ffma(w.x, xv.x, acc[r][0]);
-                        acc[r][1] = ffma(w.y, xv.y, acc[r][1]);
-                        acc[r][2] = ffma(w.z, xv.z, acc[r][2]);
-                        acc[r][3] = ffma(w.w, xv.w, acc[r][3]);
-                    }
-                }
-            }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);       // stage consumed
-        if (!active) continue;
-
-        float dot[RT];
-#pragma unroll
-        for (int r = 0; r < RT; ++r)
-            dot[r] = butterfly32(fadd(fadd(acc[r][0], acc[r][1]), fadd(acc[r][2], acc[r][3])));
-
-        // lane r finishes row gi.row0 + r
-        const int r = lane;
-        float v = 0.0f, v2 = 0.0f;
-#pragma unroll
-        for (int k = 0; k < R; ++k)
-            if (r == k) { v = dot[k]; if constexpr (PAIRED) v2 = dot[R + k]; }
-        const bool live = r < gi.nrows;
-        const int row = gi.row0 + r;
-        const int seg = gi.seg;
-        if constexpr (PAIRED) {       // EPI_SWIGLU
-            if (live) {
-                const float g = fmul(v, p.S[0][row]);
-                const float u = fmul(v2, p.S[1][row]);
-                p.y[row] = fmul(silu_f(g), u);
-            }
+    const int nrows = r1 - r0;
+    const int step = p.rope ? 2 : 1;
+    for (int rl = tid * step; rl < nrows; rl += kGemvConsumerThreads * step) {
+        const int lrow = r0 + rl;
+        if constexpr (PAIRED) {                              // EPI_SWIGLU
+            const float g = fmul(tree8(part + (rl * 2 + 0) * 8), p.S[0][lrow]);
+            const float u = fmul(tree8(part + (rl * 2 + 1) * 8), p.S[1][lrow]);
+            p.y[lrow] = fmul(silu_f(g), u);
             continue;
         }
-        float val = v;
-        if (live) {
-            if constexpr (ESZ == 1) val = fmul(val, p.S[seg][row]);
-            if (p.bias[seg]) val = fadd(val, p.bias[seg][row]);
-            else if constexpr (ESZ == 4) val = fadd(val, 0.0f);
+        int seg, row;
+        seg_of(p, lrow, seg, row);
+        float val[2] = {0.0f, 0.0f};
+        for (int e = 0; e < step; ++e) {
+            float v = tree8(part + (rl + e) * 8);
+            if constexpr (ESZ == 1) v = fmul(v, p.S[seg][row + e]);
+            if (p.bias[seg]) v = fadd(v, p.bias[seg][row + e]);
+            else if constexpr (ESZ == 4) v = fadd(v, 0.0f);
+            val[e] = v;
         }
         if (p.epi == EPI_QKV) {
-            float out = val;
+            float out[2] = {val[0], val[1]};
             if (p.rope && seg < 2) {
-                const float partner = __shfl_xor_sync(0xffffffffu, val, 1);
+                // pair (2i, 2i+1): rows start even and segment sizes are even
                 const int hd = row % p.dh;
-                const float* tr = p.rope_tab + (size_t)pos * p.dh + (hd & ~1);
-                const float c = tr[0], s = tr[1];
-                out = (hd & 1) ? fadd(fmul(partner, s), fmul(val, c))
-                               : fsub(fmul(val, c), fmul(partner, s));
+                const float* tr = p.rope_tab + (size_t)pos * p.dh + hd;
+                const float c = tr[0], sn = tr[1];
+                out[0] = fsub(fmul(val[0], c), fmul(val[1], sn));
+                out[1] = fadd(fmul(val[0], sn), fmul(val[1], c));
             }
-            if (live) {
+            for (int e = 0; e < step; ++e) {
+                const int rr = row + e;
                 if (seg == 0) {
-                    p.qout[row] = fmul(out, p.qscale);
+                    p.qout[rr] = fmul(out[e], p.qscale);
                 } else if (pos < p.max_seq) {
-                    const int kvh = row / p.dh, hd = row % p.dh;
+                    const int kvh = rr / p.dh, hd = rr % p.dh;
                     float* cache = seg == 1 ? p.kcache : p.vcache;
-                    cache[((size_t)kvh * p.max_seq + pos) * p.dh + hd] = out;
+                    cache[((size_t)kvh * p.max_seq + pos) * p.dh + hd] = out[e];
                 } else {
                     set_err(p.err, B2_DEV_ERR_KV_OVERFLOW);
                 }
             }
         } else if (p.epi == EPI_RESID) {
-            if (live) p.y[row] = fadd(val, p.resid[row]);
+            p.y[row] = fadd(val[0], p.resid[row]);
         } else if (p.epi == EPI_GELU) {
-            if (live) p.y[row] = gelu_f(val);
+            p.y[row] = gelu_f(val[0]);
         } else if (p.epi == EPI_ARGMAX) {
-            if (live) {
-                if (p.y) p.y[row] = val;
-                if (row == 0 && p.amax_v0nan) *p.amax_v0nan = (val != val) ? 1 : 0;
-                if (!have_best || amax_better(val, row, best_v, best_i)) {
-                    best_v = val; best_i = row; have_best = true;
-                }
+            if (p.y) p.y[row] = val[0];
+            if (row == 0 && p.amax_v0nan) *p.amax_v0nan = (val[0] != val[0]) ? 1 : 0;
+            if (!have_best || amax_better(val[0], row, best_v, best_i)) {
+                best_v = val[0]; best_i = row; have_best = true;
             }
         } else {
-            if (live) p.y[row] = val;
+            p.y[row] = val[0];
         }
     }
-    (void)ok;
 
-    if (p.epi == EPI_ARGMAX && active) {
-        // warp -> CTA -> grid argmax (the comparator is a total order, so the
+    if (p.epi == EPI_ARGMAX) {
+        // thread -> warp -> CTA -> grid (the comparator is a total order, so the
         // result does not depend on the reduction shape)
         for (int s = 16; s >= 1; s >>= 1) {
             const float ov = __shfl_xor_sync(0xffffffffu, best_v, s);
@@ -378,7 +450,7 @@ gemv_kernel(const __grid_constant__ GemvParams p) {
         __shared__ int wh[kGemvConsumerWarps];
         __shared__ int last;
         if (lane == 0) { wv[warp] = best_v; wi[warp] = best_i; wh[warp] = have_best; }
-        asm volatile("bar.sync 1, %0;" ::"r"(kGemvConsumerWarps * 32) : "memory");
+        consumer_bar();
         if (tid == 0) {
             float cv = 0.0f; int ci = 0x7fffffff; bool ch = false;
             for (int w = 0; w < kGemvConsumerWarps; ++w)
@@ -389,7 +461,7 @@ gemv_kernel(const __grid_constant__ GemvParams p) {
             const unsigned t = atomicAdd(p.amax_count, 1u);
             last = (t == gridDim.x - 1);
         }
-        asm volatile("bar.sync 1, %0;" ::"r"(kGemvConsumerWarps * 32) : "memory");
+        consumer_bar();
         if (last && tid == 0) {
             __threadfence();
             float cv = 0.0f; int ci = 0x7fffffff; bool ch = false;

@@ -272,104 +272,105 @@ inline cudaError_t launch_ex(K kernel, dim3 grid, dim3 block, size_t smem, cudaS
     return cudaLaunchKernelEx(&cfg, kernel, params);
 }
 
-constexpr size_t kGemvSmemBudget = 110 * 1024;
+constexpr size_t kGemvSmemBudget = 200 * 1024;   // one 544-thread CTA per SM
 constexpr size_t kGemvStageTarget = 16 * 1024;
+constexpr int kGemvMaxK = 4;                       // 16-byte blocks per thread per row
 
 struct GemvShape {
-    int R;
+    int K;          // 16-byte blocks per thread per row
+    int R;          // rows per stage
     bool paired;
     int grid;
     int nstages;
+    int ring_offset;
     size_t smem;
 };
 
-template <int R>
-inline long long host_total_groups(const GemvParams& p) {
-    long long t = 0;
-    const int nseg = p.paired ? 1 : p.nseg;
-    for (int s = 0; s < nseg; ++s) t += (p.rows[s] + R - 1) / R;
+inline int host_total_rows(const GemvParams& p) {
+    if (p.paired) return p.rows[0];
+    int t = 0;
+    for (int s = 0; s < p.nseg; ++s) t += p.rows[s];
     return t;
 }
 
-inline long long host_groups(const GemvParams& p, int R) {
-    long long t = 0;
-    const int nseg = p.paired ? 1 : p.nseg;
-    for (int s = 0; s < nseg; ++s) t += (p.rows[s] + R - 1) / R;
-    return t;
-}
-
-// Ring geometry. The ring depth is a multiple of the 8 consumer warps: group j
-// goes to warp j % 8 and slot j % NS, so each slot is only ever consumed by one
-// warp and its mbarrier phases advance strictly in order (a warp never waits for
-// round r+1 of a slot whose round r is still pending, which parity waits cannot
-// tell apart). Rows per group: the largest power of two <= 8 whose stage keeps 8
-// stages inside the shared-memory budget.
-inline GemvShape gemv_shape(const GemvParams& p, int esz, int min_r, int grid_cap) {
+inline GemvShape gemv_shape(const GemvParams& p, int esz, int grid_cap) {
     GemvShape sh{};
     sh.paired = p.paired != 0;
-    const size_t row_bytes = (size_t)p.ld * esz * (sh.paired ? 2 : 1);
-    const size_t xs = ((size_t)p.ld * 4 + 127) & ~(size_t)127;
-    const size_t fixed = 1024 + xs;
-    const size_t per_stage_cap = kGemvSmemBudget > fixed + 8 * row_bytes * min_r
-                                     ? (kGemvSmemBudget - fixed) / 8 : row_bytes * min_r;
-    size_t cap = per_stage_cap < kGemvStageTarget ? per_stage_cap : kGemvStageTarget;
-    int R = 8;
-    while (R > min_r && (size_t)R * row_bytes > cap) R >>= 1;
-    if (sh.paired && R > 4) R = 4;
-    sh.R = R;
-    const long long G = host_groups(p, R);
-    sh.grid = (int)(G < grid_cap ? G : grid_cap);
+    const int nm = sh.paired ? 2 : 1;
+    const size_t row_bytes = (size_t)p.ld * esz;
+    sh.K = (int)((row_bytes / 16 + 255) / 256);
+    const int unit = p.rope ? 2 : 1;
+    const int total = host_total_rows(p);
+    const int units = (total + unit - 1) / unit;
+    sh.grid = units < grid_cap ? units : grid_cap;
     if (sh.grid < 1) sh.grid = 1;
-    const size_t stage = (size_t)R * row_bytes;
+    // rows per stage: a power of two (<= 16, <= 8 when paired) keeping the stage near 16 KB
+    int R = sh.paired ? 8 : 16;
+    while (R > 1 && (size_t)R * row_bytes * nm > kGemvStageTarget) R >>= 1;
+    sh.R = R;
+    const int rows_cta = ((units + sh.grid - 1) / sh.grid) * unit;
+    const size_t part_bytes = (size_t)rows_cta * nm * 8 * sizeof(float);
+    sh.ring_offset = (int)((1024 + part_bytes + 127) & ~(size_t)127);
+    const size_t stage = (size_t)R * row_bytes * nm;
     size_t budget = kGemvSmemBudget;
-    if (budget < fixed + 8 * stage) budget = fixed + 8 * stage;
-    long long ns = (long long)((budget - fixed) / stage) / 8 * 8;
-    const long long per_cta = (G + sh.grid - 1) / sh.grid;
-    const long long need = (per_cta + 7) / 8 * 8;
-    if (ns > need) ns = need;
-    if (ns < 8) ns = 8;
+    if (budget < sh.ring_offset + 2 * kGemvGroups * stage) budget = sh.ring_offset + 2 * kGemvGroups * stage;
+    long long ns = (long long)((budget - sh.ring_offset) / stage);
+    const long long stages_cta = (rows_cta + R - 1) / R + (p.paired ? 0 : p.nseg);
+    if (ns > stages_cta) ns = stages_cta;
+    ns = ns / kGemvGroups * kGemvGroups;               // each slot belongs to one group
+    if (ns < 2 * kGemvGroups) ns = 2 * kGemvGroups;
     if (ns > kGemvMaxStages) ns = kGemvMaxStages;
     sh.nstages = (int)ns;
-    sh.smem = fixed + (size_t)ns * stage;
+    sh.smem = sh.ring_offset + (size_t)ns * stage;
     return sh;
 }
 
-template <typename WT, int R, bool PAIRED>
+template <typename WT, int KMAX, int RS, bool PAIRED>
 inline cudaError_t launch_gemv_t(GemvParams p, const GemvShape& sh, cudaStream_t s, bool pdl) {
     p.nstages = sh.nstages;
-    auto k = gemv_kernel<WT, R, PAIRED>;
+    p.stage_rows = sh.R;
+    p.ring_offset = sh.ring_offset;
+    auto k = gemv_kernel<WT, KMAX, RS, PAIRED>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sh.smem);
     if (e != cudaSuccess) return e;
     return launch_ex(k, dim3(sh.grid), dim3(kGemvThreads), sh.smem, s, pdl, p);
 }
 
-// weights int8 (w_i8) or f32; returns the shape used through *out_shape
+template <typename WT, int KMAX, bool PAIRED>
+inline cudaError_t launch_gemv_r(const GemvParams& p, const GemvShape& sh, cudaStream_t s, bool pdl) {
+    if constexpr (KMAX > 1) {               // rows over 4 KB: at most 2 rows fit a 16 KB stage
+        if (sh.R == 1) return launch_gemv_t<WT, KMAX, 1, PAIRED>(p, sh, s, pdl);
+        if (sh.R == 2) return launch_gemv_t<WT, KMAX, 2, PAIRED>(p, sh, s, pdl);
+        return cudaErrorInvalidValue;
+    }
+    switch (sh.R) {
+        case 1: return launch_gemv_t<WT, KMAX, 1, PAIRED>(p, sh, s, pdl);
+        case 2: return launch_gemv_t<WT, KMAX, 2, PAIRED>(p, sh, s, pdl);
+        case 4: return launch_gemv_t<WT, KMAX, 4, PAIRED>(p, sh, s, pdl);
+        case 8: return launch_gemv_t<WT, KMAX, 8, PAIRED>(p, sh, s, pdl);
+        default:
+            if constexpr (PAIRED) return cudaErrorInvalidValue;
+            else return launch_gemv_t<WT, KMAX, 16, PAIRED>(p, sh, s, pdl);
+    }
+}
+
+// weights int8 (w_i8) or f32; rows up to kGemvMaxK*256 16-byte blocks long
 inline cudaError_t launch_gemv(const GemvParams& p, bool w_i8, cudaStream_t s, bool pdl,
-                               int grid_cap, int min_r = 1, GemvShape* out_shape = nullptr) {
-    const GemvShape sh = gemv_shape(p, w_i8 ? 1 : 4, min_r, grid_cap);
+                               int grid_cap, GemvShape* out_shape = nullptr) {
+    const GemvShape sh = gemv_shape(p, w_i8 ? 1 : 4, grid_cap);
     if (out_shape) *out_shape = sh;
+    if (sh.K < 1 || sh.K > kGemvMaxK || sh.smem > 227 * 1024) return cudaErrorInvalidValue;
     if (w_i8) {
         if (sh.paired) {
-            switch (sh.R) {
-                case 1: return launch_gemv_t<int8_t, 1, true>(p, sh, s, pdl);
-                case 2: return launch_gemv_t<int8_t, 2, true>(p, sh, s, pdl);
-                default: return launch_gemv_t<int8_t, 4, true>(p, sh, s, pdl);
-            }
+            if (sh.K <= 1) return launch_gemv_r<int8_t, 1, true>(p, sh, s, pdl);
+            return launch_gemv_r<int8_t, kGemvMaxK, true>(p, sh, s, pdl);
         }
-        switch (sh.R) {
-            case 1: return launch_gemv_t<int8_t, 1, false>(p, sh, s, pdl);
-            case 2: return launch_gemv_t<int8_t, 2, false>(p, sh, s, pdl);
-            case 4: return launch_gemv_t<int8_t, 4, false>(p, sh, s, pdl);
-            default: return launch_gemv_t<int8_t, 8, false>(p, sh, s, pdl);
-        }
+        if (sh.K <= 1) return launch_gemv_r<int8_t, 1, false>(p, sh, s, pdl);
+        return launch_gemv_r<int8_t, kGemvMaxK, false>(p, sh, s, pdl);
     }
     if (sh.paired) return cudaErrorInvalidValue;
-    switch (sh.R) {
-        case 1: return launch_gemv_t<float, 1, false>(p, sh, s, pdl);
-        case 2: return launch_gemv_t<float, 2, false>(p, sh, s, pdl);
-        case 4: return launch_gemv_t<float, 4, false>(p, sh, s, pdl);
-        default: return launch_gemv_t<float, 8, false>(p, sh, s, pdl);
-    }
+    if (sh.K <= 1) return launch_gemv_r<float, 1, false>(p, sh, s, pdl);
+    return launch_gemv_r<float, kGemvMaxK, false>(p, sh, s, pdl);
 }
 
 inline cudaError_t launch_attn(const AttnParams& p, cudaStream_t s, bool pdl) {

@@ -80,7 +80,8 @@ extern "C" int b2_attn_decode_static(const float* q, const float* K, const float
                                      int n_heads, int n_kv_heads, int d_head, int n, int max_seq,
                                      void* stream) {
     if (!q || !K || !V || !out || n_heads <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads ||
-        d_head <= 0 || d_head > 256 || n <= 0 || n > max_seq) {
+        d_head <= 0 || d_head > 256 || d_head % 4 || n <= 0 || n > max_seq ||
+        (reinterpret_cast<uintptr_t>(K) & 15) || (reinterpret_cast<uintptr_t>(V) & 15)) {
         b2_internal_set_error("b2_attn_decode_static: invalid arguments");
         return B2_E_INVALID;
     }

@@ -322,8 +322,9 @@ void assemble(b2_ctx* c, const b2json::Value& plan) {
             B.H = (int)b["n_heads"].as_int();
             B.KVH = (int)b["n_kv_heads"].as_int();
             B.dh = (int)b["d_head"].as_int();
-            if (B.H <= 0 || B.KVH <= 0 || B.H % B.KVH || B.dh <= 0 || B.dh > 256)
-                throw Err(B2_E_UNSUPPORTED, "attention heads/head_dim not supported");
+            if (B.H <= 0 || B.KVH <= 0 || B.H % B.KVH || B.dh <= 0 || B.dh > 256 || B.dh % 4)
+                throw Err(B2_E_UNSUPPORTED, "attention needs n_heads % n_kv_heads == 0 and head_dim "
+                                            "a multiple of 4 up to 256");
             if (B.rope && (B.dh % 2)) throw Err(B2_E_FORMAT, "RoPE needs an even head_dim");
             const int qd = B.H * B.dh, kd = B.KVH * B.dh;
             B.q = c->mat(b["q"].as_str(), qd, c->d);
@@ -496,7 +497,7 @@ int enqueue_step(b2_ctx* c, bool with_head, cudaStream_t s) {
             p.qout = c->q;
             p.kcache = B.K; p.vcache = B.V;
             p.max_seq = c->max_seq;
-            CK(launch_gemv(p, B.q.i8, s, pdl, c->sm_count, B.rope ? 2 : 1)); ++n;
+            CK(launch_gemv(p, B.q.i8, s, pdl, c->sm_count)); ++n;
 
             AttnParams a{};
             a.q = c->q; a.K = B.K; a.V = B.V; a.out = c->att;

@@ -130,7 +130,8 @@ int b2_layernorm(const float* x, const float* g, const float* b, float* y, int d
 int b2_rope_apply(float* v, const float* table, int pos, int d_head, int n_vec, void* stream);
 
 /* Decode attention for one step: q [n_heads*d_head] (rotated, pre-scaled),
- * K/V caches [n_kv_heads][max_seq][d_head], n valid keys, inactive tail = -60.
+ * K/V caches [n_kv_heads][max_seq][d_head] (16-byte aligned, d_head % 4 == 0,
+ * d_head <= 256), n valid keys, inactive tail = -60.
  * workspace: b2_attn_decode_workspace() bytes of device memory, zero-filled
  * before the first call (the kernel leaves it zero again).
  * Replaces: _gqa_score_head_i8 (attention_gqa_kv_i8.ari:97-117) /

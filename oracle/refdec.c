@@ -188,13 +188,9 @@ void b2o_quantize_rows(const float* W, int64_t m, int64_t n,
 }
 
 /* ------------------------------------------------------------------------
- * Dot products. Shared order (the CUDA GEMV uses the same):
- *  - the row is viewed as 16-byte blocks (16 int8 or 4 f32); bytes past n are 0
- *    and so is x there;
- *  - lane L in 0..31 owns blocks L, L+32, L+64, ... in ascending order and keeps
- *    four accumulators a[t&3] over element t of each block (fused multiply-add);
- *  - lane partial = (a0 + a1) + (a2 + a3);
- *  - XOR butterfly over lanes with strides 16, 8, 4, 2, 1: p[L] <- p[L] + p[L^s].
+ * 256-partial reduction (norms and dot products): partial j sits in warp j/32,
+ * lane j%32; each warp butterflies (XOR strides 16, 8, 4, 2, 1:
+ * p[L] <- p[L] + p[L^s]); warps combine as ((W0+W1)+(W2+W3)) + ((W4+W5)+(W6+W7)).
  * ------------------------------------------------------------------------ */
 static float butterfly32(float* p) {
     float t[32];
@@ -205,12 +201,27 @@ static float butterfly32(float* p) {
     return p[0];
 }
 
+static float reduce256(float* s) {
+    float W[8];
+    for (int w = 0; w < 8; ++w) W[w] = butterfly32(s + 32 * w);
+    return ((W[0] + W[1]) + (W[2] + W[3])) + ((W[4] + W[5]) + (W[6] + W[7]));
+}
+
+/* ------------------------------------------------------------------------
+ * Dot products. Shared order (the CUDA GEMV uses the same):
+ *  - the row is viewed as 16-byte blocks (16 int8 or 4 f32); bytes past n are 0
+ *    and so is x there;
+ *  - slot s in 0..255 owns blocks s, s+256, s+512, ... in ascending order and
+ *    keeps four accumulators a[t&3] over element t of each block (fused
+ *    multiply-add); slot partial = (a0 + a1) + (a2 + a3);
+ *  - the 256 slot partials go through reduce256().
+ * ------------------------------------------------------------------------ */
 float b2o_dot_i8(const int8_t* w, const float* x, int64_t n) {
     const int64_t nblk = (n + 15) / 16;
-    float p[32];
-    for (int L = 0; L < 32; ++L) {
+    float part[256];
+    for (int sl = 0; sl < 256; ++sl) {
         float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        for (int64_t b = L; b < nblk; b += 32) {
+        for (int64_t b = sl; b < nblk; b += 256) {
             for (int t = 0; t < 16; ++t) {
                 const int64_t k = 16 * b + t;
                 const float wv = k < n ? (float)w[k] : 0.0f;
@@ -218,17 +229,17 @@ float b2o_dot_i8(const int8_t* w, const float* x, int64_t n) {
                 a[t & 3] = fmaf(wv, xv, a[t & 3]);
             }
         }
-        p[L] = (a[0] + a[1]) + (a[2] + a[3]);
+        part[sl] = (a[0] + a[1]) + (a[2] + a[3]);
     }
-    return butterfly32(p);
+    return reduce256(part);
 }
 
 float b2o_dot_f32(const float* w, const float* x, int64_t n) {
     const int64_t nblk = (n + 3) / 4;
-    float p[32];
-    for (int L = 0; L < 32; ++L) {
+    float part[256];
+    for (int sl = 0; sl < 256; ++sl) {
         float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        for (int64_t b = L; b < nblk; b += 32) {
+        for (int64_t b = sl; b < nblk; b += 256) {
             for (int t = 0; t < 4; ++t) {
                 const int64_t k = 4 * b + t;
                 const float wv = k < n ? w[k] : 0.0f;
@@ -236,9 +247,9 @@ float b2o_dot_f32(const float* w, const float* x, int64_t n) {
                 a[t] = fmaf(wv, xv, a[t]);
             }
         }
-        p[L] = (a[0] + a[1]) + (a[2] + a[3]);
+        part[sl] = (a[0] + a[1]) + (a[2] + a[3]);
     }
-    return butterfly32(p);
+    return reduce256(part);
 }
 
 typedef struct { const void* W; int64_t ld; const float* scale; const float* x; int64_t n; float* y; } gemv_ctx;
@@ -264,17 +275,6 @@ void b2o_gemv_f32(const float* W, int64_t ld, const float* x,
                   int64_t m, int64_t n, float* y) {
     gemv_ctx g = {W, ld, NULL, x, n, y};
     parallel_for(m, gemv_f32_range, &g);
-}
-
-/* ------------------------------------------------------------------------
- * 256-partial reduction used by both norms: element i goes to partial i%256
- * (ascending i); partial j sits in warp j/32, lane j%32; each warp butterflies;
- * warps combine as ((W0+W1)+(W2+W3)) + ((W4+W5)+(W6+W7)).
- * ------------------------------------------------------------------------ */
-static float reduce256(float* s) {
-    float W[8];
-    for (int w = 0; w < 8; ++w) W[w] = butterfly32(s + 32 * w);
-    return ((W[0] + W[1]) + (W[2] + W[3])) + ((W[4] + W[5]) + (W[6] + W[7]));
 }
 
 /* rmsnorm_affine_f32 (aricode_pack.py:585-607): x * (1/sqrt(mean(x^2)+eps)), then * g */

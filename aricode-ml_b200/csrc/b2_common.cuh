@@ -173,13 +173,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the phase
+// completes or ~2 us pass, instead of spinning through issue slots
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity), "r"(2000u) : "memory");
+    return ok != 0;
+}
+
 // bounded wait on an mbarrier phase; false after ~1 s (caller reports the timeout)
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t it = 1;; ++it) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((it & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) return false;
+        if (mbar_try_wait_sleep(bar, parity)) return true;
+        if ((it & 7u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) return false;
     }
 }
 

@@ -273,7 +273,7 @@ inline cudaError_t launch_ex(K kernel, dim3 grid, dim3 block, size_t smem, cudaS
 }
 
 constexpr size_t kGemvSmemBudget = 200 * 1024;   // one 544-thread CTA per SM
-constexpr size_t kGemvStageTarget = 16 * 1024;
+constexpr size_t kGemvStageTarget = 32 * 1024;   // >= 16 KB: bulk copies stream at full rate
 constexpr int kGemvMaxK = 4;                       // 16-byte blocks per thread per row
 
 struct GemvShape {
@@ -304,7 +304,7 @@ inline GemvShape gemv_shape(const GemvParams& p, int esz, int grid_cap) {
     const int units = (total + unit - 1) / unit;
     sh.grid = units < grid_cap ? units : grid_cap;
     if (sh.grid < 1) sh.grid = 1;
-    // rows per stage: a power of two (<= 16, <= 8 when paired) keeping the stage near 16 KB
+    // rows per stage: a power of two (<= 16, <= 8 when paired) keeping the stage <= 32 KB
     int R = sh.paired ? 8 : 16;
     while (R > 1 && (size_t)R * row_bytes * nm > kGemvStageTarget) R >>= 1;
     sh.R = R;
@@ -338,9 +338,11 @@ inline cudaError_t launch_gemv_t(GemvParams p, const GemvShape& sh, cudaStream_t
 
 template <typename WT, int KMAX, bool PAIRED>
 inline cudaError_t launch_gemv_r(const GemvParams& p, const GemvShape& sh, cudaStream_t s, bool pdl) {
-    if constexpr (KMAX > 1) {               // rows over 4 KB: at most 2 rows fit a 16 KB stage
+    if constexpr (KMAX > 1) {               // rows over 4 KB: at most 4 rows fit a 32 KB stage
         if (sh.R == 1) return launch_gemv_t<WT, KMAX, 1, PAIRED>(p, sh, s, pdl);
         if (sh.R == 2) return launch_gemv_t<WT, KMAX, 2, PAIRED>(p, sh, s, pdl);
+        if constexpr (!PAIRED)
+            if (sh.R == 4) return launch_gemv_t<WT, KMAX, 4, PAIRED>(p, sh, s, pdl);
         return cudaErrorInvalidValue;
     }
     switch (sh.R) {

@@ -344,7 +344,7 @@ inline cudaError_t launch_gemv_r(const GemvParams& p, const GemvShape& sh, cudaS
         if constexpr (!PAIRED)
             if (sh.R == 4) return launch_gemv_t<WT, KMAX, 4, PAIRED>(p, sh, s, pdl);
         return cudaErrorInvalidValue;
-    }
+    } else {
     switch (sh.R) {
         case 1: return launch_gemv_t<WT, KMAX, 1, PAIRED>(p, sh, s, pdl);
         case 2: return launch_gemv_t<WT, KMAX, 2, PAIRED>(p, sh, s, pdl);
@@ -353,6 +353,7 @@ inline cudaError_t launch_gemv_r(const GemvParams& p, const GemvShape& sh, cudaS
         default:
             if constexpr (PAIRED) return cudaErrorInvalidValue;
             else return launch_gemv_t<WT, KMAX, 16, PAIRED>(p, sh, s, pdl);
+    }
     }
 }
 

@@ -261,12 +261,14 @@ def attn_workspace_bytes(n_heads, n_kv_heads, d_head, max_seq):
     return int(lib().b2_attn_decode_workspace(n_heads, n_kv_heads, d_head, max_seq))
 
 
-def attn_decode(q, K, V, n_heads, n_kv_heads, d_head, n, max_seq, workspace=None, stream=None):
+def attn_decode(q, K, V, n_heads, n_kv_heads, d_head, n, max_seq, workspace=None, out=None,
+                stream=None):
     import torch
     ws_bytes = attn_workspace_bytes(n_heads, n_kv_heads, d_head, max_seq)
     if workspace is None:
         workspace = torch.zeros(ws_bytes, dtype=torch.uint8, device=q.device)
-    out = torch.empty(n_heads * d_head, dtype=torch.float32, device=q.device)
+    if out is None:
+        out = torch.empty(n_heads * d_head, dtype=torch.float32, device=q.device)
     check(lib().b2_attn_decode(_ptr(q), _ptr(K), _ptr(V), _ptr(out), n_heads, n_kv_heads, d_head,
                                int(n), int(max_seq), _ptr(workspace), workspace.numel(),
                                _stream(stream)))

@@ -258,7 +258,7 @@ def main():
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "config": workload_config(args, plan),
         "roofline": {"bound": "hbm", "achieved": gemv["gbs"], "peak": hbm, "unit": "GB/s",
-                     "frac": gemv["gbs"] / hbm, "traffic": None,
+                     "frac": gemv["gbs"] / hbm, "traffic": gemv["traffic"],
                      "kernel": gemv["kernel"], "bytes_per_launch": gemv["bytes"],
                      "us_per_launch": gemv["us"], "peak_kind": f"{peak_kind} hbm_gbs"},
         "step_roofline": {"bound": "hbm", "bytes_per_token": bytes_tok, "achieved": step_gbs,
@@ -280,7 +280,9 @@ def main():
 
 def time_gemv(torch, rt, plan, stream, reps=3):
     """int8 GEMV alone on the FFN gate shape [d_ffn, d_model], cycling over one
-    weight matrix per layer so every launch streams from HBM."""
+    weight matrix per layer so every launch streams from HBM; all launches are
+    captured in one CUDA graph and timed with CUDA events around a replay."""
+    kb = importlib.import_module("aricode-ml_b200.kbench")
     blk = next(b for b in plan["blocks"] if b["type"] == "ffn")
     m, n = blk["d_ffn"], plan["d_model"]
     L = max(2, plan["n_layers"])
@@ -288,20 +290,24 @@ def time_gemv(torch, rt, plan, stream, reps=3):
     s = torch.rand(m, device="cuda") * 1e-3
     x = torch.randn(n, device="cuda")
     y = torch.empty(m, device="cuda")
-    for W in Ws:
-        rt.gemv_i8(W, s, x, y=y, stream=stream.cuda_stream)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(reps):
-        for W in Ws:
-            rt.gemv_i8(W, s, x, y=y, stream=stream.cuda_stream)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    us = e0.elapsed_time(e1) * 1000.0 / (reps * L)
+    us = kb.timed(torch, lambda W, h: rt.gemv_i8(W, s, x, y=y, stream=h), Ws, reps)
     nbytes = m * n + 4 * m + 4 * n + 4 * m
     del Ws
-    return {"kernel": f"gemv_i8 {m}x{n}", "us": us, "bytes": nbytes, "gbs": nbytes / (us * 1e-6) / 1e9}
+    return {"kernel": f"gemv_i8 {m}x{n}", "us": us, "bytes": nbytes,
+            "gbs": nbytes / (us * 1e-6) / 1e9, "traffic": profiled_traffic(m, n)}
+
+
+def profiled_traffic(m, n):
+    """DRAM bytes (read + write) per launch of the GEMV on this shape from the
+    committed ncu summary, or None when there is none."""
+    f = ROOT / "profiles" / f"gemv_i8_{m}x{n}.md"
+    try:
+        for line in f.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
 
 
 def time_e2e(torch, dec, prompt, new, stream, world, reps=2):

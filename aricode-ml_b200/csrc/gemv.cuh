@@ -139,11 +139,11 @@ __device__ __forceinline__ int total_rows(const GemvParams& p) {
     return t;
 }
 
-// rows [r0, r1) of CTA b: balanced in units of `unit` rows (2 keeps RoPE pairs together)
-__device__ __forceinline__ void cta_rows(int total, int unit, int& r0, int& r1) {
+// rows [r0, r1) of CTA b of nb: balanced in units of `unit` rows (2 keeps RoPE pairs together)
+__device__ __forceinline__ void cta_rows(int total, int unit, int b, int nb, int& r0, int& r1) {
     const long long units = (total + unit - 1) / unit;
-    const long long u0 = (long long)blockIdx.x * units / gridDim.x;
-    const long long u1 = (long long)(blockIdx.x + 1) * units / gridDim.x;
+    const long long u0 = (long long)b * units / nb;
+    const long long u1 = (long long)(b + 1) * units / nb;
     r0 = (int)(u0 * unit);
     r1 = (int)(u1 * unit < (long long)total ? u1 * unit : (long long)total);
 }
@@ -192,111 +192,108 @@ __device__ __forceinline__ void exchange_butterfly(float (&v)[N], int lane) {
 template <int N> struct Log2 { static constexpr int v = 1 + Log2<N / 2>::v; };
 template <> struct Log2<1> { static constexpr int v = 0; };
 
-template <typename WT, int KMAX, int RS, bool PAIRED>
-__global__ void __launch_bounds__(kGemvThreads, 1)
-gemv_kernel(const __grid_constant__ GemvParams p) {
-    constexpr int ESZ = (int)sizeof(WT);
-    constexpr int EPB = 16 / ESZ;                                // elements per 16-byte block
-    constexpr int NM = PAIRED ? 2 : 1;                           // matrices per stage
-    constexpr int NR = RS * NM;                                  // rows reduced together
-    constexpr int LG = Log2<NR>::v;
-    extern __shared__ __align__(128) unsigned char smem[];
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* empty = full + kGemvMaxStages;
-    float* red = reinterpret_cast<float*>(empty + kGemvMaxStages);      // 8 floats
-    float* part = reinterpret_cast<float*>(smem + 1024);                 // [rows_cta][NM][8]
-    const int ld = p.ld;
-    const uint32_t row_bytes = (uint32_t)ld * ESZ;
-    const uint32_t stage_bytes = (uint32_t)RS * row_bytes * NM;
-    unsigned char* ring = smem + p.ring_offset;
-    const int NS = p.nstages;
-    const int nblk = (int)(row_bytes >> 4);
 
-    const int tid = threadIdx.x;
-    const int warp = tid >> 5, lane = tid & 31;
-    int r0, r1;
-    cta_rows(total_rows(p), p.rope ? 2 : 1, r0, r1);
+// ============================================================================
+// Building blocks shared by the per-launch kernel below and the persistent
+// token kernel (token.cuh): the same code, so both give identical bits.
+// ============================================================================
 
-    if (NS < 2 * kGemvGroups || NS > kGemvMaxStages || NS % kGemvGroups || p.stage_rows != RS) {
-        if (tid == 0) set_err(p.err, B2_DEV_ERR_TIMEOUT);     // uniform per grid
-        return;
-    }
-    if (tid == 0) {
-        for (int s = 0; s < NS; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kGemvGroupWarps);
+template <typename WT> struct GemvElems { static constexpr int EPB = 16 / (int)sizeof(WT); };
+
+// EPB consecutive floats from v[i0 ..] (zeros past n), as 16-byte vector loads
+// when allowed; cg: through L2 (values written by other CTAs of the same kernel)
+template <int EPB>
+__device__ __forceinline__ void load_slice(const float* v, int i0, int n, bool vec, bool cg, float (&out)[EPB]) {
+    if (vec) {
+#pragma unroll
+        for (int q = 0; q < EPB / 4; ++q) {
+            const int i = i0 + 4 * q;
+            float4 t = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (i < n)
+                t = cg ? __ldcg(reinterpret_cast<const float4*>(v + i)) : __ldg(reinterpret_cast<const float4*>(v + i));
+            out[4 * q] = t.x; out[4 * q + 1] = t.y; out[4 * q + 2] = t.z; out[4 * q + 3] = t.w;
         }
-        fence_mbar_init();
-    }
-    __syncthreads();
-    pdl_launch_dependents();
-
-    if (warp == kGemvConsumerWarps) {
-        // ---------------- producer: one bulk copy (two when paired) per stage
-        if (lane == 0) {
-            int issued = 0;
-            bool ok = true;
-            int cur = r0;
-            for (int j = 0; cur < r1; ++j) {
-                const StageRows sr = next_stage(p, cur, r1, RS);
-                const int slot = j % NS, round = j / NS;
-                if (round > 0 && !mbar_wait_bounded(&empty[slot], (uint32_t)((round - 1) & 1))) {
-                    ok = false;
-                    break;
-                }
-                const uint32_t bytes = (uint32_t)sr.nr * row_bytes;
-                unsigned char* dst = ring + (size_t)slot * stage_bytes;
-                mbar_arrive_expect_tx(&full[slot], bytes * NM);
-                bulk_g2s(dst, reinterpret_cast<const unsigned char*>(p.W[sr.seg]) +
-                                  (size_t)sr.local * row_bytes, bytes, &full[slot]);
-                if constexpr (PAIRED)
-                    bulk_g2s(dst + (size_t)RS * row_bytes, reinterpret_cast<const unsigned char*>(p.W[1]) +
-                                                               (size_t)sr.local * row_bytes, bytes, &full[slot]);
-                ++issued;
-                cur += sr.nr;
-            }
-            if (!ok) set_err(p.err, B2_DEV_ERR_TIMEOUT);
-            // drain: no copy may still be in flight when the CTA exits
-            for (int j = max(0, issued - NS); j < issued; ++j)
-                if (!mbar_wait_bounded(&full[j % NS], (uint32_t)((j / NS) & 1))) {
-                    set_err(p.err, B2_DEV_ERR_TIMEOUT);
-                    break;
-                }
+    } else {
+#pragma unroll
+        for (int t = 0; t < EPB; ++t) {
+            const int i = i0 + t;
+            out[t] = i < n ? (cg ? __ldcg(v + i) : __ldg(v + i)) : 0.0f;
         }
-        return;
     }
+}
 
-    // ---------------- consumers: group g takes stages j with j % kGemvGroups == g
-    const int group = warp / kGemvGroupWarps;
-    const int gwarp = warp % kGemvGroupWarps;
-    const int slotid = tid % 256;                                // this thread's block slot
-    pdl_wait();
-    const bool active = p.st ? (*(volatile int*)&p.st->active != 0) : true;
-    const int pos = p.st ? *(volatile int*)&p.st->pos : p.pos_fixed;
+// Consumer prologue: this thread's slice of x (blocks slot, slot+256, ...), after
+// RMSNorm / LayerNorm when p.norm asks for it. Every consumer thread calls it (the
+// norm's reduction uses the consumer barrier). x was written by other CTAs of the
+// same token kernel, so it is read through L2 (ld.global.cg). With one block per
+// row, the slice and its norm gains are requested before the norm's own strided
+// values, so the prologue costs about one L2 round trip.
+template <typename WT, int KMAX>
+__device__ __forceinline__ void gemv_load_x(const GemvParams& p, float2 (&xr)[KMAX][GemvElems<WT>::EPB / 2],
+                                            float* red, int tid) {
+    constexpr int EPB = GemvElems<WT>::EPB;
     const int n = p.n;
-
-    // prologue: this thread's slice of x (blocks slot, slot+256, ...), normalised
+    const float* x = p.x;
+    const int slotid = tid % 256;
+    const int nblk = (int)(((size_t)p.ld * sizeof(WT)) >> 4);
+    const int K = (nblk + 255) / 256;
+    auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+    const bool vec = (n % 4) == 0 && al16(x) && (!p.ng || al16(p.ng)) && (!p.nb || al16(p.nb));
+    // 1. the slice (raw, into xr) and, for one block per row, its norm gains;
+    // with several blocks per row the slice is loaded after the norm (registers)
+    float gs[KMAX == 1 ? EPB : 1], bs[KMAX == 1 ? EPB : 1];
+    auto load_raw = [&]() {
+#pragma unroll
+        for (int k = 0; k < KMAX; ++k) {
+            const int b = slotid + 256 * k;
+            float t4[EPB];
+            if (k < K && b < nblk) load_slice<EPB>(x, b * EPB, n, vec, true, t4);
+            else {
+#pragma unroll
+                for (int t = 0; t < EPB; ++t) t4[t] = 0.0f;
+            }
+#pragma unroll
+            for (int t = 0; t < EPB / 2; ++t) xr[k][t] = make_float2(t4[2 * t], t4[2 * t + 1]);
+        }
+        if constexpr (KMAX == 1) {
+            const bool have = K >= 1 && slotid < nblk;
+            if (p.norm != NORM_NONE && have) load_slice<EPB>(p.ng, slotid * EPB, n, vec, false, gs);
+            if (p.norm == NORM_LN && have) load_slice<EPB>(p.nb, slotid * EPB, n, vec, false, bs);
+        }
+    };
+    if constexpr (KMAX == 1) load_raw();
+    // 2. the norm: 256 partials (thread t: elements t, t + 256, ... in order)
+    constexpr int NB = KMAX == 1 ? 16 : 4;           // loads in flight per batch (registers)
     float scale_a = 1.0f, shift_m = 0.0f;
-    if (p.norm == NORM_RMS) {
+    auto partial = [&](int kind, float mean) {       // 0: sum x^2, 1: sum x, 2: sum (x-mean)^2
         float a = 0.0f;
-        if (tid < 256)
-            for (int i = tid; i < n; i += 256) { const float v = p.x[i]; a = ffma(v, v, a); }
-        const float tot = consumer_reduce256(a, red, tid);
+        if (tid < 256) {
+            for (int base = tid; base < n; base += 256 * NB) {
+                float v[NB];
+#pragma unroll
+                for (int u = 0; u < NB; ++u) { const int i = base + 256 * u; v[u] = i < n ? __ldcg(x + i) : 0.0f; }
+#pragma unroll
+                for (int u = 0; u < NB; ++u) {
+                    if (base + 256 * u >= n) continue;
+                    if (kind == 0) a = ffma(v[u], v[u], a);
+                    else if (kind == 1) a = fadd(a, v[u]);
+                    else { const float dx = fsub(v[u], mean); a = ffma(dx, dx, a); }
+                }
+            }
+        }
+        return a;
+    };
+    if (p.norm == NORM_RMS) {
+        const float tot = consumer_reduce256(partial(0, 0.0f), red, tid);
         const float ms = fdiv(tot, (float)n);
         scale_a = fdiv(1.0f, __fsqrt_rn(fadd(ms, p.eps)));
     } else if (p.norm == NORM_LN) {
-        float a = 0.0f;
-        if (tid < 256)
-            for (int i = tid; i < n; i += 256) a = fadd(a, p.x[i]);
-        shift_m = fdiv(consumer_reduce256(a, red, tid), (float)n);
-        a = 0.0f;
-        if (tid < 256)
-            for (int i = tid; i < n; i += 256) { const float dx = fsub(p.x[i], shift_m); a = ffma(dx, dx, a); }
-        const float var = fdiv(consumer_reduce256(a, red, tid), (float)n);
+        shift_m = fdiv(consumer_reduce256(partial(1, 0.0f), red, tid), (float)n);
+        const float var = fdiv(consumer_reduce256(partial(2, shift_m), red, tid), (float)n);
         scale_a = fdiv(1.0f, __fsqrt_rn(fadd(var, p.eps)));
     }
-    const int K = (nblk + 255) / 256;
-    float2 xr[KMAX][EPB / 2];
+    if constexpr (KMAX > 1) load_raw();
+    // 3. normalise the slice
 #pragma unroll
     for (int k = 0; k < KMAX; ++k) {
         const int b = slotid + 256 * k;
@@ -305,75 +302,181 @@ gemv_kernel(const __grid_constant__ GemvParams p) {
             const int i = b * EPB + t;
             float v = 0.0f;
             if (k < K && b < nblk && i < n) {
-                const float xv = p.x[i];
-                if (p.norm == NORM_RMS) v = fmul(fmul(xv, scale_a), p.ng[i]);
+                const float xv = (t & 1) ? xr[k][t / 2].y : xr[k][t / 2].x;
+                float g = 0.0f, bb = 0.0f;
+                if (p.norm != NORM_NONE) {
+                    if constexpr (KMAX == 1) { g = gs[t]; bb = bs[t]; }
+                    else { g = p.ng[i]; if (p.norm == NORM_LN) bb = p.nb[i]; }
+                }
+                if (p.norm == NORM_RMS) v = fmul(fmul(xv, scale_a), g);
                 else if (p.norm == NORM_LN)
-                    v = (float)dadd(dmul((double)fmul(fsub(xv, shift_m), scale_a), (double)p.ng[i]),
-                                    (double)p.nb[i]);
+                    v = (float)dadd(dmul((double)fmul(fsub(xv, shift_m), scale_a), (double)g), (double)bb);
                 else v = xv;
             }
             if (t & 1) xr[k][t / 2].y = v;
             else xr[k][t / 2].x = v;
         }
     }
+}
 
-    // stream the stages: all rows of a stage at once, then one exchange butterfly
-    int cur = r0;
-    for (int j = 0; cur < r1; ++j) {
-        const StageRows sr = next_stage(p, cur, r1, RS);
-        if (j % kGemvGroups == group) {
-            const int slot = j % NS;
-            if (!mbar_wait_bounded(&full[slot], (uint32_t)((j / NS) & 1))) {
-                set_err(p.err, B2_DEV_ERR_TIMEOUT);
-                break;
-            }
-            const unsigned char* stage = ring + (size_t)slot * stage_bytes;
-            if (active) {
-                float2 a01[NR], a23[NR];
+// One stage: nr (<= RS) rows of each of the NM matrices at `stage` (row stride
+// row_bytes; the second matrix starts RS rows in). Writes this warp's sums to
+// part[(row * NM + m) * 8 + gwarp] for rows rl0 .. rl0 + nr - 1 of the CTA. Rows
+// are reduced four at a time (each row's butterfly is the same either way).
+template <typename WT, int KMAX, int RS, bool PAIRED>
+__device__ __forceinline__ void gemv_consume_stage(const unsigned char* stage, uint32_t row_bytes, int nblk,
+                                                   int slotid, int lane, int gwarp,
+                                                   const float2 (&xr)[KMAX][GemvElems<WT>::EPB / 2],
+                                                   float* part, int rl0, int nr) {
+    constexpr int ESZ = (int)sizeof(WT);
+    constexpr int NM = PAIRED ? 2 : 1;
+    constexpr int NR = RS * NM;
+    constexpr int NH = NR < 4 ? NR : 4;
+    constexpr int LG = Log2<NH>::v;
+    const int K = (nblk + 255) / 256;
 #pragma unroll
-                for (int r = 0; r < NR; ++r) a01[r] = a23[r] = make_float2(0.0f, 0.0f);
+    for (int h0 = 0; h0 < NR; h0 += NH) {
+        float2 a01[NH], a23[NH];
 #pragma unroll
-                for (int k = 0; k < KMAX; ++k) {
-                    const int b = slotid + 256 * k;
-                    if (k < K && b < nblk) {
+        for (int r = 0; r < NH; ++r) a01[r] = a23[r] = make_float2(0.0f, 0.0f);
 #pragma unroll
-                        for (int r = 0; r < NR; ++r) {
-                            // rows past sr.nr read stale (in-bounds) stage bytes; never stored
-                            const unsigned char* row = stage + (size_t)r * row_bytes + 16 * b;
-                            if constexpr (ESZ == 1) {
-                                const uint4 w = lds128(row);
-                                fma_word2(a01[r], a23[r], w.x ^ 0x80808080u, xr[k][0], xr[k][1]);
-                                fma_word2(a01[r], a23[r], w.y ^ 0x80808080u, xr[k][2], xr[k][3]);
-                                fma_word2(a01[r], a23[r], w.z ^ 0x80808080u, xr[k][4], xr[k][5]);
-                                fma_word2(a01[r], a23[r], w.w ^ 0x80808080u, xr[k][6], xr[k][7]);
-                            } else {
-                                const float4 w = lds128f(row);
-                                a01[r] = __ffma2_rn(make_float2(w.x, w.y), xr[k][0], a01[r]);
-                                a23[r] = __ffma2_rn(make_float2(w.z, w.w), xr[k][1], a23[r]);
-                            }
-                        }
+        for (int k = 0; k < KMAX; ++k) {
+            const int b = slotid + 256 * k;
+            if (k < K && b < nblk) {
+#pragma unroll
+                for (int r = 0; r < NH; ++r) {
+                    // rows past nr read stale (in-bounds) stage bytes; never stored
+                    const unsigned char* row = stage + (size_t)(h0 + r) * row_bytes + 16 * b;
+                    if constexpr (ESZ == 1) {
+                        const uint4 w = lds128(row);
+                        fma_word2(a01[r], a23[r], w.x ^ 0x80808080u, xr[k][0], xr[k][1]);
+                        fma_word2(a01[r], a23[r], w.y ^ 0x80808080u, xr[k][2], xr[k][3]);
+                        fma_word2(a01[r], a23[r], w.z ^ 0x80808080u, xr[k][4], xr[k][5]);
+                        fma_word2(a01[r], a23[r], w.w ^ 0x80808080u, xr[k][6], xr[k][7]);
+                    } else {
+                        const float4 w = lds128f(row);
+                        a01[r] = __ffma2_rn(make_float2(w.x, w.y), xr[k][0], a01[r]);
+                        a23[r] = __ffma2_rn(make_float2(w.z, w.w), xr[k][1], a23[r]);
                     }
                 }
-                float v[NR];
-#pragma unroll
-                for (int r = 0; r < NR; ++r)
-                    v[r] = fadd(fadd(a01[r].x, a01[r].y), fadd(a23[r].x, a23[r].y));
-                exchange_butterfly<NR>(v, lane);
-                if ((lane & ((32 >> LG) - 1)) == 0) {
-                    const int rr = lane >> (5 - LG);             // stage row (m * RS + r)
-                    const int m = rr / RS, r = rr % RS;
-                    if (r < sr.nr) part[((cur - r0 + r) * NM + m) * 8 + gwarp] = v[0];
-                }
             }
+        }
+        float v[NH];
+#pragma unroll
+        for (int r = 0; r < NH; ++r) v[r] = fadd(fadd(a01[r].x, a01[r].y), fadd(a23[r].x, a23[r].y));
+        exchange_butterfly<NH>(v, lane);
+        if ((lane & ((32 >> LG) - 1)) == 0) {
+            const int rr = h0 + (lane >> (5 - LG));        // stage row (m * RS + r)
+            const int m = rr / RS, r = rr % RS;
+            if (r < nr) part[((rl0 + r) * NM + m) * 8 + gwarp] = v[0];
+        }
+    }
+}
+
+// Producer: issue the stages of rows [r0, r1) into the ring, one bulk copy per
+// matrix per stage; j is the running stage index (slot j % NS, round j / NS).
+// With inflight > 0 (< NS), at most that many copies are outstanding: stage
+// j - inflight is complete before stage j is issued, which keeps the memory
+// queues short for everyone else's loads. Returns false on a timed-out wait.
+template <int NM>
+__device__ __forceinline__ bool gemv_produce(const GemvParams& p, int r0, int r1, int RS, uint32_t row_bytes,
+                                             unsigned char* ring, uint32_t slot_stride, int NS,
+                                             uint64_t* full, uint64_t* empty, int& j, int inflight = 0) {
+    int cur = r0;
+    while (cur < r1) {
+        const StageRows sr = next_stage(p, cur, r1, RS);
+        const int slot = j % NS, round = j / NS;
+        if (round > 0 && !mbar_wait_bounded(&empty[slot], (uint32_t)((round - 1) & 1))) return false;
+        if (inflight > 0 && j >= inflight &&
+            !mbar_wait_bounded(&full[(j - inflight) % NS], (uint32_t)(((j - inflight) / NS) & 1)))
+            return false;
+        const uint32_t bytes = (uint32_t)sr.nr * row_bytes;
+        unsigned char* dst = ring + (size_t)slot * slot_stride;
+        mbar_arrive_expect_tx(&full[slot], bytes * NM);
+        bulk_g2s(dst, reinterpret_cast<const unsigned char*>(p.W[sr.seg]) + (size_t)sr.local * row_bytes, bytes,
+                 &full[slot]);
+        if constexpr (NM == 2)
+            bulk_g2s(dst + (size_t)RS * row_bytes,
+                     reinterpret_cast<const unsigned char*>(p.W[1]) + (size_t)sr.local * row_bytes, bytes,
+                     &full[slot]);
+        ++j;
+        cur += sr.nr;
+    }
+    return true;
+}
+
+// Consumers: walk the same stages; group g takes stage j when (j % NS) % 2 == g
+// (NS even, so every slot belongs to one group and its phases advance in order).
+// compute = false only releases the slots. Returns false on a timed-out wait.
+template <typename WT, int KMAX, int RS, bool PAIRED>
+__device__ __forceinline__ bool gemv_consume(const GemvParams& p, int r0, int r1, const unsigned char* ring,
+                                             uint32_t slot_stride, int NS, uint64_t* full, uint64_t* empty,
+                                             int& j, int group, int gwarp, int lane, int slotid,
+                                             const float2 (&xr)[KMAX][GemvElems<WT>::EPB / 2], float* part,
+                                             bool compute) {
+    const uint32_t row_bytes = (uint32_t)p.ld * (uint32_t)sizeof(WT);
+    const int nblk = (int)(row_bytes >> 4);
+    int cur = r0;
+    while (cur < r1) {
+        const StageRows sr = next_stage(p, cur, r1, RS);
+        const int slot = j % NS;
+        if ((slot & 1) == group) {
+            if (!mbar_wait_bounded(&full[slot], (uint32_t)((j / NS) & 1))) return false;
+            if (compute)
+                gemv_consume_stage<WT, KMAX, RS, PAIRED>(ring + (size_t)slot * slot_stride, row_bytes, nblk, slotid,
+                                                         lane, gwarp, xr, part, cur - r0, sr.nr);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
         }
+        ++j;
         cur += sr.nr;
     }
-    consumer_bar();
-    if (!active) return;
+    return true;
+}
 
-    // ---------------- epilogue: thread per row (per row pair with RoPE)
+// Per-row epilogue inputs for rows r0 .. r0 + 511 of the CTA, loaded during the
+// prologue (their latency overlaps the x loads) and parked in shared memory as
+// epi[rl * 4 + k]: k = 0 scale (gate scale when paired), 1 bias (up scale when
+// paired), 2 RoPE cos or residual, 3 RoPE sin.
+struct EpiRow { float v[4]; };
+
+template <int ESZ, bool PAIRED>
+__device__ __forceinline__ EpiRow gemv_epi_load(const GemvParams& p, int r0, int r1, int pos, int tid) {
+    EpiRow e{{1.0f, 0.0f, 0.0f, 0.0f}};
+    if (tid >= r1 - r0) return e;
+    const int lrow = r0 + tid;
+    if constexpr (PAIRED) {
+        e.v[0] = p.S[0][lrow];
+        e.v[1] = p.S[1][lrow];
+    } else {
+        int seg, row;
+        seg_of(p, lrow, seg, row);
+        if constexpr (ESZ == 1) e.v[0] = p.S[seg][row];
+        if (p.bias[seg]) e.v[1] = p.bias[seg][row];
+        if (p.epi == EPI_QKV && p.rope && seg < 2 && !(row & 1)) {
+            const float* tr = p.rope_tab + (size_t)pos * p.dh + row % p.dh;
+            e.v[2] = tr[0];
+            e.v[3] = tr[1];
+        } else if (p.epi == EPI_RESID) {
+            e.v[2] = __ldcg(p.resid + row);
+        }
+    }
+    return e;
+}
+
+__device__ __forceinline__ void gemv_epi_store(const EpiRow& e, int nrows, int tid, float* epi) {
+    if (tid < nrows) *reinterpret_cast<float4*>(epi + tid * 4) = make_float4(e.v[0], e.v[1], e.v[2], e.v[3]);
+}
+
+// Epilogue: one consumer thread per row (per row pair with RoPE) finishes the rows
+// [r0, r1) from the warp sums in part[]. CTA `cta` of `ncta` takes part in the
+// grid-wide argmax (EPI_ARGMAX) through amax_* and the last-CTA ticket. epi, when
+// given, holds the preloaded per-row inputs of the first 512 rows.
+template <int ESZ, bool PAIRED>
+__device__ __forceinline__ void gemv_epilogue(const GemvParams& p, int r0, int r1, const float* part, int pos,
+                                              int tid, int cta, int ncta, const float* epi = nullptr) {
+    const int warp = tid >> 5, lane = tid & 31;
+    auto pre = [&](int rl) { return epi && rl < kGemvConsumerThreads; };
     float best_v = 0.0f;
     int best_i = 0x7fffffff;
     bool have_best = false;
@@ -382,8 +485,10 @@ gemv_kernel(const __grid_constant__ GemvParams p) {
     for (int rl = tid * step; rl < nrows; rl += kGemvConsumerThreads * step) {
         const int lrow = r0 + rl;
         if constexpr (PAIRED) {                              // EPI_SWIGLU
-            const float g = fmul(tree8(part + (rl * 2 + 0) * 8), p.S[0][lrow]);
-            const float u = fmul(tree8(part + (rl * 2 + 1) * 8), p.S[1][lrow]);
+            const float sg = pre(rl) ? epi[rl * 4] : p.S[0][lrow];
+            const float su = pre(rl) ? epi[rl * 4 + 1] : p.S[1][lrow];
+            const float g = fmul(tree8(part + (rl * 2 + 0) * 8), sg);
+            const float u = fmul(tree8(part + (rl * 2 + 1) * 8), su);
             p.y[lrow] = fmul(silu_f(g), u);
             continue;
         }
@@ -392,8 +497,8 @@ gemv_kernel(const __grid_constant__ GemvParams p) {
         float val[2] = {0.0f, 0.0f};
         for (int e = 0; e < step; ++e) {
             float v = tree8(part + (rl + e) * 8);
-            if constexpr (ESZ == 1) v = fmul(v, p.S[seg][row + e]);
-            if (p.bias[seg]) v = fadd(v, p.bias[seg][row + e]);
+            if constexpr (ESZ == 1) v = fmul(v, pre(rl + e) ? epi[(rl + e) * 4] : p.S[seg][row + e]);
+            if (p.bias[seg]) v = fadd(v, pre(rl + e) ? epi[(rl + e) * 4 + 1] : p.bias[seg][row + e]);
             else if constexpr (ESZ == 4) v = fadd(v, 0.0f);
             val[e] = v;
         }
@@ -403,7 +508,8 @@ gemv_kernel(const __grid_constant__ GemvParams p) {
                 // pair (2i, 2i+1): rows start even and segment sizes are even
                 const int hd = row % p.dh;
                 const float* tr = p.rope_tab + (size_t)pos * p.dh + hd;
-                const float c = tr[0], sn = tr[1];
+                const float c = pre(rl) ? epi[rl * 4 + 2] : tr[0];
+                const float sn = pre(rl) ? epi[rl * 4 + 3] : tr[1];
                 out[0] = fsub(fmul(val[0], c), fmul(val[1], sn));
                 out[1] = fadd(fmul(val[0], sn), fmul(val[1], c));
             }
@@ -420,7 +526,7 @@ gemv_kernel(const __grid_constant__ GemvParams p) {
                 }
             }
         } else if (p.epi == EPI_RESID) {
-            p.y[row] = fadd(val[0], p.resid[row]);
+            p.y[row] = fadd(val[0], pre(rl) ? epi[rl * 4 + 2] : __ldcg(p.resid + row));
         } else if (p.epi == EPI_GELU) {
             p.y[row] = gelu_f(val[0]);
         } else if (p.epi == EPI_ARGMAX) {
@@ -455,17 +561,17 @@ gemv_kernel(const __grid_constant__ GemvParams p) {
             float cv = 0.0f; int ci = 0x7fffffff; bool ch = false;
             for (int w = 0; w < kGemvConsumerWarps; ++w)
                 if (wh[w] && (!ch || amax_better(wv[w], wi[w], cv, ci))) { cv = wv[w]; ci = wi[w]; ch = true; }
-            p.amax_val[blockIdx.x] = cv;
-            p.amax_idx[blockIdx.x] = ch ? ci : 0x7fffffff;
+            p.amax_val[cta] = cv;
+            p.amax_idx[cta] = ch ? ci : 0x7fffffff;
             __threadfence();
             const unsigned t = atomicAdd(p.amax_count, 1u);
-            last = (t == gridDim.x - 1);
+            last = (t == (unsigned)ncta - 1);
         }
         consumer_bar();
         if (last && tid == 0) {
             __threadfence();
             float cv = 0.0f; int ci = 0x7fffffff; bool ch = false;
-            for (int c = 0; c < (int)gridDim.x; ++c) {
+            for (int c = 0; c < ncta; ++c) {
                 const int ii = __ldcg(p.amax_idx + c);
                 const float vv = __ldcg(p.amax_val + c);
                 if (ii != 0x7fffffff && (!ch || amax_better(vv, ii, cv, ci))) { cv = vv; ci = ii; ch = true; }
@@ -476,7 +582,7 @@ gemv_kernel(const __grid_constant__ GemvParams p) {
             if (p.st) {
                 StepState* st = p.st;
                 st->next_tok = tok;
-                if (st->pos >= st->prompt_len - 1) {
+                if (pos >= st->prompt_len - 1) {
                     if (st->eos >= 0 && tok == st->eos) {
                         st->active = 0;                          // EOS is not emitted
                     } else {
@@ -490,6 +596,78 @@ gemv_kernel(const __grid_constant__ GemvParams p) {
             __threadfence();
         }
     }
+}
+
+// ============================================================================
+// Per-launch GEMV kernel (one kernel per projection; kernel-level C ABI and the
+// per-layer decode path).
+// ============================================================================
+template <typename WT, int KMAX, int RS, bool PAIRED>
+__global__ void __launch_bounds__(kGemvThreads, 1)
+gemv_kernel(const __grid_constant__ GemvParams p) {
+    constexpr int ESZ = (int)sizeof(WT);
+    constexpr int NM = PAIRED ? 2 : 1;
+    extern __shared__ __align__(128) unsigned char smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + kGemvMaxStages;
+    float* red = reinterpret_cast<float*>(empty + kGemvMaxStages);      // 8 floats
+    float* part = reinterpret_cast<float*>(smem + 1024);                 // [rows_cta][NM][8]
+    const uint32_t row_bytes = (uint32_t)p.ld * ESZ;
+    const uint32_t stage_bytes = (uint32_t)RS * row_bytes * NM;
+    unsigned char* ring = smem + p.ring_offset;
+    const int NS = p.nstages;
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    int r0, r1;
+    cta_rows(total_rows(p), p.rope ? 2 : 1, blockIdx.x, gridDim.x, r0, r1);
+
+    if (NS < 2 * kGemvGroups || NS > kGemvMaxStages || NS % kGemvGroups || p.stage_rows != RS) {
+        if (tid == 0) set_err(p.err, B2_DEV_ERR_TIMEOUT);     // uniform per grid
+        return;
+    }
+    if (tid == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kGemvGroupWarps);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+    pdl_launch_dependents();
+
+    if (warp == kGemvConsumerWarps) {
+        // producer: its copies start before griddepcontrol.wait (weights do not
+        // depend on the previous kernel)
+        if (lane == 0) {
+            int j = 0;
+            if (!gemv_produce<NM>(p, r0, r1, RS, row_bytes, ring, stage_bytes, NS, full, empty, j))
+                set_err(p.err, B2_DEV_ERR_TIMEOUT);
+            // drain: no copy may still be in flight when the CTA exits
+            for (int i = max(0, j - NS); i < j; ++i)
+                if (!mbar_wait_bounded(&full[i % NS], (uint32_t)((i / NS) & 1))) {
+                    set_err(p.err, B2_DEV_ERR_TIMEOUT);
+                    break;
+                }
+        }
+        return;
+    }
+
+    const int group = warp / kGemvGroupWarps;
+    const int gwarp = warp % kGemvGroupWarps;
+    pdl_wait();
+    const bool active = p.st ? (*(volatile int*)&p.st->active != 0) : true;
+    const int pos = p.st ? *(volatile int*)&p.st->pos : p.pos_fixed;
+
+    float2 xr[KMAX][GemvElems<WT>::EPB / 2];
+    gemv_load_x<WT, KMAX>(p, xr, red, tid);
+    int j = 0;
+    if (!gemv_consume<WT, KMAX, RS, PAIRED>(p, r0, r1, ring, stage_bytes, NS, full, empty, j, group, gwarp, lane,
+                                            tid % 256, xr, part, active))
+        set_err(p.err, B2_DEV_ERR_TIMEOUT);
+    consumer_bar();
+    if (!active) return;
+    gemv_epilogue<ESZ, PAIRED>(p, r0, r1, part, pos, tid, blockIdx.x, gridDim.x);
 }
 
 }  // namespace b2

@@ -23,7 +23,7 @@
 
 #include "../../include/b2dec.h"
 #include "json.h"
-#include "kernels.cuh"
+#include "token.cuh"
 
 using namespace b2;
 
@@ -155,6 +155,19 @@ struct b2_ctx {
     cudaGraphExec_t g_prefill = nullptr, g_decode = nullptr;
     int kernels_prefill = 0, kernels_decode = 0;
     bool pdl = true;               // programmatic dependent launch between kernels
+    // persistent token kernel (token.cuh): one launch per step
+    bool token = false;
+    int token_vs = 0;              // compiled variant set (0 int8 only, 1 int8 + f32)
+    TkPhase* d_phases = nullptr;   // [prefill phases][decode phases]
+    int nph_prefill = 0, nph_decode = 0;
+    unsigned* tk_bar = nullptr;    // grid-barrier counters, zero between launches
+    int n_attn_cnt = 0;
+    int tk_ns = 0, tk_ring_offset = 0;
+    size_t tk_smem = 0;
+    std::string token_why;         // why the per-layer kernels are used instead
+    unsigned long long* d_trace = nullptr;   // token-kernel timeline (B2_TK_TRACE)
+    std::string trace_path;
+    std::vector<int> trace_kinds;  // per phase of both tables: kind, or 10 + GEMV variant
     int host_step = 0;
 
     ~b2_ctx() {
@@ -164,6 +177,8 @@ struct b2_ctx {
         if (d_weights) cudaFree(d_weights);
         if (d_kv) cudaFree(d_kv);
         if (d_work) cudaFree(d_work);
+        if (d_phases) cudaFree(d_phases);
+        if (d_trace) cudaFree(d_trace);
         if (h_st) cudaFreeHost(h_st);
         if (own_stream && stream) cudaStreamDestroy(stream);
         if (cap_stream) cudaStreamDestroy(cap_stream);
@@ -413,11 +428,12 @@ void assemble(b2_ctx* c, const b2json::Value& plan) {
     const size_t i_f = add((size_t)max_ffn * 4);
     const size_t i_logits = add((size_t)c->vocab * 4);
     const size_t i_part = add((size_t)max_H * c->attn_nsplit_max * (max_dh + 2) * 4);
-    const size_t i_acnt = add((size_t)max_KVH * 4);
+    const size_t i_acnt = add((size_t)std::max(max_H, max_KVH) * 4);   // per query head (token kernel)
     const size_t i_aval = add((size_t)c->sm_count * 4);
     const size_t i_aidx = add((size_t)c->sm_count * 4);
     const size_t i_anan = add(4);
     const size_t i_amcnt = add(4);
+    const size_t i_tkbar = add(8);
     const size_t i_st = add(sizeof(StepState));
     const size_t i_prompt = add((size_t)c->max_seq * 4);
     const size_t i_out = add((size_t)c->max_seq * 4);
@@ -437,6 +453,8 @@ void assemble(b2_ctx* c, const b2json::Value& plan) {
     c->amax_idx = reinterpret_cast<int*>(w + offs[i_aidx]);
     c->amax_v0nan = reinterpret_cast<int*>(w + offs[i_anan]);
     c->amax_cnt = reinterpret_cast<unsigned*>(w + offs[i_amcnt]);
+    c->tk_bar = reinterpret_cast<unsigned*>(w + offs[i_tkbar]);
+    c->n_attn_cnt = std::max(max_H, max_KVH);
     c->st = reinterpret_cast<StepState*>(w + offs[i_st]);
     c->prompt = reinterpret_cast<int*>(w + offs[i_prompt]);
     c->out_ids = reinterpret_cast<int*>(w + offs[i_out]);
@@ -462,15 +480,25 @@ void assemble(b2_ctx* c, const b2json::Value& plan) {
 }
 
 // ------------------------------------------------------------------ one step's launches
-int enqueue_step(b2_ctx* c, bool with_head, cudaStream_t s) {
-    int n = 0;
-    const bool pdl = c->pdl;
+// One operation of a step: what the per-layer path launches as one kernel and
+// the token kernel runs as one phase.
+struct Op {
+    int kind = TK_GEMV;
+    bool i8 = true;
+    GemvParams g{};
+    AttnParams a{};
+    EmbedParams e{};
+};
+
+std::vector<Op> build_ops(b2_ctx* c, bool with_head) {
+    std::vector<Op> ops;
+    auto gemv = [&](const GemvParams& g, bool i8) { Op o; o.kind = TK_GEMV; o.g = g; o.i8 = i8; ops.push_back(o); };
     EmbedParams ep{};
     ep.emb = c->emb.w; ep.emb_i8 = c->emb.i8; ep.emb_s = c->emb.s; ep.ld = c->emb.ld;
     ep.pos_tab = c->pos_tab; ep.max_pos = c->max_pos;
     ep.d = c->d; ep.vocab = c->vocab; ep.max_seq = c->max_seq;
     ep.prompt = c->prompt; ep.st = c->st; ep.x = c->x;
-    CK(launch_embed(ep, s, pdl)); ++n;
+    { Op o; o.kind = TK_EMBED; o.e = ep; ops.push_back(o); }
 
     for (const Block& B : c->blocks) {
         GemvParams p{};
@@ -497,7 +525,7 @@ int enqueue_step(b2_ctx* c, bool with_head, cudaStream_t s) {
             p.qout = c->q;
             p.kcache = B.K; p.vcache = B.V;
             p.max_seq = c->max_seq;
-            CK(launch_gemv(p, B.q.i8, s, pdl, c->sm_count)); ++n;
+            gemv(p, B.q.i8);
 
             AttnParams a{};
             a.q = c->q; a.K = B.K; a.V = B.V; a.out = c->att;
@@ -505,7 +533,7 @@ int enqueue_step(b2_ctx* c, bool with_head, cudaStream_t s) {
             a.H = B.H; a.KVH = B.KVH; a.dh = B.dh; a.max_seq = c->max_seq;
             a.nsplit_max = c->attn_nsplit_max;
             a.st = c->st; a.err = &c->st->err;
-            CK(launch_attn(a, s, pdl)); ++n;
+            { Op op; op.kind = TK_ATTN; op.a = a; ops.push_back(op); }
 
             GemvParams o{};
             o.st = c->st; o.err = &c->st->err;
@@ -513,14 +541,14 @@ int enqueue_step(b2_ctx* c, bool with_head, cudaStream_t s) {
             o.rows[0] = B.o.rows; o.nseg = 1; o.ld = B.o.ld;
             o.x = c->att; o.n = B.o.cols; o.norm = NORM_NONE;
             o.epi = EPI_RESID; o.y = c->x; o.resid = c->x;
-            CK(launch_gemv(o, B.o.i8, s, pdl, c->sm_count)); ++n;
+            gemv(o, B.o.i8);
         } else if (B.swiglu) {
             p.W[0] = B.w1.w; p.W[1] = B.w3.w;
             p.S[0] = B.w1.s; p.S[1] = B.w3.s;
             p.rows[0] = B.d_ffn; p.rows[1] = B.d_ffn;
             p.nseg = 2; p.paired = 1; p.ld = B.w1.ld;
             p.epi = EPI_SWIGLU; p.y = c->f;
-            CK(launch_gemv(p, true, s, pdl, c->sm_count)); ++n;
+            gemv(p, true);
 
             GemvParams dn{};
             dn.st = c->st; dn.err = &c->st->err;
@@ -528,12 +556,12 @@ int enqueue_step(b2_ctx* c, bool with_head, cudaStream_t s) {
             dn.rows[0] = c->d; dn.nseg = 1; dn.ld = B.w2.ld;
             dn.x = c->f; dn.n = B.d_ffn; dn.norm = NORM_NONE;
             dn.epi = EPI_RESID; dn.y = c->x; dn.resid = c->x;
-            CK(launch_gemv(dn, true, s, pdl, c->sm_count)); ++n;
+            gemv(dn, true);
         } else {
             p.W[0] = B.w1.w; p.S[0] = B.w1.s; p.bias[0] = B.b1;
             p.rows[0] = B.d_ffn; p.nseg = 1; p.ld = B.w1.ld;
             p.epi = EPI_GELU; p.y = c->f;
-            CK(launch_gemv(p, true, s, pdl, c->sm_count)); ++n;
+            gemv(p, true);
 
             GemvParams f2{};
             f2.st = c->st; f2.err = &c->st->err;
@@ -541,7 +569,7 @@ int enqueue_step(b2_ctx* c, bool with_head, cudaStream_t s) {
             f2.rows[0] = c->d; f2.nseg = 1; f2.ld = B.w2.ld;
             f2.x = c->f; f2.n = B.d_ffn; f2.norm = NORM_NONE;
             f2.epi = EPI_RESID; f2.y = c->x; f2.resid = c->x;
-            CK(launch_gemv(f2, true, s, pdl, c->sm_count)); ++n;
+            gemv(f2, true);
         }
     }
     if (with_head) {
@@ -554,9 +582,152 @@ int enqueue_step(b2_ctx* c, bool with_head, cudaStream_t s) {
         h.epi = EPI_ARGMAX; h.y = c->logits;
         h.amax_val = c->amax_val; h.amax_idx = c->amax_idx; h.amax_v0nan = c->amax_v0nan;
         h.amax_count = c->amax_cnt; h.out_ids = c->out_ids;
-        CK(launch_gemv(h, true, s, pdl, c->sm_count)); ++n;
+        gemv(h, true);
     }
-    return n;
+    return ops;
+}
+
+// per-layer path: one kernel per operation, chained by programmatic dependent launch
+int enqueue_step(b2_ctx* c, bool with_head, cudaStream_t s) {
+    const std::vector<Op> ops = build_ops(c, with_head);
+    for (const Op& o : ops) {
+        if (o.kind == TK_EMBED) CK(launch_embed(o.e, s, c->pdl));
+        else if (o.kind == TK_ATTN) CK(launch_attn(o.a, s, c->pdl));
+        else CK(launch_gemv(o.g, o.i8, s, c->pdl, c->sm_count));
+    }
+    return (int)ops.size();
+}
+
+
+// ------------------------------------------------------------------ token kernel
+// The phase of one operation; false (with the reason) when its shape is outside
+// what the token kernel is compiled for.
+bool tk_phase_of(const b2_ctx* c, const Op& o, TkPhase& T, size_t& part_bytes, std::string& why) {
+    T = TkPhase{};
+    T.kind = o.kind;
+    if (o.kind == TK_EMBED) {
+        T.e = o.e;
+        return true;
+    }
+    if (o.kind == TK_ATTN) {
+        T.a = o.a;
+        if (o.a.dh > 128 || o.a.dh % 4) { why = "head_dim above 128"; return false; }
+        if (c->attn_nsplit_max > kTkMaxSplits) { why = "max_seq above 16384"; return false; }
+        return true;
+    }
+    T.g = o.g;
+    const GemvParams& g = o.g;
+    const size_t row_bytes = (size_t)g.ld * (o.i8 ? 1 : 4);
+    const int K = (int)((row_bytes / 16 + 255) / 256);
+    if (K < 1 || K > 3) { why = "weight rows longer than 12 KB"; return false; }
+    const bool paired = g.paired != 0;
+    if (o.i8) {
+        if (K == 1) { T.variant = paired ? TV_I8_K1_R4_P : TV_I8_K1_R8; T.rs = paired ? 4 : 8; }
+        else { T.variant = paired ? TV_I8_K3_R1_P : TV_I8_K3_R2; T.rs = paired ? 1 : 2; }
+    } else {
+        if (paired) { why = "paired f32 weights"; return false; }
+        if (K == 1) { T.variant = TV_F32_K1_R8; T.rs = 8; }
+        else { T.variant = TV_F32_K3_R2; T.rs = 2; }
+    }
+    if ((size_t)T.rs * row_bytes * (paired ? 2 : 1) > kTkSlotBytes) { why = "stage above 32 KB"; return false; }
+    T.unit = g.rope ? 2 : 1;
+    long long total = paired ? g.rows[0] : 0;
+    if (!paired)
+        for (int k = 0; k < g.nseg; ++k) total += g.rows[k];
+    const long long units = (total + T.unit - 1) / T.unit;
+    const long long rows_cta = (units + c->sm_count - 1) / c->sm_count * T.unit;
+    part_bytes = std::max(part_bytes, (size_t)rows_cta * ((paired ? 2 : 1) * 8 + 4) * sizeof(float));
+    return true;
+}
+
+template <int VS>
+bool tk_prepare_kernel(b2_ctx* c) {
+    CK(cudaFuncSetAttribute(token_kernel<VS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c->tk_smem));
+    int per_sm = 0;
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, token_kernel<VS>, kTkThreads, c->tk_smem));
+    return per_sm >= 1;
+}
+
+// Build both phase tables (prefill: no LM head; decode: with it) and size the
+// kernel's shared memory; leaves c->token false with c->token_why otherwise.
+void setup_token(b2_ctx* c) {
+    c->token = false;
+    const char* env = std::getenv("B2_TOKEN_KERNEL");
+    if (!env || env[0] != '1') { c->token_why = "token kernel not requested (B2_TOKEN_KERNEL=1)"; return; }
+    int coop = 0;
+    CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->device));
+    if (!coop) { c->token_why = "no cooperative launch"; return; }
+    std::vector<TkPhase> ph;
+    size_t part = 0;
+    std::string why;
+    bool f32 = false;
+    for (int head = 0; head < 2; ++head) {
+        for (const Op& o : build_ops(c, head == 1)) {
+            TkPhase T;
+            if (!tk_phase_of(c, o, T, part, why)) { c->token_why = why; return; }
+            if (T.kind == TK_GEMV && T.variant >= TV_F32_K1_R8) f32 = true;
+            ph.push_back(T);
+        }
+        if (head == 0) c->nph_prefill = (int)ph.size();
+        else c->nph_decode = (int)ph.size() - c->nph_prefill;
+    }
+    const size_t ring_off = (kTkPartOffset + part + 127) & ~(size_t)127;
+    const size_t smem_max = 226 * 1024;             // dynamic; the static argmax slots need the rest
+    if (ring_off + 4 * (size_t)kTkSlotBytes > smem_max) { c->token_why = "too many rows per CTA"; return; }
+    int ns = (int)((smem_max - ring_off) / kTkSlotBytes);
+    ns = std::min(ns, kTkMaxSlots) & ~1;
+    c->tk_ns = ns;
+    c->tk_ring_offset = (int)ring_off;
+    c->tk_smem = ring_off + (size_t)ns * kTkSlotBytes;
+    c->token_vs = f32 ? 1 : 0;
+    if (!(f32 ? tk_prepare_kernel<1>(c) : tk_prepare_kernel<0>(c))) {
+        c->token_why = "token kernel does not fit an SM";
+        return;
+    }
+    if (c->d_phases) { cudaFree(c->d_phases); c->d_phases = nullptr; }
+    if (cudaMalloc(&c->d_phases, ph.size() * sizeof(TkPhase)) != cudaSuccess)
+        throw Err(B2_E_OOM, "phase table allocation failed");
+    CK(cudaMemcpy(c->d_phases, ph.data(), ph.size() * sizeof(TkPhase), cudaMemcpyHostToDevice));
+    c->token = true;
+    c->token_why.clear();
+    const char* tr = std::getenv("B2_TK_TRACE");
+    if (tr && tr[0] && !c->d_trace) {
+        const size_t n = (size_t)std::max(c->nph_prefill, c->nph_decode) * c->sm_count * 4;
+        if (cudaMalloc(&c->d_trace, n * sizeof(unsigned long long)) != cudaSuccess)
+            throw Err(B2_E_OOM, "trace allocation failed");
+        CK(cudaMemset(c->d_trace, 0, n * sizeof(unsigned long long)));
+        c->trace_path = tr;
+        c->trace_kinds.clear();
+        for (const TkPhase& T : ph) c->trace_kinds.push_back(T.kind == TK_GEMV ? 10 + T.variant : T.kind);
+    }
+}
+
+// one step as one cooperative launch (all CTAs resident: the grid barriers need it)
+void launch_token(b2_ctx* c, bool with_head, cudaStream_t s) {
+    TkParams P{};
+    P.phases = c->d_phases + (with_head ? c->nph_prefill : 0);
+    P.nphases = with_head ? c->nph_decode : c->nph_prefill;
+    P.ns = c->tk_ns;
+    P.ring_offset = c->tk_ring_offset;
+    P.bar = c->tk_bar;
+    P.st = c->st;
+    P.prompt = c->prompt;
+    P.max_seq = c->max_seq;
+    P.max_pos = c->pos_tab ? c->max_pos : 0;
+    P.vocab = c->vocab;
+    P.trace = c->d_trace;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)c->sm_count);
+    cfg.blockDim = dim3(kTkThreads);
+    cfg.dynamicSmemBytes = c->tk_smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeCooperative;
+    at[0].val.cooperative = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    if (c->token_vs) CK(cudaLaunchKernelEx(&cfg, token_kernel<1>, P));
+    else CK(cudaLaunchKernelEx(&cfg, token_kernel<0>, P));
 }
 
 void capture_graphs_once(b2_ctx* c);
@@ -564,6 +735,17 @@ void capture_graphs_once(b2_ctx* c);
 void capture_graphs(b2_ctx* c) {
     const char* env = std::getenv("B2_NO_PDL");
     c->pdl = !(env && env[0] == '1');
+    setup_token(c);
+    if (c->token) {
+        try {
+            capture_graphs_once(c);
+            return;
+        } catch (const Err& e) {
+            cudaGetLastError();
+            c->token = false;
+            c->token_why = std::string("graph capture failed: ") + e.what();
+        }
+    }
     try {
         capture_graphs_once(c);
     } catch (const Err&) {
@@ -582,7 +764,12 @@ void capture_graphs_once(b2_ctx* c) {
         CK(cudaStreamBeginCapture(c->cap_stream, cudaStreamCaptureModeThreadLocal));
         int n = 0;
         try {
-            n = enqueue_step(c, head == 1, c->cap_stream);
+            if (c->token) {
+                launch_token(c, head == 1, c->cap_stream);
+                n = 1;
+            } else {
+                n = enqueue_step(c, head == 1, c->cap_stream);
+            }
         } catch (...) {
             cudaStreamEndCapture(c->cap_stream, &g);
             if (g) cudaGraphDestroy(g);
@@ -598,6 +785,14 @@ void capture_graphs_once(b2_ctx* c) {
     }
 }
 
+// grid-barrier and last-CTA counters back to zero (they are zero after every
+// completed step; a step that timed out may leave them set)
+void clear_tickets(b2_ctx* c, cudaStream_t s) {
+    CK(cudaMemsetAsync(c->tk_bar, 0, 2 * sizeof(unsigned), s));
+    CK(cudaMemsetAsync(c->amax_cnt, 0, sizeof(unsigned), s));
+    CK(cudaMemsetAsync(c->attn_cnt, 0, (size_t)c->n_attn_cnt * sizeof(unsigned), s));
+}
+
 void upload_state(b2_ctx* c, int step, int prompt_len, int max_new, int next_tok, int eos) {
     StepState& h = *c->h_st;
     std::memset(&h, 0, sizeof(h));
@@ -611,6 +806,7 @@ void upload_state(b2_ctx* c, int step, int prompt_len, int max_new, int next_tok
     h.eos = eos;
     h.err = 0;
     CK(cudaMemcpyAsync(c->st, c->h_st, sizeof(StepState), cudaMemcpyHostToDevice, c->stream));
+    clear_tickets(c, c->stream);
 }
 
 int fetch_state(b2_ctx* c) {
@@ -801,6 +997,23 @@ int create_common(b2_ctx** out, int device, const std::function<void(b2_ctx*)>& 
 
 }  // namespace
 
+// Timeline of the last token-kernel step (B2_TK_TRACE=<file>): "B2TRACE1", then
+// int32 nphases, ncta, the phase kinds of the decode table (0 embed, 2 attention,
+// 10 + GEMV variant), then u64 [nphases][ncta][4] global-timer stamps.
+void dump_trace(b2_ctx* c) {
+    const int nph = c->nph_decode, ncta = c->sm_count;
+    std::vector<unsigned long long> t((size_t)nph * ncta * 4);
+    if (cudaMemcpy(t.data(), c->d_trace, t.size() * 8, cudaMemcpyDeviceToHost) != cudaSuccess) return;
+    FILE* f = std::fopen(c->trace_path.c_str(), "wb");
+    if (!f) return;
+    std::fwrite("B2TRACE1", 1, 8, f);
+    std::fwrite(&nph, 4, 1, f);
+    std::fwrite(&ncta, 4, 1, f);
+    std::fwrite(c->trace_kinds.data() + c->nph_prefill, 4, (size_t)nph, f);
+    std::fwrite(t.data(), 8, t.size(), f);
+    std::fclose(f);
+}
+
 // message for b2_last_error(NULL, ...) from the context-free entry points
 void b2_internal_set_error(const std::string& msg) { g_last_create_error = msg; }
 
@@ -830,6 +1043,7 @@ int b2_destroy(b2_ctx* ctx) {
     if (!ctx) return B2_E_INVALID;
     cudaSetDevice(ctx->device);
     cudaStreamSynchronize(ctx->stream);
+    if (ctx->d_trace) dump_trace(ctx);
     delete ctx;
     return B2_OK;
 }
@@ -902,6 +1116,7 @@ int b2_set_position(b2_ctx* ctx, int pos, int32_t next_tok) {
     return guarded(ctx, [&] {
         if (pos < 0 || pos > ctx->max_seq || next_tok < 0 || next_tok >= ctx->vocab) return B2_E_INVALID;
         // enqueued on the stream (no host synchronisation): one tiny kernel
+        clear_tickets(ctx, ctx->stream);
         set_state_kernel<<<1, 1, 0, ctx->stream>>>(ctx->st, pos, pos, 1 << 30, next_tok, -1);
         CK(cudaGetLastError());
         ctx->host_step = pos;
@@ -961,6 +1176,7 @@ int b2_query(b2_ctx* ctx, const char* key, double* value) {
     else if (k == "device_err") *value = ctx->h_st->err;
     else if (k == "sm_count") *value = ctx->sm_count;
     else if (k == "pdl") *value = ctx->pdl ? 1 : 0;
+    else if (k == "token_kernel") *value = ctx->token ? 1 : 0;
     else return B2_E_INVALID;
     return B2_OK;
 }

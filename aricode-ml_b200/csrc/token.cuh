@@ -1,0 +1,570 @@
+// token.cuh — the persistent token kernel: one launch runs a whole decode step
+// (embedding, every sub-block, LM head + greedy argmax) on one CTA per SM.
+//
+// Why: a batch-1 step of a 7B model is 160 weight-streaming phases of 17-90 MB.
+// As separate kernels each pays a few microseconds of ring fill, prologue and
+// drain. Here the phases are a table walked by every CTA, and the producer warp
+// streams the CTA's weight rows of phase p+1 into the shared-memory ring while
+// the consumers still work on phase p or wait at the grid barrier. Weights do
+// not depend on the activations, so HBM does not wait for a phase boundary.
+//
+// Structure of a CTA (640 threads, ~208 KB shared memory):
+//   warpgroup 4    producer: one lane walks all phases, one 1-D bulk copy per
+//                  stage into a ring of NS 32 KB slots (mbarrier complete_tx), at
+//                  most kTkInflight copies outstanding; it also prefetches each
+//                  phase's small vectors (norm gains, scales, biases) into L2;
+//   warpgroups 0-3 consumers in two groups of 8 warps; slot s belongs to group
+//                  s & 1 in GEMV phases and to group (s / 2) & 1 in attention
+//                  phases (an item's K stage and V stage go to the same group);
+//                  between phases: consumer barrier + grid barrier (atomic
+//                  arrivals, acquire spin, bounded to 1 s).
+//
+// Phases (TkPhase):
+//   TK_EMBED  CTA 0 writes x = embedding row (+ learned position);
+//   TK_GEMV   the building blocks of gemv_kernel (gemv.cuh): prologue norm,
+//             stages, epilogue (residual, RoPE + KV append, SiLU*up, GELU, argmax);
+//   TK_ATTN   split-KV decode attention: item (query head h, 64-key split s) on
+//             CTA item % grid; the K chunk and V chunk arrive as two ring
+//             stages; the row of the current position (written by this step's
+//             Q/K/V phase) is read from global memory; the last item of a head
+//             combines the splits with the -60 tail. Arithmetic order as
+//             attn_decode_kernel (attn.cuh) and oracle/refdec.c attn_head().
+//
+// Every value is computed by the same code and in the same order as the
+// per-launch kernels, so results are bit-identical to them and to the oracle.
+#pragma once
+#include "kernels.cuh"
+
+namespace b2 {
+
+enum TkKind : int { TK_EMBED = 0, TK_GEMV = 1, TK_ATTN = 2 };
+// compiled GEMV shapes: weight type, 16-byte blocks per thread per row (1, or up
+// to 3: rows of at most 12 KB), rows per stage, paired (gate+up)
+enum TkVariant : int {
+    TV_I8_K1_R8 = 0,
+    TV_I8_K1_R4_P = 1,
+    TV_I8_K3_R2 = 2,
+    TV_I8_K3_R1_P = 3,
+    TV_F32_K1_R8 = 4,
+    TV_F32_K3_R2 = 5,
+};
+
+constexpr uint32_t kTkSlotBytes = 32 * 1024;
+constexpr int kTkMaxSlots = 6;
+constexpr int kTkInflight = 3;                    // bulk copies outstanding per CTA (< slots)
+constexpr int kTkMaxSplits = 256;                 // max_seq <= 16384
+constexpr int kTkGroupScratch = 64 + 4 + kTkMaxSplits;   // floats per consumer group
+constexpr int kTkScratchOffset = 256;             // after the mbarriers and flags
+constexpr int kTkPartOffset = 4608;               // >= kTkScratchOffset + 2 * kTkGroupScratch * 4
+// 640 threads: warpgroups 0-3 consume, warpgroup 4 produces (one lane works).
+// Launched at 96 registers a thread (61,440 per CTA); the producer warpgroup
+// hands registers back (setmaxnreg.dec) and the consumers take them
+// (setmaxnreg.inc): 4 x 128 x 112 + 128 x 32 = 61,440.
+constexpr int kTkThreads = kGemvConsumerThreads + 128;
+constexpr int kTkProducerRegs = 32;
+constexpr int kTkConsumerRegs = 112;
+static_assert(4 * 128 * kTkConsumerRegs + 128 * kTkProducerRegs <= kTkThreads * 96, "register split");
+
+struct TkPhase {
+    int kind;
+    int variant;        // TK_GEMV
+    int unit;           // rows per balancing unit (2 keeps RoPE pairs in one CTA)
+    int rs;             // rows per stage of the variant
+    GemvParams g;
+    AttnParams a;
+    EmbedParams e;
+};
+
+struct TkParams {
+    const TkPhase* phases;
+    int nphases;
+    int ns;             // ring slots (even, <= kTkMaxSlots)
+    int ring_offset;    // bytes (128-aligned)
+    unsigned* bar;      // [0] grid-barrier arrivals, [1] exits; zero between launches
+    StepState* st;
+    const int* prompt;
+    int max_seq, max_pos, vocab;
+    // optional timeline (nullptr: off): [phase][cta][4] global-timer stamps at the
+    // phase start (after the grid barrier), after the prologue, after the stages
+    // and after the epilogue
+    unsigned long long* trace;
+};
+
+__device__ __forceinline__ void tk_stamp(unsigned long long* tr, int k, int tid) {
+    if (tr && tid == 0) tr[k] = globaltimer_ns();
+}
+
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void group_bar(int group) {
+    asm volatile("bar.sync %0, 256;" ::"r"(2 + group) : "memory");
+}
+
+// Grid barrier among the consumers of all CTAs: every CTA adds one arrival and
+// waits until `target` arrivals are visible. Bounded: false after ~1 s, and at
+// once when this CTA has already failed (*abort set). The result is the same for
+// every consumer thread of the CTA.
+__device__ __forceinline__ bool tk_grid_sync(unsigned* ctr, unsigned target, int tid, volatile int* flag,
+                                             volatile int* abort) {
+    consumer_bar();
+    if (tid == 0) {
+        bool ok = *abort == 0;
+        if (ok) {
+            __threadfence();
+            atomicAdd(ctr, 1u);
+            if (ld_acquire_gpu(ctr) < target) {
+                const uint64_t t0 = globaltimer_ns();
+                for (uint32_t it = 1;; ++it) {
+                    __nanosleep(32);
+                    if (ld_acquire_gpu(ctr) >= target) break;
+                    if ((it & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) { ok = false; break; }
+                }
+            }
+            __threadfence();
+        }
+        *flag = ok ? 1 : 0;
+    }
+    consumer_bar();
+    const bool ok = *flag != 0;
+    consumer_bar();                                     // flag is rewritten by the next call
+    return ok;
+}
+
+// Wait for a ring stage with one decision for the whole consumer group: one thread
+// waits (bounded), the group learns the outcome, then every thread takes the
+// completed phase itself (returns at once) for its own acquire of the stage.
+__device__ __forceinline__ bool group_wait(uint64_t* bar, uint32_t parity, int group, int gt, volatile int* f) {
+    if (gt == 0) *f = mbar_wait_bounded(bar, parity) ? 1 : 0;
+    group_bar(group);
+    const bool ok = *f != 0;
+    group_bar(group);
+    if (ok) mbar_wait_bounded(bar, parity);
+    return ok;
+}
+
+// L2 prefetch of a small read-only vector range (16-byte granules inside the
+// 256-byte aligned tensors of the weight arena)
+__device__ __forceinline__ void tk_prefetch(const void* ptr, size_t bytes) {
+    if (!ptr || !bytes) return;
+    const uintptr_t a = reinterpret_cast<uintptr_t>(ptr) & ~(uintptr_t)15;
+    const uintptr_t e = (reinterpret_cast<uintptr_t>(ptr) + bytes + 15) & ~(uintptr_t)15;
+    bulk_prefetch_l2(reinterpret_cast<const void*>(a), (uint32_t)(e - a));
+}
+
+// Producer, before a GEMV phase's stages: bring the phase's small weight vectors
+// (norm gains, this CTA's scales and biases, the RoPE row) into L2, so that the
+// consumers' prologue and epilogue do not wait behind the weight stream in DRAM.
+__device__ __forceinline__ void tk_prefetch_vectors(const GemvParams& p, int r0, int r1, int pos, bool i8) {
+    if (r0 >= r1) return;
+    if (p.norm != NORM_NONE) tk_prefetch(p.ng, (size_t)p.n * 4);
+    if (p.norm == NORM_LN) tk_prefetch(p.nb, (size_t)p.n * 4);
+    if (p.paired) {
+        tk_prefetch(p.S[0] + r0, (size_t)(r1 - r0) * 4);
+        tk_prefetch(p.S[1] + r0, (size_t)(r1 - r0) * 4);
+        return;
+    }
+    int base = 0;
+    for (int sg = 0; sg < p.nseg; ++sg) {
+        const int lo = max(r0, base), hi = min(r1, base + p.rows[sg]);
+        if (lo < hi) {
+            if (i8) tk_prefetch(p.S[sg] + (lo - base), (size_t)(hi - lo) * 4);
+            if (p.bias[sg]) tk_prefetch(p.bias[sg] + (lo - base), (size_t)(hi - lo) * 4);
+        }
+        base += p.rows[sg];
+    }
+    if (p.epi == EPI_QKV && p.rope) tk_prefetch(p.rope_tab + (size_t)pos * p.dh, (size_t)p.dh * 4);
+}
+
+// --------------------------------------------------------------------- attention
+__device__ __forceinline__ int tk_attn_items(const AttnParams& a, int n, int& nsplit) {
+    nsplit = (n + kAttnChunk - 1) / kAttnChunk;
+    return a.H * nsplit;
+}
+
+// producer side: a padding stage keeps every item's K stage on an even index
+__device__ __forceinline__ bool tk_attn_produce(const AttnParams& a, int n, int cta, int ncta,
+                                                unsigned char* ring, int NS, uint64_t* full, uint64_t* empty,
+                                                int& j) {
+    int nsplit;
+    const int items = tk_attn_items(a, n, nsplit);
+    const int G = a.H / a.KVH, dh = a.dh;
+    if (j & 1) {
+        const int slot = j % NS, round = j / NS;
+        if (round > 0 && !mbar_wait_bounded(&empty[slot], (uint32_t)((round - 1) & 1))) return false;
+        mbar_arrive(&full[slot]);
+        ++j;
+    }
+    for (int it = cta; it < items; it += ncta) {
+        const int h = it / nsplit, s = it % nsplit, kvh = h / G;
+        const int j0 = s * kAttnChunk, len = min(kAttnChunk, n - j0);
+        const uint32_t bytes = (uint32_t)len * dh * 4;
+        const size_t off = ((size_t)kvh * a.max_seq + j0) * dh;
+        for (int kv = 0; kv < 2; ++kv) {
+            const int slot = j % NS, round = j / NS;
+            if (round > 0 && !mbar_wait_bounded(&empty[slot], (uint32_t)((round - 1) & 1))) return false;
+            if (j >= kTkInflight &&
+                !mbar_wait_bounded(&full[(j - kTkInflight) % NS], (uint32_t)(((j - kTkInflight) / NS) & 1)))
+                return false;
+            mbar_arrive_expect_tx(&full[slot], bytes);
+            bulk_g2s(ring + (size_t)slot * kTkSlotBytes, (kv ? a.V : a.K) + off, bytes, &full[slot]);
+            ++j;
+        }
+    }
+    return true;
+}
+
+// consumer side: the owning group of each item computes it; all walk j. Every
+// wait is decided once per group (group_wait), so a timeout ends the phase for
+// the whole group together.
+__device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, int cta, int ncta,
+                                                const unsigned char* ring, int NS, uint64_t* full,
+                                                uint64_t* empty, int& j, int group, int gwarp, int lane,
+                                                float* scr, volatile int* gflag) {
+    const int n = pos + 1;
+    int nsplit;
+    const int items = tk_attn_items(a, n, nsplit);
+    const int G = a.H / a.KVH, dh = a.dh;
+    const int gt = gwarp * 32 + lane;                   // thread index within the group
+    if (j & 1) {                                        // padding stage
+        const int slot = j % NS;
+        if ((slot & 1) == group) {
+            if (!group_wait(&full[slot], (uint32_t)((j / NS) & 1), group, gt, gflag)) return false;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+        ++j;
+    }
+    float* sc = scr;                  // [64] scores, then exp
+    float* ml = scr + 64;             // m, l, (int) last, L
+    float* wsm = scr + 68;            // [nsplit] combine weights
+    for (int it = cta; it < items; it += ncta, j += 2) {
+        const int slotk = j % NS, slotv = slotk + 1;
+        if (((slotk >> 1) & 1) != group) continue;
+        const int h = it / nsplit, s = it % nsplit, kvh = h / G;
+        const int j0 = s * kAttnChunk, len = min(kAttnChunk, n - j0);
+        const int jnew = pos - j0;                      // this step's row, if in the chunk
+        const float* knew = a.K + ((size_t)kvh * a.max_seq + pos) * dh;
+        const float* vnew = a.V + ((size_t)kvh * a.max_seq + pos) * dh;
+        float qv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int d = lane + 32 * i;
+            qv[i] = d < dh ? __ldcg(a.q + (size_t)h * dh + d) : 0.0f;
+        }
+        if (!group_wait(&full[slotk], (uint32_t)((j / NS) & 1), group, gt, gflag)) return false;
+        const float* Ks = reinterpret_cast<const float*>(ring + (size_t)slotk * kTkSlotBytes);
+        // scores: warp gwarp takes keys gwarp + 8 i; lane L sums d = L, L + 32, ...
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int jj = gwarp + 8 * i;
+            float acc = 0.0f;
+            if (jj < len) {
+                const bool fresh = jj == jnew;
+                const float* kr = Ks + jj * dh;
+#pragma unroll
+                for (int ii = 0; ii < 4; ++ii) {
+                    const int d = lane + 32 * ii;
+                    if (d < dh) acc = ffma(qv[ii], fresh ? __ldcg(knew + d) : kr[d], acc);
+                }
+            }
+            v[i] = acc;
+        }
+        exchange_butterfly<8>(v, lane);
+        if ((lane & 3) == 0) {
+            const int jj = gwarp + 8 * (lane >> 2);
+            if (jj < len) sc[jj] = v[0];
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slotk]);
+        group_bar(group);
+        if (gwarp == 0) {                               // chunk max, exp, chunk sum
+            float m = -__int_as_float(0x7f800000);
+            bool any = false;
+            for (int jj = lane; jj < len; jj += 32) {
+                const float x = sc[jj];
+                m = any ? fmaxf(m, x) : x;
+                any = true;
+            }
+            for (int o = 16; o >= 1; o >>= 1) {
+                const float om = __shfl_xor_sync(0xffffffffu, m, o);
+                const int oa = __shfl_xor_sync(0xffffffffu, (int)any, o);
+                if (oa) { m = any ? fmaxf(m, om) : om; any = true; }
+            }
+            float acc = 0.0f;
+            for (int jj = lane; jj < len; jj += 32) {
+                const float e = exp_f(fsub(sc[jj], m));
+                sc[jj] = e;
+                acc = fadd(acc, e);
+            }
+            acc = butterfly32(acc);
+            if (lane == 0) { ml[0] = m; ml[1] = acc; }
+        }
+        group_bar(group);
+        // o_s[d] = sum_j e_j V[j][d], j ascending (one thread per d)
+        if (!group_wait(&full[slotv], (uint32_t)(((j + 1) / NS) & 1), group, gt, gflag)) return false;
+        const float* Vs = reinterpret_cast<const float*>(ring + (size_t)slotv * kTkSlotBytes);
+        const int stride = dh + 2;
+        float* pp = a.part + ((size_t)h * a.nsplit_max + s) * stride;
+        if (gt < dh) {
+            float acc = 0.0f;
+            for (int jj = 0; jj < len; ++jj)
+                acc = ffma(sc[jj], jj == jnew ? __ldcg(vnew + gt) : Vs[jj * dh + gt], acc);
+            pp[gt] = acc;
+            if (gt == 0) { pp[dh] = ml[0]; pp[dh + 1] = ml[1]; }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slotv]);
+        __threadfence();
+        group_bar(group);
+        if (gt == 0) {
+            const unsigned t = atomicAdd(a.counters + h, 1u);
+            reinterpret_cast<int*>(ml)[2] = (t == (unsigned)(nsplit - 1));
+        }
+        group_bar(group);
+        if (!reinterpret_cast<int*>(ml)[2]) continue;
+        // last split of head h: combine the splits and the -60 tail
+        __threadfence();
+        const float* base = a.part + (size_t)h * a.nsplit_max * stride;
+        if (gt == 0) {
+            float M = __ldcg(base + dh);
+            for (int t = 1; t < nsplit; ++t) M = fmaxf(M, __ldcg(base + (size_t)t * stride + dh));
+            if (n < a.max_seq) M = fmaxf(M, -60.0f);
+            float l = 0.0f;
+            for (int t = 0; t < nsplit; ++t) {
+                const float w = exp_f(fsub(__ldcg(base + (size_t)t * stride + dh), M));
+                wsm[t] = w;
+                l = ffma(__ldcg(base + (size_t)t * stride + dh + 1), w, l);
+            }
+            if (n < a.max_seq) l = ffma((float)(a.max_seq - n), exp_f(fsub(-60.0f, M)), l);
+            ml[3] = l;
+            a.counters[h] = 0u;
+        }
+        group_bar(group);
+        if (gt < dh) {
+            float o = 0.0f;
+            for (int t = 0; t < nsplit; ++t) o = ffma(__ldcg(base + (size_t)t * stride + gt), wsm[t], o);
+            a.out[(size_t)h * dh + gt] = fdiv(o, ml[3]);
+        }
+        group_bar(group);                               // scratch reused by the next item
+    }
+    return true;
+}
+
+// --------------------------------------------------------------------- GEMV phase
+template <typename WT, int KMAX, int RS, bool PAIRED>
+__device__ __forceinline__ bool tk_gemv(const GemvParams& p, int unit, int pos, const unsigned char* ring, int NS,
+                                        uint64_t* full, uint64_t* empty, int& j, int group, int gwarp, int lane,
+                                        int tid, float* red, float* part, int cta, int ncta,
+                                        unsigned long long* tr) {
+    int r0, r1;
+    cta_rows(total_rows(p), unit, cta, ncta, r0, r1);
+    // part[]: [rows][NM][8] warp sums, then epi[]: [rows][4] epilogue inputs
+    float* epi = part + (size_t)(r1 - r0) * (PAIRED ? 2 : 1) * 8;
+    const EpiRow er = gemv_epi_load<(int)sizeof(WT), PAIRED>(p, r0, r1, pos, tid);
+    float2 xr[KMAX][GemvElems<WT>::EPB / 2];
+    gemv_load_x<WT, KMAX>(p, xr, red, tid);
+    gemv_epi_store(er, r1 - r0, tid, epi);
+    tk_stamp(tr, 1, tid);
+    const bool ok = gemv_consume<WT, KMAX, RS, PAIRED>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group,
+                                                       gwarp, lane, tid % 256, xr, part, true);
+    consumer_bar();
+    tk_stamp(tr, 2, tid);
+    gemv_epilogue<(int)sizeof(WT), PAIRED>(p, r0, r1, part, pos, tid, cta, ncta, epi);
+    return ok;
+}
+
+// Variant sets compiled into one kernel: fewer shapes, fewer registers held
+// across the switch. VS 0: int8 weights only; VS 1: int8 and f32.
+template <int VS> struct TkSet { static constexpr bool f32 = VS == 1; };
+
+template <int VS>
+__device__ __forceinline__ bool tk_gemv_dispatch(const TkPhase& T, int pos, const unsigned char* ring, int NS,
+                                                 uint64_t* full, uint64_t* empty, int& j, int group, int gwarp,
+                                                 int lane, int tid, float* red, float* part, int cta, int ncta,
+                                                 unsigned long long* tr) {
+    const GemvParams& p = T.g;
+    switch (T.variant) {
+        case TV_I8_K1_R8:
+            return tk_gemv<int8_t, 1, 8, false>(p, T.unit, pos, ring, NS, full, empty, j, group, gwarp, lane, tid,
+                                                red, part, cta, ncta, tr);
+        case TV_I8_K1_R4_P:
+            return tk_gemv<int8_t, 1, 4, true>(p, T.unit, pos, ring, NS, full, empty, j, group, gwarp, lane, tid,
+                                               red, part, cta, ncta, tr);
+        case TV_I8_K3_R2:
+            return tk_gemv<int8_t, 3, 2, false>(p, T.unit, pos, ring, NS, full, empty, j, group, gwarp, lane, tid,
+                                                red, part, cta, ncta, tr);
+        case TV_I8_K3_R1_P:
+            return tk_gemv<int8_t, 3, 1, true>(p, T.unit, pos, ring, NS, full, empty, j, group, gwarp, lane, tid,
+                                               red, part, cta, ncta, tr);
+        default:
+            if constexpr (TkSet<VS>::f32) {
+                if (T.variant == TV_F32_K1_R8)
+                    return tk_gemv<float, 1, 8, false>(p, T.unit, pos, ring, NS, full, empty, j, group, gwarp, lane,
+                                                       tid, red, part, cta, ncta, tr);
+                return tk_gemv<float, 3, 2, false>(p, T.unit, pos, ring, NS, full, empty, j, group, gwarp, lane, tid,
+                                                   red, part, cta, ncta, tr);
+            }
+            return false;
+    }
+}
+
+// --------------------------------------------------------------------- the kernel
+template <int VS>
+__global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_constant__ TkParams P) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);                 // [kTkMaxSlots]
+    uint64_t* empty = full + 8;                                          // [kTkMaxSlots]
+    float* red = reinterpret_cast<float*>(smem + 128);                   // 8 floats
+    volatile int* flag = reinterpret_cast<volatile int*>(smem + 192);    // [0] grid sync, [2..3] groups
+    volatile int* abort = reinterpret_cast<volatile int*>(smem + 208);
+    float* scratch = reinterpret_cast<float*>(smem + kTkScratchOffset);
+    float* part = reinterpret_cast<float*>(smem + kTkPartOffset);
+    unsigned char* ring = smem + P.ring_offset;
+    const int NS = P.ns;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int cta = blockIdx.x, ncta = gridDim.x;
+    StepState* st = P.st;
+    int* err = &st->err;
+
+    // The step's inputs, read by every CTA before its first grid barrier; this
+    // launch writes the step state only after its last one.
+    const int active = *(volatile int*)&st->active;
+    if (!active) return;
+    const int pos = *(volatile int*)&st->step;
+    int bad = 0, tok = 0;
+    if (pos >= P.max_seq || (P.max_pos > 0 && pos >= P.max_pos)) {
+        bad = B2_DEV_ERR_KV_OVERFLOW;
+    } else {
+        const int plen = *(volatile int*)&st->prompt_len;
+        tok = pos < plen ? P.prompt[pos] : *(volatile int*)&st->next_tok;
+        if (tok < 0 || tok >= P.vocab) bad = B2_DEV_ERR_BAD_TOKEN;
+    }
+    if (bad) {
+        if (cta == 0 && tid == 0) { atomicCAS(err, 0, bad); st->active = 0; }
+        return;
+    }
+    if (NS < 4 || NS > kTkMaxSlots || (NS & 1)) {
+        if (cta == 0 && tid == 0) set_err(err, B2_DEV_ERR_TIMEOUT);
+        return;
+    }
+    if (tid == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kGemvGroupWarps);
+        }
+        fence_mbar_init();
+        *abort = 0;
+    }
+    __syncthreads();
+
+    if (warp >= kGemvConsumerWarps) {
+        // ---------------- producer: every phase's stages, in order, never waiting
+        // for a grid barrier
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kTkProducerRegs));
+        if (warp == kGemvConsumerWarps && lane == 0) {
+            int j = 0;
+            bool ok = true;
+            for (int ph = 0; ph < P.nphases && ok; ++ph) {
+                const TkPhase& T = P.phases[ph];
+                if (T.kind == TK_GEMV) {
+                    const GemvParams& p = T.g;
+                    int r0, r1;
+                    cta_rows(total_rows(p), T.unit, cta, ncta, r0, r1);
+                    const bool i8 = T.variant < TV_F32_K1_R8;
+                    const uint32_t row_bytes = (uint32_t)p.ld * (i8 ? 1u : 4u);
+                    tk_prefetch_vectors(p, r0, r1, pos, i8);
+                    ok = p.paired ? gemv_produce<2>(p, r0, r1, T.rs, row_bytes, ring, kTkSlotBytes, NS, full, empty, j,
+                                                    kTkInflight)
+                                  : gemv_produce<1>(p, r0, r1, T.rs, row_bytes, ring, kTkSlotBytes, NS, full, empty, j,
+                                                    kTkInflight);
+                } else if (T.kind == TK_ATTN) {
+                    ok = tk_attn_produce(T.a, pos + 1, cta, ncta, ring, NS, full, empty, j);
+                }
+            }
+            if (!ok) set_err(err, B2_DEV_ERR_TIMEOUT);
+            for (int i = max(0, j - NS); i < j; ++i)        // no copy in flight at exit
+                if (!mbar_wait_bounded(&full[i % NS], (uint32_t)((i / NS) & 1))) {
+                    set_err(err, B2_DEV_ERR_TIMEOUT);
+                    break;
+                }
+        }
+        return;
+    }
+
+    // ---------------- consumers: every thread goes through the same barriers;
+    // a failure anywhere in the CTA sets *abort and ends the walk for all of them
+    // at the next phase boundary
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kTkConsumerRegs));
+    const int group = warp / kGemvGroupWarps;
+    const int gwarp = warp % kGemvGroupWarps;
+    float* gscr = scratch + group * kTkGroupScratch;
+    volatile int* gflag = flag + 2 + group;
+    int j = 0;
+    unsigned arrivals = 0;
+    for (int ph = 0; ph < P.nphases; ++ph) {
+        const TkPhase& T = P.phases[ph];
+        if (ph > 0) {
+            arrivals += (unsigned)ncta;
+            if (!tk_grid_sync(P.bar, arrivals, tid, flag, abort)) {
+                if (tid == 0) *abort = 1;
+                break;
+            }
+        }
+        unsigned long long* tr = P.trace ? P.trace + ((size_t)ph * ncta + cta) * 4 : nullptr;
+        tk_stamp(tr, 0, tid);
+        bool ok = true;
+        if (T.kind == TK_EMBED) {
+            if (cta == 0) {
+                const EmbedParams& e = T.e;
+                for (int i = tid; i < e.d; i += kGemvConsumerThreads) {
+                    float v;
+                    if (e.emb_i8) {
+                        const int8_t q = reinterpret_cast<const int8_t*>(e.emb)[(size_t)tok * e.ld + i];
+                        v = fmul((float)q, e.emb_s[tok]);
+                    } else {
+                        v = reinterpret_cast<const float*>(e.emb)[(size_t)tok * e.ld + i];
+                    }
+                    if (e.pos_tab) v = fadd(v, e.pos_tab[(size_t)pos * e.d + i]);
+                    e.x[i] = v;
+                }
+            }
+        } else if (T.kind == TK_GEMV) {
+            ok = tk_gemv_dispatch<VS>(T, pos, ring, NS, full, empty, j, group, gwarp, lane, tid, red, part, cta,
+                                      ncta, tr);
+        } else {
+            tk_stamp(tr, 1, tid);
+            ok = tk_attn_consume(T.a, pos, cta, ncta, ring, NS, full, empty, j, group, gwarp, lane, gscr, gflag);
+            if (tr) {
+                consumer_bar();
+                tk_stamp(tr, 2, tid);
+            }
+        }
+        if (tr) {
+            consumer_bar();
+            tk_stamp(tr, 3, tid);
+        }
+        if (!ok) *abort = 1;
+    }
+    consumer_bar();
+    if (tid == 0) {
+        if (*abort) set_err(err, B2_DEV_ERR_TIMEOUT);
+        __threadfence();
+        const unsigned t = atomicAdd(P.bar + 1, 1u);
+        if (t == (unsigned)ncta - 1) {                  // every CTA is past its last barrier
+            if (!*abort) {
+                st->pos = pos;
+                st->step = pos + 1;
+            }
+            P.bar[0] = 0u;
+            P.bar[1] = 0u;
+            __threadfence();
+        }
+    }
+}
+
+}  // namespace b2

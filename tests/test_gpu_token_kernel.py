@@ -1,0 +1,90 @@
+"""The persistent token kernel (one cooperative launch per step) against the
+per-layer kernels and the oracle: greedy ids and logits bit-identical, across
+64-key split boundaries, for every synthetic architecture."""
+import os
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _pair(pkg, plan, seed=0):
+    """(token-kernel decoder, per-layer decoder) over the same synthetic weights."""
+    old = os.environ.get("B2_TOKEN_KERNEL")
+    try:
+        os.environ["B2_TOKEN_KERNEL"] = "1"
+        tk = pkg.runtime.Decoder.synthetic(plan, seed=seed)
+        os.environ["B2_TOKEN_KERNEL"] = "0"
+        pl = pkg.runtime.Decoder.synthetic(plan, seed=seed)
+    finally:
+        if old is None:
+            del os.environ["B2_TOKEN_KERNEL"]
+        else:
+            os.environ["B2_TOKEN_KERNEL"] = old
+    return tk, pl
+
+
+@pytest.mark.parametrize("name,layers,max_seq", [
+    ("tiny-llama", None, None),
+    ("gpt2-small", 2, None),
+    ("tinyllama-1.1b", 2, 256),
+    ("llama2-7b", 2, 160),
+])
+def test_token_kernel_matches_per_layer_kernels_and_oracle(pkg, oracle, name, layers, max_seq):
+    plan = pkg.synth.config_plan(name, n_layers=layers, max_seq=max_seq)
+    tk, pl = _pair(pkg, plan)
+    assert tk.query("token_kernel") == 1
+    assert tk.query("kernels_per_step") == 1
+    assert pl.query("token_kernel") == 0
+    om = oracle.OracleModel(plan, oracle.synth_tensors(plan, seed=0), threads=8)
+    rng = np.random.default_rng(7)
+    n = min(plan["max_seq"], 140)            # crosses the 64- and 128-key split boundaries
+    ids = rng.integers(0, plan["vocab"], n).tolist()
+    for t in ids:
+        r_tok, r_log = om.step(t)
+        a_tok, a_log = tk.step(t, want_logits=True)
+        b_tok, b_log = pl.step(t, want_logits=True)
+        assert a_tok == b_tok == r_tok
+        assert np.array_equal(a_log, r_log)
+        assert np.array_equal(b_log, r_log)
+    tk.close()
+    pl.close()
+
+
+def test_token_kernel_generate_and_async_decode(pkg, oracle):
+    plan = pkg.synth.config_plan("llama2-7b", n_layers=2, max_seq=200)
+    dec, other = _pair(pkg, plan, seed=5)
+    other.close()
+    assert dec.query("token_kernel") == 1
+    om = oracle.OracleModel(plan, oracle.synth_tensors(plan, seed=5), threads=8)
+    prompt = list(range(300, 430))
+    ref = om.generate(prompt, 60)
+    assert dec.generate(prompt, 60) == ref
+    # rewind into the middle of the generation and decode again on the device
+    dec.set_position(len(prompt), ref[0])
+    dec.decode_async(59)
+    dec.sync()
+    assert dec.read_output(59) == ref[1:]
+    dec.close()
+
+
+def test_token_kernel_full_size_llama2_7b_equals_per_layer_kernels(pkg):
+    """All 32 layers at the bench's positions: the two paths give the same bits."""
+    plan = pkg.synth.config_plan("llama2-7b")
+    tk, pl = _pair(pkg, plan, seed=0)
+    assert tk.query("token_kernel") == 1
+    prompt = list(range(1, 9))
+    outs = []
+    for dec in (tk, pl):
+        dec.reset()
+        dec.prefill(prompt[:-1])
+        logs = []
+        tok = prompt[-1]
+        for _ in range(4):
+            tok, lg = dec.step(tok, want_logits=True)
+            logs.append(lg)
+        outs.append(logs)
+        dec.close()
+    for a, b in zip(*outs):
+        assert np.array_equal(a, b)

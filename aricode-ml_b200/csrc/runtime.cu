@@ -162,7 +162,7 @@ struct b2_ctx {
     int nph_prefill = 0, nph_decode = 0;
     unsigned* tk_bar = nullptr;    // grid-barrier counters, zero between launches
     int n_attn_cnt = 0;
-    int tk_ns = 0, tk_ring_offset = 0;
+    int tk_ns = 0, tk_ring_offset = 0, tk_inflight = kTkInflight;
     size_t tk_smem = 0;
     std::string token_why;         // why the per-layer kernels are used instead
     unsigned long long* d_trace = nullptr;   // token-kernel timeline (B2_TK_TRACE)
@@ -679,6 +679,8 @@ void setup_token(b2_ctx* c) {
     c->tk_ns = ns;
     c->tk_ring_offset = (int)ring_off;
     c->tk_smem = ring_off + (size_t)ns * kTkSlotBytes;
+    const char* inf = std::getenv("B2_TK_INFLIGHT");          // tuning: 0 = no cap
+    c->tk_inflight = inf ? std::max(0, std::min(ns - 1, std::atoi(inf))) : std::min(kTkInflight, ns - 1);
     c->token_vs = f32 ? 1 : 0;
     if (!(f32 ? tk_prepare_kernel<1>(c) : tk_prepare_kernel<0>(c))) {
         c->token_why = "token kernel does not fit an SM";
@@ -692,7 +694,7 @@ void setup_token(b2_ctx* c) {
     c->token_why.clear();
     const char* tr = std::getenv("B2_TK_TRACE");
     if (tr && tr[0] && !c->d_trace) {
-        const size_t n = (size_t)std::max(c->nph_prefill, c->nph_decode) * c->sm_count * 4;
+        const size_t n = (size_t)std::max(c->nph_prefill, c->nph_decode) * c->sm_count * kTkStamps;
         if (cudaMalloc(&c->d_trace, n * sizeof(unsigned long long)) != cudaSuccess)
             throw Err(B2_E_OOM, "trace allocation failed");
         CK(cudaMemset(c->d_trace, 0, n * sizeof(unsigned long long)));
@@ -716,6 +718,7 @@ void launch_token(b2_ctx* c, bool with_head, cudaStream_t s) {
     P.max_pos = c->pos_tab ? c->max_pos : 0;
     P.vocab = c->vocab;
     P.trace = c->d_trace;
+    P.inflight = c->tk_inflight;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)c->sm_count);
     cfg.blockDim = dim3(kTkThreads);
@@ -998,17 +1001,20 @@ int create_common(b2_ctx** out, int device, const std::function<void(b2_ctx*)>& 
 }  // namespace
 
 // Timeline of the last token-kernel step (B2_TK_TRACE=<file>): "B2TRACE1", then
-// int32 nphases, ncta, the phase kinds of the decode table (0 embed, 2 attention,
-// 10 + GEMV variant), then u64 [nphases][ncta][4] global-timer stamps.
+// int32 nphases, ncta, stamps per phase, the phase kinds of the decode table (0
+// embed, 2 attention, 10 + GEMV variant), then u64 [nphases][ncta][stamps]
+// global-timer stamps (see TkParams::trace).
 void dump_trace(b2_ctx* c) {
     const int nph = c->nph_decode, ncta = c->sm_count;
-    std::vector<unsigned long long> t((size_t)nph * ncta * 4);
+    std::vector<unsigned long long> t((size_t)nph * ncta * kTkStamps);
     if (cudaMemcpy(t.data(), c->d_trace, t.size() * 8, cudaMemcpyDeviceToHost) != cudaSuccess) return;
     FILE* f = std::fopen(c->trace_path.c_str(), "wb");
     if (!f) return;
     std::fwrite("B2TRACE1", 1, 8, f);
     std::fwrite(&nph, 4, 1, f);
     std::fwrite(&ncta, 4, 1, f);
+    const int ns = kTkStamps;
+    std::fwrite(&ns, 4, 1, f);
     std::fwrite(c->trace_kinds.data() + c->nph_prefill, 4, (size_t)nph, f);
     std::fwrite(t.data(), 8, t.size(), f);
     std::fclose(f);

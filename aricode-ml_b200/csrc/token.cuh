@@ -51,7 +51,8 @@ enum TkVariant : int {
 
 constexpr uint32_t kTkSlotBytes = 32 * 1024;
 constexpr int kTkMaxSlots = 6;
-constexpr int kTkInflight = 3;                    // bulk copies outstanding per CTA (< slots)
+constexpr int kTkStamps = 8;                      // timeline slots per phase and CTA
+constexpr int kTkInflight = 3;                    // default bulk copies outstanding per CTA (< slots)
 constexpr int kTkMaxSplits = 256;                 // max_seq <= 16384
 constexpr int kTkGroupScratch = 64 + 4 + kTkMaxSplits;   // floats per consumer group
 constexpr int kTkScratchOffset = 256;             // after the mbarriers and flags
@@ -84,9 +85,10 @@ struct TkParams {
     StepState* st;
     const int* prompt;
     int max_seq, max_pos, vocab;
-    // optional timeline (nullptr: off): [phase][cta][4] global-timer stamps at the
-    // phase start (after the grid barrier), after the prologue, after the stages
-    // and after the epilogue
+    int inflight;       // bulk copies outstanding per CTA (1 .. ns - 1)
+    // optional timeline (nullptr: off): [phase][cta][kTkStamps] global-timer stamps
+    // at the phase start (after the grid barrier), when x is loaded, after the
+    // prologue, after the stages and after the epilogue
     unsigned long long* trace;
 };
 
@@ -188,7 +190,7 @@ __device__ __forceinline__ int tk_attn_items(const AttnParams& a, int n, int& ns
 // producer side: a padding stage keeps every item's K stage on an even index
 __device__ __forceinline__ bool tk_attn_produce(const AttnParams& a, int n, int cta, int ncta,
                                                 unsigned char* ring, int NS, uint64_t* full, uint64_t* empty,
-                                                int& j) {
+                                                int& j, int inflight) {
     int nsplit;
     const int items = tk_attn_items(a, n, nsplit);
     const int G = a.H / a.KVH, dh = a.dh;
@@ -206,8 +208,8 @@ __device__ __forceinline__ bool tk_attn_produce(const AttnParams& a, int n, int 
         for (int kv = 0; kv < 2; ++kv) {
             const int slot = j % NS, round = j / NS;
             if (round > 0 && !mbar_wait_bounded(&empty[slot], (uint32_t)((round - 1) & 1))) return false;
-            if (j >= kTkInflight &&
-                !mbar_wait_bounded(&full[(j - kTkInflight) % NS], (uint32_t)(((j - kTkInflight) / NS) & 1)))
+            if (inflight > 0 && j >= inflight &&
+                !mbar_wait_bounded(&full[(j - inflight) % NS], (uint32_t)(((j - inflight) / NS) & 1)))
                 return false;
             mbar_arrive_expect_tx(&full[slot], bytes);
             bulk_g2s(ring + (size_t)slot * kTkSlotBytes, (kv ? a.V : a.K) + off, bytes, &full[slot]);
@@ -249,12 +251,17 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
         const int jnew = pos - j0;                      // this step's row, if in the chunk
         const float* knew = a.K + ((size_t)kvh * a.max_seq + pos) * dh;
         const float* vnew = a.V + ((size_t)kvh * a.max_seq + pos) * dh;
-        float qv[4];
+        // loads that do not need the ring: q, and this step's K/V row when it falls
+        // in the chunk (issued before the waits, so their latency overlaps them)
+        const bool has_new = jnew >= 0 && jnew < len;
+        float qv[4], kn[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int d = lane + 32 * i;
             qv[i] = d < dh ? __ldcg(a.q + (size_t)h * dh + d) : 0.0f;
+            kn[i] = (has_new && d < dh) ? __ldcg(knew + d) : 0.0f;
         }
+        const float vn = (has_new && gt < dh) ? __ldcg(vnew + gt) : 0.0f;
         if (!group_wait(&full[slotk], (uint32_t)((j / NS) & 1), group, gt, gflag)) return false;
         const float* Ks = reinterpret_cast<const float*>(ring + (size_t)slotk * kTkSlotBytes);
         // scores: warp gwarp takes keys gwarp + 8 i; lane L sums d = L, L + 32, ...
@@ -269,7 +276,7 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
 #pragma unroll
                 for (int ii = 0; ii < 4; ++ii) {
                     const int d = lane + 32 * ii;
-                    if (d < dh) acc = ffma(qv[ii], fresh ? __ldcg(knew + d) : kr[d], acc);
+                    if (d < dh) acc = ffma(qv[ii], fresh ? kn[ii] : kr[d], acc);
                 }
             }
             v[i] = acc;
@@ -313,7 +320,7 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
         if (gt < dh) {
             float acc = 0.0f;
             for (int jj = 0; jj < len; ++jj)
-                acc = ffma(sc[jj], jj == jnew ? __ldcg(vnew + gt) : Vs[jj * dh + gt], acc);
+                acc = ffma(sc[jj], jj == jnew ? vn : Vs[jj * dh + gt], acc);
             pp[gt] = acc;
             if (gt == 0) { pp[dh] = ml[0]; pp[dh + 1] = ml[1]; }
         }
@@ -330,15 +337,22 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
         // last split of head h: combine the splits and the -60 tail
         __threadfence();
         const float* base = a.part + (size_t)h * a.nsplit_max * stride;
+        // every split's (m, l) in one parallel round of loads: m into wsm, l into sc
+        for (int t = gt; t < nsplit; t += 256) {
+            wsm[t] = __ldcg(base + (size_t)t * stride + dh);
+            if (t < 64) sc[t] = __ldcg(base + (size_t)t * stride + dh + 1);
+        }
+        group_bar(group);
         if (gt == 0) {
-            float M = __ldcg(base + dh);
-            for (int t = 1; t < nsplit; ++t) M = fmaxf(M, __ldcg(base + (size_t)t * stride + dh));
+            float M = wsm[0];
+            for (int t = 1; t < nsplit; ++t) M = fmaxf(M, wsm[t]);
             if (n < a.max_seq) M = fmaxf(M, -60.0f);
             float l = 0.0f;
             for (int t = 0; t < nsplit; ++t) {
-                const float w = exp_f(fsub(__ldcg(base + (size_t)t * stride + dh), M));
+                const float lt = t < 64 ? sc[t] : __ldcg(base + (size_t)t * stride + dh + 1);
+                const float w = exp_f(fsub(wsm[t], M));
                 wsm[t] = w;
-                l = ffma(__ldcg(base + (size_t)t * stride + dh + 1), w, l);
+                l = ffma(lt, w, l);
             }
             if (n < a.max_seq) l = ffma((float)(a.max_seq - n), exp_f(fsub(-60.0f, M)), l);
             ml[3] = l;
@@ -347,7 +361,15 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
         group_bar(group);
         if (gt < dh) {
             float o = 0.0f;
-            for (int t = 0; t < nsplit; ++t) o = ffma(__ldcg(base + (size_t)t * stride + gt), wsm[t], o);
+            for (int t0 = 0; t0 < nsplit; t0 += 8) {
+                float pv[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    pv[u] = t0 + u < nsplit ? __ldcg(base + (size_t)(t0 + u) * stride + gt) : 0.0f;
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    if (t0 + u < nsplit) o = ffma(pv[u], wsm[t0 + u], o);
+            }
             a.out[(size_t)h * dh + gt] = fdiv(o, ml[3]);
         }
         group_bar(group);                               // scratch reused by the next item
@@ -368,12 +390,13 @@ __device__ __forceinline__ bool tk_gemv(const GemvParams& p, int unit, int pos, 
     const EpiRow er = gemv_epi_load<(int)sizeof(WT), PAIRED>(p, r0, r1, pos, tid);
     float2 xr[KMAX][GemvElems<WT>::EPB / 2];
     gemv_load_x<WT, KMAX>(p, xr, red, tid);
-    gemv_epi_store(er, r1 - r0, tid, epi);
     tk_stamp(tr, 1, tid);
+    gemv_epi_store(er, r1 - r0, tid, epi);
+    tk_stamp(tr, 2, tid);
     const bool ok = gemv_consume<WT, KMAX, RS, PAIRED>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group,
                                                        gwarp, lane, tid % 256, xr, part, true);
     consumer_bar();
-    tk_stamp(tr, 2, tid);
+    tk_stamp(tr, 3, tid);
     gemv_epilogue<(int)sizeof(WT), PAIRED>(p, r0, r1, part, pos, tid, cta, ncta, epi);
     return ok;
 }
@@ -448,7 +471,7 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
         if (cta == 0 && tid == 0) { atomicCAS(err, 0, bad); st->active = 0; }
         return;
     }
-    if (NS < 4 || NS > kTkMaxSlots || (NS & 1)) {
+    if (NS < 4 || NS > kTkMaxSlots || (NS & 1) || P.inflight < 0 || P.inflight >= NS) {
         if (cta == 0 && tid == 0) set_err(err, B2_DEV_ERR_TIMEOUT);
         return;
     }
@@ -479,11 +502,11 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
                     const uint32_t row_bytes = (uint32_t)p.ld * (i8 ? 1u : 4u);
                     tk_prefetch_vectors(p, r0, r1, pos, i8);
                     ok = p.paired ? gemv_produce<2>(p, r0, r1, T.rs, row_bytes, ring, kTkSlotBytes, NS, full, empty, j,
-                                                    kTkInflight)
+                                                    P.inflight)
                                   : gemv_produce<1>(p, r0, r1, T.rs, row_bytes, ring, kTkSlotBytes, NS, full, empty, j,
-                                                    kTkInflight);
+                                                    P.inflight);
                 } else if (T.kind == TK_ATTN) {
-                    ok = tk_attn_produce(T.a, pos + 1, cta, ncta, ring, NS, full, empty, j);
+                    ok = tk_attn_produce(T.a, pos + 1, cta, ncta, ring, NS, full, empty, j, P.inflight);
                 }
             }
             if (!ok) set_err(err, B2_DEV_ERR_TIMEOUT);
@@ -515,7 +538,7 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
                 break;
             }
         }
-        unsigned long long* tr = P.trace ? P.trace + ((size_t)ph * ncta + cta) * 4 : nullptr;
+        unsigned long long* tr = P.trace ? P.trace + ((size_t)ph * ncta + cta) * kTkStamps : nullptr;
         tk_stamp(tr, 0, tid);
         bool ok = true;
         if (T.kind == TK_EMBED) {
@@ -538,15 +561,16 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
                                       ncta, tr);
         } else {
             tk_stamp(tr, 1, tid);
+            tk_stamp(tr, 2, tid);
             ok = tk_attn_consume(T.a, pos, cta, ncta, ring, NS, full, empty, j, group, gwarp, lane, gscr, gflag);
             if (tr) {
                 consumer_bar();
-                tk_stamp(tr, 2, tid);
+                tk_stamp(tr, 3, tid);
             }
         }
         if (tr) {
             consumer_bar();
-            tk_stamp(tr, 3, tid);
+            tk_stamp(tr, 4, tid);
         }
         if (!ok) *abort = 1;
     }

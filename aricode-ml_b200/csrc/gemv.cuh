@@ -228,7 +228,7 @@ __device__ __forceinline__ void load_slice(const float* v, int i0, int n, bool v
 // same token kernel, so it is read through L2 (ld.global.cg). With one block per
 // row, the slice and its norm gains are requested before the norm's own strided
 // values, so the prologue costs about one L2 round trip.
-template <typename WT, int KMAX>
+template <typename WT, int KMAX, bool EARLY = (KMAX == 1)>
 __device__ __forceinline__ void gemv_load_x(const GemvParams& p, float2 (&xr)[KMAX][GemvElems<WT>::EPB / 2],
                                             float* red, int tid) {
     constexpr int EPB = GemvElems<WT>::EPB;
@@ -239,9 +239,10 @@ __device__ __forceinline__ void gemv_load_x(const GemvParams& p, float2 (&xr)[KM
     const int K = (nblk + 255) / 256;
     auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
     const bool vec = (n % 4) == 0 && al16(x) && (!p.ng || al16(p.ng)) && (!p.nb || al16(p.nb));
-    // 1. the slice (raw, into xr) and, for one block per row, its norm gains;
-    // with several blocks per row the slice is loaded after the norm (registers)
-    float gs[KMAX == 1 ? EPB : 1], bs[KMAX == 1 ? EPB : 1];
+    // 1. the slice (raw, into xr) and the norm gains of its first block; EARLY
+    // requests them before the norm's loads (one round trip), otherwise after it
+    // (fewer registers live during the norm)
+    float gs[EPB], bs[EPB];
     auto load_raw = [&]() {
 #pragma unroll
         for (int k = 0; k < KMAX; ++k) {
@@ -255,13 +256,11 @@ __device__ __forceinline__ void gemv_load_x(const GemvParams& p, float2 (&xr)[KM
 #pragma unroll
             for (int t = 0; t < EPB / 2; ++t) xr[k][t] = make_float2(t4[2 * t], t4[2 * t + 1]);
         }
-        if constexpr (KMAX == 1) {
-            const bool have = K >= 1 && slotid < nblk;
-            if (p.norm != NORM_NONE && have) load_slice<EPB>(p.ng, slotid * EPB, n, vec, false, gs);
-            if (p.norm == NORM_LN && have) load_slice<EPB>(p.nb, slotid * EPB, n, vec, false, bs);
-        }
+        const bool have = K >= 1 && slotid < nblk;
+        if (p.norm != NORM_NONE && have) load_slice<EPB>(p.ng, slotid * EPB, n, vec, false, gs);
+        if (p.norm == NORM_LN && have) load_slice<EPB>(p.nb, slotid * EPB, n, vec, false, bs);
     };
-    if constexpr (KMAX == 1) load_raw();
+    if constexpr (EARLY) load_raw();
     // 2. the norm: 256 partials (thread t: elements t, t + 256, ... in order)
     constexpr int NB = KMAX == 1 ? 16 : 4;           // loads in flight per batch (registers)
     float scale_a = 1.0f, shift_m = 0.0f;
@@ -292,7 +291,7 @@ __device__ __forceinline__ void gemv_load_x(const GemvParams& p, float2 (&xr)[KM
         const float var = fdiv(consumer_reduce256(partial(2, shift_m), red, tid), (float)n);
         scale_a = fdiv(1.0f, __fsqrt_rn(fadd(var, p.eps)));
     }
-    if constexpr (KMAX > 1) load_raw();
+    if constexpr (!EARLY) load_raw();
     // 3. normalise the slice
 #pragma unroll
     for (int k = 0; k < KMAX; ++k) {
@@ -305,7 +304,7 @@ __device__ __forceinline__ void gemv_load_x(const GemvParams& p, float2 (&xr)[KM
                 const float xv = (t & 1) ? xr[k][t / 2].y : xr[k][t / 2].x;
                 float g = 0.0f, bb = 0.0f;
                 if (p.norm != NORM_NONE) {
-                    if constexpr (KMAX == 1) { g = gs[t]; bb = bs[t]; }
+                    if (k == 0) { g = gs[t]; bb = bs[t]; }
                     else { g = p.ng[i]; if (p.norm == NORM_LN) bb = p.nb[i]; }
                 }
                 if (p.norm == NORM_RMS) v = fmul(fmul(xv, scale_a), g);
@@ -371,6 +370,87 @@ __device__ __forceinline__ void gemv_consume_stage(const unsigned char* stage, u
             if (r < nr) part[((rl0 + r) * NM + m) * 8 + gwarp] = v[0];
         }
     }
+}
+
+// The same stage with its shape known only at run time (one compiled copy for
+// every row length up to KMAX blocks per thread, rows per stage and pairing):
+// NR = RS * NM rows at `stage`, reduced NH at a time; rows past NR are not read.
+// Each row's arithmetic is the one of gemv_consume_stage, so the bits are equal.
+template <typename WT, int KMAX, int NH>
+__device__ __forceinline__ void gemv_consume_stage_rt(const unsigned char* stage, uint32_t row_bytes, int nblk,
+                                                      int slotid, int lane, int gwarp,
+                                                      const float2 (&xr)[KMAX][GemvElems<WT>::EPB / 2],
+                                                      float* part, int rl0, int nr, int RS, int NM) {
+    constexpr int ESZ = (int)sizeof(WT);
+    constexpr int LG = Log2<NH>::v;
+    const int K = (nblk + 255) / 256;
+    const int NR = RS * NM;
+#pragma unroll 1
+    for (int h0 = 0; h0 < NR; h0 += NH) {
+        float2 a01[NH], a23[NH];
+#pragma unroll
+        for (int r = 0; r < NH; ++r) a01[r] = a23[r] = make_float2(0.0f, 0.0f);
+#pragma unroll
+        for (int k = 0; k < KMAX; ++k) {
+            const int b = slotid + 256 * k;
+            if (k < K && b < nblk) {
+#pragma unroll
+                for (int r = 0; r < NH; ++r) {
+                    if (h0 + r >= NR) break;
+                    const unsigned char* row = stage + (size_t)(h0 + r) * row_bytes + 16 * b;
+                    if constexpr (ESZ == 1) {
+                        const uint4 w = lds128(row);
+                        fma_word2(a01[r], a23[r], w.x ^ 0x80808080u, xr[k][0], xr[k][1]);
+                        fma_word2(a01[r], a23[r], w.y ^ 0x80808080u, xr[k][2], xr[k][3]);
+                        fma_word2(a01[r], a23[r], w.z ^ 0x80808080u, xr[k][4], xr[k][5]);
+                        fma_word2(a01[r], a23[r], w.w ^ 0x80808080u, xr[k][6], xr[k][7]);
+                    } else {
+                        const float4 w = lds128f(row);
+                        a01[r] = __ffma2_rn(make_float2(w.x, w.y), xr[k][0], a01[r]);
+                        a23[r] = __ffma2_rn(make_float2(w.z, w.w), xr[k][1], a23[r]);
+                    }
+                }
+            }
+        }
+        float v[NH];
+#pragma unroll
+        for (int r = 0; r < NH; ++r) v[r] = fadd(fadd(a01[r].x, a01[r].y), fadd(a23[r].x, a23[r].y));
+        exchange_butterfly<NH>(v, lane);
+        if ((lane & ((32 >> LG) - 1)) == 0) {
+            const int rr = h0 + (lane >> (5 - LG));        // stage row (m * RS + r)
+            if (rr < NR) {
+                const int m = rr / RS, r = rr - m * RS;
+                if (r < nr) part[((rl0 + r) * NM + m) * 8 + gwarp] = v[0];
+            }
+        }
+    }
+}
+
+// Consumer walk for the run-time shaped stage (see gemv_consume).
+template <typename WT, int KMAX, int NH>
+__device__ __forceinline__ bool gemv_consume_rt(const GemvParams& p, int r0, int r1, int RS,
+                                                const unsigned char* ring, uint32_t slot_stride, int NS,
+                                                uint64_t* full, uint64_t* empty, int& j, int group, int gwarp,
+                                                int lane, int slotid,
+                                                const float2 (&xr)[KMAX][GemvElems<WT>::EPB / 2], float* part) {
+    const uint32_t row_bytes = (uint32_t)p.ld * (uint32_t)sizeof(WT);
+    const int nblk = (int)(row_bytes >> 4);
+    const int NM = p.paired ? 2 : 1;
+    int cur = r0;
+    while (cur < r1) {
+        const StageRows sr = next_stage(p, cur, r1, RS);
+        const int slot = j % NS;
+        if ((slot & 1) == group) {
+            if (!mbar_wait_bounded(&full[slot], (uint32_t)((j / NS) & 1))) return false;
+            gemv_consume_stage_rt<WT, KMAX, NH>(ring + (size_t)slot * slot_stride, row_bytes, nblk, slotid, lane,
+                                                gwarp, xr, part, cur - r0, sr.nr, RS, NM);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+        ++j;
+        cur += sr.nr;
+    }
+    return true;
 }
 
 // Producer: issue the stages of rows [r0, r1) into the ring, one bulk copy per

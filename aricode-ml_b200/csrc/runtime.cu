@@ -676,6 +676,8 @@ void setup_token(b2_ctx* c) {
     if (ring_off + 4 * (size_t)kTkSlotBytes > smem_max) { c->token_why = "too many rows per CTA"; return; }
     int ns = (int)((smem_max - ring_off) / kTkSlotBytes);
     ns = std::min(ns, kTkMaxSlots) & ~1;
+    if (const char* sl = std::getenv("B2_TK_SLOTS"))             // tuning: fewer slots, more L1
+        ns = std::max(4, std::min(ns, std::atoi(sl) & ~1));
     c->tk_ns = ns;
     c->tk_ring_offset = (int)ring_off;
     c->tk_smem = ring_off + (size_t)ns * kTkSlotBytes;

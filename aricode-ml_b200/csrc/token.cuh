@@ -378,62 +378,46 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
 }
 
 // --------------------------------------------------------------------- GEMV phase
-template <typename WT, int KMAX, int RS, bool PAIRED>
-__device__ __forceinline__ bool tk_gemv(const GemvParams& p, int unit, int pos, const unsigned char* ring, int NS,
-                                        uint64_t* full, uint64_t* empty, int& j, int group, int gwarp, int lane,
-                                        int tid, float* red, float* part, int cta, int ncta,
+// One compiled copy per weight type: rows of up to 3 blocks per thread, rows per
+// stage and pairing at run time (one copy keeps the consumers free of spills).
+template <typename WT>
+__device__ __forceinline__ bool tk_gemv(const GemvParams& p, int unit, int rs, int pos, const unsigned char* ring,
+                                        int NS, uint64_t* full, uint64_t* empty, int& j, int group, int gwarp,
+                                        int lane, int tid, float* red, float* part, int cta, int ncta,
                                         unsigned long long* tr) {
+    constexpr int ESZ = (int)sizeof(WT);
     int r0, r1;
     cta_rows(total_rows(p), unit, cta, ncta, r0, r1);
+    const bool paired = p.paired != 0;
     // part[]: [rows][NM][8] warp sums, then epi[]: [rows][4] epilogue inputs
-    float* epi = part + (size_t)(r1 - r0) * (PAIRED ? 2 : 1) * 8;
-    const EpiRow er = gemv_epi_load<(int)sizeof(WT), PAIRED>(p, r0, r1, pos, tid);
-    float2 xr[KMAX][GemvElems<WT>::EPB / 2];
-    gemv_load_x<WT, KMAX>(p, xr, red, tid);
+    float* epi = part + (size_t)(r1 - r0) * (paired ? 2 : 1) * 8;
+    const EpiRow er = paired ? gemv_epi_load<ESZ, true>(p, r0, r1, pos, tid)
+                             : gemv_epi_load<ESZ, false>(p, r0, r1, pos, tid);
+    float2 xr[3][GemvElems<WT>::EPB / 2];
+    gemv_load_x<WT, 3, true>(p, xr, red, tid);
     tk_stamp(tr, 1, tid);
     gemv_epi_store(er, r1 - r0, tid, epi);
     tk_stamp(tr, 2, tid);
-    const bool ok = gemv_consume<WT, KMAX, RS, PAIRED>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group,
-                                                       gwarp, lane, tid % 256, xr, part, true);
+    const bool ok = gemv_consume_rt<WT, 3, 4>(p, r0, r1, rs, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp,
+                                              lane, tid % 256, xr, part);
     consumer_bar();
     tk_stamp(tr, 3, tid);
-    gemv_epilogue<(int)sizeof(WT), PAIRED>(p, r0, r1, part, pos, tid, cta, ncta, epi);
+    if (paired) gemv_epilogue<ESZ, true>(p, r0, r1, part, pos, tid, cta, ncta, epi);
+    else gemv_epilogue<ESZ, false>(p, r0, r1, part, pos, tid, cta, ncta, epi);
     return ok;
 }
 
-// Variant sets compiled into one kernel: fewer shapes, fewer registers held
-// across the switch. VS 0: int8 weights only; VS 1: int8 and f32.
-template <int VS> struct TkSet { static constexpr bool f32 = VS == 1; };
-
+// VS 0: int8 weights only; VS 1: int8 and f32.
 template <int VS>
 __device__ __forceinline__ bool tk_gemv_dispatch(const TkPhase& T, int pos, const unsigned char* ring, int NS,
                                                  uint64_t* full, uint64_t* empty, int& j, int group, int gwarp,
                                                  int lane, int tid, float* red, float* part, int cta, int ncta,
                                                  unsigned long long* tr) {
-    const GemvParams& p = T.g;
-    switch (T.variant) {
-        case TV_I8_K1_R8:
-            return tk_gemv<int8_t, 1, 8, false>(p, T.unit, pos, ring, NS, full, empty, j, group, gwarp, lane, tid,
-                                                red, part, cta, ncta, tr);
-        case TV_I8_K1_R4_P:
-            return tk_gemv<int8_t, 1, 4, true>(p, T.unit, pos, ring, NS, full, empty, j, group, gwarp, lane, tid,
-                                               red, part, cta, ncta, tr);
-        case TV_I8_K3_R2:
-            return tk_gemv<int8_t, 3, 2, false>(p, T.unit, pos, ring, NS, full, empty, j, group, gwarp, lane, tid,
-                                                red, part, cta, ncta, tr);
-        case TV_I8_K3_R1_P:
-            return tk_gemv<int8_t, 3, 1, true>(p, T.unit, pos, ring, NS, full, empty, j, group, gwarp, lane, tid,
-                                               red, part, cta, ncta, tr);
-        default:
-            if constexpr (TkSet<VS>::f32) {
-                if (T.variant == TV_F32_K1_R8)
-                    return tk_gemv<float, 1, 8, false>(p, T.unit, pos, ring, NS, full, empty, j, group, gwarp, lane,
-                                                       tid, red, part, cta, ncta, tr);
-                return tk_gemv<float, 3, 2, false>(p, T.unit, pos, ring, NS, full, empty, j, group, gwarp, lane, tid,
-                                                   red, part, cta, ncta, tr);
-            }
-            return false;
-    }
+    if (VS == 1 && T.variant >= TV_F32_K1_R8)
+        return tk_gemv<float>(T.g, T.unit, T.rs, pos, ring, NS, full, empty, j, group, gwarp, lane, tid, red, part,
+                              cta, ncta, tr);
+    return tk_gemv<int8_t>(T.g, T.unit, T.rs, pos, ring, NS, full, empty, j, group, gwarp, lane, tid, red, part, cta,
+                           ncta, tr);
 }
 
 // --------------------------------------------------------------------- the kernel

@@ -56,7 +56,9 @@ constexpr int kTkInflight = 3;                    // default bulk copies outstan
 constexpr int kTkMaxSplits = 256;                 // max_seq <= 16384
 constexpr int kTkGroupScratch = 64 + 4 + kTkMaxSplits;   // floats per consumer group
 constexpr int kTkScratchOffset = 256;             // after the mbarriers and flags
-constexpr int kTkPartOffset = 4608;               // >= kTkScratchOffset + 2 * kTkGroupScratch * 4
+constexpr int kTkDescBytes = 864;                 // one phase descriptor copy (>= sizeof(TkPhase))
+constexpr int kTkDescOffset = 2880;               // >= kTkScratchOffset + 2 * kTkGroupScratch * 4
+constexpr int kTkPartOffset = kTkDescOffset + 3 * kTkDescBytes + 32;   // 2 consumer + 1 producer copies
 // 640 threads: warpgroups 0-3 consume, warpgroup 4 produces (one lane works).
 // Launched at 96 registers a thread (61,440 per CTA); the producer warpgroup
 // hands registers back (setmaxnreg.dec) and the consumers take them
@@ -66,7 +68,7 @@ constexpr int kTkProducerRegs = 32;
 constexpr int kTkConsumerRegs = 112;
 static_assert(4 * 128 * kTkConsumerRegs + 128 * kTkProducerRegs <= kTkThreads * 96, "register split");
 
-struct TkPhase {
+struct alignas(16) TkPhase {
     int kind;
     int variant;        // TK_GEMV
     int unit;           // rows per balancing unit (2 keeps RoPE pairs in one CTA)
@@ -75,6 +77,33 @@ struct TkPhase {
     AttnParams a;
     EmbedParams e;
 };
+
+static_assert(sizeof(TkPhase) <= kTkDescBytes && sizeof(TkPhase) % 16 == 0, "descriptor copy size");
+static_assert(kTkDescOffset % 16 == 0 && kTkDescBytes % 16 == 0, "descriptor alignment");
+static_assert(kTkPartOffset % 16 == 0, "part alignment");
+
+// Copy a phase descriptor from the table (global, read-only) into shared memory,
+// 16 bytes per load, across `nthreads` threads, loads issued in batches of 16: its
+// fields are then read at shared-memory latency instead of one dependent L2 round
+// trip each.
+__device__ __forceinline__ void tk_copy_desc(TkPhase* dst, const TkPhase* src, int t, int nthreads) {
+    constexpr int NV = (int)(sizeof(TkPhase) / 16);
+    const uint4* s = reinterpret_cast<const uint4*>(src);
+    uint4* d = reinterpret_cast<uint4*>(dst);
+    for (int w0 = t; w0 < NV; w0 += 16 * nthreads) {
+        uint4 v[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+            const int w = w0 + u * nthreads;
+            if (w < NV) v[u] = __ldg(s + w);
+        }
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+            const int w = w0 + u * nthreads;
+            if (w < NV) d[w] = v[u];
+        }
+    }
+}
 
 struct TkParams {
     const TkPhase* phases;
@@ -476,8 +505,10 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
         if (warp == kGemvConsumerWarps && lane == 0) {
             int j = 0;
             bool ok = true;
+            TkPhase* pdesc = reinterpret_cast<TkPhase*>(smem + kTkDescOffset + 2 * kTkDescBytes);
             for (int ph = 0; ph < P.nphases && ok; ++ph) {
-                const TkPhase& T = P.phases[ph];
+                tk_copy_desc(pdesc, P.phases + ph, 0, 1);
+                const TkPhase& T = *pdesc;
                 if (T.kind == TK_GEMV) {
                     const GemvParams& p = T.g;
                     int r0, r1;
@@ -513,8 +544,11 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
     volatile int* gflag = flag + 2 + group;
     int j = 0;
     unsigned arrivals = 0;
+    TkPhase* cdesc = reinterpret_cast<TkPhase*>(smem + kTkDescOffset);      // [2]: phase ph in ph & 1
+    tk_copy_desc(cdesc, P.phases, tid, kGemvConsumerThreads);
+    consumer_bar();
     for (int ph = 0; ph < P.nphases; ++ph) {
-        const TkPhase& T = P.phases[ph];
+        const TkPhase& T = cdesc[ph & 1];
         if (ph > 0) {
             arrivals += (unsigned)ncta;
             if (!tk_grid_sync(P.bar, arrivals, tid, flag, abort)) {
@@ -557,6 +591,9 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
             tk_stamp(tr, 4, tid);
         }
         if (!ok) *abort = 1;
+        // the next phase's descriptor, in place after the grid barrier (the buffer
+        // it overwrites was last read in phase ph - 1)
+        if (ph + 1 < P.nphases) tk_copy_desc(cdesc + ((ph + 1) & 1), P.phases + ph + 1, tid, kGemvConsumerThreads);
     }
     consumer_bar();
     if (tid == 0) {

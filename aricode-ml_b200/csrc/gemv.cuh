@@ -318,6 +318,71 @@ __device__ __forceinline__ void gemv_load_x(const GemvParams& p, float2 (&xr)[KM
     }
 }
 
+// The prologue of gemv_load_x with x (and the norm gains) already in shared
+// memory: xs[n], gs[n], bs[n] (plain loads). Same arithmetic, same order.
+template <typename WT, int KMAX>
+__device__ __forceinline__ void gemv_load_x_smem(const GemvParams& p, const float* xs, const float* gs,
+                                                 const float* bs, float2 (&xr)[KMAX][GemvElems<WT>::EPB / 2],
+                                                 float* red, int tid) {
+    constexpr int EPB = GemvElems<WT>::EPB;
+    const int n = p.n;
+    const int slotid = tid % 256;
+    const int nblk = (int)(((size_t)p.ld * sizeof(WT)) >> 4);
+    const int K = (nblk + 255) / 256;
+    float scale_a = 1.0f, shift_m = 0.0f;
+    if (p.norm == NORM_RMS) {
+        float a = 0.0f;
+        if (tid < 256)
+            for (int i = tid; i < n; i += 256) { const float v = xs[i]; a = ffma(v, v, a); }
+        const float tot = consumer_reduce256(a, red, tid);
+        const float ms = fdiv(tot, (float)n);
+        scale_a = fdiv(1.0f, __fsqrt_rn(fadd(ms, p.eps)));
+    } else if (p.norm == NORM_LN) {
+        float a = 0.0f;
+        if (tid < 256)
+            for (int i = tid; i < n; i += 256) a = fadd(a, xs[i]);
+        shift_m = fdiv(consumer_reduce256(a, red, tid), (float)n);
+        a = 0.0f;
+        if (tid < 256)
+            for (int i = tid; i < n; i += 256) { const float dx = fsub(xs[i], shift_m); a = ffma(dx, dx, a); }
+        const float var = fdiv(consumer_reduce256(a, red, tid), (float)n);
+        scale_a = fdiv(1.0f, __fsqrt_rn(fadd(var, p.eps)));
+    }
+    // the slice, 16 bytes at a time (n % 4 == 0)
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k) {
+        const int b = slotid + 256 * k;
+#pragma unroll
+        for (int q = 0; q < EPB / 4; ++q) {
+            const int i0 = b * EPB + 4 * q;
+            float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            if (k < K && b < nblk && i0 < n) {
+                const float4 x4 = *reinterpret_cast<const float4*>(xs + i0);
+                const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
+                float g[4] = {0.0f, 0.0f, 0.0f, 0.0f}, bb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                if (p.norm != NORM_NONE) {
+                    const float4 g4 = *reinterpret_cast<const float4*>(gs + i0);
+                    g[0] = g4.x; g[1] = g4.y; g[2] = g4.z; g[3] = g4.w;
+                }
+                if (p.norm == NORM_LN) {
+                    const float4 b4 = *reinterpret_cast<const float4*>(bs + i0);
+                    bb[0] = b4.x; bb[1] = b4.y; bb[2] = b4.z; bb[3] = b4.w;
+                }
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    if (p.norm == NORM_RMS) v[e] = fmul(fmul(xv[e], scale_a), g[e]);
+                    else if (p.norm == NORM_LN)
+                        v[e] = (float)dadd(dmul((double)fmul(fsub(xv[e], shift_m), scale_a), (double)g[e]),
+                                           (double)bb[e]);
+                    else v[e] = xv[e];
+                }
+            }
+            xr[k][2 * q] = make_float2(v[0], v[1]);
+            xr[k][2 * q + 1] = make_float2(v[2], v[3]);
+        }
+    }
+}
+
 // One stage: nr (<= RS) rows of each of the NM matrices at `stage` (row stride
 // row_bytes; the second matrix starts RS rows in). Writes this warp's sums to
 // part[(row * NM + m) * 8 + gwarp] for rows rl0 .. rl0 + nr - 1 of the CTA. Rows

@@ -162,7 +162,7 @@ struct b2_ctx {
     int nph_prefill = 0, nph_decode = 0;
     unsigned* tk_bar = nullptr;    // grid-barrier counters, zero between launches
     int n_attn_cnt = 0;
-    int tk_ns = 0, tk_ring_offset = 0, tk_inflight = kTkInflight;
+    int tk_ns = 0, tk_ring_offset = 0, tk_inflight = kTkInflight, tk_vec_offset = 0, tk_vec_floats = 0;
     size_t tk_smem = 0;
     std::string token_why;         // why the per-layer kernels are used instead
     unsigned long long* d_trace = nullptr;   // token-kernel timeline (B2_TK_TRACE)
@@ -602,7 +602,8 @@ int enqueue_step(b2_ctx* c, bool with_head, cudaStream_t s) {
 // ------------------------------------------------------------------ token kernel
 // The phase of one operation; false (with the reason) when its shape is outside
 // what the token kernel is compiled for.
-bool tk_phase_of(const b2_ctx* c, const Op& o, TkPhase& T, size_t& part_bytes, std::string& why) {
+bool tk_phase_of(const b2_ctx* c, const Op& o, TkPhase& T, size_t& part_bytes, size_t& vec_floats,
+                 std::string& why) {
     T = TkPhase{};
     T.kind = o.kind;
     if (o.kind == TK_EMBED) {
@@ -637,6 +638,8 @@ bool tk_phase_of(const b2_ctx* c, const Op& o, TkPhase& T, size_t& part_bytes, s
     const long long units = (total + T.unit - 1) / T.unit;
     const long long rows_cta = (units + c->sm_count - 1) / c->sm_count * T.unit;
     part_bytes = std::max(part_bytes, (size_t)rows_cta * ((paired ? 2 : 1) * 8 + 4) * sizeof(float));
+    const size_t nv = (size_t)g.n * (1 + (g.norm != NORM_NONE) + (g.norm == NORM_LN));
+    if (g.n % 4 == 0) vec_floats = std::max(vec_floats, nv);
     return true;
 }
 
@@ -658,20 +661,23 @@ void setup_token(b2_ctx* c) {
     CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->device));
     if (!coop) { c->token_why = "no cooperative launch"; return; }
     std::vector<TkPhase> ph;
-    size_t part = 0;
+    size_t part = 0, vec_floats = 0;
     std::string why;
     bool f32 = false;
     for (int head = 0; head < 2; ++head) {
         for (const Op& o : build_ops(c, head == 1)) {
             TkPhase T;
-            if (!tk_phase_of(c, o, T, part, why)) { c->token_why = why; return; }
+            if (!tk_phase_of(c, o, T, part, vec_floats, why)) { c->token_why = why; return; }
             if (T.kind == TK_GEMV && T.variant >= TV_F32_K1_R8) f32 = true;
             ph.push_back(T);
         }
         if (head == 0) c->nph_prefill = (int)ph.size();
         else c->nph_decode = (int)ph.size() - c->nph_prefill;
     }
-    const size_t ring_off = (kTkPartOffset + part + 127) & ~(size_t)127;
+    const size_t vec_off = (kTkPartOffset + part + 127) & ~(size_t)127;
+    const size_t ring_off = (vec_off + vec_floats * 4 + 127) & ~(size_t)127;
+    c->tk_vec_offset = (int)vec_off;
+    c->tk_vec_floats = (int)vec_floats;
     const size_t smem_max = 226 * 1024;             // dynamic; the static argmax slots need the rest
     if (ring_off + 4 * (size_t)kTkSlotBytes > smem_max) { c->token_why = "too many rows per CTA"; return; }
     int ns = (int)((smem_max - ring_off) / kTkSlotBytes);
@@ -721,6 +727,8 @@ void launch_token(b2_ctx* c, bool with_head, cudaStream_t s) {
     P.vocab = c->vocab;
     P.trace = c->d_trace;
     P.inflight = c->tk_inflight;
+    P.vec_offset = c->tk_vec_offset;
+    P.vec_floats = c->tk_vec_floats;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)c->sm_count);
     cfg.blockDim = dim3(kTkThreads);

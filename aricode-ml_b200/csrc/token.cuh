@@ -115,6 +115,8 @@ struct TkParams {
     const int* prompt;
     int max_seq, max_pos, vocab;
     int inflight;       // bulk copies outstanding per CTA (1 .. ns - 1)
+    int vec_offset;     // shared-memory buffer for a phase's x and norm gains (bytes, 128-aligned)
+    int vec_floats;     // its capacity
     // optional timeline (nullptr: off): [phase][cta][kTkStamps] global-timer stamps
     // at the phase start (after the grid barrier), when x is loaded, after the
     // prologue, after the stages and after the epilogue
@@ -413,22 +415,44 @@ template <typename WT>
 __device__ __forceinline__ bool tk_gemv(const GemvParams& p, int unit, int rs, int pos, const unsigned char* ring,
                                         int NS, uint64_t* full, uint64_t* empty, int& j, int group, int gwarp,
                                         int lane, int tid, float* red, float* part, int cta, int ncta,
-                                        unsigned long long* tr) {
+                                        unsigned long long* tr, float* vec, int vec_floats, uint64_t* vbar,
+                                        uint32_t& vphase) {
     constexpr int ESZ = (int)sizeof(WT);
     int r0, r1;
     cta_rows(total_rows(p), unit, cta, ncta, r0, r1);
     const bool paired = p.paired != 0;
     // part[]: [rows][NM][8] warp sums, then epi[]: [rows][4] epilogue inputs
     float* epi = part + (size_t)(r1 - r0) * (paired ? 2 : 1) * 8;
+    // x and the norm gains: one bulk copy each into shared memory (every CTA reads
+    // the same vector; one L2 read per CTA instead of one per thread and pass)
+    const int n = p.n;
+    const int nv = n * (1 + (p.norm != NORM_NONE) + (p.norm == NORM_LN));
+    auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+    const bool staged = (n % 4) == 0 && nv <= vec_floats && al16(p.x) &&
+                        (p.norm == NORM_NONE || al16(p.ng)) && (p.norm != NORM_LN || al16(p.nb));
+    if (staged && tid == 0) {
+        asm volatile("fence.proxy.async.global;" ::: "memory");    // generic writes -> bulk-copy reads
+        mbar_arrive_expect_tx(vbar, (uint32_t)nv * 4);
+        bulk_g2s(vec, p.x, (uint32_t)n * 4, vbar);
+        if (p.norm != NORM_NONE) bulk_g2s(vec + n, p.ng, (uint32_t)n * 4, vbar);
+        if (p.norm == NORM_LN) bulk_g2s(vec + 2 * n, p.nb, (uint32_t)n * 4, vbar);
+    }
     const EpiRow er = paired ? gemv_epi_load<ESZ, true>(p, r0, r1, pos, tid)
                              : gemv_epi_load<ESZ, false>(p, r0, r1, pos, tid);
     float2 xr[3][GemvElems<WT>::EPB / 2];
-    gemv_load_x<WT, 3, true>(p, xr, red, tid);
+    bool ok = true;
+    if (staged) {
+        if (!mbar_wait_bounded(vbar, vphase & 1)) ok = false;
+        ++vphase;
+        gemv_load_x_smem<WT, 3>(p, vec, vec + n, vec + 2 * n, xr, red, tid);
+    } else {
+        gemv_load_x<WT, 3, true>(p, xr, red, tid);
+    }
     tk_stamp(tr, 1, tid);
     gemv_epi_store(er, r1 - r0, tid, epi);
     tk_stamp(tr, 2, tid);
-    const bool ok = gemv_consume_rt<WT, 3, 4>(p, r0, r1, rs, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp,
-                                              lane, tid % 256, xr, part);
+    ok = gemv_consume_rt<WT, 3, 4>(p, r0, r1, rs, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp, lane,
+                                   tid % 256, xr, part) && ok;
     consumer_bar();
     tk_stamp(tr, 3, tid);
     if (paired) gemv_epilogue<ESZ, true>(p, r0, r1, part, pos, tid, cta, ncta, epi);
@@ -441,12 +465,13 @@ template <int VS>
 __device__ __forceinline__ bool tk_gemv_dispatch(const TkPhase& T, int pos, const unsigned char* ring, int NS,
                                                  uint64_t* full, uint64_t* empty, int& j, int group, int gwarp,
                                                  int lane, int tid, float* red, float* part, int cta, int ncta,
-                                                 unsigned long long* tr) {
+                                                 unsigned long long* tr, float* vec, int vec_floats, uint64_t* vbar,
+                                                 uint32_t& vphase) {
     if (VS == 1 && T.variant >= TV_F32_K1_R8)
         return tk_gemv<float>(T.g, T.unit, T.rs, pos, ring, NS, full, empty, j, group, gwarp, lane, tid, red, part,
-                              cta, ncta, tr);
+                              cta, ncta, tr, vec, vec_floats, vbar, vphase);
     return tk_gemv<int8_t>(T.g, T.unit, T.rs, pos, ring, NS, full, empty, j, group, gwarp, lane, tid, red, part, cta,
-                           ncta, tr);
+                           ncta, tr, vec, vec_floats, vbar, vphase);
 }
 
 // --------------------------------------------------------------------- the kernel
@@ -458,6 +483,8 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
     float* red = reinterpret_cast<float*>(smem + 128);                   // 8 floats
     volatile int* flag = reinterpret_cast<volatile int*>(smem + 192);    // [0] grid sync, [2..3] groups
     volatile int* abort = reinterpret_cast<volatile int*>(smem + 208);
+    uint64_t* vbar = reinterpret_cast<uint64_t*>(smem + 216);           // vector staging
+    float* vec = reinterpret_cast<float*>(smem + P.vec_offset);
     float* scratch = reinterpret_cast<float*>(smem + kTkScratchOffset);
     float* part = reinterpret_cast<float*>(smem + kTkPartOffset);
     unsigned char* ring = smem + P.ring_offset;
@@ -493,6 +520,7 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kGemvGroupWarps);
         }
+        mbar_init(vbar, 1);
         fence_mbar_init();
         *abort = 0;
     }
@@ -544,6 +572,7 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
     volatile int* gflag = flag + 2 + group;
     int j = 0;
     unsigned arrivals = 0;
+    uint32_t vphase = 0;                                // phases of vbar used so far
     TkPhase* cdesc = reinterpret_cast<TkPhase*>(smem + kTkDescOffset);      // [2]: phase ph in ph & 1
     tk_copy_desc(cdesc, P.phases, tid, kGemvConsumerThreads);
     consumer_bar();
@@ -576,7 +605,7 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
             }
         } else if (T.kind == TK_GEMV) {
             ok = tk_gemv_dispatch<VS>(T, pos, ring, NS, full, empty, j, group, gwarp, lane, tid, red, part, cta,
-                                      ncta, tr);
+                                      ncta, tr, vec, P.vec_floats, vbar, vphase);
         } else {
             tk_stamp(tr, 1, tid);
             tk_stamp(tr, 2, tid);

@@ -383,6 +383,197 @@ __device__ __forceinline__ void gemv_load_x_smem(const GemvParams& p, const floa
     }
 }
 
+// ---------------------------------------------------------------------------
+// x in shared memory (token kernel): the vector is staged once per CTA and phase
+// at xs[0 .. L) (zeros past n, L = n rounded up to 16), its norm gains at gs[],
+// bs[]. The prologue normalises it in place; the stages read one 16-byte block
+// of x per row group from shared memory instead of holding the slice in
+// registers. Same operations, in the same order, as gemv_load_x + the stages.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void gemv_norm_smem(const GemvParams& p, float* xs, const float* gs, const float* bs,
+                                               float* red, int tid) {
+    const int n = p.n;
+    if (p.norm == NORM_NONE) return;
+    float scale_a = 1.0f, shift_m = 0.0f;
+    if (p.norm == NORM_RMS) {
+        float a = 0.0f;
+        if (tid < 256)
+            for (int i = tid; i < n; i += 256) { const float v = xs[i]; a = ffma(v, v, a); }
+        const float tot = consumer_reduce256(a, red, tid);
+        const float ms = fdiv(tot, (float)n);
+        scale_a = fdiv(1.0f, __fsqrt_rn(fadd(ms, p.eps)));
+    } else {
+        float a = 0.0f;
+        if (tid < 256)
+            for (int i = tid; i < n; i += 256) a = fadd(a, xs[i]);
+        shift_m = fdiv(consumer_reduce256(a, red, tid), (float)n);
+        a = 0.0f;
+        if (tid < 256)
+            for (int i = tid; i < n; i += 256) { const float dx = fsub(xs[i], shift_m); a = ffma(dx, dx, a); }
+        const float var = fdiv(consumer_reduce256(a, red, tid), (float)n);
+        scale_a = fdiv(1.0f, __fsqrt_rn(fadd(var, p.eps)));
+    }
+    // every raw value has been read (the reduction's barriers); normalise in place
+    for (int i = tid; i < n; i += kGemvConsumerThreads) {
+        const float xv = xs[i];
+        xs[i] = p.norm == NORM_RMS
+                    ? fmul(fmul(xv, scale_a), gs[i])
+                    : (float)dadd(dmul((double)fmul(fsub(xv, shift_m), scale_a), (double)gs[i]), (double)bs[i]);
+    }
+}
+
+template <typename WT, int NH>
+__device__ __forceinline__ void gemv_consume_stage_xs(const unsigned char* stage, uint32_t row_bytes, int nblk,
+                                                      int slotid, int lane, int gwarp, const float* xs,
+                                                      float* part, int rl0, int nr, int RS, int NM) {
+    constexpr int ESZ = (int)sizeof(WT);
+    constexpr int EPB = GemvElems<WT>::EPB;
+    constexpr int LG = Log2<NH>::v;
+    const int NR = RS * NM;
+#pragma unroll 1
+    for (int h0 = 0; h0 < NR; h0 += NH) {
+        float2 a01[NH], a23[NH];
+#pragma unroll
+        for (int r = 0; r < NH; ++r) a01[r] = a23[r] = make_float2(0.0f, 0.0f);
+#pragma unroll 1
+        for (int b = slotid; b < nblk; b += 256) {
+            float2 xb[EPB / 2];
+#pragma unroll
+            for (int q = 0; q < EPB / 4; ++q) {
+                const float4 x4 = lds128f(xs + b * EPB + 4 * q);
+                xb[2 * q] = make_float2(x4.x, x4.y);
+                xb[2 * q + 1] = make_float2(x4.z, x4.w);
+            }
+#pragma unroll
+            for (int r = 0; r < NH; ++r) {
+                if (h0 + r >= NR) break;
+                const unsigned char* row = stage + (size_t)(h0 + r) * row_bytes + 16 * b;
+                if constexpr (ESZ == 1) {
+                    const uint4 w = lds128(row);
+                    fma_word2(a01[r], a23[r], w.x ^ 0x80808080u, xb[0], xb[1]);
+                    fma_word2(a01[r], a23[r], w.y ^ 0x80808080u, xb[2], xb[3]);
+                    fma_word2(a01[r], a23[r], w.z ^ 0x80808080u, xb[4], xb[5]);
+                    fma_word2(a01[r], a23[r], w.w ^ 0x80808080u, xb[6], xb[7]);
+                } else {
+                    const float4 w = lds128f(row);
+                    a01[r] = __ffma2_rn(make_float2(w.x, w.y), xb[0], a01[r]);
+                    a23[r] = __ffma2_rn(make_float2(w.z, w.w), xb[1], a23[r]);
+                }
+            }
+        }
+        float v[NH];
+#pragma unroll
+        for (int r = 0; r < NH; ++r) v[r] = fadd(fadd(a01[r].x, a01[r].y), fadd(a23[r].x, a23[r].y));
+        exchange_butterfly<NH>(v, lane);
+        if ((lane & ((32 >> LG) - 1)) == 0) {
+            const int rr = h0 + (lane >> (5 - LG));
+            if (rr < NR) {
+                const int m = rr / RS, r = rr - m * RS;
+                if (r < nr) part[((rl0 + r) * NM + m) * 8 + gwarp] = v[0];
+            }
+        }
+    }
+}
+
+// Compile-time shaped stage with x read from shared memory: RS rows per matrix,
+// NM matrices, all NR = RS * NM rows reduced by one exchange butterfly.
+template <typename WT, int RS, int NM>
+__device__ __forceinline__ void gemv_consume_stage_xt(const unsigned char* stage, uint32_t row_bytes, int nblk,
+                                                      int slotid, int lane, int gwarp, const float* xs,
+                                                      float* part, int rl0, int nr) {
+    constexpr int ESZ = (int)sizeof(WT);
+    constexpr int EPB = GemvElems<WT>::EPB;
+    constexpr int NR = RS * NM;
+    constexpr int LG = Log2<NR>::v;
+    float2 a01[NR], a23[NR];
+#pragma unroll
+    for (int r = 0; r < NR; ++r) a01[r] = a23[r] = make_float2(0.0f, 0.0f);
+#pragma unroll 1
+    for (int b = slotid; b < nblk; b += 256) {
+        float2 xb[EPB / 2];
+#pragma unroll
+        for (int q = 0; q < EPB / 4; ++q) {
+            const float4 x4 = lds128f(xs + b * EPB + 4 * q);
+            xb[2 * q] = make_float2(x4.x, x4.y);
+            xb[2 * q + 1] = make_float2(x4.z, x4.w);
+        }
+#pragma unroll
+        for (int r = 0; r < NR; ++r) {
+            // rows past nr read stale (in-bounds) stage bytes; never stored
+            const unsigned char* row = stage + (size_t)r * row_bytes + 16 * b;
+            if constexpr (ESZ == 1) {
+                const uint4 w = lds128(row);
+                fma_word2(a01[r], a23[r], w.x ^ 0x80808080u, xb[0], xb[1]);
+                fma_word2(a01[r], a23[r], w.y ^ 0x80808080u, xb[2], xb[3]);
+                fma_word2(a01[r], a23[r], w.z ^ 0x80808080u, xb[4], xb[5]);
+                fma_word2(a01[r], a23[r], w.w ^ 0x80808080u, xb[6], xb[7]);
+            } else {
+                const float4 w = lds128f(row);
+                a01[r] = __ffma2_rn(make_float2(w.x, w.y), xb[0], a01[r]);
+                a23[r] = __ffma2_rn(make_float2(w.z, w.w), xb[1], a23[r]);
+            }
+        }
+    }
+    float v[NR];
+#pragma unroll
+    for (int r = 0; r < NR; ++r) v[r] = fadd(fadd(a01[r].x, a01[r].y), fadd(a23[r].x, a23[r].y));
+    exchange_butterfly<NR>(v, lane);
+    if ((lane & ((32 >> LG) - 1)) == 0) {
+        const int rr = lane >> (5 - LG);
+        const int m = rr / RS, r = rr % RS;
+        if (r < nr) part[((rl0 + r) * NM + m) * 8 + gwarp] = v[0];
+    }
+}
+
+template <typename WT, int RS, int NM>
+__device__ __forceinline__ bool gemv_consume_xt(const GemvParams& p, int r0, int r1, const unsigned char* ring,
+                                                uint32_t slot_stride, int NS, uint64_t* full, uint64_t* empty,
+                                                int& j, int group, int gwarp, int lane, int slotid, const float* xs,
+                                                float* part) {
+    const uint32_t row_bytes = (uint32_t)p.ld * (uint32_t)sizeof(WT);
+    const int nblk = (int)(row_bytes >> 4);
+    int cur = r0;
+    while (cur < r1) {
+        const StageRows sr = next_stage(p, cur, r1, RS);
+        const int slot = j % NS;
+        if ((slot & 1) == group) {
+            if (!mbar_wait_bounded(&full[slot], (uint32_t)((j / NS) & 1))) return false;
+            gemv_consume_stage_xt<WT, RS, NM>(ring + (size_t)slot * slot_stride, row_bytes, nblk, slotid, lane,
+                                              gwarp, xs, part, cur - r0, sr.nr);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+        ++j;
+        cur += sr.nr;
+    }
+    return true;
+}
+
+template <typename WT, int NH>
+__device__ __forceinline__ bool gemv_consume_xs(const GemvParams& p, int r0, int r1, int RS,
+                                                const unsigned char* ring, uint32_t slot_stride, int NS,
+                                                uint64_t* full, uint64_t* empty, int& j, int group, int gwarp,
+                                                int lane, int slotid, const float* xs, float* part) {
+    const uint32_t row_bytes = (uint32_t)p.ld * (uint32_t)sizeof(WT);
+    const int nblk = (int)(row_bytes >> 4);
+    const int NM = p.paired ? 2 : 1;
+    int cur = r0;
+    while (cur < r1) {
+        const StageRows sr = next_stage(p, cur, r1, RS);
+        const int slot = j % NS;
+        if ((slot & 1) == group) {
+            if (!mbar_wait_bounded(&full[slot], (uint32_t)((j / NS) & 1))) return false;
+            gemv_consume_stage_xs<WT, NH>(ring + (size_t)slot * slot_stride, row_bytes, nblk, slotid, lane, gwarp, xs,
+                                          part, cur - r0, sr.nr, RS, NM);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+        ++j;
+        cur += sr.nr;
+    }
+    return true;
+}
+
 // One stage: nr (<= RS) rows of each of the NM matrices at `stage` (row stride
 // row_bytes; the second matrix starts RS rows in). Writes this warp's sums to
 // part[(row * NM + m) * 8 + gwarp] for rows rl0 .. rl0 + nr - 1 of the CTA. Rows

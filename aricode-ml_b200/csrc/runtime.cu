@@ -638,8 +638,17 @@ bool tk_phase_of(const b2_ctx* c, const Op& o, TkPhase& T, size_t& part_bytes, s
     const long long units = (total + T.unit - 1) / T.unit;
     const long long rows_cta = (units + c->sm_count - 1) / c->sm_count * T.unit;
     part_bytes = std::max(part_bytes, (size_t)rows_cta * ((paired ? 2 : 1) * 8 + 4) * sizeof(float));
-    const size_t nv = (size_t)g.n * (1 + (g.norm != NORM_NONE) + (g.norm == NORM_LN));
-    if (g.n % 4 == 0) vec_floats = std::max(vec_floats, nv);
+    // x and its norm gains staged in shared memory: n % 4 (16-byte bulk copies),
+    // 16-aligned pointers, L = n rounded up to 16 covering the padded rows
+    const size_t L = ((size_t)g.n + 15) & ~(size_t)15;
+    const size_t nv = L * (1 + (g.norm != NORM_NONE) + (g.norm == NORM_LN));
+    auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+    if (g.n % 4 || !al16(g.x) || (g.norm != NORM_NONE && !al16(g.ng)) || (g.norm == NORM_LN && !al16(g.nb)) ||
+        (size_t)g.ld * (o.i8 ? 1 : 4) > L * (o.i8 ? 1 : 4)) {
+        why = "input vector not stageable";
+        return false;
+    }
+    vec_floats = std::max(vec_floats, nv);
     return true;
 }
 
@@ -656,7 +665,7 @@ bool tk_prepare_kernel(b2_ctx* c) {
 void setup_token(b2_ctx* c) {
     c->token = false;
     const char* env = std::getenv("B2_TOKEN_KERNEL");
-    if (!env || env[0] != '1') { c->token_why = "token kernel not requested (B2_TOKEN_KERNEL=1)"; return; }
+    if (env && env[0] == '0') { c->token_why = "per-layer kernels requested (B2_TOKEN_KERNEL=0)"; return; }
     int coop = 0;
     CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->device));
     if (!coop) { c->token_why = "no cooperative launch"; return; }

@@ -409,50 +409,59 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
 }
 
 // --------------------------------------------------------------------- GEMV phase
-// One compiled copy per weight type: rows of up to 3 blocks per thread, rows per
-// stage and pairing at run time (one copy keeps the consumers free of spills).
+// One compiled copy per weight type: any row length (blocks per thread at run
+// time), rows per stage and pairing at run time. x and its norm gains are staged
+// in shared memory (vec: x at [0, L), gains at [L, 2L), LN bias at [2L, 3L) with
+// L = n rounded up to 16, zeros in [n, L)), normalised in place, and read by the
+// stages from there.
 template <typename WT>
 __device__ __forceinline__ bool tk_gemv(const GemvParams& p, int unit, int rs, int pos, const unsigned char* ring,
                                         int NS, uint64_t* full, uint64_t* empty, int& j, int group, int gwarp,
                                         int lane, int tid, float* red, float* part, int cta, int ncta,
-                                        unsigned long long* tr, float* vec, int vec_floats, uint64_t* vbar,
-                                        uint32_t& vphase) {
+                                        unsigned long long* tr, float* vec, uint64_t* vbar, uint32_t& vphase) {
     constexpr int ESZ = (int)sizeof(WT);
     int r0, r1;
     cta_rows(total_rows(p), unit, cta, ncta, r0, r1);
     const bool paired = p.paired != 0;
+    const int n = p.n, L = (n + 15) & ~15;
+    if (tid == 0) {
+        // generic-proxy writes (x by other CTAs; vec by this CTA's last phase) are
+        // ordered before the bulk copies that read / overwrite them
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        const uint32_t nb = (uint32_t)n * 4 * (1 + (p.norm != NORM_NONE) + (p.norm == NORM_LN));
+        mbar_arrive_expect_tx(vbar, nb);
+        bulk_g2s(vec, p.x, (uint32_t)n * 4, vbar);
+        if (p.norm != NORM_NONE) bulk_g2s(vec + L, p.ng, (uint32_t)n * 4, vbar);
+        if (p.norm == NORM_LN) bulk_g2s(vec + 2 * L, p.nb, (uint32_t)n * 4, vbar);
+    }
+    for (int i = n + tid; i < L; i += kGemvConsumerThreads) vec[i] = 0.0f;     // row padding
     // part[]: [rows][NM][8] warp sums, then epi[]: [rows][4] epilogue inputs
     float* epi = part + (size_t)(r1 - r0) * (paired ? 2 : 1) * 8;
-    // x and the norm gains: one bulk copy each into shared memory (every CTA reads
-    // the same vector; one L2 read per CTA instead of one per thread and pass)
-    const int n = p.n;
-    const int nv = n * (1 + (p.norm != NORM_NONE) + (p.norm == NORM_LN));
-    auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
-    const bool staged = (n % 4) == 0 && nv <= vec_floats && al16(p.x) &&
-                        (p.norm == NORM_NONE || al16(p.ng)) && (p.norm != NORM_LN || al16(p.nb));
-    if (staged && tid == 0) {
-        asm volatile("fence.proxy.async.global;" ::: "memory");    // generic writes -> bulk-copy reads
-        mbar_arrive_expect_tx(vbar, (uint32_t)nv * 4);
-        bulk_g2s(vec, p.x, (uint32_t)n * 4, vbar);
-        if (p.norm != NORM_NONE) bulk_g2s(vec + n, p.ng, (uint32_t)n * 4, vbar);
-        if (p.norm == NORM_LN) bulk_g2s(vec + 2 * n, p.nb, (uint32_t)n * 4, vbar);
-    }
     const EpiRow er = paired ? gemv_epi_load<ESZ, true>(p, r0, r1, pos, tid)
                              : gemv_epi_load<ESZ, false>(p, r0, r1, pos, tid);
-    float2 xr[3][GemvElems<WT>::EPB / 2];
-    bool ok = true;
-    if (staged) {
-        if (!mbar_wait_bounded(vbar, vphase & 1)) ok = false;
-        ++vphase;
-        gemv_load_x_smem<WT, 3>(p, vec, vec + n, vec + 2 * n, xr, red, tid);
-    } else {
-        gemv_load_x<WT, 3, true>(p, xr, red, tid);
-    }
+    bool ok = mbar_wait_bounded(vbar, vphase & 1);
+    ++vphase;
+    gemv_norm_smem(p, vec, vec + L, vec + 2 * L, red, tid);
     tk_stamp(tr, 1, tid);
     gemv_epi_store(er, r1 - r0, tid, epi);
+    consumer_bar();                                     // normalised x and epi[] visible
     tk_stamp(tr, 2, tid);
-    ok = gemv_consume_rt<WT, 3, 4>(p, r0, r1, rs, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp, lane,
-                                   tid % 256, xr, part) && ok;
+    // the stage shapes the host chose (rows per stage x matrices), compiled
+    const int slotid = tid % 256;
+    bool okc;
+    if (paired) {
+        okc = rs == 4 ? gemv_consume_xt<WT, 4, 2>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp,
+                                                   lane, slotid, vec, part)
+                      : gemv_consume_xt<WT, 1, 2>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp,
+                                                   lane, slotid, vec, part);
+    } else {
+        okc = rs == 8 ? gemv_consume_xt<WT, 8, 1>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp,
+                                                   lane, slotid, vec, part)
+                      : gemv_consume_xt<WT, 2, 1>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp,
+                                                   lane, slotid, vec, part);
+    }
+    ok = okc && ok;
     consumer_bar();
     tk_stamp(tr, 3, tid);
     if (paired) gemv_epilogue<ESZ, true>(p, r0, r1, part, pos, tid, cta, ncta, epi);
@@ -465,13 +474,13 @@ template <int VS>
 __device__ __forceinline__ bool tk_gemv_dispatch(const TkPhase& T, int pos, const unsigned char* ring, int NS,
                                                  uint64_t* full, uint64_t* empty, int& j, int group, int gwarp,
                                                  int lane, int tid, float* red, float* part, int cta, int ncta,
-                                                 unsigned long long* tr, float* vec, int vec_floats, uint64_t* vbar,
+                                                 unsigned long long* tr, float* vec, uint64_t* vbar,
                                                  uint32_t& vphase) {
     if (VS == 1 && T.variant >= TV_F32_K1_R8)
         return tk_gemv<float>(T.g, T.unit, T.rs, pos, ring, NS, full, empty, j, group, gwarp, lane, tid, red, part,
-                              cta, ncta, tr, vec, vec_floats, vbar, vphase);
+                              cta, ncta, tr, vec, vbar, vphase);
     return tk_gemv<int8_t>(T.g, T.unit, T.rs, pos, ring, NS, full, empty, j, group, gwarp, lane, tid, red, part, cta,
-                           ncta, tr, vec, vec_floats, vbar, vphase);
+                           ncta, tr, vec, vbar, vphase);
 }
 
 // --------------------------------------------------------------------- the kernel
@@ -605,7 +614,7 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
             }
         } else if (T.kind == TK_GEMV) {
             ok = tk_gemv_dispatch<VS>(T, pos, ring, NS, full, empty, j, group, gwarp, lane, tid, red, part, cta,
-                                      ncta, tr, vec, P.vec_floats, vbar, vphase);
+                                      ncta, tr, vec, vbar, vphase);
         } else {
             tk_stamp(tr, 1, tid);
             tk_stamp(tr, 2, tid);

@@ -9,9 +9,11 @@ once before timing and every step rewinds to position 512, so all steps do the
 same work. value = generated tokens per second over all GPUs (N independent
 replicas when N > 1). e2e = the same metric through the public C ABI call
 b2_generate (prompt from pinned host memory, prefill + decode, ids back to
-pinned host memory). The roofline object is the int8 GEMV timed alone on the
-model's FFN shape. `--impl reference` times the CPU restatement of the
-reference decode path (oracle/) on the host cores.
+pinned host memory). The roofline object is the dominant kernel, the token
+kernel that runs one whole decode step per launch: algorithmic bytes per token
+over its average launch time; gemv_roofline is the per-launch int8 GEMV timed
+alone on the model's FFN shape. `--impl reference` times the CPU restatement of
+the reference decode path (oracle/) on the host cores.
 
 Weights: random N(0, 0.02)-like synthetic weights of the Llama-2-7B architecture
 (counter-based generator, identical on GPU and host); prompt ids uniform random.
@@ -257,12 +259,18 @@ def main():
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "config": workload_config(args, plan),
-        "roofline": {"bound": "hbm", "achieved": gemv["gbs"], "peak": hbm, "unit": "GB/s",
-                     "frac": gemv["gbs"] / hbm, "traffic": gemv["traffic"],
-                     "kernel": gemv["kernel"], "bytes_per_launch": gemv["bytes"],
-                     "us_per_launch": gemv["us"], "peak_kind": f"{peak_kind} hbm_gbs"},
-        "step_roofline": {"bound": "hbm", "bytes_per_token": bytes_tok, "achieved": step_gbs,
-                          "peak": hbm, "unit": "GB/s", "frac": step_gbs / hbm},
+        # dominant kernel: the decode step itself (one launch of the token kernel per
+        # token when kernels_per_step == 1); algorithmic bytes = weights + KV read
+        # and written, per token, over the launch's average duration
+        "roofline": {"bound": "hbm", "achieved": step_gbs, "peak": hbm, "unit": "GB/s",
+                     "frac": step_gbs / hbm, "traffic": profiled_traffic("token_kernel_llama2-7b"),
+                     "kernel": "token_kernel (whole decode step)" if kps == 1 else "per-layer kernels",
+                     "bytes_per_launch": bytes_tok, "us_per_launch": 1000.0 * ms / toks,
+                     "peak_kind": f"{peak_kind} hbm_gbs"},
+        "gemv_roofline": {"bound": "hbm", "achieved": gemv["gbs"], "peak": hbm, "unit": "GB/s",
+                          "frac": gemv["gbs"] / hbm, "traffic": gemv["traffic"],
+                          "kernel": gemv["kernel"] + " (per-launch GEMV alone)",
+                          "bytes_per_launch": gemv["bytes"], "us_per_launch": gemv["us"]},
         "e2e": e2e, "gpu_launches": launches, "clocks": clk,
         "decode_ms_per_token": ms / toks, "prefill_s_untimed": prefill_s,
         "tokens_head": ids[:8],
@@ -294,13 +302,13 @@ def time_gemv(torch, rt, plan, stream, reps=3):
     nbytes = m * n + 4 * m + 4 * n + 4 * m
     del Ws
     return {"kernel": f"gemv_i8 {m}x{n}", "us": us, "bytes": nbytes,
-            "gbs": nbytes / (us * 1e-6) / 1e9, "traffic": profiled_traffic(m, n)}
+            "gbs": nbytes / (us * 1e-6) / 1e9, "traffic": profiled_traffic(f"gemv_i8_{m}x{n}")}
 
 
-def profiled_traffic(m, n):
-    """DRAM bytes (read + write) per launch of the GEMV on this shape from the
-    committed ncu summary, or None when there is none."""
-    f = ROOT / "profiles" / f"gemv_i8_{m}x{n}.md"
+def profiled_traffic(name):
+    """DRAM bytes (read + write) per launch from the committed ncu summary
+    profiles/<name>.md (its traffic_bytes_per_launch line), or None."""
+    f = ROOT / "profiles" / f"{name}.md"
     try:
         for line in f.read_text().splitlines():
             if line.startswith("traffic_bytes_per_launch:"):

@@ -476,8 +476,9 @@ __device__ __forceinline__ void gemv_consume_stage_xs(const unsigned char* stage
 }
 
 // Compile-time shaped stage with x read from shared memory: RS rows per matrix,
-// NM matrices, all NR = RS * NM rows reduced by one exchange butterfly.
-template <typename WT, int RS, int NM>
+// NM matrices, all NR = RS * NM rows reduced by one exchange butterfly; KB = most
+// 16-byte blocks a thread owns in a row (the block loop is unrolled).
+template <typename WT, int RS, int NM, int KB>
 __device__ __forceinline__ void gemv_consume_stage_xt(const unsigned char* stage, uint32_t row_bytes, int nblk,
                                                       int slotid, int lane, int gwarp, const float* xs,
                                                       float* part, int rl0, int nr) {
@@ -488,8 +489,10 @@ __device__ __forceinline__ void gemv_consume_stage_xt(const unsigned char* stage
     float2 a01[NR], a23[NR];
 #pragma unroll
     for (int r = 0; r < NR; ++r) a01[r] = a23[r] = make_float2(0.0f, 0.0f);
-#pragma unroll 1
-    for (int b = slotid; b < nblk; b += 256) {
+#pragma unroll
+    for (int k = 0; k < KB; ++k) {
+        const int b = slotid + 256 * k;
+        if (b >= nblk) break;
         float2 xb[EPB / 2];
 #pragma unroll
         for (int q = 0; q < EPB / 4; ++q) {
@@ -525,7 +528,7 @@ __device__ __forceinline__ void gemv_consume_stage_xt(const unsigned char* stage
     }
 }
 
-template <typename WT, int RS, int NM>
+template <typename WT, int RS, int NM, int KB>
 __device__ __forceinline__ bool gemv_consume_xt(const GemvParams& p, int r0, int r1, const unsigned char* ring,
                                                 uint32_t slot_stride, int NS, uint64_t* full, uint64_t* empty,
                                                 int& j, int group, int gwarp, int lane, int slotid, const float* xs,
@@ -538,7 +541,7 @@ __device__ __forceinline__ bool gemv_consume_xt(const GemvParams& p, int r0, int
         const int slot = j % NS;
         if ((slot & 1) == group) {
             if (!mbar_wait_bounded(&full[slot], (uint32_t)((j / NS) & 1))) return false;
-            gemv_consume_stage_xt<WT, RS, NM>(ring + (size_t)slot * slot_stride, row_bytes, nblk, slotid, lane,
+            gemv_consume_stage_xt<WT, RS, NM, KB>(ring + (size_t)slot * slot_stride, row_bytes, nblk, slotid, lane,
                                               gwarp, xs, part, cur - r0, sr.nr);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);

@@ -451,14 +451,14 @@ __device__ __forceinline__ bool tk_gemv(const GemvParams& p, int unit, int rs, i
     const int slotid = tid % 256;
     bool okc;
     if (paired) {
-        okc = rs == 4 ? gemv_consume_xt<WT, 4, 2>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp,
+        okc = rs == 4 ? gemv_consume_xt<WT, 4, 2, 1>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp,
                                                    lane, slotid, vec, part)
-                      : gemv_consume_xt<WT, 1, 2>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp,
+                      : gemv_consume_xt<WT, 1, 2, 3>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp,
                                                    lane, slotid, vec, part);
     } else {
-        okc = rs == 8 ? gemv_consume_xt<WT, 8, 1>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp,
+        okc = rs == 8 ? gemv_consume_xt<WT, 8, 1, 1>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp,
                                                    lane, slotid, vec, part)
-                      : gemv_consume_xt<WT, 2, 1>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp,
+                      : gemv_consume_xt<WT, 2, 1, 3>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp,
                                                    lane, slotid, vec, part);
     }
     ok = okc && ok;

@@ -57,7 +57,7 @@ def timed(torch, fn, items, reps):
 
 
 def decode(torch, pkg, args):
-    plan = pkg.synth.config_plan(args.config)
+    plan = pkg.synth.config_plan(args.config, n_layers=args.layers)
     if not 0 <= args.pos or args.pos + args.tokens + 1 > plan["max_seq"]:
         raise SystemExit("--pos + --tokens + 1 must fit max_seq")
     stream = torch.cuda.Stream()
@@ -74,7 +74,7 @@ def decode(torch, pkg, args):
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1000.0 / args.tokens
     nbytes = sum(pkg.synth.bytes_per_token(plan, args.pos + 2 + i) for i in range(args.tokens)) / args.tokens
-    print(json.dumps({"kernel": "decode_step", "config": args.config, "pos": args.pos,
+    print(json.dumps({"kernel": "decode_step", "config": args.config, "layers": plan["n_layers"], "pos": args.pos,
                       "tokens": args.tokens, "kernels_per_token": int(dec.query("kernels_per_step")),
                       "us_per_token": us, "bytes_per_token": nbytes,
                       "gbs": nbytes / (us * 1e-6) / 1e9}), flush=True)
@@ -101,6 +101,7 @@ def main():
     d.add_argument("--config", default="llama2-7b")
     d.add_argument("--pos", type=int, default=512)
     d.add_argument("--tokens", type=int, default=8)
+    d.add_argument("--layers", type=int, default=None, help="fewer layers (small profiler captures)")
     args = ap.parse_args()
 
     import torch

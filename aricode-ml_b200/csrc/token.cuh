@@ -408,6 +408,32 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
     return true;
 }
 
+// Long rows (up to 3 blocks a thread, 2 rows a stage): this thread's slice of the
+// normalised x is read once from shared memory into registers, then the stages
+// run as in gemv_kernel (few rows per stage: x from registers keeps the shared
+// memory traffic at the weight bytes).
+template <typename WT, int RS, bool PAIRED>
+__device__ __forceinline__ bool tk_consume_xreg(const GemvParams& p, int r0, int r1, const unsigned char* ring,
+                                                int NS, uint64_t* full, uint64_t* empty, int& j, int group,
+                                                int gwarp, int lane, int slotid, const float* xs, float* part) {
+    constexpr int EPB = GemvElems<WT>::EPB;
+    const int nblk = (int)(((size_t)p.ld * sizeof(WT)) >> 4);
+    float2 xr[3][EPB / 2];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        const int b = slotid + 256 * k;
+#pragma unroll
+        for (int q = 0; q < EPB / 4; ++q) {
+            float4 x4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (b < nblk) x4 = lds128f(xs + b * EPB + 4 * q);
+            xr[k][2 * q] = make_float2(x4.x, x4.y);
+            xr[k][2 * q + 1] = make_float2(x4.z, x4.w);
+        }
+    }
+    return gemv_consume<WT, 3, RS, PAIRED>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp, lane,
+                                           slotid, xr, part, true);
+}
+
 // --------------------------------------------------------------------- GEMV phase
 // One compiled copy per weight type: any row length (blocks per thread at run
 // time), rows per stage and pairing at run time. x and its norm gains are staged
@@ -453,13 +479,13 @@ __device__ __forceinline__ bool tk_gemv(const GemvParams& p, int unit, int rs, i
     if (paired) {
         okc = rs == 4 ? gemv_consume_xt<WT, 4, 2, 1>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp,
                                                    lane, slotid, vec, part)
-                      : gemv_consume_xt<WT, 1, 2, 3>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp,
-                                                   lane, slotid, vec, part);
+                      : tk_consume_xreg<WT, 1, true>(p, r0, r1, ring, NS, full, empty, j, group, gwarp, lane, slotid,
+                                                      vec, part);
     } else {
         okc = rs == 8 ? gemv_consume_xt<WT, 8, 1, 1>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp,
                                                    lane, slotid, vec, part)
-                      : gemv_consume_xt<WT, 2, 1, 3>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp,
-                                                   lane, slotid, vec, part);
+                      : tk_consume_xreg<WT, 2, false>(p, r0, r1, ring, NS, full, empty, j, group, gwarp, lane, slotid,
+                                                       vec, part);
     }
     ok = okc && ok;
     consumer_bar();

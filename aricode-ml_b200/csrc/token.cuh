@@ -83,22 +83,23 @@ static_assert(kTkDescOffset % 16 == 0 && kTkDescBytes % 16 == 0, "descriptor ali
 static_assert(kTkPartOffset % 16 == 0, "part alignment");
 
 // Copy a phase descriptor from the table (global, read-only) into shared memory,
-// 16 bytes per load, across `nthreads` threads, loads issued in batches of 16: its
+// 16 bytes per load, across `nthreads` threads, B loads in flight per thread: its
 // fields are then read at shared-memory latency instead of one dependent L2 round
 // trip each.
+template <int B>
 __device__ __forceinline__ void tk_copy_desc(TkPhase* dst, const TkPhase* src, int t, int nthreads) {
     constexpr int NV = (int)(sizeof(TkPhase) / 16);
     const uint4* s = reinterpret_cast<const uint4*>(src);
     uint4* d = reinterpret_cast<uint4*>(dst);
-    for (int w0 = t; w0 < NV; w0 += 16 * nthreads) {
-        uint4 v[16];
+    for (int w0 = t; w0 < NV; w0 += B * nthreads) {
+        uint4 v[B];
 #pragma unroll
-        for (int u = 0; u < 16; ++u) {
+        for (int u = 0; u < B; ++u) {
             const int w = w0 + u * nthreads;
             if (w < NV) v[u] = __ldg(s + w);
         }
 #pragma unroll
-        for (int u = 0; u < 16; ++u) {
+        for (int u = 0; u < B; ++u) {
             const int w = w0 + u * nthreads;
             if (w < NV) d[w] = v[u];
         }
@@ -137,34 +138,30 @@ __device__ __forceinline__ void group_bar(int group) {
     asm volatile("bar.sync %0, 256;" ::"r"(2 + group) : "memory");
 }
 
-// Grid barrier among the consumers of all CTAs: every CTA adds one arrival and
-// waits until `target` arrivals are visible. Bounded: false after ~1 s, and at
-// once when this CTA has already failed (*abort set). The result is the same for
-// every consumer thread of the CTA.
+// Grid barrier among the consumers of all CTAs: every CTA adds one arrival
+// (release) and waits until `target` arrivals are visible (acquire). Bounded:
+// false after ~1 s, and at once when this CTA has already failed (*abort set).
+// The result is the same for every consumer thread of the CTA; `flag` alternates
+// between two slots (phase parity), so one barrier publishes it.
 __device__ __forceinline__ bool tk_grid_sync(unsigned* ctr, unsigned target, int tid, volatile int* flag,
                                              volatile int* abort) {
     consumer_bar();
     if (tid == 0) {
         bool ok = *abort == 0;
         if (ok) {
-            __threadfence();
-            atomicAdd(ctr, 1u);
+            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
             if (ld_acquire_gpu(ctr) < target) {
                 const uint64_t t0 = globaltimer_ns();
                 for (uint32_t it = 1;; ++it) {
-                    __nanosleep(32);
                     if (ld_acquire_gpu(ctr) >= target) break;
-                    if ((it & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) { ok = false; break; }
+                    if ((it & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) { ok = false; break; }
                 }
             }
-            __threadfence();
         }
         *flag = ok ? 1 : 0;
     }
     consumer_bar();
-    const bool ok = *flag != 0;
-    consumer_bar();                                     // flag is rewritten by the next call
-    return ok;
+    return *flag != 0;
 }
 
 // Wait for a ring stage with one decision for the whole consumer group: one thread
@@ -516,8 +513,8 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);                 // [kTkMaxSlots]
     uint64_t* empty = full + 8;                                          // [kTkMaxSlots]
     float* red = reinterpret_cast<float*>(smem + 128);                   // 8 floats
-    volatile int* flag = reinterpret_cast<volatile int*>(smem + 192);    // [0] grid sync, [2..3] groups
-    volatile int* abort = reinterpret_cast<volatile int*>(smem + 208);
+    volatile int* flag = reinterpret_cast<volatile int*>(smem + 192);    // [0], [4] grid sync, [2..3] groups
+    volatile int* abort = reinterpret_cast<volatile int*>(smem + 212);
     uint64_t* vbar = reinterpret_cast<uint64_t*>(smem + 216);           // vector staging
     float* vec = reinterpret_cast<float*>(smem + P.vec_offset);
     float* scratch = reinterpret_cast<float*>(smem + kTkScratchOffset);
@@ -570,7 +567,7 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
             bool ok = true;
             TkPhase* pdesc = reinterpret_cast<TkPhase*>(smem + kTkDescOffset + 2 * kTkDescBytes);
             for (int ph = 0; ph < P.nphases && ok; ++ph) {
-                tk_copy_desc(pdesc, P.phases + ph, 0, 1);
+                tk_copy_desc<16>(pdesc, P.phases + ph, 0, 1);
                 const TkPhase& T = *pdesc;
                 if (T.kind == TK_GEMV) {
                     const GemvParams& p = T.g;
@@ -609,19 +606,23 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
     unsigned arrivals = 0;
     uint32_t vphase = 0;                                // phases of vbar used so far
     TkPhase* cdesc = reinterpret_cast<TkPhase*>(smem + kTkDescOffset);      // [2]: phase ph in ph & 1
-    tk_copy_desc(cdesc, P.phases, tid, kGemvConsumerThreads);
+    tk_copy_desc<1>(cdesc, P.phases, tid, kGemvConsumerThreads);
     consumer_bar();
     for (int ph = 0; ph < P.nphases; ++ph) {
         const TkPhase& T = cdesc[ph & 1];
         if (ph > 0) {
             arrivals += (unsigned)ncta;
-            if (!tk_grid_sync(P.bar, arrivals, tid, flag, abort)) {
+            if (!tk_grid_sync(P.bar, arrivals, tid, flag + 4 * (ph & 1), abort)) {
                 if (tid == 0) *abort = 1;
                 break;
             }
         }
         unsigned long long* tr = P.trace ? P.trace + ((size_t)ph * ncta + cta) * kTkStamps : nullptr;
         tk_stamp(tr, 0, tid);
+        // the next phase's descriptor, by the last consumer warps (in place after the
+        // next grid barrier; the buffer it overwrites was last read in phase ph - 1)
+        if (ph + 1 < P.nphases && tid >= kGemvConsumerThreads - 64)
+            tk_copy_desc<1>(cdesc + ((ph + 1) & 1), P.phases + ph + 1, tid - (kGemvConsumerThreads - 64), 64);
         bool ok = true;
         if (T.kind == TK_EMBED) {
             if (cta == 0) {
@@ -655,9 +656,6 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
             tk_stamp(tr, 4, tid);
         }
         if (!ok) *abort = 1;
-        // the next phase's descriptor, in place after the grid barrier (the buffer
-        // it overwrites was last read in phase ph - 1)
-        if (ph + 1 < P.nphases) tk_copy_desc(cdesc + ((ph + 1) & 1), P.phases + ph + 1, tid, kGemvConsumerThreads);
     }
     consumer_bar();
     if (tid == 0) {

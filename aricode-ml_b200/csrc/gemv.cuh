@@ -532,12 +532,12 @@ template <typename WT, int RS, int NM, int KB>
 __device__ __forceinline__ bool gemv_consume_xt(const GemvParams& p, int r0, int r1, const unsigned char* ring,
                                                 uint32_t slot_stride, int NS, uint64_t* full, uint64_t* empty,
                                                 int& j, int group, int gwarp, int lane, int slotid, const float* xs,
-                                                float* part) {
+                                                float* part, int rows = RS) {
     const uint32_t row_bytes = (uint32_t)p.ld * (uint32_t)sizeof(WT);
     const int nblk = (int)(row_bytes >> 4);
     int cur = r0;
     while (cur < r1) {
-        const StageRows sr = next_stage(p, cur, r1, RS);
+        const StageRows sr = next_stage(p, cur, r1, rows);
         const int slot = j % NS;
         if ((slot & 1) == group) {
             if (!mbar_wait_bounded(&full[slot], (uint32_t)((j / NS) & 1))) return false;
@@ -720,10 +720,12 @@ __device__ __forceinline__ bool gemv_consume_rt(const GemvParams& p, int r0, int
 template <int NM>
 __device__ __forceinline__ bool gemv_produce(const GemvParams& p, int r0, int r1, int RS, uint32_t row_bytes,
                                              unsigned char* ring, uint32_t slot_stride, int NS,
-                                             uint64_t* full, uint64_t* empty, int& j, int inflight = 0) {
+                                             uint64_t* full, uint64_t* empty, int& j, int inflight = 0,
+                                             int rows = 0) {
+    const int R = rows > 0 ? rows : RS;          // rows per stage (<= RS, the paired matrix offset)
     int cur = r0;
     while (cur < r1) {
-        const StageRows sr = next_stage(p, cur, r1, RS);
+        const StageRows sr = next_stage(p, cur, r1, R);
         const int slot = j % NS, round = j / NS;
         if (round > 0 && !mbar_wait_bounded(&empty[slot], (uint32_t)((round - 1) & 1))) return false;
         if (inflight > 0 && j >= inflight &&
@@ -752,12 +754,12 @@ __device__ __forceinline__ bool gemv_consume(const GemvParams& p, int r0, int r1
                                              uint32_t slot_stride, int NS, uint64_t* full, uint64_t* empty,
                                              int& j, int group, int gwarp, int lane, int slotid,
                                              const float2 (&xr)[KMAX][GemvElems<WT>::EPB / 2], float* part,
-                                             bool compute) {
+                                             bool compute, int rows = RS) {
     const uint32_t row_bytes = (uint32_t)p.ld * (uint32_t)sizeof(WT);
     const int nblk = (int)(row_bytes >> 4);
     int cur = r0;
     while (cur < r1) {
-        const StageRows sr = next_stage(p, cur, r1, RS);
+        const StageRows sr = next_stage(p, cur, r1, rows);
         const int slot = j % NS;
         if ((slot & 1) == group) {
             if (!mbar_wait_bounded(&full[slot], (uint32_t)((j / NS) & 1))) return false;

@@ -638,6 +638,7 @@ bool tk_phase_of(const b2_ctx* c, const Op& o, TkPhase& T, size_t& part_bytes, s
     const long long units = (total + T.unit - 1) / T.unit;
     const long long rows_cta = (units + c->sm_count - 1) / c->sm_count * T.unit;
     part_bytes = std::max(part_bytes, (size_t)rows_cta * ((paired ? 2 : 1) * 8 + 4) * sizeof(float));
+    T.rows = T.rs;                      // rows per stage (the compiled capacity: all of it is computed)
     // x and its norm gains staged in shared memory: n % 4 (16-byte bulk copies),
     // 16-aligned pointers, L = n rounded up to 16 covering the padded rows
     const size_t L = ((size_t)g.n + 15) & ~(size_t)15;

@@ -72,7 +72,8 @@ struct alignas(16) TkPhase {
     int kind;
     int variant;        // TK_GEMV
     int unit;           // rows per balancing unit (2 keeps RoPE pairs in one CTA)
-    int rs;             // rows per stage of the variant
+    int rs;             // rows per stage the variant is compiled for (paired: second matrix offset)
+    int rows;           // rows per stage used (<= rs; chosen so the two groups get equal stage counts)
     GemvParams g;
     AttnParams a;
     EmbedParams e;
@@ -412,7 +413,8 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
 template <typename WT, int RS, bool PAIRED>
 __device__ __forceinline__ bool tk_consume_xreg(const GemvParams& p, int r0, int r1, const unsigned char* ring,
                                                 int NS, uint64_t* full, uint64_t* empty, int& j, int group,
-                                                int gwarp, int lane, int slotid, const float* xs, float* part) {
+                                                int gwarp, int lane, int slotid, const float* xs, float* part,
+                                                int rows) {
     constexpr int EPB = GemvElems<WT>::EPB;
     const int nblk = (int)(((size_t)p.ld * sizeof(WT)) >> 4);
     float2 xr[3][EPB / 2];
@@ -428,7 +430,7 @@ __device__ __forceinline__ bool tk_consume_xreg(const GemvParams& p, int r0, int
         }
     }
     return gemv_consume<WT, 3, RS, PAIRED>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp, lane,
-                                           slotid, xr, part, true);
+                                           slotid, xr, part, true, rows);
 }
 
 // --------------------------------------------------------------------- GEMV phase
@@ -438,7 +440,8 @@ __device__ __forceinline__ bool tk_consume_xreg(const GemvParams& p, int r0, int
 // L = n rounded up to 16, zeros in [n, L)), normalised in place, and read by the
 // stages from there.
 template <typename WT>
-__device__ __forceinline__ bool tk_gemv(const GemvParams& p, int unit, int rs, int pos, const unsigned char* ring,
+__device__ __forceinline__ bool tk_gemv(const GemvParams& p, int unit, int rs, int rows, int pos,
+                                        const unsigned char* ring,
                                         int NS, uint64_t* full, uint64_t* empty, int& j, int group, int gwarp,
                                         int lane, int tid, float* red, float* part, int cta, int ncta,
                                         unsigned long long* tr, float* vec, uint64_t* vbar, uint32_t& vphase) {
@@ -475,14 +478,14 @@ __device__ __forceinline__ bool tk_gemv(const GemvParams& p, int unit, int rs, i
     bool okc;
     if (paired) {
         okc = rs == 4 ? gemv_consume_xt<WT, 4, 2, 1>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp,
-                                                   lane, slotid, vec, part)
+                                                   lane, slotid, vec, part, rows)
                       : tk_consume_xreg<WT, 1, true>(p, r0, r1, ring, NS, full, empty, j, group, gwarp, lane, slotid,
-                                                      vec, part);
+                                                      vec, part, rows);
     } else {
         okc = rs == 8 ? gemv_consume_xt<WT, 8, 1, 1>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp,
-                                                   lane, slotid, vec, part)
+                                                   lane, slotid, vec, part, rows)
                       : tk_consume_xreg<WT, 2, false>(p, r0, r1, ring, NS, full, empty, j, group, gwarp, lane, slotid,
-                                                       vec, part);
+                                                       vec, part, rows);
     }
     ok = okc && ok;
     consumer_bar();
@@ -500,9 +503,9 @@ __device__ __forceinline__ bool tk_gemv_dispatch(const TkPhase& T, int pos, cons
                                                  unsigned long long* tr, float* vec, uint64_t* vbar,
                                                  uint32_t& vphase) {
     if (VS == 1 && T.variant >= TV_F32_K1_R8)
-        return tk_gemv<float>(T.g, T.unit, T.rs, pos, ring, NS, full, empty, j, group, gwarp, lane, tid, red, part,
+        return tk_gemv<float>(T.g, T.unit, T.rs, T.rows, pos, ring, NS, full, empty, j, group, gwarp, lane, tid, red, part,
                               cta, ncta, tr, vec, vbar, vphase);
-    return tk_gemv<int8_t>(T.g, T.unit, T.rs, pos, ring, NS, full, empty, j, group, gwarp, lane, tid, red, part, cta,
+    return tk_gemv<int8_t>(T.g, T.unit, T.rs, T.rows, pos, ring, NS, full, empty, j, group, gwarp, lane, tid, red, part, cta,
                            ncta, tr, vec, vbar, vphase);
 }
 
@@ -577,9 +580,9 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
                     const uint32_t row_bytes = (uint32_t)p.ld * (i8 ? 1u : 4u);
                     tk_prefetch_vectors(p, r0, r1, pos, i8);
                     ok = p.paired ? gemv_produce<2>(p, r0, r1, T.rs, row_bytes, ring, kTkSlotBytes, NS, full, empty, j,
-                                                    P.inflight)
+                                                    P.inflight, T.rows)
                                   : gemv_produce<1>(p, r0, r1, T.rs, row_bytes, ring, kTkSlotBytes, NS, full, empty, j,
-                                                    P.inflight);
+                                                    P.inflight, T.rows);
                 } else if (T.kind == TK_ATTN) {
                     ok = tk_attn_produce(T.a, pos + 1, cta, ncta, ring, NS, full, empty, j, P.inflight);
                 }

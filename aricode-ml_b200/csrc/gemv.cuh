@@ -105,6 +105,15 @@ __device__ __forceinline__ void fma_word2(float2& a01, float2& a23, uint32_t u, 
     a23 = __ffma2_rn(w23, x23, a23);
 }
 
+// int8 codes as the magic-number conversion wants them: b ^ 0x80 per byte. PRE:
+// the weights are stored that way already (the model arenas of the token kernel,
+// biased once at load), so no per-word XOR is needed.
+template <bool PRE>
+__device__ __forceinline__ uint32_t bias_codes(uint32_t w) {
+    if constexpr (PRE) return w;
+    else return w ^ 0x80808080u;
+}
+
 __device__ __forceinline__ void consumer_bar() {
     asm volatile("bar.sync 1, %0;" ::"r"(kGemvConsumerThreads) : "memory");
 }
@@ -318,71 +327,6 @@ __device__ __forceinline__ void gemv_load_x(const GemvParams& p, float2 (&xr)[KM
     }
 }
 
-// The prologue of gemv_load_x with x (and the norm gains) already in shared
-// memory: xs[n], gs[n], bs[n] (plain loads). Same arithmetic, same order.
-template <typename WT, int KMAX>
-__device__ __forceinline__ void gemv_load_x_smem(const GemvParams& p, const float* xs, const float* gs,
-                                                 const float* bs, float2 (&xr)[KMAX][GemvElems<WT>::EPB / 2],
-                                                 float* red, int tid) {
-    constexpr int EPB = GemvElems<WT>::EPB;
-    const int n = p.n;
-    const int slotid = tid % 256;
-    const int nblk = (int)(((size_t)p.ld * sizeof(WT)) >> 4);
-    const int K = (nblk + 255) / 256;
-    float scale_a = 1.0f, shift_m = 0.0f;
-    if (p.norm == NORM_RMS) {
-        float a = 0.0f;
-        if (tid < 256)
-            for (int i = tid; i < n; i += 256) { const float v = xs[i]; a = ffma(v, v, a); }
-        const float tot = consumer_reduce256(a, red, tid);
-        const float ms = fdiv(tot, (float)n);
-        scale_a = fdiv(1.0f, __fsqrt_rn(fadd(ms, p.eps)));
-    } else if (p.norm == NORM_LN) {
-        float a = 0.0f;
-        if (tid < 256)
-            for (int i = tid; i < n; i += 256) a = fadd(a, xs[i]);
-        shift_m = fdiv(consumer_reduce256(a, red, tid), (float)n);
-        a = 0.0f;
-        if (tid < 256)
-            for (int i = tid; i < n; i += 256) { const float dx = fsub(xs[i], shift_m); a = ffma(dx, dx, a); }
-        const float var = fdiv(consumer_reduce256(a, red, tid), (float)n);
-        scale_a = fdiv(1.0f, __fsqrt_rn(fadd(var, p.eps)));
-    }
-    // the slice, 16 bytes at a time (n % 4 == 0)
-#pragma unroll
-    for (int k = 0; k < KMAX; ++k) {
-        const int b = slotid + 256 * k;
-#pragma unroll
-        for (int q = 0; q < EPB / 4; ++q) {
-            const int i0 = b * EPB + 4 * q;
-            float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            if (k < K && b < nblk && i0 < n) {
-                const float4 x4 = *reinterpret_cast<const float4*>(xs + i0);
-                const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
-                float g[4] = {0.0f, 0.0f, 0.0f, 0.0f}, bb[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-                if (p.norm != NORM_NONE) {
-                    const float4 g4 = *reinterpret_cast<const float4*>(gs + i0);
-                    g[0] = g4.x; g[1] = g4.y; g[2] = g4.z; g[3] = g4.w;
-                }
-                if (p.norm == NORM_LN) {
-                    const float4 b4 = *reinterpret_cast<const float4*>(bs + i0);
-                    bb[0] = b4.x; bb[1] = b4.y; bb[2] = b4.z; bb[3] = b4.w;
-                }
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    if (p.norm == NORM_RMS) v[e] = fmul(fmul(xv[e], scale_a), g[e]);
-                    else if (p.norm == NORM_LN)
-                        v[e] = (float)dadd(dmul((double)fmul(fsub(xv[e], shift_m), scale_a), (double)g[e]),
-                                           (double)bb[e]);
-                    else v[e] = xv[e];
-                }
-            }
-            xr[k][2 * q] = make_float2(v[0], v[1]);
-            xr[k][2 * q + 1] = make_float2(v[2], v[3]);
-        }
-    }
-}
-
 // ---------------------------------------------------------------------------
 // x in shared memory (token kernel): the vector is staged once per CTA and phase
 // at xs[0 .. L) (zeros past n, L = n rounded up to 16), its norm gains at gs[],
@@ -422,63 +366,10 @@ __device__ __forceinline__ void gemv_norm_smem(const GemvParams& p, float* xs, c
     }
 }
 
-template <typename WT, int NH>
-__device__ __forceinline__ void gemv_consume_stage_xs(const unsigned char* stage, uint32_t row_bytes, int nblk,
-                                                      int slotid, int lane, int gwarp, const float* xs,
-                                                      float* part, int rl0, int nr, int RS, int NM) {
-    constexpr int ESZ = (int)sizeof(WT);
-    constexpr int EPB = GemvElems<WT>::EPB;
-    constexpr int LG = Log2<NH>::v;
-    const int NR = RS * NM;
-#pragma unroll 1
-    for (int h0 = 0; h0 < NR; h0 += NH) {
-        float2 a01[NH], a23[NH];
-#pragma unroll
-        for (int r = 0; r < NH; ++r) a01[r] = a23[r] = make_float2(0.0f, 0.0f);
-#pragma unroll 1
-        for (int b = slotid; b < nblk; b += 256) {
-            float2 xb[EPB / 2];
-#pragma unroll
-            for (int q = 0; q < EPB / 4; ++q) {
-                const float4 x4 = lds128f(xs + b * EPB + 4 * q);
-                xb[2 * q] = make_float2(x4.x, x4.y);
-                xb[2 * q + 1] = make_float2(x4.z, x4.w);
-            }
-#pragma unroll
-            for (int r = 0; r < NH; ++r) {
-                if (h0 + r >= NR) break;
-                const unsigned char* row = stage + (size_t)(h0 + r) * row_bytes + 16 * b;
-                if constexpr (ESZ == 1) {
-                    const uint4 w = lds128(row);
-                    fma_word2(a01[r], a23[r], w.x ^ 0x80808080u, xb[0], xb[1]);
-                    fma_word2(a01[r], a23[r], w.y ^ 0x80808080u, xb[2], xb[3]);
-                    fma_word2(a01[r], a23[r], w.z ^ 0x80808080u, xb[4], xb[5]);
-                    fma_word2(a01[r], a23[r], w.w ^ 0x80808080u, xb[6], xb[7]);
-                } else {
-                    const float4 w = lds128f(row);
-                    a01[r] = __ffma2_rn(make_float2(w.x, w.y), xb[0], a01[r]);
-                    a23[r] = __ffma2_rn(make_float2(w.z, w.w), xb[1], a23[r]);
-                }
-            }
-        }
-        float v[NH];
-#pragma unroll
-        for (int r = 0; r < NH; ++r) v[r] = fadd(fadd(a01[r].x, a01[r].y), fadd(a23[r].x, a23[r].y));
-        exchange_butterfly<NH>(v, lane);
-        if ((lane & ((32 >> LG) - 1)) == 0) {
-            const int rr = h0 + (lane >> (5 - LG));
-            if (rr < NR) {
-                const int m = rr / RS, r = rr - m * RS;
-                if (r < nr) part[((rl0 + r) * NM + m) * 8 + gwarp] = v[0];
-            }
-        }
-    }
-}
-
 // Compile-time shaped stage with x read from shared memory: RS rows per matrix,
 // NM matrices, all NR = RS * NM rows reduced by one exchange butterfly; KB = most
 // 16-byte blocks a thread owns in a row (the block loop is unrolled).
-template <typename WT, int RS, int NM, int KB>
+template <typename WT, int RS, int NM, int KB, bool PRE = false>
 __device__ __forceinline__ void gemv_consume_stage_xt(const unsigned char* stage, uint32_t row_bytes, int nblk,
                                                       int slotid, int lane, int gwarp, const float* xs,
                                                       float* part, int rl0, int nr) {
@@ -506,10 +397,10 @@ __device__ __forceinline__ void gemv_consume_stage_xt(const unsigned char* stage
             const unsigned char* row = stage + (size_t)r * row_bytes + 16 * b;
             if constexpr (ESZ == 1) {
                 const uint4 w = lds128(row);
-                fma_word2(a01[r], a23[r], w.x ^ 0x80808080u, xb[0], xb[1]);
-                fma_word2(a01[r], a23[r], w.y ^ 0x80808080u, xb[2], xb[3]);
-                fma_word2(a01[r], a23[r], w.z ^ 0x80808080u, xb[4], xb[5]);
-                fma_word2(a01[r], a23[r], w.w ^ 0x80808080u, xb[6], xb[7]);
+                fma_word2(a01[r], a23[r], bias_codes<PRE>(w.x), xb[0], xb[1]);
+                fma_word2(a01[r], a23[r], bias_codes<PRE>(w.y), xb[2], xb[3]);
+                fma_word2(a01[r], a23[r], bias_codes<PRE>(w.z), xb[4], xb[5]);
+                fma_word2(a01[r], a23[r], bias_codes<PRE>(w.w), xb[6], xb[7]);
             } else {
                 const float4 w = lds128f(row);
                 a01[r] = __ffma2_rn(make_float2(w.x, w.y), xb[0], a01[r]);
@@ -528,7 +419,7 @@ __device__ __forceinline__ void gemv_consume_stage_xt(const unsigned char* stage
     }
 }
 
-template <typename WT, int RS, int NM, int KB>
+template <typename WT, int RS, int NM, int KB, bool PRE = false>
 __device__ __forceinline__ bool gemv_consume_xt(const GemvParams& p, int r0, int r1, const unsigned char* ring,
                                                 uint32_t slot_stride, int NS, uint64_t* full, uint64_t* empty,
                                                 int& j, int group, int gwarp, int lane, int slotid, const float* xs,
@@ -541,33 +432,8 @@ __device__ __forceinline__ bool gemv_consume_xt(const GemvParams& p, int r0, int
         const int slot = j % NS;
         if ((slot & 1) == group) {
             if (!mbar_wait_bounded(&full[slot], (uint32_t)((j / NS) & 1))) return false;
-            gemv_consume_stage_xt<WT, RS, NM, KB>(ring + (size_t)slot * slot_stride, row_bytes, nblk, slotid, lane,
+            gemv_consume_stage_xt<WT, RS, NM, KB, PRE>(ring + (size_t)slot * slot_stride, row_bytes, nblk, slotid, lane,
                                               gwarp, xs, part, cur - r0, sr.nr);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[slot]);
-        }
-        ++j;
-        cur += sr.nr;
-    }
-    return true;
-}
-
-template <typename WT, int NH>
-__device__ __forceinline__ bool gemv_consume_xs(const GemvParams& p, int r0, int r1, int RS,
-                                                const unsigned char* ring, uint32_t slot_stride, int NS,
-                                                uint64_t* full, uint64_t* empty, int& j, int group, int gwarp,
-                                                int lane, int slotid, const float* xs, float* part) {
-    const uint32_t row_bytes = (uint32_t)p.ld * (uint32_t)sizeof(WT);
-    const int nblk = (int)(row_bytes >> 4);
-    const int NM = p.paired ? 2 : 1;
-    int cur = r0;
-    while (cur < r1) {
-        const StageRows sr = next_stage(p, cur, r1, RS);
-        const int slot = j % NS;
-        if ((slot & 1) == group) {
-            if (!mbar_wait_bounded(&full[slot], (uint32_t)((j / NS) & 1))) return false;
-            gemv_consume_stage_xs<WT, NH>(ring + (size_t)slot * slot_stride, row_bytes, nblk, slotid, lane, gwarp, xs,
-                                          part, cur - r0, sr.nr, RS, NM);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
         }
@@ -581,7 +447,7 @@ __device__ __forceinline__ bool gemv_consume_xs(const GemvParams& p, int r0, int
 // row_bytes; the second matrix starts RS rows in). Writes this warp's sums to
 // part[(row * NM + m) * 8 + gwarp] for rows rl0 .. rl0 + nr - 1 of the CTA. Rows
 // are reduced four at a time (each row's butterfly is the same either way).
-template <typename WT, int KMAX, int RS, bool PAIRED>
+template <typename WT, int KMAX, int RS, bool PAIRED, bool PRE = false>
 __device__ __forceinline__ void gemv_consume_stage(const unsigned char* stage, uint32_t row_bytes, int nblk,
                                                    int slotid, int lane, int gwarp,
                                                    const float2 (&xr)[KMAX][GemvElems<WT>::EPB / 2],
@@ -607,10 +473,10 @@ __device__ __forceinline__ void gemv_consume_stage(const unsigned char* stage, u
                     const unsigned char* row = stage + (size_t)(h0 + r) * row_bytes + 16 * b;
                     if constexpr (ESZ == 1) {
                         const uint4 w = lds128(row);
-                        fma_word2(a01[r], a23[r], w.x ^ 0x80808080u, xr[k][0], xr[k][1]);
-                        fma_word2(a01[r], a23[r], w.y ^ 0x80808080u, xr[k][2], xr[k][3]);
-                        fma_word2(a01[r], a23[r], w.z ^ 0x80808080u, xr[k][4], xr[k][5]);
-                        fma_word2(a01[r], a23[r], w.w ^ 0x80808080u, xr[k][6], xr[k][7]);
+                        fma_word2(a01[r], a23[r], bias_codes<PRE>(w.x), xr[k][0], xr[k][1]);
+                        fma_word2(a01[r], a23[r], bias_codes<PRE>(w.y), xr[k][2], xr[k][3]);
+                        fma_word2(a01[r], a23[r], bias_codes<PRE>(w.z), xr[k][4], xr[k][5]);
+                        fma_word2(a01[r], a23[r], bias_codes<PRE>(w.w), xr[k][6], xr[k][7]);
                     } else {
                         const float4 w = lds128f(row);
                         a01[r] = __ffma2_rn(make_float2(w.x, w.y), xr[k][0], a01[r]);
@@ -629,87 +495,6 @@ __device__ __forceinline__ void gemv_consume_stage(const unsigned char* stage, u
             if (r < nr) part[((rl0 + r) * NM + m) * 8 + gwarp] = v[0];
         }
     }
-}
-
-// The same stage with its shape known only at run time (one compiled copy for
-// every row length up to KMAX blocks per thread, rows per stage and pairing):
-// NR = RS * NM rows at `stage`, reduced NH at a time; rows past NR are not read.
-// Each row's arithmetic is the one of gemv_consume_stage, so the bits are equal.
-template <typename WT, int KMAX, int NH>
-__device__ __forceinline__ void gemv_consume_stage_rt(const unsigned char* stage, uint32_t row_bytes, int nblk,
-                                                      int slotid, int lane, int gwarp,
-                                                      const float2 (&xr)[KMAX][GemvElems<WT>::EPB / 2],
-                                                      float* part, int rl0, int nr, int RS, int NM) {
-    constexpr int ESZ = (int)sizeof(WT);
-    constexpr int LG = Log2<NH>::v;
-    const int K = (nblk + 255) / 256;
-    const int NR = RS * NM;
-#pragma unroll 1
-    for (int h0 = 0; h0 < NR; h0 += NH) {
-        float2 a01[NH], a23[NH];
-#pragma unroll
-        for (int r = 0; r < NH; ++r) a01[r] = a23[r] = make_float2(0.0f, 0.0f);
-#pragma unroll
-        for (int k = 0; k < KMAX; ++k) {
-            const int b = slotid + 256 * k;
-            if (k < K && b < nblk) {
-#pragma unroll
-                for (int r = 0; r < NH; ++r) {
-                    if (h0 + r >= NR) break;
-                    const unsigned char* row = stage + (size_t)(h0 + r) * row_bytes + 16 * b;
-                    if constexpr (ESZ == 1) {
-                        const uint4 w = lds128(row);
-                        fma_word2(a01[r], a23[r], w.x ^ 0x80808080u, xr[k][0], xr[k][1]);
-                        fma_word2(a01[r], a23[r], w.y ^ 0x80808080u, xr[k][2], xr[k][3]);
-                        fma_word2(a01[r], a23[r], w.z ^ 0x80808080u, xr[k][4], xr[k][5]);
-                        fma_word2(a01[r], a23[r], w.w ^ 0x80808080u, xr[k][6], xr[k][7]);
-                    } else {
-                        const float4 w = lds128f(row);
-                        a01[r] = __ffma2_rn(make_float2(w.x, w.y), xr[k][0], a01[r]);
-                        a23[r] = __ffma2_rn(make_float2(w.z, w.w), xr[k][1], a23[r]);
-                    }
-                }
-            }
-        }
-        float v[NH];
-#pragma unroll
-        for (int r = 0; r < NH; ++r) v[r] = fadd(fadd(a01[r].x, a01[r].y), fadd(a23[r].x, a23[r].y));
-        exchange_butterfly<NH>(v, lane);
-        if ((lane & ((32 >> LG) - 1)) == 0) {
-            const int rr = h0 + (lane >> (5 - LG));        // stage row (m * RS + r)
-            if (rr < NR) {
-                const int m = rr / RS, r = rr - m * RS;
-                if (r < nr) part[((rl0 + r) * NM + m) * 8 + gwarp] = v[0];
-            }
-        }
-    }
-}
-
-// Consumer walk for the run-time shaped stage (see gemv_consume).
-template <typename WT, int KMAX, int NH>
-__device__ __forceinline__ bool gemv_consume_rt(const GemvParams& p, int r0, int r1, int RS,
-                                                const unsigned char* ring, uint32_t slot_stride, int NS,
-                                                uint64_t* full, uint64_t* empty, int& j, int group, int gwarp,
-                                                int lane, int slotid,
-                                                const float2 (&xr)[KMAX][GemvElems<WT>::EPB / 2], float* part) {
-    const uint32_t row_bytes = (uint32_t)p.ld * (uint32_t)sizeof(WT);
-    const int nblk = (int)(row_bytes >> 4);
-    const int NM = p.paired ? 2 : 1;
-    int cur = r0;
-    while (cur < r1) {
-        const StageRows sr = next_stage(p, cur, r1, RS);
-        const int slot = j % NS;
-        if ((slot & 1) == group) {
-            if (!mbar_wait_bounded(&full[slot], (uint32_t)((j / NS) & 1))) return false;
-            gemv_consume_stage_rt<WT, KMAX, NH>(ring + (size_t)slot * slot_stride, row_bytes, nblk, slotid, lane,
-                                                gwarp, xr, part, cur - r0, sr.nr, RS, NM);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[slot]);
-        }
-        ++j;
-        cur += sr.nr;
-    }
-    return true;
 }
 
 // Producer: issue the stages of rows [r0, r1) into the ring, one bulk copy per
@@ -749,7 +534,7 @@ __device__ __forceinline__ bool gemv_produce(const GemvParams& p, int r0, int r1
 // Consumers: walk the same stages; group g takes stage j when (j % NS) % 2 == g
 // (NS even, so every slot belongs to one group and its phases advance in order).
 // compute = false only releases the slots. Returns false on a timed-out wait.
-template <typename WT, int KMAX, int RS, bool PAIRED>
+template <typename WT, int KMAX, int RS, bool PAIRED, bool PRE = false>
 __device__ __forceinline__ bool gemv_consume(const GemvParams& p, int r0, int r1, const unsigned char* ring,
                                              uint32_t slot_stride, int NS, uint64_t* full, uint64_t* empty,
                                              int& j, int group, int gwarp, int lane, int slotid,
@@ -764,7 +549,7 @@ __device__ __forceinline__ bool gemv_consume(const GemvParams& p, int r0, int r1
         if ((slot & 1) == group) {
             if (!mbar_wait_bounded(&full[slot], (uint32_t)((j / NS) & 1))) return false;
             if (compute)
-                gemv_consume_stage<WT, KMAX, RS, PAIRED>(ring + (size_t)slot * slot_stride, row_bytes, nblk, slotid,
+                gemv_consume_stage<WT, KMAX, RS, PAIRED, PRE>(ring + (size_t)slot * slot_stride, row_bytes, nblk, slotid,
                                                          lane, gwarp, xr, part, cur - r0, sr.nr);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);

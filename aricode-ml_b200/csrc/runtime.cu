@@ -10,6 +10,7 @@
 // whole generation is a sequence of graph launches with no host round trips.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -755,6 +756,37 @@ void launch_token(b2_ctx* c, bool with_head, cudaStream_t s) {
 
 void capture_graphs_once(b2_ctx* c);
 
+// The token kernel reads the model's int8 GEMV matrices as biased codes (b ^ 0x80):
+// bias each distinct matrix once, in place (rows x ld bytes, ld % 16 == 0). Not
+// done (the token kernel is then disabled) when a GEMV matrix shares storage with
+// the embedding, which is read as plain codes.
+void bias_gemv_codes(b2_ctx* c) {
+    std::vector<const DevMat*> mats;
+    for (const Block& B : c->blocks) {
+        if (B.attn) {
+            for (const DevMat* m : {&B.q, &B.k, &B.v, &B.o}) if (m->i8) mats.push_back(m);
+        } else {
+            mats.push_back(&B.w1);
+            if (B.swiglu) mats.push_back(&B.w3);
+            mats.push_back(&B.w2);
+        }
+    }
+    mats.push_back(&c->lm);
+    std::vector<const void*> seen;
+    for (const DevMat* m : mats) {
+        if (m->w == c->emb.w) throw Err(B2_E_UNSUPPORTED, "a GEMV matrix shares the embedding's storage");
+    }
+    for (const DevMat* m : mats) {
+        if (std::find(seen.begin(), seen.end(), m->w) != seen.end()) continue;
+        seen.push_back(m->w);
+        const size_t n16 = (size_t)m->rows * m->ld / 16;
+        bias_codes_kernel<<<(unsigned)std::min<size_t>((n16 + 255) / 256, 4096), 256, 0, c->stream>>>(
+            reinterpret_cast<uint4*>(const_cast<void*>(m->w)), n16);
+        CK(cudaGetLastError());
+    }
+    CK(cudaStreamSynchronize(c->stream));
+}
+
 void capture_graphs(b2_ctx* c) {
     const char* env = std::getenv("B2_NO_PDL");
     c->pdl = !(env && env[0] == '1');
@@ -762,6 +794,7 @@ void capture_graphs(b2_ctx* c) {
     if (c->token) {
         try {
             capture_graphs_once(c);
+            bias_gemv_codes(c);
             return;
         } catch (const Err& e) {
             cudaGetLastError();

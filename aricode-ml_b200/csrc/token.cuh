@@ -23,6 +23,8 @@
 //   TK_EMBED  CTA 0 writes x = embedding row (+ learned position);
 //   TK_GEMV   the building blocks of gemv_kernel (gemv.cuh): prologue norm,
 //             stages, epilogue (residual, RoPE + KV append, SiLU*up, GELU, argmax);
+//             the int8 matrices of the model are stored biased (code ^ 0x80, done
+//             once when the token kernel is set up), which saves the per-word XOR;
 //   TK_ATTN   split-KV decode attention: item (query head h, 64-key split s) on
 //             CTA item % grid; the K chunk and V chunk arrive as two ring
 //             stages; the row of the current position (written by this step's
@@ -429,7 +431,8 @@ __device__ __forceinline__ bool tk_consume_xreg(const GemvParams& p, int r0, int
             xr[k][2 * q + 1] = make_float2(x4.z, x4.w);
         }
     }
-    return gemv_consume<WT, 3, RS, PAIRED>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp, lane,
+    return gemv_consume<WT, 3, RS, PAIRED, true>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp,
+                                                 lane,
                                            slotid, xr, part, true, rows);
 }
 
@@ -477,12 +480,12 @@ __device__ __forceinline__ bool tk_gemv(const GemvParams& p, int unit, int rs, i
     const int slotid = tid % 256;
     bool okc;
     if (paired) {
-        okc = rs == 4 ? gemv_consume_xt<WT, 4, 2, 1>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp,
+        okc = rs == 4 ? gemv_consume_xt<WT, 4, 2, 1, true>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp,
                                                    lane, slotid, vec, part, rows)
                       : tk_consume_xreg<WT, 1, true>(p, r0, r1, ring, NS, full, empty, j, group, gwarp, lane, slotid,
                                                       vec, part, rows);
     } else {
-        okc = rs == 8 ? gemv_consume_xt<WT, 8, 1, 1>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp,
+        okc = rs == 8 ? gemv_consume_xt<WT, 8, 1, 1, true>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp,
                                                    lane, slotid, vec, part, rows)
                       : tk_consume_xreg<WT, 2, false>(p, r0, r1, ring, NS, full, empty, j, group, gwarp, lane, slotid,
                                                        vec, part, rows);

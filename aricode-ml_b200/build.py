@@ -17,7 +17,7 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libb2dec.so"
 SOURCES = ["runtime.cu", "capi.cu", "noalloc.cu"]
-HEADERS = ["b2_common.cuh", "gemv.cuh", "attn.cuh", "kernels.cuh", "json.h"]
+HEADERS = ["b2_common.cuh", "gemv.cuh", "attn.cuh", "kernels.cuh", "token.cuh", "json.h"]
 
 NVCC_FLAGS = [
     "-O3", "-std=c++17", "-lineinfo",

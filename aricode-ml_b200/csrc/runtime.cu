@@ -690,11 +690,11 @@ void setup_token(b2_ctx* c) {
     c->tk_vec_offset = (int)vec_off;
     c->tk_vec_floats = (int)vec_floats;
     const size_t smem_max = 226 * 1024;             // dynamic; the static argmax slots need the rest
-    if (ring_off + 4 * (size_t)kTkSlotBytes > smem_max) { c->token_why = "too many rows per CTA"; return; }
+    if (ring_off + 3 * (size_t)kTkSlotBytes > smem_max) { c->token_why = "too many rows per CTA"; return; }
     int ns = (int)((smem_max - ring_off) / kTkSlotBytes);
-    ns = std::min(ns, kTkMaxSlots) & ~1;
+    ns = std::min(ns, kTkMaxSlots);
     if (const char* sl = std::getenv("B2_TK_SLOTS"))             // tuning: fewer slots, more L1
-        ns = std::max(4, std::min(ns, std::atoi(sl) & ~1));
+        ns = std::max(3, std::min(ns, std::atoi(sl)));
     c->tk_ns = ns;
     c->tk_ring_offset = (int)ring_off;
     c->tk_smem = ring_off + (size_t)ns * kTkSlotBytes;

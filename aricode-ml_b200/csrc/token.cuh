@@ -13,9 +13,11 @@
 //                  stage into a ring of NS 32 KB slots (mbarrier complete_tx), at
 //                  most kTkInflight copies outstanding; it also prefetches each
 //                  phase's small vectors (norm gains, scales, biases) into L2;
-//   warpgroups 0-3 consumers in two groups of 8 warps; slot s belongs to group
-//                  s & 1 in GEMV phases and to group (s / 2) & 1 in attention
+//   warpgroups 0-3 consumers in two groups of 8 warps; stage j belongs to group
+//                  j & 1 in GEMV phases and to group (j / 2) & 1 in attention
 //                  phases (an item's K stage and V stage go to the same group);
+//                  four full barriers per slot keep this exact for any slot count
+//                  (tk_full);
 //                  between phases: consumer barrier + grid barrier (atomic
 //                  arrivals, acquire spin, bounded to 1 s).
 //
@@ -52,14 +54,23 @@ enum TkVariant : int {
 };
 
 constexpr uint32_t kTkSlotBytes = 32 * 1024;
-constexpr int kTkMaxSlots = 6;
+constexpr int kTkMaxSlots = 7;                    // any count >= 3 (see tk_full)
 constexpr int kTkStamps = 8;                      // timeline slots per phase and CTA
 constexpr int kTkInflight = 3;                    // default bulk copies outstanding per CTA (< slots)
 constexpr int kTkMaxSplits = 256;                 // max_seq <= 16384
 constexpr int kTkGroupScratch = 64 + 4 + kTkMaxSplits;   // floats per consumer group
-constexpr int kTkScratchOffset = 256;             // after the mbarriers and flags
+// shared memory: full barriers [0, 224) (4 per slot), empty barriers [224, 288),
+// reduction slots [288, 320), flags [320, 352), vector-staging barrier 352
+constexpr int kTkFullOffset = 0;
+constexpr int kTkEmptyOffset = 224;
+constexpr int kTkRedOffset = 288;
+constexpr int kTkFlagOffset = 320;
+constexpr int kTkVbarOffset = 352;
+constexpr int kTkScratchOffset = 384;             // after the mbarriers and flags
 constexpr int kTkDescBytes = 864;                 // one phase descriptor copy (>= sizeof(TkPhase))
-constexpr int kTkDescOffset = 2880;               // >= kTkScratchOffset + 2 * kTkGroupScratch * 4
+constexpr int kTkDescOffset = 3072;               // >= kTkScratchOffset + 2 * kTkGroupScratch * 4
+static_assert(kTkScratchOffset + 2 * kTkGroupScratch * 4 <= kTkDescOffset, "scratch layout");
+static_assert(4 * kTkMaxSlots * 8 <= kTkEmptyOffset && kTkEmptyOffset + kTkMaxSlots * 8 <= kTkRedOffset, "barriers");
 constexpr int kTkPartOffset = kTkDescOffset + 3 * kTkDescBytes + 32;   // 2 consumer + 1 producer copies
 // 640 threads: warpgroups 0-3 consume, warpgroup 4 produces (one lane works).
 // Launched at 96 registers a thread (61,440 per CTA); the producer warpgroup
@@ -139,6 +150,29 @@ __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
 
 __device__ __forceinline__ void group_bar(int group) {
     asm volatile("bar.sync %0, 256;" ::"r"(2 + group) : "memory");
+}
+
+// Ring stage j: slot j % NS, round j / NS. Its "full" barrier is one of four per
+// slot (round % 4), waited with parity (round / 4) & 1. A stage belongs to one
+// consumer group (GEMV: j & 1; attention: (j / 2) & 1 for an item's two stages),
+// and for any slot count the stages j and j + 4 NS that share a barrier belong
+// to the same group: each barrier's phases are waited in order by one group, so
+// a parity wait never mistakes an earlier phase. The empty barrier (one per slot,
+// the owner's 8 warps arrive) is waited only by the producer, in order.
+__device__ __forceinline__ uint64_t* tk_full(uint64_t* full, int j, int NS) {
+    return full + (j % NS) * 4 + ((j / NS) & 3);
+}
+__device__ __forceinline__ uint32_t tk_full_parity(int j, int NS) { return (uint32_t)((j / NS) >> 2) & 1u; }
+
+// Producer: wait until stage j may be issued (its slot released by round - 1,
+// and at most `inflight` copies outstanding); returns its full barrier or null.
+__device__ __forceinline__ uint64_t* tk_issue_wait(uint64_t* full, uint64_t* empty, int NS, int j, int inflight) {
+    const int slot = j % NS, round = j / NS;
+    if (round > 0 && !mbar_wait_bounded(&empty[slot], (uint32_t)((round - 1) & 1))) return nullptr;
+    if (inflight > 0 && j >= inflight &&
+        !mbar_wait_bounded(tk_full(full, j - inflight, NS), tk_full_parity(j - inflight, NS)))
+        return nullptr;
+    return tk_full(full, j, NS);
 }
 
 // Grid barrier among the consumers of all CTAs: every CTA adds one arrival
@@ -226,9 +260,9 @@ __device__ __forceinline__ bool tk_attn_produce(const AttnParams& a, int n, int 
     const int items = tk_attn_items(a, n, nsplit);
     const int G = a.H / a.KVH, dh = a.dh;
     if (j & 1) {
-        const int slot = j % NS, round = j / NS;
-        if (round > 0 && !mbar_wait_bounded(&empty[slot], (uint32_t)((round - 1) & 1))) return false;
-        mbar_arrive(&full[slot]);
+        uint64_t* bar = tk_issue_wait(full, empty, NS, j, 0);
+        if (!bar) return false;
+        mbar_arrive(bar);
         ++j;
     }
     for (int it = cta; it < items; it += ncta) {
@@ -237,13 +271,10 @@ __device__ __forceinline__ bool tk_attn_produce(const AttnParams& a, int n, int 
         const uint32_t bytes = (uint32_t)len * dh * 4;
         const size_t off = ((size_t)kvh * a.max_seq + j0) * dh;
         for (int kv = 0; kv < 2; ++kv) {
-            const int slot = j % NS, round = j / NS;
-            if (round > 0 && !mbar_wait_bounded(&empty[slot], (uint32_t)((round - 1) & 1))) return false;
-            if (inflight > 0 && j >= inflight &&
-                !mbar_wait_bounded(&full[(j - inflight) % NS], (uint32_t)(((j - inflight) / NS) & 1)))
-                return false;
-            mbar_arrive_expect_tx(&full[slot], bytes);
-            bulk_g2s(ring + (size_t)slot * kTkSlotBytes, (kv ? a.V : a.K) + off, bytes, &full[slot]);
+            uint64_t* bar = tk_issue_wait(full, empty, NS, j, inflight);
+            if (!bar) return false;
+            mbar_arrive_expect_tx(bar, bytes);
+            bulk_g2s(ring + (size_t)(j % NS) * kTkSlotBytes, (kv ? a.V : a.K) + off, bytes, bar);
             ++j;
         }
     }
@@ -262,12 +293,11 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
     const int items = tk_attn_items(a, n, nsplit);
     const int G = a.H / a.KVH, dh = a.dh;
     const int gt = gwarp * 32 + lane;                   // thread index within the group
-    if (j & 1) {                                        // padding stage
-        const int slot = j % NS;
-        if ((slot & 1) == group) {
-            if (!group_wait(&full[slot], (uint32_t)((j / NS) & 1), group, gt, gflag)) return false;
+    if (j & 1) {                                        // padding stage (owner j & 1)
+        if ((j & 1) == group) {
+            if (!group_wait(tk_full(full, j, NS), tk_full_parity(j, NS), group, gt, gflag)) return false;
             __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[slot]);
+            if (lane == 0) mbar_arrive(&empty[j % NS]);
         }
         ++j;
     }
@@ -275,8 +305,8 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
     float* ml = scr + 64;             // m, l, (int) last, L
     float* wsm = scr + 68;            // [nsplit] combine weights
     for (int it = cta; it < items; it += ncta, j += 2) {
-        const int slotk = j % NS, slotv = slotk + 1;
-        if (((slotk >> 1) & 1) != group) continue;
+        const int slotk = j % NS, slotv = (j + 1) % NS;
+        if (((j >> 1) & 1) != group) continue;
         const int h = it / nsplit, s = it % nsplit, kvh = h / G;
         const int j0 = s * kAttnChunk, len = min(kAttnChunk, n - j0);
         const int jnew = pos - j0;                      // this step's row, if in the chunk
@@ -293,7 +323,7 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
             kn[i] = (has_new && d < dh) ? __ldcg(knew + d) : 0.0f;
         }
         const float vn = (has_new && gt < dh) ? __ldcg(vnew + gt) : 0.0f;
-        if (!group_wait(&full[slotk], (uint32_t)((j / NS) & 1), group, gt, gflag)) return false;
+        if (!group_wait(tk_full(full, j, NS), tk_full_parity(j, NS), group, gt, gflag)) return false;
         const float* Ks = reinterpret_cast<const float*>(ring + (size_t)slotk * kTkSlotBytes);
         // scores: warp gwarp takes keys gwarp + 8 i; lane L sums d = L, L + 32, ...
         float v[8];
@@ -344,7 +374,7 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
         }
         group_bar(group);
         // o_s[d] = sum_j e_j V[j][d], j ascending (one thread per d)
-        if (!group_wait(&full[slotv], (uint32_t)(((j + 1) / NS) & 1), group, gt, gflag)) return false;
+        if (!group_wait(tk_full(full, j + 1, NS), tk_full_parity(j + 1, NS), group, gt, gflag)) return false;
         const float* Vs = reinterpret_cast<const float*>(ring + (size_t)slotv * kTkSlotBytes);
         const int stride = dh + 2;
         float* pp = a.part + ((size_t)h * a.nsplit_max + s) * stride;
@@ -408,32 +438,74 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
     return true;
 }
 
-// Long rows (up to 3 blocks a thread, 2 rows a stage): this thread's slice of the
-// normalised x is read once from shared memory into registers, then the stages
-// run as in gemv_kernel (few rows per stage: x from registers keeps the shared
-// memory traffic at the weight bytes).
-template <typename WT, int RS, bool PAIRED>
-__device__ __forceinline__ bool tk_consume_xreg(const GemvParams& p, int r0, int r1, const unsigned char* ring,
-                                                int NS, uint64_t* full, uint64_t* empty, int& j, int group,
-                                                int gwarp, int lane, int slotid, const float* xs, float* part,
-                                                int rows) {
+// GEMV producer over the token ring: one bulk copy per matrix per stage (the
+// second matrix of a paired stage starts RS rows in).
+template <int NM>
+__device__ __forceinline__ bool tk_gemv_produce(const GemvParams& p, int r0, int r1, int RS, int rows,
+                                                uint32_t row_bytes, unsigned char* ring, int NS, uint64_t* full,
+                                                uint64_t* empty, int& j, int inflight) {
+    int cur = r0;
+    while (cur < r1) {
+        const StageRows sr = next_stage(p, cur, r1, rows);
+        uint64_t* bar = tk_issue_wait(full, empty, NS, j, inflight);
+        if (!bar) return false;
+        const uint32_t bytes = (uint32_t)sr.nr * row_bytes;
+        unsigned char* dst = ring + (size_t)(j % NS) * kTkSlotBytes;
+        mbar_arrive_expect_tx(bar, bytes * NM);
+        bulk_g2s(dst, reinterpret_cast<const unsigned char*>(p.W[sr.seg]) + (size_t)sr.local * row_bytes, bytes, bar);
+        if constexpr (NM == 2)
+            bulk_g2s(dst + (size_t)RS * row_bytes,
+                     reinterpret_cast<const unsigned char*>(p.W[1]) + (size_t)sr.local * row_bytes, bytes, bar);
+        ++j;
+        cur += sr.nr;
+    }
+    return true;
+}
+
+// GEMV consumers over the token ring: group j & 1 takes stage j. XREG: x slice in
+// registers (long rows, gemv_consume_stage); otherwise x from shared memory
+// (gemv_consume_stage_xt).
+template <typename WT, int RS, int NM, int KB, bool XREG>
+__device__ __forceinline__ bool tk_gemv_consume(const GemvParams& p, int r0, int r1, int rows,
+                                                const unsigned char* ring, int NS, uint64_t* full, uint64_t* empty,
+                                                int& j, int group, int gwarp, int lane, int slotid, const float* xs,
+                                                float* part) {
     constexpr int EPB = GemvElems<WT>::EPB;
-    const int nblk = (int)(((size_t)p.ld * sizeof(WT)) >> 4);
-    float2 xr[3][EPB / 2];
+    const uint32_t row_bytes = (uint32_t)p.ld * (uint32_t)sizeof(WT);
+    const int nblk = (int)(row_bytes >> 4);
+    float2 xr[XREG ? 3 : 1][EPB / 2];
+    if constexpr (XREG) {
 #pragma unroll
-    for (int k = 0; k < 3; ++k) {
-        const int b = slotid + 256 * k;
+        for (int k = 0; k < 3; ++k) {
+            const int b = slotid + 256 * k;
 #pragma unroll
-        for (int q = 0; q < EPB / 4; ++q) {
-            float4 x4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            if (b < nblk) x4 = lds128f(xs + b * EPB + 4 * q);
-            xr[k][2 * q] = make_float2(x4.x, x4.y);
-            xr[k][2 * q + 1] = make_float2(x4.z, x4.w);
+            for (int q = 0; q < EPB / 4; ++q) {
+                float4 x4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                if (b < nblk) x4 = lds128f(xs + b * EPB + 4 * q);
+                xr[k][2 * q] = make_float2(x4.x, x4.y);
+                xr[k][2 * q + 1] = make_float2(x4.z, x4.w);
+            }
         }
     }
-    return gemv_consume<WT, 3, RS, PAIRED, true>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp,
-                                                 lane,
-                                           slotid, xr, part, true, rows);
+    int cur = r0;
+    while (cur < r1) {
+        const StageRows sr = next_stage(p, cur, r1, rows);
+        if ((j & 1) == group) {
+            if (!mbar_wait_bounded(tk_full(full, j, NS), tk_full_parity(j, NS))) return false;
+            const unsigned char* st = ring + (size_t)(j % NS) * kTkSlotBytes;
+            if constexpr (XREG)
+                gemv_consume_stage<WT, 3, RS, NM == 2, true>(st, row_bytes, nblk, slotid, lane, gwarp, xr, part,
+                                                             cur - r0, sr.nr);
+            else
+                gemv_consume_stage_xt<WT, RS, NM, KB, true>(st, row_bytes, nblk, slotid, lane, gwarp, xs, part,
+                                                            cur - r0, sr.nr);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[j % NS]);
+        }
+        ++j;
+        cur += sr.nr;
+    }
+    return true;
 }
 
 // --------------------------------------------------------------------- GEMV phase
@@ -480,15 +552,15 @@ __device__ __forceinline__ bool tk_gemv(const GemvParams& p, int unit, int rs, i
     const int slotid = tid % 256;
     bool okc;
     if (paired) {
-        okc = rs == 4 ? gemv_consume_xt<WT, 4, 2, 1, true>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp,
-                                                   lane, slotid, vec, part, rows)
-                      : tk_consume_xreg<WT, 1, true>(p, r0, r1, ring, NS, full, empty, j, group, gwarp, lane, slotid,
-                                                      vec, part, rows);
+        okc = rs == 4 ? tk_gemv_consume<WT, 4, 2, 1, false>(p, r0, r1, rows, ring, NS, full, empty, j, group, gwarp,
+                                                            lane, slotid, vec, part)
+                      : tk_gemv_consume<WT, 1, 2, 3, true>(p, r0, r1, rows, ring, NS, full, empty, j, group, gwarp,
+                                                           lane, slotid, vec, part);
     } else {
-        okc = rs == 8 ? gemv_consume_xt<WT, 8, 1, 1, true>(p, r0, r1, ring, kTkSlotBytes, NS, full, empty, j, group, gwarp,
-                                                   lane, slotid, vec, part, rows)
-                      : tk_consume_xreg<WT, 2, false>(p, r0, r1, ring, NS, full, empty, j, group, gwarp, lane, slotid,
-                                                       vec, part, rows);
+        okc = rs == 8 ? tk_gemv_consume<WT, 8, 1, 1, false>(p, r0, r1, rows, ring, NS, full, empty, j, group, gwarp,
+                                                            lane, slotid, vec, part)
+                      : tk_gemv_consume<WT, 2, 1, 3, true>(p, r0, r1, rows, ring, NS, full, empty, j, group, gwarp,
+                                                           lane, slotid, vec, part);
     }
     ok = okc && ok;
     consumer_bar();
@@ -516,12 +588,12 @@ __device__ __forceinline__ bool tk_gemv_dispatch(const TkPhase& T, int pos, cons
 template <int VS>
 __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_constant__ TkParams P) {
     extern __shared__ __align__(128) unsigned char smem[];
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem);                 // [kTkMaxSlots]
-    uint64_t* empty = full + 8;                                          // [kTkMaxSlots]
-    float* red = reinterpret_cast<float*>(smem + 128);                   // 8 floats
-    volatile int* flag = reinterpret_cast<volatile int*>(smem + 192);    // [0], [4] grid sync, [2..3] groups
-    volatile int* abort = reinterpret_cast<volatile int*>(smem + 212);
-    uint64_t* vbar = reinterpret_cast<uint64_t*>(smem + 216);           // vector staging
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kTkFullOffset);   // [4 * NS]
+    uint64_t* empty = reinterpret_cast<uint64_t*>(smem + kTkEmptyOffset); // [NS]
+    float* red = reinterpret_cast<float*>(smem + kTkRedOffset);           // 8 floats
+    volatile int* flag = reinterpret_cast<volatile int*>(smem + kTkFlagOffset);   // [0], [4] grid sync, [2..3] groups
+    volatile int* abort = flag + 6;
+    uint64_t* vbar = reinterpret_cast<uint64_t*>(smem + kTkVbarOffset);  // vector staging
     float* vec = reinterpret_cast<float*>(smem + P.vec_offset);
     float* scratch = reinterpret_cast<float*>(smem + kTkScratchOffset);
     float* part = reinterpret_cast<float*>(smem + kTkPartOffset);
@@ -549,13 +621,13 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
         if (cta == 0 && tid == 0) { atomicCAS(err, 0, bad); st->active = 0; }
         return;
     }
-    if (NS < 4 || NS > kTkMaxSlots || (NS & 1) || P.inflight < 0 || P.inflight >= NS) {
+    if (NS < 3 || NS > kTkMaxSlots || P.inflight < 0 || P.inflight >= NS) {
         if (cta == 0 && tid == 0) set_err(err, B2_DEV_ERR_TIMEOUT);
         return;
     }
     if (tid == 0) {
         for (int s = 0; s < NS; ++s) {
-            mbar_init(&full[s], 1);
+            for (int q = 0; q < 4; ++q) mbar_init(&full[4 * s + q], 1);
             mbar_init(&empty[s], kGemvGroupWarps);
         }
         mbar_init(vbar, 1);
@@ -582,17 +654,17 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
                     const bool i8 = T.variant < TV_F32_K1_R8;
                     const uint32_t row_bytes = (uint32_t)p.ld * (i8 ? 1u : 4u);
                     tk_prefetch_vectors(p, r0, r1, pos, i8);
-                    ok = p.paired ? gemv_produce<2>(p, r0, r1, T.rs, row_bytes, ring, kTkSlotBytes, NS, full, empty, j,
-                                                    P.inflight, T.rows)
-                                  : gemv_produce<1>(p, r0, r1, T.rs, row_bytes, ring, kTkSlotBytes, NS, full, empty, j,
-                                                    P.inflight, T.rows);
+                    ok = p.paired ? tk_gemv_produce<2>(p, r0, r1, T.rs, T.rows, row_bytes, ring, NS, full, empty, j,
+                                                       P.inflight)
+                                  : tk_gemv_produce<1>(p, r0, r1, T.rs, T.rows, row_bytes, ring, NS, full, empty, j,
+                                                       P.inflight);
                 } else if (T.kind == TK_ATTN) {
                     ok = tk_attn_produce(T.a, pos + 1, cta, ncta, ring, NS, full, empty, j, P.inflight);
                 }
             }
             if (!ok) set_err(err, B2_DEV_ERR_TIMEOUT);
             for (int i = max(0, j - NS); i < j; ++i)        // no copy in flight at exit
-                if (!mbar_wait_bounded(&full[i % NS], (uint32_t)((i / NS) & 1))) {
+                if (!mbar_wait_bounded(tk_full(full, i, NS), tk_full_parity(i, NS))) {
                     set_err(err, B2_DEV_ERR_TIMEOUT);
                     break;
                 }

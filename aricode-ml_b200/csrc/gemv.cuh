@@ -20,11 +20,14 @@
 // Compute: two groups of 8 consumer warps take alternate stages. Within a group
 // the 256 threads split every row: thread s owns the 16-byte blocks s, s+256, ...
 // (its slice of x lives in registers, normalised once), so a stage is read once
-// from shared memory, conflict-free. Per row: four accumulators a[t & 3] updated
-// by fused multiply-adds (issued as packed f32x2 pairs: two independent IEEE
-// round-to-nearest operations, the same results as scalar ones), slot partial
-// (a0+a1)+(a2+a3), warp butterfly, then the 8 warp sums
-// ((W0+W1)+(W2+W3))+((W4+W5)+(W6+W7)) — oracle/refdec.c b2o_dot_i8 / b2o_dot_f32.
+// from shared memory, conflict-free.
+//   int8 rows: an exact integer dot on a 32-bit fixed-point copy of x, four dp4a
+//   per 4 codes (one per byte plane of x), plane sums reduced in any order and
+//   rounded once (oracle/refdec.c b2o_xfix / b2o_dot_i8x; see gemv_stage_i8);
+//   f32 rows: four accumulators a[t] updated by fused multiply-adds (packed f32x2
+//   pairs: two independent IEEE round-to-nearest operations), slot partial
+//   (a0+a1)+(a2+a3), warp butterfly, then the 8 warp sums
+//   ((W0+W1)+(W2+W3))+((W4+W5)+(W6+W7)) — oracle/refdec.c b2o_dot_f32.
 #pragma once
 #include "b2_common.cuh"
 
@@ -89,29 +92,6 @@ __device__ __forceinline__ bool amax_better(float va, int ia, float vb, int ib) 
     if (na != nb) return nb;                   // a wins iff b is NaN
     if (!na && va != vb) return va > vb;
     return ia < ib;
-}
-
-// 4 int8 of u (xor 0x80 applied) against x: (a0,a1) += (w0,w1)*(x0,x1),
-// (a2,a3) += (w2,w3)*(x2,x3); w = (2^23 + 128 + b) - (2^23 + 128), exact.
-__device__ __forceinline__ void fma_word2(float2& a01, float2& a23, uint32_t u, float2 x01, float2 x23) {
-    const float2 c = make_float2(-8388736.0f, -8388736.0f);
-    float2 w01 = make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7440u)),
-                             __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7441u)));
-    float2 w23 = make_float2(__uint_as_float(__byte_perm(u, 0x4B000000u, 0x7442u)),
-                             __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7443u)));
-    w01 = __fadd2_rn(w01, c);
-    w23 = __fadd2_rn(w23, c);
-    a01 = __ffma2_rn(w01, x01, a01);
-    a23 = __ffma2_rn(w23, x23, a23);
-}
-
-// int8 codes as the magic-number conversion wants them: b ^ 0x80 per byte. PRE:
-// the weights are stored that way already (the model arenas of the token kernel,
-// biased once at load), so no per-word XOR is needed.
-template <bool PRE>
-__device__ __forceinline__ uint32_t bias_codes(uint32_t w) {
-    if constexpr (PRE) return w;
-    else return w ^ 0x80808080u;
 }
 
 __device__ __forceinline__ void consumer_bar() {
@@ -200,6 +180,173 @@ __device__ __forceinline__ void exchange_butterfly(float (&v)[N], int lane) {
 
 template <int N> struct Log2 { static constexpr int v = 1 + Log2<N / 2>::v; };
 template <> struct Log2<1> { static constexpr int v = 0; };
+
+// The same exchange over integers (exact in any order: only the lane layout matters)
+template <int N>
+__device__ __forceinline__ void exchange_butterfly_i(int (&v)[N], int lane) {
+    int cnt = N;
+#pragma unroll
+    for (int s = 16; s >= 1; s >>= 1) {
+        if (cnt > 1) {
+            const bool upper = (lane & s) != 0;
+            const int h = cnt / 2;
+#pragma unroll
+            for (int i = 0; i < (N > 1 ? N / 2 : 1); ++i) {
+                if (i < h) {
+                    const int send = upper ? v[i] : v[h + i];
+                    const int keep = upper ? v[h + i] : v[i];
+                    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+                }
+            }
+            cnt = h;
+        } else {
+            v[0] += __shfl_xor_sync(0xffffffffu, v[0], s);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// int8 rows: exact dot product on a fixed-point copy of x (oracle/refdec.c
+// b2o_xfix / b2o_dot_i8x). With max|x| < 2^E, S = 31 - E and X_i = trunc(x_i 2^S)
+// (|X_i| < 2^31), a row's dot is the exact integer D = sum_i w_i X_i rounded once,
+// f32((double)D 2^-S). Integer sums are exact in any order, so the thread layout
+// and the reduction tree do not change the bits. X is split into byte planes
+// X = P0 + 2^8 P1 + 2^16 P2 + 2^24 P3 (P0..P2 unsigned, P3 signed); one dp4a
+// takes four codes of a row against the same four elements of one plane. Each
+// plane sum stays below 128 * 255 * 16384 < 2^31 for rows of up to 16384 codes.
+// ---------------------------------------------------------------------------
+constexpr int kXfixBad = -100000;                  // S when x holds a NaN or an infinity
+constexpr int kXfixMaxN = 16384;
+
+// S from the largest |x| bit pattern (non-negative floats order as their bits)
+__device__ __forceinline__ int xfix_shift(uint32_t amax_bits) {
+    if (amax_bits >= 0x7f800000u) return kXfixBad;
+    if (amax_bits == 0u) return 0;
+    const int e = (int)(amax_bits >> 23);
+    const int E = e > 0 ? e - 126 : (32 - __clz((int)amax_bits)) - 149;   // frexp exponent
+    return 31 - E;
+}
+
+__device__ __forceinline__ double pow2d(int k) { return __longlong_as_double((long long)(1023 + k) << 52); }
+
+__device__ __forceinline__ uint32_t abs_bits(float v) { return __float_as_uint(v) & 0x7fffffffu; }
+
+// 16 consecutive elements of x -> their planes: w[p * 4 + q] holds byte p of
+// elements 4q .. 4q + 3 (element 4q in the low byte)
+__device__ __forceinline__ void xfix_block(const float (&x)[16], int S, uint32_t (&w)[16]) {
+    if (S == kXfixBad) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) w[i] = 0u;
+        return;
+    }
+    const double p2s = pow2d(S);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        uint32_t X[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) X[k] = (uint32_t)__double2int_rz(__dmul_rn((double)x[4 * q + k], p2s));
+        const uint32_t lo01 = __byte_perm(X[0], X[1], 0x5140u), hi01 = __byte_perm(X[0], X[1], 0x7362u);
+        const uint32_t lo23 = __byte_perm(X[2], X[3], 0x5140u), hi23 = __byte_perm(X[2], X[3], 0x7362u);
+        w[0 * 4 + q] = __byte_perm(lo01, lo23, 0x5410u);
+        w[1 * 4 + q] = __byte_perm(lo01, lo23, 0x7632u);
+        w[2 * 4 + q] = __byte_perm(hi01, hi23, 0x5410u);
+        w[3 * 4 + q] = __byte_perm(hi01, hi23, 0x7632u);
+    }
+}
+
+// c + sum of 4 signed codes (a) times 4 unsigned / signed plane bytes (b)
+__device__ __forceinline__ int dp4a_su(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// one row's value from its four plane sums
+__device__ __forceinline__ float xfix_row(const int* pl, int S) {
+    if (S == kXfixBad) return __uint_as_float(0x7fc00000u);
+    const long long D = (long long)pl[0] + (long long)pl[1] * 256ll + (long long)pl[2] * 65536ll +
+                        (long long)pl[3] * 16777216ll;
+    return __double2float_rn(__dmul_rn(__ll2double_rn(D), pow2d(-S)));
+}
+
+// Block-wide S: every consumer thread passes the largest |x| bits it has seen;
+// amx (shared, zero on entry) collects them. Ends with the consumer barrier.
+__device__ __forceinline__ int xfix_shift_cta(uint32_t local, unsigned* amx) {
+    local = __reduce_max_sync(0xffffffffu, local);
+    if ((threadIdx.x & 31) == 0) atomicMax(amx, local);
+    asm volatile("bar.sync 1, %0;" ::"r"(kGemvConsumerThreads) : "memory");
+    return xfix_shift(*(volatile unsigned*)amx);
+}
+
+// One int8 stage: nr (<= RS) rows of each of the NM matrices at `stage` (the
+// second matrix starts RS rows in), x as planes in registers (KB 16-byte blocks a
+// thread: s, s + 256, ...). Each row's four plane sums are added into
+// part[((row * NM + m) * 4 + plane] (shared, zeroed before the first stage) for
+// rows rl0 .. rl0 + nr - 1 of the CTA. Rows are reduced eight at a time.
+template <int KB, int RS, int NM>
+__device__ __forceinline__ void gemv_stage_i8(const unsigned char* stage, uint32_t row_bytes, int nblk, int slotid,
+                                              int lane, const uint32_t (&xp)[KB][16], int* part, int rl0, int nr) {
+    constexpr int NR = RS * NM;
+    constexpr int NH = NR < 8 ? NR : 8;
+    constexpr int NV = NH * 4;
+    constexpr int LG = Log2<NV>::v;
+#pragma unroll
+    for (int h0 = 0; h0 < NR; h0 += NH) {
+        int acc[NH][4];
+#pragma unroll
+        for (int r = 0; r < NH; ++r)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) acc[r][q] = 0;
+#pragma unroll
+        for (int k = 0; k < KB; ++k) {
+            const int b = slotid + 256 * k;
+            if (b < nblk) {
+#pragma unroll
+                for (int r = 0; r < NH; ++r) {
+                    // rows past nr read stale (in-bounds) stage bytes; never stored
+                    const uint4 w = lds128(stage + (size_t)(h0 + r) * row_bytes + 16 * b);
+                    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        acc[r][0] = dp4a_su(ww[q], xp[k][0 * 4 + q], acc[r][0]);
+                        acc[r][1] = dp4a_su(ww[q], xp[k][1 * 4 + q], acc[r][1]);
+                        acc[r][2] = dp4a_su(ww[q], xp[k][2 * 4 + q], acc[r][2]);
+                        acc[r][3] = dp4a_ss(ww[q], xp[k][3 * 4 + q], acc[r][3]);
+                    }
+                }
+            }
+        }
+        int v[NV];
+#pragma unroll
+        for (int r = 0; r < NH; ++r)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) v[r * 4 + q] = acc[r][q];
+        exchange_butterfly_i<NV>(v, lane);
+        if ((lane & ((32 >> LG) - 1)) == 0) {
+            const int vi = lane >> (5 - LG);
+            const int rr = h0 + vi / 4, pl = vi % 4;       // stage row (m * RS + r), plane
+            const int m = rr / RS, r = rr % RS;
+            if (r < nr) atomicAdd(part + ((rl0 + r) * NM + m) * 4 + pl, v[0]);
+        }
+    }
+}
+
+// A thread's planes from the f32 slice gemv_load_x left in registers
+template <int KMAX>
+__device__ __forceinline__ void xfix_from_slice(const float2 (&xr)[KMAX][8], int S, uint32_t (&xp)[KMAX][16]) {
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k) {
+        float t[16];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) { t[2 * i] = xr[k][i].x; t[2 * i + 1] = xr[k][i].y; }
+        xfix_block(t, S, xp[k]);
+    }
+}
 
 
 // ============================================================================
@@ -334,10 +481,16 @@ __device__ __forceinline__ void gemv_load_x(const GemvParams& p, float2 (&xr)[KM
 // of x per row group from shared memory instead of holding the slice in
 // registers. Same operations, in the same order, as gemv_load_x + the stages.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void gemv_norm_smem(const GemvParams& p, float* xs, const float* gs, const float* bs,
-                                               float* red, int tid) {
+// Returns the largest |x| bit pattern among the values this thread normalised
+// (or, without a norm, read): the int8 rows' fixed-point shift needs the CTA max.
+__device__ __forceinline__ uint32_t gemv_norm_smem(const GemvParams& p, float* xs, const float* gs, const float* bs,
+                                                   float* red, int tid) {
     const int n = p.n;
-    if (p.norm == NORM_NONE) return;
+    uint32_t am = 0u;
+    if (p.norm == NORM_NONE) {
+        for (int i = tid; i < n; i += kGemvConsumerThreads) am = max(am, abs_bits(xs[i]));
+        return am;
+    }
     float scale_a = 1.0f, shift_m = 0.0f;
     if (p.norm == NORM_RMS) {
         float a = 0.0f;
@@ -360,20 +513,23 @@ __device__ __forceinline__ void gemv_norm_smem(const GemvParams& p, float* xs, c
     // every raw value has been read (the reduction's barriers); normalise in place
     for (int i = tid; i < n; i += kGemvConsumerThreads) {
         const float xv = xs[i];
-        xs[i] = p.norm == NORM_RMS
-                    ? fmul(fmul(xv, scale_a), gs[i])
-                    : (float)dadd(dmul((double)fmul(fsub(xv, shift_m), scale_a), (double)gs[i]), (double)bs[i]);
+        const float v = p.norm == NORM_RMS
+                            ? fmul(fmul(xv, scale_a), gs[i])
+                            : (float)dadd(dmul((double)fmul(fsub(xv, shift_m), scale_a), (double)gs[i]), (double)bs[i]);
+        xs[i] = v;
+        am = max(am, abs_bits(v));
     }
+    return am;
 }
 
 // Compile-time shaped stage with x read from shared memory: RS rows per matrix,
 // NM matrices, all NR = RS * NM rows reduced by one exchange butterfly; KB = most
 // 16-byte blocks a thread owns in a row (the block loop is unrolled).
-template <typename WT, int RS, int NM, int KB, bool PRE = false>
+template <typename WT, int RS, int NM, int KB>
 __device__ __forceinline__ void gemv_consume_stage_xt(const unsigned char* stage, uint32_t row_bytes, int nblk,
                                                       int slotid, int lane, int gwarp, const float* xs,
                                                       float* part, int rl0, int nr) {
-    constexpr int ESZ = (int)sizeof(WT);
+    static_assert(sizeof(WT) == 4, "f32 rows (int8 rows: gemv_stage_i8)");
     constexpr int EPB = GemvElems<WT>::EPB;
     constexpr int NR = RS * NM;
     constexpr int LG = Log2<NR>::v;
@@ -395,17 +551,9 @@ __device__ __forceinline__ void gemv_consume_stage_xt(const unsigned char* stage
         for (int r = 0; r < NR; ++r) {
             // rows past nr read stale (in-bounds) stage bytes; never stored
             const unsigned char* row = stage + (size_t)r * row_bytes + 16 * b;
-            if constexpr (ESZ == 1) {
-                const uint4 w = lds128(row);
-                fma_word2(a01[r], a23[r], bias_codes<PRE>(w.x), xb[0], xb[1]);
-                fma_word2(a01[r], a23[r], bias_codes<PRE>(w.y), xb[2], xb[3]);
-                fma_word2(a01[r], a23[r], bias_codes<PRE>(w.z), xb[4], xb[5]);
-                fma_word2(a01[r], a23[r], bias_codes<PRE>(w.w), xb[6], xb[7]);
-            } else {
-                const float4 w = lds128f(row);
-                a01[r] = __ffma2_rn(make_float2(w.x, w.y), xb[0], a01[r]);
-                a23[r] = __ffma2_rn(make_float2(w.z, w.w), xb[1], a23[r]);
-            }
+            const float4 w = lds128f(row);
+            a01[r] = __ffma2_rn(make_float2(w.x, w.y), xb[0], a01[r]);
+            a23[r] = __ffma2_rn(make_float2(w.z, w.w), xb[1], a23[r]);
         }
     }
     float v[NR];
@@ -419,40 +567,16 @@ __device__ __forceinline__ void gemv_consume_stage_xt(const unsigned char* stage
     }
 }
 
-template <typename WT, int RS, int NM, int KB, bool PRE = false>
-__device__ __forceinline__ bool gemv_consume_xt(const GemvParams& p, int r0, int r1, const unsigned char* ring,
-                                                uint32_t slot_stride, int NS, uint64_t* full, uint64_t* empty,
-                                                int& j, int group, int gwarp, int lane, int slotid, const float* xs,
-                                                float* part, int rows = RS) {
-    const uint32_t row_bytes = (uint32_t)p.ld * (uint32_t)sizeof(WT);
-    const int nblk = (int)(row_bytes >> 4);
-    int cur = r0;
-    while (cur < r1) {
-        const StageRows sr = next_stage(p, cur, r1, rows);
-        const int slot = j % NS;
-        if ((slot & 1) == group) {
-            if (!mbar_wait_bounded(&full[slot], (uint32_t)((j / NS) & 1))) return false;
-            gemv_consume_stage_xt<WT, RS, NM, KB, PRE>(ring + (size_t)slot * slot_stride, row_bytes, nblk, slotid, lane,
-                                              gwarp, xs, part, cur - r0, sr.nr);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[slot]);
-        }
-        ++j;
-        cur += sr.nr;
-    }
-    return true;
-}
-
 // One stage: nr (<= RS) rows of each of the NM matrices at `stage` (row stride
 // row_bytes; the second matrix starts RS rows in). Writes this warp's sums to
 // part[(row * NM + m) * 8 + gwarp] for rows rl0 .. rl0 + nr - 1 of the CTA. Rows
 // are reduced four at a time (each row's butterfly is the same either way).
-template <typename WT, int KMAX, int RS, bool PAIRED, bool PRE = false>
+template <typename WT, int KMAX, int RS, bool PAIRED>
 __device__ __forceinline__ void gemv_consume_stage(const unsigned char* stage, uint32_t row_bytes, int nblk,
                                                    int slotid, int lane, int gwarp,
                                                    const float2 (&xr)[KMAX][GemvElems<WT>::EPB / 2],
                                                    float* part, int rl0, int nr) {
-    constexpr int ESZ = (int)sizeof(WT);
+    static_assert(sizeof(WT) == 4, "f32 rows (int8 rows: gemv_stage_i8)");
     constexpr int NM = PAIRED ? 2 : 1;
     constexpr int NR = RS * NM;
     constexpr int NH = NR < 4 ? NR : 4;
@@ -471,17 +595,9 @@ __device__ __forceinline__ void gemv_consume_stage(const unsigned char* stage, u
                 for (int r = 0; r < NH; ++r) {
                     // rows past nr read stale (in-bounds) stage bytes; never stored
                     const unsigned char* row = stage + (size_t)(h0 + r) * row_bytes + 16 * b;
-                    if constexpr (ESZ == 1) {
-                        const uint4 w = lds128(row);
-                        fma_word2(a01[r], a23[r], bias_codes<PRE>(w.x), xr[k][0], xr[k][1]);
-                        fma_word2(a01[r], a23[r], bias_codes<PRE>(w.y), xr[k][2], xr[k][3]);
-                        fma_word2(a01[r], a23[r], bias_codes<PRE>(w.z), xr[k][4], xr[k][5]);
-                        fma_word2(a01[r], a23[r], bias_codes<PRE>(w.w), xr[k][6], xr[k][7]);
-                    } else {
-                        const float4 w = lds128f(row);
-                        a01[r] = __ffma2_rn(make_float2(w.x, w.y), xr[k][0], a01[r]);
-                        a23[r] = __ffma2_rn(make_float2(w.z, w.w), xr[k][1], a23[r]);
-                    }
+                    const float4 w = lds128f(row);
+                    a01[r] = __ffma2_rn(make_float2(w.x, w.y), xr[k][0], a01[r]);
+                    a23[r] = __ffma2_rn(make_float2(w.z, w.w), xr[k][1], a23[r]);
                 }
             }
         }
@@ -534,7 +650,7 @@ __device__ __forceinline__ bool gemv_produce(const GemvParams& p, int r0, int r1
 // Consumers: walk the same stages; group g takes stage j when (j % NS) % 2 == g
 // (NS even, so every slot belongs to one group and its phases advance in order).
 // compute = false only releases the slots. Returns false on a timed-out wait.
-template <typename WT, int KMAX, int RS, bool PAIRED, bool PRE = false>
+template <typename WT, int KMAX, int RS, bool PAIRED>
 __device__ __forceinline__ bool gemv_consume(const GemvParams& p, int r0, int r1, const unsigned char* ring,
                                              uint32_t slot_stride, int NS, uint64_t* full, uint64_t* empty,
                                              int& j, int group, int gwarp, int lane, int slotid,
@@ -549,8 +665,34 @@ __device__ __forceinline__ bool gemv_consume(const GemvParams& p, int r0, int r1
         if ((slot & 1) == group) {
             if (!mbar_wait_bounded(&full[slot], (uint32_t)((j / NS) & 1))) return false;
             if (compute)
-                gemv_consume_stage<WT, KMAX, RS, PAIRED, PRE>(ring + (size_t)slot * slot_stride, row_bytes, nblk, slotid,
+                gemv_consume_stage<WT, KMAX, RS, PAIRED>(ring + (size_t)slot * slot_stride, row_bytes, nblk, slotid,
                                                          lane, gwarp, xr, part, cur - r0, sr.nr);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+        ++j;
+        cur += sr.nr;
+    }
+    return true;
+}
+
+// The same walk for int8 rows (x as planes, plane sums into part[] as int32)
+template <int KMAX, int RS, int NM>
+__device__ __forceinline__ bool gemv_consume_i8(const GemvParams& p, int r0, int r1, const unsigned char* ring,
+                                                uint32_t slot_stride, int NS, uint64_t* full, uint64_t* empty,
+                                                int& j, int group, int lane, int slotid,
+                                                const uint32_t (&xp)[KMAX][16], int* part, bool compute) {
+    const uint32_t row_bytes = (uint32_t)p.ld;
+    const int nblk = (int)(row_bytes >> 4);
+    int cur = r0;
+    while (cur < r1) {
+        const StageRows sr = next_stage(p, cur, r1, RS);
+        const int slot = j % NS;
+        if ((slot & 1) == group) {
+            if (!mbar_wait_bounded(&full[slot], (uint32_t)((j / NS) & 1))) return false;
+            if (compute)
+                gemv_stage_i8<KMAX, RS, NM>(ring + (size_t)slot * slot_stride, row_bytes, nblk, slotid, lane, xp, part,
+                                            cur - r0, sr.nr);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
         }
@@ -600,7 +742,13 @@ __device__ __forceinline__ void gemv_epi_store(const EpiRow& e, int nrows, int t
 // given, holds the preloaded per-row inputs of the first 512 rows.
 template <int ESZ, bool PAIRED>
 __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, int r0, int r1, const float* part, int pos,
-                                              int tid, int cta, int ncta, const float* epi = nullptr) {
+                                              int tid, int cta, int ncta, const float* epi = nullptr, int S = 0) {
+    // int8: part holds int32 plane sums [row][NM][4]; f32: warp sums [row][NM][8]
+    const int* parti = reinterpret_cast<const int*>(part);
+    auto dotv = [&](int rl, int m) {
+        if constexpr (ESZ == 1) return xfix_row(parti + (rl * (PAIRED ? 2 : 1) + m) * 4, S);
+        else return tree8(part + (rl * (PAIRED ? 2 : 1) + m) * 8);
+    };
     const int warp = tid >> 5, lane = tid & 31;
     auto pre = [&](int rl) { return epi && rl < kGemvConsumerThreads; };
     float best_v = 0.0f;
@@ -613,8 +761,8 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, int r0, int r
         if constexpr (PAIRED) {                              // EPI_SWIGLU
             const float sg = pre(rl) ? epi[rl * 4] : p.S[0][lrow];
             const float su = pre(rl) ? epi[rl * 4 + 1] : p.S[1][lrow];
-            const float g = fmul(tree8(part + (rl * 2 + 0) * 8), sg);
-            const float u = fmul(tree8(part + (rl * 2 + 1) * 8), su);
+            const float g = fmul(dotv(rl, 0), sg);
+            const float u = fmul(dotv(rl, 1), su);
             p.y[lrow] = fmul(silu_f(g), u);
             continue;
         }
@@ -622,7 +770,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, int r0, int r
         seg_of(p, lrow, seg, row);
         float val[2] = {0.0f, 0.0f};
         for (int e = 0; e < step; ++e) {
-            float v = tree8(part + (rl + e) * 8);
+            float v = dotv(rl + e, 0);
             if constexpr (ESZ == 1) v = fmul(v, pre(rl + e) ? epi[(rl + e) * 4] : p.S[seg][row + e]);
             if (p.bias[seg]) v = fadd(v, pre(rl + e) ? epi[(rl + e) * 4 + 1] : p.bias[seg][row + e]);
             else if constexpr (ESZ == 4) v = fadd(v, 0.0f);
@@ -737,7 +885,8 @@ gemv_kernel(const __grid_constant__ GemvParams p) {
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + kGemvMaxStages;
     float* red = reinterpret_cast<float*>(empty + kGemvMaxStages);      // 8 floats
-    float* part = reinterpret_cast<float*>(smem + 1024);                 // [rows_cta][NM][8]
+    float* part = reinterpret_cast<float*>(smem + 1024);                 // [rows_cta][NM][8] (f32) / [4] (int8)
+    unsigned* amx = reinterpret_cast<unsigned*>(red + 8);                // int8: largest |x| bits
     const uint32_t row_bytes = (uint32_t)p.ld * ESZ;
     const uint32_t stage_bytes = (uint32_t)RS * row_bytes * NM;
     unsigned char* ring = smem + p.ring_offset;
@@ -758,7 +907,10 @@ gemv_kernel(const __grid_constant__ GemvParams p) {
             mbar_init(&empty[s], kGemvGroupWarps);
         }
         fence_mbar_init();
+        *amx = 0u;
     }
+    if constexpr (ESZ == 1)                                              // plane sums start at 0
+        for (int i = tid; i < (r1 - r0) * NM * 4; i += kGemvThreads) reinterpret_cast<int*>(part)[i] = 0;
     __syncthreads();
     pdl_launch_dependents();
 
@@ -788,12 +940,27 @@ gemv_kernel(const __grid_constant__ GemvParams p) {
     float2 xr[KMAX][GemvElems<WT>::EPB / 2];
     gemv_load_x<WT, KMAX>(p, xr, red, tid);
     int j = 0;
-    if (!gemv_consume<WT, KMAX, RS, PAIRED>(p, r0, r1, ring, stage_bytes, NS, full, empty, j, group, gwarp, lane,
-                                            tid % 256, xr, part, active))
-        set_err(p.err, B2_DEV_ERR_TIMEOUT);
+    int S = 0;
+    bool ok;
+    if constexpr (ESZ == 1) {
+        uint32_t am = 0u;                       // the 256 slices cover x (threads s and s + 256 share one)
+#pragma unroll
+        for (int k = 0; k < KMAX; ++k)
+#pragma unroll
+            for (int t = 0; t < 8; ++t) am = max(am, max(abs_bits(xr[k][t].x), abs_bits(xr[k][t].y)));
+        S = xfix_shift_cta(am, amx);
+        uint32_t xp[KMAX][16];
+        xfix_from_slice<KMAX>(xr, S, xp);
+        ok = gemv_consume_i8<KMAX, RS, NM>(p, r0, r1, ring, stage_bytes, NS, full, empty, j, group, lane, tid % 256,
+                                           xp, reinterpret_cast<int*>(part), active);
+    } else {
+        ok = gemv_consume<WT, KMAX, RS, PAIRED>(p, r0, r1, ring, stage_bytes, NS, full, empty, j, group, gwarp, lane,
+                                                tid % 256, xr, part, active);
+    }
+    if (!ok) set_err(p.err, B2_DEV_ERR_TIMEOUT);
     consumer_bar();
     if (!active) return;
-    gemv_epilogue<ESZ, PAIRED>(p, r0, r1, part, pos, tid, blockIdx.x, gridDim.x);
+    gemv_epilogue<ESZ, PAIRED>(p, r0, r1, part, pos, tid, blockIdx.x, gridDim.x, nullptr, S);
 }
 
 }  // namespace b2

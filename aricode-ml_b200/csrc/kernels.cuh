@@ -70,15 +70,6 @@ static __global__ void embed_kernel(const __grid_constant__ EmbedParams p) {
     }
 }
 
-// int8 codes -> biased codes (b ^ 0x80) in place, 16 bytes per thread per step
-static __global__ void bias_codes_kernel(uint4* p, size_t n16) {
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n16; i += (size_t)gridDim.x * blockDim.x) {
-        uint4 v = p[i];
-        v.x ^= 0x80808080u; v.y ^= 0x80808080u; v.z ^= 0x80808080u; v.w ^= 0x80808080u;
-        p[i] = v;
-    }
-}
-
 // (re)start a decode sequence on the device without a host round trip
 static __global__ void set_state_kernel(StepState* st, int step, int prompt_len, int max_new,
                                         int next_tok, int eos) {
@@ -375,9 +366,11 @@ inline cudaError_t launch_gemv(const GemvParams& p, bool w_i8, cudaStream_t s, b
     if (w_i8) {
         if (sh.paired) {
             if (sh.K <= 1) return launch_gemv_r<int8_t, 1, true>(p, sh, s, pdl);
+            if (sh.K <= 3) return launch_gemv_r<int8_t, 3, true>(p, sh, s, pdl);
             return launch_gemv_r<int8_t, kGemvMaxK, true>(p, sh, s, pdl);
         }
         if (sh.K <= 1) return launch_gemv_r<int8_t, 1, false>(p, sh, s, pdl);
+        if (sh.K <= 3) return launch_gemv_r<int8_t, 3, false>(p, sh, s, pdl);
         return launch_gemv_r<int8_t, kGemvMaxK, false>(p, sh, s, pdl);
     }
     if (sh.paired) return cudaErrorInvalidValue;

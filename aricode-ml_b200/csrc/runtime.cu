@@ -164,6 +164,7 @@ struct b2_ctx {
     unsigned* tk_bar = nullptr;    // grid-barrier counters, zero between launches
     int n_attn_cnt = 0;
     int tk_ns = 0, tk_ring_offset = 0, tk_inflight = kTkInflight, tk_vec_offset = 0, tk_vec_floats = 0;
+    int tk_l2_ahead = 0;
     size_t tk_smem = 0;
     std::string token_why;         // why the per-layer kernels are used instead
     unsigned long long* d_trace = nullptr;   // token-kernel timeline (B2_TK_TRACE)
@@ -700,6 +701,8 @@ void setup_token(b2_ctx* c) {
     c->tk_smem = ring_off + (size_t)ns * kTkSlotBytes;
     const char* inf = std::getenv("B2_TK_INFLIGHT");          // tuning: 0 = no cap
     c->tk_inflight = inf ? std::max(0, std::min(ns - 1, std::atoi(inf))) : std::min(kTkInflight, ns - 1);
+    const char* ahead = std::getenv("B2_TK_L2AHEAD");         // tuning: stages prefetched into L2
+    c->tk_l2_ahead = ahead ? std::max(0, std::min(64, std::atoi(ahead))) : 0;
     c->token_vs = f32 ? 1 : 0;
     if (!(f32 ? tk_prepare_kernel<1>(c) : tk_prepare_kernel<0>(c))) {
         c->token_why = "token kernel does not fit an SM";
@@ -738,6 +741,7 @@ void launch_token(b2_ctx* c, bool with_head, cudaStream_t s) {
     P.vocab = c->vocab;
     P.trace = c->d_trace;
     P.inflight = c->tk_inflight;
+    P.l2_ahead = c->tk_l2_ahead;
     P.vec_offset = c->tk_vec_offset;
     P.vec_floats = c->tk_vec_floats;
     cudaLaunchConfig_t cfg{};
@@ -756,37 +760,6 @@ void launch_token(b2_ctx* c, bool with_head, cudaStream_t s) {
 
 void capture_graphs_once(b2_ctx* c);
 
-// The token kernel reads the model's int8 GEMV matrices as biased codes (b ^ 0x80):
-// bias each distinct matrix once, in place (rows x ld bytes, ld % 16 == 0). Not
-// done (the token kernel is then disabled) when a GEMV matrix shares storage with
-// the embedding, which is read as plain codes.
-void bias_gemv_codes(b2_ctx* c) {
-    std::vector<const DevMat*> mats;
-    for (const Block& B : c->blocks) {
-        if (B.attn) {
-            for (const DevMat* m : {&B.q, &B.k, &B.v, &B.o}) if (m->i8) mats.push_back(m);
-        } else {
-            mats.push_back(&B.w1);
-            if (B.swiglu) mats.push_back(&B.w3);
-            mats.push_back(&B.w2);
-        }
-    }
-    mats.push_back(&c->lm);
-    std::vector<const void*> seen;
-    for (const DevMat* m : mats) {
-        if (m->w == c->emb.w) throw Err(B2_E_UNSUPPORTED, "a GEMV matrix shares the embedding's storage");
-    }
-    for (const DevMat* m : mats) {
-        if (std::find(seen.begin(), seen.end(), m->w) != seen.end()) continue;
-        seen.push_back(m->w);
-        const size_t n16 = (size_t)m->rows * m->ld / 16;
-        bias_codes_kernel<<<(unsigned)std::min<size_t>((n16 + 255) / 256, 4096), 256, 0, c->stream>>>(
-            reinterpret_cast<uint4*>(const_cast<void*>(m->w)), n16);
-        CK(cudaGetLastError());
-    }
-    CK(cudaStreamSynchronize(c->stream));
-}
-
 void capture_graphs(b2_ctx* c) {
     const char* env = std::getenv("B2_NO_PDL");
     c->pdl = !(env && env[0] == '1');
@@ -794,7 +767,6 @@ void capture_graphs(b2_ctx* c) {
     if (c->token) {
         try {
             capture_graphs_once(c);
-            bias_gemv_codes(c);
             return;
         } catch (const Err& e) {
             cudaGetLastError();

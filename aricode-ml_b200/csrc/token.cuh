@@ -25,8 +25,7 @@
 //   TK_EMBED  CTA 0 writes x = embedding row (+ learned position);
 //   TK_GEMV   the building blocks of gemv_kernel (gemv.cuh): prologue norm,
 //             stages, epilogue (residual, RoPE + KV append, SiLU*up, GELU, argmax);
-//             the int8 matrices of the model are stored biased (code ^ 0x80, done
-//             once when the token kernel is set up), which saves the per-word XOR;
+//             int8 rows as the exact fixed-point dot of gemv_stage_i8;
 //   TK_ATTN   split-KV decode attention: item (query head h, 64-key split s) on
 //             CTA item % grid; the K chunk and V chunk arrive as two ring
 //             stages; the row of the current position (written by this step's
@@ -71,7 +70,9 @@ constexpr int kTkDescBytes = 864;                 // one phase descriptor copy (
 constexpr int kTkDescOffset = 3072;               // >= kTkScratchOffset + 2 * kTkGroupScratch * 4
 static_assert(kTkScratchOffset + 2 * kTkGroupScratch * 4 <= kTkDescOffset, "scratch layout");
 static_assert(4 * kTkMaxSlots * 8 <= kTkEmptyOffset && kTkEmptyOffset + kTkMaxSlots * 8 <= kTkRedOffset, "barriers");
-constexpr int kTkPartOffset = kTkDescOffset + 3 * kTkDescBytes + 32;   // 2 consumer + 1 producer copies
+constexpr int kTkPjOffset = kTkDescOffset + 4 * kTkDescBytes;          // 2 consumer, producer, look-ahead copies
+constexpr int kTkPartOffset = kTkPjOffset + 64;                       // producer's next stage index
+constexpr int kTkDone = 1 << 30;                                       // ... once it has finished
 // 640 threads: warpgroups 0-3 consume, warpgroup 4 produces (one lane works).
 // Launched at 96 registers a thread (61,440 per CTA); the producer warpgroup
 // hands registers back (setmaxnreg.dec) and the consumers take them
@@ -123,7 +124,7 @@ __device__ __forceinline__ void tk_copy_desc(TkPhase* dst, const TkPhase* src, i
 struct TkParams {
     const TkPhase* phases;
     int nphases;
-    int ns;             // ring slots (even, <= kTkMaxSlots)
+    int ns;             // ring slots (3 .. kTkMaxSlots)
     int ring_offset;    // bytes (128-aligned)
     unsigned* bar;      // [0] grid-barrier arrivals, [1] exits; zero between launches
     StepState* st;
@@ -132,6 +133,7 @@ struct TkParams {
     int inflight;       // bulk copies outstanding per CTA (1 .. ns - 1)
     int vec_offset;     // shared-memory buffer for a phase's x and norm gains (bytes, 128-aligned)
     int vec_floats;     // its capacity
+    int l2_ahead;       // stages brought into L2 ahead of their bulk copy (0: off)
     // optional timeline (nullptr: off): [phase][cta][kTkStamps] global-timer stamps
     // at the phase start (after the grid barrier), when x is loaded, after the
     // prologue, after the stages and after the epilogue
@@ -252,10 +254,93 @@ __device__ __forceinline__ int tk_attn_items(const AttnParams& a, int n, int& ns
     return a.H * nsplit;
 }
 
+// L2 look-ahead, run by a second warp of the producer warpgroup: a cursor over
+// the producer's stage sequence (every phase's stages in order, attention padding
+// included, so its count is the ring index j of the stage it touches) that issues
+// `cp.async.bulk.prefetch.L2` up to `ahead` stages past the producer's next bulk
+// copy (published in shared memory). DRAM keeps streaming while the ring is
+// full, e.g. across a grid barrier, and the bulk copies that follow hit L2. The
+// cursor reads its phase descriptors into its own shared copy.
+struct alignas(16) TkAhead {
+    const TkPhase* phases;
+    TkPhase* desc;
+    int nphases, ahead, cta, ncta, n;       // n: keys attended this step
+    int ph = 0, cur = 0, end = 0, sub = 0, wj = 0;
+    bool init = false;
+
+    __device__ __forceinline__ bool step() {
+        while (ph < nphases) {
+            const TkPhase& T = *desc;
+            if (!init) {
+                tk_copy_desc<16>(desc, phases + ph, 0, 1);
+                init = true;
+                sub = 0;
+                if (T.kind == TK_GEMV) {
+                    cta_rows(total_rows(T.g), T.unit, cta, ncta, cur, end);
+                } else if (T.kind == TK_ATTN) {
+                    int nsplit;
+                    end = tk_attn_items(T.a, n, nsplit);
+                    cur = cta;
+                    if (wj & 1) ++wj;                   // the padding stage copies nothing
+                } else {
+                    cur = end = 0;
+                }
+            }
+            if (T.kind == TK_GEMV && cur < end) {
+                const GemvParams& p = T.g;
+                const uint32_t row_bytes = (uint32_t)p.ld * (T.variant < TV_F32_K1_R8 ? 1u : 4u);
+                const StageRows sr = next_stage(p, cur, end, T.rows);
+                const uint32_t bytes = (uint32_t)sr.nr * row_bytes;
+                bulk_prefetch_l2(reinterpret_cast<const unsigned char*>(p.W[sr.seg]) + (size_t)sr.local * row_bytes,
+                                 bytes);
+                if (p.paired)
+                    bulk_prefetch_l2(reinterpret_cast<const unsigned char*>(p.W[1]) + (size_t)sr.local * row_bytes,
+                                     bytes);
+                cur += sr.nr;
+                ++wj;
+                return true;
+            }
+            if (T.kind == TK_ATTN && cur < end) {
+                const AttnParams& a = T.a;
+                int nsplit;
+                tk_attn_items(a, n, nsplit);
+                const int h = cur / nsplit, sp = cur % nsplit, kvh = h / (a.H / a.KVH);
+                const int j0 = sp * kAttnChunk, len = min(kAttnChunk, n - j0);
+                const size_t off = ((size_t)kvh * a.max_seq + j0) * a.dh;
+                bulk_prefetch_l2(sub ? a.V + off : a.K + off, (uint32_t)len * a.dh * 4);
+                if (++sub == 2) {
+                    sub = 0;
+                    cur += ncta;
+                }
+                ++wj;
+                return true;
+            }
+            ++ph;
+            init = false;
+        }
+        return false;
+    }
+    // follow the producer's published stage index until it is done (kTkDone) or
+    // the cursor has no stage left; bounded by the usual wait limit
+    __device__ void follow(const volatile int* pj) {
+        const uint64_t t0 = globaltimer_ns();
+        for (;;) {
+            const int j = *pj;
+            if (j >= kTkDone) return;
+            bool more = true;
+            while (wj <= j + ahead && (more = step())) {
+            }
+            if (!more) return;
+            __nanosleep(256);
+            if (globaltimer_ns() - t0 > kWaitLimitNs) return;
+        }
+    }
+};
+
 // producer side: a padding stage keeps every item's K stage on an even index
 __device__ __forceinline__ bool tk_attn_produce(const AttnParams& a, int n, int cta, int ncta,
                                                 unsigned char* ring, int NS, uint64_t* full, uint64_t* empty,
-                                                int& j, int inflight) {
+                                                int& j, int inflight, volatile int* pj) {
     int nsplit;
     const int items = tk_attn_items(a, n, nsplit);
     const int G = a.H / a.KVH, dh = a.dh;
@@ -271,6 +356,7 @@ __device__ __forceinline__ bool tk_attn_produce(const AttnParams& a, int n, int 
         const uint32_t bytes = (uint32_t)len * dh * 4;
         const size_t off = ((size_t)kvh * a.max_seq + j0) * dh;
         for (int kv = 0; kv < 2; ++kv) {
+            *pj = j;
             uint64_t* bar = tk_issue_wait(full, empty, NS, j, inflight);
             if (!bar) return false;
             mbar_arrive_expect_tx(bar, bytes);
@@ -443,10 +529,11 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
 template <int NM>
 __device__ __forceinline__ bool tk_gemv_produce(const GemvParams& p, int r0, int r1, int RS, int rows,
                                                 uint32_t row_bytes, unsigned char* ring, int NS, uint64_t* full,
-                                                uint64_t* empty, int& j, int inflight) {
+                                                uint64_t* empty, int& j, int inflight, volatile int* pj) {
     int cur = r0;
     while (cur < r1) {
         const StageRows sr = next_stage(p, cur, r1, rows);
+        *pj = j;
         uint64_t* bar = tk_issue_wait(full, empty, NS, j, inflight);
         if (!bar) return false;
         const uint32_t bytes = (uint32_t)sr.nr * row_bytes;
@@ -462,8 +549,8 @@ __device__ __forceinline__ bool tk_gemv_produce(const GemvParams& p, int r0, int
     return true;
 }
 
-// GEMV consumers over the token ring: group j & 1 takes stage j. XREG: x slice in
-// registers (long rows, gemv_consume_stage); otherwise x from shared memory
+// f32 GEMV consumers over the token ring: group j & 1 takes stage j. XREG: x slice
+// in registers (long rows, gemv_consume_stage); otherwise x from shared memory
 // (gemv_consume_stage_xt).
 template <typename WT, int RS, int NM, int KB, bool XREG>
 __device__ __forceinline__ bool tk_gemv_consume(const GemvParams& p, int r0, int r1, int rows,
@@ -494,11 +581,50 @@ __device__ __forceinline__ bool tk_gemv_consume(const GemvParams& p, int r0, int
             if (!mbar_wait_bounded(tk_full(full, j, NS), tk_full_parity(j, NS))) return false;
             const unsigned char* st = ring + (size_t)(j % NS) * kTkSlotBytes;
             if constexpr (XREG)
-                gemv_consume_stage<WT, 3, RS, NM == 2, true>(st, row_bytes, nblk, slotid, lane, gwarp, xr, part,
-                                                             cur - r0, sr.nr);
+                gemv_consume_stage<WT, 3, RS, NM == 2>(st, row_bytes, nblk, slotid, lane, gwarp, xr, part,
+                                                       cur - r0, sr.nr);
             else
-                gemv_consume_stage_xt<WT, RS, NM, KB, true>(st, row_bytes, nblk, slotid, lane, gwarp, xs, part,
-                                                            cur - r0, sr.nr);
+                gemv_consume_stage_xt<WT, RS, NM, KB>(st, row_bytes, nblk, slotid, lane, gwarp, xs, part,
+                                                      cur - r0, sr.nr);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[j % NS]);
+        }
+        ++j;
+        cur += sr.nr;
+    }
+    return true;
+}
+
+// int8 GEMV consumers over the token ring: the thread's planes of the staged,
+// normalised x (blocks slotid, slotid + 256, ... of KB) in registers, then the
+// stages (group j & 1 takes stage j), plane sums into part[] (int32).
+template <int KB, int RS, int NM>
+__device__ __forceinline__ bool tk_gemv_consume_i8(const GemvParams& p, int r0, int r1, int rows,
+                                                   const unsigned char* ring, int NS, uint64_t* full, uint64_t* empty,
+                                                   int& j, int group, int lane, int slotid, const float* xs, int S,
+                                                   int* part) {
+    const uint32_t row_bytes = (uint32_t)p.ld;
+    const int nblk = (int)(row_bytes >> 4);
+    uint32_t xp[KB][16];
+#pragma unroll
+    for (int k = 0; k < KB; ++k) {
+        const int b = slotid + 256 * k;
+        float t[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            float4 x4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            if (b < nblk) x4 = lds128f(xs + b * 16 + 4 * q);
+            t[4 * q] = x4.x; t[4 * q + 1] = x4.y; t[4 * q + 2] = x4.z; t[4 * q + 3] = x4.w;
+        }
+        xfix_block(t, S, xp[k]);
+    }
+    int cur = r0;
+    while (cur < r1) {
+        const StageRows sr = next_stage(p, cur, r1, rows);
+        if ((j & 1) == group) {
+            if (!mbar_wait_bounded(tk_full(full, j, NS), tk_full_parity(j, NS))) return false;
+            gemv_stage_i8<KB, RS, NM>(ring + (size_t)(j % NS) * kTkSlotBytes, row_bytes, nblk, slotid, lane, xp, part,
+                                      cur - r0, sr.nr);
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[j % NS]);
         }
@@ -519,7 +645,8 @@ __device__ __forceinline__ bool tk_gemv(const GemvParams& p, int unit, int rs, i
                                         const unsigned char* ring,
                                         int NS, uint64_t* full, uint64_t* empty, int& j, int group, int gwarp,
                                         int lane, int tid, float* red, float* part, int cta, int ncta,
-                                        unsigned long long* tr, float* vec, uint64_t* vbar, uint32_t& vphase) {
+                                        unsigned long long* tr, float* vec, uint64_t* vbar, uint32_t& vphase,
+                                        unsigned* amx) {
     constexpr int ESZ = (int)sizeof(WT);
     int r0, r1;
     cta_rows(total_rows(p), unit, cta, ncta, r0, r1);
@@ -537,37 +664,65 @@ __device__ __forceinline__ bool tk_gemv(const GemvParams& p, int unit, int rs, i
         if (p.norm == NORM_LN) bulk_g2s(vec + 2 * L, p.nb, (uint32_t)n * 4, vbar);
     }
     for (int i = n + tid; i < L; i += kGemvConsumerThreads) vec[i] = 0.0f;     // row padding
-    // part[]: [rows][NM][8] warp sums, then epi[]: [rows][4] epilogue inputs
-    float* epi = part + (size_t)(r1 - r0) * (paired ? 2 : 1) * 8;
+    // part[]: [rows][NM][8] f32 warp sums (int8: [rows][NM][4] int32 plane sums),
+    // then epi[]: [rows][4] epilogue inputs
+    const int nm = paired ? 2 : 1;
+    float* epi = part + (size_t)(r1 - r0) * nm * 8;
+    if constexpr (ESZ == 1)
+        for (int i = tid; i < (r1 - r0) * nm * 4; i += kGemvConsumerThreads) reinterpret_cast<int*>(part)[i] = 0;
     const EpiRow er = paired ? gemv_epi_load<ESZ, true>(p, r0, r1, pos, tid)
                              : gemv_epi_load<ESZ, false>(p, r0, r1, pos, tid);
     bool ok = mbar_wait_bounded(vbar, vphase & 1);
     ++vphase;
-    gemv_norm_smem(p, vec, vec + L, vec + 2 * L, red, tid);
+    const uint32_t am = gemv_norm_smem(p, vec, vec + L, vec + 2 * L, red, tid);
     tk_stamp(tr, 1, tid);
     gemv_epi_store(er, r1 - r0, tid, epi);
-    consumer_bar();                                     // normalised x and epi[] visible
-    tk_stamp(tr, 2, tid);
-    // the stage shapes the host chose (rows per stage x matrices), compiled
     const int slotid = tid % 256;
     bool okc;
-    if (paired) {
-        okc = rs == 4 ? tk_gemv_consume<WT, 4, 2, 1, false>(p, r0, r1, rows, ring, NS, full, empty, j, group, gwarp,
-                                                            lane, slotid, vec, part)
-                      : tk_gemv_consume<WT, 1, 2, 3, true>(p, r0, r1, rows, ring, NS, full, empty, j, group, gwarp,
-                                                           lane, slotid, vec, part);
+    int S = 0;
+    if constexpr (ESZ == 1) {
+        S = xfix_shift_cta(am, amx);                    // also publishes x, epi[] and the zeroed part[]
+        tk_stamp(tr, 2, tid);
+        int* parti = reinterpret_cast<int*>(part);
+        if (paired)
+            okc = rs == 4 ? tk_gemv_consume_i8<1, 4, 2>(p, r0, r1, rows, ring, NS, full, empty, j, group, lane, slotid,
+                                                        vec, S, parti)
+                          : tk_gemv_consume_i8<3, 1, 2>(p, r0, r1, rows, ring, NS, full, empty, j, group, lane, slotid,
+                                                        vec, S, parti);
+        else
+            okc = rs == 8 ? tk_gemv_consume_i8<1, 8, 1>(p, r0, r1, rows, ring, NS, full, empty, j, group, lane, slotid,
+                                                        vec, S, parti)
+                          : tk_gemv_consume_i8<3, 2, 1>(p, r0, r1, rows, ring, NS, full, empty, j, group, lane, slotid,
+                                                        vec, S, parti);
+        ok = okc && ok;
+        consumer_bar();
+        if (tid == 0) *amx = 0u;                        // every thread read it before its stages
+        tk_stamp(tr, 3, tid);
+        if (paired) gemv_epilogue<ESZ, true>(p, r0, r1, part, pos, tid, cta, ncta, epi, S);
+        else gemv_epilogue<ESZ, false>(p, r0, r1, part, pos, tid, cta, ncta, epi, S);
+        return ok;
     } else {
-        okc = rs == 8 ? tk_gemv_consume<WT, 8, 1, 1, false>(p, r0, r1, rows, ring, NS, full, empty, j, group, gwarp,
-                                                            lane, slotid, vec, part)
-                      : tk_gemv_consume<WT, 2, 1, 3, true>(p, r0, r1, rows, ring, NS, full, empty, j, group, gwarp,
-                                                           lane, slotid, vec, part);
+        consumer_bar();                                     // normalised x and epi[] visible
+        tk_stamp(tr, 2, tid);
+        // the stage shapes the host chose (rows per stage x matrices), compiled
+        if (paired) {
+            okc = rs == 4 ? tk_gemv_consume<WT, 4, 2, 1, false>(p, r0, r1, rows, ring, NS, full, empty, j, group, gwarp,
+                                                                lane, slotid, vec, part)
+                          : tk_gemv_consume<WT, 1, 2, 3, true>(p, r0, r1, rows, ring, NS, full, empty, j, group, gwarp,
+                                                               lane, slotid, vec, part);
+        } else {
+            okc = rs == 8 ? tk_gemv_consume<WT, 8, 1, 1, false>(p, r0, r1, rows, ring, NS, full, empty, j, group, gwarp,
+                                                                lane, slotid, vec, part)
+                          : tk_gemv_consume<WT, 2, 1, 3, true>(p, r0, r1, rows, ring, NS, full, empty, j, group, gwarp,
+                                                               lane, slotid, vec, part);
+        }
+        ok = okc && ok;
+        consumer_bar();
+        tk_stamp(tr, 3, tid);
+        if (paired) gemv_epilogue<ESZ, true>(p, r0, r1, part, pos, tid, cta, ncta, epi);
+        else gemv_epilogue<ESZ, false>(p, r0, r1, part, pos, tid, cta, ncta, epi);
+        return ok;
     }
-    ok = okc && ok;
-    consumer_bar();
-    tk_stamp(tr, 3, tid);
-    if (paired) gemv_epilogue<ESZ, true>(p, r0, r1, part, pos, tid, cta, ncta, epi);
-    else gemv_epilogue<ESZ, false>(p, r0, r1, part, pos, tid, cta, ncta, epi);
-    return ok;
 }
 
 // VS 0: int8 weights only; VS 1: int8 and f32.
@@ -576,12 +731,12 @@ __device__ __forceinline__ bool tk_gemv_dispatch(const TkPhase& T, int pos, cons
                                                  uint64_t* full, uint64_t* empty, int& j, int group, int gwarp,
                                                  int lane, int tid, float* red, float* part, int cta, int ncta,
                                                  unsigned long long* tr, float* vec, uint64_t* vbar,
-                                                 uint32_t& vphase) {
+                                                 uint32_t& vphase, unsigned* amx) {
     if (VS == 1 && T.variant >= TV_F32_K1_R8)
         return tk_gemv<float>(T.g, T.unit, T.rs, T.rows, pos, ring, NS, full, empty, j, group, gwarp, lane, tid, red, part,
-                              cta, ncta, tr, vec, vbar, vphase);
+                              cta, ncta, tr, vec, vbar, vphase, amx);
     return tk_gemv<int8_t>(T.g, T.unit, T.rs, T.rows, pos, ring, NS, full, empty, j, group, gwarp, lane, tid, red, part, cta,
-                           ncta, tr, vec, vbar, vphase);
+                           ncta, tr, vec, vbar, vphase, amx);
 }
 
 // --------------------------------------------------------------------- the kernel
@@ -593,7 +748,9 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
     float* red = reinterpret_cast<float*>(smem + kTkRedOffset);           // 8 floats
     volatile int* flag = reinterpret_cast<volatile int*>(smem + kTkFlagOffset);   // [0], [4] grid sync, [2..3] groups
     volatile int* abort = flag + 6;
+    unsigned* amx = reinterpret_cast<unsigned*>(smem + kTkFlagOffset + 28);   // int8 GEMV: largest |x| bits
     uint64_t* vbar = reinterpret_cast<uint64_t*>(smem + kTkVbarOffset);  // vector staging
+    volatile int* pj = reinterpret_cast<volatile int*>(smem + kTkPjOffset);
     float* vec = reinterpret_cast<float*>(smem + P.vec_offset);
     float* scratch = reinterpret_cast<float*>(smem + kTkScratchOffset);
     float* part = reinterpret_cast<float*>(smem + kTkPartOffset);
@@ -633,6 +790,8 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
         mbar_init(vbar, 1);
         fence_mbar_init();
         *abort = 0;
+        *amx = 0u;
+        *pj = 0;
     }
     __syncthreads();
 
@@ -655,19 +814,24 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
                     const uint32_t row_bytes = (uint32_t)p.ld * (i8 ? 1u : 4u);
                     tk_prefetch_vectors(p, r0, r1, pos, i8);
                     ok = p.paired ? tk_gemv_produce<2>(p, r0, r1, T.rs, T.rows, row_bytes, ring, NS, full, empty, j,
-                                                       P.inflight)
+                                                       P.inflight, pj)
                                   : tk_gemv_produce<1>(p, r0, r1, T.rs, T.rows, row_bytes, ring, NS, full, empty, j,
-                                                       P.inflight);
+                                                       P.inflight, pj);
                 } else if (T.kind == TK_ATTN) {
-                    ok = tk_attn_produce(T.a, pos + 1, cta, ncta, ring, NS, full, empty, j, P.inflight);
+                    ok = tk_attn_produce(T.a, pos + 1, cta, ncta, ring, NS, full, empty, j, P.inflight, pj);
                 }
             }
+            *pj = kTkDone;
             if (!ok) set_err(err, B2_DEV_ERR_TIMEOUT);
             for (int i = max(0, j - NS); i < j; ++i)        // no copy in flight at exit
                 if (!mbar_wait_bounded(tk_full(full, i, NS), tk_full_parity(i, NS))) {
                     set_err(err, B2_DEV_ERR_TIMEOUT);
                     break;
                 }
+        } else if (warp == kGemvConsumerWarps + 1 && lane == 0 && P.l2_ahead > 0) {
+            TkAhead ah{P.phases, reinterpret_cast<TkPhase*>(smem + kTkDescOffset + 3 * kTkDescBytes), P.nphases,
+                       P.l2_ahead, cta, ncta, pos + 1};
+            ah.follow(pj);
         }
         return;
     }
@@ -719,7 +883,7 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
             }
         } else if (T.kind == TK_GEMV) {
             ok = tk_gemv_dispatch<VS>(T, pos, ring, NS, full, empty, j, group, gwarp, lane, tid, red, part, cta,
-                                      ncta, tr, vec, vbar, vphase);
+                                      ncta, tr, vec, vbar, vphase, amx);
         } else {
             tk_stamp(tr, 1, tid);
             tk_stamp(tr, 2, tid);

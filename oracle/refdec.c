@@ -208,32 +208,57 @@ static float reduce256(float* s) {
 }
 
 /* ------------------------------------------------------------------------
- * Dot products. Shared order (the CUDA GEMV uses the same):
- *  - the row is viewed as 16-byte blocks (16 int8 or 4 f32); bytes past n are 0
- *    and so is x there;
+ * int8 rows (arr_i8_matvec_f32_perrow; call sites tools/aricode_pack.py:183,
+ * :1789-1808, attention_gqa_kv_i8.ari:149-151): the dot product is computed
+ * exactly on a fixed-point copy of x and rounded once, so it has no association
+ * order (integer sums are exact in any order) and any thread layout on the GPU
+ * gives these bits:
+ *   max|x| < 2^E (frexp exponent), S = 31 - E, X_i = trunc(x_i * 2^S), |X_i| < 2^31;
+ *   D = sum_i w_i * X_i (exact in int64), dot = f32((double)D * 2^-S), one rounding;
+ *   y = dot * scale (f32).
+ * Truncating x to 31 bits below its largest element errs by at most 2^-31 max|x|
+ * per element, far below the rounding of an f32 accumulation. A NaN or an
+ * infinity in x makes every row NaN.
+ * ------------------------------------------------------------------------ */
+int b2o_xfix(const float* x, int64_t n, int32_t* X) {
+    uint32_t amax = 0;
+    for (int64_t i = 0; i < n; ++i) {
+        uint32_t u;
+        memcpy(&u, &x[i], 4);
+        u &= 0x7fffffffu;                       /* non-negative floats order as their bits */
+        if (u > amax) amax = u;
+    }
+    if (amax >= 0x7f800000u) return B2O_XFIX_BAD;
+    if (amax == 0) {
+        memset(X, 0, (size_t)n * sizeof(int32_t));
+        return 0;
+    }
+    float am;
+    memcpy(&am, &amax, 4);
+    int E;
+    frexp((double)am, &E);
+    const int S = 31 - E;
+    const double p = ldexp(1.0, S);
+    for (int64_t i = 0; i < n; ++i) X[i] = (int32_t)((double)x[i] * p);   /* exact product, truncation */
+    return S;
+}
+
+float b2o_dot_i8x(const int8_t* w, const int32_t* X, int64_t n, int S) {
+    if (S == B2O_XFIX_BAD) return NAN;
+    int64_t D = 0;
+    for (int64_t i = 0; i < n; ++i) D += (int64_t)w[i] * (int64_t)X[i];
+    return (float)((double)D * ldexp(1.0, -S));
+}
+
+/* ------------------------------------------------------------------------
+ * f32 rows, shared order (the CUDA GEMV uses the same):
+ *  - the row is viewed as 16-byte blocks (4 f32); elements past n are 0 and so
+ *    is x there;
  *  - slot s in 0..255 owns blocks s, s+256, s+512, ... in ascending order and
- *    keeps four accumulators a[t&3] over element t of each block (fused
+ *    keeps four accumulators a[t] over element t of each block (fused
  *    multiply-add); slot partial = (a0 + a1) + (a2 + a3);
  *  - the 256 slot partials go through reduce256().
  * ------------------------------------------------------------------------ */
-float b2o_dot_i8(const int8_t* w, const float* x, int64_t n) {
-    const int64_t nblk = (n + 15) / 16;
-    float part[256];
-    for (int sl = 0; sl < 256; ++sl) {
-        float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        for (int64_t b = sl; b < nblk; b += 256) {
-            for (int t = 0; t < 16; ++t) {
-                const int64_t k = 16 * b + t;
-                const float wv = k < n ? (float)w[k] : 0.0f;
-                const float xv = k < n ? x[k] : 0.0f;
-                a[t & 3] = fmaf(wv, xv, a[t & 3]);
-            }
-        }
-        part[sl] = (a[0] + a[1]) + (a[2] + a[3]);
-    }
-    return reduce256(part);
-}
-
 float b2o_dot_f32(const float* w, const float* x, int64_t n) {
     const int64_t nblk = (n + 3) / 4;
     float part[256];
@@ -252,12 +277,15 @@ float b2o_dot_f32(const float* w, const float* x, int64_t n) {
     return reduce256(part);
 }
 
-typedef struct { const void* W; int64_t ld; const float* scale; const float* x; int64_t n; float* y; } gemv_ctx;
+typedef struct {
+    const void* W; int64_t ld; const float* scale; const float* x; int64_t n; float* y;
+    const int32_t* X; int S;
+} gemv_ctx;
 
 static void gemv_i8_range(void* c, int64_t r0, int64_t r1) {
     const gemv_ctx* g = (const gemv_ctx*)c;
     const int8_t* W = (const int8_t*)g->W;
-    for (int64_t r = r0; r < r1; ++r) g->y[r] = b2o_dot_i8(W + r * g->ld, g->x, g->n) * g->scale[r];
+    for (int64_t r = r0; r < r1; ++r) g->y[r] = b2o_dot_i8x(W + r * g->ld, g->X, g->n, g->S) * g->scale[r];
 }
 static void gemv_f32_range(void* c, int64_t r0, int64_t r1) {
     const gemv_ctx* g = (const gemv_ctx*)c;
@@ -267,13 +295,17 @@ static void gemv_f32_range(void* c, int64_t r0, int64_t r1) {
 
 void b2o_gemv_i8(const int8_t* W, int64_t ld, const float* scale, const float* x,
                  int64_t m, int64_t n, float* y) {
-    gemv_ctx g = {W, ld, scale, x, n, y};
+    int32_t* X = (int32_t*)malloc((size_t)(n > 0 ? n : 1) * sizeof(int32_t));
+    if (!X) abort();
+    const int S = b2o_xfix(x, n, X);
+    gemv_ctx g = {W, ld, scale, x, n, y, X, S};
     parallel_for(m, gemv_i8_range, &g);
+    free(X);
 }
 
 void b2o_gemv_f32(const float* W, int64_t ld, const float* x,
                   int64_t m, int64_t n, float* y) {
-    gemv_ctx g = {W, ld, NULL, x, n, y};
+    gemv_ctx g = {W, ld, NULL, x, n, y, NULL, 0};
     parallel_for(m, gemv_f32_range, &g);
 }
 

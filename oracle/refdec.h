@@ -56,8 +56,13 @@ void b2o_gemv_i8(const int8_t* W, int64_t ld, const float* scale, const float* x
                  int64_t m, int64_t n, float* y);
 void b2o_gemv_f32(const float* W, int64_t ld, const float* x,
                   int64_t m, int64_t n, float* y);
-/* dot products in the shared order, exposed for tests */
-float b2o_dot_i8(const int8_t* w, const float* x, int64_t n);
+/* int8 rows: x as 32-bit block fixed point X = trunc(x * 2^S); returns S, or
+ * B2O_XFIX_BAD when x holds a NaN or an infinity (every row is then NaN) */
+#define B2O_XFIX_BAD (-100000)
+int b2o_xfix(const float* x, int64_t n, int32_t* X);
+/* one row: f32(sum w*X exactly, times 2^-S) */
+float b2o_dot_i8x(const int8_t* w, const int32_t* X, int64_t n, int S);
+/* f32 rows: dot product in the shared order, exposed for tests */
 float b2o_dot_f32(const float* w, const float* x, int64_t n);
 
 /* ---- norms ---- */

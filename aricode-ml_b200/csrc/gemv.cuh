@@ -231,6 +231,72 @@ __device__ __forceinline__ double pow2d(int k) { return __longlong_as_double((lo
 
 __device__ __forceinline__ uint32_t abs_bits(float v) { return __float_as_uint(v) & 0x7fffffffu; }
 
+// trunc(x * 2^S) from the bits of x (integer operations only): x = man * 2^(e - 150)
+// with the implicit bit in man (subnormals: e = 1, no implicit bit), so the
+// magnitude is man shifted by k = e - 150 + S (k <= 7, as |x| 2^S < 2^31), and the
+// shift right truncates toward zero like the conversion it replaces.
+__device__ __forceinline__ uint32_t xfix_elem(float x, int S) {
+    const uint32_t u = __float_as_uint(x);
+    const int ex = (int)((u >> 23) & 0xffu);
+    const uint32_t man = (u & 0x7fffffu) | (ex ? 0x800000u : 0u);
+    const int k = (ex ? ex : 1) - 150 + S;
+    const uint32_t mag = k >= 0 ? (man << k) : (k > -32 ? (man >> (-k)) : 0u);
+    return (u >> 31) ? 0u - mag : mag;
+}
+
+// chunk swizzle of a block of planes in shared memory (xfix_smem)
+__device__ __forceinline__ int xfix_swz(int b) { return (b >> 1) & 3; }
+
+// four X values -> their four byte planes (element 0 in the low byte)
+__device__ __forceinline__ void xfix_planes4(uint32_t x0, uint32_t x1, uint32_t x2, uint32_t x3, uint32_t (&pl)[4]) {
+    const uint32_t lo01 = __byte_perm(x0, x1, 0x5140u), hi01 = __byte_perm(x0, x1, 0x7362u);
+    const uint32_t lo23 = __byte_perm(x2, x3, 0x5140u), hi23 = __byte_perm(x2, x3, 0x7362u);
+    pl[0] = __byte_perm(lo01, lo23, 0x5410u);
+    pl[1] = __byte_perm(lo01, lo23, 0x7632u);
+    pl[2] = __byte_perm(hi01, hi23, 0x5410u);
+    pl[3] = __byte_perm(hi01, hi23, 0x7632u);
+}
+
+// Shared-memory x (L floats, L a multiple of 16) -> planes in place: block b's
+// 16 words hold w[p * 4 + q] = byte p of elements 16b + 4q .. + 3, its four
+// 16-byte chunks (plane p in chunk p) stored at chunk p ^ xfix_swz(b), so that
+// eight threads reading consecutive blocks hit eight bank groups. A thread
+// converts one group of 4 elements per pass (a warp covers 8 whole blocks, so
+// every read of a block precedes its writes after __syncwarp). With S <= 127,
+// x * 2^S is exact in f32 (|x| 2^S < 2^31; a product that underflows is below 1
+// and truncates to 0 either way) and cvt.rzi gives trunc; otherwise the integer
+// path. Every consumer thread calls it; it ends with the consumer barrier.
+__device__ __forceinline__ void xfix_smem(float* xs, int L, int S, int tid) {
+    const int nq = L / 4;
+    const float p2 = S <= 127 ? __uint_as_float((uint32_t)(S + 127) << 23) : 0.0f;
+    for (int q0 = tid - (tid & 31); q0 < nq; q0 += kGemvConsumerThreads) {
+        const int qd = q0 + (tid & 31);
+        uint32_t pl[4] = {0u, 0u, 0u, 0u};
+        if (qd < nq && S != kXfixBad) {
+            const float4 v = *reinterpret_cast<const float4*>(xs + 4 * qd);
+            uint32_t X[4];
+            if (S <= 127) {
+                X[0] = (uint32_t)__float2int_rz(__fmul_rn(v.x, p2));
+                X[1] = (uint32_t)__float2int_rz(__fmul_rn(v.y, p2));
+                X[2] = (uint32_t)__float2int_rz(__fmul_rn(v.z, p2));
+                X[3] = (uint32_t)__float2int_rz(__fmul_rn(v.w, p2));
+            } else {
+                X[0] = xfix_elem(v.x, S); X[1] = xfix_elem(v.y, S);
+                X[2] = xfix_elem(v.z, S); X[3] = xfix_elem(v.w, S);
+            }
+            xfix_planes4(X[0], X[1], X[2], X[3], pl);
+        }
+        __syncwarp();
+        if (qd < nq) {
+            const int b = qd >> 2, f = xfix_swz(b);
+            uint32_t* wb = reinterpret_cast<uint32_t*>(xs) + 16 * b + (qd & 3);
+            wb[4 * (0 ^ f)] = pl[0]; wb[4 * (1 ^ f)] = pl[1]; wb[4 * (2 ^ f)] = pl[2]; wb[4 * (3 ^ f)] = pl[3];
+        }
+        __syncwarp();
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(kGemvConsumerThreads) : "memory");
+}
+
 // 16 consecutive elements of x -> their planes: w[p * 4 + q] holds byte p of
 // elements 4q .. 4q + 3 (element 4q in the low byte)
 __device__ __forceinline__ void xfix_block(const float (&x)[16], int S, uint32_t (&w)[16]) {
@@ -239,12 +305,11 @@ __device__ __forceinline__ void xfix_block(const float (&x)[16], int S, uint32_t
         for (int i = 0; i < 16; ++i) w[i] = 0u;
         return;
     }
-    const double p2s = pow2d(S);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
         uint32_t X[4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) X[k] = (uint32_t)__double2int_rz(__dmul_rn((double)x[4 * q + k], p2s));
+        for (int k = 0; k < 4; ++k) X[k] = xfix_elem(x[4 * q + k], S);
         const uint32_t lo01 = __byte_perm(X[0], X[1], 0x5140u), hi01 = __byte_perm(X[0], X[1], 0x7362u);
         const uint32_t lo23 = __byte_perm(X[2], X[3], 0x5140u), hi23 = __byte_perm(X[2], X[3], 0x7362u);
         w[0 * 4 + q] = __byte_perm(lo01, lo23, 0x5410u);

@@ -11,7 +11,8 @@
 // Structure of a CTA (640 threads, ~208 KB shared memory):
 //   warpgroup 4    producer: one lane walks all phases, one 1-D bulk copy per
 //                  stage into a ring of NS 32 KB slots (mbarrier complete_tx), at
-//                  most kTkInflight copies outstanding; it also prefetches each
+//                  most kTkInflight copies outstanding (0: no cap beyond the
+//                  ring); it also prefetches each
 //                  phase's small vectors (norm gains, scales, biases) into L2;
 //   warpgroups 0-3 consumers in two groups of 8 warps; stage j belongs to group
 //                  j & 1 in GEMV phases and to group (j / 2) & 1 in attention
@@ -55,8 +56,9 @@ enum TkVariant : int {
 constexpr uint32_t kTkSlotBytes = 32 * 1024;
 constexpr int kTkMaxSlots = 7;                    // any count >= 3 (see tk_full)
 constexpr int kTkStamps = 8;                      // timeline slots per phase and CTA
-constexpr int kTkInflight = 3;                    // default bulk copies outstanding per CTA (< slots)
+constexpr int kTkInflight = 0;                    // default cap on bulk copies outstanding per CTA (0: none)
 constexpr int kTkMaxSplits = 256;                 // max_seq <= 16384
+constexpr int kTkFastCombine = 16;               // splits combined in one round of loads (n <= 1024)
 constexpr int kTkGroupScratch = 64 + 4 + kTkMaxSplits;   // floats per consumer group
 // shared memory: full barriers [0, 224) (4 per slot), empty barriers [224, 288),
 // reduction slots [288, 320), flags [320, 352), vector-staging barrier 352
@@ -134,6 +136,7 @@ struct TkParams {
     int vec_offset;     // shared-memory buffer for a phase's x and norm gains (bytes, 128-aligned)
     int vec_floats;     // its capacity
     int l2_ahead;       // stages brought into L2 ahead of their bulk copy (0: off)
+    int x_lsu;          // 1: stage a phase's x and gains with plain loads instead of a bulk copy
     // optional timeline (nullptr: off): [phase][cta][kTkStamps] global-timer stamps
     // at the phase start (after the grid barrier), when x is loaded, after the
     // prologue, after the stages and after the epilogue
@@ -484,6 +487,39 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
         // last split of head h: combine the splits and the -60 tail
         __threadfence();
         const float* base = a.part + (size_t)h * a.nsplit_max * stride;
+        if (nsplit <= kTkFastCombine) {
+            // one round of loads: every split's (m, l) into scratch by threads
+            // t < nsplit, and each thread's o[gt] of every split into registers; then
+            // each thread forms M, the weights and l itself, in split order
+            float ot[kTkFastCombine];
+            if (gt < nsplit) {
+                wsm[gt] = __ldcg(base + (size_t)gt * stride + dh);
+                sc[gt] = __ldcg(base + (size_t)gt * stride + dh + 1);
+            }
+#pragma unroll
+            for (int t = 0; t < kTkFastCombine; ++t)
+                ot[t] = (t < nsplit && gt < dh) ? __ldcg(base + (size_t)t * stride + gt) : 0.0f;
+            group_bar(group);
+            if (gt < dh) {
+                float M = wsm[0];
+                for (int t = 1; t < nsplit; ++t) M = fmaxf(M, wsm[t]);
+                if (n < a.max_seq) M = fmaxf(M, -60.0f);
+                float l = 0.0f, o = 0.0f;
+#pragma unroll
+                for (int t = 0; t < kTkFastCombine; ++t) {
+                    if (t < nsplit) {
+                        const float w = exp_f(fsub(wsm[t], M));
+                        l = ffma(sc[t], w, l);
+                        o = ffma(ot[t], w, o);
+                    }
+                }
+                if (n < a.max_seq) l = ffma((float)(a.max_seq - n), exp_f(fsub(-60.0f, M)), l);
+                a.out[(size_t)h * dh + gt] = fdiv(o, l);
+            }
+            if (gt == 0) a.counters[h] = 0u;
+            group_bar(group);                           // scratch reused by the next item
+            continue;
+        }
         // every split's (m, l) in one parallel round of loads: m into wsm, l into sc
         for (int t = gt; t < nsplit; t += 256) {
             wsm[t] = __ldcg(base + (size_t)t * stride + dh);
@@ -595,34 +631,45 @@ __device__ __forceinline__ bool tk_gemv_consume(const GemvParams& p, int r0, int
     return true;
 }
 
-// int8 GEMV consumers over the token ring: the thread's planes of the staged,
-// normalised x (blocks slotid, slotid + 256, ... of KB) in registers, then the
-// stages (group j & 1 takes stage j), plane sums into part[] (int32).
+// int8 GEMV consumers over the token ring: the thread's plane words (blocks
+// slotid, slotid + 256, ... of KB; xs holds the planes, xfix_smem) in registers,
+// then the stages (group j & 1 takes stage j), plane sums into part[] (int32).
 template <int KB, int RS, int NM>
 __device__ __forceinline__ bool tk_gemv_consume_i8(const GemvParams& p, int r0, int r1, int rows,
                                                    const unsigned char* ring, int NS, uint64_t* full, uint64_t* empty,
                                                    int& j, int group, int lane, int slotid, const float* xs, int S,
-                                                   int* part) {
+                                                   int* part, unsigned long long* tr) {
     const uint32_t row_bytes = (uint32_t)p.ld;
     const int nblk = (int)(row_bytes >> 4);
     uint32_t xp[KB][16];
 #pragma unroll
     for (int k = 0; k < KB; ++k) {
         const int b = slotid + 256 * k;
-        float t[16];
+        const int f = xfix_swz(b);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            float4 x4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-            if (b < nblk) x4 = lds128f(xs + b * 16 + 4 * q);
-            t[4 * q] = x4.x; t[4 * q + 1] = x4.y; t[4 * q + 2] = x4.z; t[4 * q + 3] = x4.w;
+        for (int q = 0; q < 4; ++q) {                   // plane q (chunk q ^ f)
+            uint4 w = make_uint4(0u, 0u, 0u, 0u);
+            if (b < nblk) w = lds128(xs + b * 16 + 4 * (q ^ f));
+            xp[k][4 * q] = w.x; xp[k][4 * q + 1] = w.y; xp[k][4 * q + 2] = w.z; xp[k][4 * q + 3] = w.w;
         }
-        xfix_block(t, S, xp[k]);
     }
+    // timeline (thread 0 only): [5] before the first stage wait, [7] after it, [6] total
+    // time waiting for stages
+    const bool stamp = tr && threadIdx.x == 0;
+    unsigned long long waited = 0;
+    bool first = true;
     int cur = r0;
     while (cur < r1) {
         const StageRows sr = next_stage(p, cur, r1, rows);
         if ((j & 1) == group) {
+            const unsigned long long tw = stamp ? globaltimer_ns() : 0ull;
             if (!mbar_wait_bounded(tk_full(full, j, NS), tk_full_parity(j, NS))) return false;
+            if (stamp) {
+                const unsigned long long t = globaltimer_ns();
+                waited += t - tw;
+                if (first) { tr[5] = tw; tr[7] = t; }
+                first = false;
+            }
             gemv_stage_i8<KB, RS, NM>(ring + (size_t)(j % NS) * kTkSlotBytes, row_bytes, nblk, slotid, lane, xp, part,
                                       cur - r0, sr.nr);
             __syncwarp();
@@ -631,6 +678,7 @@ __device__ __forceinline__ bool tk_gemv_consume_i8(const GemvParams& p, int r0, 
         ++j;
         cur += sr.nr;
     }
+    if (stamp) tr[6] = waited;
     return true;
 }
 
@@ -646,13 +694,25 @@ __device__ __forceinline__ bool tk_gemv(const GemvParams& p, int unit, int rs, i
                                         int NS, uint64_t* full, uint64_t* empty, int& j, int group, int gwarp,
                                         int lane, int tid, float* red, float* part, int cta, int ncta,
                                         unsigned long long* tr, float* vec, uint64_t* vbar, uint32_t& vphase,
-                                        unsigned* amx) {
+                                        unsigned* amx, bool xlsu) {
     constexpr int ESZ = (int)sizeof(WT);
     int r0, r1;
     cta_rows(total_rows(p), unit, cta, ncta, r0, r1);
     const bool paired = p.paired != 0;
     const int n = p.n, L = (n + 15) & ~15;
-    if (tid == 0) {
+    if (xlsu) {
+        // plain 16-byte loads through L2: they do not queue behind the producer's
+        // bulk copies in this SM's copy engine (n % 4 == 0, 16-byte aligned)
+        const int n4 = n / 4;
+        float4* v4 = reinterpret_cast<float4*>(vec);
+        for (int i = tid; i < n4; i += kGemvConsumerThreads) v4[i] = __ldcg(reinterpret_cast<const float4*>(p.x) + i);
+        if (p.norm != NORM_NONE)
+            for (int i = tid; i < n4; i += kGemvConsumerThreads)
+                v4[L / 4 + i] = __ldg(reinterpret_cast<const float4*>(p.ng) + i);
+        if (p.norm == NORM_LN)
+            for (int i = tid; i < n4; i += kGemvConsumerThreads)
+                v4[L / 2 + i] = __ldg(reinterpret_cast<const float4*>(p.nb) + i);
+    } else if (tid == 0) {
         // generic-proxy writes (x by other CTAs; vec by this CTA's last phase) are
         // ordered before the bulk copies that read / overwrite them
         asm volatile("fence.proxy.async.global;" ::: "memory");
@@ -672,8 +732,13 @@ __device__ __forceinline__ bool tk_gemv(const GemvParams& p, int unit, int rs, i
         for (int i = tid; i < (r1 - r0) * nm * 4; i += kGemvConsumerThreads) reinterpret_cast<int*>(part)[i] = 0;
     const EpiRow er = paired ? gemv_epi_load<ESZ, true>(p, r0, r1, pos, tid)
                              : gemv_epi_load<ESZ, false>(p, r0, r1, pos, tid);
-    bool ok = mbar_wait_bounded(vbar, vphase & 1);
-    ++vphase;
+    bool ok = true;
+    if (xlsu) {
+        consumer_bar();                                 // the staged vectors are visible
+    } else {
+        ok = mbar_wait_bounded(vbar, vphase & 1);
+        ++vphase;
+    }
     const uint32_t am = gemv_norm_smem(p, vec, vec + L, vec + 2 * L, red, tid);
     tk_stamp(tr, 1, tid);
     gemv_epi_store(er, r1 - r0, tid, epi);
@@ -682,18 +747,19 @@ __device__ __forceinline__ bool tk_gemv(const GemvParams& p, int unit, int rs, i
     int S = 0;
     if constexpr (ESZ == 1) {
         S = xfix_shift_cta(am, amx);                    // also publishes x, epi[] and the zeroed part[]
+        xfix_smem(vec, L, S, tid);
         tk_stamp(tr, 2, tid);
         int* parti = reinterpret_cast<int*>(part);
         if (paired)
             okc = rs == 4 ? tk_gemv_consume_i8<1, 4, 2>(p, r0, r1, rows, ring, NS, full, empty, j, group, lane, slotid,
-                                                        vec, S, parti)
+                                                        vec, S, parti, tr)
                           : tk_gemv_consume_i8<3, 1, 2>(p, r0, r1, rows, ring, NS, full, empty, j, group, lane, slotid,
-                                                        vec, S, parti);
+                                                        vec, S, parti, tr);
         else
             okc = rs == 8 ? tk_gemv_consume_i8<1, 8, 1>(p, r0, r1, rows, ring, NS, full, empty, j, group, lane, slotid,
-                                                        vec, S, parti)
+                                                        vec, S, parti, tr)
                           : tk_gemv_consume_i8<3, 2, 1>(p, r0, r1, rows, ring, NS, full, empty, j, group, lane, slotid,
-                                                        vec, S, parti);
+                                                        vec, S, parti, tr);
         ok = okc && ok;
         consumer_bar();
         if (tid == 0) *amx = 0u;                        // every thread read it before its stages
@@ -731,12 +797,12 @@ __device__ __forceinline__ bool tk_gemv_dispatch(const TkPhase& T, int pos, cons
                                                  uint64_t* full, uint64_t* empty, int& j, int group, int gwarp,
                                                  int lane, int tid, float* red, float* part, int cta, int ncta,
                                                  unsigned long long* tr, float* vec, uint64_t* vbar,
-                                                 uint32_t& vphase, unsigned* amx) {
+                                                 uint32_t& vphase, unsigned* amx, bool xlsu) {
     if (VS == 1 && T.variant >= TV_F32_K1_R8)
         return tk_gemv<float>(T.g, T.unit, T.rs, T.rows, pos, ring, NS, full, empty, j, group, gwarp, lane, tid, red, part,
-                              cta, ncta, tr, vec, vbar, vphase, amx);
+                              cta, ncta, tr, vec, vbar, vphase, amx, xlsu);
     return tk_gemv<int8_t>(T.g, T.unit, T.rs, T.rows, pos, ring, NS, full, empty, j, group, gwarp, lane, tid, red, part, cta,
-                           ncta, tr, vec, vbar, vphase, amx);
+                           ncta, tr, vec, vbar, vphase, amx, xlsu);
 }
 
 // --------------------------------------------------------------------- the kernel
@@ -883,7 +949,7 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
             }
         } else if (T.kind == TK_GEMV) {
             ok = tk_gemv_dispatch<VS>(T, pos, ring, NS, full, empty, j, group, gwarp, lane, tid, red, part, cta,
-                                      ncta, tr, vec, vbar, vphase, amx);
+                                      ncta, tr, vec, vbar, vphase, amx, P.x_lsu != 0);
         } else {
             tk_stamp(tr, 1, tid);
             tk_stamp(tr, 2, tid);

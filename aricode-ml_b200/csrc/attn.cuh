@@ -30,6 +30,7 @@ struct AttnParams {
     StepState* st;         // nullptr: n = n_fixed
     int n_fixed;
     int* err;
+    Mirror mir;            // token kernel, tensor parallelism: out also written to the peers
 };
 
 // bytes of scratch one call needs

@@ -238,4 +238,48 @@ struct StepState {
     int pad[7];
 };
 
+// ------------------------------------------------------------------ tensor parallelism
+// Up to kMaxRanks GPUs split each matrix by output rows (attention by heads). A
+// phase whose output every rank needs writes each value into its own buffer and,
+// through NVLink peer mappings, into the same offset of every peer's buffer:
+// Mirror holds the byte distance from the local buffer to each peer's copy.
+constexpr int kMaxRanks = 8;
+struct Mirror {
+    long long delta[kMaxRanks - 1];
+    int n;                 // peers (0: single GPU)
+};
+
+template <typename T>
+__device__ __forceinline__ void mirror_store(const Mirror& m, T* p, T v) {
+    *p = v;
+    for (int i = 0; i < m.n; ++i) *reinterpret_cast<T*>(reinterpret_cast<char*>(p) + m.delta[i]) = v;
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Publish epoch e in slot `rank` of the flag array f on every rank (after a
+// system-scope fence: this thread's and its CTA's earlier writes, peer copies
+// included, become visible first), then wait until every rank's slot has
+// reached e (wrap-safe). Bounded: false after ~1 s.
+__device__ __forceinline__ bool tp_flag_exchange(unsigned* f, int rank, int nranks, const Mirror& m, unsigned e) {
+    __threadfence_system();
+    st_release_sys(f + rank, e);
+    for (int i = 0; i < m.n; ++i)
+        st_release_sys(reinterpret_cast<unsigned*>(reinterpret_cast<char*>(f + rank) + m.delta[i]), e);
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 1;; ++it) {
+        bool all = true;
+        for (int r = 0; r < nranks; ++r) all = all && (int)(ld_acquire_sys(f + r) - e) >= 0;
+        if (all) return true;
+        if ((it & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    }
+}
+
 }  // namespace b2

@@ -84,6 +84,18 @@ struct GemvParams {
     StepState* st;
     int pos_fixed;             // position when st == nullptr
     int* err;
+    // tensor parallelism (token kernel): output rows mirrored to the peers; row
+    // ids of the argmax offset by row_base; each rank's best logit exchanged
+    // through tp_cval / tp_cidx / tp_cnan / tp_aflag ([kMaxRanks] each, in the
+    // rank's exchange buffer, mirrored like the outputs)
+    Mirror mir;
+    int row_base;
+    int tp_rank, tp_size;
+    const unsigned* tp_seq;    // token-kernel launches completed (the flags' epochs)
+    float* tp_cval;
+    int* tp_cidx;
+    int* tp_cnan;
+    unsigned* tp_aflag;
 };
 
 // ordering for greedy sampling: non-NaN beats NaN, larger wins, ties -> lower index
@@ -828,7 +840,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, int r0, int r
             const float su = pre(rl) ? epi[rl * 4 + 1] : p.S[1][lrow];
             const float g = fmul(dotv(rl, 0), sg);
             const float u = fmul(dotv(rl, 1), su);
-            p.y[lrow] = fmul(silu_f(g), u);
+            mirror_store(p.mir, p.y + lrow, fmul(silu_f(g), u));
             continue;
         }
         int seg, row;
@@ -865,17 +877,17 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, int r0, int r
                 }
             }
         } else if (p.epi == EPI_RESID) {
-            p.y[row] = fadd(val[0], pre(rl) ? epi[rl * 4 + 2] : __ldcg(p.resid + row));
+            mirror_store(p.mir, p.y + row, fadd(val[0], pre(rl) ? epi[rl * 4 + 2] : __ldcg(p.resid + row)));
         } else if (p.epi == EPI_GELU) {
-            p.y[row] = gelu_f(val[0]);
+            mirror_store(p.mir, p.y + row, gelu_f(val[0]));
         } else if (p.epi == EPI_ARGMAX) {
             if (p.y) p.y[row] = val[0];
-            if (row == 0 && p.amax_v0nan) *p.amax_v0nan = (val[0] != val[0]) ? 1 : 0;
-            if (!have_best || amax_better(val[0], row, best_v, best_i)) {
-                best_v = val[0]; best_i = row; have_best = true;
+            if (row + p.row_base == 0 && p.amax_v0nan) *p.amax_v0nan = (val[0] != val[0]) ? 1 : 0;
+            if (!have_best || amax_better(val[0], row + p.row_base, best_v, best_i)) {
+                best_v = val[0]; best_i = row + p.row_base; have_best = true;
             }
         } else {
-            p.y[row] = val[0];
+            mirror_store(p.mir, p.y + row, val[0]);
         }
     }
 
@@ -916,7 +928,26 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, int r0, int r
                 if (ii != 0x7fffffff && (!ch || amax_better(vv, ii, cv, ci))) { cv = vv; ci = ii; ch = true; }
             }
             int tok = ch ? ci : 0;
-            if (p.amax_v0nan && __ldcg(p.amax_v0nan)) tok = 0;    // sequential scan keeps index 0
+            bool v0nan = p.amax_v0nan && __ldcg(p.amax_v0nan);
+            if (p.tp_size > 1) {
+                // every rank's best, slot tp_rank on every rank, then the flags; the
+                // comparator is a total order, so all ranks reach the same token
+                const int r = p.tp_rank;
+                mirror_store(p.mir, p.tp_cval + r, cv);
+                mirror_store(p.mir, p.tp_cidx + r, ch ? ci : 0x7fffffff);
+                mirror_store(p.mir, p.tp_cnan + r, (r == 0 && v0nan) ? 1 : 0);
+                const unsigned e = *(volatile const unsigned*)p.tp_seq + 1u;
+                if (!tp_flag_exchange(p.tp_aflag, r, p.tp_size, p.mir, e)) set_err(p.err, B2_DEV_ERR_TIMEOUT);
+                ch = false;
+                for (int q = 0; q < p.tp_size; ++q) {
+                    const int ii = *(volatile int*)(p.tp_cidx + q);
+                    const float vv = *(volatile float*)(p.tp_cval + q);
+                    if (ii != 0x7fffffff && (!ch || amax_better(vv, ii, cv, ci))) { cv = vv; ci = ii; ch = true; }
+                }
+                tok = ch ? ci : 0;
+                v0nan = *(volatile int*)(p.tp_cnan) != 0;
+            }
+            if (v0nan) tok = 0;                                    // sequential scan keeps index 0
             if (p.out_tok) *p.out_tok = tok;
             if (p.st) {
                 StepState* st = p.st;

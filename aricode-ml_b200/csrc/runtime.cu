@@ -51,14 +51,16 @@ struct Block {
     NormRef norm;
     // attention
     bool rope = false;
-    int H = 0, KVH = 0, dh = 0;
+    int H = 0, KVH = 0, dh = 0;        // this rank's heads (all of them on one GPU)
+    int head0 = 0, H_all = 0;          // first query head of this rank, heads of the model
     DevMat q, k, v, o;
     const float* bias[4] = {nullptr, nullptr, nullptr, nullptr};
     float* K = nullptr;
     float* V = nullptr;
     // feed-forward
     bool swiglu = false;
-    int d_ffn = 0;
+    int d_ffn = 0;                     // of the model
+    int ffn_local = 0, ffn0 = 0;       // this rank's hidden rows and the first of them
     DevMat w1, w3, w2;
     const float* b1 = nullptr;
     const float* b2 = nullptr;
@@ -171,6 +173,23 @@ struct b2_ctx {
     std::string trace_path;
     std::vector<int> trace_kinds;  // per phase of both tables: kind, or 10 + GEMV variant
     int host_step = 0;
+    unsigned* tk_seq = nullptr;    // token-kernel launches completed (cross-rank epochs)
+    int tk_final_xsync[2] = {0, 0};  // per table (prefill, decode): last phase mirrored
+    // tensor parallelism: rank tp_rank of tp_size GPUs (one process each). The
+    // exchange buffer holds what every rank reads whole (x, attention output,
+    // FFN hidden vector) and the cross-rank flags; peers write into it through
+    // CUDA IPC mappings.
+    int tp_rank = 0, tp_size = 1;
+    bool tp_connected = false;
+    void* d_xch = nullptr;
+    size_t xch_bytes = 0;
+    void* peer_base[kMaxRanks] = {};
+    Mirror mir{};
+    unsigned* tp_flag = nullptr;   // [kMaxRanks] barrier epochs
+    unsigned* tp_aflag = nullptr;  // [kMaxRanks] argmax epochs
+    float* tp_cval = nullptr;      // [kMaxRanks] each rank's best logit
+    int* tp_cidx = nullptr;
+    int* tp_cnan = nullptr;
 
     ~b2_ctx() {
         if (device >= 0) cudaSetDevice(device);
@@ -181,6 +200,9 @@ struct b2_ctx {
         if (d_work) cudaFree(d_work);
         if (d_phases) cudaFree(d_phases);
         if (d_trace) cudaFree(d_trace);
+        for (int r = 0; r < kMaxRanks; ++r)
+            if (peer_base[r]) cudaIpcCloseMemHandle(peer_base[r]);
+        if (d_xch) cudaFree(d_xch);
         if (h_st) cudaFreeHost(h_st);
         if (own_stream && stream) cudaStreamDestroy(stream);
         if (cap_stream) cudaStreamDestroy(cap_stream);
@@ -243,11 +265,25 @@ struct Need {
     int dtype;            // 1 int8 (+ _scales), 2 f32
     long long rows, cols; // cols = 0: 1-D of length rows
     int init;             // synthetic: 0 random, 1 ones, 2 zeros
+    long long row0 = 0;   // tensor parallelism: first row of this rank's share
 };
 
-std::vector<Need> plan_needs(const b2json::Value& plan) {
+// Tensor shapes of a plan; with tp > 1 the row-split tensors (Q/K/V by heads,
+// O, gate, up, down and the LM head by output rows) are this rank's share.
+std::vector<Need> plan_needs(const b2json::Value& plan, int tp = 1, int rank = 0) {
     std::vector<Need> out;
     const long long d = plan["d_model"].as_int("d_model"), vocab = plan["vocab"].as_int("vocab");
+    auto split = [&](Need n) {
+        if (tp > 1) {
+            if (n.rows % tp) throw Err(B2_E_UNSUPPORTED, "tensor '" + n.name + "' rows do not split over the ranks");
+            n.rows /= tp;
+            n.row0 = n.rows * rank;
+        }
+        out.push_back(n);
+    };
+    auto no_tp = [&](const char* what) {
+        if (tp > 1) throw Err(B2_E_UNSUPPORTED, std::string("tensor parallelism does not cover ") + what);
+    };
     auto norm = [&](const b2json::Value& n) {
         out.push_back({n["g"].as_str(), 2, d, 0, 1});
         if (n["kind"].as_str() == "ln") out.push_back({n["b"].as_str(), 2, d, 0, 2});
@@ -263,11 +299,14 @@ std::vector<Need> plan_needs(const b2json::Value& plan) {
             const long long H = b["n_heads"].as_int(), KVH = b["n_kv_heads"].as_int(),
                             dh = b["d_head"].as_int();
             const int dt = b["dtype"].as_str() == "i8" ? 1 : 2;
-            out.push_back({b["q"].as_str(), dt, H * dh, d, 0});
-            out.push_back({b["k"].as_str(), dt, KVH * dh, d, 0});
-            out.push_back({b["v"].as_str(), dt, KVH * dh, d, 0});
-            out.push_back({b["o"].as_str(), dt, d, H * dh, 0});
+            if (tp > 1 && (H % tp || KVH % tp)) throw Err(B2_E_UNSUPPORTED, "heads do not split over the ranks");
+            if (dt != 1) no_tp("f32 attention weights");
+            split({b["q"].as_str(), dt, H * dh, d, 0});
+            split({b["k"].as_str(), dt, KVH * dh, d, 0});
+            split({b["v"].as_str(), dt, KVH * dh, d, 0});
+            split({b["o"].as_str(), dt, d, H * dh, 0});
             if (b.has("bias")) {
+                no_tp("attention biases");
                 const b2json::Value& bs = b["bias"];
                 out.push_back({bs["q"].as_str(), 2, H * dh, 0, 0});
                 out.push_back({bs["k"].as_str(), 2, KVH * dh, 0, 0});
@@ -276,10 +315,11 @@ std::vector<Need> plan_needs(const b2json::Value& plan) {
             }
         } else if (b["kind"].as_str() == "swiglu") {
             const long long ffn = b["d_ffn"].as_int();
-            out.push_back({b["gate"].as_str(), 1, ffn, d, 0});
-            out.push_back({b["up"].as_str(), 1, ffn, d, 0});
-            out.push_back({b["down"].as_str(), 1, d, ffn, 0});
+            split({b["gate"].as_str(), 1, ffn, d, 0});
+            split({b["up"].as_str(), 1, ffn, d, 0});
+            split({b["down"].as_str(), 1, d, ffn, 0});
         } else {
+            no_tp("GELU feed-forward blocks");
             const long long ffn = b["d_ffn"].as_int();
             out.push_back({b["fc1"].as_str(), 1, ffn, d, 0});
             out.push_back({b["fc1_b"].as_str(), 2, ffn, 0, 0});
@@ -288,8 +328,8 @@ std::vector<Need> plan_needs(const b2json::Value& plan) {
         }
     }
     norm(plan["final_norm"]);
-    out.push_back({plan["lm_head"]["W"].as_str(), 1, vocab, d, 0});
-    out.push_back({plan["lm_head"]["b"].as_str(), 2, vocab, 0, 2});
+    split({plan["lm_head"]["W"].as_str(), 1, vocab, d, 0});
+    split({plan["lm_head"]["b"].as_str(), 2, vocab, 0, 2});
     return out;
 }
 
@@ -343,11 +383,17 @@ void assemble(b2_ctx* c, const b2json::Value& plan) {
                 throw Err(B2_E_UNSUPPORTED, "attention needs n_heads % n_kv_heads == 0 and head_dim "
                                             "a multiple of 4 up to 256");
             if (B.rope && (B.dh % 2)) throw Err(B2_E_FORMAT, "RoPE needs an even head_dim");
+            B.H_all = B.H;
+            if (B.H % c->tp_size || B.KVH % c->tp_size || c->d % c->tp_size)
+                throw Err(B2_E_UNSUPPORTED, "heads or d_model do not split over the ranks");
+            B.H /= c->tp_size;                      // this rank's query and KV heads
+            B.KVH /= c->tp_size;
+            B.head0 = c->tp_rank * B.H;
             const int qd = B.H * B.dh, kd = B.KVH * B.dh;
             B.q = c->mat(b["q"].as_str(), qd, c->d);
             B.k = c->mat(b["k"].as_str(), kd, c->d);
             B.v = c->mat(b["v"].as_str(), kd, c->d);
-            B.o = c->mat(b["o"].as_str(), c->d, qd);
+            B.o = c->mat(b["o"].as_str(), c->d / c->tp_size, B.H_all * B.dh);
             if (B.q.i8 != B.k.i8 || B.q.i8 != B.v.i8 || B.q.i8 != B.o.i8)
                 throw Err(B2_E_FORMAT, "attention projections must share one dtype");
             if (b.has("bias")) {
@@ -355,7 +401,7 @@ void assemble(b2_ctx* c, const b2json::Value& plan) {
                 B.bias[0] = c->vec(bs["q"], qd);
                 B.bias[1] = c->vec(bs["k"], kd);
                 B.bias[2] = c->vec(bs["v"], kd);
-                B.bias[3] = c->vec(bs["o"], c->d);
+                B.bias[3] = c->vec(bs["o"], c->d / c->tp_size);
             }
             if (B.rope) {
                 const double th = b["theta"].as_num("theta");
@@ -367,11 +413,14 @@ void assemble(b2_ctx* c, const b2json::Value& plan) {
             kv_total += 2ull * B.KVH * c->max_seq * B.dh;
         } else {
             B.d_ffn = (int)b["d_ffn"].as_int();
+            if (B.d_ffn % c->tp_size) throw Err(B2_E_UNSUPPORTED, "d_ffn does not split over the ranks");
+            B.ffn_local = B.d_ffn / c->tp_size;
+            B.ffn0 = c->tp_rank * B.ffn_local;
             if (b["kind"].as_str() == "swiglu") {
                 B.swiglu = true;
-                B.w1 = c->mat(b["gate"].as_str(), B.d_ffn, c->d);
-                B.w3 = c->mat(b["up"].as_str(), B.d_ffn, c->d);
-                B.w2 = c->mat(b["down"].as_str(), c->d, B.d_ffn);
+                B.w1 = c->mat(b["gate"].as_str(), B.ffn_local, c->d);
+                B.w3 = c->mat(b["up"].as_str(), B.ffn_local, c->d);
+                B.w2 = c->mat(b["down"].as_str(), c->d / c->tp_size, B.d_ffn);
                 if (!B.w1.i8 || !B.w3.i8 || !B.w2.i8)
                     throw Err(B2_E_UNSUPPORTED, "swiglu_ffn weights must be int8 (--quantize int8)");
             } else {
@@ -386,8 +435,9 @@ void assemble(b2_ctx* c, const b2json::Value& plan) {
         c->blocks.push_back(B);
     }
     c->fnorm = c->norm_of(plan["final_norm"]);
-    c->lm = c->mat(plan["lm_head"]["W"].as_str(), c->vocab, c->d);
-    c->lm_b = c->vec(plan["lm_head"]["b"], c->vocab);
+    if (c->vocab % c->tp_size) throw Err(B2_E_UNSUPPORTED, "vocab does not split over the ranks");
+    c->lm = c->mat(plan["lm_head"]["W"].as_str(), c->vocab / c->tp_size, c->d);
+    c->lm_b = c->vec(plan["lm_head"]["b"], c->vocab / c->tp_size);
     if (!c->lm.i8 || !c->emb.i8) throw Err(B2_E_UNSUPPORTED, "embedding and LM head must be int8");
 
     // ---- KV cache arena
@@ -406,10 +456,11 @@ void assemble(b2_ctx* c, const b2json::Value& plan) {
     }
 
     // ---- activations + scratch arena
-    int max_q = 1, max_ffn = 1, max_H = 1, max_KVH = 1, max_dh = 1;
+    int max_q = 1, max_q_all = 1, max_ffn = 1, max_H = 1, max_KVH = 1, max_dh = 1;
     for (const Block& B : c->blocks) {
         if (B.attn) {
             max_q = std::max(max_q, B.H * B.dh);
+            max_q_all = std::max(max_q_all, B.H_all * B.dh);
             max_H = std::max(max_H, B.H);
             max_KVH = std::max(max_KVH, B.KVH);
             max_dh = std::max(max_dh, B.dh);
@@ -424,10 +475,8 @@ void assemble(b2_ctx* c, const b2json::Value& plan) {
     std::vector<size_t> offs;
     auto add = [&](size_t bytes) { offs.push_back(off); off += al(bytes); return offs.size() - 1; };
     const size_t i_rope = add(c->rope_dh ? (size_t)c->max_seq * c->rope_dh * 4 : 16);
-    const size_t i_x = add((size_t)c->d * 4);
     const size_t i_q = add((size_t)max_q * 4);
-    const size_t i_att = add((size_t)max_q * 4);
-    const size_t i_f = add((size_t)max_ffn * 4);
+    const size_t i_seq = add(4);
     const size_t i_logits = add((size_t)c->vocab * 4);
     const size_t i_part = add((size_t)max_H * c->attn_nsplit_max * (max_dh + 2) * 4);
     const size_t i_acnt = add((size_t)std::max(max_H, max_KVH) * 4);   // per query head (token kernel)
@@ -444,10 +493,29 @@ void assemble(b2_ctx* c, const b2json::Value& plan) {
     CK(cudaMemsetAsync(c->d_work, 0, c->work_bytes, c->stream));
     char* w = static_cast<char*>(c->d_work);
     c->rope_tab = reinterpret_cast<float*>(w + offs[i_rope]);
-    c->x = reinterpret_cast<float*>(w + offs[i_x]);
     c->q = reinterpret_cast<float*>(w + offs[i_q]);
-    c->att = reinterpret_cast<float*>(w + offs[i_att]);
-    c->f = reinterpret_cast<float*>(w + offs[i_f]);
+    c->tk_seq = reinterpret_cast<unsigned*>(w + offs[i_seq]);
+    // exchange buffer: x, attention output, FFN hidden vector (whole, on every
+    // rank), then the cross-rank flags and argmax candidates
+    {
+        size_t xo = 0;
+        auto xadd = [&](size_t bytes) { const size_t o = xo; xo += al(bytes); return o; };
+        const size_t o_x = xadd((size_t)c->d * 4), o_att = xadd((size_t)max_q_all * 4),
+                     o_f = xadd((size_t)max_ffn * 4), o_fl = xadd(kMaxRanks * 4), o_afl = xadd(kMaxRanks * 4),
+                     o_cv = xadd(kMaxRanks * 4), o_ci = xadd(kMaxRanks * 4), o_cn = xadd(kMaxRanks * 4);
+        c->xch_bytes = xo;
+        if (cudaMalloc(&c->d_xch, c->xch_bytes) != cudaSuccess) throw Err(B2_E_OOM, "exchange buffer allocation failed");
+        CK(cudaMemsetAsync(c->d_xch, 0, c->xch_bytes, c->stream));
+        char* xb = static_cast<char*>(c->d_xch);
+        c->x = reinterpret_cast<float*>(xb + o_x);
+        c->att = reinterpret_cast<float*>(xb + o_att);
+        c->f = reinterpret_cast<float*>(xb + o_f);
+        c->tp_flag = reinterpret_cast<unsigned*>(xb + o_fl);
+        c->tp_aflag = reinterpret_cast<unsigned*>(xb + o_afl);
+        c->tp_cval = reinterpret_cast<float*>(xb + o_cv);
+        c->tp_cidx = reinterpret_cast<int*>(xb + o_ci);
+        c->tp_cnan = reinterpret_cast<int*>(xb + o_cn);
+    }
     c->logits = reinterpret_cast<float*>(w + offs[i_logits]);
     c->attn_part = reinterpret_cast<float*>(w + offs[i_part]);
     c->attn_cnt = reinterpret_cast<unsigned*>(w + offs[i_acnt]);
@@ -487,6 +555,7 @@ void assemble(b2_ctx* c, const b2json::Value& plan) {
 struct Op {
     int kind = TK_GEMV;
     bool i8 = true;
+    bool mirror = false;      // its output is written to every rank (tensor parallelism)
     GemvParams g{};
     AttnParams a{};
     EmbedParams e{};
@@ -494,7 +563,13 @@ struct Op {
 
 std::vector<Op> build_ops(b2_ctx* c, bool with_head) {
     std::vector<Op> ops;
-    auto gemv = [&](const GemvParams& g, bool i8) { Op o; o.kind = TK_GEMV; o.g = g; o.i8 = i8; ops.push_back(o); };
+    const bool tp = c->tp_size > 1;
+    auto gemv = [&](const GemvParams& g, bool i8, bool mirror = false) {
+        Op o; o.kind = TK_GEMV; o.g = g; o.i8 = i8; o.mirror = tp && mirror;
+        if (o.mirror) o.g.mir = c->mir;
+        ops.push_back(o);
+    };
+    const int d_local = c->d / c->tp_size, d0 = c->tp_rank * d_local;   // this rank's rows of x
     EmbedParams ep{};
     ep.emb = c->emb.w; ep.emb_i8 = c->emb.i8; ep.emb_s = c->emb.s; ep.ld = c->emb.ld;
     ep.pos_tab = c->pos_tab; ep.max_pos = c->max_pos;
@@ -530,35 +605,36 @@ std::vector<Op> build_ops(b2_ctx* c, bool with_head) {
             gemv(p, B.q.i8);
 
             AttnParams a{};
-            a.q = c->q; a.K = B.K; a.V = B.V; a.out = c->att;
+            a.q = c->q; a.K = B.K; a.V = B.V; a.out = c->att + (size_t)B.head0 * B.dh;
             a.part = c->attn_part; a.counters = c->attn_cnt;
             a.H = B.H; a.KVH = B.KVH; a.dh = B.dh; a.max_seq = c->max_seq;
             a.nsplit_max = c->attn_nsplit_max;
             a.st = c->st; a.err = &c->st->err;
-            { Op op; op.kind = TK_ATTN; op.a = a; ops.push_back(op); }
+            if (tp) a.mir = c->mir;
+            { Op op; op.kind = TK_ATTN; op.a = a; op.mirror = tp; ops.push_back(op); }
 
             GemvParams o{};
             o.st = c->st; o.err = &c->st->err;
             o.W[0] = B.o.w; o.S[0] = B.o.s; o.bias[0] = B.bias[3];
             o.rows[0] = B.o.rows; o.nseg = 1; o.ld = B.o.ld;
             o.x = c->att; o.n = B.o.cols; o.norm = NORM_NONE;
-            o.epi = EPI_RESID; o.y = c->x; o.resid = c->x;
-            gemv(o, B.o.i8);
+            o.epi = EPI_RESID; o.y = c->x + d0; o.resid = c->x + d0;
+            gemv(o, B.o.i8, true);
         } else if (B.swiglu) {
             p.W[0] = B.w1.w; p.W[1] = B.w3.w;
             p.S[0] = B.w1.s; p.S[1] = B.w3.s;
-            p.rows[0] = B.d_ffn; p.rows[1] = B.d_ffn;
+            p.rows[0] = B.ffn_local; p.rows[1] = B.ffn_local;
             p.nseg = 2; p.paired = 1; p.ld = B.w1.ld;
-            p.epi = EPI_SWIGLU; p.y = c->f;
-            gemv(p, true);
+            p.epi = EPI_SWIGLU; p.y = c->f + B.ffn0;
+            gemv(p, true, true);
 
             GemvParams dn{};
             dn.st = c->st; dn.err = &c->st->err;
             dn.W[0] = B.w2.w; dn.S[0] = B.w2.s;
-            dn.rows[0] = c->d; dn.nseg = 1; dn.ld = B.w2.ld;
+            dn.rows[0] = d_local; dn.nseg = 1; dn.ld = B.w2.ld;
             dn.x = c->f; dn.n = B.d_ffn; dn.norm = NORM_NONE;
-            dn.epi = EPI_RESID; dn.y = c->x; dn.resid = c->x;
-            gemv(dn, true);
+            dn.epi = EPI_RESID; dn.y = c->x + d0; dn.resid = c->x + d0;
+            gemv(dn, true, true);
         } else {
             p.W[0] = B.w1.w; p.S[0] = B.w1.s; p.bias[0] = B.b1;
             p.rows[0] = B.d_ffn; p.nseg = 1; p.ld = B.w1.ld;
@@ -578,10 +654,16 @@ std::vector<Op> build_ops(b2_ctx* c, bool with_head) {
         GemvParams h{};
         h.st = c->st; h.err = &c->st->err;
         h.W[0] = c->lm.w; h.S[0] = c->lm.s; h.bias[0] = c->lm_b;
-        h.rows[0] = c->vocab; h.nseg = 1; h.ld = c->lm.ld;
+        h.rows[0] = c->lm.rows; h.nseg = 1; h.ld = c->lm.ld;
         h.x = c->x; h.n = c->d;
         h.norm = c->fnorm.kind; h.ng = c->fnorm.g; h.nb = c->fnorm.b; h.eps = c->eps;
-        h.epi = EPI_ARGMAX; h.y = c->logits;
+        h.row_base = c->tp_rank * c->lm.rows;
+        h.epi = EPI_ARGMAX; h.y = c->logits + h.row_base;
+        if (tp) {
+            h.mir = c->mir;
+            h.tp_rank = c->tp_rank; h.tp_size = c->tp_size; h.tp_seq = c->tk_seq;
+            h.tp_cval = c->tp_cval; h.tp_cidx = c->tp_cidx; h.tp_cnan = c->tp_cnan; h.tp_aflag = c->tp_aflag;
+        }
         h.amax_val = c->amax_val; h.amax_idx = c->amax_idx; h.amax_v0nan = c->amax_v0nan;
         h.amax_count = c->amax_cnt; h.out_ids = c->out_ids;
         gemv(h, true);
@@ -677,14 +759,22 @@ void setup_token(b2_ctx* c) {
     std::string why;
     bool f32 = false;
     for (int head = 0; head < 2; ++head) {
+        bool prev_mirror = false;
         for (const Op& o : build_ops(c, head == 1)) {
             TkPhase T;
             if (!tk_phase_of(c, o, T, part, vec_floats, why)) { c->token_why = why; return; }
             if (T.kind == TK_GEMV && T.variant >= TV_F32_K1_R8) f32 = true;
+            T.xsync = prev_mirror ? 1 : 0;              // the outputs it reads came from every rank
+            prev_mirror = o.mirror;
             ph.push_back(T);
         }
+        c->tk_final_xsync[head] = prev_mirror ? 1 : 0;
         if (head == 0) c->nph_prefill = (int)ph.size();
         else c->nph_decode = (int)ph.size() - c->nph_prefill;
+    }
+    if (c->tp_size > 1 && std::max(c->nph_prefill, c->nph_decode) >= 1024) {
+        c->token_why = "more than 1023 phases (cross-rank epochs)";
+        return;
     }
     const size_t vec_off = (kTkPartOffset + part + 127) & ~(size_t)127;
     const size_t ring_off = (vec_off + vec_floats * 4 + 127) & ~(size_t)127;
@@ -747,6 +837,12 @@ void launch_token(b2_ctx* c, bool with_head, cudaStream_t s) {
     P.x_lsu = c->tk_x_lsu;
     P.vec_offset = c->tk_vec_offset;
     P.vec_floats = c->tk_vec_floats;
+    P.seq = c->tk_seq;
+    P.tp_rank = c->tp_rank;
+    P.tp_size = c->tp_size;
+    P.tp_flag = c->tp_flag;
+    P.mir = c->mir;
+    P.final_xsync = with_head ? c->tk_final_xsync[1] : c->tk_final_xsync[0];
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)c->sm_count);
     cfg.blockDim = dim3(kTkThreads);
@@ -767,11 +863,14 @@ void capture_graphs(b2_ctx* c) {
     const char* env = std::getenv("B2_NO_PDL");
     c->pdl = !(env && env[0] == '1');
     setup_token(c);
+    if (c->tp_size > 1 && !c->token)
+        throw Err(B2_E_UNSUPPORTED, "tensor parallelism needs the token kernel: " + c->token_why);
     if (c->token) {
         try {
             capture_graphs_once(c);
             return;
         } catch (const Err& e) {
+            if (c->tp_size > 1) throw;
             cudaGetLastError();
             c->token = false;
             c->token_why = std::string("graph capture failed: ") + e.what();
@@ -934,7 +1033,7 @@ void load_blob(b2_ctx* c, const char* path, std::string* embedded_plan) {
 }
 
 void synth_weights(b2_ctx* c, const b2json::Value& plan, uint64_t seed, float stdv) {
-    std::vector<Need> needs = plan_needs(plan);
+    std::vector<Need> needs = plan_needs(plan, c->tp_size, c->tp_rank);
     size_t off = 0;
     auto al = [](size_t n) { return (n + 255) & ~(size_t)255; };
     for (const Need& nd : needs) {
@@ -968,9 +1067,10 @@ void synth_weights(b2_ctx* c, const b2json::Value& plan, uint64_t seed, float st
             const TensorInfo& s = c->tensors[nd.name + "_scales"];
             const long long rows = t.rows;
             synth_quant_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, c->stream>>>(
-                seed, tid, t.cols, stdv, 0, rows, 0, t.cols, reinterpret_cast<int8_t*>(base + t.off), t.ld,
-                reinterpret_cast<float*>(base + s.off));
+                seed, tid, t.cols, stdv, nd.row0, nd.row0 + rows, 0, t.cols, reinterpret_cast<int8_t*>(base + t.off),
+                t.ld, reinterpret_cast<float*>(base + s.off));
         } else if (nd.init == 0) {
+            if (nd.row0) throw Err(B2_E_UNSUPPORTED, "random f32 tensors are not split");
             const long long tot = t.rows * t.ld;
             synth_fill_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, c->stream>>>(
                 seed, tid, t.rows, t.cols, t.ld, stdv, reinterpret_cast<float*>(base + t.off));
@@ -1004,16 +1104,22 @@ int guarded(b2_ctx* c, F&& f) {
     }
 }
 
-int create_common(b2_ctx** out, int device, const std::function<void(b2_ctx*)>& body) {
+int create_common(b2_ctx** out, int device, const std::function<void(b2_ctx*)>& body, int tp_rank = 0,
+                  int tp_size = 1) {
     if (!out) return B2_E_INVALID;
     *out = nullptr;
+    if (tp_size < 1 || tp_size > kMaxRanks || tp_rank < 0 || tp_rank >= tp_size) return B2_E_INVALID;
     auto c = std::make_unique<b2_ctx>();
     c->device = -1;
+    c->tp_rank = tp_rank;
+    c->tp_size = tp_size;
     try {
         setup_device(c.get(), device);
         body(c.get());
-        capture_graphs(c.get());
-        upload_state(c.get(), 0, 0, 0, 0, -1);
+        if (tp_size == 1) {                             // with ranks: after b2_tp_connect
+            capture_graphs(c.get());
+            upload_state(c.get(), 0, 0, 0, 0, -1);
+        }
         CK(cudaStreamSynchronize(c->stream));
     } catch (const Err& e) {
         g_last_create_error = e.what();
@@ -1073,6 +1179,49 @@ int b2_create_synthetic(const char* plan_json, uint64_t seed, float stdv, int de
     });
 }
 
+int b2_create_synthetic_tp(const char* plan_json, uint64_t seed, float stdv, int device, int tp_rank,
+                           int tp_size, b2_ctx** out) {
+    if (!plan_json) return B2_E_INVALID;
+    return create_common(out, device, [&](b2_ctx* c) {
+        const b2json::Value plan = b2json::parse(plan_json);
+        synth_weights(c, plan, seed, stdv);
+        assemble(c, plan);
+    }, tp_rank, tp_size);
+}
+
+int b2_tp_handle(b2_ctx* ctx, void* handle, int len) {
+    return guarded(ctx, [&] {
+        if (!handle || len < (int)sizeof(cudaIpcMemHandle_t)) return B2_E_INVALID;
+        cudaIpcMemHandle_t h;
+        CK(cudaIpcGetMemHandle(&h, ctx->d_xch));
+        std::memcpy(handle, &h, sizeof(h));
+        return B2_OK;
+    });
+}
+
+int b2_tp_connect(b2_ctx* ctx, const void* handles, int len) {
+    return guarded(ctx, [&] {
+        const int N = ctx->tp_size;
+        if (N < 2 || ctx->tp_connected || !handles || len != N * (int)sizeof(cudaIpcMemHandle_t))
+            return B2_E_INVALID;
+        const char* hp = static_cast<const char*>(handles);
+        Mirror m{};
+        for (int r = 0; r < N; ++r) {
+            if (r == ctx->tp_rank) continue;
+            cudaIpcMemHandle_t h;
+            std::memcpy(&h, hp + (size_t)r * sizeof(h), sizeof(h));
+            CK(cudaIpcOpenMemHandle(&ctx->peer_base[r], h, cudaIpcMemLazyEnablePeerAccess));
+            m.delta[m.n++] = static_cast<char*>(ctx->peer_base[r]) - static_cast<char*>(ctx->d_xch);
+        }
+        ctx->mir = m;
+        capture_graphs(ctx);
+        upload_state(ctx, 0, 0, 0, 0, -1);
+        CK(cudaStreamSynchronize(ctx->stream));
+        ctx->tp_connected = true;
+        return B2_OK;
+    });
+}
+
 int b2_destroy(b2_ctx* ctx) {
     if (!ctx) return B2_E_INVALID;
     cudaSetDevice(ctx->device);
@@ -1093,6 +1242,7 @@ int b2_reset(b2_ctx* ctx) {
 
 int b2_step(b2_ctx* ctx, const int32_t* tok, int n_seq, int32_t* next_tok, float* logits) {
     return guarded(ctx, [&] {
+        if (!ctx->g_decode) throw Err(B2_E_INVALID, "ranks not connected (b2_tp_connect)");
         if (!tok || n_seq != 1) return n_seq == 1 ? B2_E_INVALID : B2_E_UNSUPPORTED;
         if (ctx->host_step >= ctx->max_seq) throw Err(B2_E_KV_OVERFLOW, "position reached max_seq");
         if (tok[0] < 0 || tok[0] >= ctx->vocab) throw Err(B2_E_INVALID, "token id outside the vocabulary");
@@ -1110,6 +1260,7 @@ int b2_step(b2_ctx* ctx, const int32_t* tok, int n_seq, int32_t* next_tok, float
 
 int b2_prefill(b2_ctx* ctx, const int32_t* toks, int n) {
     return guarded(ctx, [&] {
+        if (!ctx->g_decode) throw Err(B2_E_INVALID, "ranks not connected (b2_tp_connect)");
         if (n < 0 || (n > 0 && !toks)) return B2_E_INVALID;
         if (ctx->host_step + n > ctx->max_seq) throw Err(B2_E_KV_OVERFLOW, "prefill passes max_seq");
         for (int i = 0; i < n; ++i)
@@ -1126,6 +1277,7 @@ int b2_prefill(b2_ctx* ctx, const int32_t* toks, int n) {
 int b2_generate(b2_ctx* ctx, const int32_t* prompt, int n_prompt, int max_new, int32_t eos,
                 int32_t* out_ids, int* n_out) {
     return guarded(ctx, [&] {
+        if (!ctx->g_decode) throw Err(B2_E_INVALID, "ranks not connected (b2_tp_connect)");
         if (n_out) *n_out = 0;
         if (!prompt || n_prompt <= 0 || max_new < 0 || (max_new > 0 && !out_ids)) return B2_E_INVALID;
         if (max_new == 0) return B2_OK;
@@ -1148,6 +1300,7 @@ int b2_generate(b2_ctx* ctx, const int32_t* prompt, int n_prompt, int max_new, i
 
 int b2_set_position(b2_ctx* ctx, int pos, int32_t next_tok) {
     return guarded(ctx, [&] {
+        if (!ctx->g_decode) throw Err(B2_E_INVALID, "ranks not connected (b2_tp_connect)");
         if (pos < 0 || pos > ctx->max_seq || next_tok < 0 || next_tok >= ctx->vocab) return B2_E_INVALID;
         // enqueued on the stream (no host synchronisation): one tiny kernel
         clear_tickets(ctx, ctx->stream);
@@ -1160,6 +1313,7 @@ int b2_set_position(b2_ctx* ctx, int pos, int32_t next_tok) {
 
 int b2_decode_async(b2_ctx* ctx, int n_steps) {
     return guarded(ctx, [&] {
+        if (!ctx->g_decode) throw Err(B2_E_INVALID, "ranks not connected (b2_tp_connect)");
         if (n_steps < 0) return B2_E_INVALID;
         if (ctx->host_step + n_steps > ctx->max_seq) throw Err(B2_E_KV_OVERFLOW, "decode passes max_seq");
         for (int i = 0; i < n_steps; ++i) CK(cudaGraphLaunch(ctx->g_decode, ctx->stream));

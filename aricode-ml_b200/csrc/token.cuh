@@ -90,6 +90,7 @@ struct alignas(16) TkPhase {
     int unit;           // rows per balancing unit (2 keeps RoPE pairs in one CTA)
     int rs;             // rows per stage the variant is compiled for (paired: second matrix offset)
     int rows;           // rows per stage used (<= rs; chosen so the two groups get equal stage counts)
+    int xsync;          // tensor parallelism: the barrier before this phase also waits for every rank
     GemvParams g;
     AttnParams a;
     EmbedParams e;
@@ -137,6 +138,15 @@ struct TkParams {
     int vec_floats;     // its capacity
     int l2_ahead;       // stages brought into L2 ahead of their bulk copy (0: off)
     int x_lsu;          // 1: stage a phase's x and gains with plain loads instead of a bulk copy
+    // tensor parallelism: this GPU's rank of tp_size; tp_flag[kMaxRanks] barrier
+    // epochs in the exchange buffer (slot r written by rank r), mir: its peer copies
+    int tp_rank, tp_size;
+    unsigned* tp_flag;
+    Mirror mir;
+    unsigned* seq;      // launches completed on this GPU (kept apart from the step state, which
+                        // the host rewrites; every rank launches in lockstep, so epochs agree)
+    int final_xsync;    // the last phase's outputs went to every rank: a closing cross-rank
+                        // barrier, so that no peer still writes them when the next launch starts
     // optional timeline (nullptr: off): [phase][cta][kTkStamps] global-timer stamps
     // at the phase start (after the grid barrier), when x is loaded, after the
     // prologue, after the stages and after the epilogue
@@ -185,18 +195,41 @@ __device__ __forceinline__ uint64_t* tk_issue_wait(uint64_t* full, uint64_t* emp
 // false after ~1 s, and at once when this CTA has already failed (*abort set).
 // The result is the same for every consumer thread of the CTA; `flag` alternates
 // between two slots (phase parity), so one barrier publishes it.
+//
+// With tensor parallelism (xsync), the previous phase's outputs were also written
+// into the peers' buffers: every CTA fences at system scope before it arrives, and
+// once the local barrier is complete CTA 0 publishes epoch `e` to every rank;
+// every CTA then waits for all ranks' epochs (tp_flag_exchange, bounded).
+// xs: the cross-rank request, e.g. the next phase's xsync (read after the first
+// consumer barrier, which publishes the descriptor copy other warps made).
 __device__ __forceinline__ bool tk_grid_sync(unsigned* ctr, unsigned target, int tid, volatile int* flag,
-                                             volatile int* abort) {
+                                             volatile int* abort, const int* xs = nullptr,
+                                             const TkParams* P = nullptr, unsigned e = 0, int cta = 0) {
     consumer_bar();
     if (tid == 0) {
+        const bool xsync = xs && *xs && P && P->tp_size > 1;
         bool ok = *abort == 0;
         if (ok) {
+            if (xsync) __threadfence_system();
             asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
             if (ld_acquire_gpu(ctr) < target) {
                 const uint64_t t0 = globaltimer_ns();
                 for (uint32_t it = 1;; ++it) {
                     if (ld_acquire_gpu(ctr) >= target) break;
                     if ((it & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) { ok = false; break; }
+                }
+            }
+            if (ok && xsync) {
+                if (cta == 0) {
+                    ok = tp_flag_exchange(P->tp_flag, P->tp_rank, P->tp_size, P->mir, e);
+                } else {
+                    const uint64_t t0 = globaltimer_ns();
+                    for (uint32_t it = 1;; ++it) {
+                        bool all = true;
+                        for (int r = 0; r < P->tp_size; ++r) all = all && (int)(ld_acquire_sys(P->tp_flag + r) - e) >= 0;
+                        if (all) break;
+                        if ((it & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) { ok = false; break; }
+                    }
                 }
             }
         }
@@ -514,7 +547,7 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
                     }
                 }
                 if (n < a.max_seq) l = ffma((float)(a.max_seq - n), exp_f(fsub(-60.0f, M)), l);
-                a.out[(size_t)h * dh + gt] = fdiv(o, l);
+                mirror_store(a.mir, a.out + (size_t)h * dh + gt, fdiv(o, l));
             }
             if (gt == 0) a.counters[h] = 0u;
             group_bar(group);                           // scratch reused by the next item
@@ -553,7 +586,7 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
                 for (int u = 0; u < 8; ++u)
                     if (t0 + u < nsplit) o = ffma(pv[u], wsm[t0 + u], o);
             }
-            a.out[(size_t)h * dh + gt] = fdiv(o, ml[3]);
+            mirror_store(a.mir, a.out + (size_t)h * dh + gt, fdiv(o, ml[3]));
         }
         group_bar(group);                               // scratch reused by the next item
     }
@@ -832,6 +865,7 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
     const int active = *(volatile int*)&st->active;
     if (!active) return;
     const int pos = *(volatile int*)&st->step;
+    const unsigned seq = *(volatile unsigned*)P.seq;
     int bad = 0, tok = 0;
     if (pos >= P.max_seq || (P.max_pos > 0 && pos >= P.max_pos)) {
         bad = B2_DEV_ERR_KV_OVERFLOW;
@@ -920,7 +954,8 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
         const TkPhase& T = cdesc[ph & 1];
         if (ph > 0) {
             arrivals += (unsigned)ncta;
-            if (!tk_grid_sync(P.bar, arrivals, tid, flag + 4 * (ph & 1), abort)) {
+            if (!tk_grid_sync(P.bar, arrivals, tid, flag + 4 * (ph & 1), abort, &T.xsync, &P,
+                              seq * 1024u + (unsigned)ph, cta)) {
                 if (tid == 0) *abort = 1;
                 break;
             }
@@ -965,6 +1000,16 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
         }
         if (!ok) *abort = 1;
     }
+    if (P.final_xsync && P.tp_size > 1) {
+        consumer_bar();
+        if (!*abort) {
+            arrivals += (unsigned)ncta;
+            const int one = 1;
+            if (!tk_grid_sync(P.bar, arrivals, tid, flag + 4 * (P.nphases & 1), abort, &one, &P,
+                              seq * 1024u + (unsigned)P.nphases, cta) && tid == 0)
+                *abort = 1;
+        }
+    }
     consumer_bar();
     if (tid == 0) {
         if (*abort) set_err(err, B2_DEV_ERR_TIMEOUT);
@@ -975,6 +1020,7 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
                 st->pos = pos;
                 st->step = pos + 1;
             }
+            *P.seq = seq + 1u;
             P.bar[0] = 0u;
             P.bar[1] = 0u;
             __threadfence();

@@ -54,6 +54,10 @@ def lib():
 def _declare(L):
     L.b2_create.argtypes = [C.c_char_p, C.c_char_p, C.c_int, C.POINTER(vp)]
     L.b2_create_synthetic.argtypes = [C.c_char_p, C.c_uint64, C.c_float, C.c_int, C.POINTER(vp)]
+    L.b2_create_synthetic_tp.argtypes = [C.c_char_p, C.c_uint64, C.c_float, C.c_int, C.c_int, C.c_int,
+                                         C.POINTER(vp)]
+    L.b2_tp_handle.argtypes = [vp, C.c_void_p, C.c_int]
+    L.b2_tp_connect.argtypes = [vp, C.c_void_p, C.c_int]
     L.b2_destroy.argtypes = [vp]
     L.b2_reset.argtypes = [vp]
     L.b2_step.argtypes = [vp, i32p, C.c_int, i32p, f32p]
@@ -133,6 +137,27 @@ class Decoder:
         check(lib().b2_create_synthetic(json.dumps(plan).encode(), int(seed), float(stdv),
                                         int(device), C.byref(ctx)))
         return cls(_ctx=ctx)
+
+    @classmethod
+    def synthetic_tp(cls, plan, rank, size, exchange, seed=0, stdv=0.02, device=0):
+        """Rank `rank` of a tensor-parallel decoder over `size` GPUs (one process
+        per GPU). `exchange(handle_bytes) -> list of every rank's bytes, in rank
+        order` moves the 64-byte buffer handles between the processes (for example
+        torch.distributed.all_gather_object). Every rank must then call the same
+        methods in the same order."""
+        ctx = vp()
+        check(lib().b2_create_synthetic_tp(json.dumps(plan).encode(), int(seed), float(stdv), int(device),
+                                           int(rank), int(size), C.byref(ctx)))
+        dec = cls(_ctx=ctx)
+        if size > 1:
+            h = C.create_string_buffer(64)
+            dec._ck(lib().b2_tp_handle(ctx, h, 64))
+            handles = exchange(h.raw)
+            if len(handles) != size or any(len(b) != 64 for b in handles):
+                raise ValueError("exchange must return one 64-byte handle per rank")
+            allh = C.create_string_buffer(b"".join(handles), 64 * size)
+            dec._ck(lib().b2_tp_connect(ctx, allh, 64 * size))
+        return dec
 
     def close(self):
         if self._ctx:

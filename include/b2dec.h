@@ -56,6 +56,25 @@ int b2_create(const char* blob_path, const char* plan_json, int device, b2_ctx**
 int b2_create_synthetic(const char* plan_json, uint64_t seed, float stdv, int device,
                         b2_ctx** out);
 
+/* Tensor parallelism over tp_size GPUs, one process (and context) per GPU: rank
+ * tp_rank holds its share of every matrix (Q/K/V by heads, O, gate, up, down and
+ * the LM head by output rows) and computes exactly those rows of the one-GPU
+ * step, so tokens and logits are bit-identical to one GPU. The step runs as one
+ * token-kernel launch per rank; outputs every rank needs are written into the
+ * peers' buffers over NVLink and the phase barriers span the ranks.
+ * Set-up: b2_create_synthetic_tp on every rank, b2_tp_handle (64 bytes per rank),
+ * exchange the handles between the processes, b2_tp_connect with all of them in
+ * rank order. Every rank must then make the same calls in the same order (steps,
+ * prefill, generate, decode). A rank that stops makes the others' waits time out
+ * (B2_E_DEVICE after about 1 s); the contexts must then be recreated. Logits
+ * returned by b2_step hold only this rank's vocabulary rows.
+ * Replaces: the plan's b2_create(blob, plan, device, tp_rank, tp_size, nccl_id);
+ * the reference itself runs on one CPU thread and has no counterpart. */
+int b2_create_synthetic_tp(const char* plan_json, uint64_t seed, float stdv, int device, int tp_rank,
+                           int tp_size, b2_ctx** out);
+int b2_tp_handle(b2_ctx* ctx, void* handle, int len);
+int b2_tp_connect(b2_ctx* ctx, const void* handles, int len);
+
 int b2_destroy(b2_ctx* ctx);
 
 /* Forget the sequence: position 0, no generated ids (KV contents need no zeroing:

@@ -118,6 +118,20 @@ def _i32(seq):
     return arr
 
 
+def tp_gather_handles(handle, rank, size, exchange):
+    """Every rank's 64-byte exchange-buffer handle, concatenated in rank order (the
+    b2_tp_connect argument). `exchange(handle)` returns the list of all ranks'
+    handles in rank order; this rank's own must come back in its slot."""
+    if len(handle) != 64:
+        raise ValueError("a handle is 64 bytes")
+    handles = list(exchange(bytes(handle)))
+    if len(handles) != size or any(len(b) != 64 for b in handles):
+        raise ValueError("exchange must return one 64-byte handle per rank")
+    if handles[rank] != bytes(handle):
+        raise ValueError("exchange returned the handles out of rank order")
+    return b"".join(handles)
+
+
 class Decoder:
     """One model on one GPU. ``Decoder(blob_path)`` or ``Decoder.synthetic(plan, seed)``."""
 
@@ -152,10 +166,8 @@ class Decoder:
         if size > 1:
             h = C.create_string_buffer(64)
             dec._ck(lib().b2_tp_handle(ctx, h, 64))
-            handles = exchange(h.raw)
-            if len(handles) != size or any(len(b) != 64 for b in handles):
-                raise ValueError("exchange must return one 64-byte handle per rank")
-            allh = C.create_string_buffer(b"".join(handles), 64 * size)
+            joined = tp_gather_handles(h.raw, rank, size, exchange)
+            allh = C.create_string_buffer(joined, 64 * size)
             dec._ck(lib().b2_tp_connect(ctx, allh, 64 * size))
         return dec
 

@@ -6,8 +6,10 @@
 One step = decoding the 256 new tokens after the 512-token prompt (positions
 512..767) with every input already in HBM; the KV cache of the prompt is filled
 once before timing and every step rewinds to position 512, so all steps do the
-same work. value = generated tokens per second over all GPUs (N independent
-replicas when N > 1). e2e = the same metric through the public C ABI call
+same work. value = generated tokens per second of that one sequence; with N > 1
+GPUs (one process each, torchrun) the model is split over them (tensor
+parallelism: every matrix by output rows, attention by heads), so N GPUs decode
+the same batch-1 sequence faster (strong scaling). e2e = the same metric through the public C ABI call
 b2_generate (prompt from pinned host memory, prefill + decode, ids back to
 pinned host memory). The roofline object is the dominant kernel, the token
 kernel that runs one whole decode step per launch: algorithmic bytes per token
@@ -153,7 +155,7 @@ def run_reference(args):
     line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tokens/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1000.0 * 256 / cb["value"], "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8 x f32", "data": "synthetic",
             "config": workload_config(args, plan),
             "cpu_baseline": cb,
             "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
@@ -168,7 +170,7 @@ def workload_config(args, plan):
                         f"{c['new']} greedy tokens, batch 1",
             "layers": plan["n_layers"], "d_model": plan["d_model"], "vocab": plan["vocab"],
             "prompt_tokens": c["prompt"], "decode_tokens": c["new"], "batch": 1,
-            "parallelism": "replicas" if args.gpus > 1 else "single",
+            "parallelism": f"tp{args.gpus}" if args.gpus > 1 else "single",
             "l2": "weights (6.6 GB) exceed L2 (126 MB); no flush needed"}
 
 
@@ -195,7 +197,14 @@ def main():
     plan = pkg.synth.config_plan(args.config, n_layers=args.layers)
     P, NEW = c["prompt"], c["new"]
 
-    dec = rt.Decoder.synthetic(plan, seed=0, device=local_rank)
+    if world > 1:
+        def exchange(handle):
+            got = [None] * world
+            dist.all_gather_object(got, handle)
+            return got
+        dec = rt.Decoder.synthetic_tp(plan, rank, world, exchange, seed=0, device=local_rank)
+    else:
+        dec = rt.Decoder.synthetic(plan, seed=0, device=local_rank)
     stream = torch.cuda.Stream()
     torch.cuda.set_stream(stream)
     dec.set_stream(stream.cuda_stream)
@@ -238,13 +247,13 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     toks = NEW - 1
-    value = world * toks / (ms / 1000.0)
+    value = toks / (ms / 1000.0)
     kps = int(dec.query("kernels_per_step"))
     launches = args.steps * (toks * kps + 1)
 
     # ---- whole-step roofline: algorithmic bytes per token / time per token
     peaks, peak_kind = measured_peaks()
-    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    hbm = world * float(peaks.get("hbm_gbs", 6650.0))      # every rank streams its share
     bytes_tok = sum(pkg.synth.bytes_per_token(plan, P + i) for i in range(1, NEW)) / toks
     step_gbs = bytes_tok / (ms / 1000.0 / toks) / 1e9
 
@@ -252,12 +261,12 @@ def main():
     gemv = time_gemv(torch, rt, plan, stream)
 
     # ---- e2e through b2_generate with pinned host buffers
-    e2e = time_e2e(torch, dec, prompt, NEW, stream, world)
+    e2e = time_e2e(torch, dec, prompt, NEW, stream, dist)
 
     out = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8 x f32",
         "data": "synthetic", "config": workload_config(args, plan),
         # dominant kernel: the decode step itself (one launch of the token kernel per
         # token when kernels_per_step == 1); algorithmic bytes = weights + KV read
@@ -266,7 +275,7 @@ def main():
                      "frac": step_gbs / hbm, "traffic": profiled_traffic("token_kernel_llama2-7b"),
                      "kernel": "token_kernel (whole decode step)" if kps == 1 else "per-layer kernels",
                      "bytes_per_launch": bytes_tok, "us_per_launch": 1000.0 * ms / toks,
-                     "peak_kind": f"{peak_kind} hbm_gbs"},
+                     "peak_kind": f"{peak_kind} hbm_gbs" + (f" x {world} GPUs" if world > 1 else "")},
         "gemv_roofline": {"bound": "hbm", "achieved": gemv["gbs"], "peak": hbm, "unit": "GB/s",
                           "frac": gemv["gbs"] / hbm, "traffic": gemv["traffic"],
                           "kernel": gemv["kernel"] + " (per-launch GEMV alone)",
@@ -277,6 +286,8 @@ def main():
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(pkg, plan, args.cpu_seconds)
+    if dist:
+        dist.barrier()              # no rank frees its exchange buffer while a peer may still use it
     dec.close()
     if dist:
         dist.barrier()
@@ -318,7 +329,7 @@ def profiled_traffic(name):
     return None
 
 
-def time_e2e(torch, dec, prompt, new, stream, world, reps=2):
+def time_e2e(torch, dec, prompt, new, stream, dist=None, reps=2):
     import ctypes
     import numpy as np
     rt = importlib.import_module("aricode-ml_b200").runtime
@@ -338,7 +349,11 @@ def time_e2e(torch, dec, prompt, new, stream, world, reps=2):
     e1.record(stream)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps
-    return {"value": world * new / (ms / 1000.0), "unit": "tokens/s",
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return {"value": new / (ms / 1000.0), "unit": "tokens/s",
             "h2d_bytes_per_step": 4 * P + 64, "d2h_bytes_per_step": 4 * new + 64,
             "ms_per_generate": ms, "includes": "token-at-a-time prefill of the prompt"}
 

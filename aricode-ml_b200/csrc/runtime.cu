@@ -166,7 +166,6 @@ struct b2_ctx {
     unsigned* tk_bar = nullptr;    // grid-barrier counters, zero between launches
     int n_attn_cnt = 0;
     int tk_ns = 0, tk_ring_offset = 0, tk_inflight = kTkInflight, tk_vec_offset = 0, tk_vec_floats = 0;
-    int tk_l2_ahead = 0, tk_x_lsu = 0;
     size_t tk_smem = 0;
     std::string token_why;         // why the per-layer kernels are used instead
     unsigned long long* d_trace = nullptr;   // token-kernel timeline (B2_TK_TRACE)
@@ -791,10 +790,6 @@ void setup_token(b2_ctx* c) {
     c->tk_smem = ring_off + (size_t)ns * kTkSlotBytes;
     const char* inf = std::getenv("B2_TK_INFLIGHT");          // tuning: 0 = no cap
     c->tk_inflight = inf ? std::max(0, std::min(ns - 1, std::atoi(inf))) : std::min(kTkInflight, ns - 1);
-    const char* ahead = std::getenv("B2_TK_L2AHEAD");         // tuning: stages prefetched into L2
-    c->tk_l2_ahead = ahead ? std::max(0, std::min(64, std::atoi(ahead))) : 0;
-    const char* xl = std::getenv("B2_TK_XLSU");               // tuning: x staging with plain loads
-    c->tk_x_lsu = xl ? (std::atoi(xl) != 0) : 0;
     c->token_vs = f32 ? 1 : 0;
     if (!(f32 ? tk_prepare_kernel<1>(c) : tk_prepare_kernel<0>(c))) {
         c->token_why = "token kernel does not fit an SM";
@@ -833,8 +828,6 @@ void launch_token(b2_ctx* c, bool with_head, cudaStream_t s) {
     P.vocab = c->vocab;
     P.trace = c->d_trace;
     P.inflight = c->tk_inflight;
-    P.l2_ahead = c->tk_l2_ahead;
-    P.x_lsu = c->tk_x_lsu;
     P.vec_offset = c->tk_vec_offset;
     P.vec_floats = c->tk_vec_floats;
     P.seq = c->tk_seq;

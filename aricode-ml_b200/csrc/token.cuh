@@ -55,7 +55,7 @@ enum TkVariant : int {
 
 constexpr uint32_t kTkSlotBytes = 32 * 1024;
 constexpr int kTkMaxSlots = 7;                    // any count >= 3 (see tk_full)
-constexpr int kTkStamps = 8;                      // timeline slots per phase and CTA
+constexpr int kTkStamps = 12;                     // timeline slots per phase and CTA
 constexpr int kTkInflight = 0;                    // default cap on bulk copies outstanding per CTA (0: none)
 constexpr int kTkMaxSplits = 256;                 // max_seq <= 16384
 constexpr int kTkFastCombine = 16;               // splits combined in one round of loads (n <= 1024)
@@ -72,9 +72,7 @@ constexpr int kTkDescBytes = 864;                 // one phase descriptor copy (
 constexpr int kTkDescOffset = 3072;               // >= kTkScratchOffset + 2 * kTkGroupScratch * 4
 static_assert(kTkScratchOffset + 2 * kTkGroupScratch * 4 <= kTkDescOffset, "scratch layout");
 static_assert(4 * kTkMaxSlots * 8 <= kTkEmptyOffset && kTkEmptyOffset + kTkMaxSlots * 8 <= kTkRedOffset, "barriers");
-constexpr int kTkPjOffset = kTkDescOffset + 4 * kTkDescBytes;          // 2 consumer, producer, look-ahead copies
-constexpr int kTkPartOffset = kTkPjOffset + 64;                       // producer's next stage index
-constexpr int kTkDone = 1 << 30;                                       // ... once it has finished
+constexpr int kTkPartOffset = kTkDescOffset + 3 * kTkDescBytes + 32;   // 2 consumer + 1 producer copies
 // 640 threads: warpgroups 0-3 consume, warpgroup 4 produces (one lane works).
 // Launched at 96 registers a thread (61,440 per CTA); the producer warpgroup
 // hands registers back (setmaxnreg.dec) and the consumers take them
@@ -136,8 +134,6 @@ struct TkParams {
     int inflight;       // bulk copies outstanding per CTA (1 .. ns - 1)
     int vec_offset;     // shared-memory buffer for a phase's x and norm gains (bytes, 128-aligned)
     int vec_floats;     // its capacity
-    int l2_ahead;       // stages brought into L2 ahead of their bulk copy (0: off)
-    int x_lsu;          // 1: stage a phase's x and gains with plain loads instead of a bulk copy
     // tensor parallelism: this GPU's rank of tp_size; tp_flag[kMaxRanks] barrier
     // epochs in the exchange buffer (slot r written by rank r), mir: its peer copies
     int tp_rank, tp_size;
@@ -204,21 +200,26 @@ __device__ __forceinline__ uint64_t* tk_issue_wait(uint64_t* full, uint64_t* emp
 // consumer barrier, which publishes the descriptor copy other warps made).
 __device__ __forceinline__ bool tk_grid_sync(unsigned* ctr, unsigned target, int tid, volatile int* flag,
                                              volatile int* abort, const int* xs = nullptr,
-                                             const TkParams* P = nullptr, unsigned e = 0, int cta = 0) {
+                                             const TkParams* P = nullptr, unsigned e = 0, int cta = 0,
+                                             unsigned long long* tr = nullptr) {
     consumer_bar();
     if (tid == 0) {
         const bool xsync = xs && *xs && P && P->tp_size > 1;
         bool ok = *abort == 0;
         if (ok) {
             if (xsync) __threadfence_system();
+            if (tr) tr[8] = globaltimer_ns();
             asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
-            if (ld_acquire_gpu(ctr) < target) {
+            const unsigned first = ld_acquire_gpu(ctr);
+            if (tr) tr[9] = globaltimer_ns();
+            if (first < target) {
                 const uint64_t t0 = globaltimer_ns();
                 for (uint32_t it = 1;; ++it) {
                     if (ld_acquire_gpu(ctr) >= target) break;
                     if ((it & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) { ok = false; break; }
                 }
             }
+            if (tr) tr[10] = globaltimer_ns();
             if (ok && xsync) {
                 if (cta == 0) {
                     ok = tp_flag_exchange(P->tp_flag, P->tp_rank, P->tp_size, P->mir, e);
@@ -290,93 +291,10 @@ __device__ __forceinline__ int tk_attn_items(const AttnParams& a, int n, int& ns
     return a.H * nsplit;
 }
 
-// L2 look-ahead, run by a second warp of the producer warpgroup: a cursor over
-// the producer's stage sequence (every phase's stages in order, attention padding
-// included, so its count is the ring index j of the stage it touches) that issues
-// `cp.async.bulk.prefetch.L2` up to `ahead` stages past the producer's next bulk
-// copy (published in shared memory). DRAM keeps streaming while the ring is
-// full, e.g. across a grid barrier, and the bulk copies that follow hit L2. The
-// cursor reads its phase descriptors into its own shared copy.
-struct alignas(16) TkAhead {
-    const TkPhase* phases;
-    TkPhase* desc;
-    int nphases, ahead, cta, ncta, n;       // n: keys attended this step
-    int ph = 0, cur = 0, end = 0, sub = 0, wj = 0;
-    bool init = false;
-
-    __device__ __forceinline__ bool step() {
-        while (ph < nphases) {
-            const TkPhase& T = *desc;
-            if (!init) {
-                tk_copy_desc<16>(desc, phases + ph, 0, 1);
-                init = true;
-                sub = 0;
-                if (T.kind == TK_GEMV) {
-                    cta_rows(total_rows(T.g), T.unit, cta, ncta, cur, end);
-                } else if (T.kind == TK_ATTN) {
-                    int nsplit;
-                    end = tk_attn_items(T.a, n, nsplit);
-                    cur = cta;
-                    if (wj & 1) ++wj;                   // the padding stage copies nothing
-                } else {
-                    cur = end = 0;
-                }
-            }
-            if (T.kind == TK_GEMV && cur < end) {
-                const GemvParams& p = T.g;
-                const uint32_t row_bytes = (uint32_t)p.ld * (T.variant < TV_F32_K1_R8 ? 1u : 4u);
-                const StageRows sr = next_stage(p, cur, end, T.rows);
-                const uint32_t bytes = (uint32_t)sr.nr * row_bytes;
-                bulk_prefetch_l2(reinterpret_cast<const unsigned char*>(p.W[sr.seg]) + (size_t)sr.local * row_bytes,
-                                 bytes);
-                if (p.paired)
-                    bulk_prefetch_l2(reinterpret_cast<const unsigned char*>(p.W[1]) + (size_t)sr.local * row_bytes,
-                                     bytes);
-                cur += sr.nr;
-                ++wj;
-                return true;
-            }
-            if (T.kind == TK_ATTN && cur < end) {
-                const AttnParams& a = T.a;
-                int nsplit;
-                tk_attn_items(a, n, nsplit);
-                const int h = cur / nsplit, sp = cur % nsplit, kvh = h / (a.H / a.KVH);
-                const int j0 = sp * kAttnChunk, len = min(kAttnChunk, n - j0);
-                const size_t off = ((size_t)kvh * a.max_seq + j0) * a.dh;
-                bulk_prefetch_l2(sub ? a.V + off : a.K + off, (uint32_t)len * a.dh * 4);
-                if (++sub == 2) {
-                    sub = 0;
-                    cur += ncta;
-                }
-                ++wj;
-                return true;
-            }
-            ++ph;
-            init = false;
-        }
-        return false;
-    }
-    // follow the producer's published stage index until it is done (kTkDone) or
-    // the cursor has no stage left; bounded by the usual wait limit
-    __device__ void follow(const volatile int* pj) {
-        const uint64_t t0 = globaltimer_ns();
-        for (;;) {
-            const int j = *pj;
-            if (j >= kTkDone) return;
-            bool more = true;
-            while (wj <= j + ahead && (more = step())) {
-            }
-            if (!more) return;
-            __nanosleep(256);
-            if (globaltimer_ns() - t0 > kWaitLimitNs) return;
-        }
-    }
-};
-
 // producer side: a padding stage keeps every item's K stage on an even index
 __device__ __forceinline__ bool tk_attn_produce(const AttnParams& a, int n, int cta, int ncta,
                                                 unsigned char* ring, int NS, uint64_t* full, uint64_t* empty,
-                                                int& j, int inflight, volatile int* pj) {
+                                                int& j, int inflight) {
     int nsplit;
     const int items = tk_attn_items(a, n, nsplit);
     const int G = a.H / a.KVH, dh = a.dh;
@@ -392,7 +310,6 @@ __device__ __forceinline__ bool tk_attn_produce(const AttnParams& a, int n, int 
         const uint32_t bytes = (uint32_t)len * dh * 4;
         const size_t off = ((size_t)kvh * a.max_seq + j0) * dh;
         for (int kv = 0; kv < 2; ++kv) {
-            *pj = j;
             uint64_t* bar = tk_issue_wait(full, empty, NS, j, inflight);
             if (!bar) return false;
             mbar_arrive_expect_tx(bar, bytes);
@@ -598,11 +515,10 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
 template <int NM>
 __device__ __forceinline__ bool tk_gemv_produce(const GemvParams& p, int r0, int r1, int RS, int rows,
                                                 uint32_t row_bytes, unsigned char* ring, int NS, uint64_t* full,
-                                                uint64_t* empty, int& j, int inflight, volatile int* pj) {
+                                                uint64_t* empty, int& j, int inflight) {
     int cur = r0;
     while (cur < r1) {
         const StageRows sr = next_stage(p, cur, r1, rows);
-        *pj = j;
         uint64_t* bar = tk_issue_wait(full, empty, NS, j, inflight);
         if (!bar) return false;
         const uint32_t bytes = (uint32_t)sr.nr * row_bytes;
@@ -727,25 +643,13 @@ __device__ __forceinline__ bool tk_gemv(const GemvParams& p, int unit, int rs, i
                                         int NS, uint64_t* full, uint64_t* empty, int& j, int group, int gwarp,
                                         int lane, int tid, float* red, float* part, int cta, int ncta,
                                         unsigned long long* tr, float* vec, uint64_t* vbar, uint32_t& vphase,
-                                        unsigned* amx, bool xlsu) {
+                                        unsigned* amx) {
     constexpr int ESZ = (int)sizeof(WT);
     int r0, r1;
     cta_rows(total_rows(p), unit, cta, ncta, r0, r1);
     const bool paired = p.paired != 0;
     const int n = p.n, L = (n + 15) & ~15;
-    if (xlsu) {
-        // plain 16-byte loads through L2: they do not queue behind the producer's
-        // bulk copies in this SM's copy engine (n % 4 == 0, 16-byte aligned)
-        const int n4 = n / 4;
-        float4* v4 = reinterpret_cast<float4*>(vec);
-        for (int i = tid; i < n4; i += kGemvConsumerThreads) v4[i] = __ldcg(reinterpret_cast<const float4*>(p.x) + i);
-        if (p.norm != NORM_NONE)
-            for (int i = tid; i < n4; i += kGemvConsumerThreads)
-                v4[L / 4 + i] = __ldg(reinterpret_cast<const float4*>(p.ng) + i);
-        if (p.norm == NORM_LN)
-            for (int i = tid; i < n4; i += kGemvConsumerThreads)
-                v4[L / 2 + i] = __ldg(reinterpret_cast<const float4*>(p.nb) + i);
-    } else if (tid == 0) {
+    if (tid == 0) {
         // generic-proxy writes (x by other CTAs; vec by this CTA's last phase) are
         // ordered before the bulk copies that read / overwrite them
         asm volatile("fence.proxy.async.global;" ::: "memory");
@@ -765,13 +669,8 @@ __device__ __forceinline__ bool tk_gemv(const GemvParams& p, int unit, int rs, i
         for (int i = tid; i < (r1 - r0) * nm * 4; i += kGemvConsumerThreads) reinterpret_cast<int*>(part)[i] = 0;
     const EpiRow er = paired ? gemv_epi_load<ESZ, true>(p, r0, r1, pos, tid)
                              : gemv_epi_load<ESZ, false>(p, r0, r1, pos, tid);
-    bool ok = true;
-    if (xlsu) {
-        consumer_bar();                                 // the staged vectors are visible
-    } else {
-        ok = mbar_wait_bounded(vbar, vphase & 1);
-        ++vphase;
-    }
+    bool ok = mbar_wait_bounded(vbar, vphase & 1);
+    ++vphase;
     const uint32_t am = gemv_norm_smem(p, vec, vec + L, vec + 2 * L, red, tid);
     tk_stamp(tr, 1, tid);
     gemv_epi_store(er, r1 - r0, tid, epi);
@@ -830,12 +729,12 @@ __device__ __forceinline__ bool tk_gemv_dispatch(const TkPhase& T, int pos, cons
                                                  uint64_t* full, uint64_t* empty, int& j, int group, int gwarp,
                                                  int lane, int tid, float* red, float* part, int cta, int ncta,
                                                  unsigned long long* tr, float* vec, uint64_t* vbar,
-                                                 uint32_t& vphase, unsigned* amx, bool xlsu) {
+                                                 uint32_t& vphase, unsigned* amx) {
     if (VS == 1 && T.variant >= TV_F32_K1_R8)
         return tk_gemv<float>(T.g, T.unit, T.rs, T.rows, pos, ring, NS, full, empty, j, group, gwarp, lane, tid, red, part,
-                              cta, ncta, tr, vec, vbar, vphase, amx, xlsu);
+                              cta, ncta, tr, vec, vbar, vphase, amx);
     return tk_gemv<int8_t>(T.g, T.unit, T.rs, T.rows, pos, ring, NS, full, empty, j, group, gwarp, lane, tid, red, part, cta,
-                           ncta, tr, vec, vbar, vphase, amx, xlsu);
+                           ncta, tr, vec, vbar, vphase, amx);
 }
 
 // --------------------------------------------------------------------- the kernel
@@ -849,7 +748,6 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
     volatile int* abort = flag + 6;
     unsigned* amx = reinterpret_cast<unsigned*>(smem + kTkFlagOffset + 28);   // int8 GEMV: largest |x| bits
     uint64_t* vbar = reinterpret_cast<uint64_t*>(smem + kTkVbarOffset);  // vector staging
-    volatile int* pj = reinterpret_cast<volatile int*>(smem + kTkPjOffset);
     float* vec = reinterpret_cast<float*>(smem + P.vec_offset);
     float* scratch = reinterpret_cast<float*>(smem + kTkScratchOffset);
     float* part = reinterpret_cast<float*>(smem + kTkPartOffset);
@@ -891,7 +789,6 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
         fence_mbar_init();
         *abort = 0;
         *amx = 0u;
-        *pj = 0;
     }
     __syncthreads();
 
@@ -914,24 +811,19 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
                     const uint32_t row_bytes = (uint32_t)p.ld * (i8 ? 1u : 4u);
                     tk_prefetch_vectors(p, r0, r1, pos, i8);
                     ok = p.paired ? tk_gemv_produce<2>(p, r0, r1, T.rs, T.rows, row_bytes, ring, NS, full, empty, j,
-                                                       P.inflight, pj)
+                                                       P.inflight)
                                   : tk_gemv_produce<1>(p, r0, r1, T.rs, T.rows, row_bytes, ring, NS, full, empty, j,
-                                                       P.inflight, pj);
+                                                       P.inflight);
                 } else if (T.kind == TK_ATTN) {
-                    ok = tk_attn_produce(T.a, pos + 1, cta, ncta, ring, NS, full, empty, j, P.inflight, pj);
+                    ok = tk_attn_produce(T.a, pos + 1, cta, ncta, ring, NS, full, empty, j, P.inflight);
                 }
             }
-            *pj = kTkDone;
             if (!ok) set_err(err, B2_DEV_ERR_TIMEOUT);
             for (int i = max(0, j - NS); i < j; ++i)        // no copy in flight at exit
                 if (!mbar_wait_bounded(tk_full(full, i, NS), tk_full_parity(i, NS))) {
                     set_err(err, B2_DEV_ERR_TIMEOUT);
                     break;
                 }
-        } else if (warp == kGemvConsumerWarps + 1 && lane == 0 && P.l2_ahead > 0) {
-            TkAhead ah{P.phases, reinterpret_cast<TkPhase*>(smem + kTkDescOffset + 3 * kTkDescBytes), P.nphases,
-                       P.l2_ahead, cta, ncta, pos + 1};
-            ah.follow(pj);
         }
         return;
     }
@@ -954,8 +846,9 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
         const TkPhase& T = cdesc[ph & 1];
         if (ph > 0) {
             arrivals += (unsigned)ncta;
+            unsigned long long* trb = P.trace ? P.trace + ((size_t)ph * ncta + cta) * kTkStamps : nullptr;
             if (!tk_grid_sync(P.bar, arrivals, tid, flag + 4 * (ph & 1), abort, &T.xsync, &P,
-                              seq * 1024u + (unsigned)ph, cta)) {
+                              seq * 1024u + (unsigned)ph, cta, trb)) {
                 if (tid == 0) *abort = 1;
                 break;
             }
@@ -984,7 +877,7 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
             }
         } else if (T.kind == TK_GEMV) {
             ok = tk_gemv_dispatch<VS>(T, pos, ring, NS, full, empty, j, group, gwarp, lane, tid, red, part, cta,
-                                      ncta, tr, vec, vbar, vphase, amx, P.x_lsu != 0);
+                                      ncta, tr, vec, vbar, vphase, amx);
         } else {
             tk_stamp(tr, 1, tid);
             tk_stamp(tr, 2, tid);

@@ -169,6 +169,10 @@ class Decoder:
             joined = tp_gather_handles(h.raw, rank, size, exchange)
             allh = C.create_string_buffer(joined, 64 * size)
             dec._ck(lib().b2_tp_connect(ctx, allh, 64 * size))
+            # graph capture in b2_tp_connect takes each rank its own time: meet once
+            # more, so that the first step's cross-rank waits (bounded at about 1 s)
+            # do not start seconds apart
+            exchange(bytes(64))
         return dec
 
     def close(self):

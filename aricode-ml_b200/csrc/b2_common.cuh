@@ -264,15 +264,21 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
     return v;
 }
 
-// Publish epoch e in slot `rank` of the flag array f on every rank (after a
-// system-scope fence: this thread's and its CTA's earlier writes, peer copies
-// included, become visible first), then wait until every rank's slot has
-// reached e (wrap-safe). Bounded: false after ~1 s.
+__device__ __forceinline__ void st_relaxed_sys(unsigned* p, unsigned v) {
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Publish epoch e in slot `rank` of the flag array f on every rank, then wait
+// until every rank's slot has reached e (wrap-safe). One system-scope fence
+// before the relaxed flag stores makes them a release: every write this thread
+// has observed (the other CTAs' outputs and peer copies, acquired through the
+// local grid barrier) is visible on every rank before its flag. Bounded: false
+// after ~1 s.
 __device__ __forceinline__ bool tp_flag_exchange(unsigned* f, int rank, int nranks, const Mirror& m, unsigned e) {
     __threadfence_system();
-    st_release_sys(f + rank, e);
+    st_relaxed_sys(f + rank, e);
     for (int i = 0; i < m.n; ++i)
-        st_release_sys(reinterpret_cast<unsigned*>(reinterpret_cast<char*>(f + rank) + m.delta[i]), e);
+        st_relaxed_sys(reinterpret_cast<unsigned*>(reinterpret_cast<char*>(f + rank) + m.delta[i]), e);
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t it = 1;; ++it) {
         bool all = true;

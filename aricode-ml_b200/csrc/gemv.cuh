@@ -321,7 +321,9 @@ __device__ __forceinline__ void xfix_block(const float (&x)[16], int S, uint32_t
     for (int q = 0; q < 4; ++q) {
         uint32_t X[4];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) X[k] = xfix_elem(x[4 * q + k], S);
+        for (int k = 0; k < 4; ++k)
+            X[k] = S <= 127 ? (uint32_t)__float2int_rz(__fmul_rn(x[4 * q + k], __uint_as_float((uint32_t)(S + 127) << 23)))
+                            : xfix_elem(x[4 * q + k], S);   // exact either way (see xfix_smem)
         const uint32_t lo01 = __byte_perm(X[0], X[1], 0x5140u), hi01 = __byte_perm(X[0], X[1], 0x7362u);
         const uint32_t lo23 = __byte_perm(X[2], X[3], 0x5140u), hi23 = __byte_perm(X[2], X[3], 0x7362u);
         w[0 * 4 + q] = __byte_perm(lo01, lo23, 0x5410u);

@@ -193,9 +193,10 @@ __device__ __forceinline__ uint64_t* tk_issue_wait(uint64_t* full, uint64_t* emp
 // between two slots (phase parity), so one barrier publishes it.
 //
 // With tensor parallelism (xsync), the previous phase's outputs were also written
-// into the peers' buffers: every CTA fences at system scope before it arrives, and
-// once the local barrier is complete CTA 0 publishes epoch `e` to every rank;
-// every CTA then waits for all ranks' epochs (tp_flag_exchange, bounded).
+// into the peers' buffers: once the local barrier is complete CTA 0 publishes
+// epoch `e` to every rank (tp_flag_exchange: a system-scope release, cumulative
+// over the other CTAs' writes it acquired through the barrier); every CTA then
+// waits for all ranks' epochs (bounded).
 // xs: the cross-rank request, e.g. the next phase's xsync (read after the first
 // consumer barrier, which publishes the descriptor copy other warps made).
 __device__ __forceinline__ bool tk_grid_sync(unsigned* ctr, unsigned target, int tid, volatile int* flag,
@@ -207,7 +208,9 @@ __device__ __forceinline__ bool tk_grid_sync(unsigned* ctr, unsigned target, int
         const bool xsync = xs && *xs && P && P->tp_size > 1;
         bool ok = *abort == 0;
         if (ok) {
-            if (xsync) __threadfence_system();
+            // (with xsync no system-scope fence here: this release at gpu scope, CTA 0's
+            // acquire of the count and its system-scope release of the epoch order this
+            // CTA's peer copies before every rank's flag)
             if (tr) tr[8] = globaltimer_ns();
             asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(ctr) : "memory");
             const unsigned first = ld_acquire_gpu(ctr);

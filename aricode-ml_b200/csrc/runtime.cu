@@ -477,7 +477,7 @@ void assemble(b2_ctx* c, const b2json::Value& plan) {
     const size_t i_q = add((size_t)max_q * 4);
     const size_t i_seq = add(4);
     const size_t i_logits = add((size_t)c->vocab * 4);
-    const size_t i_part = add((size_t)max_H * c->attn_nsplit_max * (max_dh + 2) * 4);
+    const size_t i_part = add((size_t)max_H * c->attn_nsplit_max * (max_dh + 2) * 8);   // token kernel: (value, tag) pairs
     const size_t i_acnt = add((size_t)std::max(max_H, max_KVH) * 4);   // per query head (token kernel)
     const size_t i_aval = add((size_t)c->sm_count * 4);
     const size_t i_aidx = add((size_t)c->sm_count * 4);

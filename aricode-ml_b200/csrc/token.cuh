@@ -329,7 +329,7 @@ __device__ __forceinline__ bool tk_attn_produce(const AttnParams& a, int n, int 
 __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, int cta, int ncta,
                                                 const unsigned char* ring, int NS, uint64_t* full,
                                                 uint64_t* empty, int& j, int group, int gwarp, int lane,
-                                                float* scr, volatile int* gflag) {
+                                                float* scr, volatile int* gflag, unsigned tag) {
     const int n = pos + 1;
     int nsplit;
     const int items = tk_attn_items(a, n, nsplit);
@@ -419,17 +419,31 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
         if (!group_wait(tk_full(full, j + 1, NS), tk_full_parity(j + 1, NS), group, gt, gflag)) return false;
         const float* Vs = reinterpret_cast<const float*>(ring + (size_t)slotv * kTkSlotBytes);
         const int stride = dh + 2;
+        // up to kTkFastCombine splits, each value goes out with this phase's tag in one
+        // 8-byte store (value, tag) and the last arriver checks the tags instead of
+        // both sides fencing; more splits: plain floats and fences
+        const bool tagged = nsplit <= kTkFastCombine;
         float* pp = a.part + ((size_t)h * a.nsplit_max + s) * stride;
+        unsigned long long* pq = reinterpret_cast<unsigned long long*>(a.part) + ((size_t)h * a.nsplit_max + s) * stride;
+        auto pack = [&](float v) { return (unsigned long long)__float_as_uint(v) | ((unsigned long long)tag << 32); };
         if (gt < dh) {
             float acc = 0.0f;
             for (int jj = 0; jj < len; ++jj)
                 acc = ffma(sc[jj], jj == jnew ? vn : Vs[jj * dh + gt], acc);
-            pp[gt] = acc;
-            if (gt == 0) { pp[dh] = ml[0]; pp[dh + 1] = ml[1]; }
+            if (tagged) {
+                *reinterpret_cast<volatile unsigned long long*>(pq + gt) = pack(acc);
+                if (gt == 0) {
+                    *reinterpret_cast<volatile unsigned long long*>(pq + dh) = pack(ml[0]);
+                    *reinterpret_cast<volatile unsigned long long*>(pq + dh + 1) = pack(ml[1]);
+                }
+            } else {
+                pp[gt] = acc;
+                if (gt == 0) { pp[dh] = ml[0]; pp[dh + 1] = ml[1]; }
+            }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slotv]);
-        __threadfence();
+        if (!tagged) __threadfence();
         group_bar(group);
         if (gt == 0) {
             const unsigned t = atomicAdd(a.counters + h, 1u);
@@ -438,20 +452,36 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
         group_bar(group);
         if (!reinterpret_cast<int*>(ml)[2]) continue;
         // last split of head h: combine the splits and the -60 tail
-        __threadfence();
         const float* base = a.part + (size_t)h * a.nsplit_max * stride;
-        if (nsplit <= kTkFastCombine) {
-            // one round of loads: every split's (m, l) into scratch by threads
-            // t < nsplit, and each thread's o[gt] of every split into registers; then
-            // each thread forms M, the weights and l itself, in split order
+        if (tagged) {
+            // one round of loads (repeated, bounded, until every tag is this phase's:
+            // the other splits have issued their stores, which may still be landing):
+            // every split's (m, l) into scratch by threads t < nsplit, and each
+            // thread's o[gt] of every split into registers; then each thread forms M,
+            // the weights and l itself, in split order
+            const unsigned long long* bq = reinterpret_cast<const unsigned long long*>(a.part) +
+                                           (size_t)h * a.nsplit_max * stride;
+            auto get = [&](const unsigned long long* q, float& v) {
+                const unsigned long long w = __ldcg(q);
+                v = __uint_as_float((unsigned)w);
+                return (unsigned)(w >> 32) == tag;
+            };
             float ot[kTkFastCombine];
-            if (gt < nsplit) {
-                wsm[gt] = __ldcg(base + (size_t)gt * stride + dh);
-                sc[gt] = __ldcg(base + (size_t)gt * stride + dh + 1);
-            }
+            const uint64_t tw = globaltimer_ns();
+            for (;;) {
+                bool all = true;
+                if (gt < nsplit) {
+                    all = get(bq + (size_t)gt * stride + dh, wsm[gt]) && all;
+                    all = get(bq + (size_t)gt * stride + dh + 1, sc[gt]) && all;
+                }
 #pragma unroll
-            for (int t = 0; t < kTkFastCombine; ++t)
-                ot[t] = (t < nsplit && gt < dh) ? __ldcg(base + (size_t)t * stride + gt) : 0.0f;
+                for (int t = 0; t < kTkFastCombine; ++t) {
+                    ot[t] = 0.0f;
+                    if (t < nsplit && gt < dh) all = get(bq + (size_t)t * stride + gt, ot[t]) && all;
+                }
+                if (all) break;
+                if (globaltimer_ns() - tw > kWaitLimitNs) { set_err(a.err, B2_DEV_ERR_TIMEOUT); break; }
+            }
             group_bar(group);
             if (gt < dh) {
                 float M = wsm[0];
@@ -473,6 +503,7 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
             group_bar(group);                           // scratch reused by the next item
             continue;
         }
+        __threadfence();
         // every split's (m, l) in one parallel round of loads: m into wsm, l into sc
         for (int t = gt; t < nsplit; t += 256) {
             wsm[t] = __ldcg(base + (size_t)t * stride + dh);
@@ -884,7 +915,8 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
         } else {
             tk_stamp(tr, 1, tid);
             tk_stamp(tr, 2, tid);
-            ok = tk_attn_consume(T.a, pos, cta, ncta, ring, NS, full, empty, j, group, gwarp, lane, gscr, gflag);
+            ok = tk_attn_consume(T.a, pos, cta, ncta, ring, NS, full, empty, j, group, gwarp, lane, gscr, gflag,
+                                 seq * 1024u + (unsigned)ph + 1u);
             if (tr) {
                 consumer_bar();
                 tk_stamp(tr, 3, tid);

@@ -27,6 +27,7 @@ extern "C" {
 int b2_gemv_i8_rowscale(const int8_t* W, int64_t ld, const float* scale, const float* x,
                         const float* bias, float* y, int m, int n, void* stream) {
     if (!W || !scale || !x || !y || m <= 0 || n <= 0 || ld < n || ld % 16 || !al16(W)) return B2_E_INVALID;
+    if (n > kXfixMaxN) return B2_E_INVALID;          // the int32 plane sums would overflow
     GemvParams p{};
     p.W[0] = W; p.S[0] = scale; p.bias[0] = bias;
     p.rows[0] = m; p.nseg = 1; p.n = n; p.ld = (int)ld;

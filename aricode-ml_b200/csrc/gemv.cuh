@@ -224,11 +224,13 @@ __device__ __forceinline__ void exchange_butterfly_i(int (&v)[N], int lane) {
 // f32((double)D 2^-S). Integer sums are exact in any order, so the thread layout
 // and the reduction tree do not change the bits. X is split into byte planes
 // X = P0 + 2^8 P1 + 2^16 P2 + 2^24 P3 (P0..P2 unsigned, P3 signed); one dp4a
-// takes four codes of a row against the same four elements of one plane. Each
-// plane sum stays below 128 * 255 * 16384 < 2^31 for rows of up to 16384 codes.
+// takes four codes of a row against the same four elements of one plane. A
+// plane sum of a row is at most 128 * 255 * n in magnitude, below 2^31 for rows
+// of up to kXfixMaxN = 65536 codes (128 * 255 * 65536 = 2,139,095,040); longer
+// rows would overflow the int32 sums, so every entry point refuses them.
 // ---------------------------------------------------------------------------
 constexpr int kXfixBad = -100000;                  // S when x holds a NaN or an infinity
-constexpr int kXfixMaxN = 16384;
+constexpr int kXfixMaxN = 65536;
 
 // S from the largest |x| bit pattern (non-negative floats order as their bits)
 __device__ __forceinline__ int xfix_shift(uint32_t amax_bits) {

@@ -245,6 +245,21 @@ static __global__ void synth_fill_kernel(unsigned long long seed, unsigned long 
     out[i] = c < n ? synth_value(seed, tid, (unsigned long long)(r * n + c), stdv) : 0.0f;
 }
 
+// Synthetic KV rows [0, count) of one attention sub-block: value of global
+// element ((kv0 + kh) * max_seq + pos) * dh + i with unit std, written at the
+// local head kh (oracle b2o_state_fill_kv; kv0 = this rank's first KV head)
+static __global__ void synth_kv_kernel(unsigned long long seed, unsigned long long tid, float* cache, int kvh,
+                                       int kv0, int max_seq, int dh, int count) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long long per = (long long)count * dh;
+    if (i >= per * kvh) return;
+    const int kh = (int)(i / per);
+    const long long rem = i % per;
+    const int pos = (int)(rem / dh), d = (int)(rem % dh);
+    const unsigned long long at = ((unsigned long long)(kv0 + kh) * max_seq + pos) * dh + d;
+    cache[((long long)kh * max_seq + pos) * dh + d] = synth_value(seed, tid, at, 1.0f);
+}
+
 static __global__ void fill_kernel(float* out, long long n, float v) {
     const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) out[i] = v;
@@ -325,70 +340,12 @@ inline GemvShape gemv_shape(const GemvParams& p, int esz, int grid_cap) {
     return sh;
 }
 
-template <typename WT, int KMAX, int RS, bool PAIRED>
-inline cudaError_t launch_gemv_t(GemvParams p, const GemvShape& sh, cudaStream_t s, bool pdl) {
-    p.nstages = sh.nstages;
-    p.stage_rows = sh.R;
-    p.ring_offset = sh.ring_offset;
-    auto k = gemv_kernel<WT, KMAX, RS, PAIRED>;
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sh.smem);
-    if (e != cudaSuccess) return e;
-    return launch_ex(k, dim3(sh.grid), dim3(kGemvThreads), sh.smem, s, pdl, p);
-}
-
-template <typename WT, int KMAX, bool PAIRED>
-inline cudaError_t launch_gemv_r(const GemvParams& p, const GemvShape& sh, cudaStream_t s, bool pdl) {
-    if constexpr (KMAX > 1) {               // rows over 4 KB: at most 4 rows fit a 32 KB stage
-        if (sh.R == 1) return launch_gemv_t<WT, KMAX, 1, PAIRED>(p, sh, s, pdl);
-        if (sh.R == 2) return launch_gemv_t<WT, KMAX, 2, PAIRED>(p, sh, s, pdl);
-        if constexpr (!PAIRED)
-            if (sh.R == 4) return launch_gemv_t<WT, KMAX, 4, PAIRED>(p, sh, s, pdl);
-        return cudaErrorInvalidValue;
-    } else {
-    switch (sh.R) {
-        case 1: return launch_gemv_t<WT, KMAX, 1, PAIRED>(p, sh, s, pdl);
-        case 2: return launch_gemv_t<WT, KMAX, 2, PAIRED>(p, sh, s, pdl);
-        case 4: return launch_gemv_t<WT, KMAX, 4, PAIRED>(p, sh, s, pdl);
-        case 8: return launch_gemv_t<WT, KMAX, 8, PAIRED>(p, sh, s, pdl);
-        default:
-            if constexpr (PAIRED) return cudaErrorInvalidValue;
-            else return launch_gemv_t<WT, KMAX, 16, PAIRED>(p, sh, s, pdl);
-    }
-    }
-}
-
+// Launchers (defined once, in launch.cu, so that the GEMV kernel templates are
+// instantiated in one translation unit only).
 // weights int8 (w_i8) or f32; rows up to kGemvMaxK*256 16-byte blocks long
-inline cudaError_t launch_gemv(const GemvParams& p, bool w_i8, cudaStream_t s, bool pdl,
-                               int grid_cap, GemvShape* out_shape = nullptr) {
-    const GemvShape sh = gemv_shape(p, w_i8 ? 1 : 4, grid_cap);
-    if (out_shape) *out_shape = sh;
-    if (sh.K < 1 || sh.K > kGemvMaxK || sh.smem > 227 * 1024) return cudaErrorInvalidValue;
-    if (w_i8) {
-        if (sh.paired) {
-            if (sh.K <= 1) return launch_gemv_r<int8_t, 1, true>(p, sh, s, pdl);
-            if (sh.K <= 3) return launch_gemv_r<int8_t, 3, true>(p, sh, s, pdl);
-            return launch_gemv_r<int8_t, kGemvMaxK, true>(p, sh, s, pdl);
-        }
-        if (sh.K <= 1) return launch_gemv_r<int8_t, 1, false>(p, sh, s, pdl);
-        if (sh.K <= 3) return launch_gemv_r<int8_t, 3, false>(p, sh, s, pdl);
-        return launch_gemv_r<int8_t, kGemvMaxK, false>(p, sh, s, pdl);
-    }
-    if (sh.paired) return cudaErrorInvalidValue;
-    if (sh.K <= 1) return launch_gemv_r<float, 1, false>(p, sh, s, pdl);
-    return launch_gemv_r<float, kGemvMaxK, false>(p, sh, s, pdl);
-}
-
-inline cudaError_t launch_attn(const AttnParams& p, cudaStream_t s, bool pdl) {
-    const int G = p.H / p.KVH;
-    const size_t smem = attn_smem_bytes(G, p.dh, p.nsplit_max);
-    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
-    if (e != cudaSuccess) return e;
-    return launch_ex(attn_decode_kernel, dim3(p.nsplit_max, p.KVH), dim3(kAttnThreads), smem, s, pdl, p);
-}
-
-inline cudaError_t launch_embed(const EmbedParams& p, cudaStream_t s, bool pdl) {
-    return launch_ex(embed_kernel, dim3(1), dim3(256), 0, s, pdl, p);
-}
+cudaError_t launch_gemv(const GemvParams& p, bool w_i8, cudaStream_t s, bool pdl, int grid_cap,
+                        GemvShape* out_shape = nullptr);
+cudaError_t launch_attn(const AttnParams& p, cudaStream_t s, bool pdl);
+cudaError_t launch_embed(const EmbedParams& p, cudaStream_t s, bool pdl);
 
 }  // namespace b2

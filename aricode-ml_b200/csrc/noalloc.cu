@@ -16,7 +16,9 @@
 //   * every GPU that loads the library keeps the 4 MiB until the process exits;
 //   * the first call on a device looks up the array's device address there
 //     (cudaGetSymbolAddress with that device current); make that first call
-//     before any stream capture;
+//     before any stream capture. The address is cached per device for the life
+//     of the process and never looked up again, so a host that resets a device
+//     (cudaDeviceReset) must not call this entry point on it afterwards;
 //   * all calls share the array and it keeps the last call's contents: the
 //     per-head counters are cleared on the caller's stream at the start of every
 //     call (the partials are always written before they are read), and calls

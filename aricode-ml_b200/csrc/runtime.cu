@@ -233,6 +233,9 @@ struct b2_ctx {
         m.i8 = t.dtype == 1;
         if (m.i8) {
             if (t.ld % 16) throw Err(B2_E_FORMAT, "int8 tensor '" + name + "' row stride not 16-aligned");
+            if (cols > kXfixMaxN)
+                throw Err(B2_E_UNSUPPORTED, "int8 tensor '" + name + "' has rows longer than " +
+                                                std::to_string(kXfixMaxN) + " codes (the exact dot's int32 sums)");
             b2json::Value sname;
             sname.kind = b2json::Value::String;
             sname.str = name + "_scales";
@@ -736,11 +739,9 @@ bool tk_phase_of(const b2_ctx* c, const Op& o, TkPhase& T, size_t& part_bytes, s
     return true;
 }
 
-template <int VS>
-bool tk_prepare_kernel(b2_ctx* c) {
-    CK(cudaFuncSetAttribute(token_kernel<VS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c->tk_smem));
+bool tk_prepare_kernel(b2_ctx* c, int vs) {
     int per_sm = 0;
-    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, token_kernel<VS>, kTkThreads, c->tk_smem));
+    CK(tk_prepare(vs, c->tk_smem, &per_sm));
     return per_sm >= 1;
 }
 
@@ -771,8 +772,11 @@ void setup_token(b2_ctx* c) {
         if (head == 0) c->nph_prefill = (int)ph.size();
         else c->nph_decode = (int)ph.size() - c->nph_prefill;
     }
-    if (c->tp_size > 1 && std::max(c->nph_prefill, c->nph_decode) >= 1024) {
-        c->token_why = "more than 1023 phases (cross-rank epochs)";
+    // phase tags and cross-rank epochs are launch count x 1024 + phase: a table of
+    // 1024 or more phases would give phase 1024 + k of one launch the tag of phase k
+    // of the next one
+    if (std::max(c->nph_prefill, c->nph_decode) >= 1024) {
+        c->token_why = "more than 1023 phases (phase tags)";
         return;
     }
     const size_t vec_off = (kTkPartOffset + part + 127) & ~(size_t)127;
@@ -791,7 +795,7 @@ void setup_token(b2_ctx* c) {
     const char* inf = std::getenv("B2_TK_INFLIGHT");          // tuning: 0 = no cap
     c->tk_inflight = inf ? std::max(0, std::min(ns - 1, std::atoi(inf))) : std::min(kTkInflight, ns - 1);
     c->token_vs = f32 ? 1 : 0;
-    if (!(f32 ? tk_prepare_kernel<1>(c) : tk_prepare_kernel<0>(c))) {
+    if (!tk_prepare_kernel(c, f32 ? 1 : 0)) {
         c->token_why = "token kernel does not fit an SM";
         return;
     }
@@ -846,8 +850,7 @@ void launch_token(b2_ctx* c, bool with_head, cudaStream_t s) {
     at[0].val.cooperative = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    if (c->token_vs) CK(cudaLaunchKernelEx(&cfg, token_kernel<1>, P));
-    else CK(cudaLaunchKernelEx(&cfg, token_kernel<0>, P));
+    CK(tk_launch(c->token_vs, cfg, P));
 }
 
 void capture_graphs_once(b2_ctx* c);
@@ -1300,6 +1303,29 @@ int b2_set_position(b2_ctx* ctx, int pos, int32_t next_tok) {
         set_state_kernel<<<1, 1, 0, ctx->stream>>>(ctx->st, pos, pos, 1 << 30, next_tok, -1);
         CK(cudaGetLastError());
         ctx->host_step = pos;
+        return B2_OK;
+    });
+}
+
+int b2_fill_kv_synthetic(b2_ctx* ctx, int count, uint64_t seed) {
+    return guarded(ctx, [&] {
+        if (!ctx->g_decode) throw Err(B2_E_INVALID, "ranks not connected (b2_tp_connect)");
+        if (count < 0 || count > ctx->max_seq) return B2_E_INVALID;
+        for (size_t b = 0; b < ctx->blocks.size(); ++b) {
+            const Block& B = ctx->blocks[b];
+            if (!B.attn || count == 0) continue;
+            const long long n = (long long)B.KVH * count * B.dh;
+            const unsigned grid = (unsigned)((n + 255) / 256);
+            const int kv0 = ctx->tp_rank * B.KVH;
+            synth_kv_kernel<<<grid, 256, 0, ctx->stream>>>(seed, 0xC0DE0000ull + 2 * b, B.K, B.KVH, kv0,
+                                                           ctx->max_seq, B.dh, count);
+            synth_kv_kernel<<<grid, 256, 0, ctx->stream>>>(seed, 0xC0DE0001ull + 2 * b, B.V, B.KVH, kv0,
+                                                           ctx->max_seq, B.dh, count);
+            CK(cudaGetLastError());
+        }
+        upload_state(ctx, count, count, 1 << 30, 0, -1);
+        CK(cudaStreamSynchronize(ctx->stream));
+        ctx->host_step = count;
         return B2_OK;
     });
 }

@@ -159,6 +159,18 @@ __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
     return v;
 }
 
+// (value, tag) words of the tagged attention partials: relaxed gpu-scope loads and
+// stores, so that the reader's tag check is a morally strong read of the writer's
+// store under the PTX memory model
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_relaxed_gpu_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
 __device__ __forceinline__ void group_bar(int group) {
     asm volatile("bar.sync %0, 256;" ::"r"(2 + group) : "memory");
 }
@@ -431,10 +443,10 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
             for (int jj = 0; jj < len; ++jj)
                 acc = ffma(sc[jj], jj == jnew ? vn : Vs[jj * dh + gt], acc);
             if (tagged) {
-                *reinterpret_cast<volatile unsigned long long*>(pq + gt) = pack(acc);
+                st_relaxed_gpu_u64(pq + gt, pack(acc));
                 if (gt == 0) {
-                    *reinterpret_cast<volatile unsigned long long*>(pq + dh) = pack(ml[0]);
-                    *reinterpret_cast<volatile unsigned long long*>(pq + dh + 1) = pack(ml[1]);
+                    st_relaxed_gpu_u64(pq + dh, pack(ml[0]));
+                    st_relaxed_gpu_u64(pq + dh + 1, pack(ml[1]));
                 }
             } else {
                 pp[gt] = acc;
@@ -462,7 +474,7 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
             const unsigned long long* bq = reinterpret_cast<const unsigned long long*>(a.part) +
                                            (size_t)h * a.nsplit_max * stride;
             auto get = [&](const unsigned long long* q, float& v) {
-                const unsigned long long w = __ldcg(q);
+                const unsigned long long w = ld_relaxed_gpu_u64(q);
                 v = __uint_as_float((unsigned)w);
                 return (unsigned)(w >> 32) == tag;
             };
@@ -955,5 +967,10 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
         }
     }
 }
+
+// Host side (token.cu, where the kernel is instantiated): set the dynamic shared
+// memory of variant set vs and report how many CTAs fit an SM; launch one step.
+cudaError_t tk_prepare(int vs, size_t smem, int* per_sm);
+cudaError_t tk_launch(int vs, const cudaLaunchConfig_t& cfg, const TkParams& P);
 
 }  // namespace b2

@@ -65,6 +65,7 @@ def _declare(L):
     L.b2_generate.argtypes = [vp, i32p, C.c_int, C.c_int, C.c_int32, i32p, C.POINTER(C.c_int)]
     L.b2_set_position.argtypes = [vp, C.c_int, C.c_int32]
     L.b2_decode_async.argtypes = [vp, C.c_int]
+    L.b2_fill_kv_synthetic.argtypes = [vp, C.c_int, C.c_uint64]
     L.b2_sync.argtypes = [vp]
     L.b2_read_output.argtypes = [vp, i32p, C.c_int, C.POINTER(C.c_int)]
     L.b2_set_stream.argtypes = [vp, vp]
@@ -228,6 +229,11 @@ class Decoder:
 
     def set_position(self, pos, next_tok):
         self._ck(lib().b2_set_position(self._ctx, int(pos), int(next_tok)))
+
+    def fill_kv_synthetic(self, count, seed=0):
+        """KV rows [0, count) from the synthetic generator (the oracle's fill_kv) and
+        the position set to count: decoding can start mid-sequence without a prefill."""
+        self._ck(lib().b2_fill_kv_synthetic(self._ctx, int(count), int(seed)))
 
     def decode_async(self, n_steps):
         self._ck(lib().b2_decode_async(self._ctx, int(n_steps)))

@@ -33,6 +33,8 @@ import tempfile
 import time
 from pathlib import Path
 
+import numpy as np
+
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
@@ -119,46 +121,108 @@ class Clocks:
                 "samples": len(rows), "reasons": sorted(reasons)}
 
 
-def cpu_baseline(pkg, plan, seconds, threads=None):
-    """The oracle (CPU restatement of the reference decode path) on the host cores:
-    decode steps at positions 512.. over a synthetic KV prefix, as many as fit in
-    `seconds` (at least 2)."""
-    sys.path.insert(0, str(ROOT / "oracle"))
-    import oracle as O
-    threads = threads or os.cpu_count() or 1
+def cpu_model():
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+_ORACLE = {}
+
+
+def oracle_model(pkg, plan):
+    """The oracle (CPU restatement of the reference decode path) over the same
+    synthetic weights as the GPU (generated on the host, untimed); built once."""
+    key = json.dumps(plan, sort_keys=True)
+    if key not in _ORACLE:
+        sys.path.insert(0, str(ROOT / "oracle"))
+        import oracle as O
+        t0 = time.time()
+        om = O.OracleModel(plan, O.synth_tensors(plan, seed=0), threads=os.cpu_count() or 1)
+        _ORACLE[key] = (O, om, time.time() - t0)
+    return _ORACLE[key]
+
+
+def cpu_decode(pkg, plan, n_tokens, threads, start, seconds=None, n_min=2):
+    """Decode greedy tokens with the oracle in f32-accumulate mode (the reference
+    builtin's arithmetic as its README describes it: 8-lane sign-extend, convert,
+    FMA) over the synthetic KV prefix of `start` positions: n_tokens of them, or
+    with `seconds` as many as fit (at least n_min); returns (seconds per token, ids)."""
+    O, om, _ = oracle_model(pkg, plan)
     O.set_threads(threads)
-    t0 = time.time()
-    om = O.OracleModel(plan, O.synth_tensors(plan, seed=0), threads=threads)
-    setup_s = time.time() - t0
+    om.threads = threads
+    times, ids, tok = [], [], 1
+    t_end = time.time() + seconds if seconds else None
+    with O.matvec_mode(O.MATVEC_F32ACC):
+        om.reset()
+        om.fill_kv(start, seed=1)
+        for i in range(n_tokens):
+            if t_end and i >= n_min and time.time() > t_end:
+                break
+            if om.count >= plan["max_seq"]:
+                om.reset()
+                om.fill_kv(start, seed=1)
+            t0 = time.perf_counter()
+            tok, _ = om.step(tok)
+            times.append(time.perf_counter() - t0)
+            ids.append(tok)
+    return times, ids
+
+
+def cpu_baseline(pkg, plan, seconds):
+    """Reported CPU baseline: the oracle on all host cores (as many tokens as fit in
+    `seconds`, at least 2) and on one core (2 tokens, how the reference's decoder
+    runs: it has no threads)."""
+    threads = os.cpu_count() or 1
     P = pkg.synth.CONFIGS[CONFIG]["prompt"] if plan["max_seq"] > 512 else plan["max_seq"] // 2
-    om.fill_kv(P, seed=1)
-    tok = 1
-    n = 0
-    t0 = time.time()
-    while n < 2 or (time.time() - t0 < seconds and om.count < plan["max_seq"]):
-        tok, _ = om.step(tok)
-        n += 1
-    dt = time.time() - t0
-    return {"value": n / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"{n} greedy decode tokens at positions {P}..{P + n - 1} of the same "
-                      f"synthetic model (KV prefix synthetic), {threads} host threads; "
-                      f"weight generation {setup_s:.1f} s untimed"}
+    _, _, setup_s = oracle_model(pkg, plan)
+    times, _ = cpu_decode(pkg, plan, plan["max_seq"] - P, threads, P, seconds=seconds)
+    t1, _ = cpu_decode(pkg, plan, 2, 1, P)
+    return {"value": len(times) / sum(times), "unit": "tokens/s", "cores": threads, "kind": "port",
+            "single_thread": {"value": len(t1) / sum(t1), "unit": "tokens/s", "cores": 1},
+            "cpu": cpu_model(),
+            "sample": f"{len(times)} greedy decode tokens (positions {P}..) of the same synthetic model "
+                      f"over a synthetic KV prefix, int8 matvec as f32 8-lane FMA accumulation, "
+                      f"{threads} host threads; single_thread: 2 tokens on 1 thread; "
+                      f"host weight generation {setup_s:.1f} s untimed"}
 
 
 def run_reference(args):
+    """The reference arm: the oracle (CPU restatement of the reference decode path;
+    the reference's own `aric` toolchain is not installable here) on the host
+    cores, all threads. One step = one greedy decode token at positions 512.. of
+    the Llama-2-7B workload; W untimed steps, then K timed steps."""
     rank, _, world = env_rank()
     if rank != 0:
         return 0
     pkg = importlib.import_module("aricode-ml_b200")
     plan = pkg.synth.config_plan(args.config, n_layers=args.layers)
-    cb = cpu_baseline(pkg, plan, seconds=max(args.cpu_seconds, 10.0))
-    line = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tokens/s",
-            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1000.0 * 256 / cb["value"], "higher_is_better": True,
+    threads = os.cpu_count() or 1
+    P = pkg.synth.CONFIGS[args.config]["prompt"]
+    _, _, setup_s = oracle_model(pkg, plan)
+    times, ids = cpu_decode(pkg, plan, args.warmup + args.steps, threads, P)
+    timed = times[args.warmup:]
+    value = len(timed) / sum(timed)
+    t1, _ = cpu_decode(pkg, plan, 2, 1, P)
+    cb = {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "cpu": cpu_model(),
+          "single_thread": {"value": len(t1) / sum(t1), "unit": "tokens/s", "cores": 1},
+          "sample": f"{args.steps} timed greedy decode tokens (after {args.warmup} untimed) at positions "
+                    f"{P}.. over a synthetic KV prefix, int8 matvec as f32 8-lane FMA accumulation, "
+                    f"{threads} host threads; single_thread: 2 tokens on 1 thread; host weight "
+                    f"generation {setup_s:.1f} s untimed"}
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s",
+            "n_gpus": args.gpus, "device": "host CPU (no GPU used)",
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000.0 * sum(timed) / len(timed), "step": "one decode token",
+            "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "int8 x f32", "data": "synthetic",
             "config": workload_config(args, plan),
-            "cpu_baseline": cb,
-            "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+            "cpu_baseline": cb, "tokens_head": ids[:8],
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -182,7 +246,6 @@ def main():
     args = parse()
     if args.impl == "reference":
         return run_reference(args)
-    import numpy as np
     import torch
     rank, local_rank, world = env_rank()
     torch.cuda.set_device(local_rank)
@@ -284,7 +347,8 @@ def main():
         "decode_ms_per_token": ms / toks, "prefill_s_untimed": prefill_s,
         "tokens_head": ids[:8],
     }
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if world == 1 and not args.no_cpu_baseline:
+        out["oracle_check"] = oracle_check(pkg, dec, plan, P)
         out["cpu_baseline"] = cpu_baseline(pkg, plan, args.cpu_seconds)
     if dist:
         dist.barrier()              # no rank frees its exchange buffer while a peer may still use it
@@ -295,6 +359,30 @@ def main():
     if rank == 0:
         print(json.dumps(out), flush=True)
     return 0
+
+
+def oracle_check(pkg, dec, plan, P, n=8):
+    """Outside the timed region: decode n tokens on the GPU and in the oracle's exact
+    mode from the same synthetic KV prefix of P positions; ids and logits must be
+    bit-identical."""
+    O, om, _ = oracle_model(pkg, plan)
+    O.set_threads(os.cpu_count() or 1)
+    om.threads = os.cpu_count() or 1
+    om.reset()
+    om.fill_kv(P, seed=1)
+    dec.fill_kv_synthetic(P, seed=1)
+    tok_g = tok_o = 1
+    ids_g, ids_o, same = [], [], True
+    for _ in range(n):
+        tok_g, lg = dec.step(tok_g, want_logits=True)
+        tok_o, lo = om.step(tok_o)
+        ids_g.append(tok_g)
+        ids_o.append(tok_o)
+        same = same and bool(np.array_equal(lg, lo))
+    ok = same and ids_g == ids_o
+    assert ok, f"GPU decode differs from the oracle: {ids_g} vs {ids_o}"
+    return {"ids": ids_g, "logits_bit_identical": same, "positions": f"{P}..{P + n - 1}",
+            "what": "GPU vs oracle (exact mode) from the same synthetic KV prefix"}
 
 
 def time_gemv(torch, rt, plan, stream, reps=3):

@@ -106,6 +106,15 @@ int b2_generate(b2_ctx* ctx, const int32_t* prompt, int n_prompt, int max_new, i
  * token fed at pos), then enqueue n decode steps whose argmax feeds the next
  * step. Both only enqueue work on the context's stream. */
 int b2_set_position(b2_ctx* ctx, int pos, int32_t next_tok);
+
+/* Fill KV rows [0, count) of every attention sub-block with synthetic values and
+ * set the position to count: value of element ((kv_head * max_seq + pos) * d_head
+ * + i) of sub-block b (index in the plan's block list) is the synthetic generator's
+ * value for (seed, tensor 0xC0DE0000 + 2b for K / + 2b + 1 for V, that index,
+ * std 1). Lets a test or benchmark start decoding mid-sequence with the same
+ * cache as the oracle's b2o_state_fill_kv, without a prefill. No reference
+ * counterpart. */
+int b2_fill_kv_synthetic(b2_ctx* ctx, int count, uint64_t seed);
 int b2_decode_async(b2_ctx* ctx, int n_steps);
 int b2_sync(b2_ctx* ctx);
 int b2_read_output(b2_ctx* ctx, int32_t* ids, int max_ids, int* n_ids);
@@ -168,8 +177,10 @@ int b2_attn_decode(const float* q, const float* K, const float* V, float* out, i
  * exit; problems needing more scratch than that (n_heads * ceil(max_seq/64) *
  * (d_head+2) * 4 + n_kv_heads * 4 bytes) return B2_E_INVALID, with the reason in
  * b2_last_error(NULL, ...). The first call on a device looks the array up on that
- * device, so make it before any stream capture. All calls share the array: calls
- * that overlap on the GPU race. Allocates nothing. */
+ * device, so make it before any stream capture; the address found there is kept
+ * for the life of the process, so a host that resets the device (cudaDeviceReset)
+ * must not call this entry point on that device afterwards. All calls share the
+ * array: calls that overlap on the GPU race. Allocates nothing. */
 #define B2_ATTN_STATIC_SCRATCH_BYTES (4u << 20)
 int b2_attn_decode_static(const float* q, const float* K, const float* V, float* out,
                           int n_heads, int n_kv_heads, int d_head, int n, int max_seq,

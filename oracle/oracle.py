@@ -109,6 +109,12 @@ def _declare(L):
     L.b2o_state_fill_kv.argtypes = [C.POINTER(Model), C.POINTER(State), C.c_int, C.c_uint64]
     L.b2o_set_threads.argtypes = [C.c_int]
     L.b2o_get_threads.restype = C.c_int
+    L.b2o_set_matvec_mode.argtypes = [C.c_int]
+    L.b2o_get_matvec_mode.restype = C.c_int
+    L.b2o_dot_i8_f32acc.restype = C.c_float
+    L.b2o_dot_i8_f32acc.argtypes = [i8p, f32p, C.c_int64]
+    L.b2o_dot_i8_f64.restype = C.c_double
+    L.b2o_dot_i8_f64.argtypes = [i8p, f32p, C.c_int64]
 
 
 def _p(a, t=f32p):
@@ -122,6 +128,38 @@ def _c(a, dt):
 # ------------------------------------------------------------------ kernels (numpy in/out)
 def set_threads(n):
     lib().b2o_set_threads(int(n))
+
+
+MATVEC_EXACT, MATVEC_F32ACC, MATVEC_F64 = 0, 1, 2
+
+
+class matvec_mode:
+    """Context manager: the int8 matvec the oracle uses inside the block —
+    MATVEC_EXACT (fixed-point dot, the GPU's bits), MATVEC_F32ACC (8-lane f32 FMA
+    accumulation, the reference builtin as README.md:128-131 describes it) or
+    MATVEC_F64 (f64 accumulation, the truth model for the matvec)."""
+
+    def __init__(self, mode):
+        self.mode = mode
+
+    def __enter__(self):
+        self.old = lib().b2o_get_matvec_mode()
+        lib().b2o_set_matvec_mode(self.mode)
+        return self
+
+    def __exit__(self, *exc):
+        lib().b2o_set_matvec_mode(self.old)
+        return False
+
+
+def dot_i8_f32acc(w, x):
+    w = _c(w, np.int8); x = _c(x, np.float32)
+    return np.float32(lib().b2o_dot_i8_f32acc(_p(w, i8p), _p(x), w.size))
+
+
+def dot_i8_f64(w, x):
+    w = _c(w, np.int8); x = _c(x, np.float32)
+    return lib().b2o_dot_i8_f64(_p(w, i8p), _p(x), w.size)
 
 
 def exp_f(x):

@@ -12,6 +12,9 @@
 
 #include <math.h>
 #include <pthread.h>
+#if defined(__AVX2__) && defined(__FMA__)
+#include <immintrin.h>
+#endif
 #include <stdlib.h>
 #include <string.h>
 
@@ -277,35 +280,106 @@ float b2o_dot_f32(const float* w, const float* x, int64_t n) {
     return reduce256(part);
 }
 
+/* ------------------------------------------------------------------------
+ * Two more restatements of the int8 matvec, used to measure how far the exact
+ * fixed-point dot above (the one the GPU reproduces bit for bit) sits from the
+ * reference's own arithmetic and from a high-precision truth:
+ *
+ *  - f32 accumulation as README.md:128-131 describes the builtin
+ *    arr_i8_matvec_f32(_perrow): 8 codes sign-extended (vpmovsxbd), converted to
+ *    f32 (vcvtdq2ps), one vfmadd231ps per 8 lanes into one accumulator vector,
+ *    lane l holding the elements 8b + l. The builtin's source (codegen_builtins.c
+ *    of the aric compiler) is not in the reference tree, so its horizontal sum
+ *    and tail handling are restated in the usual AVX2 form: fold the upper 128
+ *    bits onto the lower (l, l+4), then the upper 64 (l, l+2), then the odd lane,
+ *    i.e. ((a0+a4)+(a2+a6)) + ((a1+a5)+(a3+a7)); the n % 8 tail elements follow
+ *    one by one with fmaf. Then y = dot * scale.
+ *  - f64 accumulation: every product and sum in double, rounded to f32 once
+ *    after the scale (truth model for the matvec; everything else in the model
+ *    keeps the reference's f32 arithmetic).
+ *
+ * b2o_set_matvec_mode selects which one b2o_gemv_i8 and the whole-model step
+ * use: 0 the fixed-point dot (default), 1 f32 accumulation, 2 f64. Mode 2 also
+ * takes the f32-weight projections in f64.
+ * ------------------------------------------------------------------------ */
+static int g_matvec_mode = 0;
+void b2o_set_matvec_mode(int mode) { g_matvec_mode = (mode >= 0 && mode <= 2) ? mode : 0; }
+int  b2o_get_matvec_mode(void) { return g_matvec_mode; }
+
+float b2o_dot_i8_f32acc(const int8_t* w, const float* x, int64_t n) {
+    float a[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+    const int64_t n8 = n / 8 * 8;
+#if defined(__AVX2__) && defined(__FMA__)
+    /* the described instruction sequence itself: vpmovsxbd, vcvtdq2ps, vfmadd231ps */
+    __m256 acc = _mm256_setzero_ps();
+    for (int64_t b = 0; b < n8; b += 8) {
+        const __m256i wi = _mm256_cvtepi8_epi32(_mm_loadl_epi64((const __m128i*)(w + b)));
+        acc = _mm256_fmadd_ps(_mm256_cvtepi32_ps(wi), _mm256_loadu_ps(x + b), acc);
+    }
+    _mm256_storeu_ps(a, acc);
+#else
+    for (int64_t b = 0; b < n8; b += 8)
+        for (int l = 0; l < 8; ++l) a[l] = fmaf((float)w[b + l], x[b + l], a[l]);
+#endif
+    float t = ((a[0] + a[4]) + (a[2] + a[6])) + ((a[1] + a[5]) + (a[3] + a[7]));
+    for (int64_t i = n8; i < n; ++i) t = fmaf((float)w[i], x[i], t);
+    return t;
+}
+
+double b2o_dot_i8_f64(const int8_t* w, const float* x, int64_t n) {
+    double t = 0.0;
+    for (int64_t i = 0; i < n; ++i) t += (double)w[i] * (double)x[i];
+    return t;
+}
+
+static double dot_f32_f64(const float* w, const float* x, int64_t n) {
+    double t = 0.0;
+    for (int64_t i = 0; i < n; ++i) t += (double)w[i] * (double)x[i];
+    return t;
+}
+
 typedef struct {
     const void* W; int64_t ld; const float* scale; const float* x; int64_t n; float* y;
-    const int32_t* X; int S;
+    const int32_t* X; int S; int mode;
 } gemv_ctx;
 
 static void gemv_i8_range(void* c, int64_t r0, int64_t r1) {
     const gemv_ctx* g = (const gemv_ctx*)c;
     const int8_t* W = (const int8_t*)g->W;
-    for (int64_t r = r0; r < r1; ++r) g->y[r] = b2o_dot_i8x(W + r * g->ld, g->X, g->n, g->S) * g->scale[r];
+    if (g->mode == 1)
+        for (int64_t r = r0; r < r1; ++r) g->y[r] = b2o_dot_i8_f32acc(W + r * g->ld, g->x, g->n) * g->scale[r];
+    else if (g->mode == 2)
+        for (int64_t r = r0; r < r1; ++r)
+            g->y[r] = (float)(b2o_dot_i8_f64(W + r * g->ld, g->x, g->n) * (double)g->scale[r]);
+    else
+        for (int64_t r = r0; r < r1; ++r) g->y[r] = b2o_dot_i8x(W + r * g->ld, g->X, g->n, g->S) * g->scale[r];
 }
 static void gemv_f32_range(void* c, int64_t r0, int64_t r1) {
     const gemv_ctx* g = (const gemv_ctx*)c;
     const float* W = (const float*)g->W;
-    for (int64_t r = r0; r < r1; ++r) g->y[r] = b2o_dot_f32(W + r * g->ld, g->x, g->n);
+    if (g->mode == 2)
+        for (int64_t r = r0; r < r1; ++r) g->y[r] = (float)dot_f32_f64(W + r * g->ld, g->x, g->n);
+    else
+        for (int64_t r = r0; r < r1; ++r) g->y[r] = b2o_dot_f32(W + r * g->ld, g->x, g->n);
 }
 
 void b2o_gemv_i8(const int8_t* W, int64_t ld, const float* scale, const float* x,
                  int64_t m, int64_t n, float* y) {
-    int32_t* X = (int32_t*)malloc((size_t)(n > 0 ? n : 1) * sizeof(int32_t));
-    if (!X) abort();
-    const int S = b2o_xfix(x, n, X);
-    gemv_ctx g = {W, ld, scale, x, n, y, X, S};
+    int32_t* X = NULL;
+    int S = 0;
+    if (g_matvec_mode == 0) {
+        X = (int32_t*)malloc((size_t)(n > 0 ? n : 1) * sizeof(int32_t));
+        if (!X) abort();
+        S = b2o_xfix(x, n, X);
+    }
+    gemv_ctx g = {W, ld, scale, x, n, y, X, S, g_matvec_mode};
     parallel_for(m, gemv_i8_range, &g);
     free(X);
 }
 
 void b2o_gemv_f32(const float* W, int64_t ld, const float* x,
                   int64_t m, int64_t n, float* y) {
-    gemv_ctx g = {W, ld, NULL, x, n, y, NULL, 0};
+    gemv_ctx g = {W, ld, NULL, x, n, y, NULL, 0, g_matvec_mode};
     parallel_for(m, gemv_f32_range, &g);
 }
 

@@ -64,6 +64,14 @@ int b2o_xfix(const float* x, int64_t n, int32_t* X);
 float b2o_dot_i8x(const int8_t* w, const int32_t* X, int64_t n, int S);
 /* f32 rows: dot product in the shared order, exposed for tests */
 float b2o_dot_f32(const float* w, const float* x, int64_t n);
+/* int8 rows, for measuring tolerances: f32 8-lane FMA accumulation as the
+ * reference's builtin is described (README.md:128-131), and f64 accumulation */
+float  b2o_dot_i8_f32acc(const int8_t* w, const float* x, int64_t n);
+double b2o_dot_i8_f64(const int8_t* w, const float* x, int64_t n);
+/* which matvec b2o_gemv_i8 / b2o_step use: 0 fixed-point (the GPU's bits, default),
+ * 1 f32 accumulation, 2 f64 accumulation (f32-weight matvecs too) */
+void b2o_set_matvec_mode(int mode);
+int  b2o_get_matvec_mode(void);
 
 /* ---- norms ---- */
 void b2o_rmsnorm(const float* x, const float* g, int d, float eps, float* y);

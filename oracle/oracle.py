@@ -109,6 +109,15 @@ def _declare(L):
     L.b2o_state_fill_kv.argtypes = [C.POINTER(Model), C.POINTER(State), C.c_int, C.c_uint64]
     L.b2o_set_threads.argtypes = [C.c_int]
     L.b2o_get_threads.restype = C.c_int
+    L.b2o_lcg_next.restype = C.c_uint32; L.b2o_lcg_next.argtypes = [C.c_uint32]
+    L.b2o_topk_filter.argtypes = [f32p, C.c_int64, C.c_int]
+    L.b2o_sample_temperature.restype = C.c_int32
+    L.b2o_sample_temperature.argtypes = [f32p, C.c_int64, C.c_double, C.c_double]
+    L.b2o_sample.restype = C.c_int32
+    L.b2o_sample.argtypes = [f32p, C.c_int64, C.c_int, C.c_int, C.c_double, C.POINTER(C.c_uint32)]
+    L.b2o_generate_ex.restype = C.c_int
+    L.b2o_generate_ex.argtypes = [C.POINTER(Model), C.POINTER(State), i32p, C.c_int, C.c_int, C.c_int32,
+                                  C.c_int, C.c_int, C.c_double, C.c_uint32, i32p]
     L.b2o_set_matvec_mode.argtypes = [C.c_int]
     L.b2o_get_matvec_mode.restype = C.c_int
     L.b2o_dot_i8_f32acc.restype = C.c_float
@@ -235,6 +244,37 @@ def attn_decode(q, K, V, n_heads, n_kv_heads, d_head, n, max_seq):
     out = np.zeros(n_heads * d_head, np.float32)
     lib().b2o_attn_decode(_p(q), _p(K), _p(V), n_heads, n_kv_heads, d_head, n, max_seq, _p(out))
     return out
+
+
+SAMPLE_GREEDY, SAMPLE_TEMPERATURE, SAMPLE_TOPK = 0, 1, 2
+
+
+def parse_sample(spec):
+    """--sample spec -> (mode, top_k, temperature): greedy | temperature:T | topk:K:T
+    (aricode_pack.py:2035-2065)."""
+    parts = spec.split(":")
+    if parts[0] == "greedy" and len(parts) == 1:
+        return SAMPLE_GREEDY, 0, 0.0
+    if parts[0] == "temperature" and len(parts) == 2:
+        return SAMPLE_TEMPERATURE, 0, float(parts[1])
+    if parts[0] == "topk" and len(parts) == 3:
+        return SAMPLE_TOPK, int(parts[1]), float(parts[2])
+    raise ValueError(f"bad --sample spec {spec!r}")
+
+
+def lcg_next(state):
+    return int(lib().b2o_lcg_next(state & 0xFFFFFFFF))
+
+
+def topk_filter(v, k):
+    v = _c(v, np.float32).copy()
+    lib().b2o_topk_filter(_p(v), v.size, int(k))
+    return v
+
+
+def sample_temperature(v, temperature, unit):
+    v = _c(v, np.float32).copy()
+    return int(lib().b2o_sample_temperature(_p(v), v.size, float(temperature), float(unit))), v
 
 
 def argmax(v):
@@ -364,6 +404,20 @@ class OracleModel:
         r = lib().b2o_step(C.byref(self.model), C.byref(self.state), int(tok),
                            _p(logits) if want_logits else None, 1 if want_logits else 0)
         return int(r), logits
+
+    def generate_sampled(self, prompt, max_new, sample="greedy", seed=20260502, eos=-1):
+        """The reference loop with a --sample spec and an rng seed (the head runs and
+        the rng advances on every step, prompt steps included)."""
+        mode, k, temp = parse_sample(sample)
+        set_threads(self.threads)
+        prompt = np.ascontiguousarray(prompt, np.int32)
+        out = np.zeros(max(max_new, 1), np.int32)
+        n = lib().b2o_generate_ex(C.byref(self.model), C.byref(self.state), _p(prompt, i32p),
+                                  prompt.size, max_new, int(eos), mode, k, temp, seed & 0xFFFFFFFF,
+                                  _p(out, i32p))
+        if n < 0:
+            raise OverflowError("KV cache overflow" if n == -1 else "bad token id")
+        return out[:n].tolist()
 
     def generate(self, prompt, max_new):
         set_threads(self.threads)

@@ -539,6 +539,76 @@ int32_t b2o_argmax(const float* v, int64_t n) {
 }
 
 /* ------------------------------------------------------------------------
+ * Sampling beyond greedy (sampling_f32.ari:31-153, driven by the decoder loop at
+ * aricode_pack.py:2186-2306):
+ *   rng_state = rng_state * 1103515245 + 12345  (32-bit wrap-around), then
+ *   unit = (rng_state & 65535) / 65536.0, advanced once per loop step (prompt
+ *   steps included: the loop evaluates the head and samples on every step);
+ *   topk:K:T first keeps the K largest distinct values (K passes of "largest
+ *   value below the previous one", values below the K-th become -1e6; K <= 0
+ *   keeps only the first maximum, K >= n changes nothing);
+ *   temperature T <= 0 returns the greedy id; otherwise l = f32(l * (1/T)),
+ *   e = exp(l - max) in f64 stored as f32 while the f64 e's are summed in index
+ *   order, p = f32(p * (1/sum)), and the id is the first whose running f64 sum of
+ *   p exceeds unit (n - 1 if none does). The f64 exp is b2o_exp_d (the aric
+ *   compiler's math_exp is not in the reference tree).
+ * ------------------------------------------------------------------------ */
+uint32_t b2o_lcg_next(uint32_t state) { return state * 1103515245u + 12345u; }
+
+void b2o_topk_filter(float* l, int64_t n, int k) {
+    if (k >= n) return;
+    if (k <= 0) {
+        const int32_t best = b2o_argmax(l, n);
+        for (int64_t j = 0; j < n; ++j)
+            if (j != best) l[j] = -1.0e6f;
+        return;
+    }
+    double prev = 1.0e30, kth = (double)l[0];
+    for (int pass = 0; pass < k; ++pass) {
+        double cur = -1.0e30;
+        for (int64_t i = 0; i < n; ++i) {
+            const double v = (double)l[i];
+            if (v < prev && v > cur) cur = v;
+        }
+        kth = cur;
+        prev = cur;
+    }
+    for (int64_t j = 0; j < n; ++j)
+        if ((double)l[j] < kth) l[j] = -1.0e6f;
+}
+
+int32_t b2o_sample_temperature(float* l, int64_t n, double temperature, double unit) {
+    if (temperature <= 0.0) return b2o_argmax(l, n);
+    const double inv_t = 1.0 / temperature;
+    for (int64_t i = 0; i < n; ++i) l[i] = (float)((double)l[i] * inv_t);
+    double mx = (double)l[0];
+    for (int64_t i = 1; i < n; ++i)
+        if ((double)l[i] > mx) mx = (double)l[i];
+    double sum = 0.0;
+    for (int64_t i = 0; i < n; ++i) {
+        const double e = b2o_exp_d((double)l[i] - mx);
+        l[i] = (float)e;
+        sum = sum + e;
+    }
+    const double inv_sum = 1.0 / sum;
+    for (int64_t i = 0; i < n; ++i) l[i] = (float)((double)l[i] * inv_sum);
+    double cum = 0.0;
+    for (int64_t i = 0; i < n; ++i) {
+        cum = cum + (double)l[i];
+        if (cum > unit) return (int32_t)i;
+    }
+    return (int32_t)(n - 1);
+}
+
+int32_t b2o_sample(float* l, int64_t n, int mode, int top_k, double temperature, uint32_t* rng) {
+    if (mode == B2O_SAMPLE_GREEDY) return b2o_argmax(l, n);
+    if (mode == B2O_SAMPLE_TOPK) b2o_topk_filter(l, n, top_k);
+    *rng = b2o_lcg_next(*rng);
+    const double unit = (double)(int32_t)(*rng & 65535u) / 65536.0;
+    return b2o_sample_temperature(l, n, temperature, unit);
+}
+
+/* ------------------------------------------------------------------------
  * Synthetic weights: splitmix64 of a (seed, tensor, index) key; four 16-bit
  * uniforms summed (Irwin-Hall(4), centred) and scaled to the requested std.
  * Integer maths + one f32 multiply, so the GPU generator is bit-identical.
@@ -757,6 +827,28 @@ int32_t b2o_step(const b2o_model* m, b2o_state* s, int32_t tok, float* logits, i
     proj(&m->lm, m->lm_b, s->h, m->vocab, d, s->logits);
     if (logits) memcpy(logits, s->logits, sizeof(float) * (size_t)m->vocab);
     return b2o_argmax(s->logits, m->vocab);
+}
+
+int b2o_generate_ex(const b2o_model* m, b2o_state* s, const int32_t* prompt, int n_prompt,
+                    int max_new, int32_t eos, int mode, int top_k, double temperature, uint32_t seed,
+                    int32_t* out_ids) {
+    if (n_prompt <= 0) return 0;
+    const int total = n_prompt + max_new - 1;
+    uint32_t rng = seed;
+    int32_t cur = 0;
+    int n_out = 0;
+    for (int t = 0; t < total; ++t) {
+        if (t < n_prompt) cur = prompt[t];
+        const int32_t r = b2o_step(m, s, cur, NULL, 1);
+        if (r < 0) return r == -1 ? -1 : -2;
+        const int32_t nxt = b2o_sample(s->logits, m->vocab, mode, top_k, temperature, &rng);
+        if (t >= n_prompt - 1) {
+            if (eos >= 0 && nxt == eos) break;
+            out_ids[n_out++] = nxt;
+        }
+        cur = nxt;
+    }
+    return n_out;
 }
 
 int b2o_generate(const b2o_model* m, b2o_state* s, const int32_t* prompt, int n_prompt,

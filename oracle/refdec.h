@@ -90,8 +90,15 @@ void b2o_attn_decode(const float* q, const float* Kc, const float* Vc,
                      int n_heads, int n_kv_heads, int d_head, int n, int max_seq,
                      float* out);
 
-/* ---- greedy sampling ---- */
+/* ---- sampling ---- */
 int32_t b2o_argmax(const float* v, int64_t n);
+enum { B2O_SAMPLE_GREEDY = 0, B2O_SAMPLE_TEMPERATURE = 1, B2O_SAMPLE_TOPK = 2 };
+uint32_t b2o_lcg_next(uint32_t state);
+/* sample_topk_filter_f32 / sample_temperature_f32 (in place, like the reference) */
+void    b2o_topk_filter(float* logits, int64_t n, int k);
+int32_t b2o_sample_temperature(float* logits, int64_t n, double temperature, double unit);
+/* one loop step's choice: greedy, or advance *rng and sample (logits overwritten) */
+int32_t b2o_sample(float* logits, int64_t n, int mode, int top_k, double temperature, uint32_t* rng);
 
 /* ---- synthetic weights (counter-based, identical on the GPU) ---- */
 float b2o_synth_value(uint64_t seed, uint64_t tensor_id, uint64_t index, float stdv);
@@ -163,6 +170,13 @@ int32_t b2o_step(const b2o_model* m, b2o_state* s, int32_t tok, float* logits, i
  * emit argmax for t >= P-1). Returns number of ids written, or -1 on overflow. */
 int b2o_generate(const b2o_model* m, b2o_state* s, const int32_t* prompt, int n_prompt,
                  int max_new, int32_t* out_ids);
+
+/* The reference loop with a sampler (the head runs and the rng advances on every
+ * step, prompt steps included) and an EOS id (eos < 0: none; generation stops
+ * before emitting it). Returns ids written, -1 on overflow, -2 on a bad id. */
+int b2o_generate_ex(const b2o_model* m, b2o_state* s, const int32_t* prompt, int n_prompt,
+                    int max_new, int32_t eos, int mode, int top_k, double temperature, uint32_t seed,
+                    int32_t* out_ids);
 
 /* worker threads for matvecs/attention (pthreads); 1 = single-threaded like the reference */
 void b2o_set_threads(int n);

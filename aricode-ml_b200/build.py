@@ -20,6 +20,7 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 OBJ = CSRC / "_obj"
 LIB = PKG / "libb2dec.so"
+FRONT = PKG / "b2run"                    # stdin-tokens front end (host program over the library)
 SOURCES = ["runtime.cu", "launch.cu", "token.cu", "capi.cu", "noalloc.cu"]
 HEADERS = ["b2_common.cuh", "gemv.cuh", "attn.cuh", "kernels.cuh", "token.cuh", "json.h"]
 
@@ -53,7 +54,7 @@ def _stale_obj(src, hdr_t):
 
 
 def stale():
-    if not LIB.exists():
+    if not LIB.exists() or not FRONT.exists() or FRONT.stat().st_mtime < (CSRC / "b2run.cpp").stat().st_mtime:
         return True
     hdr_t = _deps_time()
     t = LIB.stat().st_mtime
@@ -84,7 +85,18 @@ def build(force=False, verbose=False):
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError("nvcc link failed:\n" + r.stdout + r.stderr)
+    build_front()
     return LIB
+
+
+def build_front():
+    """The stdin-tokens front end, a host program linked against libb2dec.so."""
+    cmd = ["g++", "-O2", "-std=c++17", "-Wall", str(CSRC / "b2run.cpp"), "-o", str(FRONT),
+           "-L" + str(PKG), "-lb2dec", "-Wl,-rpath,$ORIGIN"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError("g++ failed on b2run.cpp:\n" + r.stdout + r.stderr)
+    return FRONT
 
 
 if __name__ == "__main__":

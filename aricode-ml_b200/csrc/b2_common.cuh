@@ -235,7 +235,8 @@ struct StepState {
     int active;        // 0 once the generation finished (EOS / limit) or failed
     int eos;           // -1: none
     int err;           // B2_DEV_ERR_*
-    int pad[7];
+    unsigned rng;      // sampling: LCG state before this step's advance
+    int pad[6];
 };
 
 // ------------------------------------------------------------------ tensor parallelism

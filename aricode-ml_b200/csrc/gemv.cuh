@@ -92,6 +92,7 @@ struct GemvParams {
     int row_base;
     int tp_rank, tp_size;
     const unsigned* tp_seq;    // token-kernel launches completed (the flags' epochs)
+    int defer_tok;             // EPI_ARGMAX: a sampler kernel chooses the token (no step bookkeeping here)
     float* tp_cval;
     int* tp_cidx;
     int* tp_cnan;
@@ -953,7 +954,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, int r0, int r
             }
             if (v0nan) tok = 0;                                    // sequential scan keeps index 0
             if (p.out_tok) *p.out_tok = tok;
-            if (p.st) {
+            if (p.st && !p.defer_tok) {
                 StepState* st = p.st;
                 st->next_tok = tok;
                 if (pos >= st->prompt_len - 1) {

@@ -85,6 +85,182 @@ static __global__ void set_state_kernel(StepState* st, int step, int prompt_len,
     st->err = 0;
 }
 
+// ------------------------------------------------------------------ sampling
+// Sampling beyond greedy, one step (sampling_f32.ari:31-153 as the decoder loop
+// calls it, aricode_pack.py:2291-2306; oracle b2o_sample): advance the step's
+// LCG, optionally keep the top-k distinct logits, then temperature softmax and
+// an inverse-CDF draw. Runs after the LM head (which wrote the logits and left
+// the token choice to this kernel) as one CTA; the two f64 running sums are
+// sequential on one thread, as in the reference (their rounding order is the
+// result), with their inputs loaded in batches.
+enum SampleMode : int { SAMPLE_GREEDY = 0, SAMPLE_TEMPERATURE = 1, SAMPLE_TOPK = 2 };
+constexpr int kSampleThreads = 1024;
+
+struct SampleParams {
+    float* logits;          // [vocab], overwritten (filtered, then probabilities)
+    double* e;              // [vocab] scratch: the unrounded f64 exponentials
+    int vocab;
+    int mode, top_k;
+    double temperature;
+    StepState* st;
+    int* out_ids;
+};
+
+// first index of the maximum, NaN never wins, logits[0] NaN -> 0 (sample_greedy_f32)
+__device__ __forceinline__ int sample_block_argmax(const float* l, int n, float* wv, int* wi) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float bv = 0.0f;
+    int bi = 0x7fffffff;
+    for (int i = tid; i < n; i += kSampleThreads) {
+        const float v = l[i];
+        if (bi == 0x7fffffff || amax_better(v, i, bv, bi)) { bv = v; bi = i; }
+    }
+    for (int s = 16; s >= 1; s >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, s);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, s);
+        if (oi != 0x7fffffff && (bi == 0x7fffffff || amax_better(ov, oi, bv, bi))) { bv = ov; bi = oi; }
+    }
+    if (lane == 0) { wv[warp] = bv; wi[warp] = bi; }
+    __syncthreads();
+    float cv = 0.0f;
+    int ci = 0x7fffffff;
+    for (int w = 0; w < kSampleThreads / 32; ++w)
+        if (wi[w] != 0x7fffffff && (ci == 0x7fffffff || amax_better(wv[w], wi[w], cv, ci))) { cv = wv[w]; ci = wi[w]; }
+    __syncthreads();
+    const float v0 = l[0];
+    return (v0 != v0 || ci == 0x7fffffff) ? 0 : ci;
+}
+
+// largest f64 value of the logits strictly below `below` (or -1e30): one top-k pass
+__device__ __forceinline__ double sample_block_max_below(const float* l, int n, double below, double* wd) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    double cur = -1.0e30;
+    for (int i = tid; i < n; i += kSampleThreads) {
+        const double v = (double)l[i];
+        if (v < below && v > cur) cur = v;
+    }
+    for (int s = 16; s >= 1; s >>= 1) cur = fmax(cur, __shfl_xor_sync(0xffffffffu, cur, s));
+    if (lane == 0) wd[warp] = cur;
+    __syncthreads();
+    double r = -1.0e30;
+    for (int w = 0; w < kSampleThreads / 32; ++w) r = fmax(r, wd[w]);
+    __syncthreads();
+    return r;
+}
+
+static __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const __grid_constant__ SampleParams p) {
+    __shared__ float wv[kSampleThreads / 32];
+    __shared__ int wi[kSampleThreads / 32];
+    __shared__ double wd[kSampleThreads / 32];
+    __shared__ double s_mx, s_inv;
+    __shared__ int s_tok;
+    StepState* st = p.st;
+    if (!*(volatile int*)&st->active || *(volatile int*)&st->err) return;
+    const int tid = threadIdx.x, n = p.vocab;
+    float* l = p.logits;
+    const unsigned rng = *(volatile unsigned*)&st->rng * 1103515245u + 12345u;
+    const double unit = ddiv((double)(int)(rng & 65535u), 65536.0);
+    if (p.mode == SAMPLE_TOPK && p.top_k < n) {
+        if (p.top_k <= 0) {
+            const int best = sample_block_argmax(l, n, wv, wi);
+            for (int j = tid; j < n; j += kSampleThreads)
+                if (j != best) l[j] = -1.0e6f;
+        } else {
+            double prev = 1.0e30, kth = 0.0;
+            for (int pass = 0; pass < p.top_k; ++pass) {
+                kth = sample_block_max_below(l, n, prev, wd);
+                prev = kth;
+            }
+            for (int j = tid; j < n; j += kSampleThreads)
+                if ((double)l[j] < kth) l[j] = -1.0e6f;
+        }
+        __syncthreads();
+    }
+    int tok;
+    if (p.temperature <= 0.0) {
+        tok = sample_block_argmax(l, n, wv, wi);
+    } else {
+        const double inv_t = ddiv(1.0, p.temperature);
+        for (int i = tid; i < n; i += kSampleThreads) l[i] = __double2float_rn(dmul((double)l[i], inv_t));
+        __syncthreads();
+        // max with the reference's scan semantics: l[0] NaN stays NaN, later NaNs never win
+        {
+            double cur = -__longlong_as_double(0x7ff0000000000000ll);
+            for (int i = tid; i < n; i += kSampleThreads) {
+                const double v = (double)l[i];
+                if (v > cur) cur = v;
+            }
+            for (int s = 16; s >= 1; s >>= 1) cur = fmax(cur, __shfl_xor_sync(0xffffffffu, cur, s));
+            if ((tid & 31) == 0) wd[tid >> 5] = cur;
+            __syncthreads();
+            if (tid == 0) {
+                double r = wd[0];
+                for (int w = 1; w < kSampleThreads / 32; ++w) r = fmax(r, wd[w]);
+                const double v0 = (double)l[0];
+                s_mx = v0 != v0 ? v0 : r;
+            }
+            __syncthreads();
+        }
+        const double mx = s_mx;
+        for (int i = tid; i < n; i += kSampleThreads) {
+            const double e = exp_d(__dsub_rn((double)l[i], mx));
+            p.e[i] = e;
+            l[i] = __double2float_rn(e);
+        }
+        __syncthreads();
+        if (tid == 0) {
+            double sum = 0.0;
+            int i = 0;
+            for (; i + 16 <= n; i += 16) {
+                double b[16];
+#pragma unroll
+                for (int u = 0; u < 16; ++u) b[u] = p.e[i + u];
+#pragma unroll
+                for (int u = 0; u < 16; ++u) sum = dadd(sum, b[u]);
+            }
+            for (; i < n; ++i) sum = dadd(sum, p.e[i]);
+            s_inv = ddiv(1.0, sum);
+        }
+        __syncthreads();
+        const double inv_sum = s_inv;
+        for (int i = tid; i < n; i += kSampleThreads) l[i] = __double2float_rn(dmul((double)l[i], inv_sum));
+        __syncthreads();
+        if (tid == 0) {
+            double cum = 0.0;
+            int found = n - 1;
+            bool done = false;
+            for (int i = 0; i < n && !done; i += 16) {
+                float b[16];
+#pragma unroll
+                for (int u = 0; u < 16; ++u) b[u] = i + u < n ? l[i + u] : 0.0f;
+#pragma unroll
+                for (int u = 0; u < 16; ++u) {
+                    if (!done && i + u < n) {
+                        cum = dadd(cum, (double)b[u]);
+                        if (cum > unit) { found = i + u; done = true; }
+                    }
+                }
+            }
+            s_tok = found;
+        }
+        __syncthreads();
+        tok = s_tok;
+    }
+    if (tid == 0) {
+        st->rng = rng;
+        st->next_tok = tok;
+        if (st->pos >= st->prompt_len - 1) {
+            if (st->eos >= 0 && tok == st->eos) {
+                st->active = 0;                          // EOS is not emitted
+            } else {
+                p.out_ids[st->n_out] = tok;
+                st->n_out += 1;
+                if (st->n_out >= st->max_new) st->active = 0;
+            }
+        }
+    }
+}
+
 // ------------------------------------------------------------------ standalone ops
 // 256-thread block; same reduction pattern as the GEMV prologue / oracle reduce256
 __device__ __forceinline__ float block_reduce256(float part, float* red) {

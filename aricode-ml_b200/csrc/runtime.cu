@@ -189,6 +189,11 @@ struct b2_ctx {
     float* tp_cval = nullptr;      // [kMaxRanks] each rank's best logit
     int* tp_cidx = nullptr;
     int* tp_cnan = nullptr;
+    // sampling beyond greedy (b2_set_sampling): a sampler kernel follows the LM head
+    int samp_mode = 0, samp_k = 0;
+    double samp_t = 0.0;
+    unsigned seed = 0, rng = 0;    // rng: LCG state before the next step's advance
+    double* samp_e = nullptr;
 
     ~b2_ctx() {
         if (device >= 0) cudaSetDevice(device);
@@ -436,6 +441,16 @@ void assemble(b2_ctx* c, const b2json::Value& plan) {
         }
         c->blocks.push_back(B);
     }
+    if (plan.has("generation")) {                 // --sample / --rng-seed of the packer
+        const b2json::Value& g = plan["generation"];
+        if (g.has("sample_mode")) c->samp_mode = (int)g["sample_mode"].as_int();
+        if (g.has("top_k")) c->samp_k = (int)g["top_k"].as_int();
+        if (g.has("temperature")) c->samp_t = g["temperature"].as_num();
+        if (g.has("rng_seed") && !g["rng_seed"].is_null()) c->seed = (unsigned)(long long)g["rng_seed"].as_num();
+        c->rng = c->seed;
+        if (c->samp_mode < 0 || c->samp_mode > 2) throw Err(B2_E_FORMAT, "unknown sample mode in the plan");
+        if (c->samp_mode && c->tp_size > 1) throw Err(B2_E_UNSUPPORTED, "sampling needs every logit on one GPU");
+    }
     c->fnorm = c->norm_of(plan["final_norm"]);
     if (c->vocab % c->tp_size) throw Err(B2_E_UNSUPPORTED, "vocab does not split over the ranks");
     c->lm = c->mat(plan["lm_head"]["W"].as_str(), c->vocab / c->tp_size, c->d);
@@ -490,6 +505,7 @@ void assemble(b2_ctx* c, const b2json::Value& plan) {
     const size_t i_st = add(sizeof(StepState));
     const size_t i_prompt = add((size_t)c->max_seq * 4);
     const size_t i_out = add((size_t)c->max_seq * 4);
+    const size_t i_samp = add((size_t)c->vocab * 8);
     c->work_bytes = off;
     if (cudaMalloc(&c->d_work, c->work_bytes) != cudaSuccess) throw Err(B2_E_OOM, "workspace allocation failed");
     CK(cudaMemsetAsync(c->d_work, 0, c->work_bytes, c->stream));
@@ -530,6 +546,7 @@ void assemble(b2_ctx* c, const b2json::Value& plan) {
     c->st = reinterpret_cast<StepState*>(w + offs[i_st]);
     c->prompt = reinterpret_cast<int*>(w + offs[i_prompt]);
     c->out_ids = reinterpret_cast<int*>(w + offs[i_out]);
+    c->samp_e = reinterpret_cast<double*>(w + offs[i_samp]);
 
     // RoPE table in f64 via libm, stored f32 (rope_alloc_f32, rope_f32.ari:34-55)
     if (c->rope_dh) {
@@ -668,6 +685,7 @@ std::vector<Op> build_ops(b2_ctx* c, bool with_head) {
         }
         h.amax_val = c->amax_val; h.amax_idx = c->amax_idx; h.amax_v0nan = c->amax_v0nan;
         h.amax_count = c->amax_cnt; h.out_ids = c->out_ids;
+        h.defer_tok = c->samp_mode != 0;
         gemv(h, true);
     }
     return ops;
@@ -682,6 +700,18 @@ int enqueue_step(b2_ctx* c, bool with_head, cudaStream_t s) {
         else CK(launch_gemv(o.g, o.i8, s, c->pdl, c->sm_count));
     }
     return (int)ops.size();
+}
+
+// the sampler after the LM head (sampling modes only); returns kernels launched
+int enqueue_sampler(b2_ctx* c, cudaStream_t s) {
+    if (!c->samp_mode) return 0;
+    SampleParams sp{};
+    sp.logits = c->logits; sp.e = c->samp_e; sp.vocab = c->vocab;
+    sp.mode = c->samp_mode; sp.top_k = c->samp_k; sp.temperature = c->samp_t;
+    sp.st = c->st; sp.out_ids = c->out_ids;
+    sample_kernel<<<1, kSampleThreads, 0, s>>>(sp);
+    CK(cudaGetLastError());
+    return 1;
 }
 
 
@@ -896,6 +926,7 @@ void capture_graphs_once(b2_ctx* c) {
             } else {
                 n = enqueue_step(c, head == 1, c->cap_stream);
             }
+            if (head == 1) n += enqueue_sampler(c, c->cap_stream);
         } catch (...) {
             cudaStreamEndCapture(c->cap_stream, &g);
             if (g) cudaGraphDestroy(g);
@@ -931,6 +962,7 @@ void upload_state(b2_ctx* c, int step, int prompt_len, int max_new, int next_tok
     h.active = 1;
     h.eos = eos;
     h.err = 0;
+    h.rng = c->rng;
     CK(cudaMemcpyAsync(c->st, c->h_st, sizeof(StepState), cudaMemcpyHostToDevice, c->stream));
     clear_tickets(c, c->stream);
 }
@@ -939,6 +971,7 @@ int fetch_state(b2_ctx* c) {
     CK(cudaMemcpyAsync(c->h_st, c->st, sizeof(StepState), cudaMemcpyDeviceToHost, c->stream));
     CK(cudaStreamSynchronize(c->stream));
     c->host_step = c->h_st->step;
+    c->rng = c->h_st->rng;
     if (c->h_st->err == B2_DEV_ERR_KV_OVERFLOW) throw Err(B2_E_KV_OVERFLOW, "KV cache overflow on the device");
     if (c->h_st->err == B2_DEV_ERR_BAD_TOKEN) throw Err(B2_E_INVALID, "token id outside the vocabulary");
     if (c->h_st->err) throw Err(B2_E_DEVICE, "device wait timed out (error word " +
@@ -1227,8 +1260,14 @@ int b2_destroy(b2_ctx* ctx) {
     return B2_OK;
 }
 
+unsigned lcg_advance(unsigned s, long long n) {
+    for (long long i = 0; i < n; ++i) s = s * 1103515245u + 12345u;
+    return s;
+}
+
 int b2_reset(b2_ctx* ctx) {
     return guarded(ctx, [&] {
+        ctx->rng = ctx->seed;
         upload_state(ctx, 0, 0, 0, 0, -1);
         CK(cudaStreamSynchronize(ctx->stream));
         ctx->host_step = 0;
@@ -1263,6 +1302,8 @@ int b2_prefill(b2_ctx* ctx, const int32_t* toks, int n) {
             if (toks[i] < 0 || toks[i] >= ctx->vocab) throw Err(B2_E_INVALID, "token id outside the vocabulary");
         const int t = ctx->host_step;
         if (n) CK(cudaMemcpyAsync(ctx->prompt + t, toks, (size_t)n * 4, cudaMemcpyHostToDevice, ctx->stream));
+        // the reference samples (and advances its generator) on prompt steps too
+        if (ctx->samp_mode) ctx->rng = lcg_advance(ctx->rng, n);
         upload_state(ctx, t, t + n, 1 << 30, 0, -1);
         for (int i = 0; i < n; ++i) CK(cudaGraphLaunch(ctx->g_prefill, ctx->stream));
         fetch_state(ctx);
@@ -1281,6 +1322,10 @@ int b2_generate(b2_ctx* ctx, const int32_t* prompt, int n_prompt, int max_new, i
             if (prompt[i] < 0 || prompt[i] >= ctx->vocab) throw Err(B2_E_INVALID, "token id outside the vocabulary");
         const int np = std::min(n_prompt, ctx->max_seq);
         CK(cudaMemcpyAsync(ctx->prompt, prompt, (size_t)np * 4, cudaMemcpyHostToDevice, ctx->stream));
+        // a new sequence: the generator restarts at the seed and advances once per
+        // prompt step before the first emitted token (the prefill graph runs no head)
+        ctx->rng = ctx->samp_mode ? lcg_advance(ctx->seed, (long long)std::min(n_prompt, ctx->max_seq + 1) - 1)
+                                  : ctx->seed;
         upload_state(ctx, 0, n_prompt, max_new, 0, eos);
         const long long total = (long long)n_prompt + max_new - 1;
         const int steps = (int)std::min<long long>(total, ctx->max_seq);
@@ -1303,6 +1348,23 @@ int b2_set_position(b2_ctx* ctx, int pos, int32_t next_tok) {
         set_state_kernel<<<1, 1, 0, ctx->stream>>>(ctx->st, pos, pos, 1 << 30, next_tok, -1);
         CK(cudaGetLastError());
         ctx->host_step = pos;
+        return B2_OK;
+    });
+}
+
+int b2_set_sampling(b2_ctx* ctx, int mode, int top_k, double temperature, uint32_t seed) {
+    return guarded(ctx, [&] {
+        if (mode < 0 || mode > 2) return B2_E_INVALID;
+        if (mode && ctx->tp_size > 1) throw Err(B2_E_UNSUPPORTED, "sampling needs every logit on one GPU");
+        const bool recapture = mode != ctx->samp_mode || (mode && (top_k != ctx->samp_k || temperature != ctx->samp_t));
+        ctx->samp_mode = mode;
+        ctx->samp_k = top_k;
+        ctx->samp_t = temperature;
+        ctx->seed = seed;
+        ctx->rng = seed;
+        if (recapture) capture_graphs(ctx);
+        upload_state(ctx, ctx->host_step, ctx->host_step, 1 << 30, 0, -1);
+        CK(cudaStreamSynchronize(ctx->stream));
         return B2_OK;
     });
 }

@@ -49,8 +49,8 @@ def load_state_dict(path):
     if suffix == ".safetensors":
         from safetensors.torch import load_file
         return load_file(str(p))
-    raise PackError(f"error: unsupported checkpoint extension '{suffix}'.  "
-                    "Expected .pt, .pth, or .safetensors.")
+    raise PackError(f"cannot load a checkpoint with suffix '{suffix}': give a .pt, .pth or "
+                    ".safetensors file")
 
 
 def _f32(t):
@@ -125,14 +125,19 @@ _POS_CANDIDATES = ["embeddings.position_embeddings.weight", "position_embeddings
 
 def _need_shape(what, arr, shape):
     if tuple(arr.shape) != tuple(shape):
-        raise PackError(f"{what}: shape mismatch.  expected {tuple(shape)}; "
-                        f"got {tuple(arr.shape)}.")
+        raise PackError(f"{what} has shape {tuple(arr.shape)}; the arch JSON implies {tuple(shape)}")
+
+
+def _not_found(what, tried, sd):
+    keys = sorted(sd.keys())
+    sample = ", ".join(keys[:8]) + (f", ... ({len(keys)} keys)" if len(keys) > 8 else "")
+    raise PackError(f"{what} not found in the checkpoint (looked for {', '.join(tried[:4])}"
+                    f"{', ...' if len(tried) > 4 else ''}); checkpoint keys: {sample}")
 
 
 def resolve(arch, sd, keys_template="fc{idx_plus_1}.{kind}"):
     """Arch + state dict -> list of (kind, idx, suffix, W f32, b f32 or None)."""
     keys = expand_keys(keys_template)
-    avail = lambda: sorted(sd.keys())
     out = []
     for kind, idx, args in A.arch_walk(arch):
         if idx is None:
@@ -141,12 +146,10 @@ def resolve(arch, sd, keys_template="fc{idx_plus_1}.{kind}"):
             in_f, out_f = args
             wk, bk = keys(idx, "weight"), keys(idx, "bias")
             if wk not in sd or bk not in sd:
-                raise PackError(f"linear #{idx}: missing '{wk}' or '{bk}' in checkpoint. "
-                                f"Available keys: {avail()}")
+                _not_found(f"weight and bias of linear op {idx} (--keys {keys_template!r})", [wk, bk], sd)
             W, b = _f32(sd[wk]), _f32(sd[bk])
-            if W.shape != (out_f, in_f) or b.shape != (out_f,):
-                raise PackError(f"linear #{idx}: shape mismatch.  expected ({out_f},{in_f}) "
-                                f"+ ({out_f},); got {tuple(W.shape)} + {tuple(b.shape)}.")
+            _need_shape(f"linear op {idx} weight '{wk}'", W, (out_f, in_f))
+            _need_shape(f"linear op {idx} bias '{bk}'", b, (out_f,))
             out.append((kind, idx, "", W, b))
         elif kind == "multi_head_attention_kv":
             _, d, _ = args
@@ -156,24 +159,19 @@ def resolve(arch, sd, keys_template="fc{idx_plus_1}.{kind}"):
                 wk = _first(sd, cw)
                 bk = _first(sd, [c.replace(".weight", ".bias") for c in cw])
                 if wk is None or bk is None:
-                    raise PackError(f"multi_head_attention_kv #{idx}: missing {proj} weight or "
-                                    f"bias.  Tried: {cw[0]} / {cw[3]}.  Available: {avail()}")
+                    _not_found(f"the {proj} projection (weight and bias) of attention op {idx}", cw, sd)
                 W, b = _f32(sd[wk]), _f32(sd[bk])
-                if W.shape != (d, d) or b.shape != (d,):
-                    raise PackError(f"multi_head_attention_kv #{idx} {proj}: shape mismatch.  "
-                                    f"expected ({d},{d}) + ({d},); got {tuple(W.shape)} + "
-                                    f"{tuple(b.shape)}.")
+                _need_shape(f"attention op {idx} {proj} weight '{wk}'", W, (d, d))
+                _need_shape(f"attention op {idx} {proj} bias '{bk}'", b, (d,))
                 out.append((kind, idx, proj, W, b))
         elif kind == "multi_head_attention_gqa_kv":
             for proj, (_, shape, _) in zip("qkvo", A.tensor_specs(kind, args)):
                 cw = _gqa_candidates(idx, proj)
                 wk = _first(sd, cw)
                 if wk is None:
-                    hf = "o_proj" if proj == "o" else f"{proj}_proj"
-                    raise PackError(f"multi_head_attention_gqa_kv #{idx}: missing {hf} weight.  "
-                                    f"Tried: {cw[0]} / {cw[3]}.  Available: {avail()}")
+                    _not_found(f"the {proj} projection weight of GQA attention op {idx}", cw, sd)
                 W = _f32(sd[wk])
-                _need_shape(f"multi_head_attention_gqa_kv #{idx} {proj}", W, shape)
+                _need_shape(f"GQA attention op {idx} {proj} weight '{wk}'", W, shape)
                 out.append((kind, idx, proj, W, None))
         elif kind == "layernorm":
             dim = args[0]
@@ -181,53 +179,46 @@ def resolve(arch, sd, keys_template="fc{idx_plus_1}.{kind}"):
             wk = _first(sd, cw)
             bk = _first(sd, [c.replace(".weight", ".bias") for c in cw])
             if wk is None or bk is None:
-                raise PackError(f"layernorm #{idx}: missing γ / β.  Tried: {cw[0]} / {cw[1]}.  "
-                                f"Available: {avail()}")
+                _not_found(f"the gain and shift of layernorm op {idx}", cw, sd)
             W, b = _f32(sd[wk]), _f32(sd[bk])
-            if W.shape != (dim,) or b.shape != (dim,):
-                raise PackError(f"layernorm #{idx}: shape mismatch.  expected ({dim},) + "
-                                f"({dim},); got {tuple(W.shape)} + {tuple(b.shape)}.")
+            _need_shape(f"layernorm op {idx} gain '{wk}'", W, (dim,))
+            _need_shape(f"layernorm op {idx} shift '{bk}'", b, (dim,))
             out.append((kind, idx, "", W, b))
         elif kind == "rmsnorm":
             dim = args[0]
             cw = _rmsnorm_candidates(idx)
             wk = _first(sd, cw)
             if wk is None:
-                raise PackError(f"rmsnorm #{idx}: missing γ.  Tried: {cw[0]} / {cw[1]} / "
-                                f"{cw[2]}.  Available: {avail()}")
+                _not_found(f"the gain of rmsnorm op {idx}", cw, sd)
             W = _f32(sd[wk])
-            _need_shape(f"rmsnorm #{idx}", W, (dim,))
+            _need_shape(f"rmsnorm op {idx} gain '{wk}'", W, (dim,))
             out.append((kind, idx, "", W, None))
         elif kind == "swiglu_ffn":
             for proj, (_, shape, _) in zip(("gate", "up", "down"), A.tensor_specs(kind, args)):
                 cw = _swiglu_candidates(idx, proj)
                 wk = _first(sd, cw)
                 if wk is None:
-                    raise PackError(f"swiglu_ffn #{idx}: missing {proj}_proj weight.  Tried: "
-                                    f"{cw[0]} / {cw[1]} / {cw[2]}.  Available: {avail()}")
+                    _not_found(f"the {proj} projection of SwiGLU op {idx}", cw, sd)
                 W = _f32(sd[wk])
-                _need_shape(f"swiglu_ffn #{idx} {proj}", W, shape)
+                _need_shape(f"SwiGLU op {idx} {proj} weight '{wk}'", W, shape)
                 out.append((kind, idx, proj, W, None))
         elif kind == "embedding":
             vocab, d, _ = args
             cw = _EMB_CANDIDATES + [f"layers.{idx}.embed.weight"]
             wk = _first(sd, cw)
             if wk is None:
-                raise PackError(f"embedding #{idx}: cannot find weight in checkpoint.  Tried: "
-                                f"{cw[0]} / {cw[1]} / ...  Available: {avail()}")
+                _not_found(f"the token embedding of op {idx}", cw, sd)
             W = _f32(sd[wk])
-            _need_shape(f"embedding #{idx}", W, (vocab, d))
+            _need_shape(f"token embedding '{wk}'", W, (vocab, d))
             out.append((kind, idx, "", W, None))
         elif kind == "positional_embedding":
             max_pos, d, _ = args
             cw = _POS_CANDIDATES + [f"layers.{idx}.pos_embed.weight"]
             wk = _first(sd, cw)
             if wk is None:
-                raise PackError(f"positional_embedding #{idx}: cannot find weight in "
-                                f"checkpoint.  Tried: {cw[0]} / {cw[1]} / ...  Available: "
-                                f"{avail()}")
+                _not_found(f"the positional embedding of op {idx}", cw, sd)
             W = _f32(sd[wk])
-            _need_shape(f"positional_embedding #{idx}", W, (max_pos, d))
+            _need_shape(f"positional embedding '{wk}'", W, (max_pos, d))
             out.append((kind, idx, "", W, None))
         else:
             raise PackError(f"op {kind!r} is not part of the decoder decode path")
@@ -294,11 +285,13 @@ def parse_args(argv=None):
                    default="stdin-tokens")
     p.add_argument("--max-prompt-tokens", type=int, default=512)
     p.add_argument("--input-file")
+    # classifier-only flags of the reference CLI: accepted by the parser so that a
+    # decoder command line parses the same, refused in main() when given
     p.add_argument("--input-images", default=None)
     p.add_argument("--input-labels", default=None)
-    p.add_argument("--n-test", type=int, default=10000)
-    p.add_argument("--mean", type=float, default=0.1307)
-    p.add_argument("--std", type=float, default=0.3081)
+    p.add_argument("--n-test", type=int, default=None)
+    p.add_argument("--mean", type=float, default=None)
+    p.add_argument("--std", type=float, default=None)
     p.add_argument("--no-argmax", action="store_true")
     p.add_argument("--max-new-tokens", type=int, default=16)
     p.add_argument("--sample", default="greedy")
@@ -316,8 +309,8 @@ def parse_args(argv=None):
     p.add_argument("--target", choices=("aric", "b200"), default="b200",
                    help="b200: weight blob + launch plan for the CUDA runtime")
     p.add_argument("--tp", type=int, default=1,
-                   help="tensor-parallel degree for the launch plan (blob stays whole; "
-                        "each rank slices its shard at load)")
+                   help="tensor-parallel degree recorded in the plan (the blob stays whole; "
+                        "each rank slices its rows at load)")
     p.add_argument("--emit-staging", action="store_true",
                    help="also write the reference's per-tensor staging files")
     return p.parse_args(argv)
@@ -325,7 +318,8 @@ def parse_args(argv=None):
 
 def pack(arch, sd, *, keys="fc{idx_plus_1}.{kind}", quantize="int8", int8_attention=False,
          out=None, max_new_tokens=16, sample="greedy", eos_token=None, rng_seed=20260502,
-         tp=1, emit_staging=False, input_format="stdin-tokens", input_file=None):
+         tp=1, emit_staging=False, input_format="stdin-tokens", input_file=None,
+         max_prompt_tokens=512):
     plan = A.decoder_plan(arch, int8_attention=int8_attention)
     collected = resolve(arch, sd, keys)
     tensors = build_tensors(arch, collected, quantize=quantize, int8_attention=int8_attention)
@@ -333,9 +327,15 @@ def pack(arch, sd, *, keys="fc{idx_plus_1}.{kind}", quantize="int8", int8_attent
     if missing:
         raise PackError(f"internal: plan references tensors the packer did not produce: "
                         f"{missing}")
+    try:
+        from .runtime import parse_sample
+        mode, top_k, temperature = parse_sample(sample)
+    except ValueError as e:
+        raise PackError(str(e)) from None
     plan["generation"] = {"max_new_tokens": max_new_tokens, "sample": sample,
-                          "eos_token": eos_token, "rng_seed": rng_seed,
-                          "input_format": input_format}
+                          "sample_mode": mode, "top_k": top_k, "temperature": temperature,
+                          "eos_token": eos_token, "rng_seed": rng_seed & 0xFFFFFFFF,
+                          "input_format": input_format, "max_prompt_tokens": max_prompt_tokens}
     plan["tp"] = {"size": tp}
     if input_file:
         plan["generation"]["prompt_file"] = str(Path(input_file).resolve())
@@ -345,7 +345,24 @@ def pack(arch, sd, *, keys="fc{idx_plus_1}.{kind}", quantize="int8", int8_attent
         base.with_suffix(".plan.json").write_text(json.dumps(plan, indent=1, sort_keys=True))
         if emit_staging:
             write_staging(base, tensors)
+        if input_format in ("stdin-tokens", "embedded"):
+            write_launcher(base)
     return plan, tensors
+
+
+def write_launcher(base):
+    """<out> itself: a symlink to the stdin-tokens front end (aricode-ml_b200/b2run),
+    which finds <out>.b2blob from the name it was started under. tools/run_decoder.py
+    starts it like the reference's packed binary (./<name> in the blob's directory)."""
+    import os
+    from .build import FRONT, build
+    if not FRONT.exists():
+        build()
+    link = Path(base)
+    if link.is_symlink() or link.exists():
+        link.unlink()
+    os.symlink(os.path.relpath(FRONT.resolve(), link.parent.resolve()), link)
+    return link
 
 
 def main(argv=None):
@@ -358,24 +375,38 @@ def main(argv=None):
                         "decoder path")
     if a.int4_linear or a.int4_embedding:
         raise PackError("--int4-linear / --int4-embedding are not supported by --target b200 yet")
-    if a.sample != "greedy":
-        raise PackError("--target b200 implements greedy sampling")
+    classifier = [f for f, v in (("--input-images", a.input_images), ("--input-labels", a.input_labels),
+                                 ("--n-test", a.n_test), ("--mean", a.mean), ("--std", a.std),
+                                 ("--no-argmax", a.no_argmax)) if v not in (None, False)]
+    if classifier or a.input_format in ("mnist", "stdin"):
+        raise PackError("--target b200 packs decoders; the classifier options "
+                        f"{', '.join(classifier) or '--input-format ' + a.input_format} do not apply")
+    if a.input_format == "embedded" and not a.input_file:
+        raise PackError("--input-format embedded reads its prompt from --input-file; none was given")
+    if a.max_prompt_tokens < 1:
+        raise PackError("--max-prompt-tokens must be at least 1")
+    if a.profile:
+        raise PackError("--profile (per-op cycle counters in the emitted binary) is not available "
+                        "with --target b200; set B2_TK_TRACE=<file> at run time for a per-phase timeline")
+    if a.tp != 1:
+        raise PackError("--tp: a packed blob is loaded on one GPU; tensor parallelism runs on "
+                        "synthetic weights only (b2_create_synthetic_tp)")
     if a.arch is None or a.out is None:
-        raise PackError("--arch, --out required for the pack flow.")
+        raise PackError("packing needs both --arch (the arch JSON) and --out (the output base name)")
     if a.quantize != "int8":
         # the reference forces --embed for int8; b200 packs only the int8 decode format
         raise PackError("--target b200 packs the --quantize int8 decode format; pass "
                         "--quantize int8")
     arch = json.loads(Path(a.arch).read_text())
     if not isinstance(arch, list):
-        raise PackError("--arch must contain a JSON list of [kind, ...args].")
+        raise PackError("the --arch file must hold a JSON list of ops, each [kind, args...]")
     sd = load_state_dict(a.checkpoint)
     plan, tensors = pack(arch, sd, keys=a.keys, quantize=a.quantize,
                          int8_attention=a.int8_attention, out=a.out,
                          max_new_tokens=a.max_new_tokens, sample=a.sample,
                          eos_token=a.eos_token, rng_seed=a.rng_seed, tp=a.tp,
                          emit_staging=a.emit_staging, input_format=a.input_format,
-                         input_file=a.input_file)
+                         input_file=a.input_file, max_prompt_tokens=a.max_prompt_tokens)
     base = Path(a.out)
     nbytes = sum(t.nbytes for t in tensors.values())
     print(f"wrote {base.with_suffix('.b2blob')}  ({len(tensors)} tensors, {nbytes} bytes)")

@@ -66,6 +66,7 @@ def _declare(L):
     L.b2_set_position.argtypes = [vp, C.c_int, C.c_int32]
     L.b2_decode_async.argtypes = [vp, C.c_int]
     L.b2_fill_kv_synthetic.argtypes = [vp, C.c_int, C.c_uint64]
+    L.b2_set_sampling.argtypes = [vp, C.c_int, C.c_int, C.c_double, C.c_uint32]
     L.b2_sync.argtypes = [vp]
     L.b2_read_output.argtypes = [vp, i32p, C.c_int, C.POINTER(C.c_int)]
     L.b2_set_stream.argtypes = [vp, vp]
@@ -103,6 +104,22 @@ def check(code, ctx=None):
         if code == -6:
             raise KVOverflow(code, msg)
         raise B2Error(code, msg)
+
+
+def parse_sample(spec):
+    """--sample spec -> (mode, top_k, temperature): 'greedy', 'temperature:T' or
+    'topk:K:T' (the reference's parse_sample_spec, aricode_pack.py:2035-2065)."""
+    parts = str(spec).split(":")
+    try:
+        if parts[0] == "greedy" and len(parts) == 1:
+            return 0, 0, 0.0
+        if parts[0] == "temperature" and len(parts) == 2:
+            return 1, 0, float(parts[1])
+        if parts[0] == "topk" and len(parts) == 3:
+            return 2, int(parts[1]), float(parts[2])
+    except ValueError:
+        pass
+    raise ValueError(f"--sample expects greedy, temperature:T or topk:K:T; got {spec!r}")
 
 
 def fnv1a64(name: str) -> int:
@@ -229,6 +246,11 @@ class Decoder:
 
     def set_position(self, pos, next_tok):
         self._ck(lib().b2_set_position(self._ctx, int(pos), int(next_tok)))
+
+    def set_sampling(self, sample="greedy", seed=20260502):
+        """--sample spec (greedy | temperature:T | topk:K:T) and the LCG seed."""
+        mode, k, temp = parse_sample(sample)
+        self._ck(lib().b2_set_sampling(self._ctx, mode, k, temp, int(seed) & 0xFFFFFFFF))
 
     def fill_kv_synthetic(self, count, seed=0):
         """KV rows [0, count) from the synthetic generator (the oracle's fill_kv) and

@@ -107,6 +107,19 @@ int b2_generate(b2_ctx* ctx, const int32_t* prompt, int n_prompt, int max_new, i
  * step. Both only enqueue work on the context's stream. */
 int b2_set_position(b2_ctx* ctx, int pos, int32_t next_tok);
 
+/* Token choice after the LM head: mode 0 greedy (the default), 1 temperature
+ * softmax, 2 top-k then temperature, with the reference's 32-bit LCG
+ * (state = state * 1103515245 + 12345, draw = (state & 65535) / 65536) seeded
+ * with `seed` at every new sequence (b2_reset, b2_generate) and advanced on every
+ * step, prompt steps included, as the reference loop does. A plan packed with
+ * --sample / --rng-seed starts with those settings. Not with tensor parallelism
+ * (B2_E_UNSUPPORTED). Returns the settings to the sequence start at the current
+ * position.
+ * Replaces: sample_temperature_f32 / sample_topk_filter_f32 (sampling_f32.ari:31-153)
+ * and the sampling branch of the decoder loop (aricode_pack.py:2186-2306). */
+enum { B2_SAMPLE_GREEDY = 0, B2_SAMPLE_TEMPERATURE = 1, B2_SAMPLE_TOPK = 2 };
+int b2_set_sampling(b2_ctx* ctx, int mode, int top_k, double temperature, uint32_t seed);
+
 /* Fill KV rows [0, count) of every attention sub-block with synthetic values and
  * set the position to count: value of element ((kv_head * max_seq + pos) * d_head
  * + i) of sub-block b (index in the plan's block list) is the synthetic generator's

@@ -68,6 +68,30 @@ def test_cli_writes_blob_and_plan(pkg, tmp_path):
     assert (tmp_path / "m.b2blob").exists()
 
 
+def _cli(pkg, tmp_path, *extra):
+    d = GOLDEN / "cfgT"
+    return pkg.pack.main(["--checkpoint", str(d / "model.safetensors"), "--arch", str(d / "arch.json"),
+                          "--quantize", "int8", "--int8-attention", "--out", str(tmp_path / "m"),
+                          *extra])
+
+
+def test_cli_sampling_flags_reach_the_plan(pkg, tmp_path):
+    assert _cli(pkg, tmp_path, "--sample", "topk:40:0.8", "--rng-seed", "77", "--eos-token", "2",
+                "--max-prompt-tokens", "20") == 0
+    g = json.loads((tmp_path / "m.plan.json").read_text())["generation"]
+    assert (g["sample_mode"], g["top_k"], g["temperature"], g["rng_seed"]) == (2, 40, 0.8, 77)
+    assert g["eos_token"] == 2 and g["max_prompt_tokens"] == 20
+
+
+@pytest.mark.parametrize("extra", [["--sample", "nucleus:0.9"], ["--sample", "topk:5"], ["--profile"],
+                                   ["--no-argmax"], ["--n-test", "5"], ["--input-format", "mnist"],
+                                   ["--input-format", "embedded"], ["--max-prompt-tokens", "0"],
+                                   ["--target", "aric"], ["--infer-arch"]])
+def test_cli_flags_that_cannot_work_are_refused(pkg, tmp_path, extra):
+    with pytest.raises(pkg.pack.PackError):
+        _cli(pkg, tmp_path, *extra)
+
+
 def test_missing_key_is_a_pack_error(pkg):
     arch = json.loads((GOLDEN / "cfgT" / "arch.json").read_text())
     sd = pkg.pack.load_state_dict(GOLDEN / "cfgT" / "model.safetensors")

@@ -298,7 +298,7 @@ def plan_tensor_names(plan):
         if b["type"] == "attn":
             out += [b[p] for p in "qkvo"]
             if b["bias"]:
-                out += list(b["bias"].values())
+                out += [v for v in b["bias"].values() if v]
         elif b["kind"] == "swiglu":
             out += [b["gate"], b["up"], b["down"]]
         else:

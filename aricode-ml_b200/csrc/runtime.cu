@@ -315,10 +315,10 @@ std::vector<Need> plan_needs(const b2json::Value& plan, int tp = 1, int rank = 0
             if (b.has("bias")) {
                 no_tp("attention biases");
                 const b2json::Value& bs = b["bias"];
-                out.push_back({bs["q"].as_str(), 2, H * dh, 0, 0});
-                out.push_back({bs["k"].as_str(), 2, KVH * dh, 0, 0});
-                out.push_back({bs["v"].as_str(), 2, KVH * dh, 0, 0});
-                out.push_back({bs["o"].as_str(), 2, d, 0, 0});
+                const char* proj[4] = {"q", "k", "v", "o"};
+                const long long len[4] = {H * dh, KVH * dh, KVH * dh, d};
+                for (int k = 0; k < 4; ++k)              // a missing projection bias adds 0
+                    if (bs.has(proj[k])) out.push_back({bs[proj[k]].as_str(), 2, len[k], 0, 0});
             }
         } else if (b["kind"].as_str() == "swiglu") {
             const long long ffn = b["d_ffn"].as_int();
@@ -979,21 +979,25 @@ int fetch_state(b2_ctx* c) {
     return B2_OK;
 }
 
-void load_blob(b2_ctx* c, const char* path, std::string* embedded_plan) {
-    FILE* f = std::fopen(path, "rb");
-    if (!f) throw Err(B2_E_IO, std::string("cannot open blob ") + path);
-    struct Closer { FILE* f; ~Closer() { std::fclose(f); } } closer{f};
+// The blob's header and tensor table (file offsets relative to its data region)
+struct BlobIndex {
+    std::map<std::string, TensorInfo> tensors;
+    uint64_t data_off = 0, data_bytes = 0, csum = 0;
+};
+
+BlobIndex read_blob_index(FILE* f, std::string* embedded_plan) {
+    BlobIndex ix;
     unsigned char hdr[64];
     if (std::fread(hdr, 1, 64, f) != 64 || std::memcmp(hdr, "B2DBLOB1", 8) != 0)
         throw Err(B2_E_FORMAT, "not a b200 decode blob");
     uint32_t ver, ntens, plan_len;
-    uint64_t table_off, data_off, data_bytes, csum, plan_off;
+    uint64_t table_off, plan_off;
     std::memcpy(&ver, hdr + 8, 4);
     std::memcpy(&ntens, hdr + 12, 4);
     std::memcpy(&table_off, hdr + 16, 8);
-    std::memcpy(&data_off, hdr + 24, 8);
-    std::memcpy(&data_bytes, hdr + 32, 8);
-    std::memcpy(&csum, hdr + 40, 8);
+    std::memcpy(&ix.data_off, hdr + 24, 8);
+    std::memcpy(&ix.data_bytes, hdr + 32, 8);
+    std::memcpy(&ix.csum, hdr + 40, 8);
     std::memcpy(&plan_len, hdr + 48, 4);
     std::memcpy(&plan_off, hdr + 56, 8);
     if (ver != 1) throw Err(B2_E_FORMAT, "unsupported blob version");
@@ -1025,13 +1029,20 @@ void load_blob(b2_ctx* c, const char* path, std::string* embedded_plan) {
         t.ld = (long long)ld;
         t.off = (size_t)off;
         t.nbytes = (size_t)nb;
-        if ((dtype != 1 && dtype != 2) || off + nb > data_bytes)
+        if ((dtype != 1 && dtype != 2) || off + nb > ix.data_bytes)
             throw Err(B2_E_FORMAT, std::string("bad table entry for ") + name);
-        c->tensors[name] = t;
+        ix.tensors[name] = t;
     }
-    if (cudaMalloc(&c->d_weights, data_bytes) != cudaSuccess) throw Err(B2_E_OOM, "weight allocation failed");
-    c->weight_bytes = data_bytes;
-    // stream the data region through two pinned buffers; checksum on the host as it passes
+    return ix;
+}
+
+// One byte range of the blob's data region and where it goes in the weight arena.
+struct CopyRange { uint64_t src, bytes; size_t dst; };
+
+// Stream the blob's whole data region through two pinned buffers, checksumming it
+// on the host as it passes and copying the parts in `ranges` (sorted by src, not
+// overlapping) to the weight arena.
+void stream_blob(b2_ctx* c, FILE* f, const BlobIndex& ix, const std::vector<CopyRange>& ranges) {
     const size_t chunk = 64ull << 20;
     unsigned char* pin[2] = {nullptr, nullptr};
     CK(cudaMallocHost(&pin[0], chunk));
@@ -1041,24 +1052,85 @@ void load_blob(b2_ctx* c, const char* path, std::string* embedded_plan) {
     CK(cudaEventCreateWithFlags(&ev[0], cudaEventDisableTiming));
     CK(cudaEventCreateWithFlags(&ev[1], cudaEventDisableTiming));
     struct EvFree { cudaEvent_t* e; ~EvFree() { cudaEventDestroy(e[0]); cudaEventDestroy(e[1]); } } ef{ev};
-    if (std::fseek(f, (long)data_off, SEEK_SET)) throw Err(B2_E_FORMAT, "truncated data region");
+    if (std::fseek(f, (long)ix.data_off, SEEK_SET)) throw Err(B2_E_FORMAT, "truncated data region");
     uint64_t sum = 0;
-    size_t done = 0;
+    size_t done = 0, ri = 0;
     int k = 0;
     bool used[2] = {false, false};
-    while (done < data_bytes) {
-        const size_t n = std::min(chunk, (size_t)data_bytes - done);
+    while (done < ix.data_bytes) {
+        const size_t n = std::min(chunk, (size_t)ix.data_bytes - done);
         if (used[k]) CK(cudaEventSynchronize(ev[k]));
         if (std::fread(pin[k], 1, n, f) != n) throw Err(B2_E_FORMAT, "truncated data region");
         sum += checksum_words(pin[k], n, done / 8);
-        CK(cudaMemcpyAsync(static_cast<char*>(c->d_weights) + done, pin[k], n, cudaMemcpyHostToDevice, c->stream));
+        while (ri < ranges.size() && ranges[ri].src + ranges[ri].bytes <= done) ++ri;
+        for (size_t r = ri; r < ranges.size() && ranges[r].src < done + n; ++r) {
+            const uint64_t lo = std::max<uint64_t>(ranges[r].src, done);
+            const uint64_t hi = std::min<uint64_t>(ranges[r].src + ranges[r].bytes, done + n);
+            if (lo < hi)
+                CK(cudaMemcpyAsync(static_cast<char*>(c->d_weights) + ranges[r].dst + (lo - ranges[r].src),
+                                   pin[k] + (lo - done), hi - lo, cudaMemcpyHostToDevice, c->stream));
+        }
         CK(cudaEventRecord(ev[k], c->stream));
         used[k] = true;
         done += n;
         k ^= 1;
     }
     CK(cudaStreamSynchronize(c->stream));
-    if (sum != csum) throw Err(B2_E_FORMAT, "blob checksum mismatch");
+    if (sum != ix.csum) throw Err(B2_E_FORMAT, "blob checksum mismatch");
+}
+
+void load_blob(b2_ctx* c, const char* path, std::string* embedded_plan) {
+    FILE* f = std::fopen(path, "rb");
+    if (!f) throw Err(B2_E_IO, std::string("cannot open blob ") + path);
+    struct Closer { FILE* f; ~Closer() { std::fclose(f); } } closer{f};
+    BlobIndex ix = read_blob_index(f, embedded_plan);
+    c->tensors = ix.tensors;
+    if (cudaMalloc(&c->d_weights, ix.data_bytes) != cudaSuccess) throw Err(B2_E_OOM, "weight allocation failed");
+    c->weight_bytes = ix.data_bytes;
+    stream_blob(c, f, ix, {CopyRange{0, ix.data_bytes, 0}});
+}
+
+// Tensor parallelism from a packed blob: this rank's rows of every row-split
+// tensor (plan_needs) and the whole of every replicated one, laid out in a new
+// arena with the blob's row strides; the whole data region is still read once
+// for the checksum.
+void load_blob_rank(b2_ctx* c, const char* path, const char* plan_json) {
+    FILE* f = std::fopen(path, "rb");
+    if (!f) throw Err(B2_E_IO, std::string("cannot open blob ") + path);
+    struct Closer { FILE* f; ~Closer() { std::fclose(f); } } closer{f};
+    std::string embedded;
+    BlobIndex ix = read_blob_index(f, &embedded);
+    const b2json::Value plan = b2json::parse(plan_json ? std::string(plan_json) : embedded);
+    std::vector<Need> needs = plan_needs(plan, c->tp_size, c->tp_rank);
+    std::vector<CopyRange> ranges;
+    size_t off = 0;
+    auto al = [](size_t n) { return (n + 255) & ~(size_t)255; };
+    auto take = [&](const std::string& name, long long row0, long long rows) {
+        auto it = ix.tensors.find(name);
+        if (it == ix.tensors.end()) throw Err(B2_E_FORMAT, "blob has no tensor '" + name + "'");
+        const TensorInfo& t = it->second;
+        const size_t esz = t.dtype == 1 ? 1 : 4;
+        TensorInfo loc = t;
+        const size_t row_bytes = t.two_d ? (size_t)t.ld * esz : esz;       // 1-D: one element a row
+        const long long full = t.two_d ? t.rows : t.cols;
+        if (row0 + rows > full) throw Err(B2_E_FORMAT, "tensor '" + name + "' is smaller than the plan says");
+        if (t.two_d) loc.rows = rows; else loc.cols = rows;
+        loc.nbytes = (size_t)rows * row_bytes;
+        loc.off = off;
+        ranges.push_back({t.off + (uint64_t)row0 * row_bytes, loc.nbytes, off});
+        off = al(off + loc.nbytes);
+        c->tensors[name] = loc;
+    };
+    for (const Need& nd : needs) {
+        if (c->tensors.count(nd.name)) continue;
+        take(nd.name, nd.row0, nd.rows);
+        if (nd.dtype == 1) take(nd.name + "_scales", nd.row0, nd.rows);
+    }
+    std::sort(ranges.begin(), ranges.end(), [](const CopyRange& a, const CopyRange& b) { return a.src < b.src; });
+    if (cudaMalloc(&c->d_weights, off) != cudaSuccess) throw Err(B2_E_OOM, "weight allocation failed");
+    c->weight_bytes = off;
+    stream_blob(c, f, ix, ranges);
+    assemble(c, plan);
 }
 
 void synth_weights(b2_ctx* c, const b2json::Value& plan, uint64_t seed, float stdv) {
@@ -1206,6 +1278,13 @@ int b2_create_synthetic(const char* plan_json, uint64_t seed, float stdv, int de
         synth_weights(c, plan, seed, stdv);
         assemble(c, plan);
     });
+}
+
+int b2_create_tp(const char* blob_path, const char* plan_json, int device, int tp_rank, int tp_size,
+                 b2_ctx** out) {
+    if (!blob_path) return B2_E_INVALID;
+    return create_common(out, device, [&](b2_ctx* c) { load_blob_rank(c, blob_path, plan_json); }, tp_rank,
+                         tp_size);
 }
 
 int b2_create_synthetic_tp(const char* plan_json, uint64_t seed, float stdv, int device, int tp_rank,

@@ -172,7 +172,15 @@ def resolve(arch, sd, keys_template="fc{idx_plus_1}.{kind}"):
                     _not_found(f"the {proj} projection weight of GQA attention op {idx}", cw, sd)
                 W = _f32(sd[wk])
                 _need_shape(f"GQA attention op {idx} {proj} weight '{wk}'", W, shape)
-                out.append((kind, idx, proj, W, None))
+                # optional bias (attn_gqa_kv_step_f32 slices b_Q/b_K/b_V/b_O when the
+                # caller binds them, attention_gqa_kv_f32.ari:209-217, :266-270; Llama
+                # checkpoints have none, Qwen-style ones have q/k/v biases)
+                bk = wk[: -len(".weight")] + ".bias"
+                b = None
+                if bk in sd:
+                    b = _f32(sd[bk])
+                    _need_shape(f"GQA attention op {idx} {proj} bias '{bk}'", b, (shape[0],))
+                out.append((kind, idx, proj, W, b))
         elif kind == "layernorm":
             dim = args[0]
             cw = _layernorm_candidates(idx)
@@ -323,6 +331,12 @@ def pack(arch, sd, *, keys="fc{idx_plus_1}.{kind}", quantize="int8", int8_attent
     plan = A.decoder_plan(arch, int8_attention=int8_attention)
     collected = resolve(arch, sd, keys)
     tensors = build_tensors(arch, collected, quantize=quantize, int8_attention=int8_attention)
+    for blk in plan["blocks"]:                 # GQA biases the checkpoint provides
+        if blk.get("kind") == "gqa":
+            gi = blk["q"][len("Wgqaq"):]
+            names = {p: f"bgqa{p}{gi}" for p in "qkvo"}
+            if any(n in tensors for n in names.values()):
+                blk["bias"] = {p: (n if n in tensors else None) for p, n in names.items()}
     missing = [n for n in A.plan_tensor_names(plan) if n not in tensors]
     if missing:
         raise PackError(f"internal: plan references tensors the packer did not produce: "
@@ -336,6 +350,8 @@ def pack(arch, sd, *, keys="fc{idx_plus_1}.{kind}", quantize="int8", int8_attent
                           "sample_mode": mode, "top_k": top_k, "temperature": temperature,
                           "eos_token": eos_token, "rng_seed": rng_seed & 0xFFFFFFFF,
                           "input_format": input_format, "max_prompt_tokens": max_prompt_tokens}
+    if tp > 1:
+        _check_tp_split(plan, tp)
     plan["tp"] = {"size": tp}
     if input_file:
         plan["generation"]["prompt_file"] = str(Path(input_file).resolve())
@@ -348,6 +364,24 @@ def pack(arch, sd, *, keys="fc{idx_plus_1}.{kind}", quantize="int8", int8_attent
         if input_format in ("stdin-tokens", "embedded"):
             write_launcher(base)
     return plan, tensors
+
+
+def _check_tp_split(plan, tp):
+    """--tp N: every row split (query and KV heads, d_model, d_ffn, vocab) must divide
+    by N, and the tensor-parallel path covers int8 attention and SwiGLU blocks only."""
+    dims = [("d_model", plan["d_model"]), ("vocab", plan["vocab"])]
+    for b in plan["blocks"]:
+        if b["type"] == "attn":
+            if b["dtype"] != "i8" or b.get("bias"):
+                raise PackError("--tp > 1 needs --int8-attention and attention without biases")
+            dims += [("n_heads", b["n_heads"]), ("n_kv_heads", b["n_kv_heads"])]
+        elif b["kind"] != "swiglu":
+            raise PackError("--tp > 1 covers SwiGLU feed-forward blocks only")
+        else:
+            dims.append(("d_ffn", b["d_ffn"]))
+    bad = [f"{k}={v}" for k, v in dims if v % tp]
+    if bad:
+        raise PackError(f"--tp {tp} does not divide {', '.join(sorted(set(bad)))}")
 
 
 def write_launcher(base):
@@ -388,9 +422,8 @@ def main(argv=None):
     if a.profile:
         raise PackError("--profile (per-op cycle counters in the emitted binary) is not available "
                         "with --target b200; set B2_TK_TRACE=<file> at run time for a per-phase timeline")
-    if a.tp != 1:
-        raise PackError("--tp: a packed blob is loaded on one GPU; tensor parallelism runs on "
-                        "synthetic weights only (b2_create_synthetic_tp)")
+    if a.tp < 1:
+        raise PackError("--tp must be at least 1")
     if a.arch is None or a.out is None:
         raise PackError("packing needs both --arch (the arch JSON) and --out (the output base name)")
     if a.quantize != "int8":

@@ -56,6 +56,7 @@ def _declare(L):
     L.b2_create_synthetic.argtypes = [C.c_char_p, C.c_uint64, C.c_float, C.c_int, C.POINTER(vp)]
     L.b2_create_synthetic_tp.argtypes = [C.c_char_p, C.c_uint64, C.c_float, C.c_int, C.c_int, C.c_int,
                                          C.POINTER(vp)]
+    L.b2_create_tp.argtypes = [C.c_char_p, C.c_char_p, C.c_int, C.c_int, C.c_int, C.POINTER(vp)]
     L.b2_tp_handle.argtypes = [vp, C.c_void_p, C.c_int]
     L.b2_tp_connect.argtypes = [vp, C.c_void_p, C.c_int]
     L.b2_destroy.argtypes = [vp]
@@ -180,7 +181,20 @@ class Decoder:
         ctx = vp()
         check(lib().b2_create_synthetic_tp(json.dumps(plan).encode(), int(seed), float(stdv), int(device),
                                            int(rank), int(size), C.byref(ctx)))
-        dec = cls(_ctx=ctx)
+        return cls(_ctx=ctx)._connect(rank, size, exchange)
+
+    @classmethod
+    def from_blob_tp(cls, blob_path, rank, size, exchange, device=0, plan=None):
+        """Rank `rank` of a tensor-parallel decoder over `size` GPUs from a packed
+        blob (each rank loads its rows); `exchange` as for synthetic_tp."""
+        ctx = vp()
+        plan_s = json.dumps(plan).encode() if plan is not None else None
+        check(lib().b2_create_tp(str(blob_path).encode(), plan_s, int(device), int(rank), int(size),
+                                 C.byref(ctx)))
+        return cls(_ctx=ctx)._connect(rank, size, exchange)
+
+    def _connect(self, rank, size, exchange):
+        dec, ctx = self, self._ctx
         if size > 1:
             h = C.create_string_buffer(64)
             dec._ck(lib().b2_tp_handle(ctx, h, 64))

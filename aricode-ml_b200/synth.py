@@ -100,8 +100,8 @@ def tensor_specs(plan):
                     (b["v"], dt, (kd, d), "rand"), (b["o"], dt, (d, qd), "rand")]
             if b.get("bias"):
                 bs = b["bias"]
-                out += [(bs["q"], "f32", (qd,), "rand"), (bs["k"], "f32", (kd,), "rand"),
-                        (bs["v"], "f32", (kd,), "rand"), (bs["o"], "f32", (d,), "rand")]
+                out += [(bs[p], "f32", (n,), "rand") for p, n in (("q", qd), ("k", kd), ("v", kd), ("o", d))
+                        if bs.get(p)]
         elif b["kind"] == "swiglu":
             f = b["d_ffn"]
             out += [(b["gate"], "i8", (f, d), "rand"), (b["up"], "i8", (f, d), "rand"),

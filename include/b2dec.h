@@ -72,6 +72,15 @@ int b2_create_synthetic(const char* plan_json, uint64_t seed, float stdv, int de
  * the reference itself runs on one CPU thread and has no counterpart. */
 int b2_create_synthetic_tp(const char* plan_json, uint64_t seed, float stdv, int device, int tp_rank,
                            int tp_size, b2_ctx** out);
+/* The same from a packed blob: each rank reads the blob once (checksummed) and
+ * keeps its rows of every row-split tensor and the whole of every replicated one;
+ * then b2_tp_handle / b2_tp_connect as above. The packer's --tp only records the
+ * degree; any blob whose head counts, d_model, d_ffn and vocab divide by tp_size
+ * loads. Same limits as the synthetic form (int8 attention weights, no attention
+ * biases, SwiGLU feed-forward blocks).
+ * Replaces: b2_create(blob, plan, device, tp_rank, tp_size, ...) of the plan. */
+int b2_create_tp(const char* blob_path, const char* plan_json, int device, int tp_rank, int tp_size,
+                 b2_ctx** out);
 int b2_tp_handle(b2_ctx* ctx, void* handle, int len);
 int b2_tp_connect(b2_ctx* ctx, const void* handles, int len);
 

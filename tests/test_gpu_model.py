@@ -100,3 +100,50 @@ def test_bad_inputs_are_errors(pkg, tmp_path):
     bad.write_bytes(b"not a blob at all" * 10)
     with pytest.raises(pkg.runtime.B2Error):
         pkg.runtime.Decoder(bad)
+
+
+def _with_gqa_biases(sd, projs="qkv", seed=3):
+    """A copy of a Llama checkpoint with biases on the given attention projections
+    (as Qwen-style checkpoints carry them)."""
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    out = dict(sd)
+    for k, v in sd.items():
+        for p in projs:
+            hf = "o_proj" if p == "o" else f"{p}_proj"
+            if k.endswith(f"self_attn.{hf}.weight"):
+                out[k[: -len("weight")] + "bias"] = torch.randn(v.shape[0], generator=g) * 0.1
+    return out
+
+
+@pytest.mark.parametrize("name", ["tiny_llama_min", "gqa_min"])
+@pytest.mark.parametrize("int8_attention", [False, True])
+@pytest.mark.parametrize("projs", ["", "qkv", "qkvo"])
+def test_gqa_f32_weights_and_optional_biases(pkg, oracle, name, int8_attention, projs, tmp_path):
+    """GQA attention with f32 weights (no --int8-attention) and with the optional
+    per-projection biases (attention_gqa_kv_f32.ari:209-217, :266-270)."""
+    import json
+    from conftest import GOLDEN
+    d = GOLDEN / name
+    man = json.loads((GOLDEN / "manifest.json").read_text())["fixtures"][name]
+    arch = json.loads((d / "arch.json").read_text())
+    sd = pkg.pack.load_state_dict(d / "synth.pt")
+    if projs:
+        sd = _with_gqa_biases(sd, projs)
+    plan, tensors = pkg.pack.pack(arch, sd, int8_attention=int8_attention)
+    gqa = [b for b in plan["blocks"] if b.get("kind") == "gqa"]
+    assert all((b["bias"] is not None) == bool(projs) for b in gqa)
+    prompt = list((d / "prompt.bin").read_bytes())
+    om = oracle.OracleModel(plan, tensors)
+    ref = om.generate(prompt, man["max_new"])
+    if not projs:
+        assert ref == man["expected_tokens"]
+    dec = _decoder(pkg, plan, tensors, tmp_path)
+    assert dec.generate(prompt, man["max_new"]) == ref
+    om.reset()
+    dec.reset()
+    for t in prompt + ref[:-1]:
+        r_tok, r_log = om.step(t)
+        g_tok, g_log = dec.step(t, want_logits=True)
+        assert g_tok == r_tok and np.array_equal(g_log, r_log)
+    dec.close()

@@ -62,9 +62,35 @@ def test_tensor_parallel_matches_one_gpu(pkg, tmp_path, world, name, layers, max
     one.reset()
     logits = [one.step(t, want_logits=True)[1] for t in prompt[:6]]
     one.close()
+    _check(res, ids, logits, plan, world)
+
+
+def _check(res, ids, logits, plan, world):
     rows = plan["vocab"] // world
     for r, got in enumerate(res):
         assert int(got["tk"][0]) == 1
         assert got["ids"].tolist() == list(ids), f"rank {r}"
         ref = np.stack([lg[r * rows:(r + 1) * rows] for lg in logits])
         assert np.array_equal(got["logits"].view(np.uint32), ref.view(np.uint32)), f"rank {r}"
+
+
+def test_tensor_parallel_from_a_packed_blob(pkg, tmp_path):
+    """b2_create_tp: every rank slices its rows out of one packed checkpoint."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from conftest import GOLDEN
+    d = GOLDEN / "cfgT"
+    out = tmp_path / "m"
+    assert pkg.pack.main(["--checkpoint", str(d / "model.safetensors"), "--arch", str(d / "arch.json"),
+                          "--quantize", "int8", "--int8-attention", "--tp", "2", "--out", str(out)]) == 0
+    blob = out.with_suffix(".b2blob")
+    res = _run_ranks(tmp_path, 2, f"blob:{blob}", None, None)
+    plan, _ = pkg.blob.read_blob(blob)
+    one = pkg.runtime.Decoder(blob)
+    prompt = [int(t) for t in np.random.default_rng(5).integers(0, plan["vocab"], 12)]
+    ids = one.generate(prompt, 20)
+    one.reset()
+    logits = [one.step(t, want_logits=True)[1] for t in prompt[:6]]
+    one.close()
+    _check(res, ids, logits, plan, 2)

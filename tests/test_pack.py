@@ -135,3 +135,18 @@ def test_keys_template_and_hf_fallbacks(pkg):
 def test_algorithmic_weight_bytes(pkg, name, gb):
     plan = pkg.synth.config_plan(name)
     assert abs(pkg.synth.weight_bytes(plan) / 1e9 - gb) < 0.01
+
+
+def test_gqa_biases_are_staged_when_the_checkpoint_has_them(pkg):
+    import torch
+    d = GOLDEN / "tiny_llama_min"
+    arch = json.loads((d / "arch.json").read_text())
+    sd = dict(pkg.pack.load_state_dict(d / "synth.pt"))
+    sd["model.layers.0.self_attn.k_proj.bias"] = torch.ones(8)
+    plan, tensors = pkg.pack.pack(arch, sd)
+    b = [blk for blk in plan["blocks"] if blk.get("kind") == "gqa"][0]["bias"]
+    assert b == {"q": None, "k": "bgqak0", "v": None, "o": None}
+    assert np.array_equal(tensors["bgqak0"], np.ones(8, np.float32))
+    sd["model.layers.0.self_attn.k_proj.bias"] = torch.ones(7)
+    with pytest.raises(pkg.pack.PackError):
+        pkg.pack.pack(arch, sd)

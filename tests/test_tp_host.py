@@ -65,3 +65,84 @@ def test_malformed_exchanges_are_rejected(pkg):
     with pytest.raises(ValueError):
         rt.tp_gather_handles(h, 0, 2, lambda x: [bytes(64), x])            # out of order
     assert rt.tp_gather_handles(h, 1, 2, lambda x: [bytes(64), x]) == bytes(64) + h
+
+
+def _better(va, ia, vb, ib):
+    """The cross-rank argmax order of the LM-head epilogue: non-NaN beats NaN,
+    larger wins, ties go to the lower vocabulary id."""
+    na, nb = va != va, vb != vb
+    if na != nb:
+        return nb
+    if not na and va != vb:
+        return va > vb
+    return ia < ib
+
+
+def _split_rank(rank, world, port, q):
+    """Each rank computes its output rows of every int8 matrix of a small model
+    (whole input vector, like the GPU split) and its best logit; the gathered rows
+    and the combined token must equal the one-rank results."""
+    sys.path.insert(0, str(ROOT))
+    sys.path.insert(0, str(ROOT / "oracle"))
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import oracle as O
+    pkg = importlib.import_module("aricode-ml_b200")
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    plan = pkg.synth.config_plan("tiny-llama")
+    t = O.synth_tensors(plan, seed=0)
+    rng = np.random.default_rng(3)
+    ok = True
+    for name, dt, shape, _ in pkg.synth.tensor_specs(plan):
+        if dt != "i8" or name == plan["embedding"]:
+            continue
+        m, n = shape
+        x = rng.standard_normal(n).astype(np.float32)
+        lo, hi = rank * m // world, (rank + 1) * m // world
+        mine = torch.from_numpy(O.gemv_i8(t[name][lo:hi], t[name + "_scales"][lo:hi], x))
+        parts = [torch.empty(m // world) for _ in range(world)]
+        dist.all_gather(parts, mine)
+        ok = ok and np.array_equal(torch.cat(parts).numpy(), O.gemv_i8(t[name], t[name + "_scales"], x))
+    # the argmax over vocabulary rows split across the ranks
+    for case in range(4):
+        v = rng.standard_normal(64).astype(np.float32)
+        if case == 1:
+            v[[5, 40]] = v.max() + 1            # tie across the rank boundary -> lower id
+        if case == 2:
+            v[0] = np.nan                       # first logit NaN -> id 0 (sequential scan)
+        if case == 3:
+            v[[3, 50]] = np.nan                 # NaNs elsewhere never win
+        lo, hi = rank * 32, (rank + 1) * 32
+        bi = lo
+        for i in range(lo, hi):
+            if _better(v[i], i, v[bi], bi):
+                bi = i
+        got = [None] * world
+        dist.all_gather_object(got, (float(v[bi]), bi))
+        best = got[0]
+        for cand in got[1:]:
+            if _better(cand[0], cand[1], best[0], best[1]):
+                best = cand
+        tok = 0 if v[0] != v[0] else best[1]
+        ok = ok and tok == O.argmax(v)
+    dist.barrier()
+    dist.destroy_process_group()
+    q.put((rank, ok))
+
+
+def test_row_split_gemv_and_argmax_equal_one_rank():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_split_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert got == {0: True, 1: True}

@@ -4,7 +4,8 @@ tests/test_gpu_tp.py (and usable by hand):
     python tests/tp_worker.py RANK WORLD PORT CONFIG LAYERS MAX_SEQ OUT.npz
 
 Creates rank RANK of a WORLD-GPU decoder over the synthetic CONFIG model
-(LAYERS, MAX_SEQ: 0 = the config's own), exchanges the buffer handles through a
+(LAYERS, MAX_SEQ: 0 = the config's own), or over a packed model when CONFIG is
+blob:<path>, exchanges the buffer handles through a
 gloo process group on 127.0.0.1:PORT, then makes the same calls on every rank:
 one greedy generation, then a few steps with logits. Writes ids and this rank's
 logit rows to OUT.npz.
@@ -31,14 +32,21 @@ def main(argv):
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
     torch.cuda.set_device(rank)
     pkg = importlib.import_module("aricode-ml_b200")
-    plan = pkg.synth.config_plan(name, n_layers=layers, max_seq=max_seq)
+    blob = name[len("blob:"):] if name.startswith("blob:") else None
+    if blob:
+        plan, _ = pkg.blob.read_blob(blob)
+    else:
+        plan = pkg.synth.config_plan(name, n_layers=layers, max_seq=max_seq)
 
     def exchange(handle):
         got = [None] * world
         dist.all_gather_object(got, handle)
         return got
 
-    dec = pkg.runtime.Decoder.synthetic_tp(plan, rank, world, exchange, seed=0, device=rank)
+    if blob:
+        dec = pkg.runtime.Decoder.from_blob_tp(blob, rank, world, exchange, device=rank)
+    else:
+        dec = pkg.runtime.Decoder.synthetic_tp(plan, rank, world, exchange, seed=0, device=rank)
     prompt = [int(t) for t in np.random.default_rng(5).integers(0, plan["vocab"], 12)]
     ids = dec.generate(prompt, 20)
     dec.reset()

@@ -21,8 +21,8 @@ CSRC = PKG / "csrc"
 OBJ = CSRC / "_obj"
 LIB = PKG / "libb2dec.so"
 FRONT = PKG / "b2run"                    # stdin-tokens front end (host program over the library)
-SOURCES = ["runtime.cu", "launch.cu", "token.cu", "capi.cu", "noalloc.cu"]
-HEADERS = ["b2_common.cuh", "gemv.cuh", "attn.cuh", "kernels.cuh", "token.cuh", "json.h"]
+SOURCES = ["runtime.cu", "launch.cu", "token.cu", "prefill.cu", "capi.cu", "noalloc.cu"]
+HEADERS = ["b2_common.cuh", "gemv.cuh", "attn.cuh", "kernels.cuh", "token.cuh", "prefill.cuh", "json.h"]
 
 NVCC_FLAGS = [
     "-O3", "-std=c++17", "-lineinfo",

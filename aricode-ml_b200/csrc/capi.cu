@@ -4,7 +4,7 @@
 #include <cuda_runtime.h>
 
 #include "../../include/b2dec.h"
-#include "kernels.cuh"
+#include "prefill.cuh"
 
 using namespace b2;
 
@@ -33,6 +33,35 @@ int b2_gemv_i8_rowscale(const int8_t* W, int64_t ld, const float* scale, const f
     p.rows[0] = m; p.nseg = 1; p.n = n; p.ld = (int)ld;
     p.x = x; p.norm = NORM_NONE; p.epi = EPI_STORE; p.y = y;
     return status(launch_gemv(p, true, static_cast<cudaStream_t>(stream), false, sm_count_current()));
+}
+
+size_t b2_gemm_i8_rowscale_workspace(int T, int64_t ld) {
+    const size_t Tpad = ((size_t)T + kPfTokenTile - 1) / kPfTokenTile * kPfTokenTile;
+    const size_t ldp = ((size_t)ld + 127) / 128 * 128;
+    return ((4 * Tpad * ldp + 255) & ~(size_t)255) + (size_t)T * sizeof(int);
+}
+
+int b2_gemm_i8_rowscale(const int8_t* W, int64_t ld, const float* scale, const float* X, int64_t ldx,
+                        const float* bias, float* Y, int64_t ldy, int m, int n, int T, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+    if (!W || !scale || !X || !Y || !workspace || m <= 0 || n <= 0 || T <= 0 || ld < n || ld % 16 || !al16(W) ||
+        ldx < n || ldy < m || n > kXfixMaxN || workspace_bytes < b2_gemm_i8_rowscale_workspace(T, ld) ||
+        !al16(workspace))
+        return B2_E_INVALID;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int Tpad = (T + kPfTokenTile - 1) / kPfTokenTile * kPfTokenTile;
+    const int ldp = (int)((ld + 127) / 128 * 128);
+    unsigned char* planes = static_cast<unsigned char*>(workspace);
+    int* S = reinterpret_cast<int*>(planes + ((4 * (size_t)Tpad * ldp + 255) & ~(size_t)255));
+    PfPlanesParams pp{};
+    pp.x = X; pp.ldx = (int)ldx; pp.n = n; pp.norm = NORM_NONE; pp.eps = 0.0f;
+    pp.planes = planes; pp.ldp = ldp; pp.kp = ldp; pp.Tpad = Tpad; pp.S = S;
+    cudaError_t e = launch_prefill_planes(pp, T, s);
+    if (e != cudaSuccess) return B2_E_CUDA;
+    PfGemmParams g{};
+    g.M = m; g.K = (int)ld; g.T = T; g.Tpad = Tpad; g.epi = PF_STORE; g.S = S;
+    g.scale[0] = scale; g.scale[1] = scale; g.bias = bias; g.out = Y; g.ldo = (int)ldy;
+    return status(launch_prefill_gemm(1, W, nullptr, planes, ldp, g, s));
 }
 
 int b2_gemv_f32(const float* W, int64_t ld, const float* x, const float* bias, float* y, int m, int n,

@@ -1,0 +1,99 @@
+// prefill.cu — host side of the batched prefill kernels (prefill.cuh): TMA tensor
+// maps (through the driver entry point, no libcuda link) and the launches.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "prefill.cuh"
+
+namespace b2 {
+
+namespace {
+
+typedef CUresult (*EncodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encoder() {
+    static std::once_flag once;
+    static EncodeTiled fn = nullptr;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(p);
+    });
+    return fn;
+}
+
+// 2-D byte matrix [rows][cols] with row stride `stride` bytes; box = 128 bytes of
+// a row x box_rows rows, 128-byte swizzle (the UMMA K-major SW128 layout);
+// reads past cols or rows are zeros
+bool byte_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint64_t stride, uint32_t box_rows) {
+    EncodeTiled enc = encoder();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {stride};
+    const cuuint32_t box[2] = {(cuuint32_t)kPfKBlock, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int NM>
+cudaError_t launch_nm(const void* A0, const void* A1, const unsigned char* planes, int ldp, const PfGemmParams& p,
+                      cudaStream_t s) {
+    using Sh = PfShape<NM>;
+    CUtensorMap a0, a1, b;
+    if (!byte_map(&a0, A0, (uint64_t)p.K, (uint64_t)p.M, (uint64_t)p.K, kPfRows) ||
+        !byte_map(&a1, NM == 2 ? A1 : A0, (uint64_t)p.K, (uint64_t)p.M, (uint64_t)p.K, kPfRows) ||
+        !byte_map(&b, planes, (uint64_t)p.K, 4ull * p.Tpad, (uint64_t)ldp, Sh::N))
+        return cudaErrorInvalidValue;
+    auto k = prefill_gemm_kernel<NM>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, Sh::SmemBytes);
+    if (e != cudaSuccess) return e;
+    const dim3 grid((unsigned)((p.M + kPfRows - 1) / kPfRows), (unsigned)((p.T + Sh::N - 1) / Sh::N));
+    k<<<grid, kPfThreads, Sh::SmemBytes, s>>>(a0, a1, b, p);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_prefill_gemm(int nm, const void* A0, const void* A1, const unsigned char* planes, int ldp,
+                                const PfGemmParams& p, cudaStream_t s) {
+    // TMA rules: 16-byte aligned bases and row strides; every x coordinate is a
+    // multiple of 128 bytes
+    if ((reinterpret_cast<uintptr_t>(A0) & 15) || (nm == 2 && (reinterpret_cast<uintptr_t>(A1) & 15)) ||
+        (reinterpret_cast<uintptr_t>(planes) & 15) || (p.K & 15) || (ldp & 15) || ldp < p.K || p.Tpad % 128)
+        return cudaErrorInvalidValue;
+    return nm == 2 ? launch_nm<2>(A0, A1, planes, ldp, p, s) : launch_nm<1>(A0, A1, planes, ldp, p, s);
+}
+
+cudaError_t launch_prefill_planes(const PfPlanesParams& p, int T, cudaStream_t s) {
+    const size_t smem = (size_t)p.n * sizeof(float);
+    cudaError_t e = cudaFuncSetAttribute(prefill_planes_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    prefill_planes_kernel<<<T, 256, smem, s>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_prefill_attn(const PfAttnParams& p, cudaStream_t s) {
+    const int G = p.H / p.KVH;
+    const size_t smem = prefill_attn_smem(G, p.dh);
+    cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    const dim3 grid((unsigned)p.KVH, (unsigned)((p.T + kPfAttnTokens - 1) / kPfAttnTokens));
+    prefill_attn_kernel<<<grid, kAttnThreads, smem, s>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_prefill_embed(const int8_t* emb, const float* emb_s, long long ld, const int* ids, int pos0,
+                                 int vocab, int d, float* x, int T, int* err, cudaStream_t s) {
+    prefill_embed_kernel<<<T, 256, 0, s>>>(emb, emb_s, ld, ids, pos0, vocab, d, x, err);
+    return cudaGetLastError();
+}
+
+}  // namespace b2

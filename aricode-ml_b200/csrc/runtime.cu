@@ -24,6 +24,7 @@
 
 #include "../../include/b2dec.h"
 #include "json.h"
+#include "prefill.cuh"
 #include "token.cuh"
 
 using namespace b2;
@@ -194,6 +195,14 @@ struct b2_ctx {
     double samp_t = 0.0;
     unsigned seed = 0, rng = 0;    // rng: LCG state before the next step's advance
     double* samp_e = nullptr;
+    // batched prefill (prefill.cuh): whether the plan is covered, and its workspace
+    bool pf_ok = false;
+    std::string pf_why;
+    void* pf_base = nullptr;
+    int pf_tmax = 0, pf_ldp = 0;
+    unsigned char* pf_planes = nullptr;
+    int* pf_S = nullptr;
+    float *pf_x = nullptr, *pf_q = nullptr, *pf_att = nullptr, *pf_f = nullptr, *pf_part = nullptr;
 
     ~b2_ctx() {
         if (device >= 0) cudaSetDevice(device);
@@ -204,6 +213,7 @@ struct b2_ctx {
         if (d_work) cudaFree(d_work);
         if (d_phases) cudaFree(d_phases);
         if (d_trace) cudaFree(d_trace);
+        if (pf_base) cudaFree(pf_base);
         for (int r = 0; r < kMaxRanks; ++r)
             if (peer_base[r]) cudaIpcCloseMemHandle(peer_base[r]);
         if (d_xch) cudaFree(d_xch);
@@ -566,6 +576,23 @@ void assemble(b2_ctx* c, const b2json::Value& plan) {
     }
     CK(cudaMallocHost(&c->h_st, sizeof(StepState)));
     std::memset(c->h_st, 0, sizeof(StepState));
+
+    // batched prefill covers one-GPU Llama-family plans: RMSNorm, int8 RoPE attention,
+    // int8 SwiGLU, no learned positions
+    c->pf_ok = false;
+    const char* pe = std::getenv("B2_PREFILL_BATCHED");
+    if (pe && pe[0] == '0') c->pf_why = "batched prefill disabled (B2_PREFILL_BATCHED=0)";
+    else if (c->tp_size > 1) c->pf_why = "tensor parallelism";
+    else if (c->pos_tab) c->pf_why = "learned positional embedding";
+    else {
+        c->pf_ok = true;
+        for (const Block& B : c->blocks) {
+            if (B.norm.kind != NORM_RMS) { c->pf_ok = false; c->pf_why = "LayerNorm"; }
+            else if (B.attn && (!B.q.i8 || !B.rope)) { c->pf_ok = false; c->pf_why = "f32 or RoPE-less attention"; }
+            else if (B.attn && (B.dh > 256 || B.dh % 4)) { c->pf_ok = false; c->pf_why = "head_dim"; }
+            else if (!B.attn && !B.swiglu) { c->pf_ok = false; c->pf_why = "GELU feed-forward"; }
+        }
+    }
 }
 
 // ------------------------------------------------------------------ one step's launches
@@ -881,6 +908,94 @@ void launch_token(b2_ctx* c, bool with_head, cudaStream_t s) {
     cfg.attrs = at;
     cfg.numAttrs = 1;
     CK(tk_launch(c->token_vs, cfg, P));
+}
+
+// ------------------------------------------------------------------ batched prefill
+void prefill_workspace(b2_ctx* c) {
+    if (c->pf_base) return;
+    int ld_max = 16, qd = 1, ffn = 1, H = 1, dh = 1;
+    for (const Block& B : c->blocks) {
+        if (B.attn) {
+            ld_max = std::max({ld_max, B.q.ld, B.o.ld});
+            qd = std::max(qd, B.H * B.dh);
+            H = std::max(H, B.H);
+            dh = std::max(dh, B.dh);
+        } else {
+            ld_max = std::max({ld_max, B.w1.ld, B.w2.ld});
+            ffn = std::max(ffn, B.ffn_local);
+        }
+    }
+    c->pf_ldp = (ld_max + 127) / 128 * 128;
+    c->pf_tmax = std::min(512, (c->max_seq + kPfTokenTile - 1) / kPfTokenTile * kPfTokenTile);
+    const size_t T = (size_t)c->pf_tmax;
+    auto al = [](size_t n) { return (n + 255) & ~(size_t)255; };
+    const size_t b_planes = al(4 * T * c->pf_ldp), b_S = al(T * 4), b_x = al(T * c->d * 4),
+                 b_q = al(T * qd * 4), b_f = al(T * ffn * 4),
+                 b_part = al(T * H * (size_t)c->attn_nsplit_max * (dh + 2) * 4);
+    const size_t total = b_planes + b_S + b_x + 2 * b_q + b_f + b_part;
+    if (cudaMalloc(&c->pf_base, total) != cudaSuccess) throw Err(B2_E_OOM, "prefill workspace allocation failed");
+    char* w = static_cast<char*>(c->pf_base);
+    c->pf_planes = reinterpret_cast<unsigned char*>(w); w += b_planes;
+    c->pf_S = reinterpret_cast<int*>(w); w += b_S;
+    c->pf_x = reinterpret_cast<float*>(w); w += b_x;
+    c->pf_q = reinterpret_cast<float*>(w); w += b_q;
+    c->pf_att = reinterpret_cast<float*>(w); w += b_q;
+    c->pf_f = reinterpret_cast<float*>(w); w += b_f;
+    c->pf_part = reinterpret_cast<float*>(w);
+    // plane rows past the chunk's tokens must read as zeros
+    CK(cudaMemsetAsync(c->pf_planes, 0, b_planes, c->stream));
+}
+
+// Tokens [p0, p0 + T) of the device prompt buffer through every sub-block, no LM
+// head: the KV cache ends as n decode steps would leave it, bit for bit.
+void enqueue_prefill_chunk(b2_ctx* c, int p0, int T, cudaStream_t s) {
+    int* err = &c->st->err;
+    const int Tpad = (T + kPfTokenTile - 1) / kPfTokenTile * kPfTokenTile;
+    auto planes = [&](const float* x, int ldx, int n, const NormRef* nr) {
+        PfPlanesParams pp{};
+        pp.x = x; pp.ldx = ldx; pp.n = n;
+        pp.norm = nr ? nr->kind : NORM_NONE; pp.g = nr ? nr->g : nullptr; pp.eps = c->eps;
+        pp.planes = c->pf_planes; pp.ldp = c->pf_ldp; pp.kp = c->pf_ldp; pp.Tpad = Tpad; pp.S = c->pf_S;
+        CK(launch_prefill_planes(pp, T, s));
+    };
+    auto gemm = [&](int nm, const DevMat& A, const DevMat* A1, int epi, float* out, int ldo, const float* bias,
+                    const Block* B, float* cache) {
+        PfGemmParams g{};
+        g.M = A.rows; g.K = A.ld; g.T = T; g.Tpad = Tpad; g.epi = epi; g.S = c->pf_S;
+        g.scale[0] = A.s; g.scale[1] = A1 ? A1->s : A.s; g.bias = bias;
+        g.out = out; g.ldo = ldo; g.err = err; g.pos0 = p0; g.max_seq = c->max_seq;
+        if (B) { g.rope = B->rope; g.rope_tab = c->rope_tab; g.dh = B->dh; g.qscale = (float)(1.0 / std::sqrt((double)B->dh)); }
+        g.cache = cache;
+        CK(launch_prefill_gemm(nm, A.w, A1 ? A1->w : nullptr, c->pf_planes, c->pf_ldp, g, s));
+    };
+    CK(launch_prefill_embed(static_cast<const int8_t*>(c->emb.w), c->emb.s, c->emb.ld, c->prompt, p0, c->vocab,
+                            c->d, c->pf_x, T, err, s));
+    for (const Block& B : c->blocks) {
+        planes(c->pf_x, c->d, c->d, &B.norm);
+        if (B.attn) {
+            const int qd = B.H * B.dh;
+            gemm(1, B.q, nullptr, PF_Q, c->pf_q, qd, B.bias[0], &B, nullptr);
+            gemm(1, B.k, nullptr, PF_K, nullptr, 0, B.bias[1], &B, B.K);
+            gemm(1, B.v, nullptr, PF_V, nullptr, 0, B.bias[2], &B, B.V);
+            PfAttnParams a{};
+            a.q = c->pf_q; a.K = B.K; a.V = B.V; a.out = c->pf_att; a.part = c->pf_part;
+            a.H = B.H; a.KVH = B.KVH; a.dh = B.dh; a.max_seq = c->max_seq; a.nsplit_max = c->attn_nsplit_max;
+            a.T = T; a.pos0 = p0; a.err = err;
+            CK(launch_prefill_attn(a, s));
+            planes(c->pf_att, qd, qd, nullptr);
+            gemm(1, B.o, nullptr, PF_RESID, c->pf_x, c->d, B.bias[3], nullptr, nullptr);
+        } else {
+            gemm(2, B.w1, &B.w3, PF_SWIGLU, c->pf_f, B.ffn_local, nullptr, nullptr, nullptr);
+            planes(c->pf_f, B.ffn_local, B.ffn_local, nullptr);
+            gemm(1, B.w2, nullptr, PF_RESID, c->pf_x, c->d, nullptr, nullptr, nullptr);
+        }
+    }
+}
+
+void enqueue_prefill(b2_ctx* c, int p0, int n, cudaStream_t s) {
+    prefill_workspace(c);
+    for (int done = 0; done < n; done += c->pf_tmax)
+        enqueue_prefill_chunk(c, p0 + done, std::min(c->pf_tmax, n - done), s);
 }
 
 void capture_graphs_once(b2_ctx* c);
@@ -1383,6 +1498,12 @@ int b2_prefill(b2_ctx* ctx, const int32_t* toks, int n) {
         if (n) CK(cudaMemcpyAsync(ctx->prompt + t, toks, (size_t)n * 4, cudaMemcpyHostToDevice, ctx->stream));
         // the reference samples (and advances its generator) on prompt steps too
         if (ctx->samp_mode) ctx->rng = lcg_advance(ctx->rng, n);
+        if (ctx->pf_ok && n >= 2) {
+            upload_state(ctx, t + n, t + n, 1 << 30, 0, -1);
+            enqueue_prefill(ctx, t, n, ctx->stream);
+            fetch_state(ctx);
+            return B2_OK;
+        }
         upload_state(ctx, t, t + n, 1 << 30, 0, -1);
         for (int i = 0; i < n; ++i) CK(cudaGraphLaunch(ctx->g_prefill, ctx->stream));
         fetch_state(ctx);
@@ -1405,10 +1526,13 @@ int b2_generate(b2_ctx* ctx, const int32_t* prompt, int n_prompt, int max_new, i
         // prompt step before the first emitted token (the prefill graph runs no head)
         ctx->rng = ctx->samp_mode ? lcg_advance(ctx->seed, (long long)std::min(n_prompt, ctx->max_seq + 1) - 1)
                                   : ctx->seed;
-        upload_state(ctx, 0, n_prompt, max_new, 0, eos);
         const long long total = (long long)n_prompt + max_new - 1;
         const int steps = (int)std::min<long long>(total, ctx->max_seq);
-        for (int t = 0; t < steps; ++t)
+        // prompt steps before the last one: one batched prefill when the plan is covered
+        const int pre = ctx->pf_ok ? std::min(n_prompt - 1, steps) : 0;
+        upload_state(ctx, pre, n_prompt, max_new, 0, eos);
+        if (pre >= 1) enqueue_prefill(ctx, 0, pre, ctx->stream);
+        for (int t = pre; t < steps; ++t)
             CK(cudaGraphLaunch(t < n_prompt - 1 ? ctx->g_prefill : ctx->g_decode, ctx->stream));
         CK(cudaMemcpyAsync(out_ids, ctx->out_ids, (size_t)max_new * 4, cudaMemcpyDeviceToHost, ctx->stream));
         fetch_state(ctx);
@@ -1525,6 +1649,7 @@ int b2_query(b2_ctx* ctx, const char* key, double* value) {
     else if (k == "sm_count") *value = ctx->sm_count;
     else if (k == "pdl") *value = ctx->pdl ? 1 : 0;
     else if (k == "token_kernel") *value = ctx->token ? 1 : 0;
+    else if (k == "prefill_batched") *value = ctx->pf_ok ? 1 : 0;
     else return B2_E_INVALID;
     return B2_OK;
 }

@@ -75,6 +75,10 @@ def _declare(L):
     L.b2_last_error.argtypes = [vp, C.c_char_p, C.c_int]
     L.b2_gemv_i8_rowscale.argtypes = [vp, C.c_int64, vp, vp, vp, vp, C.c_int, C.c_int, vp]
     L.b2_gemv_f32.argtypes = [vp, C.c_int64, vp, vp, vp, C.c_int, C.c_int, vp]
+    L.b2_gemm_i8_rowscale_workspace.restype = C.c_size_t
+    L.b2_gemm_i8_rowscale_workspace.argtypes = [C.c_int, C.c_int64]
+    L.b2_gemm_i8_rowscale.argtypes = [vp, C.c_int64, vp, vp, C.c_int64, vp, vp, C.c_int64, C.c_int, C.c_int,
+                                      C.c_int, vp, C.c_size_t, vp]
     L.b2_rmsnorm.argtypes = [vp, vp, vp, C.c_int, C.c_float, vp]
     L.b2_layernorm.argtypes = [vp, vp, vp, vp, C.c_int, C.c_float, vp]
     L.b2_rope_apply.argtypes = [vp, vp, C.c_int, C.c_int, C.c_int, vp]
@@ -309,6 +313,20 @@ def gemv_i8(W, scale, x, bias=None, y=None, n=None, stream=None):
     check(lib().b2_gemv_i8_rowscale(_ptr(W), ld, _ptr(scale), _ptr(x), _ptr(bias), _ptr(y), m, n,
                                     _stream(stream)))
     return y
+
+
+def gemm_i8(W, scale, X, bias=None, n=None, stream=None):
+    """T vectors at once on the tensor cores: X [T, n] f32 -> Y [T, m]; W int8 [m, ld]."""
+    import torch
+    m, ld = W.shape
+    T = X.shape[0]
+    n = n or ld
+    Y = torch.empty(T, m, dtype=torch.float32, device=W.device)
+    nb = lib().b2_gemm_i8_rowscale_workspace(T, ld)
+    ws = torch.empty(nb, dtype=torch.uint8, device=W.device)
+    check(lib().b2_gemm_i8_rowscale(_ptr(W), ld, _ptr(scale), _ptr(X), X.stride(0), _ptr(bias), _ptr(Y), m, m, n, T,
+                                    _ptr(ws), nb, _stream(stream)))
+    return Y
 
 
 def gemv_f32(W, x, bias=None, y=None, n=None, stream=None):

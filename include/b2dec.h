@@ -163,6 +163,19 @@ int b2_last_error(b2_ctx* ctx, char* buf, int len);
 int b2_gemv_i8_rowscale(const int8_t* W, int64_t ld, const float* scale, const float* x,
                         const float* bias, float* y, int m, int n, void* stream);
 
+/* The same for T input vectors at once, on the tensor cores (tcgen05 kind::i8
+ * over the byte planes of each vector's fixed-point copy): Y[t][j] = scale[j] *
+ * dot(W[j,:], X[t,:]) (+ bias[j]), bit-identical to T calls of
+ * b2_gemv_i8_rowscale. X [T][ldx] f32, Y [T][ldy] f32; rows (tokens) padded
+ * planes need b2_gemm_i8_rowscale_workspace(T, ld) bytes of workspace (16-byte
+ * aligned, no initialisation).
+ * Replaces: the batched linear loop the packer emits for seq > 1
+ * (aricode_pack.py:186-210: one arr_i8_matvec_f32_perrow per row of the input). */
+size_t b2_gemm_i8_rowscale_workspace(int T, int64_t ld);
+int b2_gemm_i8_rowscale(const int8_t* W, int64_t ld, const float* scale, const float* X, int64_t ldx,
+                        const float* bias, float* Y, int64_t ldy, int m, int n, int T, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
 /* y = W x + bias (bias NULL adds 0), W f32 with row stride ld (ld % 4 == 0).
  * Replaces: arr_f32_matvec (attention_kv_f32.ari:122-140, attention_mh_kv_f32.ari:150). */
 int b2_gemv_f32(const float* W, int64_t ld, const float* x, const float* bias, float* y,

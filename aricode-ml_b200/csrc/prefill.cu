@@ -3,7 +3,10 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <cstdio>
+#include <cstdlib>
 #include <mutex>
+#include <vector>
 
 #include "prefill.cuh"
 
@@ -43,6 +46,13 @@ bool byte_map(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, ui
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// B2_PF_TRACE=<file>: every GEMM launch synchronises and appends its per-CTA
+// timeline (u32 grid x, grid y, K; then u64 [CTA][8], see PfGemmParams::trace)
+const char* trace_path() {
+    static const char* p = std::getenv("B2_PF_TRACE");
+    return (p && p[0]) ? p : nullptr;
+}
+
 template <int NM>
 cudaError_t launch_nm(const void* A0, const void* A1, const unsigned char* planes, int ldp, const PfGemmParams& p,
                       cudaStream_t s) {
@@ -56,8 +66,26 @@ cudaError_t launch_nm(const void* A0, const void* A1, const unsigned char* plane
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, Sh::SmemBytes);
     if (e != cudaSuccess) return e;
     const dim3 grid((unsigned)((p.M + kPfRows - 1) / kPfRows), (unsigned)((p.T + Sh::N - 1) / Sh::N));
-    k<<<grid, kPfThreads, Sh::SmemBytes, s>>>(a0, a1, b, p);
-    return cudaGetLastError();
+    if (!trace_path()) {
+        k<<<grid, kPfThreads, Sh::SmemBytes, s>>>(a0, a1, b, p);
+        return cudaGetLastError();
+    }
+    PfGemmParams q = p;
+    const size_t n = (size_t)grid.x * grid.y * 8;
+    if ((e = cudaMalloc(&q.trace, n * 8)) != cudaSuccess) return e;
+    cudaMemsetAsync(q.trace, 0, n * 8, s);
+    k<<<grid, kPfThreads, Sh::SmemBytes, s>>>(a0, a1, b, q);
+    e = cudaStreamSynchronize(s);
+    std::vector<unsigned long long> h(n);
+    if (e == cudaSuccess) e = cudaMemcpy(h.data(), q.trace, n * 8, cudaMemcpyDeviceToHost);
+    cudaFree(q.trace);
+    if (FILE* f = std::fopen(trace_path(), "ab")) {
+        const unsigned hdr[4] = {grid.x, grid.y, (unsigned)p.K, (unsigned)NM};
+        std::fwrite(hdr, 4, 4, f);
+        std::fwrite(h.data(), 8, n, f);
+        std::fclose(f);
+    }
+    return e;
 }
 
 }  // namespace
@@ -83,10 +111,18 @@ cudaError_t launch_prefill_planes(const PfPlanesParams& p, int T, cudaStream_t s
 cudaError_t launch_prefill_attn(const PfAttnParams& p, cudaStream_t s) {
     const int G = p.H / p.KVH;
     const size_t smem = prefill_attn_smem(G, p.dh);
-    cudaError_t e = cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const int kd = (p.dh + 31) / 32;
+    auto k = kd <= 1 ? prefill_attn_part_kernel<1> : kd == 2 ? prefill_attn_part_kernel<2>
+                                                 : kd <= 4 ? prefill_attn_part_kernel<4> : prefill_attn_part_kernel<8>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    const dim3 grid((unsigned)p.KVH, (unsigned)((p.T + kPfAttnTokens - 1) / kPfAttnTokens));
-    prefill_attn_kernel<<<grid, kAttnThreads, smem, s>>>(p);
+    const int nchunks = (p.pos0 + p.T + kAttnChunk - 1) / kAttnChunk;
+    const dim3 grid((unsigned)p.KVH, (unsigned)nchunks, (unsigned)((p.T + kPfAttnGroup - 1) / kPfAttnGroup));
+    k<<<grid, kPfAttnWarps * 32, smem, s>>>(p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    const long long items = (long long)p.T * p.H;
+    prefill_attn_combine_kernel<<<(unsigned)((items + 7) / 8), 256, 0, s>>>(p);
     return cudaGetLastError();
 }
 

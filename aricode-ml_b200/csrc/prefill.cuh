@@ -24,8 +24,8 @@
 //           per CTA sharing each K/V chunk.
 //
 // Tile: 128 weight rows (TMEM lanes) x N tokens (TMEM columns), K in 128-byte
-// blocks. One matrix: N = 128, 4 accumulators = 512 TMEM columns; gate + up
-// paired: N = 64, 8 accumulators.
+// blocks; one accumulator per plane and matrix: one matrix N = 128 (4 x 128 TMEM
+// columns), gate + up paired N = 64 (8 x 64).
 #pragma once
 #include <cuda.h>
 
@@ -35,8 +35,8 @@ namespace b2 {
 
 constexpr int kPfRows = 128;           // weight rows per tile (MMA M)
 constexpr int kPfKBlock = 128;         // bytes of K per stage (one 128-byte swizzle row)
-constexpr int kPfThreads = 192;        // warps 0-3 epilogue, warp 4 copies, warp 5 MMAs
-constexpr int kPfAttnTokens = 4;       // prompt tokens per attention CTA
+constexpr int kPfEpiWarps = 8;         // epilogue warps: TMEM lane quarter w % 4, column half w / 4
+constexpr int kPfThreads = (kPfEpiWarps + 3) * 32;   // + weight copies, MMAs, plane copies
 
 enum PfEpi : int { PF_Q = 0, PF_K = 1, PF_V = 2, PF_RESID = 3, PF_SWIGLU = 4, PF_STORE = 5 };
 
@@ -60,6 +60,10 @@ struct PfGemmParams {
     int max_seq;
     int pos0;
     int* err;
+    // optional timeline (B2_PF_TRACE): per CTA 8 global-timer values: start, MMA
+    // thread's waits on weight / plane tiles (total ns), MMA loop end, weight and
+    // plane copy threads' waits for free slots (total ns), epilogue start and end
+    unsigned long long* trace;
 };
 
 struct PfAttnParams {
@@ -194,18 +198,25 @@ static __global__ void __launch_bounds__(256) prefill_planes_kernel(const __grid
 }
 
 // ------------------------------------------------------------------ GEMM
-// One CTA per (128 weight rows, N tokens) tile. NM = 1: one matrix, N = 128;
-// NM = 2: gate and up rows side by side (SwiGLU), N = 64. Shared memory: ring of
-// NS stages, each NM A tiles [128][128 B] then 4 plane tiles [N][128 B], all
-// 1024-byte aligned (swizzle atoms); then the mbarriers and the TMEM address.
+// One CTA per (128 weight rows, N tokens) tile; NM = 2 takes the gate and up
+// rows side by side (SwiGLU). Two rings in shared
+// memory: weight tiles (NM x [128][128 B] per K block, streamed from HBM, deeper)
+// and plane tiles (4 x [N][128 B] per K block, L2-resident), each with its own
+// copy warp, so the weight stream runs ahead of the plane stream; all tiles are
+// 1024-byte aligned (swizzle atoms).
+// (measured on B200: the single-matrix GEMM is fastest with 128 tokens a tile --
+// each MMA then reads 4 KB of weights and 4 KB of planes from shared memory for
+// 128 x 128 x 32 products; 64 tokens a tile with deeper rings ran 1.4x slower)
 template <int NM>
 struct PfShape {
     static constexpr int N = 128 / NM;
     static constexpr int ABytes = kPfRows * kPfKBlock;            // 16 KB
     static constexpr int BBytes = N * kPfKBlock;                  // one plane tile
-    static constexpr int StageBytes = NM * ABytes + 4 * BBytes;
-    static constexpr int NS = NM == 1 ? 2 : 3;
-    static constexpr int SmemBytes = 1024 + NS * StageBytes + 256;
+    static constexpr int AStage = NM * ABytes;
+    static constexpr int BStage = 4 * BBytes;
+    static constexpr int NSA = NM == 1 ? 4 : 3;
+    static constexpr int NSB = NM == 1 ? 2 : 3;
+    static constexpr int SmemBytes = 1024 + NSA * AStage + NSB * BStage + 1024;
     static constexpr int TmemCols = 512;
 };
 
@@ -214,14 +225,17 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 prefill_gemm_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_constant__ CUtensorMap mapA1,
                     const __grid_constant__ CUtensorMap mapB, const __grid_constant__ PfGemmParams p) {
     using Sh = PfShape<NM>;
-    constexpr int N = Sh::N, NS = Sh::NS;
+    constexpr int N = Sh::N, NSA = Sh::NSA, NSB = Sh::NSB;
     extern __shared__ unsigned char pf_smem_raw[];
     unsigned char* sm = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(pf_smem_raw) + 1023) & ~(uintptr_t)1023);
-    unsigned char* ring = sm;
-    uint64_t* full = reinterpret_cast<uint64_t*>(sm + NS * Sh::StageBytes);
-    uint64_t* empty = full + NS;
-    uint64_t* done = empty + NS;
+    unsigned char* ringA = sm;
+    unsigned char* ringB = sm + NSA * Sh::AStage;
+    uint64_t* fullA = reinterpret_cast<uint64_t*>(ringB + NSB * Sh::BStage);
+    uint64_t* emptyA = fullA + NSA;
+    uint64_t* fullB = emptyA + NSA;
+    uint64_t* emptyB = fullB + NSB;
+    uint64_t* done = emptyB + NSB;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
     volatile int* fail = reinterpret_cast<volatile int*>(tmem_slot + 1);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -229,12 +243,13 @@ prefill_gemm_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_cons
     const int KB = (p.K + kPfKBlock - 1) / kPfKBlock;
 
     if (tid == 0) {
-        for (int s = 0; s < NS; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int s = 0; s < NSA; ++s) { mbar_init(&fullA[s], 1); mbar_init(&emptyA[s], 1); }
+        for (int s = 0; s < NSB; ++s) { mbar_init(&fullB[s], 1); mbar_init(&emptyB[s], 1); }
         mbar_init(done, 1);
         fence_mbar_init();
         *fail = 0;
     }
-    if (warp == 0) {                                          // TMEM: all 512 columns (one CTA per SM)
+    if (warp == 0) {                                          // TMEM (one CTA per SM: shared memory)
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
                      ::"r"(smem_u32(tmem_slot)), "r"((uint32_t)Sh::TmemCols) : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -243,62 +258,116 @@ prefill_gemm_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_cons
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    unsigned long long* tr = p.trace ? p.trace + ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 8 : nullptr;
+    if (tr && tid == 0) tr[0] = globaltimer_ns();
 
-    if (warp == 4) {
-        // ---- copies: stage kb = NM weight tiles + the 4 plane tiles of K block kb
+    if (warp == kPfEpiWarps) {
+        // ---- weight copies: NM tiles of K block kb
         if (lane == 0) {
+            unsigned long long waited = 0;
             for (int kb = 0; kb < KB; ++kb) {
-                const int s = kb % NS, r = kb / NS;
-                if (r > 0 && !mbar_wait_bounded(&empty[s], (uint32_t)((r - 1) & 1))) { *fail = 1; break; }
-                unsigned char* st = ring + (size_t)s * Sh::StageBytes;
-                mbar_arrive_expect_tx(&full[s], (uint32_t)Sh::StageBytes);
-                tma_load_2d(st, &mapA0, kb * kPfKBlock, m0, &full[s]);
-                if constexpr (NM == 2) tma_load_2d(st + Sh::ABytes, &mapA1, kb * kPfKBlock, m0, &full[s]);
+                const int s = kb % NSA, r = kb / NSA;
+                const unsigned long long tw = tr ? globaltimer_ns() : 0ull;
+                if (r > 0 && !mbar_wait_bounded(&emptyA[s], (uint32_t)((r - 1) & 1))) { *fail = 1; break; }
+                if (tr) waited += globaltimer_ns() - tw;
+                unsigned char* st = ringA + (size_t)s * Sh::AStage;
+                mbar_arrive_expect_tx(&fullA[s], (uint32_t)Sh::AStage);
+                tma_load_2d(st, &mapA0, kb * kPfKBlock, m0, &fullA[s]);
+                if constexpr (NM == 2) tma_load_2d(st + Sh::ABytes, &mapA1, kb * kPfKBlock, m0, &fullA[s]);
+            }
+            if (tr) tr[4] = waited;
+        }
+    } else if (warp == kPfEpiWarps + 2) {
+        // ---- plane copies: the 4 plane tiles of K block kb
+        if (lane == 0) {
+            unsigned long long waited = 0;
+            for (int kb = 0; kb < KB; ++kb) {
+                const int s = kb % NSB, r = kb / NSB;
+                const unsigned long long tw = tr ? globaltimer_ns() : 0ull;
+                if (r > 0 && !mbar_wait_bounded(&emptyB[s], (uint32_t)((r - 1) & 1))) { *fail = 1; break; }
+                if (tr) waited += globaltimer_ns() - tw;
+                unsigned char* st = ringB + (size_t)s * Sh::BStage;
+                mbar_arrive_expect_tx(&fullB[s], (uint32_t)Sh::BStage);
 #pragma unroll
                 for (int pl = 0; pl < 4; ++pl)
-                    tma_load_2d(st + NM * Sh::ABytes + pl * Sh::BBytes, &mapB, kb * kPfKBlock, pl * p.Tpad + n0,
-                                &full[s]);
+                    tma_load_2d(st + pl * Sh::BBytes, &mapB, kb * kPfKBlock, pl * p.Tpad + n0, &fullB[s]);
             }
+            if (tr) tr[5] = waited;
         }
-    } else if (warp == 5) {
+    } else if (warp == kPfEpiWarps + 1) {
         // ---- MMAs: per K block 4 steps of 32 bytes x NM matrices x 4 planes
         if (lane == 0) {
             const uint32_t id_u = umma_idesc_i8(N, false), id_s = umma_idesc_i8(N, true);
+            unsigned long long wa = 0, wb = 0;
             for (int kb = 0; kb < KB; ++kb) {
-                const int s = kb % NS;
-                if (!mbar_wait_bounded(&full[s], (uint32_t)((kb / NS) & 1))) { *fail = 1; break; }
+                const int sa = kb % NSA, sb = kb % NSB;
+                const unsigned long long t0 = tr ? globaltimer_ns() : 0ull;
+                if (!mbar_wait_bounded(&fullA[sa], (uint32_t)((kb / NSA) & 1))) { *fail = 1; break; }
+                const unsigned long long t1 = tr ? globaltimer_ns() : 0ull;
+                if (!mbar_wait_bounded(&fullB[sb], (uint32_t)((kb / NSB) & 1))) { *fail = 1; break; }
+                if (tr) { wa += t1 - t0; wb += globaltimer_ns() - t1; }
                 tc_fence_after();
-                const uint32_t st = smem_u32(ring + (size_t)s * Sh::StageBytes);
+                const uint32_t sta = smem_u32(ringA + (size_t)sa * Sh::AStage);
+                const uint32_t stb = smem_u32(ringB + (size_t)sb * Sh::BStage);
 #pragma unroll
                 for (int kk = 0; kk < kPfKBlock / 32; ++kk) {
 #pragma unroll
                     for (int mt = 0; mt < NM; ++mt) {
-                        const uint64_t ad = umma_desc_sw128(st + mt * Sh::ABytes + 32 * kk);
+                        const uint64_t ad = umma_desc_sw128(sta + mt * Sh::ABytes + 32 * kk);
 #pragma unroll
                         for (int pl = 0; pl < 4; ++pl) {
-                            const uint64_t bd = umma_desc_sw128(st + NM * Sh::ABytes + pl * Sh::BBytes + 32 * kk);
+                            const uint64_t bd = umma_desc_sw128(stb + pl * Sh::BBytes + 32 * kk);
                             umma_i8(tmem + (uint32_t)((mt * 4 + pl) * N), ad, bd, pl == 3 ? id_s : id_u,
                                     (kb > 0 || kk > 0) ? 1u : 0u);
                         }
                     }
                 }
-                umma_commit(&empty[s]);                        // the stage is free once these MMAs are done
+                umma_commit(&emptyA[sa]);                      // both stages are free once these MMAs are done
+                umma_commit(&emptyB[sb]);
             }
             umma_commit(done);
+            if (tr) { tr[1] = wa; tr[2] = wb; tr[3] = globaltimer_ns(); }
         }
     } else {
-        // ---- epilogue: warp w reads TMEM lanes 32w .. 32w + 31 = weight rows m0 + 32w + lane
-        const bool ok = mbar_wait_bounded(done, 0);
-        tc_fence_after();
-        const int m = m0 + 32 * warp + lane;
-        const uint32_t trow = tmem + ((uint32_t)(32 * warp) << 16);
+        // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 = weight rows
+        // m0 + 32 (w % 4) + lane, token columns of half w / 4. Per 16-token chunk
+        // every global input (the residual, the RoPE rows) is requested before the
+        // TMEM reads, so their latencies overlap; the tokens' shifts were staged in
+        // shared memory while the MMAs ran.
+        int* sS = reinterpret_cast<int*>(const_cast<int*>(fail) + 1);        // [N]
+        for (int i = tid; i < N; i += kPfEpiWarps * 32) sS[i] = n0 + i < p.T ? p.S[n0 + i] : 0;
+        const int quarter = warp & 3, half = warp >> 2;
+        const int m = m0 + 32 * quarter + lane;
+        const uint32_t trow = tmem + ((uint32_t)(32 * quarter) << 16);
         float sc[2] = {0.0f, 0.0f}, bi = 0.0f;
         if (m < p.M) {
             sc[0] = p.scale[0][m];
             if (NM == 2) sc[1] = p.scale[1][m];
             if (p.bias) bi = p.bias[m];
         }
-        for (int c0 = 0; c0 < N; c0 += 16) {
+        const bool rope = (p.epi == PF_Q || p.epi == PF_K) && p.rope;
+        const int hd = rope ? (m & ~1) % p.dh : 0;
+        asm volatile("bar.sync 2, %0;" ::"n"(kPfEpiWarps * 32) : "memory");   // sS complete
+        const bool ok = mbar_wait_bounded(done, 0);
+        tc_fence_after();
+        if (tr && tid == 0) tr[6] = globaltimer_ns();
+        constexpr int NH = N / (kPfEpiWarps / 4);                   // columns per warp
+        for (int c0 = half * NH; c0 < (half + 1) * NH; c0 += 16) {
+            float in0[16], in1[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                const int t = n0 + c0 + j;
+                in0[j] = 0.0f; in1[j] = 0.0f;
+                if (t < p.T && m < p.M) {
+                    if (p.epi == PF_RESID) {
+                        in0[j] = p.out[(size_t)t * p.ldo + m];
+                    } else if (rope) {
+                        const float* tr = p.rope_tab + (size_t)(p.pos0 + t) * p.dh + hd;
+                        in0[j] = tr[0];
+                        in1[j] = tr[1];
+                    }
+                }
+            }
             float v[NM][16];
 #pragma unroll
             for (int mt = 0; mt < NM; ++mt) {
@@ -308,10 +377,8 @@ prefill_gemm_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_cons
                 tmem_wait_ld();
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
-                    const int t = n0 + c0 + j;
-                    const int S = t < p.T ? p.S[t] : 0;
                     const int pls[4] = {(int)r[0][j], (int)r[1][j], (int)r[2][j], (int)r[3][j]};
-                    v[mt][j] = xfix_row(pls, S);
+                    v[mt][j] = xfix_row(pls, sS[c0 + j]);
                 }
             }
 #pragma unroll
@@ -327,11 +394,8 @@ prefill_gemm_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_cons
                 if (p.epi == PF_Q || p.epi == PF_K) {
                     // interleaved RoPE pair (2i, 2i + 1) = lanes (2i, 2i + 1) of this warp
                     const float other = __shfl_xor_sync(0xffffffffu, y, 1);
-                    if (p.rope) {
-                        const int pos = p.pos0 + (t < p.T ? t : 0);
-                        const int hd = (m & ~1) % p.dh;
-                        const float* tr = p.rope_tab + (size_t)pos * p.dh + hd;
-                        const float c = tr[0], sn = tr[1];
+                    if (rope) {
+                        const float c = in0[j], sn = in1[j];
                         y = (m & 1) ? fadd(fmul(other, sn), fmul(y, c)) : fsub(fmul(y, c), fmul(other, sn));
                     }
                 }
@@ -340,18 +404,18 @@ prefill_gemm_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_cons
                     p.out[(size_t)t * p.ldo + m] = fmul(y, p.qscale);
                 } else if (p.epi == PF_K || p.epi == PF_V) {
                     const int pos = p.pos0 + t;
-                    const int kvh = m / p.dh, hd = m % p.dh;
-                    if (pos < p.max_seq) p.cache[((size_t)kvh * p.max_seq + pos) * p.dh + hd] = y;
+                    const int kvh = m / p.dh, hdv = m % p.dh;
+                    if (pos < p.max_seq) p.cache[((size_t)kvh * p.max_seq + pos) * p.dh + hdv] = y;
                     else set_err(p.err, B2_DEV_ERR_KV_OVERFLOW);
                 } else if (p.epi == PF_RESID) {
-                    float* o = p.out + (size_t)t * p.ldo + m;
-                    *o = fadd(y, *o);
+                    p.out[(size_t)t * p.ldo + m] = fadd(y, in0[j]);
                 } else {
                     p.out[(size_t)t * p.ldo + m] = y;
                 }
             }
         }
         if (!ok) *fail = 1;
+        if (tr && tid == 0) tr[7] = globaltimer_ns();
     }
     tc_fence_before();
     __syncthreads();
@@ -364,149 +428,168 @@ prefill_gemm_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_cons
 }
 
 // ------------------------------------------------------------------ attention
-// CTA (kv head, group of kPfAttnTokens consecutive tokens): the K and V chunks of
-// keys [64s, 64s + 64) are copied once and used by every token of the group that
-// sees them; per token and query head the decode kernel's chunk arithmetic gives
-// (m_s, l_s, o_s) into `part`; then the same combine with the -60 tail.
+// Two launches, with the decode attention's arithmetic in the same order:
+//  part:    CTA (kv head, 64-key chunk s, group of 64 tokens) copies K and V of keys
+//           [64s, 64s + 64) into shared memory once; its 8 warps take the group's
+//           tokens that see the chunk (token t sees keys 0 .. pos0 + t), and for
+//           each of them and each query head of the kv head compute the chunk's
+//           (o_s, m_s, l_s): scores as lane partials over d = lane, lane + 32, ...
+//           reduced by butterflies, chunk max / exp / sum with lane L on keys L and
+//           L + 32, o[d] a sequential FMA chain over the keys;
+//  combine: one warp per (token, query head) merges its splits in split order
+//           with the -60 tail, exactly as the decode combine does.
+constexpr int kPfAttnGroup = 64;        // tokens per attention CTA
+constexpr int kPfAttnWarps = 8;
+
 inline size_t prefill_attn_smem(int G, int dh) {
-    return 64 + 2 * (size_t)kAttnChunk * dh * 4 + (size_t)kPfAttnTokens * G * dh * 4 +
-           (size_t)G * kAttnChunk * 4 + 4 * (size_t)G * 4 + 64;
+    (void)G;
+    return 64 + 2 * (size_t)kAttnChunk * dh * 4 + (size_t)kPfAttnWarps * kAttnChunk * 4 + 64;
 }
 
-static __global__ void __launch_bounds__(kAttnThreads) prefill_attn_kernel(const __grid_constant__ PfAttnParams p) {
+// KD: head dimensions a lane owns (d = lane, lane + 32, ...; dh <= 32 KD, exact
+// when dh == 32 KD, guarded otherwise)
+template <int KD>
+__global__ void __launch_bounds__(kPfAttnWarps * 32) prefill_attn_part_kernel(const __grid_constant__ PfAttnParams p) {
     extern __shared__ __align__(128) unsigned char asm_raw[];
     uint64_t* bar = reinterpret_cast<uint64_t*>(asm_raw);
     const int G = p.H / p.KVH, dh = p.dh;
     float* Ks = reinterpret_cast<float*>(asm_raw + 64);        // [64][dh]
     float* Vs = Ks + kAttnChunk * dh;                           // [64][dh]
-    float* qs = Vs + kAttnChunk * dh;                           // [tokens][G][dh]
-    float* sc = qs + kPfAttnTokens * G * dh;                    // [G][64]
-    float* mpart = sc + G * kAttnChunk;                         // [G]
-    float* lpart = mpart + G;
-    float* wtot = lpart + G;                                    // [G] combine: l
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int kvh = blockIdx.x, t0 = blockIdx.y * kPfAttnTokens;
-    const int nt = min(kPfAttnTokens, p.T - t0);
-    if (tid == 0) { mbar_init(bar, 1); fence_mbar_init(); }
-    const int h0 = kvh * G;
-    for (int i = tid; i < nt * G * dh; i += kAttnThreads) {
-        const int tt = i / (G * dh), r = i % (G * dh);
-        qs[i] = p.q[(size_t)(t0 + tt) * p.H * dh + (size_t)h0 * dh + r];
+    const int kvh = blockIdx.x, s = blockIdx.y, g0 = blockIdx.z * kPfAttnGroup;
+    float* e = Vs + kAttnChunk * dh + warp * kAttnChunk;        // [64] this warp's exponentials
+    const int j0 = s * kAttnChunk;
+    const int tlast = min(g0 + kPfAttnGroup, p.T) - 1;
+    const int n_max = p.pos0 + tlast + 1;
+    if (j0 >= n_max) return;                                    // no token of the group reaches the chunk
+    const int clen = min(kAttnChunk, n_max - j0);
+    if (tid == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+        const uint32_t bytes = (uint32_t)clen * dh * 4;
+        mbar_arrive_expect_tx(bar, 2 * bytes);
+        bulk_g2s(Ks, p.K + ((size_t)kvh * p.max_seq + j0) * dh, bytes, bar);
+        bulk_g2s(Vs, p.V + ((size_t)kvh * p.max_seq + j0) * dh, bytes, bar);
     }
     __syncthreads();
-    const int n_last = p.pos0 + t0 + nt;                        // keys seen by the group's last token
-    const int nsplit_all = (n_last + kAttnChunk - 1) / kAttnChunk;
-    const float* Kh = p.K + (size_t)kvh * p.max_seq * dh;
-    const float* Vh = p.V + (size_t)kvh * p.max_seq * dh;
+    if (!mbar_wait_bounded(bar, 0)) {
+        set_err(p.err, B2_DEV_ERR_TIMEOUT);
+        return;
+    }
+    const int h0 = kvh * G;
     const int stride = dh + 2;
-    __shared__ int s_ok;
-    bool ok = true;
-    for (int s = 0; s < nsplit_all; ++s) {
-        const int j0 = s * kAttnChunk;
-        const int clen = min(kAttnChunk, n_last - j0);
-        if (tid == 0) {
-            // the previous chunk's generic reads are ordered before the copy's writes
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            const uint32_t bytes = (uint32_t)clen * dh * 4;
-            mbar_arrive_expect_tx(bar, 2 * bytes);
-            bulk_g2s(Ks, Kh + (size_t)j0 * dh, bytes, bar);
-            bulk_g2s(Vs, Vh + (size_t)j0 * dh, bytes, bar);
-            s_ok = mbar_wait_bounded(bar, (uint32_t)(s & 1)) ? 1 : 0;
-            if (!s_ok) {
-                set_err(p.err, B2_DEV_ERR_TIMEOUT);
-                mbar_wait_bounded(bar, (uint32_t)(s & 1));      // last bounded wait for the copies in flight
-            }
-        }
-        __syncthreads();
-        if (!s_ok) { ok = false; break; }                        // uniform over the CTA
-        mbar_wait_bounded(bar, (uint32_t)(s & 1));               // complete: each thread's own acquire
-        for (int tt = 0; tt < nt; ++tt) {
-            const int n = p.pos0 + t0 + tt + 1;                  // keys of this token
-            if (j0 >= n) continue;                               // uniform over the CTA
-            const int len = min(kAttnChunk, n - j0);
-            const float* qt = qs + tt * G * dh;
-            for (int jj = warp; jj < len; jj += kAttnThreads / 32) {
-                const float* kr = Ks + jj * dh;
-                float kv[8];
+    // first token of the group that sees the chunk: pos0 + t + 1 > j0
+    const int tfirst = max(g0, j0 - p.pos0);
+    for (int t = tfirst + warp; t <= tlast; t += kPfAttnWarps) {
+        const int n = p.pos0 + t + 1;
+        const int len = min(kAttnChunk, n - j0);
+        for (int g = 0; g < G; ++g) {
+            const float* qt = p.q + (size_t)t * p.H * dh + (size_t)(h0 + g) * dh;
+            const bool full = dh == 32 * KD;
+            float qv[KD];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int d = lane + 32 * i;
-                    kv[i] = d < dh ? kr[d] : 0.0f;
-                }
-                for (int g = 0; g < G; ++g) {
+            for (int i = 0; i < KD; ++i) {
+                const int d = lane + 32 * i;
+                qv[i] = (full || d < dh) ? __ldg(qt + d) : 0.0f;
+            }
+            // scores, eight keys at a time: lane partials, then the exchange butterfly
+            // (each key's total bit-identical to its own butterfly); key jj0 + lane / 4
+            // ends in lanes 4k .. 4k + 3, parked in e[]
+            for (int jj0 = 0; jj0 < len; jj0 += 8) {
+                float v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
                     float a = 0.0f;
+                    if (jj0 + u < len) {
+                        const float* kr = Ks + (jj0 + u) * dh;
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const int d = lane + 32 * i;
-                        if (d < dh) a = ffma(qt[g * dh + d], kv[i], a);
+                        for (int i = 0; i < KD; ++i) {
+                            const int d = lane + 32 * i;
+                            if (full || d < dh) a = ffma(qv[i], kr[d], a);
+                        }
                     }
-                    a = butterfly32(a);
-                    if (lane == 0) sc[g * kAttnChunk + jj] = a;
+                    v[u] = a;
+                }
+                exchange_butterfly<8>(v, lane);
+                if ((lane & 3) == 0 && jj0 + (lane >> 2) < len) e[jj0 + (lane >> 2)] = v[0];
+            }
+            __syncwarp();
+            const float sc0 = lane < len ? e[lane] : 0.0f;
+            const float sc1 = lane + 32 < len ? e[lane + 32] : 0.0f;
+            __syncwarp();
+            // chunk max (the decode order: lane-strided, then the xor tree), exp, sum
+            float mx = -__int_as_float(0x7f800000);
+            bool any = false;
+            if (lane < len) { mx = sc0; any = true; }
+            if (lane + 32 < len) { mx = any ? fmaxf(mx, sc1) : sc1; any = true; }
+            for (int o = 16; o >= 1; o >>= 1) {
+                const float om = __shfl_xor_sync(0xffffffffu, mx, o);
+                const int oa = __shfl_xor_sync(0xffffffffu, (int)any, o);
+                if (oa) { mx = any ? fmaxf(mx, om) : om; any = true; }
+            }
+            float a = 0.0f;
+            if (lane < len) { const float v = exp_f(fsub(sc0, mx)); e[lane] = v; a = fadd(a, v); }
+            if (lane + 32 < len) { const float v = exp_f(fsub(sc1, mx)); e[lane + 32] = v; a = fadd(a, v); }
+            a = butterfly32(a);
+            __syncwarp();
+            float* pp = p.part + (((size_t)t * p.H + h0 + g) * p.nsplit_max + s) * stride;
+            float o[KD];
+#pragma unroll
+            for (int i = 0; i < KD; ++i) o[i] = 0.0f;
+            for (int jj = 0; jj < len; ++jj) {
+                const float ej = e[jj];
+                const float* vr = Vs + jj * dh;
+#pragma unroll
+                for (int i = 0; i < KD; ++i) {
+                    const int d = lane + 32 * i;
+                    if (full || d < dh) o[i] = ffma(ej, vr[d], o[i]);
                 }
             }
-            __syncthreads();
-            for (int g = warp; g < G; g += kAttnThreads / 32) {
-                float mx = -__int_as_float(0x7f800000);
-                bool any = false;
-                for (int jj = lane; jj < len; jj += 32) {
-                    const float v = sc[g * kAttnChunk + jj];
-                    mx = any ? fmaxf(mx, v) : v;
-                    any = true;
-                }
-                for (int o = 16; o >= 1; o >>= 1) {
-                    const float om = __shfl_xor_sync(0xffffffffu, mx, o);
-                    const int oa = __shfl_xor_sync(0xffffffffu, (int)any, o);
-                    if (oa) { mx = any ? fmaxf(mx, om) : om; any = true; }
-                }
-                float a = 0.0f;
-                for (int jj = lane; jj < len; jj += 32) {
-                    const float e = exp_f(fsub(sc[g * kAttnChunk + jj], mx));
-                    sc[g * kAttnChunk + jj] = e;
-                    a = fadd(a, e);
-                }
-                a = butterfly32(a);
-                if (lane == 0) { mpart[g] = mx; lpart[g] = a; }
+#pragma unroll
+            for (int i = 0; i < KD; ++i) {
+                const int d = lane + 32 * i;
+                if (full || d < dh) pp[d] = o[i];
             }
-            __syncthreads();
-            for (int it = tid; it < G * dh; it += kAttnThreads) {
-                const int g = it / dh, d = it % dh;
-                const float* e = sc + g * kAttnChunk;
-                float a = 0.0f;
-                for (int jj = 0; jj < len; ++jj) a = ffma(e[jj], Vs[jj * dh + d], a);
-                float* pp = p.part + (((size_t)(t0 + tt) * p.H + h0 + g) * p.nsplit_max + s) * stride;
-                pp[d] = a;
-                if (d == 0) { pp[dh] = mpart[g]; pp[dh + 1] = lpart[g]; }
-            }
-            __syncthreads();                                     // sc / mpart reused by the next token
+            if (lane == 0) { pp[dh] = mx; pp[dh + 1] = a; }
+            __syncwarp();                                       // e[] reused by the next head / token
         }
     }
-    if (!ok) return;
-    __syncthreads();                                             // this CTA's partials are visible to it
-    for (int tt = 0; tt < nt; ++tt) {
-        const int n = p.pos0 + t0 + tt + 1;
-        const int nsplit = (n + kAttnChunk - 1) / kAttnChunk;
-        for (int g = tid; g < G; g += kAttnThreads) {
-            const float* base = p.part + ((size_t)(t0 + tt) * p.H + h0 + g) * p.nsplit_max * stride;
-            float M = base[dh];
-            for (int s = 1; s < nsplit; ++s) M = fmaxf(M, base[(size_t)s * stride + dh]);
-            if (n < p.max_seq) M = fmaxf(M, -60.0f);
-            float l = 0.0f;
-            for (int s = 0; s < nsplit; ++s) l = ffma(base[(size_t)s * stride + dh + 1], exp_f(fsub(base[(size_t)s * stride + dh], M)), l);
-            if (n < p.max_seq) l = ffma((float)(p.max_seq - n), exp_f(fsub(-60.0f, M)), l);
-            wtot[g] = l;
-            mpart[g] = M;
+}
+
+static __global__ void __launch_bounds__(256) prefill_attn_combine_kernel(const __grid_constant__ PfAttnParams p) {
+    const int lane = threadIdx.x & 31;
+    const long long item = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);   // (token, query head)
+    if (item >= (long long)p.T * p.H) return;
+    const int t = (int)(item / p.H), h = (int)(item % p.H), dh = p.dh;
+    const int n = p.pos0 + t + 1;
+    const int nsplit = (n + kAttnChunk - 1) / kAttnChunk;
+    const int stride = dh + 2;
+    const float* base = p.part + ((size_t)t * p.H + h) * p.nsplit_max * stride;
+    float M = __ldg(base + dh);
+    for (int s = 1; s < nsplit; ++s) M = fmaxf(M, __ldg(base + (size_t)s * stride + dh));
+    if (n < p.max_seq) M = fmaxf(M, -60.0f);
+    float l = 0.0f;
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = 0.0f;
+    for (int s = 0; s < nsplit; ++s) {
+        const float* ps = base + (size_t)s * stride;
+        float ov[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int d = lane + 32 * i;
+            ov[i] = d < dh ? __ldg(ps + d) : 0.0f;
         }
-        __syncthreads();
-        for (int it = tid; it < G * dh; it += kAttnThreads) {
-            const int g = it / dh, d = it % dh;
-            const float* base = p.part + ((size_t)(t0 + tt) * p.H + h0 + g) * p.nsplit_max * stride;
-            const float M = mpart[g];
-            float o = 0.0f;
-            for (int s = 0; s < nsplit; ++s)
-                o = ffma(base[(size_t)s * stride + d], exp_f(fsub(base[(size_t)s * stride + dh], M)), o);
-            p.out[(size_t)(t0 + tt) * p.H * dh + (size_t)(h0 + g) * dh + d] = fdiv(o, wtot[g]);
-        }
-        __syncthreads();
+        const float w = exp_f(fsub(__ldg(ps + dh), M));
+        l = ffma(__ldg(ps + dh + 1), w, l);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = ffma(ov[i], w, o[i]);
+    }
+    if (n < p.max_seq) l = ffma((float)(p.max_seq - n), exp_f(fsub(-60.0f, M)), l);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int d = lane + 32 * i;
+        if (d < dh) p.out[(size_t)t * p.H * dh + (size_t)h * dh + d] = fdiv(o[i], l);
     }
 }
 

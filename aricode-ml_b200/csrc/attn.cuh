@@ -31,6 +31,11 @@ struct AttnParams {
     int n_fixed;
     int* err;
     Mirror mir;            // token kernel, tensor parallelism: out also written to the peers
+    // batched decode (grid z = sequence): sequence z reads q + z * sq, K/V + z * skv,
+    // writes out + z * sq, uses part + z * spart and counters + z * KVH, and sees
+    // n_of[z] + 1 keys (n_of: positions; nullptr for one sequence)
+    const int* n_of;
+    long long sq, skv, spart;
 };
 
 // bytes of scratch one call needs
@@ -69,14 +74,20 @@ attn_decode_kernel(const __grid_constant__ AttnParams p) {
     pdl_wait();
     const bool active = p.st ? (*(volatile int*)&p.st->active != 0) : true;
     if (!active) return;
-    const int n = p.st ? *(volatile int*)&p.st->pos + 1 : p.n_fixed;
+    const int z = blockIdx.z;
+    const int n = p.n_of ? p.n_of[z] + 1 : (p.st ? *(volatile int*)&p.st->pos + 1 : p.n_fixed);
     const int s = blockIdx.x, kvh = blockIdx.y;
+    // this sequence's inputs, cache, outputs and scratch (z = 0 for one sequence)
+    const float* __restrict__ qz = p.q + z * p.sq;
+    float* outz = p.out + z * p.sq;
+    float* partz = p.part + z * p.spart;
+    unsigned* cntz = p.counters + (size_t)z * p.KVH;
     const int nsplit = (n + kAttnChunk - 1) / kAttnChunk;
     if (s >= nsplit) return;
     const int j0 = s * kAttnChunk;
     const int len = min(kAttnChunk, n - j0);
-    const float* Kh = p.K + (size_t)kvh * p.max_seq * dh;
-    const float* Vh = p.V + (size_t)kvh * p.max_seq * dh;
+    const float* Kh = p.K + z * p.skv + (size_t)kvh * p.max_seq * dh;
+    const float* Vh = p.V + z * p.skv + (size_t)kvh * p.max_seq * dh;
     if (tid == 0) {
         const uint32_t bytes = (uint32_t)len * dh * 4;
         mbar_arrive_expect_tx(bar, 2 * bytes);
@@ -84,7 +95,7 @@ attn_decode_kernel(const __grid_constant__ AttnParams p) {
         bulk_g2s(Vs, Vh + (size_t)j0 * dh, bytes, bar);
     }
     const int h0 = kvh * G;
-    for (int i = tid; i < G * dh; i += kAttnThreads) qs[i] = p.q[(size_t)h0 * dh + i];
+    for (int i = tid; i < G * dh; i += kAttnThreads) qs[i] = qz[(size_t)h0 * dh + i];
     if (!mbar_wait_bounded(bar, 0)) {
         set_err(p.err, B2_DEV_ERR_TIMEOUT);
         mbar_wait_bounded(bar, 0);                 // last bounded wait for the copies in flight
@@ -146,20 +157,20 @@ attn_decode_kernel(const __grid_constant__ AttnParams p) {
         const float* e = sc + g * kAttnChunk;
         float a = 0.0f;
         for (int jj = 0; jj < len; ++jj) a = ffma(e[jj], Vs[jj * dh + d], a);
-        float* pp = p.part + ((size_t)(h0 + g) * p.nsplit_max + s) * stride;
+        float* pp = partz + ((size_t)(h0 + g) * p.nsplit_max + s) * stride;
         pp[d] = a;
         if (d == 0) { pp[dh] = mpart[g]; pp[dh + 1] = lpart[g]; }
     }
     __threadfence();
     __syncthreads();
-    if (tid == 0) last = (atomicAdd(p.counters + kvh, 1u) == (unsigned)(nsplit - 1));
+    if (tid == 0) last = (atomicAdd(cntz + kvh, 1u) == (unsigned)(nsplit - 1));
     __syncthreads();
     if (!last) return;
     __threadfence();
 
     // combine the splits (and the -60 tail) for the G heads of this kv head
     for (int g = tid; g < G; g += kAttnThreads) {
-        const float* base = p.part + (size_t)(h0 + g) * p.nsplit_max * stride;
+        const float* base = partz + (size_t)(h0 + g) * p.nsplit_max * stride;
         float M = __ldcg(base + dh);
         for (int t = 1; t < nsplit; ++t) M = fmaxf(M, __ldcg(base + (size_t)t * stride + dh));
         if (n < p.max_seq) M = fmaxf(M, -60.0f);
@@ -175,13 +186,13 @@ attn_decode_kernel(const __grid_constant__ AttnParams p) {
     __syncthreads();
     for (int it = tid; it < G * dh; it += kAttnThreads) {
         const int g = it / dh, d = it % dh;
-        const float* base = p.part + (size_t)(h0 + g) * p.nsplit_max * stride;
+        const float* base = partz + (size_t)(h0 + g) * p.nsplit_max * stride;
         float o = 0.0f;
         for (int t = 0; t < nsplit; ++t)
             o = ffma(__ldcg(base + (size_t)t * stride + d), wsm[g * p.nsplit_max + t], o);
-        p.out[(size_t)(h0 + g) * dh + d] = fdiv(o, Lsm[g]);
+        outz[(size_t)(h0 + g) * dh + d] = fdiv(o, Lsm[g]);
     }
-    if (tid == 0) p.counters[kvh] = 0u;
+    if (tid == 0) cntz[kvh] = 0u;
 }
 
 }  // namespace b2

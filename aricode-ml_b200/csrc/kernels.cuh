@@ -522,6 +522,8 @@ inline GemvShape gemv_shape(const GemvParams& p, int esz, int grid_cap) {
 cudaError_t launch_gemv(const GemvParams& p, bool w_i8, cudaStream_t s, bool pdl, int grid_cap,
                         GemvShape* out_shape = nullptr);
 cudaError_t launch_attn(const AttnParams& p, cudaStream_t s, bool pdl);
+// the same kernel over nseq sequences (grid z; AttnParams::n_of and the strides)
+cudaError_t launch_attn_batched(const AttnParams& p, int nseq, cudaStream_t s);
 cudaError_t launch_embed(const EmbedParams& p, cudaStream_t s, bool pdl);
 
 }  // namespace b2

@@ -69,6 +69,15 @@ cudaError_t launch_attn(const AttnParams& p, cudaStream_t s, bool pdl) {
     return launch_ex(attn_decode_kernel, dim3(p.nsplit_max, p.KVH), dim3(kAttnThreads), smem, s, pdl, p);
 }
 
+cudaError_t launch_attn_batched(const AttnParams& p, int nseq, cudaStream_t s) {
+    const int G = p.H / p.KVH;
+    const size_t smem = attn_smem_bytes(G, p.dh, p.nsplit_max);
+    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return e;
+    return launch_ex(attn_decode_kernel, dim3(p.nsplit_max, p.KVH, nseq), dim3(kAttnThreads), smem, s, false, p);
+}
+
 cudaError_t launch_embed(const EmbedParams& p, cudaStream_t s, bool pdl) {
     return launch_ex(embed_kernel, dim3(1), dim3(256), 0, s, pdl, p);
 }

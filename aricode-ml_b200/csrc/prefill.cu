@@ -126,6 +126,17 @@ cudaError_t launch_prefill_attn(const PfAttnParams& p, cudaStream_t s) {
     return cudaGetLastError();
 }
 
+cudaError_t launch_batch_tail(const float* logits, int vocab, const BatchState& b, int B, cudaStream_t s) {
+    batch_argmax_kernel<<<B, 1024, 0, s>>>(logits, vocab, b);
+    batch_count_kernel<<<1, 1, 0, s>>>(b);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_batch_check(const BatchState& b, int B, cudaStream_t s) {
+    batch_check_kernel<<<(B + 127) / 128, 128, 0, s>>>(b, B);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_prefill_embed(const int8_t* emb, const float* emb_s, long long ld, const int* ids, int pos0,
                                  int vocab, int d, float* x, int T, int* err, cudaStream_t s) {
     prefill_embed_kernel<<<T, 256, 0, s>>>(emb, emb_s, ld, ids, pos0, vocab, d, x, err);

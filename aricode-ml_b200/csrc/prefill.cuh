@@ -59,6 +59,11 @@ struct PfGemmParams {
     float* cache;            // [kv_heads][max_seq][dh]
     int max_seq;
     int pos0;
+    // batched decode: token t is the next token of sequence t, at position
+    // tok_pos[t], its cache rows at cache + t * cache_seq (nullptr / 0: one
+    // sequence, token t at position pos0 + t)
+    const int* tok_pos;
+    long long cache_seq;
     int* err;
     // optional timeline (B2_PF_TRACE): per CTA 8 global-timer values: start, MMA
     // thread's waits on weight / plane tiles (total ns), MMA loop end, weight and
@@ -216,7 +221,7 @@ struct PfShape {
     static constexpr int BStage = 4 * BBytes;
     static constexpr int NSA = NM == 1 ? 4 : 3;
     static constexpr int NSB = NM == 1 ? 2 : 3;
-    static constexpr int SmemBytes = 1024 + NSA * AStage + NSB * BStage + 1024;
+    static constexpr int SmemBytes = 1024 + NSA * AStage + NSB * BStage + 2048;
     static constexpr int TmemCols = 512;
 };
 
@@ -335,7 +340,11 @@ prefill_gemm_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_cons
         // TMEM reads, so their latencies overlap; the tokens' shifts were staged in
         // shared memory while the MMAs ran.
         int* sS = reinterpret_cast<int*>(const_cast<int*>(fail) + 1);        // [N]
-        for (int i = tid; i < N; i += kPfEpiWarps * 32) sS[i] = n0 + i < p.T ? p.S[n0 + i] : 0;
+        int* sP = sS + N;                                                     // [N] positions
+        for (int i = tid; i < N; i += kPfEpiWarps * 32) {
+            sS[i] = n0 + i < p.T ? p.S[n0 + i] : 0;
+            sP[i] = n0 + i < p.T ? (p.tok_pos ? p.tok_pos[n0 + i] : p.pos0 + n0 + i) : 0;
+        }
         const int quarter = warp & 3, half = warp >> 2;
         const int m = m0 + 32 * quarter + lane;
         const uint32_t trow = tmem + ((uint32_t)(32 * quarter) << 16);
@@ -362,7 +371,7 @@ prefill_gemm_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_cons
                     if (p.epi == PF_RESID) {
                         in0[j] = p.out[(size_t)t * p.ldo + m];
                     } else if (rope) {
-                        const float* tr = p.rope_tab + (size_t)(p.pos0 + t) * p.dh + hd;
+                        const float* tr = p.rope_tab + (size_t)sP[c0 + j] * p.dh + hd;
                         in0[j] = tr[0];
                         in1[j] = tr[1];
                     }
@@ -403,9 +412,10 @@ prefill_gemm_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_cons
                 if (p.epi == PF_Q) {
                     p.out[(size_t)t * p.ldo + m] = fmul(y, p.qscale);
                 } else if (p.epi == PF_K || p.epi == PF_V) {
-                    const int pos = p.pos0 + t;
+                    const int pos = sP[c0 + j];
                     const int kvh = m / p.dh, hdv = m % p.dh;
-                    if (pos < p.max_seq) p.cache[((size_t)kvh * p.max_seq + pos) * p.dh + hdv] = y;
+                    if (pos < p.max_seq)
+                        p.cache[t * p.cache_seq + ((size_t)kvh * p.max_seq + pos) * p.dh + hdv] = y;
                     else set_err(p.err, B2_DEV_ERR_KV_OVERFLOW);
                 } else if (p.epi == PF_RESID) {
                     p.out[(size_t)t * p.ldo + m] = fadd(y, in0[j]);
@@ -609,6 +619,61 @@ static __global__ void __launch_bounds__(256) prefill_embed_kernel(const int8_t*
     for (int i = threadIdx.x; i < d; i += 256) x[(size_t)t * d + i] = fmul((float)emb[(size_t)tok * ld + i], s);
 }
 
+// ------------------------------------------------------------------ batched decode
+// Greedy token of each sequence (one CTA per sequence, sample_greedy_f32 order:
+// first maximum, NaN never wins, logit 0 NaN -> 0); the token is fed to the next
+// step, recorded in out[step][seq], and the sequence's position advances.
+struct BatchState {
+    int* tok;          // [B] token each sequence feeds to the next step
+    int* pos;          // [B] its position (tokens in its cache)
+    int* out;          // [max_steps][B] generated ids
+    int* n_steps;      // steps recorded so far (one counter)
+    int max_steps;
+    int max_seq;
+    int* err;
+};
+
+static __global__ void __launch_bounds__(1024) batch_argmax_kernel(const float* logits, int vocab, BatchState b) {
+    __shared__ float wv[32];
+    __shared__ int wi[32];
+    const int z = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float* l = logits + (size_t)z * vocab;
+    float bv = 0.0f;
+    int bi = 0x7fffffff;
+    for (int i = tid; i < vocab; i += 1024) {
+        const float v = l[i];
+        if (bi == 0x7fffffff || amax_better(v, i, bv, bi)) { bv = v; bi = i; }
+    }
+    for (int s = 16; s >= 1; s >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, s);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, s);
+        if (oi != 0x7fffffff && (bi == 0x7fffffff || amax_better(ov, oi, bv, bi))) { bv = ov; bi = oi; }
+    }
+    if (lane == 0) { wv[warp] = bv; wi[warp] = bi; }
+    __syncthreads();
+    if (tid == 0) {
+        float cv = 0.0f;
+        int ci = 0x7fffffff;
+        for (int w = 0; w < 32; ++w)
+            if (wi[w] != 0x7fffffff && (ci == 0x7fffffff || amax_better(wv[w], wi[w], cv, ci))) { cv = wv[w]; ci = wi[w]; }
+        const float v0 = l[0];
+        const int tok = (v0 != v0 || ci == 0x7fffffff) ? 0 : ci;
+        b.tok[z] = tok;
+        b.pos[z] += 1;
+        const int step = *b.n_steps;
+        if (step < b.max_steps) b.out[(size_t)step * gridDim.x + z] = tok;
+    }
+}
+
+// after the argmax of every sequence: one more recorded step
+static __global__ void batch_count_kernel(BatchState b) { *b.n_steps += 1; }
+
+// positions of a batch step: every sequence must have room for one more row
+static __global__ void batch_check_kernel(BatchState b, int B) {
+    const int z = blockIdx.x * blockDim.x + threadIdx.x;
+    if (z < B && (b.pos[z] < 0 || b.pos[z] >= b.max_seq)) set_err(b.err, B2_DEV_ERR_KV_OVERFLOW);
+}
+
 // ------------------------------------------------------------------ host side (prefill.cu)
 // Build the TMA maps and launch one GEMM: A = the weight matrix (or the gate and
 // up matrices, NM = 2) int8 [M][K] with row stride K bytes; B = the planes
@@ -617,6 +682,8 @@ cudaError_t launch_prefill_gemm(int nm, const void* A0, const void* A1, const un
                                 const PfGemmParams& p, cudaStream_t s);
 cudaError_t launch_prefill_planes(const PfPlanesParams& p, int T, cudaStream_t s);
 cudaError_t launch_prefill_attn(const PfAttnParams& p, cudaStream_t s);
+cudaError_t launch_batch_tail(const float* logits, int vocab, const BatchState& b, int B, cudaStream_t s);
+cudaError_t launch_batch_check(const BatchState& b, int B, cudaStream_t s);
 cudaError_t launch_prefill_embed(const int8_t* emb, const float* emb_s, long long ld, const int* ids, int pos0,
                                  int vocab, int d, float* x, int T, int* err, cudaStream_t s);
 // tokens per plane tile row block (the GEMM's N for one matrix)

@@ -203,6 +203,17 @@ struct b2_ctx {
     unsigned char* pf_planes = nullptr;
     int* pf_S = nullptr;
     float *pf_x = nullptr, *pf_q = nullptr, *pf_att = nullptr, *pf_f = nullptr, *pf_part = nullptr;
+    // batched decode (b2_batch_init): bt_n sequences, each with its own KV cache
+    int bt_n = 0, bt_max_steps = 0;
+    void* bt_base = nullptr;
+    std::vector<float*> bt_K, bt_V;          // per block: [bt_n][KVH][max_seq][dh] (attention blocks)
+    long long bt_seq_stride = 0;             // floats between two sequences' caches of one block
+    int *bt_tok = nullptr, *bt_pos = nullptr, *bt_out = nullptr, *bt_nsteps = nullptr, *bt_ids = nullptr;
+    float *bt_logits = nullptr, *bt_part = nullptr;
+    unsigned* bt_cnt = nullptr;
+    std::vector<int> bt_pos_host;
+    int bt_steps_host = 0;
+    cudaGraphExec_t g_batch = nullptr;
 
     ~b2_ctx() {
         if (device >= 0) cudaSetDevice(device);
@@ -214,6 +225,8 @@ struct b2_ctx {
         if (d_phases) cudaFree(d_phases);
         if (d_trace) cudaFree(d_trace);
         if (pf_base) cudaFree(pf_base);
+        if (g_batch) cudaGraphExecDestroy(g_batch);
+        if (bt_base) cudaFree(bt_base);
         for (int r = 0; r < kMaxRanks; ++r)
             if (peer_base[r]) cudaIpcCloseMemHandle(peer_base[r]);
         if (d_xch) cudaFree(d_xch);
@@ -946,9 +959,11 @@ void prefill_workspace(b2_ctx* c) {
     CK(cudaMemsetAsync(c->pf_planes, 0, b_planes, c->stream));
 }
 
-// Tokens [p0, p0 + T) of the device prompt buffer through every sub-block, no LM
-// head: the KV cache ends as n decode steps would leave it, bit for bit.
-void enqueue_prefill_chunk(b2_ctx* c, int p0, int T, cudaStream_t s) {
+// Tokens [p0, p0 + T) of the device id buffer `ids` through every sub-block, no LM
+// head: the KV cache ends as n decode steps would leave it, bit for bit. seq >= 0:
+// sequence seq of the batched state (its own cache).
+void enqueue_prefill_chunk(b2_ctx* c, int p0, int T, cudaStream_t s, const int* ids = nullptr, int seq = -1) {
+    if (!ids) ids = c->prompt;
     int* err = &c->st->err;
     const int Tpad = (T + kPfTokenTile - 1) / kPfTokenTile * kPfTokenTile;
     auto planes = [&](const float* x, int ldx, int n, const NormRef* nr) {
@@ -968,17 +983,20 @@ void enqueue_prefill_chunk(b2_ctx* c, int p0, int T, cudaStream_t s) {
         g.cache = cache;
         CK(launch_prefill_gemm(nm, A.w, A1 ? A1->w : nullptr, c->pf_planes, c->pf_ldp, g, s));
     };
-    CK(launch_prefill_embed(static_cast<const int8_t*>(c->emb.w), c->emb.s, c->emb.ld, c->prompt, p0, c->vocab,
+    CK(launch_prefill_embed(static_cast<const int8_t*>(c->emb.w), c->emb.s, c->emb.ld, ids, p0, c->vocab,
                             c->d, c->pf_x, T, err, s));
-    for (const Block& B : c->blocks) {
+    for (size_t bi = 0; bi < c->blocks.size(); ++bi) {
+        const Block& B = c->blocks[bi];
         planes(c->pf_x, c->d, c->d, &B.norm);
         if (B.attn) {
             const int qd = B.H * B.dh;
+            float* Kc = seq < 0 ? B.K : c->bt_K[bi] + (size_t)seq * c->bt_seq_stride;
+            float* Vc = seq < 0 ? B.V : c->bt_V[bi] + (size_t)seq * c->bt_seq_stride;
             gemm(1, B.q, nullptr, PF_Q, c->pf_q, qd, B.bias[0], &B, nullptr);
-            gemm(1, B.k, nullptr, PF_K, nullptr, 0, B.bias[1], &B, B.K);
-            gemm(1, B.v, nullptr, PF_V, nullptr, 0, B.bias[2], &B, B.V);
+            gemm(1, B.k, nullptr, PF_K, nullptr, 0, B.bias[1], &B, Kc);
+            gemm(1, B.v, nullptr, PF_V, nullptr, 0, B.bias[2], &B, Vc);
             PfAttnParams a{};
-            a.q = c->pf_q; a.K = B.K; a.V = B.V; a.out = c->pf_att; a.part = c->pf_part;
+            a.q = c->pf_q; a.K = Kc; a.V = Vc; a.out = c->pf_att; a.part = c->pf_part;
             a.H = B.H; a.KVH = B.KVH; a.dh = B.dh; a.max_seq = c->max_seq; a.nsplit_max = c->attn_nsplit_max;
             a.T = T; a.pos0 = p0; a.err = err;
             CK(launch_prefill_attn(a, s));
@@ -992,10 +1010,146 @@ void enqueue_prefill_chunk(b2_ctx* c, int p0, int T, cudaStream_t s) {
     }
 }
 
-void enqueue_prefill(b2_ctx* c, int p0, int n, cudaStream_t s) {
+void enqueue_prefill(b2_ctx* c, int p0, int n, cudaStream_t s, const int* ids = nullptr, int seq = -1) {
     prefill_workspace(c);
     for (int done = 0; done < n; done += c->pf_tmax)
-        enqueue_prefill_chunk(c, p0 + done, std::min(c->pf_tmax, n - done), s);
+        enqueue_prefill_chunk(c, p0 + done, std::min(c->pf_tmax, n - done), s, ids, seq);
+}
+
+// ------------------------------------------------------------------ batched decode
+BatchState batch_state(b2_ctx* c) {
+    BatchState b{};
+    b.tok = c->bt_tok; b.pos = c->bt_pos; b.out = c->bt_out; b.n_steps = c->bt_nsteps;
+    b.max_steps = c->bt_max_steps; b.max_seq = c->max_seq; b.err = &c->st->err;
+    return b;
+}
+
+// One step of every sequence: the token each feeds (bt_tok) at its position
+// (bt_pos) through the model on the tensor cores (one GEMM over the bt_n tokens
+// per projection, each row the exact dot of the one-sequence path), decode
+// attention per sequence over its own cache, the LM head for every sequence, the
+// greedy token fed back and recorded.
+void enqueue_batch_step(b2_ctx* c, cudaStream_t s) {
+    const int Bn = c->bt_n;
+    int* err = &c->st->err;
+    const BatchState bs = batch_state(c);
+    CK(launch_batch_check(bs, Bn, s));
+    const int Tpad = (Bn + kPfTokenTile - 1) / kPfTokenTile * kPfTokenTile;
+    auto planes = [&](const float* x, int ldx, int n, const NormRef* nr) {
+        PfPlanesParams pp{};
+        pp.x = x; pp.ldx = ldx; pp.n = n;
+        pp.norm = nr ? nr->kind : NORM_NONE; pp.g = nr ? nr->g : nullptr; pp.eps = c->eps;
+        pp.planes = c->pf_planes; pp.ldp = c->pf_ldp; pp.kp = c->pf_ldp; pp.Tpad = Tpad; pp.S = c->pf_S;
+        CK(launch_prefill_planes(pp, Bn, s));
+    };
+    auto gemm = [&](int nm, const DevMat& A, const DevMat* A1, int epi, float* out, int ldo, const float* bias,
+                    const Block* B, float* cache) {
+        PfGemmParams g{};
+        g.M = A.rows; g.K = A.ld; g.T = Bn; g.Tpad = Tpad; g.epi = epi; g.S = c->pf_S;
+        g.scale[0] = A.s; g.scale[1] = A1 ? A1->s : A.s; g.bias = bias;
+        g.out = out; g.ldo = ldo; g.err = err; g.pos0 = 0; g.max_seq = c->max_seq;
+        g.tok_pos = c->bt_pos; g.cache_seq = c->bt_seq_stride;
+        if (B) { g.rope = B->rope; g.rope_tab = c->rope_tab; g.dh = B->dh; g.qscale = (float)(1.0 / std::sqrt((double)B->dh)); }
+        g.cache = cache;
+        CK(launch_prefill_gemm(nm, A.w, A1 ? A1->w : nullptr, c->pf_planes, c->pf_ldp, g, s));
+    };
+    CK(launch_prefill_embed(static_cast<const int8_t*>(c->emb.w), c->emb.s, c->emb.ld, c->bt_tok, 0, c->vocab, c->d,
+                            c->pf_x, Bn, err, s));
+    for (size_t bi = 0; bi < c->blocks.size(); ++bi) {
+        const Block& B = c->blocks[bi];
+        planes(c->pf_x, c->d, c->d, &B.norm);
+        if (B.attn) {
+            const int qd = B.H * B.dh;
+            gemm(1, B.q, nullptr, PF_Q, c->pf_q, qd, B.bias[0], &B, nullptr);
+            gemm(1, B.k, nullptr, PF_K, nullptr, 0, B.bias[1], &B, c->bt_K[bi]);
+            gemm(1, B.v, nullptr, PF_V, nullptr, 0, B.bias[2], &B, c->bt_V[bi]);
+            AttnParams a{};
+            a.q = c->pf_q; a.K = c->bt_K[bi]; a.V = c->bt_V[bi]; a.out = c->pf_att;
+            a.part = c->bt_part; a.counters = c->bt_cnt;
+            a.H = B.H; a.KVH = B.KVH; a.dh = B.dh; a.max_seq = c->max_seq; a.nsplit_max = c->attn_nsplit_max;
+            a.st = nullptr; a.err = err; a.n_of = c->bt_pos;
+            a.sq = qd; a.skv = c->bt_seq_stride; a.spart = (long long)B.H * c->attn_nsplit_max * (B.dh + 2);
+            CK(launch_attn_batched(a, Bn, s));
+            planes(c->pf_att, qd, qd, nullptr);
+            gemm(1, B.o, nullptr, PF_RESID, c->pf_x, c->d, B.bias[3], nullptr, nullptr);
+        } else {
+            gemm(2, B.w1, &B.w3, PF_SWIGLU, c->pf_f, B.ffn_local, nullptr, nullptr, nullptr);
+            planes(c->pf_f, B.ffn_local, B.ffn_local, nullptr);
+            gemm(1, B.w2, nullptr, PF_RESID, c->pf_x, c->d, nullptr, nullptr, nullptr);
+        }
+    }
+    planes(c->pf_x, c->d, c->d, &c->fnorm);
+    gemm(1, c->lm, nullptr, PF_STORE, c->bt_logits, c->vocab, c->lm_b, nullptr, nullptr);
+    CK(launch_batch_tail(c->bt_logits, c->vocab, bs, Bn, s));
+}
+
+void batch_init(b2_ctx* c, int n, int max_steps) {
+    if (!c->pf_ok) throw Err(B2_E_UNSUPPORTED, "batched decode needs a plan the tensor-core path covers: " + c->pf_why);
+    if (n < 1 || n > 512 || max_steps < 1) throw Err(B2_E_INVALID, "batch size 1..512 and max_steps >= 1");
+    if (c->bt_base) throw Err(B2_E_INVALID, "batched state already initialised");
+    prefill_workspace(c);
+    if (n > c->pf_tmax) throw Err(B2_E_UNSUPPORTED, "batch larger than the prefill tile capacity");
+    size_t kv = 0;
+    int H = 1, dh = 1;
+    for (const Block& B : c->blocks)
+        if (B.attn) {
+            kv += 2ull * n * B.KVH * c->max_seq * B.dh;
+            H = std::max(H, B.H);
+            dh = std::max(dh, B.dh);
+        }
+    auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
+    const size_t b_kv = al(kv * 4), b_i = al((size_t)n * 4), b_out = al((size_t)max_steps * n * 4),
+                 b_ids = al((size_t)c->max_seq * 4), b_log = al((size_t)n * c->vocab * 4),
+                 b_part = al((size_t)n * H * c->attn_nsplit_max * (dh + 2) * 4), b_cnt = al((size_t)n * H * 4);
+    const size_t total = b_kv + 2 * b_i + b_out + 256 + b_ids + b_log + b_part + b_cnt;
+    if (cudaMalloc(&c->bt_base, total) != cudaSuccess) throw Err(B2_E_OOM, "batched state allocation failed");
+    char* w = static_cast<char*>(c->bt_base);
+    float* kvp = reinterpret_cast<float*>(w); w += b_kv;
+    c->bt_tok = reinterpret_cast<int*>(w); w += b_i;
+    c->bt_pos = reinterpret_cast<int*>(w); w += b_i;
+    c->bt_out = reinterpret_cast<int*>(w); w += b_out;
+    c->bt_nsteps = reinterpret_cast<int*>(w); w += 256;
+    c->bt_ids = reinterpret_cast<int*>(w); w += b_ids;
+    c->bt_logits = reinterpret_cast<float*>(w); w += b_log;
+    c->bt_part = reinterpret_cast<float*>(w); w += b_part;
+    c->bt_cnt = reinterpret_cast<unsigned*>(w);
+    c->bt_K.assign(c->blocks.size(), nullptr);
+    c->bt_V.assign(c->blocks.size(), nullptr);
+    for (size_t bi = 0; bi < c->blocks.size(); ++bi) {
+        const Block& B = c->blocks[bi];
+        if (!B.attn) continue;
+        const size_t per = (size_t)n * B.KVH * c->max_seq * B.dh;
+        c->bt_K[bi] = kvp; kvp += per;
+        c->bt_V[bi] = kvp; kvp += per;
+        c->bt_seq_stride = (long long)B.KVH * c->max_seq * B.dh;
+    }
+    c->bt_n = n;
+    c->bt_max_steps = max_steps;
+    CK(cudaMemsetAsync(c->bt_tok, 0, 2 * b_i + b_out + 256, c->stream));
+    CK(cudaMemsetAsync(c->bt_cnt, 0, b_cnt, c->stream));
+    c->bt_pos_host.assign(n, 0);
+    c->bt_steps_host = 0;
+    // one step as a graph (fixed pointers; positions and tokens live on the device)
+    cudaGraph_t g = nullptr;
+    CK(cudaStreamBeginCapture(c->cap_stream, cudaStreamCaptureModeThreadLocal));
+    try {
+        enqueue_batch_step(c, c->cap_stream);
+    } catch (...) {
+        cudaStreamEndCapture(c->cap_stream, &g);
+        if (g) cudaGraphDestroy(g);
+        throw;
+    }
+    CK(cudaStreamEndCapture(c->cap_stream, &g));
+    const cudaError_t e = cudaGraphInstantiate(&c->g_batch, g, 0);
+    cudaGraphDestroy(g);
+    CK(e);
+    CK(cudaStreamSynchronize(c->stream));
+}
+
+// the batched path reports device errors through the step state's error word
+void batch_begin(b2_ctx* c) {
+    if (!c->bt_base) throw Err(B2_E_INVALID, "batched decode not initialised (b2_batch_init)");
+    CK(cudaMemsetAsync(&c->st->err, 0, sizeof(int), c->stream));
 }
 
 void capture_graphs_once(b2_ctx* c);
@@ -1470,9 +1624,13 @@ int b2_reset(b2_ctx* ctx) {
 }
 
 int b2_step(b2_ctx* ctx, const int32_t* tok, int n_seq, int32_t* next_tok, float* logits) {
-    return guarded(ctx, [&] {
+    return guarded(ctx, [&]() -> int {
         if (!ctx->g_decode) throw Err(B2_E_INVALID, "ranks not connected (b2_tp_connect)");
-        if (!tok || n_seq != 1) return n_seq == 1 ? B2_E_INVALID : B2_E_UNSUPPORTED;
+        if (n_seq > 1) {
+            if (n_seq != ctx->bt_n) throw Err(B2_E_UNSUPPORTED, "n_seq must equal the b2_batch_init batch");
+            return b2_batch_step(ctx, tok, next_tok, logits);
+        }
+        if (!tok || n_seq != 1) return B2_E_INVALID;
         if (ctx->host_step >= ctx->max_seq) throw Err(B2_E_KV_OVERFLOW, "position reached max_seq");
         if (tok[0] < 0 || tok[0] >= ctx->vocab) throw Err(B2_E_INVALID, "token id outside the vocabulary");
         const int t = ctx->host_step;
@@ -1551,6 +1709,130 @@ int b2_set_position(b2_ctx* ctx, int pos, int32_t next_tok) {
         set_state_kernel<<<1, 1, 0, ctx->stream>>>(ctx->st, pos, pos, 1 << 30, next_tok, -1);
         CK(cudaGetLastError());
         ctx->host_step = pos;
+        return B2_OK;
+    });
+}
+
+int b2_batch_init(b2_ctx* ctx, int n_seq, int max_steps) {
+    return guarded(ctx, [&] {
+        batch_init(ctx, n_seq, max_steps);
+        return B2_OK;
+    });
+}
+
+int b2_batch_reset(b2_ctx* ctx) {
+    return guarded(ctx, [&] {
+        batch_begin(ctx);
+        CK(cudaMemsetAsync(ctx->bt_pos, 0, (size_t)ctx->bt_n * 4, ctx->stream));
+        CK(cudaMemsetAsync(ctx->bt_nsteps, 0, sizeof(int), ctx->stream));
+        CK(cudaStreamSynchronize(ctx->stream));
+        ctx->bt_pos_host.assign(ctx->bt_n, 0);
+        ctx->bt_steps_host = 0;
+        return B2_OK;
+    });
+}
+
+int b2_batch_prefill(b2_ctx* ctx, int seq, const int32_t* toks, int n) {
+    return guarded(ctx, [&] {
+        batch_begin(ctx);
+        if (seq < 0 || seq >= ctx->bt_n || n < 0 || (n > 0 && !toks)) return B2_E_INVALID;
+        const int p0 = ctx->bt_pos_host[seq];
+        if (p0 + n > ctx->max_seq) throw Err(B2_E_KV_OVERFLOW, "prefill passes max_seq");
+        for (int i = 0; i < n; ++i)
+            if (toks[i] < 0 || toks[i] >= ctx->vocab) throw Err(B2_E_INVALID, "token id outside the vocabulary");
+        if (n == 0) return B2_OK;
+        CK(cudaMemcpyAsync(ctx->bt_ids + p0, toks, (size_t)n * 4, cudaMemcpyHostToDevice, ctx->stream));
+        enqueue_prefill(ctx, p0, n, ctx->stream, ctx->bt_ids, seq);
+        const int np = p0 + n;
+        CK(cudaMemcpyAsync(ctx->bt_pos + seq, &np, 4, cudaMemcpyHostToDevice, ctx->stream));
+        fetch_state(ctx);
+        ctx->bt_pos_host[seq] = np;
+        return B2_OK;
+    });
+}
+
+int b2_batch_step(b2_ctx* ctx, const int32_t* toks, int32_t* next, float* logits) {
+    return guarded(ctx, [&] {
+        batch_begin(ctx);
+        if (!toks) return B2_E_INVALID;
+        for (int z = 0; z < ctx->bt_n; ++z) {
+            if (toks[z] < 0 || toks[z] >= ctx->vocab) throw Err(B2_E_INVALID, "token id outside the vocabulary");
+            if (ctx->bt_pos_host[z] >= ctx->max_seq) throw Err(B2_E_KV_OVERFLOW, "a sequence reached max_seq");
+        }
+        if (ctx->bt_steps_host >= ctx->bt_max_steps) throw Err(B2_E_INVALID, "output record full (max_steps)");
+        CK(cudaMemcpyAsync(ctx->bt_tok, toks, (size_t)ctx->bt_n * 4, cudaMemcpyHostToDevice, ctx->stream));
+        CK(cudaGraphLaunch(ctx->g_batch, ctx->stream));
+        if (next) CK(cudaMemcpyAsync(next, ctx->bt_tok, (size_t)ctx->bt_n * 4, cudaMemcpyDeviceToHost, ctx->stream));
+        if (logits)
+            CK(cudaMemcpyAsync(logits, ctx->bt_logits, (size_t)ctx->bt_n * ctx->vocab * 4, cudaMemcpyDeviceToHost,
+                               ctx->stream));
+        fetch_state(ctx);
+        for (int& p : ctx->bt_pos_host) ++p;
+        ++ctx->bt_steps_host;
+        return B2_OK;
+    });
+}
+
+int b2_batch_decode_async(b2_ctx* ctx, int n_steps) {
+    return guarded(ctx, [&] {
+        if (!ctx->bt_base) throw Err(B2_E_INVALID, "batched decode not initialised (b2_batch_init)");
+        if (n_steps < 0) return B2_E_INVALID;
+        for (int p : ctx->bt_pos_host)
+            if (p + n_steps > ctx->max_seq) throw Err(B2_E_KV_OVERFLOW, "decode passes max_seq");
+        if (ctx->bt_steps_host + n_steps > ctx->bt_max_steps) throw Err(B2_E_INVALID, "output record full (max_steps)");
+        for (int i = 0; i < n_steps; ++i) CK(cudaGraphLaunch(ctx->g_batch, ctx->stream));
+        for (int& p : ctx->bt_pos_host) p += n_steps;
+        ctx->bt_steps_host += n_steps;
+        return B2_OK;
+    });
+}
+
+int b2_batch_read_output(b2_ctx* ctx, int32_t* ids, int max_steps, int* n_steps) {
+    return guarded(ctx, [&] {
+        if (!ctx->bt_base || !ids) return B2_E_INVALID;
+        fetch_state(ctx);
+        const int n = std::min(max_steps, ctx->bt_steps_host);
+        if (n > 0) {
+            CK(cudaMemcpyAsync(ids, ctx->bt_out, (size_t)n * ctx->bt_n * 4, cudaMemcpyDeviceToHost, ctx->stream));
+            CK(cudaStreamSynchronize(ctx->stream));
+        }
+        if (n_steps) *n_steps = n;
+        return B2_OK;
+    });
+}
+
+int b2_batch_generate(b2_ctx* ctx, const int32_t* prompts, int n_prompt, int max_new, int32_t* out_ids) {
+    return guarded(ctx, [&] {
+        if (!ctx->bt_base) throw Err(B2_E_INVALID, "batched decode not initialised (b2_batch_init)");
+        if (!prompts || n_prompt <= 0 || max_new <= 0 || !out_ids) return B2_E_INVALID;
+        if (n_prompt + max_new - 1 > ctx->max_seq) throw Err(B2_E_KV_OVERFLOW, "generation passes max_seq");
+        if (max_new > ctx->bt_max_steps) throw Err(B2_E_INVALID, "max_new above the output record (max_steps)");
+        const int Bn = ctx->bt_n;
+        for (long long i = 0; i < (long long)Bn * n_prompt; ++i)
+            if (prompts[i] < 0 || prompts[i] >= ctx->vocab) throw Err(B2_E_INVALID, "token id outside the vocabulary");
+        batch_begin(ctx);
+        CK(cudaMemsetAsync(ctx->bt_nsteps, 0, sizeof(int), ctx->stream));
+        // every prompt but its last token through the batched prefill, sequence by sequence
+        std::vector<int32_t> last(Bn), pos(Bn, n_prompt - 1);
+        for (int z = 0; z < Bn; ++z) {
+            const int32_t* pz = prompts + (size_t)z * n_prompt;
+            if (n_prompt > 1) {
+                CK(cudaMemcpyAsync(ctx->bt_ids, pz, (size_t)(n_prompt - 1) * 4, cudaMemcpyHostToDevice, ctx->stream));
+                enqueue_prefill(ctx, 0, n_prompt - 1, ctx->stream, ctx->bt_ids, z);
+                CK(cudaStreamSynchronize(ctx->stream));            // bt_ids is reused by the next sequence
+            }
+            last[z] = pz[n_prompt - 1];
+        }
+        CK(cudaMemcpyAsync(ctx->bt_pos, pos.data(), (size_t)Bn * 4, cudaMemcpyHostToDevice, ctx->stream));
+        CK(cudaMemcpyAsync(ctx->bt_tok, last.data(), (size_t)Bn * 4, cudaMemcpyHostToDevice, ctx->stream));
+        for (int i = 0; i < max_new; ++i) CK(cudaGraphLaunch(ctx->g_batch, ctx->stream));
+        std::vector<int32_t> rec((size_t)max_new * Bn);
+        CK(cudaMemcpyAsync(rec.data(), ctx->bt_out, rec.size() * 4, cudaMemcpyDeviceToHost, ctx->stream));
+        fetch_state(ctx);
+        for (int z = 0; z < Bn; ++z)
+            for (int i = 0; i < max_new; ++i) out_ids[(size_t)z * max_new + i] = rec[(size_t)i * Bn + z];
+        ctx->bt_pos_host.assign(Bn, n_prompt - 1 + max_new);
+        ctx->bt_steps_host = max_new;
         return B2_OK;
     });
 }
@@ -1650,6 +1932,7 @@ int b2_query(b2_ctx* ctx, const char* key, double* value) {
     else if (k == "pdl") *value = ctx->pdl ? 1 : 0;
     else if (k == "token_kernel") *value = ctx->token ? 1 : 0;
     else if (k == "prefill_batched") *value = ctx->pf_ok ? 1 : 0;
+    else if (k == "batch") *value = ctx->bt_n;
     else return B2_E_INVALID;
     return B2_OK;
 }

@@ -68,6 +68,13 @@ def _declare(L):
     L.b2_decode_async.argtypes = [vp, C.c_int]
     L.b2_fill_kv_synthetic.argtypes = [vp, C.c_int, C.c_uint64]
     L.b2_set_sampling.argtypes = [vp, C.c_int, C.c_int, C.c_double, C.c_uint32]
+    L.b2_batch_init.argtypes = [vp, C.c_int, C.c_int]
+    L.b2_batch_reset.argtypes = [vp]
+    L.b2_batch_prefill.argtypes = [vp, C.c_int, i32p, C.c_int]
+    L.b2_batch_step.argtypes = [vp, i32p, i32p, f32p]
+    L.b2_batch_decode_async.argtypes = [vp, C.c_int]
+    L.b2_batch_read_output.argtypes = [vp, i32p, C.c_int, C.POINTER(C.c_int)]
+    L.b2_batch_generate.argtypes = [vp, i32p, C.c_int, C.c_int, i32p]
     L.b2_sync.argtypes = [vp]
     L.b2_read_output.argtypes = [vp, i32p, C.c_int, C.POINTER(C.c_int)]
     L.b2_set_stream.argtypes = [vp, vp]
@@ -269,6 +276,45 @@ class Decoder:
         """--sample spec (greedy | temperature:T | topk:K:T) and the LCG seed."""
         mode, k, temp = parse_sample(sample)
         self._ck(lib().b2_set_sampling(self._ctx, mode, k, temp, int(seed) & 0xFFFFFFFF))
+
+    # ---- batched decode (n_seq sequences, one token each per step)
+    def batch_init(self, n_seq, max_steps=256):
+        self._ck(lib().b2_batch_init(self._ctx, int(n_seq), int(max_steps)))
+        self.n_seq = int(n_seq)
+
+    def batch_reset(self):
+        self._ck(lib().b2_batch_reset(self._ctx))
+
+    def batch_prefill(self, seq, toks):
+        self._ck(lib().b2_batch_prefill(self._ctx, int(seq), _i32(toks), len(toks)))
+
+    def batch_step(self, toks, want_logits=False):
+        """One token per sequence: returns (next ids, logits [n_seq, vocab] or None)."""
+        import numpy as np
+        nxt = (C.c_int32 * self.n_seq)()
+        logits = np.zeros((self.n_seq, self.vocab), np.float32) if want_logits else None
+        self._ck(lib().b2_batch_step(self._ctx, _i32(toks), nxt,
+                                     logits.ctypes.data_as(f32p) if want_logits else None))
+        return list(nxt), logits
+
+    def batch_decode_async(self, n_steps):
+        self._ck(lib().b2_batch_decode_async(self._ctx, int(n_steps)))
+
+    def batch_read_output(self, max_steps):
+        import numpy as np
+        out = np.zeros((max_steps, self.n_seq), np.int32)
+        n = C.c_int(0)
+        self._ck(lib().b2_batch_read_output(self._ctx, out.ctypes.data_as(i32p), int(max_steps), C.byref(n)))
+        return out[: n.value]
+
+    def batch_generate(self, prompts, max_new):
+        """prompts [n_seq][P] (equal lengths) -> generated ids [n_seq][max_new]."""
+        import numpy as np
+        p = np.ascontiguousarray(prompts, np.int32)
+        out = np.zeros((p.shape[0], max_new), np.int32)
+        self._ck(lib().b2_batch_generate(self._ctx, p.ctypes.data_as(i32p), p.shape[1], int(max_new),
+                                         out.ctypes.data_as(i32p)))
+        return out
 
     def fill_kv_synthetic(self, count, seed=0):
         """KV rows [0, count) from the synthetic generator (the oracle's fill_kv) and

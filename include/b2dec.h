@@ -92,8 +92,9 @@ int b2_destroy(b2_ctx* ctx);
  * attn_mh_kv_reset_f32 (attention_mh_kv_f32.ari:78-87). */
 int b2_reset(b2_ctx* ctx);
 
-/* One token through the model (n_seq must be 1): next_tok = greedy argmax of the
- * logits; logits (vocab floats, host) optional. Returns B2_E_KV_OVERFLOW, writing
+/* One token through the model: next_tok = greedy argmax of the logits; logits
+ * (vocab floats, host) optional. n_seq > 1: one token for each sequence of the
+ * batched state (b2_batch_init with that many sequences), as b2_batch_step. Returns B2_E_KV_OVERFLOW, writing
  * nothing, when the position has reached max_seq.
  * Replaces: one iteration of the decoder loop (aricode_pack.py:2203-2324). */
 int b2_step(b2_ctx* ctx, const int32_t* tok, int n_seq, int32_t* next_tok, float* logits);
@@ -115,6 +116,35 @@ int b2_generate(b2_ctx* ctx, const int32_t* prompt, int n_prompt, int max_new, i
  * token fed at pos), then enqueue n decode steps whose argmax feeds the next
  * step. Both only enqueue work on the context's stream. */
 int b2_set_position(b2_ctx* ctx, int pos, int32_t next_tok);
+
+/* Batched decode: n_seq independent sequences on one GPU, each with its own KV
+ * cache (n_seq x max_seq positions), advanced one token each per step. Every
+ * projection of a step is one tensor-core GEMM over the n_seq tokens (tcgen05
+ * kind::i8 over the byte planes of each token's fixed-point activations), whose
+ * rows equal the one-sequence GEMV bit for bit; attention runs per sequence over
+ * its own cache; the LM head covers every sequence and the greedy token of each
+ * is fed to its next step. So every sequence's ids and logits are those it would
+ * get decoded alone. Needs a plan the batched prefill covers (Llama family, one
+ * GPU) and n_seq <= 512.
+ *   b2_batch_init       allocate the caches and an output record of max_steps steps
+ *   b2_batch_reset      every sequence back to position 0, record emptied
+ *   b2_batch_prefill    prompt tokens of one sequence (no LM head), batched
+ *   b2_batch_step       one token per sequence (n_seq ids in, n_seq greedy ids out,
+ *                       optional logits [n_seq][vocab]); b2_step with n_seq equal
+ *                       to the batch does the same
+ *   b2_batch_decode_async  n steps on the device, each feeding its greedy ids on
+ *   b2_batch_read_output   the recorded ids [steps][n_seq]
+ *   b2_batch_generate   prompts [n_seq][n_prompt] -> out [n_seq][max_new]: prefill
+ *                       of every prompt, then max_new batched steps
+ * The reference decodes one sequence at a time; this replaces running its decoder
+ * loop (aricode_pack.py:2068-2344) once per sequence. */
+int b2_batch_init(b2_ctx* ctx, int n_seq, int max_steps);
+int b2_batch_reset(b2_ctx* ctx);
+int b2_batch_prefill(b2_ctx* ctx, int seq, const int32_t* toks, int n);
+int b2_batch_step(b2_ctx* ctx, const int32_t* toks, int32_t* next, float* logits);
+int b2_batch_decode_async(b2_ctx* ctx, int n_steps);
+int b2_batch_read_output(b2_ctx* ctx, int32_t* ids, int max_steps, int* n_steps);
+int b2_batch_generate(b2_ctx* ctx, const int32_t* prompts, int n_prompt, int max_new, int32_t* out_ids);
 
 /* Token choice after the LM head: mode 0 greedy (the default), 1 temperature
  * softmax, 2 top-k then temperature, with the reference's 32-bit LCG

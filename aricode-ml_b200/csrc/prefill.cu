@@ -126,6 +126,23 @@ cudaError_t launch_prefill_attn(const PfAttnParams& p, cudaStream_t s) {
     return cudaGetLastError();
 }
 
+cudaError_t launch_batch_attn(const AttnParams& a, int nseq, cudaStream_t s) {
+    const int kd = (a.dh + 31) / 32;
+    auto k = kd <= 1 ? attn_batch_part_kernel<1> : kd == 2 ? attn_batch_part_kernel<2>
+                                                  : kd <= 4 ? attn_batch_part_kernel<4> : attn_batch_part_kernel<8>;
+    cudaError_t e;
+    const dim3 grid((unsigned)nseq, (unsigned)a.KVH, (unsigned)((a.nsplit_max + kBtWarps - 1) / kBtWarps));
+    k<<<grid, kBtWarps * 32, 0, s>>>(a);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    // merge: prefill_attn_combine_kernel with one "token" per sequence
+    PfAttnParams c{};
+    c.out = a.out; c.part = a.part; c.H = a.H; c.KVH = a.KVH; c.dh = a.dh; c.max_seq = a.max_seq;
+    c.nsplit_max = a.nsplit_max; c.T = nseq; c.pos0 = 0; c.err = a.err; c.n_of = a.n_of;
+    const long long items = (long long)nseq * a.H;
+    prefill_attn_combine_kernel<<<(unsigned)((items + 7) / 8), 256, 0, s>>>(c);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_batch_tail(const float* logits, int vocab, const BatchState& b, int B, cudaStream_t s) {
     batch_argmax_kernel<<<B, 1024, 0, s>>>(logits, vocab, b);
     batch_count_kernel<<<1, 1, 0, s>>>(b);

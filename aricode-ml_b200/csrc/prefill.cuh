@@ -80,6 +80,7 @@ struct PfAttnParams {
     int H, KVH, dh, max_seq, nsplit_max;
     int T, pos0;
     int* err;
+    const int* n_of;         // combine only: token t sees n_of[t] + 1 keys (nullptr: pos0 + t + 1)
 };
 
 // ------------------------------------------------------------------ PTX wrappers
@@ -571,7 +572,7 @@ static __global__ void __launch_bounds__(256) prefill_attn_combine_kernel(const 
     const long long item = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);   // (token, query head)
     if (item >= (long long)p.T * p.H) return;
     const int t = (int)(item / p.H), h = (int)(item % p.H), dh = p.dh;
-    const int n = p.pos0 + t + 1;
+    const int n = p.n_of ? p.n_of[t] + 1 : p.pos0 + t + 1;
     const int nsplit = (n + kAttnChunk - 1) / kAttnChunk;
     const int stride = dh + 2;
     const float* base = p.part + ((size_t)t * p.H + h) * p.nsplit_max * stride;
@@ -617,6 +618,120 @@ static __global__ void __launch_bounds__(256) prefill_embed_kernel(const int8_t*
     }
     const float s = emb_s[tok];
     for (int i = threadIdx.x; i < d; i += 256) x[(size_t)t * d + i] = fmul((float)emb[(size_t)tok * ld + i], s);
+}
+
+// ------------------------------------------------------------------ batched decode attention
+// One warp per (sequence z, kv head, 64-key chunk s): it reads the chunk's K and V
+// rows straight from the cache (each lane the elements d = lane, lane + 32, ...;
+// kBtKeys keys' loads in flight at a time) and computes the chunk's (o_s, m_s, l_s)
+// for the kv head's query heads with the decode arithmetic: scores as lane partials
+// reduced by butterflies (kBtKeys keys through one exchange butterfly, each total
+// bit-identical to its own), chunk max / exp / sum with lane L on keys L and
+// L + 32, o[d] a sequential FMA chain over the keys. No shared-memory staging and
+// no block barriers: many warps per SM keep the cache reads in flight.
+// prefill_attn_combine_kernel then merges each (sequence, head) in split order.
+constexpr int kBtWarps = 8;
+constexpr int kBtKeys = 4;             // keys whose loads are in flight together
+
+template <int KD>
+__global__ void __launch_bounds__(kBtWarps * 32, 3) attn_batch_part_kernel(const __grid_constant__ AttnParams p) {
+    __shared__ float es[kBtWarps][kAttnChunk];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int z = blockIdx.x, kvh = blockIdx.y, s = blockIdx.z * kBtWarps + warp;
+    const int G = p.H / p.KVH, dh = p.dh;
+    const int n = p.n_of[z] + 1;
+    const int nsplit = (n + kAttnChunk - 1) / kAttnChunk;
+    if (s >= nsplit) return;
+    const bool full = dh == 32 * KD;
+    const int j0 = s * kAttnChunk, len = min(kAttnChunk, n - j0);
+    const float* Kc = p.K + z * p.skv + ((size_t)kvh * p.max_seq + j0) * dh;
+    const float* Vc = p.V + z * p.skv + ((size_t)kvh * p.max_seq + j0) * dh;
+    float* e = es[warp];
+    const int stride = dh + 2;
+#pragma unroll 1
+    for (int g = 0; g < G; ++g) {
+        const int h = kvh * G + g;
+        const float* qt = p.q + z * p.sq + (size_t)h * dh;
+        float qv[KD];
+#pragma unroll
+        for (int i = 0; i < KD; ++i) {
+            const int d = lane + 32 * i;
+            qv[i] = (full || d < dh) ? __ldg(qt + d) : 0.0f;
+        }
+#pragma unroll 1
+        for (int jj0 = 0; jj0 < len; jj0 += kBtKeys) {
+            float kk[kBtKeys][KD];
+#pragma unroll
+            for (int u = 0; u < kBtKeys; ++u)
+#pragma unroll
+                for (int i = 0; i < KD; ++i) {
+                    const int d = lane + 32 * i;
+                    kk[u][i] = (jj0 + u < len && (full || d < dh)) ? __ldcg(Kc + (size_t)(jj0 + u) * dh + d) : 0.0f;
+                }
+            float v[kBtKeys];
+#pragma unroll
+            for (int u = 0; u < kBtKeys; ++u) {
+                float a = 0.0f;
+#pragma unroll
+                for (int i = 0; i < KD; ++i)
+                    if (full || lane + 32 * i < dh) a = ffma(qv[i], kk[u][i], a);
+                v[u] = a;
+            }
+            exchange_butterfly<kBtKeys>(v, lane);
+            constexpr int LG = Log2<kBtKeys>::v;                // key jj0 + (lane >> (5 - LG))
+            const int kr = lane >> (5 - LG);
+            if ((lane & ((32 >> LG) - 1)) == 0 && jj0 + kr < len) e[jj0 + kr] = v[0];
+        }
+        __syncwarp();
+        const float sc0 = lane < len ? e[lane] : 0.0f;
+        const float sc1 = lane + 32 < len ? e[lane + 32] : 0.0f;
+        // chunk max (lane-strided, then the xor tree), exp, sum: the decode order
+        float mx = -__int_as_float(0x7f800000);
+        bool any = false;
+        if (lane < len) { mx = sc0; any = true; }
+        if (lane + 32 < len) { mx = any ? fmaxf(mx, sc1) : sc1; any = true; }
+        for (int o = 16; o >= 1; o >>= 1) {
+            const float om = __shfl_xor_sync(0xffffffffu, mx, o);
+            const int oa = __shfl_xor_sync(0xffffffffu, (int)any, o);
+            if (oa) { mx = any ? fmaxf(mx, om) : om; any = true; }
+        }
+        float a = 0.0f;
+        float e0 = 0.0f, e1 = 0.0f;
+        if (lane < len) { e0 = exp_f(fsub(sc0, mx)); a = fadd(a, e0); }
+        if (lane + 32 < len) { e1 = exp_f(fsub(sc1, mx)); a = fadd(a, e1); }
+        a = butterfly32(a);
+        float o[KD];
+#pragma unroll
+        for (int i = 0; i < KD; ++i) o[i] = 0.0f;
+#pragma unroll 1
+        for (int jj0 = 0; jj0 < len; jj0 += kBtKeys) {
+            float vv[kBtKeys][KD];
+#pragma unroll
+            for (int u = 0; u < kBtKeys; ++u)
+#pragma unroll
+                for (int i = 0; i < KD; ++i) {
+                    const int d = lane + 32 * i;
+                    vv[u][i] = (jj0 + u < len && (full || d < dh)) ? __ldcg(Vc + (size_t)(jj0 + u) * dh + d) : 0.0f;
+                }
+#pragma unroll
+            for (int u = 0; u < kBtKeys; ++u) {
+                const int jj = jj0 + u;
+                const float ej = __shfl_sync(0xffffffffu, jj < 32 ? e0 : e1, jj & 31);
+                if (jj < len) {
+#pragma unroll
+                    for (int i = 0; i < KD; ++i) o[i] = ffma(ej, vv[u][i], o[i]);
+                }
+            }
+        }
+        float* pp = p.part + z * p.spart + ((size_t)h * p.nsplit_max + s) * stride;
+#pragma unroll
+        for (int i = 0; i < KD; ++i) {
+            const int d = lane + 32 * i;
+            if (full || d < dh) pp[d] = o[i];
+        }
+        if (lane == 0) { pp[dh] = mx; pp[dh + 1] = a; }
+        __syncwarp();                                           // e[] reused by the next head
+    }
 }
 
 // ------------------------------------------------------------------ batched decode
@@ -682,6 +797,7 @@ cudaError_t launch_prefill_gemm(int nm, const void* A0, const void* A1, const un
                                 const PfGemmParams& p, cudaStream_t s);
 cudaError_t launch_prefill_planes(const PfPlanesParams& p, int T, cudaStream_t s);
 cudaError_t launch_prefill_attn(const PfAttnParams& p, cudaStream_t s);
+cudaError_t launch_batch_attn(const AttnParams& a, int nseq, cudaStream_t s);
 cudaError_t launch_batch_tail(const float* logits, int vocab, const BatchState& b, int B, cudaStream_t s);
 cudaError_t launch_batch_check(const BatchState& b, int B, cudaStream_t s);
 cudaError_t launch_prefill_embed(const int8_t* emb, const float* emb_s, long long ld, const int* ids, int pos0,

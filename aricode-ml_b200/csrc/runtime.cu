@@ -1069,7 +1069,7 @@ void enqueue_batch_step(b2_ctx* c, cudaStream_t s) {
             a.H = B.H; a.KVH = B.KVH; a.dh = B.dh; a.max_seq = c->max_seq; a.nsplit_max = c->attn_nsplit_max;
             a.st = nullptr; a.err = err; a.n_of = c->bt_pos;
             a.sq = qd; a.skv = c->bt_seq_stride; a.spart = (long long)B.H * c->attn_nsplit_max * (B.dh + 2);
-            CK(launch_attn_batched(a, Bn, s));
+            CK(launch_batch_attn(a, Bn, s));
             planes(c->pf_att, qd, qd, nullptr);
             gemm(1, B.o, nullptr, PF_RESID, c->pf_x, c->d, B.bias[3], nullptr, nullptr);
         } else {

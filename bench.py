@@ -52,6 +52,7 @@ def parse():
     p.add_argument("--layers", type=int, default=None, help="(testing only) fewer layers")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=15.0)
+    p.add_argument("--no-batched", action="store_true", help="skip the 64-sequence batched configuration")
     return p.parse_args()
 
 
@@ -354,6 +355,10 @@ def main():
     if dist:
         dist.barrier()              # no rank frees its exchange buffer while a peer may still use it
     dec.close()
+    if world == 1 and not args.no_batched and args.layers is None:
+        # the batched configuration (64 sequences x (1024 + 128)) on the same GPU
+        torch.cuda.empty_cache()
+        out["batched"] = time_batched(torch, pkg, local_rank, peaks)
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -392,6 +397,69 @@ def time_prefill(torch, dec, prompt, stream, plan, reps=3):
             "batched": bool(dec.query("prefill_batched")), "int8_tensor_ops": ops,
             "int8_tops": ops / (best / 1000.0) / 1e12,
             "what": "b2_prefill of the prompt minus its last token (no LM head), best of 3"}
+
+
+def time_batched(torch, pkg, local_rank, peaks, layers=None):
+    """The batched configuration: 64 sequences of Llama-2-7B, each a 1024-token
+    random prompt then 128 greedy tokens, all on one GPU. Decode: the 127 steps
+    after the first generated token, every sequence one token per step, timed with
+    CUDA events on the device (device-resident: each step feeds its greedy ids to
+    the next); value = aggregate generated tokens/s. e2e: b2_batch_generate from
+    host prompts (64 prefills + 128 steps), ids back to the host."""
+    name = "llama2-7b-b64"
+    c = pkg.synth.CONFIGS[name]
+    plan = pkg.synth.config_plan(name, n_layers=layers)
+    B, P, NEW = c["batch"], c["prompt"], c["new"]
+    rng = np.random.default_rng(2)
+    prompts = rng.integers(0, plan["vocab"], (B, P)).astype(np.int32)
+    dec = pkg.runtime.Decoder.synthetic(plan, seed=0, device=local_rank)
+    stream = torch.cuda.current_stream()
+    dec.set_stream(stream.cuda_stream)
+    dec.batch_init(B, max_steps=NEW)
+    t0 = time.time()
+    for z in range(B):
+        dec.batch_prefill(z, prompts[z, :-1].tolist())
+    prefill_s = time.time() - t0
+    first, _ = dec.batch_step(prompts[:, -1].tolist())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # one timed pass of the 127 decode steps (positions P .. P + 126 of every sequence)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    dec.batch_decode_async(NEW - 1)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    dec_ms = e0.elapsed_time(e1)
+    rec = dec.batch_read_output(NEW)
+    toks = B * (NEW - 1)
+    value = toks / (dec_ms / 1000.0)
+    kv_row = sum(2 * b["n_kv_heads"] * b["d_head"] * 4 for b in plan["blocks"] if b["type"] == "attn")
+    w = pkg.synth.weight_bytes(plan)
+    # bytes per step: weights once + every sequence's KV rows read (positions 0..pos) and one written
+    per_step = [w + B * kv_row * (P + i + 2) for i in range(NEW - 1)]
+    step_bytes = sum(per_step) / len(per_step)
+    gbs = step_bytes / (dec_ms / 1000.0 / (NEW - 1)) / 1e9
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    # e2e through b2_batch_generate (host prompts in, host ids out)
+    hp = torch.from_numpy(prompts).pin_memory()
+    t0 = time.time()
+    e0.record(stream)
+    out = dec.batch_generate(hp.numpy(), NEW)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    same = bool(out[:, 0].tolist() == first and (out.T == rec[:NEW]).all())
+    dec.close()
+    return {"workload": f"{name}: {B} sequences x ({P} prompt + {NEW} greedy tokens), batch decode",
+            "value": value, "unit": "tokens/s (aggregate)", "decode_steps": NEW - 1,
+            "ms_per_step": dec_ms / (NEW - 1),
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                         "bytes_per_step": step_bytes,
+                         "what": "weights once + every sequence's KV rows per step, over the step time"},
+            "prefill_s": prefill_s, "prefill_tokens_per_s": B * (P - 1) / prefill_s,
+            "e2e": {"value": B * NEW / (e2e_ms / 1000.0), "unit": "tokens/s", "ms_per_generate": e2e_ms,
+                    "h2d_bytes_per_step": int(prompts.nbytes), "d2h_bytes_per_step": B * NEW * 4,
+                    "includes": "64 batched prefills + 128 batched decode steps"},
+            "generate_equals_steps": same}
 
 
 def oracle_check(pkg, dec, plan, P, n=8):

@@ -19,8 +19,10 @@ offset size     field
 ====== ======== ==========================================================
 
 Each 128-byte table entry: name (64 bytes, NUL padded), dtype u32 (1 = int8,
-2 = f32), ndim u32, shape u64[2], ld u64 (row stride in elements), offset u64
-(relative to the data region, 256-aligned), nbytes u64, 16 reserved bytes.
+2 = f32, 3 = int4: two codes per byte, the even column in the low nibble, as the
+reference's ``.i4`` files), ndim u32, shape u64[2] (int4: the logical columns),
+ld u64 (row stride in elements; int4: in bytes), offset u64 (relative to the
+data region, 256-aligned), nbytes u64, 16 reserved bytes.
 
 2-D int8 tensors keep the reference's row-major codes with each row padded with
 zero bytes to a multiple of 16 (so every row starts on a 16-byte boundary for
@@ -38,7 +40,7 @@ import numpy as np
 
 MAGIC = b"B2DBLOB1"
 VERSION = 1
-DT_I8, DT_F32 = 1, 2
+DT_I8, DT_F32, DT_I4 = 1, 2, 3
 _HDR = struct.Struct("<8sIIQQQQIIQ")
 _ENT = struct.Struct("<64sII2QQQQ16x")
 assert _HDR.size == 64 and _ENT.size == 128
@@ -49,7 +51,7 @@ _MIX2 = np.uint64(0xBF58476D1CE4E5B9)
 
 def row_stride(cols, dtype_code):
     """Padded row stride in elements for a 2-D tensor."""
-    if dtype_code == DT_I8:
+    if dtype_code in (DT_I8, DT_I4):
         return (cols + 15) // 16 * 16
     return (cols + 3) // 4 * 4
 
@@ -90,6 +92,8 @@ def write_blob(path, tensors: dict, plan: dict):
         arr = np.asarray(arr)
         if arr.dtype == np.int8:
             code = DT_I8
+        elif arr.dtype == np.uint8:
+            code = DT_I4                    # packed nibbles [rows, cols / 2]
         elif arr.dtype == np.float32:
             code = DT_F32
         else:
@@ -103,7 +107,7 @@ def write_blob(path, tensors: dict, plan: dict):
             ld = row_stride(cols, code)
             data = np.zeros((rows, ld), arr.dtype)
             data[:, :cols] = arr
-            shape = (rows, cols)
+            shape = (rows, 2 * cols if code == DT_I4 else cols)
         else:
             raise ValueError(f"{name}: only 1-D/2-D tensors")
         raw = np.ascontiguousarray(data).view(np.uint8).ravel()
@@ -152,9 +156,9 @@ def read_blob(path, verify=True):
     for i in range(n):
         name, code, ndim, s0, s1, ld, off, nbytes = _ENT.unpack_from(raw, table_off + 128 * i)
         name = name.rstrip(b"\0").decode()
-        dt = np.int8 if code == DT_I8 else np.float32
+        dt = {DT_I8: np.int8, DT_I4: np.uint8}.get(code, np.float32)
         arr = np.frombuffer(data, dt, nbytes // np.dtype(dt).itemsize, off)
         if ndim == 2:
-            arr = arr.reshape(s0, ld)[:, :s1]
+            arr = arr.reshape(s0, ld)[:, :(s1 // 2 if code == DT_I4 else s1)]
         out[name] = arr
     return plan, out

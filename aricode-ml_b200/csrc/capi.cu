@@ -64,6 +64,18 @@ int b2_gemm_i8_rowscale(const int8_t* W, int64_t ld, const float* scale, const f
     return status(launch_prefill_gemm(1, W, nullptr, planes, ldp, g, s));
 }
 
+int b2_gemv_i4_rowscale(const uint8_t* W, int64_t ld, const float* scale, const float* x, const float* bias,
+                        float* y, int m, int n, void* stream) {
+    if (!W || !scale || !x || !y || m <= 0 || n <= 0 || n % 2 || ld * 2 < n || ld % 16 || !al16(W) ||
+        n > kXfixMaxN)
+        return B2_E_INVALID;
+    GemvParams p{};
+    p.W[0] = W; p.S[0] = scale; p.bias[0] = bias;
+    p.rows[0] = m; p.nseg = 1; p.n = n; p.ld = (int)ld; p.i4 = 1;
+    p.x = x; p.norm = NORM_NONE; p.epi = EPI_STORE; p.y = y;
+    return status(launch_gemv_i4(p, static_cast<cudaStream_t>(stream), false, sm_count_current()));
+}
+
 int b2_gemv_f32(const float* W, int64_t ld, const float* x, const float* bias, float* y, int m, int n,
                 void* stream) {
     if (!W || !x || !y || m <= 0 || n <= 0 || ld < n || ld % 4 || !al16(W)) return B2_E_INVALID;

@@ -93,6 +93,7 @@ struct GemvParams {
     int tp_rank, tp_size;
     const unsigned* tp_seq;    // token-kernel launches completed (the flags' epochs)
     int defer_tok;             // EPI_ARGMAX: a sampler kernel chooses the token (no step bookkeeping here)
+    int i4;                    // int4 rows: two codes a byte (ld in bytes), gemv_i4_kernel
     float* tp_cval;
     int* tp_cidx;
     int* tp_cnan;
@@ -1062,6 +1063,176 @@ gemv_kernel(const __grid_constant__ GemvParams p) {
     consumer_bar();
     if (!active) return;
     gemv_epilogue<ESZ, PAIRED>(p, r0, r1, part, pos, tid, blockIdx.x, gridDim.x, nullptr, S);
+}
+
+// ============================================================================
+// int4 rows (the reference's --int4-linear / --int4-embedding format: two codes a
+// byte, the even column in the low nibble; arr_i4_matvec_f32_perrow unpacks them
+// to int8 and runs the int8 dot, aricode_pack.py:168-181). The same exact
+// fixed-point dot as the int8 rows over the unpacked codes, so the results are
+// the int8 kernel's for those codes; the stages stream the packed rows (half the
+// bytes). Thread s owns the 16-byte packed blocks s, s + 256, ... = 32 codes
+// each, against the planes of 32 elements of x.
+// ============================================================================
+struct I4Tag { unsigned char b; };
+template <> struct GemvElems<I4Tag> { static constexpr int EPB = 32; };
+
+// 8 codes (one 32-bit packed word) -> two int8x4 words, elements 0-3 and 4-7
+__device__ __forceinline__ void i4_unpack8(uint32_t w, uint32_t& a, uint32_t& b) {
+    const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+    a = __vsub4(__byte_perm(lo, hi, 0x5140u) ^ 0x08080808u, 0x08080808u);   // sign-extended nibbles
+    b = __vsub4(__byte_perm(lo, hi, 0x7362u) ^ 0x08080808u, 0x08080808u);
+}
+
+template <int KB, int RS>
+__device__ __forceinline__ void gemv_stage_i4(const unsigned char* stage, uint32_t row_bytes, int nblk, int slotid,
+                                              int lane, const uint32_t (&xp)[KB][32], int* part, int rl0, int nr) {
+    constexpr int NH = RS < 8 ? RS : 8;
+    constexpr int NV = NH * 4;
+    constexpr int LG = Log2<NV>::v;
+#pragma unroll
+    for (int h0 = 0; h0 < RS; h0 += NH) {
+        int acc[NH][4];
+#pragma unroll
+        for (int r = 0; r < NH; ++r)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) acc[r][q] = 0;
+#pragma unroll
+        for (int k = 0; k < KB; ++k) {
+            const int b = slotid + 256 * k;
+            if (b < nblk) {
+#pragma unroll
+                for (int r = 0; r < NH; ++r) {
+                    // rows past nr read stale (in-bounds) stage bytes; never stored
+                    const uint4 w = lds128(stage + (size_t)(h0 + r) * row_bytes + 16 * b);
+                    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        uint32_t c0, c1;                     // elements 8q .. 8q + 3, 8q + 4 .. 8q + 7
+                        i4_unpack8(ww[q], c0, c1);
+                        const int g0 = 2 * q, g1 = 2 * q + 1;
+                        acc[r][0] = dp4a_su(c0, xp[k][0 * 8 + g0], acc[r][0]);
+                        acc[r][1] = dp4a_su(c0, xp[k][1 * 8 + g0], acc[r][1]);
+                        acc[r][2] = dp4a_su(c0, xp[k][2 * 8 + g0], acc[r][2]);
+                        acc[r][3] = dp4a_ss(c0, xp[k][3 * 8 + g0], acc[r][3]);
+                        acc[r][0] = dp4a_su(c1, xp[k][0 * 8 + g1], acc[r][0]);
+                        acc[r][1] = dp4a_su(c1, xp[k][1 * 8 + g1], acc[r][1]);
+                        acc[r][2] = dp4a_su(c1, xp[k][2 * 8 + g1], acc[r][2]);
+                        acc[r][3] = dp4a_ss(c1, xp[k][3 * 8 + g1], acc[r][3]);
+                    }
+                }
+            }
+        }
+        int v[NV];
+#pragma unroll
+        for (int r = 0; r < NH; ++r)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) v[r * 4 + q] = acc[r][q];
+        exchange_butterfly_i<NV>(v, lane);
+        if ((lane & ((32 >> LG) - 1)) == 0) {
+            const int vi = lane >> (5 - LG);
+            const int r = h0 + vi / 4, pl = vi % 4;
+            if (r < nr) atomicAdd(part + (rl0 + r) * 4 + pl, v[0]);
+        }
+    }
+}
+
+// One launch per int4 projection (per-layer path and the kernel-level C ABI): the
+// int8 kernel's producer, prologue (norm, fixed point) and epilogues, the int4
+// stage. p.ld = packed row bytes (16-byte multiple), p.n = codes per row.
+template <int KMAX, int RS>
+__global__ void __launch_bounds__(kGemvThreads, 1) gemv_i4_kernel(const __grid_constant__ GemvParams p) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + kGemvMaxStages;
+    float* red = reinterpret_cast<float*>(empty + kGemvMaxStages);
+    float* part = reinterpret_cast<float*>(smem + 1024);
+    unsigned* amx = reinterpret_cast<unsigned*>(red + 8);
+    const uint32_t row_bytes = (uint32_t)p.ld;
+    const uint32_t stage_bytes = (uint32_t)RS * row_bytes;
+    unsigned char* ring = smem + p.ring_offset;
+    const int NS = p.nstages;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    int r0, r1;
+    cta_rows(total_rows(p), 1, blockIdx.x, gridDim.x, r0, r1);
+    if (NS < 2 * kGemvGroups || NS > kGemvMaxStages || NS % kGemvGroups || p.stage_rows != RS || p.paired || p.rope) {
+        if (tid == 0) set_err(p.err, B2_DEV_ERR_TIMEOUT);
+        return;
+    }
+    if (tid == 0) {
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kGemvGroupWarps);
+        }
+        fence_mbar_init();
+        *amx = 0u;
+    }
+    for (int i = tid; i < (r1 - r0) * 4; i += kGemvThreads) reinterpret_cast<int*>(part)[i] = 0;
+    __syncthreads();
+    pdl_launch_dependents();
+    if (warp == kGemvConsumerWarps) {
+        if (lane == 0) {
+            int j = 0;
+            if (!gemv_produce<1>(p, r0, r1, RS, row_bytes, ring, stage_bytes, NS, full, empty, j))
+                set_err(p.err, B2_DEV_ERR_TIMEOUT);
+            for (int i = max(0, j - NS); i < j; ++i)
+                if (!mbar_wait_bounded(&full[i % NS], (uint32_t)((i / NS) & 1))) {
+                    set_err(p.err, B2_DEV_ERR_TIMEOUT);
+                    break;
+                }
+        }
+        return;
+    }
+    const int group = warp / kGemvGroupWarps;
+    pdl_wait();
+    const bool active = p.st ? (*(volatile int*)&p.st->active != 0) : true;
+    const int pos = p.st ? *(volatile int*)&p.st->pos : p.pos_fixed;
+    float2 xr[KMAX][16];
+    gemv_load_x<I4Tag, KMAX>(p, xr, red, tid);
+    uint32_t am = 0u;
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k)
+#pragma unroll
+        for (int t = 0; t < 16; ++t) am = max(am, max(abs_bits(xr[k][t].x), abs_bits(xr[k][t].y)));
+    const int S = xfix_shift_cta(am, amx);
+    uint32_t xp[KMAX][32];
+#pragma unroll
+    for (int k = 0; k < KMAX; ++k) {
+#pragma unroll
+        for (int hlf = 0; hlf < 2; ++hlf) {
+            float t16[16];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) { t16[2 * i] = xr[k][8 * hlf + i].x; t16[2 * i + 1] = xr[k][8 * hlf + i].y; }
+            uint32_t w16[16];
+            xfix_block(t16, S, w16);
+#pragma unroll
+            for (int pl = 0; pl < 4; ++pl)
+#pragma unroll
+                for (int g = 0; g < 4; ++g) xp[k][pl * 8 + 4 * hlf + g] = w16[pl * 4 + g];
+        }
+    }
+    const int nblk = (int)(row_bytes >> 4);
+    int j = 0;
+    bool ok = true;
+    int cur = r0;
+    while (cur < r1) {
+        const StageRows sr = next_stage(p, cur, r1, RS);
+        const int slot = j % NS;
+        if ((slot & 1) == group) {
+            if (!mbar_wait_bounded(&full[slot], (uint32_t)((j / NS) & 1))) { ok = false; break; }
+            if (active)
+                gemv_stage_i4<KMAX, RS>(ring + (size_t)slot * stage_bytes, row_bytes, nblk, tid % 256, lane, xp,
+                                        reinterpret_cast<int*>(part), cur - r0, sr.nr);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
+        }
+        ++j;
+        cur += sr.nr;
+    }
+    if (!ok) set_err(p.err, B2_DEV_ERR_TIMEOUT);
+    consumer_bar();
+    if (!active) return;
+    gemv_epilogue<1, false>(p, r0, r1, part, pos, tid, blockIdx.x, gridDim.x, nullptr, S);
 }
 
 }  // namespace b2

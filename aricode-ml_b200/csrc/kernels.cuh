@@ -15,7 +15,7 @@ namespace b2 {
 // x = f32(q[tok]) * scale[tok] (+ learned position row t).
 struct EmbedParams {
     const void* emb;        // [vocab][ld] int8 or f32
-    int emb_i8;
+    int emb_i8;             // 1 int8, 2 int4 (two codes a byte, even column low), 0 f32
     const float* emb_s;     // per-row scales (int8)
     long long ld;
     const float* pos_tab;   // [max_pos][d] or nullptr
@@ -59,7 +59,11 @@ static __global__ void embed_kernel(const __grid_constant__ EmbedParams p) {
     const int tok = s_tok, pos = s_pos;
     for (int i = threadIdx.x; i < p.d; i += blockDim.x) {
         float v;
-        if (p.emb_i8) {
+        if (p.emb_i8 == 2) {
+            const int b = reinterpret_cast<const unsigned char*>(p.emb)[(size_t)tok * p.ld + (i >> 1)];
+            const int q = (((b >> ((i & 1) * 4)) & 15) ^ 8) - 8;
+            v = fmul((float)q, p.emb_s[tok]);
+        } else if (p.emb_i8) {
             const int8_t q = reinterpret_cast<const int8_t*>(p.emb)[(size_t)tok * p.ld + i];
             v = fmul((float)q, p.emb_s[tok]);
         } else {
@@ -522,6 +526,8 @@ inline GemvShape gemv_shape(const GemvParams& p, int esz, int grid_cap) {
 cudaError_t launch_gemv(const GemvParams& p, bool w_i8, cudaStream_t s, bool pdl, int grid_cap,
                         GemvShape* out_shape = nullptr);
 cudaError_t launch_attn(const AttnParams& p, cudaStream_t s, bool pdl);
+// int4 rows (p.i4, p.ld = packed bytes per row)
+cudaError_t launch_gemv_i4(const GemvParams& p, cudaStream_t s, bool pdl, int grid_cap);
 // the same kernel over nseq sequences (grid z; AttnParams::n_of and the strides)
 cudaError_t launch_attn_batched(const AttnParams& p, int nseq, cudaStream_t s);
 cudaError_t launch_embed(const EmbedParams& p, cudaStream_t s, bool pdl);

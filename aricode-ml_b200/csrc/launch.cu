@@ -69,6 +69,36 @@ cudaError_t launch_attn(const AttnParams& p, cudaStream_t s, bool pdl) {
     return launch_ex(attn_decode_kernel, dim3(p.nsplit_max, p.KVH), dim3(kAttnThreads), smem, s, pdl, p);
 }
 
+cudaError_t launch_gemv_i4(const GemvParams& p, cudaStream_t s, bool pdl, int grid_cap) {
+    const GemvShape sh = gemv_shape(p, 1, grid_cap);
+    // packed rows of up to 2 x 256 16-byte blocks = 16384 codes a thread pass covers
+    if (sh.K < 1 || sh.K > 2 || sh.smem > 227 * 1024 || p.paired || p.rope) return cudaErrorInvalidValue;
+    auto go = [&](auto kern) {
+        GemvParams q = p;
+        q.nstages = sh.nstages;
+        q.stage_rows = sh.R;
+        q.ring_offset = sh.ring_offset;
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sh.smem);
+        if (e != cudaSuccess) return e;
+        return launch_ex(kern, dim3(sh.grid), dim3(kGemvThreads), sh.smem, s, pdl, q);
+    };
+    if (sh.K == 1) {
+        switch (sh.R) {
+            case 1: return go(gemv_i4_kernel<1, 1>);
+            case 2: return go(gemv_i4_kernel<1, 2>);
+            case 4: return go(gemv_i4_kernel<1, 4>);
+            case 8: return go(gemv_i4_kernel<1, 8>);
+            default: return go(gemv_i4_kernel<1, 16>);
+        }
+    }
+    switch (sh.R) {
+        case 1: return go(gemv_i4_kernel<2, 1>);
+        case 2: return go(gemv_i4_kernel<2, 2>);
+        case 4: return go(gemv_i4_kernel<2, 4>);
+        default: return go(gemv_i4_kernel<2, 8>);
+    }
+}
+
 cudaError_t launch_attn_batched(const AttnParams& p, int nseq, cudaStream_t s) {
     const int G = p.H / p.KVH;
     const size_t smem = attn_smem_bytes(G, p.dh, p.nsplit_max);

@@ -38,7 +38,8 @@ struct DevMat {
     const float* s = nullptr;
     int rows = 0, cols = 0;
     int ld = 0;
-    bool i8 = false;
+    bool i8 = false;        // int8 or int4 codes with per-row scales
+    bool i4 = false;        // int4: two codes a byte, ld in bytes
 };
 
 struct NormRef {
@@ -258,7 +259,10 @@ struct b2_ctx {
         m.rows = (int)rows;
         m.cols = (int)cols;
         m.ld = (int)t.ld;
-        m.i8 = t.dtype == 1;
+        m.i8 = t.dtype == 1 || t.dtype == 3;
+        m.i4 = t.dtype == 3;
+        if (m.i4 && (cols % 2 || t.ld * 2 < cols))
+            throw Err(B2_E_FORMAT, "int4 tensor '" + name + "' must have an even row length");
         if (m.i8) {
             if (t.ld % 16) throw Err(B2_E_FORMAT, "int8 tensor '" + name + "' row stride not 16-aligned");
             if (cols > kXfixMaxN)
@@ -597,6 +601,7 @@ void assemble(b2_ctx* c, const b2json::Value& plan) {
     if (pe && pe[0] == '0') c->pf_why = "batched prefill disabled (B2_PREFILL_BATCHED=0)";
     else if (c->tp_size > 1) c->pf_why = "tensor parallelism";
     else if (c->pos_tab) c->pf_why = "learned positional embedding";
+    else if (c->emb.i4 || c->lm.i4) c->pf_why = "int4 weights";
     else {
         c->pf_ok = true;
         for (const Block& B : c->blocks) {
@@ -630,7 +635,7 @@ std::vector<Op> build_ops(b2_ctx* c, bool with_head) {
     };
     const int d_local = c->d / c->tp_size, d0 = c->tp_rank * d_local;   // this rank's rows of x
     EmbedParams ep{};
-    ep.emb = c->emb.w; ep.emb_i8 = c->emb.i8; ep.emb_s = c->emb.s; ep.ld = c->emb.ld;
+    ep.emb = c->emb.w; ep.emb_i8 = c->emb.i4 ? 2 : (c->emb.i8 ? 1 : 0); ep.emb_s = c->emb.s; ep.ld = c->emb.ld;
     ep.pos_tab = c->pos_tab; ep.max_pos = c->max_pos;
     ep.d = c->d; ep.vocab = c->vocab; ep.max_seq = c->max_seq;
     ep.prompt = c->prompt; ep.st = c->st; ep.x = c->x;
@@ -696,14 +701,14 @@ std::vector<Op> build_ops(b2_ctx* c, bool with_head) {
             gemv(dn, true, true);
         } else {
             p.W[0] = B.w1.w; p.S[0] = B.w1.s; p.bias[0] = B.b1;
-            p.rows[0] = B.d_ffn; p.nseg = 1; p.ld = B.w1.ld;
+            p.rows[0] = B.d_ffn; p.nseg = 1; p.ld = B.w1.ld; p.i4 = B.w1.i4;
             p.epi = EPI_GELU; p.y = c->f;
             gemv(p, true);
 
             GemvParams f2{};
             f2.st = c->st; f2.err = &c->st->err;
             f2.W[0] = B.w2.w; f2.S[0] = B.w2.s; f2.bias[0] = B.b2;
-            f2.rows[0] = c->d; f2.nseg = 1; f2.ld = B.w2.ld;
+            f2.rows[0] = c->d; f2.nseg = 1; f2.ld = B.w2.ld; f2.i4 = B.w2.i4;
             f2.x = c->f; f2.n = B.d_ffn; f2.norm = NORM_NONE;
             f2.epi = EPI_RESID; f2.y = c->x; f2.resid = c->x;
             gemv(f2, true);
@@ -713,7 +718,7 @@ std::vector<Op> build_ops(b2_ctx* c, bool with_head) {
         GemvParams h{};
         h.st = c->st; h.err = &c->st->err;
         h.W[0] = c->lm.w; h.S[0] = c->lm.s; h.bias[0] = c->lm_b;
-        h.rows[0] = c->lm.rows; h.nseg = 1; h.ld = c->lm.ld;
+        h.rows[0] = c->lm.rows; h.nseg = 1; h.ld = c->lm.ld; h.i4 = c->lm.i4;
         h.x = c->x; h.n = c->d;
         h.norm = c->fnorm.kind; h.ng = c->fnorm.g; h.nb = c->fnorm.b; h.eps = c->eps;
         h.row_base = c->tp_rank * c->lm.rows;
@@ -737,6 +742,7 @@ int enqueue_step(b2_ctx* c, bool with_head, cudaStream_t s) {
     for (const Op& o : ops) {
         if (o.kind == TK_EMBED) CK(launch_embed(o.e, s, c->pdl));
         else if (o.kind == TK_ATTN) CK(launch_attn(o.a, s, c->pdl));
+        else if (o.g.i4) CK(launch_gemv_i4(o.g, s, c->pdl, c->sm_count));
         else CK(launch_gemv(o.g, o.i8, s, c->pdl, c->sm_count));
     }
     return (int)ops.size();
@@ -774,6 +780,7 @@ bool tk_phase_of(const b2_ctx* c, const Op& o, TkPhase& T, size_t& part_bytes, s
     }
     T.g = o.g;
     const GemvParams& g = o.g;
+    if (g.i4) { why = "int4 weights (per-layer int4 kernel)"; return false; }
     const size_t row_bytes = (size_t)g.ld * (o.i8 ? 1 : 4);
     const int K = (int)((row_bytes / 16 + 255) / 256);
     if (K < 1 || K > 3) { why = "weight rows longer than 12 KB"; return false; }
@@ -1298,7 +1305,7 @@ BlobIndex read_blob_index(FILE* f, std::string* embedded_plan) {
         t.ld = (long long)ld;
         t.off = (size_t)off;
         t.nbytes = (size_t)nb;
-        if ((dtype != 1 && dtype != 2) || off + nb > ix.data_bytes)
+        if ((dtype < 1 || dtype > 3) || off + nb > ix.data_bytes)
             throw Err(B2_E_FORMAT, std::string("bad table entry for ") + name);
         ix.tensors[name] = t;
     }

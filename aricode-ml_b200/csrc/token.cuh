@@ -911,7 +911,10 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
                 const EmbedParams& e = T.e;
                 for (int i = tid; i < e.d; i += kGemvConsumerThreads) {
                     float v;
-                    if (e.emb_i8) {
+                    if (e.emb_i8 == 2) {
+                        const int b = reinterpret_cast<const unsigned char*>(e.emb)[(size_t)tok * e.ld + (i >> 1)];
+                        v = fmul((float)((((b >> ((i & 1) * 4)) & 15) ^ 8) - 8), e.emb_s[tok]);
+                    } else if (e.emb_i8) {
                         const int8_t q = reinterpret_cast<const int8_t*>(e.emb)[(size_t)tok * e.ld + i];
                         v = fmul((float)q, e.emb_s[tok]);
                     } else {

@@ -248,9 +248,25 @@ def quantize_rows(W):
     return q, scales.astype(np.float32)
 
 
-def build_tensors(arch, collected, *, quantize="int8", int8_attention=False):
+def quantize_rows_i4(W):
+    """Per-row symmetric int4 as the reference packs --int4-linear / --int4-embedding
+    (aricode_pack.py:3299-3355, numpy f32): scale = max|row| / 7, q = clip(
+    round_half_even(W / safe), -8, 7), two codes per byte, the even column in the
+    low nibble. Returns (packed uint8 [rows, cols / 2], scales f32 [rows])."""
+    W = np.asarray(W, np.float32)
+    amax = np.abs(W).max(axis=1) if W.size else np.zeros((0,), np.float32)
+    scales = (amax / 7.0).astype(np.float32)
+    safe = np.where(scales > 0, scales, 1.0)
+    q4 = np.round(W / safe[:, None]).clip(-8, 7).astype(np.int8)
+    u = (q4 & 0x0F).astype(np.uint8)
+    return (u[:, 0::2] | (u[:, 1::2] << 4)).astype(np.uint8), scales
+
+
+def build_tensors(arch, collected, *, quantize="int8", int8_attention=False, int4_linear=False,
+                  int4_embedding=False):
     """collected (from resolve) -> {name: array} in arch order, reference names,
-    with ``<W>_scales`` companions for int8 weights."""
+    with ``<W>_scales`` companions for int8 (int8 arrays) and int4 (uint8 arrays of
+    packed nibbles) weights."""
     if quantize != "int8":
         raise PackError("--target b200 packs the --quantize int8 decode format; pass "
                         "--quantize int8")
@@ -258,7 +274,13 @@ def build_tensors(arch, collected, *, quantize="int8", int8_attention=False):
     tensors = {}
     for kind, idx, suffix, W, b in collected:
         wname, bname = A.tensor_names(kind, idx, suffix)
-        if kind in qkinds:
+        if (int4_linear and kind == "linear") or (int4_embedding and kind == "embedding"):
+            if W.shape[1] % 2:
+                raise PackError(f"int4 packing needs an even row length; {kind} op {idx} has {W.shape[1]}")
+            q, s = quantize_rows_i4(W)
+            tensors[wname] = q
+            tensors[f"{wname}_scales"] = s
+        elif kind in qkinds:
             q, s = quantize_rows(W)
             tensors[wname] = q
             tensors[f"{wname}_scales"] = s
@@ -270,14 +292,15 @@ def build_tensors(arch, collected, *, quantize="int8", int8_attention=False):
 
 
 def write_staging(out_base, tensors):
-    """The reference's per-tensor staging files (``<out>_<name>.i8/.f32``)."""
+    """The reference's per-tensor staging files (``<out>_<name>.i8/.i4/.f32``)."""
     base = Path(out_base)
     written = []
+    ext = {np.dtype(np.int8): "i8", np.dtype(np.uint8): "i4"}
     for name, arr in tensors.items():
         if name.endswith("_scales"):
             p = base.parent / f"{base.name}_{name}.f32"
         else:
-            p = base.parent / f"{base.name}_{name}.{'i8' if arr.dtype == np.int8 else 'f32'}"
+            p = base.parent / f"{base.name}_{name}.{ext.get(arr.dtype, 'f32')}"
         arr.tofile(p)
         written.append(p)
     return written
@@ -324,13 +347,15 @@ def parse_args(argv=None):
     return p.parse_args(argv)
 
 
-def pack(arch, sd, *, keys="fc{idx_plus_1}.{kind}", quantize="int8", int8_attention=False,
+def pack(arch, sd, *, keys="fc{idx_plus_1}.{kind}", quantize="int8", int8_attention=False, int4_linear=False,
+         int4_embedding=False,
          out=None, max_new_tokens=16, sample="greedy", eos_token=None, rng_seed=20260502,
          tp=1, emit_staging=False, input_format="stdin-tokens", input_file=None,
          max_prompt_tokens=512):
     plan = A.decoder_plan(arch, int8_attention=int8_attention)
     collected = resolve(arch, sd, keys)
-    tensors = build_tensors(arch, collected, quantize=quantize, int8_attention=int8_attention)
+    tensors = build_tensors(arch, collected, quantize=quantize, int8_attention=int8_attention,
+                            int4_linear=int4_linear, int4_embedding=int4_embedding)
     for blk in plan["blocks"]:                 # GQA biases the checkpoint provides
         if blk.get("kind") == "gqa":
             gi = blk["q"][len("Wgqaq"):]
@@ -407,8 +432,6 @@ def main(argv=None):
     if a.infer_arch:
         raise PackError("--infer-arch covers classifier/CNN archs, which are not part of the "
                         "decoder path")
-    if a.int4_linear or a.int4_embedding:
-        raise PackError("--int4-linear / --int4-embedding are not supported by --target b200 yet")
     classifier = [f for f, v in (("--input-images", a.input_images), ("--input-labels", a.input_labels),
                                  ("--n-test", a.n_test), ("--mean", a.mean), ("--std", a.std),
                                  ("--no-argmax", a.no_argmax)) if v not in (None, False)]
@@ -435,7 +458,8 @@ def main(argv=None):
         raise PackError("the --arch file must hold a JSON list of ops, each [kind, args...]")
     sd = load_state_dict(a.checkpoint)
     plan, tensors = pack(arch, sd, keys=a.keys, quantize=a.quantize,
-                         int8_attention=a.int8_attention, out=a.out,
+                         int8_attention=a.int8_attention, int4_linear=a.int4_linear,
+                         int4_embedding=a.int4_embedding, out=a.out,
                          max_new_tokens=a.max_new_tokens, sample=a.sample,
                          eos_token=a.eos_token, rng_seed=a.rng_seed, tp=a.tp,
                          emit_staging=a.emit_staging, input_format=a.input_format,

@@ -82,6 +82,7 @@ def _declare(L):
     L.b2_last_error.argtypes = [vp, C.c_char_p, C.c_int]
     L.b2_gemv_i8_rowscale.argtypes = [vp, C.c_int64, vp, vp, vp, vp, C.c_int, C.c_int, vp]
     L.b2_gemv_f32.argtypes = [vp, C.c_int64, vp, vp, vp, C.c_int, C.c_int, vp]
+    L.b2_gemv_i4_rowscale.argtypes = [vp, C.c_int64, vp, vp, vp, vp, C.c_int, C.c_int, vp]
     L.b2_gemm_i8_rowscale_workspace.restype = C.c_size_t
     L.b2_gemm_i8_rowscale_workspace.argtypes = [C.c_int, C.c_int64]
     L.b2_gemm_i8_rowscale.argtypes = [vp, C.c_int64, vp, vp, C.c_int64, vp, vp, C.c_int64, C.c_int, C.c_int,
@@ -358,6 +359,15 @@ def gemv_i8(W, scale, x, bias=None, y=None, n=None, stream=None):
     y = y if y is not None else torch.empty(m, dtype=torch.float32, device=W.device)
     check(lib().b2_gemv_i8_rowscale(_ptr(W), ld, _ptr(scale), _ptr(x), _ptr(bias), _ptr(y), m, n,
                                     _stream(stream)))
+    return y
+
+
+def gemv_i4(W, scale, x, n, bias=None, y=None, stream=None):
+    """W: uint8 [m, ld] packed int4 CUDA tensor (ld % 16 == 0), n codes per row."""
+    import torch
+    m, ld = W.shape
+    y = y if y is not None else torch.empty(m, dtype=torch.float32, device=W.device)
+    check(lib().b2_gemv_i4_rowscale(_ptr(W), ld, _ptr(scale), _ptr(x), _ptr(bias), _ptr(y), m, n, _stream(stream)))
     return y
 
 

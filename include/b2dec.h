@@ -193,6 +193,13 @@ int b2_last_error(b2_ctx* ctx, char* buf, int len);
 int b2_gemv_i8_rowscale(const int8_t* W, int64_t ld, const float* scale, const float* x,
                         const float* bias, float* y, int m, int n, void* stream);
 
+/* The same for int4 rows in the reference's --int4-linear format (two codes a
+ * byte, even column in the low nibble, ld = packed bytes per row, ld % 16 == 0,
+ * n even): the exact int8 dot over the unpacked codes, streaming the packed rows.
+ * Replaces: arr_i4_matvec_f32_perrow + bias add (aricode_pack.py:168-181). */
+int b2_gemv_i4_rowscale(const uint8_t* W, int64_t ld, const float* scale, const float* x, const float* bias,
+                        float* y, int m, int n, void* stream);
+
 /* The same for T input vectors at once, on the tensor cores (tcgen05 kind::i8
  * over the byte planes of each vector's fixed-point copy): Y[t][j] = scale[j] *
  * dot(W[j,:], X[t,:]) (+ bias[j]), bit-identical to T calls of

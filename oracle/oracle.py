@@ -84,6 +84,8 @@ def _declare(L):
     L.b2o_silu.restype = C.c_float; L.b2o_silu.argtypes = [C.c_float]
     L.b2o_gelu.restype = C.c_float; L.b2o_gelu.argtypes = [C.c_float]
     L.b2o_quantize_rows.argtypes = [f32p, C.c_int64, C.c_int64, i8p, C.c_int64, f32p]
+    L.b2o_gemv_i4.argtypes = [C.c_void_p, C.c_int64, f32p, f32p, C.c_int64, C.c_int64, f32p]
+    L.b2o_unpack_i4.argtypes = [C.c_void_p, C.c_int64, i8p]
     L.b2o_gemv_i8.argtypes = [i8p, C.c_int64, f32p, f32p, C.c_int64, C.c_int64, f32p]
     L.b2o_gemv_f32.argtypes = [f32p, C.c_int64, f32p, C.c_int64, C.c_int64, f32p]
     L.b2o_rmsnorm.argtypes = [f32p, f32p, C.c_int, C.c_float, f32p]
@@ -205,6 +207,22 @@ def gemv_i8(q, scale, x):
     return y
 
 
+def gemv_i4(packed, scale, x, n):
+    """packed: uint8 [m, ld] (two codes a byte, even column low), n logical columns."""
+    packed = _c(packed, np.uint8); scale = _c(scale, np.float32); x = _c(x, np.float32)
+    m, ld = packed.shape
+    y = np.zeros(m, np.float32)
+    lib().b2o_gemv_i4(packed.ctypes.data, ld, _p(scale), _p(x), m, n, _p(y))
+    return y
+
+
+def unpack_i4(packed, n):
+    packed = _c(packed, np.uint8).ravel()
+    out = np.zeros(n, np.int8)
+    lib().b2o_unpack_i4(packed.ctypes.data, n, _p(out, i8p))
+    return out
+
+
 def gemv_f32(W, x):
     W = _c(W, np.float32); x = _c(x, np.float32)
     m, n = W.shape
@@ -315,6 +333,10 @@ class OracleModel:
 
         def mat(name):
             w = t[name]
+            if w.dtype == np.uint8:                      # int4, packed two codes per byte
+                a = arr(name, np.uint8)
+                s = arr(name + "_scales")
+                return Mat(2, a.ctypes.data, _p(s), a.shape[1])
             if w.dtype == np.int8:
                 a = arr(name, np.int8)
                 s = arr(name + "_scales")

@@ -383,6 +383,47 @@ void b2o_gemv_f32(const float* W, int64_t ld, const float* x,
     parallel_for(m, gemv_f32_range, &g);
 }
 
+/* int4 rows: the reference's builtin unpacks each row's nibbles into int8 (low
+ * nibble = even column, sign-extended) and runs its int8 dot on them
+ * (aricode_pack.py:168-181); here the unpacked row goes through the selected int8
+ * matvec mode. */
+void b2o_unpack_i4(const uint8_t* packed, int64_t n, int8_t* codes) {
+    for (int64_t i = 0; i < n; ++i) {
+        const int v = (packed[i >> 1] >> ((i & 1) * 4)) & 15;
+        codes[i] = (int8_t)((v ^ 8) - 8);
+    }
+}
+
+typedef struct { const uint8_t* W; int64_t ld; const float* scale; const float* x; int64_t n; float* y;
+                 const int32_t* X; int S; int mode; } gemv4_ctx;
+
+static void gemv_i4_range(void* c, int64_t r0, int64_t r1) {
+    const gemv4_ctx* g = (const gemv4_ctx*)c;
+    int8_t* row = (int8_t*)malloc((size_t)(g->n > 0 ? g->n : 1));
+    if (!row) abort();
+    for (int64_t r = r0; r < r1; ++r) {
+        b2o_unpack_i4(g->W + r * g->ld, g->n, row);
+        if (g->mode == 1) g->y[r] = b2o_dot_i8_f32acc(row, g->x, g->n) * g->scale[r];
+        else if (g->mode == 2) g->y[r] = (float)(b2o_dot_i8_f64(row, g->x, g->n) * (double)g->scale[r]);
+        else g->y[r] = b2o_dot_i8x(row, g->X, g->n, g->S) * g->scale[r];
+    }
+    free(row);
+}
+
+void b2o_gemv_i4(const uint8_t* W, int64_t ld, const float* scale, const float* x,
+                 int64_t m, int64_t n, float* y) {
+    int32_t* X = NULL;
+    int S = 0;
+    if (g_matvec_mode == 0) {
+        X = (int32_t*)malloc((size_t)(n > 0 ? n : 1) * sizeof(int32_t));
+        if (!X) abort();
+        S = b2o_xfix(x, n, X);
+    }
+    gemv4_ctx g = {W, ld, scale, x, n, y, X, S, g_matvec_mode};
+    parallel_for(m, gemv_i4_range, &g);
+    free(X);
+}
+
 /* rmsnorm_affine_f32 (aricode_pack.py:585-607): x * (1/sqrt(mean(x^2)+eps)), then * g */
 void b2o_rmsnorm(const float* x, const float* g, int d, float eps, float* y) {
     float s[256];
@@ -753,7 +794,8 @@ void b2o_state_fill_kv(const b2o_model* m, b2o_state* s, int count, uint64_t see
 static void proj(const b2o_mat* M, const float* b, const float* x, int64_t m, int64_t n,
                  float* y) {
     if (M->is_i8) {
-        b2o_gemv_i8((const int8_t*)M->w, M->ld, M->s, x, m, n, y);
+        if (M->is_i8 == 2) b2o_gemv_i4((const uint8_t*)M->w, M->ld, M->s, x, m, n, y);
+        else b2o_gemv_i8((const int8_t*)M->w, M->ld, M->s, x, m, n, y);
         if (b) for (int64_t i = 0; i < m; ++i) y[i] = y[i] + b[i];
     } else {
         b2o_gemv_f32((const float*)M->w, M->ld, x, m, n, y);
@@ -774,7 +816,13 @@ int32_t b2o_step(const b2o_model* m, b2o_state* s, int32_t tok, float* logits, i
 
     /* embedding: f32(q) * scale — the reference's f64 product rounded to f32 is the
      * same value (aricode_pack.py:2254-2265); positional add in f32 (:2275-2284) */
-    if (m->emb.is_i8) {
+    if (m->emb.is_i8 == 2) {          /* int4 rows: nibble, sign-extended (aricode_pack.py:2226-2249) */
+        const uint8_t* row = (const uint8_t*)m->emb.w + (int64_t)tok * m->emb.ld;
+        for (int i = 0; i < d; ++i) {
+            const int v = (row[i >> 1] >> ((i & 1) * 4)) & 15;
+            s->x[i] = (float)((v ^ 8) - 8) * m->emb.s[tok];
+        }
+    } else if (m->emb.is_i8) {
         const int8_t* row = (const int8_t*)m->emb.w + (int64_t)tok * m->emb.ld;
         for (int i = 0; i < d; ++i) s->x[i] = (float)row[i] * m->emb.s[tok];
     } else {

@@ -56,6 +56,11 @@ void b2o_gemv_i8(const int8_t* W, int64_t ld, const float* scale, const float* x
                  int64_t m, int64_t n, float* y);
 void b2o_gemv_f32(const float* W, int64_t ld, const float* x,
                   int64_t m, int64_t n, float* y);
+/* int4 rows (arr_i4_matvec_f32_perrow, aricode_pack.py:168-181: the nibbles of a
+ * row unpacked to int8 codes, then the int8 matvec): packed [m][ld bytes] */
+void b2o_unpack_i4(const uint8_t* packed, int64_t n, int8_t* codes);
+void b2o_gemv_i4(const uint8_t* W, int64_t ld, const float* scale, const float* x,
+                 int64_t m, int64_t n, float* y);
 /* int8 rows: x as 32-bit block fixed point X = trunc(x * 2^S); returns S, or
  * B2O_XFIX_BAD when x holds a NaN or an infinity (every row is then NaN) */
 #define B2O_XFIX_BAD (-100000)
@@ -118,7 +123,9 @@ enum { B2O_SB_ATTN = 0, B2O_SB_FFN = 1 };
 enum { B2O_NORM_RMS = 0, B2O_NORM_LN = 1 };
 enum { B2O_FFN_SWIGLU = 0, B2O_FFN_GELU = 1 };
 
-/* a matrix: int8 codes + per-row scales, or f32; rows padded to ld elements */
+/* a matrix: is_i8 1 = int8 codes + per-row scales, 2 = int4 codes packed two per
+ * byte (even column in the low nibble; ld in bytes) + per-row scales, 0 = f32;
+ * rows padded to ld elements */
 typedef struct { int is_i8; const void* w; const float* s; int64_t ld; } b2o_mat;
 
 typedef struct {

@@ -19,6 +19,11 @@ What it writes (all small, committed):
   reference packer's int8 staging files (``ref_staging/``).
 * ``rope_golden.json``: the RoPE known-answer vector of
   examples/rope_min/test_rope.ari:20-25.
+* ``<fixture>/ref_staging_int4/`` for cfgT, tiny_decoder_packed and
+  tiny_decoder_2block: the reference packer's staging files with
+  ``--int4-linear --int4-embedding`` added (``.i4`` nibble-packed codes, low
+  nibble = even column, and their ``_scales.f32``). ``--int4-only`` writes just
+  these, from the fixtures already committed.
 
 Nothing under tests/ reads the reference at test time; only this script does.
 """
@@ -81,7 +86,7 @@ def cfg_t_state_dict():
     return sd, prompt
 
 
-def run_ref_packer(ref, workdir, checkpoint, arch_path, prompt_bin, int8_attention, max_new, out):
+def run_ref_packer(ref, workdir, checkpoint, arch_path, prompt_bin, int8_attention, max_new, out, extra=()):
     cmd = [sys.executable, str(ref / "tools" / "aricode_pack.py"), "--checkpoint", str(checkpoint),
            "--arch", str(arch_path), "--keys", "fc{idx_plus_1}.{kind}",
            "--input-format", "embedded", "--input-file", str(prompt_bin), "--embed",
@@ -89,6 +94,7 @@ def run_ref_packer(ref, workdir, checkpoint, arch_path, prompt_bin, int8_attenti
            "--out", str(workdir / out)]
     if int8_attention:
         cmd.append("--int8-attention")
+    cmd += list(extra)
     subprocess.run(cmd, check=True, cwd=workdir, stdout=subprocess.DEVNULL)
     return cmd
 
@@ -96,15 +102,42 @@ def run_ref_packer(ref, workdir, checkpoint, arch_path, prompt_bin, int8_attenti
 def collect_staging(workdir, out, dest):
     dest.mkdir(parents=True, exist_ok=True)
     for f in sorted(workdir.glob(f"{out}_*")):
-        if f.suffix in (".i8", ".f32"):
+        if f.suffix in (".i8", ".i4", ".f32"):
             shutil.copy(f, dest / f.name[len(out) + 1:])
+
+
+INT4_FIXTURES = {"cfgT": ("model.safetensors", True), "tiny_decoder_packed": ("synth.pt", False),
+                 "tiny_decoder_2block": ("synth.pt", False)}
+
+
+def int4_staging(ref, td):
+    """ref_staging_int4/ of the committed fixtures (the reference packer with
+    --int4-linear --int4-embedding)."""
+    for name, (ckpt, i8attn) in INT4_FIXTURES.items():
+        src = HERE / name
+        work = td / f"{name}_int4"
+        work.mkdir()
+        prompt = json.loads((src / "prompt.json").read_text())["prompt"] if name == "cfgT" else \
+            list((src / "prompt.bin").read_bytes())
+        (work / "prompt.bin").write_bytes(bytes(prompt))
+        run_ref_packer(ref, work, src / ckpt, src / "arch.json", work / "prompt.bin", i8attn, 4, name,
+                       extra=("--int4-linear", "--int4-embedding"))
+        dest = src / "ref_staging_int4"
+        if dest.exists():
+            shutil.rmtree(dest)
+        collect_staging(work, name, dest)
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--int4-only", action="store_true")
     a = ap.parse_args()
     ref = Path(a.reference)
+    if a.int4_only:
+        with tempfile.TemporaryDirectory() as td:
+            int4_staging(ref, Path(td))
+        return
     manifest = {"generated_by": "tests/golden/make_golden.py", "fixtures": {}}
 
     with tempfile.TemporaryDirectory() as td:
@@ -147,6 +180,7 @@ def main():
             manifest["fixtures"][ex] = {"int8_attention": i8attn, "max_new": max_new,
                                         "expected_tokens": exp,
                                         "source": f"examples/{ex}/prepare.py"}
+        int4_staging(ref, td)
 
     (HERE / "rope_golden.json").write_text(json.dumps({
         "source": "examples/rope_min/test_rope.ari:20-25,42",

@@ -150,3 +150,50 @@ def test_gqa_biases_are_staged_when_the_checkpoint_has_them(pkg):
     sd["model.layers.0.self_attn.k_proj.bias"] = torch.ones(7)
     with pytest.raises(pkg.pack.PackError):
         pkg.pack.pack(arch, sd)
+
+
+@pytest.mark.parametrize("name", ["cfgT", "tiny_decoder_packed", "tiny_decoder_2block"])
+def test_int4_codes_and_scales_bytes_equal_reference_packer(pkg, name):
+    """--int4-linear --int4-embedding: every staging file the reference packer wrote
+    (.i4 nibble-packed codes, their scales, and the int8/f32 rest) is byte-identical
+    (aricode_pack.py:3299-3355)."""
+    d = GOLDEN / name
+    arch = json.loads((d / "arch.json").read_text())
+    ckpt = "model.safetensors" if name == "cfgT" else "synth.pt"
+    sd = pkg.pack.load_state_dict(d / ckpt)
+    plan, tensors = pkg.pack.pack(arch, sd, int8_attention=(name == "cfgT"), int4_linear=True,
+                                  int4_embedding=True)
+    bad = []
+    for f in sorted((d / "ref_staging_int4").iterdir()):
+        t = tensors.get(f.stem)
+        if t is None or np.ascontiguousarray(t).tobytes() != f.read_bytes():
+            bad.append(f.name)
+    assert bad == []
+    assert tensors[plan["embedding"]].dtype == np.uint8
+
+
+def test_int4_blob_roundtrip_and_oracle_matvec(pkg, oracle, tmp_path):
+    d = GOLDEN / "cfgT"
+    arch = json.loads((d / "arch.json").read_text())
+    sd = pkg.pack.load_state_dict(d / "model.safetensors")
+    plan, tensors = pkg.pack.pack(arch, sd, int8_attention=True, int4_linear=True, int4_embedding=True)
+    pkg.blob.write_blob(tmp_path / "m.b2blob", tensors, plan)
+    plan2, t2 = pkg.blob.read_blob(tmp_path / "m.b2blob")
+    W = plan["lm_head"]["W"]
+    assert t2[W].dtype == np.uint8 and np.array_equal(t2[W], tensors[W])
+    # the int4 matvec is the int8 matvec of the unpacked codes
+    n = plan["d_model"]
+    x = np.random.default_rng(0).standard_normal(n).astype(np.float32)
+    codes = np.stack([oracle.unpack_i4(r, n) for r in tensors[W]])
+    assert codes.min() >= -8 and codes.max() <= 7
+    assert np.array_equal(oracle.gemv_i4(tensors[W], tensors[W + "_scales"], x, n),
+                          oracle.gemv_i8(codes, tensors[W + "_scales"], x))
+    # and the decoder runs on it
+    om = oracle.OracleModel(plan2, t2)
+    assert len(om.generate([1, 2, 3], 5)) == 5
+
+
+def test_int4_odd_rows_are_refused(pkg):
+    with pytest.raises(pkg.pack.PackError):
+        pkg.pack.build_tensors([["linear", 3, 2]], [("linear", 0, "", np.ones((2, 3), np.float32), None)],
+                               int4_linear=True)

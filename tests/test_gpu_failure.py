@@ -2,7 +2,7 @@
 part makes the other rank's bounded cross-rank wait run out; that rank's call
 returns B2_E_DEVICE (about a second later) instead of hanging, and its context
 can still be destroyed. Rank 1 launches nothing, so both ranks can share one GPU;
-NVLS and multicast are not involved (plain peer stores over CUDA IPC)."""
+NVLS is not involved (plain peer stores over CUDA IPC)."""
 import json
 import os
 import socket

@@ -675,7 +675,10 @@ std::vector<Op> build_ops(b2_ctx* c, bool with_head) {
             a.nsplit_max = c->attn_nsplit_max;
             a.st = c->st; a.err = &c->st->err;
             if (tp) a.mir = c->mir;
-            { Op op; op.kind = TK_ATTN; op.a = a; op.mirror = tp; ops.push_back(op); }
+            { Op op; op.kind = TK_ATTN; op.a = a; ops.push_back(op); }
+            // token kernel: the splits are merged in a phase of their own (the
+            // per-layer attention kernel merges them itself)
+            { Op op; op.kind = TK_ACOMB; op.a = a; op.mirror = tp; ops.push_back(op); }
 
             GemvParams o{};
             o.st = c->st; o.err = &c->st->err;
@@ -739,13 +742,16 @@ std::vector<Op> build_ops(b2_ctx* c, bool with_head) {
 // per-layer path: one kernel per operation, chained by programmatic dependent launch
 int enqueue_step(b2_ctx* c, bool with_head, cudaStream_t s) {
     const std::vector<Op> ops = build_ops(c, with_head);
+    int n = 0;
     for (const Op& o : ops) {
+        if (o.kind == TK_ACOMB) continue;
         if (o.kind == TK_EMBED) CK(launch_embed(o.e, s, c->pdl));
         else if (o.kind == TK_ATTN) CK(launch_attn(o.a, s, c->pdl));
         else if (o.g.i4) CK(launch_gemv_i4(o.g, s, c->pdl, c->sm_count));
         else CK(launch_gemv(o.g, o.i8, s, c->pdl, c->sm_count));
+        ++n;
     }
-    return (int)ops.size();
+    return n;
 }
 
 // the sampler after the LM head (sampling modes only); returns kernels launched
@@ -770,6 +776,10 @@ bool tk_phase_of(const b2_ctx* c, const Op& o, TkPhase& T, size_t& part_bytes, s
     T.kind = o.kind;
     if (o.kind == TK_EMBED) {
         T.e = o.e;
+        return true;
+    }
+    if (o.kind == TK_ACOMB) {
+        T.a = o.a;
         return true;
     }
     if (o.kind == TK_ATTN) {

@@ -30,9 +30,13 @@
 //   TK_ATTN   split-KV decode attention: item (query head h, 64-key split s) on
 //             CTA item % grid; the K chunk and V chunk arrive as two ring
 //             stages; the row of the current position (written by this step's
-//             Q/K/V phase) is read from global memory; the last item of a head
-//             combines the splits with the -60 tail. Arithmetic order as
-//             attn_decode_kernel (attn.cuh) and oracle/refdec.c attn_head().
+//             Q/K/V phase) is read from global memory; each item writes its
+//             split's (o_s, m_s, l_s);
+//   TK_ACOMB  after the grid barrier, the outputs (h, d) spread over the CTAs,
+//             each merging head h's splits with the -60 tail (a separate phase:
+//             no split waits for another, so no CTA's tail waits on the slowest
+//             split). Arithmetic order as attn_decode_kernel (attn.cuh) and
+//             oracle/refdec.c attn_head().
 //
 // Every value is computed by the same code and in the same order as the
 // per-launch kernels, so results are bit-identical to them and to the oracle.
@@ -41,7 +45,7 @@
 
 namespace b2 {
 
-enum TkKind : int { TK_EMBED = 0, TK_GEMV = 1, TK_ATTN = 2 };
+enum TkKind : int { TK_EMBED = 0, TK_GEMV = 1, TK_ATTN = 2, TK_ACOMB = 3 };
 // compiled GEMV shapes: weight type, 16-byte blocks per thread per row (1, or up
 // to 3: rows of at most 12 KB), rows per stage, paired (gate+up)
 enum TkVariant : int {
@@ -58,7 +62,6 @@ constexpr int kTkMaxSlots = 7;                    // any count >= 3 (see tk_full
 constexpr int kTkStamps = 12;                     // timeline slots per phase and CTA
 constexpr int kTkInflight = 0;                    // default cap on bulk copies outstanding per CTA (0: none)
 constexpr int kTkMaxSplits = 256;                 // max_seq <= 16384
-constexpr int kTkFastCombine = 16;               // splits combined in one round of loads (n <= 1024)
 constexpr int kTkGroupScratch = 64 + 4 + kTkMaxSplits;   // floats per consumer group
 // shared memory: full barriers [0, 224) (4 per slot), empty barriers [224, 288),
 // reduction slots [288, 320), flags [320, 352), vector-staging barrier 352
@@ -157,18 +160,6 @@ __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
     unsigned v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
-}
-
-// (value, tag) words of the tagged attention partials: relaxed gpu-scope loads and
-// stores, so that the reader's tag check is a morally strong read of the writer's
-// store under the PTX memory model
-__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned long long* p) {
-    unsigned long long v;
-    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void st_relaxed_gpu_u64(unsigned long long* p, unsigned long long v) {
-    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
 __device__ __forceinline__ void group_bar(int group) {
@@ -341,7 +332,12 @@ __device__ __forceinline__ bool tk_attn_produce(const AttnParams& a, int n, int 
 __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, int cta, int ncta,
                                                 const unsigned char* ring, int NS, uint64_t* full,
                                                 uint64_t* empty, int& j, int group, int gwarp, int lane,
-                                                float* scr, volatile int* gflag, unsigned tag) {
+                                                float* scr, volatile int* gflag,
+                                                unsigned long long* tr = nullptr) {
+    // timeline (thread 0 of each group): [5] group 0's, [7] group 1's total ns
+    // waiting for ring stages
+    const bool stamp = tr && gwarp == 0 && lane == 0;
+    unsigned long long wstage = 0;
     const int n = pos + 1;
     int nsplit;
     const int items = tk_attn_items(a, n, nsplit);
@@ -377,7 +373,9 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
             kn[i] = (has_new && d < dh) ? __ldcg(knew + d) : 0.0f;
         }
         const float vn = (has_new && gt < dh) ? __ldcg(vnew + gt) : 0.0f;
+        unsigned long long tw = stamp ? globaltimer_ns() : 0ull;
         if (!group_wait(tk_full(full, j, NS), tk_full_parity(j, NS), group, gt, gflag)) return false;
+        if (stamp) wstage += globaltimer_ns() - tw;
         const float* Ks = reinterpret_cast<const float*>(ring + (size_t)slotk * kTkSlotBytes);
         // scores: warp gwarp takes keys gwarp + 8 i; lane L sums d = L, L + 32, ...
         float v[8];
@@ -428,132 +426,103 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
         }
         group_bar(group);
         // o_s[d] = sum_j e_j V[j][d], j ascending (one thread per d)
+        tw = stamp ? globaltimer_ns() : 0ull;
         if (!group_wait(tk_full(full, j + 1, NS), tk_full_parity(j + 1, NS), group, gt, gflag)) return false;
+        if (stamp) wstage += globaltimer_ns() - tw;
         const float* Vs = reinterpret_cast<const float*>(ring + (size_t)slotv * kTkSlotBytes);
         const int stride = dh + 2;
-        // up to kTkFastCombine splits, each value goes out with this phase's tag in one
-        // 8-byte store (value, tag) and the last arriver checks the tags instead of
-        // both sides fencing; more splits: plain floats and fences
-        const bool tagged = nsplit <= kTkFastCombine;
+        // the split's (o_s, m_s, l_s): plain stores, merged by the combine phase after
+        // the next grid barrier
         float* pp = a.part + ((size_t)h * a.nsplit_max + s) * stride;
-        unsigned long long* pq = reinterpret_cast<unsigned long long*>(a.part) + ((size_t)h * a.nsplit_max + s) * stride;
-        auto pack = [&](float v) { return (unsigned long long)__float_as_uint(v) | ((unsigned long long)tag << 32); };
         if (gt < dh) {
             float acc = 0.0f;
             for (int jj = 0; jj < len; ++jj)
                 acc = ffma(sc[jj], jj == jnew ? vn : Vs[jj * dh + gt], acc);
-            if (tagged) {
-                st_relaxed_gpu_u64(pq + gt, pack(acc));
-                if (gt == 0) {
-                    st_relaxed_gpu_u64(pq + dh, pack(ml[0]));
-                    st_relaxed_gpu_u64(pq + dh + 1, pack(ml[1]));
-                }
-            } else {
-                pp[gt] = acc;
-                if (gt == 0) { pp[dh] = ml[0]; pp[dh + 1] = ml[1]; }
-            }
+            pp[gt] = acc;
+            if (gt == 0) { pp[dh] = ml[0]; pp[dh + 1] = ml[1]; }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slotv]);
-        if (!tagged) __threadfence();
-        group_bar(group);
-        if (gt == 0) {
-            const unsigned t = atomicAdd(a.counters + h, 1u);
-            reinterpret_cast<int*>(ml)[2] = (t == (unsigned)(nsplit - 1));
-        }
-        group_bar(group);
-        if (!reinterpret_cast<int*>(ml)[2]) continue;
-        // last split of head h: combine the splits and the -60 tail
-        const float* base = a.part + (size_t)h * a.nsplit_max * stride;
-        if (tagged) {
-            // one round of loads (repeated, bounded, until every tag is this phase's:
-            // the other splits have issued their stores, which may still be landing):
-            // every split's (m, l) into scratch by threads t < nsplit, and each
-            // thread's o[gt] of every split into registers; then each thread forms M,
-            // the weights and l itself, in split order
-            const unsigned long long* bq = reinterpret_cast<const unsigned long long*>(a.part) +
-                                           (size_t)h * a.nsplit_max * stride;
-            auto get = [&](const unsigned long long* q, float& v) {
-                const unsigned long long w = ld_relaxed_gpu_u64(q);
-                v = __uint_as_float((unsigned)w);
-                return (unsigned)(w >> 32) == tag;
-            };
-            float ot[kTkFastCombine];
-            const uint64_t tw = globaltimer_ns();
-            for (;;) {
-                bool all = true;
-                if (gt < nsplit) {
-                    all = get(bq + (size_t)gt * stride + dh, wsm[gt]) && all;
-                    all = get(bq + (size_t)gt * stride + dh + 1, sc[gt]) && all;
-                }
-#pragma unroll
-                for (int t = 0; t < kTkFastCombine; ++t) {
-                    ot[t] = 0.0f;
-                    if (t < nsplit && gt < dh) all = get(bq + (size_t)t * stride + gt, ot[t]) && all;
-                }
-                if (all) break;
-                if (globaltimer_ns() - tw > kWaitLimitNs) { set_err(a.err, B2_DEV_ERR_TIMEOUT); break; }
-            }
-            group_bar(group);
-            if (gt < dh) {
-                float M = wsm[0];
-                for (int t = 1; t < nsplit; ++t) M = fmaxf(M, wsm[t]);
-                if (n < a.max_seq) M = fmaxf(M, -60.0f);
-                float l = 0.0f, o = 0.0f;
-#pragma unroll
-                for (int t = 0; t < kTkFastCombine; ++t) {
-                    if (t < nsplit) {
-                        const float w = exp_f(fsub(wsm[t], M));
-                        l = ffma(sc[t], w, l);
-                        o = ffma(ot[t], w, o);
-                    }
-                }
-                if (n < a.max_seq) l = ffma((float)(a.max_seq - n), exp_f(fsub(-60.0f, M)), l);
-                mirror_store(a.mir, a.out + (size_t)h * dh + gt, fdiv(o, l));
-            }
-            if (gt == 0) a.counters[h] = 0u;
-            group_bar(group);                           // scratch reused by the next item
-            continue;
-        }
-        __threadfence();
-        // every split's (m, l) in one parallel round of loads: m into wsm, l into sc
-        for (int t = gt; t < nsplit; t += 256) {
-            wsm[t] = __ldcg(base + (size_t)t * stride + dh);
-            if (t < 64) sc[t] = __ldcg(base + (size_t)t * stride + dh + 1);
-        }
-        group_bar(group);
-        if (gt == 0) {
-            float M = wsm[0];
-            for (int t = 1; t < nsplit; ++t) M = fmaxf(M, wsm[t]);
-            if (n < a.max_seq) M = fmaxf(M, -60.0f);
-            float l = 0.0f;
-            for (int t = 0; t < nsplit; ++t) {
-                const float lt = t < 64 ? sc[t] : __ldcg(base + (size_t)t * stride + dh + 1);
-                const float w = exp_f(fsub(wsm[t], M));
-                wsm[t] = w;
-                l = ffma(lt, w, l);
-            }
-            if (n < a.max_seq) l = ffma((float)(a.max_seq - n), exp_f(fsub(-60.0f, M)), l);
-            ml[3] = l;
-            a.counters[h] = 0u;
-        }
-        group_bar(group);
-        if (gt < dh) {
-            float o = 0.0f;
-            for (int t0 = 0; t0 < nsplit; t0 += 8) {
-                float pv[8];
-#pragma unroll
-                for (int u = 0; u < 8; ++u)
-                    pv[u] = t0 + u < nsplit ? __ldcg(base + (size_t)(t0 + u) * stride + gt) : 0.0f;
-#pragma unroll
-                for (int u = 0; u < 8; ++u)
-                    if (t0 + u < nsplit) o = ffma(pv[u], wsm[t0 + u], o);
-            }
-            mirror_store(a.mir, a.out + (size_t)h * dh + gt, fdiv(o, ml[3]));
-        }
         group_bar(group);                               // scratch reused by the next item
     }
+    if (stamp) tr[group == 0 ? 5 : 7] = wstage;
     return true;
+}
+
+// Combine phase (after the attention phase's grid barrier): the H * dh outputs
+// are spread over the CTAs; output (h, d) merges head h's splits in split order
+// with the -60 tail, as the decode combine does (attn_decode_kernel,
+// oracle/refdec.c attn_head): M = max of the m_s (and -60 when n < max_seq),
+// w_s = exp(m_s - M), l = sum l_s w_s, o = sum o_s[d] w_s, out = o / l.
+__device__ __forceinline__ void tk_attn_combine(const AttnParams& a, int pos, int cta, int ncta, int tid) {
+    const int n = pos + 1, dh = a.dh;
+    const int nsplit = (n + kAttnChunk - 1) / kAttnChunk;
+    const int stride = dh + 2;
+    int r0, r1;
+    cta_rows(a.H * dh, 1, cta, ncta, r0, r1);
+    for (int idx = r0 + tid; idx < r1; idx += kGemvConsumerThreads) {
+        const int h = idx / dh, d = idx % dh;
+        const float* base = a.part + (size_t)h * a.nsplit_max * stride;
+        float M, l = 0.0f, o = 0.0f;
+        if (nsplit <= 16) {
+            // every split's (m, l, o[d]) in one round of loads
+            float ms[16], ls[16], os[16];
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+                const bool in = u < nsplit;
+                const float* pt = base + (size_t)u * stride;
+                ms[u] = in ? __ldcg(pt + dh) : 0.0f;
+                ls[u] = in ? __ldcg(pt + dh + 1) : 0.0f;
+                os[u] = in ? __ldcg(pt + d) : 0.0f;
+            }
+            M = ms[0];
+#pragma unroll
+            for (int u = 1; u < 16; ++u)
+                if (u < nsplit) M = fmaxf(M, ms[u]);
+            if (n < a.max_seq) M = fmaxf(M, -60.0f);
+#pragma unroll
+            for (int u = 0; u < 16; ++u) {
+                if (u < nsplit) {
+                    const float w = exp_f(fsub(ms[u], M));
+                    l = ffma(ls[u], w, l);
+                    o = ffma(os[u], w, o);
+                }
+            }
+        } else {
+            M = __ldcg(base + dh);
+            for (int t0 = 1; t0 < nsplit; t0 += 16) {
+                float ms[16];
+#pragma unroll
+                for (int u = 0; u < 16; ++u)
+                    ms[u] = t0 + u < nsplit ? __ldcg(base + (size_t)(t0 + u) * stride + dh) : 0.0f;
+#pragma unroll
+                for (int u = 0; u < 16; ++u)
+                    if (t0 + u < nsplit) M = fmaxf(M, ms[u]);
+            }
+            if (n < a.max_seq) M = fmaxf(M, -60.0f);
+            for (int t0 = 0; t0 < nsplit; t0 += 16) {
+                float ms[16], ls[16], os[16];
+#pragma unroll
+                for (int u = 0; u < 16; ++u) {
+                    const bool in = t0 + u < nsplit;
+                    const float* pt = base + (size_t)(t0 + u) * stride;
+                    ms[u] = in ? __ldcg(pt + dh) : 0.0f;
+                    ls[u] = in ? __ldcg(pt + dh + 1) : 0.0f;
+                    os[u] = in ? __ldcg(pt + d) : 0.0f;
+                }
+#pragma unroll
+                for (int u = 0; u < 16; ++u) {
+                    if (t0 + u < nsplit) {
+                        const float w = exp_f(fsub(ms[u], M));
+                        l = ffma(ls[u], w, l);
+                        o = ffma(os[u], w, o);
+                    }
+                }
+            }
+        }
+        if (n < a.max_seq) l = ffma((float)(a.max_seq - n), exp_f(fsub(-60.0f, M)), l);
+        mirror_store(a.mir, a.out + idx, fdiv(o, l));
+    }
 }
 
 // GEMV producer over the token ring: one bulk copy per matrix per stage (the
@@ -927,11 +896,12 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
         } else if (T.kind == TK_GEMV) {
             ok = tk_gemv_dispatch<VS>(T, pos, ring, NS, full, empty, j, group, gwarp, lane, tid, red, part, cta,
                                       ncta, tr, vec, vbar, vphase, amx);
+        } else if (T.kind == TK_ACOMB) {
+            tk_attn_combine(T.a, pos, cta, ncta, tid);
         } else {
             tk_stamp(tr, 1, tid);
             tk_stamp(tr, 2, tid);
-            ok = tk_attn_consume(T.a, pos, cta, ncta, ring, NS, full, empty, j, group, gwarp, lane, gscr, gflag,
-                                 seq * 1024u + (unsigned)ph + 1u);
+            ok = tk_attn_consume(T.a, pos, cta, ncta, ring, NS, full, empty, j, group, gwarp, lane, gscr, gflag, tr);
             if (tr) {
                 consumer_bar();
                 tk_stamp(tr, 3, tid);

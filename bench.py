@@ -6,7 +6,9 @@
 One step = decoding the 256 new tokens after the 512-token prompt (positions
 512..767) with every input already in HBM; the KV cache of the prompt is filled
 once before timing and every step rewinds to position 512, so all steps do the
-same work. value = generated tokens per second of that one sequence; with N > 1
+same work. The roofline traffic comes from profiles/token_kernel_llama2-7b.md
+(a reduced-case DRAM capture scaled by the algorithmic bytes); `batched` adds the
+64-sequence configuration (64 x (1024 + 128)) on the same GPU. value = generated tokens per second of that one sequence; with N > 1
 GPUs (one process each, torchrun) the model is split over them (tensor
 parallelism: every matrix by output rows, attention by heads), so N GPUs decode
 the same batch-1 sequence faster (strong scaling). e2e = the same metric through the public C ABI call
@@ -544,7 +546,9 @@ def time_e2e(torch, dec, prompt, new, stream, dist=None, reps=2):
         ms = float(t.item())
     return {"value": new / (ms / 1000.0), "unit": "tokens/s",
             "h2d_bytes_per_step": 4 * P + 64, "d2h_bytes_per_step": 4 * new + 64,
-            "ms_per_generate": ms, "includes": "token-at-a-time prefill of the prompt"}
+            "ms_per_generate": ms,
+            "includes": "prefill of the prompt (batched on the tensor cores on one GPU, token at a time "
+                        "with tensor parallelism) + 256 decode steps"}
 
 
 if __name__ == "__main__":

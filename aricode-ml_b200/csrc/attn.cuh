@@ -36,6 +36,13 @@ struct AttnParams {
     // n_of[z] + 1 keys (n_of: positions; nullptr for one sequence)
     const int* n_of;
     long long sq, skv, spart;
+    // token kernel, (value, tag) words: q, this step's K / V rows [KVH * dh], the
+    // split partials (same layout as part) and the output
+    const unsigned long long* tq;
+    const unsigned long long* tkn;
+    const unsigned long long* tvn;
+    unsigned long long* tpart;
+    unsigned long long* tout;
 };
 
 // bytes of scratch one call needs

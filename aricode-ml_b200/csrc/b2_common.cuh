@@ -195,6 +195,35 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     }
 }
 
+// (value, tag) words: one aligned 8-byte access carries an f32 and the tag of the
+// phase that wrote it, so a reader that sees the tag has the value with it (no
+// fence on either side; the tag changes every phase and launch, so an old word
+// never passes for a new one)
+__device__ __forceinline__ void st_tag(unsigned long long* p, float v, unsigned tag) {
+    const unsigned long long w = (unsigned long long)__float_as_uint(v) | ((unsigned long long)tag << 32);
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_tag(const unsigned long long* p) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
+}
+__device__ __forceinline__ void ld_tag2(const unsigned long long* p, unsigned long long& a, unsigned long long& b) {
+    asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+__device__ __forceinline__ bool tag_ok(unsigned long long w, unsigned tag) { return (unsigned)(w >> 32) == tag; }
+__device__ __forceinline__ float tag_val(unsigned long long w) { return __uint_as_float((unsigned)w); }
+// the value of a word whose tag must be `tag`: polls (bounded by the deadline;
+// false after it, with the last value)
+__device__ __forceinline__ bool tag_wait(const unsigned long long* p, unsigned tag, unsigned long long& w,
+                                         uint64_t deadline) {
+    for (uint32_t it = 0; !tag_ok(w, tag); ++it) {
+        if ((it & 15u) == 15u && globaltimer_ns() > deadline) return false;
+        w = ld_tag(p);
+    }
+    return true;
+}
+
 // 1-D bulk copy global -> shared (TMA engine), completion signalled on `bar`.
 // dst, src 16-byte aligned; bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {

@@ -98,6 +98,14 @@ struct GemvParams {
     int* tp_cidx;
     int* tp_cnan;
     unsigned* tp_aflag;
+    // token kernel, (value, tag) words (nullptr: plain floats): tx the input vector
+    // (read with tag checks), ty the output (y, or q for EPI_QKV), tresid the
+    // residual, tkn / tvn this step's K and V rows [kv_heads * dh] (EPI_QKV)
+    const unsigned long long* tx;
+    unsigned long long* ty;
+    const unsigned long long* tresid;
+    unsigned long long* tkn;
+    unsigned long long* tvn;
 };
 
 // ordering for greedy sampling: non-NaN beats NaN, larger wins, ties -> lower index
@@ -809,7 +817,7 @@ __device__ __forceinline__ EpiRow gemv_epi_load(const GemvParams& p, int r0, int
             e.v[2] = tr[0];
             e.v[3] = tr[1];
         } else if (p.epi == EPI_RESID) {
-            e.v[2] = __ldcg(p.resid + row);
+            e.v[2] = p.tresid ? tag_val(ld_tag(p.tresid + row)) : __ldcg(p.resid + row);
         }
     }
     return e;
@@ -823,9 +831,11 @@ __device__ __forceinline__ void gemv_epi_store(const EpiRow& e, int nrows, int t
 // [r0, r1) from the warp sums in part[]. CTA `cta` of `ncta` takes part in the
 // grid-wide argmax (EPI_ARGMAX) through amax_* and the last-CTA ticket. epi, when
 // given, holds the preloaded per-row inputs of the first 512 rows.
+// otag: the tag written with each output when the outputs are (value, tag) words
 template <int ESZ, bool PAIRED>
 __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, int r0, int r1, const float* part, int pos,
-                                              int tid, int cta, int ncta, const float* epi = nullptr, int S = 0) {
+                                              int tid, int cta, int ncta, const float* epi = nullptr, int S = 0,
+                                              unsigned otag = 0u) {
     // int8: part holds int32 plane sums [row][NM][4]; f32: warp sums [row][NM][8]
     const int* parti = reinterpret_cast<const int*>(part);
     auto dotv = [&](int rl, int m) {
@@ -846,7 +856,8 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, int r0, int r
             const float su = pre(rl) ? epi[rl * 4 + 1] : p.S[1][lrow];
             const float g = fmul(dotv(rl, 0), sg);
             const float u = fmul(dotv(rl, 1), su);
-            mirror_store(p.mir, p.y + lrow, fmul(silu_f(g), u));
+            if (p.ty) st_tag(p.ty + lrow, fmul(silu_f(g), u), otag);
+            else mirror_store(p.mir, p.y + lrow, fmul(silu_f(g), u));
             continue;
         }
         int seg, row;
@@ -873,19 +884,25 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, int r0, int r
             for (int e = 0; e < step; ++e) {
                 const int rr = row + e;
                 if (seg == 0) {
-                    p.qout[rr] = fmul(out[e], p.qscale);
+                    if (p.ty) st_tag(p.ty + rr, fmul(out[e], p.qscale), otag);
+                    else p.qout[rr] = fmul(out[e], p.qscale);
                 } else if (pos < p.max_seq) {
                     const int kvh = rr / p.dh, hd = rr % p.dh;
                     float* cache = seg == 1 ? p.kcache : p.vcache;
                     cache[((size_t)kvh * p.max_seq + pos) * p.dh + hd] = out[e];
+                    if (p.tkn) st_tag((seg == 1 ? p.tkn : p.tvn) + rr, out[e], otag);
                 } else {
                     set_err(p.err, B2_DEV_ERR_KV_OVERFLOW);
                 }
             }
         } else if (p.epi == EPI_RESID) {
-            mirror_store(p.mir, p.y + row, fadd(val[0], pre(rl) ? epi[rl * 4 + 2] : __ldcg(p.resid + row)));
+            const float r = pre(rl) ? epi[rl * 4 + 2]
+                                    : (p.tresid ? tag_val(ld_tag(p.tresid + row)) : __ldcg(p.resid + row));
+            if (p.ty) st_tag(p.ty + row, fadd(val[0], r), otag);
+            else mirror_store(p.mir, p.y + row, fadd(val[0], r));
         } else if (p.epi == EPI_GELU) {
-            mirror_store(p.mir, p.y + row, gelu_f(val[0]));
+            if (p.ty) st_tag(p.ty + row, gelu_f(val[0]), otag);
+            else mirror_store(p.mir, p.y + row, gelu_f(val[0]));
         } else if (p.epi == EPI_ARGMAX) {
             if (p.y) p.y[row] = val[0];
             if (row + p.row_base == 0 && p.amax_v0nan) *p.amax_v0nan = (val[0] != val[0]) ? 1 : 0;
@@ -893,7 +910,8 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, int r0, int r
                 best_v = val[0]; best_i = row + p.row_base; have_best = true;
             }
         } else {
-            mirror_store(p.mir, p.y + row, val[0]);
+            if (p.ty) st_tag(p.ty + row, val[0], otag);
+            else mirror_store(p.mir, p.y + row, val[0]);
         }
     }
 

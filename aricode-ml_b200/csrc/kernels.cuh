@@ -24,6 +24,7 @@ struct EmbedParams {
     const int* prompt;      // device prompt ids
     StepState* st;
     float* x;               // residual stream [d]
+    unsigned long long* tx; // token kernel: x as (value, tag) words instead
 };
 
 static __global__ void embed_kernel(const __grid_constant__ EmbedParams p) {

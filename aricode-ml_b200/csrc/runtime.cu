@@ -146,6 +146,10 @@ struct b2_ctx {
     float* f = nullptr;
     float* logits = nullptr;
     float* attn_part = nullptr;
+    // token kernel: the activations as (value, tag) words (x, q, attention output,
+    // FFN hidden vector, this step's K / V rows); the split partials reuse attn_part
+    unsigned long long *tx = nullptr, *tq = nullptr, *tatt = nullptr, *tf = nullptr, *tkn = nullptr, *tvn = nullptr;
+    bool tk_tags = false;   // the token kernel's phases meet through tagged words, not grid barriers
     unsigned* attn_cnt = nullptr;
     int attn_nsplit_max = 1;
     float* amax_val = nullptr;
@@ -533,6 +537,12 @@ void assemble(b2_ctx* c, const b2json::Value& plan) {
     const size_t i_prompt = add((size_t)c->max_seq * 4);
     const size_t i_out = add((size_t)c->max_seq * 4);
     const size_t i_samp = add((size_t)c->vocab * 8);
+    const size_t i_tx = add((size_t)c->d * 8);
+    const size_t i_tq = add((size_t)max_q * 8);
+    const size_t i_tatt = add((size_t)max_q_all * 8);
+    const size_t i_tf = add((size_t)max_ffn * 8);
+    const size_t i_tkn = add((size_t)max_KVH * max_dh * 8);
+    const size_t i_tvn = add((size_t)max_KVH * max_dh * 8);
     c->work_bytes = off;
     if (cudaMalloc(&c->d_work, c->work_bytes) != cudaSuccess) throw Err(B2_E_OOM, "workspace allocation failed");
     CK(cudaMemsetAsync(c->d_work, 0, c->work_bytes, c->stream));
@@ -574,6 +584,12 @@ void assemble(b2_ctx* c, const b2json::Value& plan) {
     c->prompt = reinterpret_cast<int*>(w + offs[i_prompt]);
     c->out_ids = reinterpret_cast<int*>(w + offs[i_out]);
     c->samp_e = reinterpret_cast<double*>(w + offs[i_samp]);
+    c->tx = reinterpret_cast<unsigned long long*>(w + offs[i_tx]);
+    c->tq = reinterpret_cast<unsigned long long*>(w + offs[i_tq]);
+    c->tatt = reinterpret_cast<unsigned long long*>(w + offs[i_tatt]);
+    c->tf = reinterpret_cast<unsigned long long*>(w + offs[i_tf]);
+    c->tkn = reinterpret_cast<unsigned long long*>(w + offs[i_tkn]);
+    c->tvn = reinterpret_cast<unsigned long long*>(w + offs[i_tvn]);
 
     // RoPE table in f64 via libm, stored f32 (rope_alloc_f32, rope_f32.ari:34-55)
     if (c->rope_dh) {
@@ -826,9 +842,67 @@ bool tk_phase_of(const b2_ctx* c, const Op& o, TkPhase& T, size_t& part_bytes, s
     return true;
 }
 
+// One GPU: let the phases of a table meet through (value, tag) words instead of
+// grid barriers. Every activation a phase reads from this launch gets its tagged
+// twin and the index of the phase that wrote it; false (table unchanged in its
+// meaning) when some input has no twin.
+bool tk_tag_table(b2_ctx* c, std::vector<TkPhase>& ph, size_t first, size_t count) {
+    int wx = -1, wq = -1, wpart = -1, watt = -1, wf = -1;
+    std::vector<TkPhase> out(ph.begin() + first, ph.begin() + first + count);
+    for (size_t i = 0; i < out.size(); ++i) {
+        TkPhase& T = out[i];
+        const int idx = (int)i;
+        if (T.kind == TK_EMBED) {
+            T.e.tx = c->tx;
+            wx = idx;
+            continue;
+        }
+        T.nobar = 1;
+        if (T.kind == TK_ATTN) {
+            if (wq < 0) return false;
+            T.a.tq = c->tq; T.a.tkn = c->tkn; T.a.tvn = c->tvn;
+            T.a.tpart = reinterpret_cast<unsigned long long*>(c->attn_part);
+            T.tin = wq;
+            wpart = idx;
+            continue;
+        }
+        if (T.kind == TK_ACOMB) {
+            if (wpart < 0 || T.a.out < c->att) return false;
+            T.a.tpart = reinterpret_cast<unsigned long long*>(c->attn_part);
+            T.a.tout = c->tatt + (T.a.out - c->att);
+            T.tin = wpart;
+            watt = idx;
+            continue;
+        }
+        GemvParams& g = T.g;
+        if (g.x == c->x) { g.tx = c->tx; T.tin = wx; }
+        else if (g.x == c->att) { g.tx = c->tatt; T.tin = watt; }
+        else if (g.x == c->f) { g.tx = c->tf; T.tin = wf; }
+        else return false;
+        if (T.tin < 0) return false;
+        if (g.epi == EPI_QKV) {
+            g.ty = c->tq; g.tkn = c->tkn; g.tvn = c->tvn;
+            wq = idx;
+        } else if (g.epi == EPI_RESID) {
+            if (g.y < c->x || g.y >= c->x + c->d || g.resid != g.y) return false;
+            g.ty = c->tx + (g.y - c->x);
+            g.tresid = c->tx + (g.resid - c->x);
+            wx = idx;
+        } else if (g.epi == EPI_SWIGLU || g.epi == EPI_GELU) {
+            if (g.y < c->f) return false;
+            g.ty = c->tf + (g.y - c->f);
+            wf = idx;
+        } else if (g.epi != EPI_ARGMAX) {
+            return false;
+        }
+    }
+    std::copy(out.begin(), out.end(), ph.begin() + first);
+    return true;
+}
+
 bool tk_prepare_kernel(b2_ctx* c, int vs) {
     int per_sm = 0;
-    CK(tk_prepare(vs, c->tk_smem, &per_sm));
+    CK(tk_prepare(vs, c->tk_tags, c->tk_smem, &per_sm));
     return per_sm >= 1;
 }
 
@@ -866,16 +940,28 @@ void setup_token(b2_ctx* c) {
         c->token_why = "more than 1023 phases (phase tags)";
         return;
     }
+    // one GPU: tagged words between phases instead of grid barriers (tensor
+    // parallelism keeps the barriers, which also wait for the peers)
+    c->tk_tags = false;
+    const char* tg = std::getenv("B2_TK_TAGS");
+    if (c->tp_size == 1 && !(tg && tg[0] == '0')) {
+        std::vector<TkPhase> tagged = ph;
+        if (tk_tag_table(c, tagged, 0, (size_t)c->nph_prefill) &&
+            tk_tag_table(c, tagged, (size_t)c->nph_prefill, (size_t)c->nph_decode)) {
+            ph.swap(tagged);
+            c->tk_tags = true;
+        }
+    }
     const size_t vec_off = (kTkPartOffset + part + 127) & ~(size_t)127;
     const size_t ring_off = (vec_off + vec_floats * 4 + 127) & ~(size_t)127;
     c->tk_vec_offset = (int)vec_off;
     c->tk_vec_floats = (int)vec_floats;
     const size_t smem_max = 226 * 1024;             // dynamic; the static argmax slots need the rest
     if (ring_off + 3 * (size_t)kTkSlotBytes > smem_max) { c->token_why = "too many rows per CTA"; return; }
-    int ns = (int)((smem_max - ring_off) / kTkSlotBytes);
-    ns = std::min(ns, kTkMaxSlots);
-    if (const char* sl = std::getenv("B2_TK_SLOTS"))             // tuning: fewer slots, more L1
-        ns = std::max(3, std::min(ns, std::atoi(sl)));
+    const int ns_fit = std::min((int)((smem_max - ring_off) / kTkSlotBytes), kTkMaxSlots);
+    int ns = std::min(ns_fit, kTkDefaultSlots);
+    if (const char* sl = std::getenv("B2_TK_SLOTS"))             // tuning: 3 .. what fits
+        ns = std::max(3, std::min(ns_fit, std::atoi(sl)));
     c->tk_ns = ns;
     c->tk_ring_offset = (int)ring_off;
     c->tk_smem = ring_off + (size_t)ns * kTkSlotBytes;
@@ -937,7 +1023,7 @@ void launch_token(b2_ctx* c, bool with_head, cudaStream_t s) {
     at[0].val.cooperative = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    CK(tk_launch(c->token_vs, cfg, P));
+    CK(tk_launch(c->token_vs, c->tk_tags, cfg, P));
 }
 
 // ------------------------------------------------------------------ batched prefill
@@ -1948,6 +2034,7 @@ int b2_query(b2_ctx* ctx, const char* key, double* value) {
     else if (k == "sm_count") *value = ctx->sm_count;
     else if (k == "pdl") *value = ctx->pdl ? 1 : 0;
     else if (k == "token_kernel") *value = ctx->token ? 1 : 0;
+    else if (k == "token_tags") *value = ctx->token && ctx->tk_tags ? 1 : 0;
     else if (k == "prefill_batched") *value = ctx->pf_ok ? 1 : 0;
     else if (k == "batch") *value = ctx->bt_n;
     else return B2_E_INVALID;

@@ -6,17 +6,18 @@
 
 namespace b2 {
 
-cudaError_t tk_prepare(int vs, size_t smem, int* per_sm) {
-    auto k = vs ? token_kernel<1> : token_kernel<0>;
+cudaError_t tk_prepare(int vs, bool tags, size_t smem, int* per_sm) {
+    auto k = vs ? (tags ? token_kernel<1, true> : token_kernel<1, false>)
+                : (tags ? token_kernel<0, true> : token_kernel<0, false>);
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     return cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, k, kTkThreads, smem);
 }
 
-cudaError_t tk_launch(int vs, const cudaLaunchConfig_t& cfg, const TkParams& P) {
+cudaError_t tk_launch(int vs, bool tags, const cudaLaunchConfig_t& cfg, const TkParams& P) {
     cudaLaunchConfig_t c = cfg;
-    if (vs) return cudaLaunchKernelEx(&c, token_kernel<1>, P);
-    return cudaLaunchKernelEx(&c, token_kernel<0>, P);
+    if (vs) return tags ? cudaLaunchKernelEx(&c, token_kernel<1, true>, P) : cudaLaunchKernelEx(&c, token_kernel<1, false>, P);
+    return tags ? cudaLaunchKernelEx(&c, token_kernel<0, true>, P) : cudaLaunchKernelEx(&c, token_kernel<0, false>, P);
 }
 
 }  // namespace b2

@@ -8,7 +8,7 @@
 // the consumers still work on phase p or wait at the grid barrier. Weights do
 // not depend on the activations, so HBM does not wait for a phase boundary.
 //
-// Structure of a CTA (640 threads, ~208 KB shared memory):
+// Structure of a CTA (640 threads, ~200 KB shared memory):
 //   warpgroup 4    producer: one lane walks all phases, one 1-D bulk copy per
 //                  stage into a ring of NS 32 KB slots (mbarrier complete_tx), at
 //                  most kTkInflight copies outstanding (0: no cap beyond the
@@ -19,8 +19,16 @@
 //                  phases (an item's K stage and V stage go to the same group);
 //                  four full barriers per slot keep this exact for any slot count
 //                  (tk_full);
-//                  between phases: consumer barrier + grid barrier (atomic
-//                  arrivals, acquire spin, bounded to 1 s).
+//                  between phases, on one GPU: a consumer barrier only. Every
+//                  activation a phase hands to the next (x, q, this step's K/V
+//                  rows, the split partials, the attention output, the FFN
+//                  hidden vector) is a (value, tag) word, tag = launch x 1024 +
+//                  phase + 1, and the reader polls its words until the tags are
+//                  the producing phase's (bounded to 1 s). No fence on the writer,
+//                  no counter: a CTA starts a phase as soon as its inputs are
+//                  there. With tensor parallelism (peer writes) and with
+//                  B2_TK_TAGS=0: a grid barrier (atomic arrivals, acquire spin,
+//                  bounded to 1 s) over plain floats instead.
 //
 // Phases (TkPhase):
 //   TK_EMBED  CTA 0 writes x = embedding row (+ learned position);
@@ -59,7 +67,8 @@ enum TkVariant : int {
 
 constexpr uint32_t kTkSlotBytes = 32 * 1024;
 constexpr int kTkMaxSlots = 7;                    // any count >= 3 (see tk_full)
-constexpr int kTkStamps = 12;                     // timeline slots per phase and CTA
+constexpr int kTkDefaultSlots = 4;                // measured: 4 x 32 KB streams faster than 5 for Llama-2-7B
+constexpr int kTkStamps = 24;                     // timeline slots per phase and CTA
 constexpr int kTkInflight = 0;                    // default cap on bulk copies outstanding per CTA (0: none)
 constexpr int kTkMaxSplits = 256;                 // max_seq <= 16384
 constexpr int kTkGroupScratch = 64 + 4 + kTkMaxSplits;   // floats per consumer group
@@ -70,16 +79,18 @@ constexpr int kTkEmptyOffset = 224;
 constexpr int kTkRedOffset = 288;
 constexpr int kTkFlagOffset = 320;
 constexpr int kTkVbarOffset = 352;
+constexpr int kTkDbarOffset = 360;                // producer's descriptor copies
 constexpr int kTkScratchOffset = 384;             // after the mbarriers and flags
 constexpr int kTkDescBytes = 864;                 // one phase descriptor copy (>= sizeof(TkPhase))
 constexpr int kTkDescOffset = 3072;               // >= kTkScratchOffset + 2 * kTkGroupScratch * 4
 static_assert(kTkScratchOffset + 2 * kTkGroupScratch * 4 <= kTkDescOffset, "scratch layout");
 static_assert(4 * kTkMaxSlots * 8 <= kTkEmptyOffset && kTkEmptyOffset + kTkMaxSlots * 8 <= kTkRedOffset, "barriers");
-constexpr int kTkPartOffset = kTkDescOffset + 3 * kTkDescBytes + 32;   // 2 consumer + 1 producer copies
+constexpr int kTkPartOffset = kTkDescOffset + 4 * kTkDescBytes + 32;   // 2 consumer + 2 producer copies
 // 640 threads: warpgroups 0-3 consume, warpgroup 4 produces (one lane works).
-// Launched at 96 registers a thread (61,440 per CTA); the producer warpgroup
-// hands registers back (setmaxnreg.dec) and the consumers take them
-// (setmaxnreg.inc): 4 x 128 x 112 + 128 x 32 = 61,440.
+// Registers are granted per warpgroup, so 5 warpgroups launch at 96 registers a
+// thread (61,440 per CTA); the producer warpgroup hands registers back
+// (setmaxnreg.dec) and the consumers take them (setmaxnreg.inc):
+// 4 x 128 x 112 + 128 x 32 = 61,440.
 constexpr int kTkThreads = kGemvConsumerThreads + 128;
 constexpr int kTkProducerRegs = 32;
 constexpr int kTkConsumerRegs = 112;
@@ -92,6 +103,9 @@ struct alignas(16) TkPhase {
     int rs;             // rows per stage the variant is compiled for (paired: second matrix offset)
     int rows;           // rows per stage used (<= rs; chosen so the two groups get equal stage counts)
     int xsync;          // tensor parallelism: the barrier before this phase also waits for every rank
+    int tin;            // (value, tag) inputs: the phase (of this launch) that wrote them, or -1
+    int nobar;          // set on every phase of a table the tagged kernel runs: the inputs it
+                        // reads from this launch are (value, tag) words, waited for word by word
     GemvParams g;
     AttnParams a;
     EmbedParams e;
@@ -205,8 +219,8 @@ __device__ __forceinline__ uint64_t* tk_issue_wait(uint64_t* full, uint64_t* emp
 __device__ __forceinline__ bool tk_grid_sync(unsigned* ctr, unsigned target, int tid, volatile int* flag,
                                              volatile int* abort, const int* xs = nullptr,
                                              const TkParams* P = nullptr, unsigned e = 0, int cta = 0,
-                                             unsigned long long* tr = nullptr) {
-    consumer_bar();
+                                             unsigned long long* tr = nullptr, bool entered = false) {
+    if (!entered) consumer_bar();                       // entered: the caller's threads just met
     if (tid == 0) {
         const bool xsync = xs && *xs && P && P->tp_size > 1;
         bool ok = *abort == 0;
@@ -329,11 +343,12 @@ __device__ __forceinline__ bool tk_attn_produce(const AttnParams& a, int n, int 
 // consumer side: the owning group of each item computes it; all walk j. Every
 // wait is decided once per group (group_wait), so a timeout ends the phase for
 // the whole group together.
+template <bool TAGS>
 __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, int cta, int ncta,
                                                 const unsigned char* ring, int NS, uint64_t* full,
                                                 uint64_t* empty, int& j, int group, int gwarp, int lane,
                                                 float* scr, volatile int* gflag,
-                                                unsigned long long* tr = nullptr) {
+                                                unsigned long long* tr, unsigned itag, unsigned otag) {
     // timeline (thread 0 of each group): [5] group 0's, [7] group 1's total ns
     // waiting for ring stages
     const bool stamp = tr && gwarp == 0 && lane == 0;
@@ -352,8 +367,8 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
         ++j;
     }
     float* sc = scr;                  // [64] scores, then exp
-    float* ml = scr + 64;             // m, l, (int) last, L
-    float* wsm = scr + 68;            // [nsplit] combine weights
+    float* ml = scr + 64;             // m, l
+    bool tagbad = false;
     for (int it = cta; it < items; it += ncta, j += 2) {
         const int slotk = j % NS, slotv = (j + 1) % NS;
         if (((j >> 1) & 1) != group) continue;
@@ -365,14 +380,43 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
         // loads that do not need the ring: q, and this step's K/V row when it falls
         // in the chunk (issued before the waits, so their latency overlaps them)
         const bool has_new = jnew >= 0 && jnew < len;
-        float qv[4], kn[4];
+        float qv[4], kn[4], vn = 0.0f;
+        if constexpr (TAGS) {
+            // (value, tag) words written by this step's Q/K/V phase
+            const uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
+            unsigned long long wq[4], wk[4], wv = 0ull;
+            const unsigned long long* tkn = a.tkn + (size_t)kvh * dh;
+            const unsigned long long* tvn = a.tvn + (size_t)kvh * dh;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int d = lane + 32 * i;
-            qv[i] = d < dh ? __ldcg(a.q + (size_t)h * dh + d) : 0.0f;
-            kn[i] = (has_new && d < dh) ? __ldcg(knew + d) : 0.0f;
+            for (int i = 0; i < 4; ++i) {
+                const int d = lane + 32 * i;
+                wq[i] = d < dh ? ld_tag(a.tq + (size_t)h * dh + d) : 0ull;
+                wk[i] = (has_new && d < dh) ? ld_tag(tkn + d) : 0ull;
+            }
+            if (has_new && gt < dh) wv = ld_tag(tvn + gt);
+            bool okt = true;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int d = lane + 32 * i;
+                if (d < dh) okt = tag_wait(a.tq + (size_t)h * dh + d, itag, wq[i], deadline) && okt;
+                if (has_new && d < dh) okt = tag_wait(tkn + d, itag, wk[i], deadline) && okt;
+                qv[i] = d < dh ? tag_val(wq[i]) : 0.0f;
+                kn[i] = (has_new && d < dh) ? tag_val(wk[i]) : 0.0f;
+            }
+            if (has_new && gt < dh) {
+                okt = tag_wait(tvn + gt, itag, wv, deadline) && okt;
+                vn = tag_val(wv);
+            }
+            if (!okt) tagbad = true;                    // values unusable; the CTA aborts after the phase
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int d = lane + 32 * i;
+                qv[i] = d < dh ? __ldcg(a.q + (size_t)h * dh + d) : 0.0f;
+                kn[i] = (has_new && d < dh) ? __ldcg(knew + d) : 0.0f;
+            }
+            vn = (has_new && gt < dh) ? __ldcg(vnew + gt) : 0.0f;
         }
-        const float vn = (has_new && gt < dh) ? __ldcg(vnew + gt) : 0.0f;
         unsigned long long tw = stamp ? globaltimer_ns() : 0ull;
         if (!group_wait(tk_full(full, j, NS), tk_full_parity(j, NS), group, gt, gflag)) return false;
         if (stamp) wstage += globaltimer_ns() - tw;
@@ -431,22 +475,28 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
         if (stamp) wstage += globaltimer_ns() - tw;
         const float* Vs = reinterpret_cast<const float*>(ring + (size_t)slotv * kTkSlotBytes);
         const int stride = dh + 2;
-        // the split's (o_s, m_s, l_s): plain stores, merged by the combine phase after
-        // the next grid barrier
-        float* pp = a.part + ((size_t)h * a.nsplit_max + s) * stride;
+        // the split's (o_s, m_s, l_s), merged by the combine phase: plain stores after
+        // which a grid barrier follows, or (value, tag) words
+        const size_t pbase = ((size_t)h * a.nsplit_max + s) * stride;
         if (gt < dh) {
             float acc = 0.0f;
             for (int jj = 0; jj < len; ++jj)
                 acc = ffma(sc[jj], jj == jnew ? vn : Vs[jj * dh + gt], acc);
-            pp[gt] = acc;
-            if (gt == 0) { pp[dh] = ml[0]; pp[dh + 1] = ml[1]; }
+            if constexpr (TAGS) {
+                st_tag(a.tpart + pbase + gt, acc, otag);
+                if (gt == 0) { st_tag(a.tpart + pbase + dh, ml[0], otag); st_tag(a.tpart + pbase + dh + 1, ml[1], otag); }
+            } else {
+                float* pp = a.part + pbase;
+                pp[gt] = acc;
+                if (gt == 0) { pp[dh] = ml[0]; pp[dh + 1] = ml[1]; }
+            }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slotv]);
         group_bar(group);                               // scratch reused by the next item
     }
     if (stamp) tr[group == 0 ? 5 : 7] = wstage;
-    return true;
+    return !tagbad;
 }
 
 // Combine phase (after the attention phase's grid barrier): the H * dh outputs
@@ -454,17 +504,62 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
 // with the -60 tail, as the decode combine does (attn_decode_kernel,
 // oracle/refdec.c attn_head): M = max of the m_s (and -60 when n < max_seq),
 // w_s = exp(m_s - M), l = sum l_s w_s, o = sum o_s[d] w_s, out = o / l.
-__device__ __forceinline__ void tk_attn_combine(const AttnParams& a, int pos, int cta, int ncta, int tid) {
+template <bool TAGS>
+__device__ __forceinline__ bool tk_attn_combine(const AttnParams& a, int pos, int cta, int ncta, int tid,
+                                                unsigned itag, unsigned otag) {
     const int n = pos + 1, dh = a.dh;
     const int nsplit = (n + kAttnChunk - 1) / kAttnChunk;
     const int stride = dh + 2;
     int r0, r1;
     cta_rows(a.H * dh, 1, cta, ncta, r0, r1);
+    bool ok = true;
     for (int idx = r0 + tid; idx < r1; idx += kGemvConsumerThreads) {
         const int h = idx / dh, d = idx % dh;
         const float* base = a.part + (size_t)h * a.nsplit_max * stride;
         float M, l = 0.0f, o = 0.0f;
-        if (nsplit <= 16) {
+        if constexpr (TAGS) {
+            // (value, tag) partials of the attention phase, split by split in rounds of 8
+            const unsigned long long* tb = a.tpart + (size_t)h * a.nsplit_max * stride;
+            const uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
+            M = 0.0f;
+            for (int t0 = 0; t0 < nsplit; t0 += 8) {
+                unsigned long long wm[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    wm[u] = t0 + u < nsplit ? ld_tag(tb + (size_t)(t0 + u) * stride + dh) : 0ull;
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    if (t0 + u < nsplit) {
+                        ok = tag_wait(tb + (size_t)(t0 + u) * stride + dh, itag, wm[u], deadline) && ok;
+                        M = (t0 + u == 0) ? tag_val(wm[u]) : fmaxf(M, tag_val(wm[u]));
+                    }
+                }
+            }
+            if (n < a.max_seq) M = fmaxf(M, -60.0f);
+            for (int t0 = 0; t0 < nsplit; t0 += 8) {
+                unsigned long long wm[8], wl[8], wo[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const bool in = t0 + u < nsplit;
+                    const unsigned long long* pt = tb + (size_t)(t0 + u) * stride;
+                    wm[u] = in ? ld_tag(pt + dh) : 0ull;
+                    wl[u] = in ? ld_tag(pt + dh + 1) : 0ull;
+                    wo[u] = in ? ld_tag(pt + d) : 0ull;
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    if (t0 + u < nsplit) {
+                        const unsigned long long* pt = tb + (size_t)(t0 + u) * stride;
+                        ok = tag_wait(pt + dh, itag, wm[u], deadline) && ok;
+                        ok = tag_wait(pt + dh + 1, itag, wl[u], deadline) && ok;
+                        ok = tag_wait(pt + d, itag, wo[u], deadline) && ok;
+                        const float w = exp_f(fsub(tag_val(wm[u]), M));
+                        l = ffma(tag_val(wl[u]), w, l);
+                        o = ffma(tag_val(wo[u]), w, o);
+                    }
+                }
+            }
+        } else if (nsplit <= 16) {
             // every split's (m, l, o[d]) in one round of loads
             float ms[16], ls[16], os[16];
 #pragma unroll
@@ -521,8 +616,10 @@ __device__ __forceinline__ void tk_attn_combine(const AttnParams& a, int pos, in
             }
         }
         if (n < a.max_seq) l = ffma((float)(a.max_seq - n), exp_f(fsub(-60.0f, M)), l);
-        mirror_store(a.mir, a.out + idx, fdiv(o, l));
+        if constexpr (TAGS) st_tag(a.tout + idx, fdiv(o, l), otag);
+        else mirror_store(a.mir, a.out + idx, fdiv(o, l));
     }
+    return ok;
 }
 
 // GEMV producer over the token ring: one bulk copy per matrix per stage (the
@@ -652,26 +749,74 @@ __device__ __forceinline__ bool tk_gemv_consume_i8(const GemvParams& p, int r0, 
 // in shared memory (vec: x at [0, L), gains at [L, 2L), LN bias at [2L, 3L) with
 // L = n rounded up to 16, zeros in [n, L)), normalised in place, and read by the
 // stages from there.
-template <typename WT>
+// x as (value, tag) words -> vec[0, n), every word waited for (bounded): one
+// round of loads, all in flight together; the words not yet written are then
+// polled one by one (a slow path with its own deadline). Thread t owns the word
+// pairs t, t + 512, ... in both passes.
+__device__ __forceinline__ bool tk_poll_tagged(const unsigned long long* tx, int n, unsigned tag, float* vec, int tid) {
+    const uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
+    bool ok = true;
+    for (int q = tid; q < (n >> 1); q += kGemvConsumerThreads) {  // this thread's pairs, as loaded
+        for (int i = 2 * q; i < 2 * q + 2; ++i) {
+            if (__float_as_uint(vec[i]) != 0xffffffffu) continue;  // marked: not yet written
+            unsigned long long w = ld_tag(tx + i);
+            ok = tag_wait(tx + i, tag, w, deadline) && ok;
+            vec[i] = tag_val(w);
+        }
+    }
+    return ok;
+}
+
+__device__ __forceinline__ bool tk_load_tagged(const unsigned long long* tx, int n, unsigned tag, float* vec, int tid) {
+    constexpr int U = 4;                                // word pairs per thread per round
+    const int npair = n >> 1;                           // n is a multiple of 4
+    bool miss = false;
+    for (int q0 = tid; q0 < npair; q0 += U * kGemvConsumerThreads) {
+        unsigned long long a[U], b[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int q = q0 + u * kGemvConsumerThreads;
+            if (q < npair) ld_tag2(tx + 2 * q, a[u], b[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int q = q0 + u * kGemvConsumerThreads;
+            if (q < npair) {
+                // a word whose tag is not the phase's yet is marked with an all-ones
+                // pattern; the slow path re-reads every marked word (a value that has
+                // the pattern itself is read again and kept)
+                const bool oa = tag_ok(a[u], tag), ob = tag_ok(b[u], tag);
+                miss = miss || !oa || !ob;
+                *reinterpret_cast<float2*>(vec + 2 * q) =
+                    make_float2(oa ? tag_val(a[u]) : __uint_as_float(0xffffffffu), ob ? tag_val(b[u]) : __uint_as_float(0xffffffffu));
+            }
+        }
+    }
+    return miss ? tk_poll_tagged(tx, n, tag, vec, tid) : true;
+}
+
+template <typename WT, bool TAGS>
 __device__ __forceinline__ bool tk_gemv(const GemvParams& p, int unit, int rs, int rows, int pos,
                                         const unsigned char* ring,
                                         int NS, uint64_t* full, uint64_t* empty, int& j, int group, int gwarp,
                                         int lane, int tid, float* red, float* part, int cta, int ncta,
                                         unsigned long long* tr, float* vec, uint64_t* vbar, uint32_t& vphase,
-                                        unsigned* amx) {
+                                        unsigned* amx, unsigned itag, unsigned otag) {
     constexpr int ESZ = (int)sizeof(WT);
     int r0, r1;
     cta_rows(total_rows(p), unit, cta, ncta, r0, r1);
     const bool paired = p.paired != 0;
     const int n = p.n, L = (n + 15) & ~15;
-    if (tid == 0) {
+    constexpr bool tagged = TAGS;
+    const bool bulk = !tagged || p.norm != NORM_NONE;   // anything staged by bulk copy
+    if (tid == 0 && bulk) {
         // generic-proxy writes (x by other CTAs; vec by this CTA's last phase) are
         // ordered before the bulk copies that read / overwrite them
         asm volatile("fence.proxy.async.global;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        const uint32_t nb = (uint32_t)n * 4 * (1 + (p.norm != NORM_NONE) + (p.norm == NORM_LN));
+        const uint32_t nb = (uint32_t)n * 4 * ((tagged ? 0 : 1) + (p.norm != NORM_NONE) + (p.norm == NORM_LN));
         mbar_arrive_expect_tx(vbar, nb);
-        bulk_g2s(vec, p.x, (uint32_t)n * 4, vbar);
+        if (!tagged) bulk_g2s(vec, p.x, (uint32_t)n * 4, vbar);
         if (p.norm != NORM_NONE) bulk_g2s(vec + L, p.ng, (uint32_t)n * 4, vbar);
         if (p.norm == NORM_LN) bulk_g2s(vec + 2 * L, p.nb, (uint32_t)n * 4, vbar);
     }
@@ -682,13 +827,30 @@ __device__ __forceinline__ bool tk_gemv(const GemvParams& p, int unit, int rs, i
     float* epi = part + (size_t)(r1 - r0) * nm * 8;
     if constexpr (ESZ == 1)
         for (int i = tid; i < (r1 - r0) * nm * 4; i += kGemvConsumerThreads) reinterpret_cast<int*>(part)[i] = 0;
-    const EpiRow er = paired ? gemv_epi_load<ESZ, true>(p, r0, r1, pos, tid)
-                             : gemv_epi_load<ESZ, false>(p, r0, r1, pos, tid);
-    bool ok = mbar_wait_bounded(vbar, vphase & 1);
-    ++vphase;
+    bool ok = true;
+    if constexpr (tagged) {
+        // the epilogue inputs first (parked in shared memory, so that nothing stays in
+        // registers across the input loads), then x word by word
+        {
+            const EpiRow er = paired ? gemv_epi_load<ESZ, true>(p, r0, r1, pos, tid)
+                                     : gemv_epi_load<ESZ, false>(p, r0, r1, pos, tid);
+            gemv_epi_store(er, r1 - r0, tid, epi);
+        }
+        ok = tk_load_tagged(p.tx, n, itag, vec, tid);
+        consumer_bar();                                 // vec[0, n) complete
+        if (bulk) {
+            ok = mbar_wait_bounded(vbar, vphase & 1) && ok;
+            ++vphase;
+        }
+    } else {
+        const EpiRow er = paired ? gemv_epi_load<ESZ, true>(p, r0, r1, pos, tid)
+                                 : gemv_epi_load<ESZ, false>(p, r0, r1, pos, tid);
+        ok = mbar_wait_bounded(vbar, vphase & 1);
+        ++vphase;
+        gemv_epi_store(er, r1 - r0, tid, epi);
+    }
     const uint32_t am = gemv_norm_smem(p, vec, vec + L, vec + 2 * L, red, tid);
     tk_stamp(tr, 1, tid);
-    gemv_epi_store(er, r1 - r0, tid, epi);
     const int slotid = tid % 256;
     bool okc;
     int S = 0;
@@ -711,8 +873,8 @@ __device__ __forceinline__ bool tk_gemv(const GemvParams& p, int unit, int rs, i
         consumer_bar();
         if (tid == 0) *amx = 0u;                        // every thread read it before its stages
         tk_stamp(tr, 3, tid);
-        if (paired) gemv_epilogue<ESZ, true>(p, r0, r1, part, pos, tid, cta, ncta, epi, S);
-        else gemv_epilogue<ESZ, false>(p, r0, r1, part, pos, tid, cta, ncta, epi, S);
+        if (paired) gemv_epilogue<ESZ, true>(p, r0, r1, part, pos, tid, cta, ncta, epi, S, otag);
+        else gemv_epilogue<ESZ, false>(p, r0, r1, part, pos, tid, cta, ncta, epi, S, otag);
         return ok;
     } else {
         consumer_bar();                                     // normalised x and epi[] visible
@@ -732,28 +894,31 @@ __device__ __forceinline__ bool tk_gemv(const GemvParams& p, int unit, int rs, i
         ok = okc && ok;
         consumer_bar();
         tk_stamp(tr, 3, tid);
-        if (paired) gemv_epilogue<ESZ, true>(p, r0, r1, part, pos, tid, cta, ncta, epi);
-        else gemv_epilogue<ESZ, false>(p, r0, r1, part, pos, tid, cta, ncta, epi);
+        if (paired) gemv_epilogue<ESZ, true>(p, r0, r1, part, pos, tid, cta, ncta, epi, 0, otag);
+        else gemv_epilogue<ESZ, false>(p, r0, r1, part, pos, tid, cta, ncta, epi, 0, otag);
         return ok;
     }
 }
 
 // VS 0: int8 weights only; VS 1: int8 and f32.
-template <int VS>
+template <int VS, bool TAGS>
 __device__ __forceinline__ bool tk_gemv_dispatch(const TkPhase& T, int pos, const unsigned char* ring, int NS,
                                                  uint64_t* full, uint64_t* empty, int& j, int group, int gwarp,
                                                  int lane, int tid, float* red, float* part, int cta, int ncta,
                                                  unsigned long long* tr, float* vec, uint64_t* vbar,
-                                                 uint32_t& vphase, unsigned* amx) {
+                                                 uint32_t& vphase, unsigned* amx, unsigned itag, unsigned otag) {
     if (VS == 1 && T.variant >= TV_F32_K1_R8)
-        return tk_gemv<float>(T.g, T.unit, T.rs, T.rows, pos, ring, NS, full, empty, j, group, gwarp, lane, tid, red, part,
-                              cta, ncta, tr, vec, vbar, vphase, amx);
-    return tk_gemv<int8_t>(T.g, T.unit, T.rs, T.rows, pos, ring, NS, full, empty, j, group, gwarp, lane, tid, red, part, cta,
-                           ncta, tr, vec, vbar, vphase, amx);
+        return tk_gemv<float, TAGS>(T.g, T.unit, T.rs, T.rows, pos, ring, NS, full, empty, j, group, gwarp, lane, tid, red, part,
+                              cta, ncta, tr, vec, vbar, vphase, amx, itag, otag);
+    return tk_gemv<int8_t, TAGS>(T.g, T.unit, T.rs, T.rows, pos, ring, NS, full, empty, j, group, gwarp, lane, tid, red, part, cta,
+                           ncta, tr, vec, vbar, vphase, amx, itag, otag);
 }
 
 // --------------------------------------------------------------------- the kernel
-template <int VS>
+// VS: weight types compiled in (0 int8, 1 int8 and f32). TAGS: the phases meet
+// through (value, tag) words (one GPU; every TkPhase::nobar set by the host), or
+// at grid barriers over plain floats.
+template <int VS, bool TAGS>
 __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_constant__ TkParams P) {
     extern __shared__ __align__(128) unsigned char smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kTkFullOffset);   // [4 * NS]
@@ -801,6 +966,7 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
             mbar_init(&empty[s], kGemvGroupWarps);
         }
         mbar_init(vbar, 1);
+        mbar_init(reinterpret_cast<uint64_t*>(smem + kTkDbarOffset), 1);
         fence_mbar_init();
         *abort = 0;
         *amx = 0u;
@@ -814,10 +980,26 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
         if (warp == kGemvConsumerWarps && lane == 0) {
             int j = 0;
             bool ok = true;
+            // descriptors by bulk copy, one phase ahead ([2]: phase ph in ph & 1), so
+            // that the issue of a phase's first stages never waits for its descriptor
             TkPhase* pdesc = reinterpret_cast<TkPhase*>(smem + kTkDescOffset + 2 * kTkDescBytes);
+            uint64_t* dbar = reinterpret_cast<uint64_t*>(smem + kTkDbarOffset);
+            mbar_arrive_expect_tx(dbar, (uint32_t)sizeof(TkPhase));
+            bulk_g2s(pdesc, P.phases, (uint32_t)sizeof(TkPhase), dbar);
+            int dnext = 0;                                  // phase whose descriptor copy is in flight
             for (int ph = 0; ph < P.nphases && ok; ++ph) {
-                tk_copy_desc<16>(pdesc, P.phases + ph, 0, 1);
-                const TkPhase& T = *pdesc;
+                // timeline: [11] descriptor wait started, [12] done, [13] last stage issued
+                unsigned long long* ptr = P.trace ? P.trace + ((size_t)ph * ncta + cta) * kTkStamps : nullptr;
+                if (ptr) ptr[11] = globaltimer_ns();
+                if (!mbar_wait_bounded(dbar, (uint32_t)ph & 1u)) { ok = false; break; }
+                dnext = -1;
+                if (ph + 1 < P.nphases) {                   // its buffer held phase ph - 1's
+                    mbar_arrive_expect_tx(dbar, (uint32_t)sizeof(TkPhase));
+                    bulk_g2s(pdesc + ((ph + 1) & 1), P.phases + ph + 1, (uint32_t)sizeof(TkPhase), dbar);
+                    dnext = ph + 1;
+                }
+                if (ptr) ptr[12] = globaltimer_ns();
+                const TkPhase& T = pdesc[ph & 1];
                 if (T.kind == TK_GEMV) {
                     const GemvParams& p = T.g;
                     int r0, r1;
@@ -832,8 +1014,10 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
                 } else if (T.kind == TK_ATTN) {
                     ok = tk_attn_produce(T.a, pos + 1, cta, ncta, ring, NS, full, empty, j, P.inflight);
                 }
+                if (ptr) ptr[13] = globaltimer_ns();
             }
             if (!ok) set_err(err, B2_DEV_ERR_TIMEOUT);
+            if (dnext >= 0 && !mbar_wait_bounded(dbar, (uint32_t)dnext & 1u)) set_err(err, B2_DEV_ERR_TIMEOUT);
             for (int i = max(0, j - NS); i < j; ++i)        // no copy in flight at exit
                 if (!mbar_wait_bounded(tk_full(full, i, NS), tk_full_parity(i, NS))) {
                     set_err(err, B2_DEV_ERR_TIMEOUT);
@@ -857,17 +1041,29 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
     TkPhase* cdesc = reinterpret_cast<TkPhase*>(smem + kTkDescOffset);      // [2]: phase ph in ph & 1
     tk_copy_desc<1>(cdesc, P.phases, tid, kGemvConsumerThreads);
     consumer_bar();
+    const unsigned tbase = seq * 1024u + 1u;            // tag of phase ph: tbase + ph
     for (int ph = 0; ph < P.nphases; ++ph) {
         const TkPhase& T = cdesc[ph & 1];
         if (ph > 0) {
-            arrivals += (unsigned)ncta;
-            unsigned long long* trb = P.trace ? P.trace + ((size_t)ph * ncta + cta) * kTkStamps : nullptr;
-            if (!tk_grid_sync(P.bar, arrivals, tid, flag + 4 * (ph & 1), abort, &T.xsync, &P,
-                              seq * 1024u + (unsigned)ph, cta, trb)) {
-                if (tid == 0) *abort = 1;
-                break;
+            // every consumer thread meets here first: the descriptor of phase ph (copied
+            // by other threads during phase ph - 1) is complete only after this barrier,
+            // so T is read after it and every thread takes the same path below
+            consumer_bar();
+            if constexpr (TAGS) {
+                // the inputs are (value, tag) words: no grid barrier
+                if (*abort) break;
+            } else {
+                arrivals += (unsigned)ncta;
+                unsigned long long* trb = P.trace ? P.trace + ((size_t)ph * ncta + cta) * kTkStamps : nullptr;
+                if (!tk_grid_sync(P.bar, arrivals, tid, flag + 4 * (ph & 1), abort, &T.xsync, &P,
+                                  seq * 1024u + (unsigned)ph, cta, trb, true)) {
+                    if (tid == 0) *abort = 1;
+                    break;
+                }
             }
         }
+        const unsigned otag = tbase + (unsigned)ph;
+        const unsigned itag = tbase + (unsigned)T.tin;
         unsigned long long* tr = P.trace ? P.trace + ((size_t)ph * ncta + cta) * kTkStamps : nullptr;
         tk_stamp(tr, 0, tid);
         // the next phase's descriptor, by the last consumer warps (in place after the
@@ -890,18 +1086,22 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
                         v = reinterpret_cast<const float*>(e.emb)[(size_t)tok * e.ld + i];
                     }
                     if (e.pos_tab) v = fadd(v, e.pos_tab[(size_t)pos * e.d + i]);
-                    e.x[i] = v;
+                    if constexpr (TAGS) st_tag(e.tx + i, v, otag);
+                    else e.x[i] = v;
                 }
             }
         } else if (T.kind == TK_GEMV) {
-            ok = tk_gemv_dispatch<VS>(T, pos, ring, NS, full, empty, j, group, gwarp, lane, tid, red, part, cta,
-                                      ncta, tr, vec, vbar, vphase, amx);
+            ok = tk_gemv_dispatch<VS, TAGS>(T, pos, ring, NS, full, empty, j, group, gwarp, lane, tid, red, part, cta,
+                                      ncta, tr, vec, vbar, vphase, amx, itag, otag);
+            // this phase's generic writes of vec before the next phase's bulk copies into it
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         } else if (T.kind == TK_ACOMB) {
-            tk_attn_combine(T.a, pos, cta, ncta, tid);
+            ok = tk_attn_combine<TAGS>(T.a, pos, cta, ncta, tid, itag, otag);
         } else {
             tk_stamp(tr, 1, tid);
             tk_stamp(tr, 2, tid);
-            ok = tk_attn_consume(T.a, pos, cta, ncta, ring, NS, full, empty, j, group, gwarp, lane, gscr, gflag, tr);
+            ok = tk_attn_consume<TAGS>(T.a, pos, cta, ncta, ring, NS, full, empty, j, group, gwarp, lane, gscr, gflag, tr,
+                                 itag, otag);
             if (tr) {
                 consumer_bar();
                 tk_stamp(tr, 3, tid);
@@ -942,8 +1142,8 @@ __global__ void __launch_bounds__(kTkThreads, 1) token_kernel(const __grid_const
 }
 
 // Host side (token.cu, where the kernel is instantiated): set the dynamic shared
-// memory of variant set vs and report how many CTAs fit an SM; launch one step.
-cudaError_t tk_prepare(int vs, size_t smem, int* per_sm);
-cudaError_t tk_launch(int vs, const cudaLaunchConfig_t& cfg, const TkParams& P);
+// memory of variant (vs, tags) and report how many CTAs fit an SM; launch one step.
+cudaError_t tk_prepare(int vs, bool tags, size_t smem, int* per_sm);
+cudaError_t tk_launch(int vs, bool tags, const cudaLaunchConfig_t& cfg, const TkParams& P);
 
 }  // namespace b2

@@ -177,7 +177,9 @@ int b2_read_output(b2_ctx* ctx, int32_t* ids, int max_ids, int* n_ids);
 int b2_set_stream(b2_ctx* ctx, void* stream);
 
 /* Numeric properties: "weight_bytes", "kv_bytes_per_pos", "kernels_per_step",
- * "max_seq", "vocab", "position", "n_out", "device_err", "sm_count". */
+ * "max_seq", "vocab", "position", "n_out", "device_err", "sm_count",
+ * "token_kernel" (1: one persistent launch per step), "token_tags" (1: its phases
+ * meet through tagged words instead of grid barriers), "prefill_batched". */
 int b2_query(b2_ctx* ctx, const char* key, double* value);
 
 /* Last error message of ctx (or of the last failed create when ctx is NULL). */

@@ -88,3 +88,35 @@ def test_token_kernel_full_size_llama2_7b_equals_per_layer_kernels(pkg):
         dec.close()
     for a, b in zip(*outs):
         assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("name", ["tiny-llama", "gpt2-small"])
+def test_token_kernel_tagged_words_and_grid_barriers_agree(pkg, oracle, name):
+    """On one GPU the phases meet through (value, tag) words; B2_TK_TAGS=0 makes
+    them meet at grid barriers instead (the tensor-parallel mode). Both give the
+    oracle's bits."""
+    plan = pkg.synth.config_plan(name, n_layers=2)
+    old = os.environ.get("B2_TK_TAGS")
+    try:
+        os.environ.pop("B2_TK_TAGS", None)
+        tagged = pkg.runtime.Decoder.synthetic(plan, seed=3)
+        os.environ["B2_TK_TAGS"] = "0"
+        barrier = pkg.runtime.Decoder.synthetic(plan, seed=3)
+    finally:
+        if old is None:
+            os.environ.pop("B2_TK_TAGS", None)
+        else:
+            os.environ["B2_TK_TAGS"] = old
+    assert tagged.query("token_kernel") == 1 and tagged.query("token_tags") == 1
+    assert barrier.query("token_kernel") == 1 and barrier.query("token_tags") == 0
+    om = oracle.OracleModel(plan, oracle.synth_tensors(plan, seed=3), threads=8)
+    n = min(plan["max_seq"], 70)             # crosses a 64-key split boundary where max_seq allows
+    ids = np.random.default_rng(11).integers(0, plan["vocab"], n).tolist()
+    for t in ids:
+        r_tok, r_log = om.step(t)
+        for dec in (tagged, barrier):
+            tok, log = dec.step(t, want_logits=True)
+            assert tok == r_tok
+            assert np.array_equal(log, r_log)
+    tagged.close()
+    barrier.close()

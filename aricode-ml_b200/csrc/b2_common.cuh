@@ -203,13 +203,14 @@ __device__ __forceinline__ void st_tag(unsigned long long* p, float v, unsigned 
     const unsigned long long w = (unsigned long long)__float_as_uint(v) | ((unsigned long long)tag << 32);
     asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
+// system scope: the words may come from a peer GPU's stores (tensor parallelism)
 __device__ __forceinline__ unsigned long long ld_tag(const unsigned long long* p) {
     unsigned long long w;
-    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
     return w;
 }
 __device__ __forceinline__ void ld_tag2(const unsigned long long* p, unsigned long long& a, unsigned long long& b) {
-    asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+    asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
 }
 __device__ __forceinline__ bool tag_ok(unsigned long long w, unsigned tag) { return (unsigned)(w >> 32) == tag; }
 __device__ __forceinline__ float tag_val(unsigned long long w) { return __uint_as_float((unsigned)w); }
@@ -283,6 +284,20 @@ template <typename T>
 __device__ __forceinline__ void mirror_store(const Mirror& m, T* p, T v) {
     *p = v;
     for (int i = 0; i < m.n; ++i) *reinterpret_cast<T*>(reinterpret_cast<char*>(p) + m.delta[i]) = v;
+}
+
+// a (value, tag) word here and in every peer's copy of the buffer (system scope:
+// the peers read them)
+__device__ __forceinline__ void mirror_st_tag(const Mirror& m, unsigned long long* p, float v, unsigned tag) {
+    const unsigned long long w = (unsigned long long)__float_as_uint(v) | ((unsigned long long)tag << 32);
+    if (m.n == 0) {
+        asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+        return;
+    }
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+    for (int i = 0; i < m.n; ++i)
+        asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(reinterpret_cast<char*>(p) + m.delta[i]), "l"(w)
+                     : "memory");
 }
 
 __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {

@@ -856,7 +856,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, int r0, int r
             const float su = pre(rl) ? epi[rl * 4 + 1] : p.S[1][lrow];
             const float g = fmul(dotv(rl, 0), sg);
             const float u = fmul(dotv(rl, 1), su);
-            if (p.ty) st_tag(p.ty + lrow, fmul(silu_f(g), u), otag);
+            if (p.ty) mirror_st_tag(p.mir, p.ty + lrow, fmul(silu_f(g), u), otag);
             else mirror_store(p.mir, p.y + lrow, fmul(silu_f(g), u));
             continue;
         }
@@ -898,10 +898,10 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, int r0, int r
         } else if (p.epi == EPI_RESID) {
             const float r = pre(rl) ? epi[rl * 4 + 2]
                                     : (p.tresid ? tag_val(ld_tag(p.tresid + row)) : __ldcg(p.resid + row));
-            if (p.ty) st_tag(p.ty + row, fadd(val[0], r), otag);
+            if (p.ty) mirror_st_tag(p.mir, p.ty + row, fadd(val[0], r), otag);
             else mirror_store(p.mir, p.y + row, fadd(val[0], r));
         } else if (p.epi == EPI_GELU) {
-            if (p.ty) st_tag(p.ty + row, gelu_f(val[0]), otag);
+            if (p.ty) mirror_st_tag(p.mir, p.ty + row, gelu_f(val[0]), otag);
             else mirror_store(p.mir, p.y + row, gelu_f(val[0]));
         } else if (p.epi == EPI_ARGMAX) {
             if (p.y) p.y[row] = val[0];
@@ -910,7 +910,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvParams& p, int r0, int r
                 best_v = val[0]; best_i = row + p.row_base; have_best = true;
             }
         } else {
-            if (p.ty) st_tag(p.ty + row, val[0], otag);
+            if (p.ty) mirror_st_tag(p.mir, p.ty + row, val[0], otag);
             else mirror_store(p.mir, p.y + row, val[0]);
         }
     }

@@ -537,10 +537,7 @@ void assemble(b2_ctx* c, const b2json::Value& plan) {
     const size_t i_prompt = add((size_t)c->max_seq * 4);
     const size_t i_out = add((size_t)c->max_seq * 4);
     const size_t i_samp = add((size_t)c->vocab * 8);
-    const size_t i_tx = add((size_t)c->d * 8);
     const size_t i_tq = add((size_t)max_q * 8);
-    const size_t i_tatt = add((size_t)max_q_all * 8);
-    const size_t i_tf = add((size_t)max_ffn * 8);
     const size_t i_tkn = add((size_t)max_KVH * max_dh * 8);
     const size_t i_tvn = add((size_t)max_KVH * max_dh * 8);
     c->work_bytes = off;
@@ -557,7 +554,9 @@ void assemble(b2_ctx* c, const b2json::Value& plan) {
         auto xadd = [&](size_t bytes) { const size_t o = xo; xo += al(bytes); return o; };
         const size_t o_x = xadd((size_t)c->d * 4), o_att = xadd((size_t)max_q_all * 4),
                      o_f = xadd((size_t)max_ffn * 4), o_fl = xadd(kMaxRanks * 4), o_afl = xadd(kMaxRanks * 4),
-                     o_cv = xadd(kMaxRanks * 4), o_ci = xadd(kMaxRanks * 4), o_cn = xadd(kMaxRanks * 4);
+                     o_cv = xadd(kMaxRanks * 4), o_ci = xadd(kMaxRanks * 4), o_cn = xadd(kMaxRanks * 4),
+                     o_tx = xadd((size_t)c->d * 8), o_tatt = xadd((size_t)max_q_all * 8),
+                     o_tf = xadd((size_t)max_ffn * 8);
         c->xch_bytes = xo;
         if (cudaMalloc(&c->d_xch, c->xch_bytes) != cudaSuccess) throw Err(B2_E_OOM, "exchange buffer allocation failed");
         CK(cudaMemsetAsync(c->d_xch, 0, c->xch_bytes, c->stream));
@@ -570,6 +569,11 @@ void assemble(b2_ctx* c, const b2json::Value& plan) {
         c->tp_cval = reinterpret_cast<float*>(xb + o_cv);
         c->tp_cidx = reinterpret_cast<int*>(xb + o_ci);
         c->tp_cnan = reinterpret_cast<int*>(xb + o_cn);
+        // the token kernel's tagged x, attention output and FFN hidden vector: with
+        // tensor parallelism the peers write their rows here
+        c->tx = reinterpret_cast<unsigned long long*>(xb + o_tx);
+        c->tatt = reinterpret_cast<unsigned long long*>(xb + o_tatt);
+        c->tf = reinterpret_cast<unsigned long long*>(xb + o_tf);
     }
     c->logits = reinterpret_cast<float*>(w + offs[i_logits]);
     c->attn_part = reinterpret_cast<float*>(w + offs[i_part]);
@@ -584,10 +588,7 @@ void assemble(b2_ctx* c, const b2json::Value& plan) {
     c->prompt = reinterpret_cast<int*>(w + offs[i_prompt]);
     c->out_ids = reinterpret_cast<int*>(w + offs[i_out]);
     c->samp_e = reinterpret_cast<double*>(w + offs[i_samp]);
-    c->tx = reinterpret_cast<unsigned long long*>(w + offs[i_tx]);
     c->tq = reinterpret_cast<unsigned long long*>(w + offs[i_tq]);
-    c->tatt = reinterpret_cast<unsigned long long*>(w + offs[i_tatt]);
-    c->tf = reinterpret_cast<unsigned long long*>(w + offs[i_tf]);
     c->tkn = reinterpret_cast<unsigned long long*>(w + offs[i_tkn]);
     c->tvn = reinterpret_cast<unsigned long long*>(w + offs[i_tvn]);
 
@@ -842,8 +843,8 @@ bool tk_phase_of(const b2_ctx* c, const Op& o, TkPhase& T, size_t& part_bytes, s
     return true;
 }
 
-// One GPU: let the phases of a table meet through (value, tag) words instead of
-// grid barriers. Every activation a phase reads from this launch gets its tagged
+// Let the phases of a table meet through (value, tag) words instead of grid
+// barriers. Every activation a phase reads from this launch gets its tagged
 // twin and the index of the phase that wrote it; false (table unchanged in its
 // meaning) when some input has no twin.
 bool tk_tag_table(b2_ctx* c, std::vector<TkPhase>& ph, size_t first, size_t count) {
@@ -940,11 +941,11 @@ void setup_token(b2_ctx* c) {
         c->token_why = "more than 1023 phases (phase tags)";
         return;
     }
-    // one GPU: tagged words between phases instead of grid barriers (tensor
-    // parallelism keeps the barriers, which also wait for the peers)
+    // tagged words between phases instead of grid barriers (with tensor
+    // parallelism the peers' rows arrive as tagged words too, no cross-rank barrier)
     c->tk_tags = false;
     const char* tg = std::getenv("B2_TK_TAGS");
-    if (c->tp_size == 1 && !(tg && tg[0] == '0')) {
+    if (!(tg && tg[0] == '0')) {
         std::vector<TkPhase> tagged = ph;
         if (tk_tag_table(c, tagged, 0, (size_t)c->nph_prefill) &&
             tk_tag_table(c, tagged, (size_t)c->nph_prefill, (size_t)c->nph_decode)) {

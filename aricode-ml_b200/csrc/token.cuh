@@ -616,7 +616,7 @@ __device__ __forceinline__ bool tk_attn_combine(const AttnParams& a, int pos, in
             }
         }
         if (n < a.max_seq) l = ffma((float)(a.max_seq - n), exp_f(fsub(-60.0f, M)), l);
-        if constexpr (TAGS) st_tag(a.tout + idx, fdiv(o, l), otag);
+        if constexpr (TAGS) mirror_st_tag(a.mir, a.tout + idx, fdiv(o, l), otag);
         else mirror_store(a.mir, a.out + idx, fdiv(o, l));
     }
     return ok;

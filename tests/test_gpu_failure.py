@@ -1,5 +1,5 @@
 """Failure detection without a GPU fault: a tensor-parallel rank that stops taking
-part makes the other rank's bounded cross-rank wait run out; that rank's call
+part makes the other rank's bounded wait for its rows run out; that rank's call
 returns B2_E_DEVICE (about a second later) instead of hanging, and its context
 can still be destroyed. Rank 1 launches nothing, so both ranks can share one GPU;
 NVLS is not involved (plain peer stores over CUDA IPC)."""

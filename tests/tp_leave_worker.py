@@ -7,9 +7,10 @@ a step:
 Both ranks create their share of a 2-rank tensor-parallel tiny Llama and connect
 (exchange buffers over CUDA IPC). Rank 1 then stops taking part: it launches
 nothing and only waits, alive (its buffer stays valid), until rank 0 is done.
-Rank 0 runs one step; the step's first cross-rank barrier waits for rank 1's
-epoch, which never comes, gives up after its bounded wait, and the call returns
-B2_E_DEVICE. Rank 0 then destroys its context cleanly and records the outcome.
+Rank 0 runs one step; the first phase that needs rank 1's rows (the attention
+output of rank 1's heads) waits for rank 1's tagged words, which never come, gives
+up after its bounded wait, and the call returns B2_E_DEVICE. Rank 0 then destroys
+its context cleanly and records the outcome.
 """
 import datetime
 import importlib

@@ -394,20 +394,38 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
                 wk[i] = (has_new && d < dh) ? ld_tag(tkn + d) : 0ull;
             }
             if (has_new && gt < dh) wv = ld_tag(tvn + gt);
-            bool okt = true;
+            // the late words, all loaded again together until every tag is the phase's
+            unsigned late = 0;                          // bits 0-3 q, 4-7 K row, 8 V row
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const int d = lane + 32 * i;
-                if (d < dh) okt = tag_wait(a.tq + (size_t)h * dh + d, itag, wq[i], deadline) && okt;
-                if (has_new && d < dh) okt = tag_wait(tkn + d, itag, wk[i], deadline) && okt;
+                if (d < dh && !tag_ok(wq[i], itag)) late |= 1u << i;
+                if (has_new && d < dh && !tag_ok(wk[i], itag)) late |= 16u << i;
+            }
+            if (has_new && gt < dh && !tag_ok(wv, itag)) late |= 256u;
+            while (late) {
+                if (globaltimer_ns() > deadline) { tagbad = true; break; }   // values unusable; the CTA aborts after the phase
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int d = lane + 32 * i;
+                    if (late & (1u << i)) wq[i] = ld_tag(a.tq + (size_t)h * dh + d);
+                    if (late & (16u << i)) wk[i] = ld_tag(tkn + d);
+                }
+                if (late & 256u) wv = ld_tag(tvn + gt);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    if ((late & (1u << i)) && tag_ok(wq[i], itag)) late &= ~(1u << i);
+                    if ((late & (16u << i)) && tag_ok(wk[i], itag)) late &= ~(16u << i);
+                }
+                if ((late & 256u) && tag_ok(wv, itag)) late &= ~256u;
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int d = lane + 32 * i;
                 qv[i] = d < dh ? tag_val(wq[i]) : 0.0f;
                 kn[i] = (has_new && d < dh) ? tag_val(wk[i]) : 0.0f;
             }
-            if (has_new && gt < dh) {
-                okt = tag_wait(tvn + gt, itag, wv, deadline) && okt;
-                vn = tag_val(wv);
-            }
-            if (!okt) tagbad = true;                    // values unusable; the CTA aborts after the phase
+            if (has_new && gt < dh) vn = tag_val(wv);
         } else {
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -524,16 +542,25 @@ __device__ __forceinline__ bool tk_attn_combine(const AttnParams& a, int pos, in
             M = 0.0f;
             for (int t0 = 0; t0 < nsplit; t0 += 8) {
                 unsigned long long wm[8];
+                unsigned late = 0;
 #pragma unroll
                 for (int u = 0; u < 8; ++u)
                     wm[u] = t0 + u < nsplit ? ld_tag(tb + (size_t)(t0 + u) * stride + dh) : 0ull;
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    if (t0 + u < nsplit) {
-                        ok = tag_wait(tb + (size_t)(t0 + u) * stride + dh, itag, wm[u], deadline) && ok;
-                        M = (t0 + u == 0) ? tag_val(wm[u]) : fmaxf(M, tag_val(wm[u]));
-                    }
+                for (int u = 0; u < 8; ++u)
+                    if (t0 + u < nsplit && !tag_ok(wm[u], itag)) late |= 1u << u;
+                while (late) {                          // late words loaded again together
+                    if (globaltimer_ns() > deadline) { ok = false; break; }
+#pragma unroll
+                    for (int u = 0; u < 8; ++u)
+                        if (late & (1u << u)) wm[u] = ld_tag(tb + (size_t)(t0 + u) * stride + dh);
+#pragma unroll
+                    for (int u = 0; u < 8; ++u)
+                        if ((late & (1u << u)) && tag_ok(wm[u], itag)) late &= ~(1u << u);
                 }
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    if (t0 + u < nsplit) M = (t0 + u == 0) ? tag_val(wm[u]) : fmaxf(M, tag_val(wm[u]));
             }
             if (n < a.max_seq) M = fmaxf(M, -60.0f);
             for (int t0 = 0; t0 < nsplit; t0 += 8) {
@@ -546,13 +573,30 @@ __device__ __forceinline__ bool tk_attn_combine(const AttnParams& a, int pos, in
                     wl[u] = in ? ld_tag(pt + dh + 1) : 0ull;
                     wo[u] = in ? ld_tag(pt + d) : 0ull;
                 }
+                unsigned late = 0;                      // (normally none: m was complete above)
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    if (t0 + u < nsplit && !(tag_ok(wm[u], itag) && tag_ok(wl[u], itag) && tag_ok(wo[u], itag)))
+                        late |= 1u << u;
+                while (late) {
+                    if (globaltimer_ns() > deadline) { ok = false; break; }
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        if (late & (1u << u)) {
+                            const unsigned long long* pt = tb + (size_t)(t0 + u) * stride;
+                            wm[u] = ld_tag(pt + dh);
+                            wl[u] = ld_tag(pt + dh + 1);
+                            wo[u] = ld_tag(pt + d);
+                        }
+                    }
+#pragma unroll
+                    for (int u = 0; u < 8; ++u)
+                        if ((late & (1u << u)) && tag_ok(wm[u], itag) && tag_ok(wl[u], itag) && tag_ok(wo[u], itag))
+                            late &= ~(1u << u);
+                }
 #pragma unroll
                 for (int u = 0; u < 8; ++u) {
                     if (t0 + u < nsplit) {
-                        const unsigned long long* pt = tb + (size_t)(t0 + u) * stride;
-                        ok = tag_wait(pt + dh, itag, wm[u], deadline) && ok;
-                        ok = tag_wait(pt + dh + 1, itag, wl[u], deadline) && ok;
-                        ok = tag_wait(pt + d, itag, wo[u], deadline) && ok;
                         const float w = exp_f(fsub(tag_val(wm[u]), M));
                         l = ffma(tag_val(wl[u]), w, l);
                         o = ffma(tag_val(wo[u]), w, o);
@@ -749,50 +793,43 @@ __device__ __forceinline__ bool tk_gemv_consume_i8(const GemvParams& p, int r0, 
 // in shared memory (vec: x at [0, L), gains at [L, 2L), LN bias at [2L, 3L) with
 // L = n rounded up to 16, zeros in [n, L)), normalised in place, and read by the
 // stages from there.
-// x as (value, tag) words -> vec[0, n), every word waited for (bounded): one
-// round of loads, all in flight together; the words not yet written are then
-// polled one by one (a slow path with its own deadline). Thread t owns the word
-// pairs t, t + 512, ... in both passes.
-__device__ __forceinline__ bool tk_poll_tagged(const unsigned long long* tx, int n, unsigned tag, float* vec, int tid) {
-    const uint64_t deadline = globaltimer_ns() + kWaitLimitNs;
-    bool ok = true;
-    for (int q = tid; q < (n >> 1); q += kGemvConsumerThreads) {  // this thread's pairs, as loaded
-        for (int i = 2 * q; i < 2 * q + 2; ++i) {
-            if (__float_as_uint(vec[i]) != 0xffffffffu) continue;  // marked: not yet written
-            unsigned long long w = ld_tag(tx + i);
-            ok = tag_wait(tx + i, tag, w, deadline) && ok;
-            vec[i] = tag_val(w);
-        }
-    }
-    return ok;
-}
-
+// x as (value, tag) words -> vec[0, n), every word waited for (bounded). Thread t
+// owns the word pairs t, t + 512, ..., taken U pairs at a time: their loads are in
+// flight together, and while some are not yet the phase's, all of those are
+// loaded again together (one round trip per round, not one per late word).
 __device__ __forceinline__ bool tk_load_tagged(const unsigned long long* tx, int n, unsigned tag, float* vec, int tid) {
     constexpr int U = 4;                                // word pairs per thread per round
     const int npair = n >> 1;                           // n is a multiple of 4
-    bool miss = false;
+    bool ok = true;
+    uint64_t deadline = 0;
     for (int q0 = tid; q0 < npair; q0 += U * kGemvConsumerThreads) {
         unsigned long long a[U], b[U];
+        unsigned late = 0;                              // bit u: pair u is not complete yet
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int q = q0 + u * kGemvConsumerThreads;
             if (q < npair) ld_tag2(tx + 2 * q, a[u], b[u]);
         }
 #pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (q0 + u * kGemvConsumerThreads < npair && !(tag_ok(a[u], tag) && tag_ok(b[u], tag))) late |= 1u << u;
+        while (late) {
+            if (deadline == 0) deadline = globaltimer_ns() + kWaitLimitNs;
+            else if (globaltimer_ns() > deadline) { ok = false; break; }
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+                if (late & (1u << u)) ld_tag2(tx + 2 * (q0 + u * kGemvConsumerThreads), a[u], b[u]);
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+                if ((late & (1u << u)) && tag_ok(a[u], tag) && tag_ok(b[u], tag)) late &= ~(1u << u);
+        }
+#pragma unroll
         for (int u = 0; u < U; ++u) {
             const int q = q0 + u * kGemvConsumerThreads;
-            if (q < npair) {
-                // a word whose tag is not the phase's yet is marked with an all-ones
-                // pattern; the slow path re-reads every marked word (a value that has
-                // the pattern itself is read again and kept)
-                const bool oa = tag_ok(a[u], tag), ob = tag_ok(b[u], tag);
-                miss = miss || !oa || !ob;
-                *reinterpret_cast<float2*>(vec + 2 * q) =
-                    make_float2(oa ? tag_val(a[u]) : __uint_as_float(0xffffffffu), ob ? tag_val(b[u]) : __uint_as_float(0xffffffffu));
-            }
+            if (q < npair) *reinterpret_cast<float2*>(vec + 2 * q) = make_float2(tag_val(a[u]), tag_val(b[u]));
         }
     }
-    return miss ? tk_poll_tagged(tx, n, tag, vec, tid) : true;
+    return ok;
 }
 
 template <typename WT, bool TAGS>

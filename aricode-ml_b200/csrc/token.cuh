@@ -866,15 +866,12 @@ __device__ __forceinline__ bool tk_gemv(const GemvParams& p, int unit, int rs, i
         for (int i = tid; i < (r1 - r0) * nm * 4; i += kGemvConsumerThreads) reinterpret_cast<int*>(part)[i] = 0;
     bool ok = true;
     if constexpr (tagged) {
-        // the epilogue inputs first (parked in shared memory, so that nothing stays in
-        // registers across the input loads), then x word by word
-        {
-            const EpiRow er = paired ? gemv_epi_load<ESZ, true>(p, r0, r1, pos, tid)
-                                     : gemv_epi_load<ESZ, false>(p, r0, r1, pos, tid);
-            gemv_epi_store(er, r1 - r0, tid, epi);
-        }
+        // the epilogue inputs and x word by word, their loads in flight together
+        const EpiRow er = paired ? gemv_epi_load<ESZ, true>(p, r0, r1, pos, tid)
+                                 : gemv_epi_load<ESZ, false>(p, r0, r1, pos, tid);
         ok = tk_load_tagged(p.tx, n, itag, vec, tid);
-        consumer_bar();                                 // vec[0, n) complete
+        gemv_epi_store(er, r1 - r0, tid, epi);
+        consumer_bar();                                 // vec[0, n) and epi[] complete
         if (bulk) {
             ok = mbar_wait_bounded(vbar, vphase & 1) && ok;
             ++vphase;

@@ -15,8 +15,7 @@
 //                  ring); it also prefetches each
 //                  phase's small vectors (norm gains, scales, biases) into L2;
 //   warpgroups 0-3 consumers in two groups of 8 warps; stage j belongs to group
-//                  j & 1 in GEMV phases and to group (j / 2) & 1 in attention
-//                  phases (an item's K stage and V stage go to the same group);
+//                  j & 1 (GEMV stages, and the V chunk of an attention item);
 //                  four full barriers per slot keep this exact for any slot count
 //                  (tk_full);
 //                  between phases, on one GPU: a consumer barrier only. Every
@@ -36,10 +35,11 @@
 //             stages, epilogue (residual, RoPE + KV append, SiLU*up, GELU, argmax);
 //             int8 rows as the exact fixed-point dot of gemv_stage_i8;
 //   TK_ATTN   split-KV decode attention: item (query head h, 64-key split s) on
-//             CTA item % grid; the K chunk and V chunk arrive as two ring
-//             stages; the row of the current position (written by this step's
-//             Q/K/V phase) is read from global memory; each item writes its
-//             split's (o_s, m_s, l_s);
+//             CTA item % grid; the V chunk arrives as a ring stage, the K chunk
+//             is read straight from memory (the producer requests it into L2
+//             first), so that all of a CTA's items are in flight at once; the
+//             row of the current position comes from this step's Q/K/V phase;
+//             each item writes its split's (o_s, m_s, l_s);
 //   TK_ACOMB  after the grid barrier, the outputs (h, d) spread over the CTAs,
 //             each merging head h's splits with the -60 tail (a separate phase:
 //             no split waits for another, so no CTA's tail waits on the slowest
@@ -182,7 +182,7 @@ __device__ __forceinline__ void group_bar(int group) {
 
 // Ring stage j: slot j % NS, round j / NS. Its "full" barrier is one of four per
 // slot (round % 4), waited with parity (round / 4) & 1. A stage belongs to one
-// consumer group (GEMV: j & 1; attention: (j / 2) & 1 for an item's two stages),
+// consumer group, j & 1 (a GEMV stage, or an attention item's V chunk),
 // and for any slot count the stages j and j + 4 NS that share a barrier belong
 // to the same group: each barrier's phases are waited in order by one group, so
 // a parity wait never mistakes an earlier phase. The empty barrier (one per slot,
@@ -311,31 +311,29 @@ __device__ __forceinline__ int tk_attn_items(const AttnParams& a, int n, int& ns
     return a.H * nsplit;
 }
 
-// producer side: a padding stage keeps every item's K stage on an even index
+// producer side: the K chunks of this CTA's items are requested into L2 (the
+// consumers read them with plain loads), then one ring stage per item carries
+// its V chunk, so that every item's V is in flight at once
 __device__ __forceinline__ bool tk_attn_produce(const AttnParams& a, int n, int cta, int ncta,
                                                 unsigned char* ring, int NS, uint64_t* full, uint64_t* empty,
                                                 int& j, int inflight) {
     int nsplit;
     const int items = tk_attn_items(a, n, nsplit);
     const int G = a.H / a.KVH, dh = a.dh;
-    if (j & 1) {
-        uint64_t* bar = tk_issue_wait(full, empty, NS, j, 0);
-        if (!bar) return false;
-        mbar_arrive(bar);
-        ++j;
+    for (int it = cta; it < items; it += ncta) {
+        const int h = it / nsplit, s = it % nsplit, kvh = h / G;
+        const int j0 = s * kAttnChunk, len = min(kAttnChunk, n - j0);
+        bulk_prefetch_l2(a.K + ((size_t)kvh * a.max_seq + j0) * dh, (uint32_t)len * dh * 4);
     }
     for (int it = cta; it < items; it += ncta) {
         const int h = it / nsplit, s = it % nsplit, kvh = h / G;
         const int j0 = s * kAttnChunk, len = min(kAttnChunk, n - j0);
         const uint32_t bytes = (uint32_t)len * dh * 4;
-        const size_t off = ((size_t)kvh * a.max_seq + j0) * dh;
-        for (int kv = 0; kv < 2; ++kv) {
-            uint64_t* bar = tk_issue_wait(full, empty, NS, j, inflight);
-            if (!bar) return false;
-            mbar_arrive_expect_tx(bar, bytes);
-            bulk_g2s(ring + (size_t)(j % NS) * kTkSlotBytes, (kv ? a.V : a.K) + off, bytes, bar);
-            ++j;
-        }
+        uint64_t* bar = tk_issue_wait(full, empty, NS, j, inflight);
+        if (!bar) return false;
+        mbar_arrive_expect_tx(bar, bytes);
+        bulk_g2s(ring + (size_t)(j % NS) * kTkSlotBytes, a.V + ((size_t)kvh * a.max_seq + j0) * dh, bytes, bar);
+        ++j;
     }
     return true;
 }
@@ -358,20 +356,14 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
     const int items = tk_attn_items(a, n, nsplit);
     const int G = a.H / a.KVH, dh = a.dh;
     const int gt = gwarp * 32 + lane;                   // thread index within the group
-    if (j & 1) {                                        // padding stage (owner j & 1)
-        if ((j & 1) == group) {
-            if (!group_wait(tk_full(full, j, NS), tk_full_parity(j, NS), group, gt, gflag)) return false;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[j % NS]);
-        }
-        ++j;
-    }
     float* sc = scr;                  // [64] scores, then exp
     float* ml = scr + 64;             // m, l
     bool tagbad = false;
-    for (int it = cta; it < items; it += ncta, j += 2) {
-        const int slotk = j % NS, slotv = (j + 1) % NS;
-        if (((j >> 1) & 1) != group) continue;
+    // item k of this CTA: its V chunk is ring stage j, taken by group j & 1 (as in
+    // the GEMV phases); its K chunk is read from global memory (L2, prefetched)
+    for (int it = cta; it < items; it += ncta, ++j) {
+        const int slotv = j % NS;
+        if ((j & 1) != group) continue;
         const int h = it / nsplit, s = it % nsplit, kvh = h / G;
         const int j0 = s * kAttnChunk, len = min(kAttnChunk, n - j0);
         const int jnew = pos - j0;                      // this step's row, if in the chunk
@@ -435,11 +427,20 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
             }
             vn = (has_new && gt < dh) ? __ldcg(vnew + gt) : 0.0f;
         }
-        unsigned long long tw = stamp ? globaltimer_ns() : 0ull;
-        if (!group_wait(tk_full(full, j, NS), tk_full_parity(j, NS), group, gt, gflag)) return false;
-        if (stamp) wstage += globaltimer_ns() - tw;
-        const float* Ks = reinterpret_cast<const float*>(ring + (size_t)slotk * kTkSlotBytes);
         // scores: warp gwarp takes keys gwarp + 8 i; lane L sums d = L, L + 32, ...
+        // (the chunk's earlier rows, written by earlier steps, straight from memory;
+        // this step's row from the Q/K/V phase's words)
+        const float* Kg = a.K + ((size_t)kvh * a.max_seq + j0) * dh;
+        float kk[8][4];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int jj = gwarp + 8 * i;
+#pragma unroll
+            for (int ii = 0; ii < 4; ++ii) {
+                const int d = lane + 32 * ii;
+                kk[i][ii] = (jj < len && jj != jnew && d < dh) ? __ldcg(Kg + (size_t)jj * dh + d) : 0.0f;
+            }
+        }
         float v[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -447,11 +448,10 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
             float acc = 0.0f;
             if (jj < len) {
                 const bool fresh = jj == jnew;
-                const float* kr = Ks + jj * dh;
 #pragma unroll
                 for (int ii = 0; ii < 4; ++ii) {
                     const int d = lane + 32 * ii;
-                    if (d < dh) acc = ffma(qv[ii], fresh ? kn[ii] : kr[d], acc);
+                    if (d < dh) acc = ffma(qv[ii], fresh ? kn[ii] : kk[i][ii], acc);
                 }
             }
             v[i] = acc;
@@ -461,8 +461,6 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
             const int jj = gwarp + 8 * (lane >> 2);
             if (jj < len) sc[jj] = v[0];
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slotk]);
         group_bar(group);
         if (gwarp == 0) {                               // chunk max, exp, chunk sum
             float m = -__int_as_float(0x7f800000);
@@ -488,8 +486,8 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
         }
         group_bar(group);
         // o_s[d] = sum_j e_j V[j][d], j ascending (one thread per d)
-        tw = stamp ? globaltimer_ns() : 0ull;
-        if (!group_wait(tk_full(full, j + 1, NS), tk_full_parity(j + 1, NS), group, gt, gflag)) return false;
+        const unsigned long long tw = stamp ? globaltimer_ns() : 0ull;
+        if (!group_wait(tk_full(full, j, NS), tk_full_parity(j, NS), group, gt, gflag)) return false;
         if (stamp) wstage += globaltimer_ns() - tw;
         const float* Vs = reinterpret_cast<const float*>(ring + (size_t)slotv * kTkSlotBytes);
         const int stride = dh + 2;

@@ -36,8 +36,8 @@
 //             int8 rows as the exact fixed-point dot of gemv_stage_i8;
 //   TK_ATTN   split-KV decode attention: item (query head h, 64-key split s) on
 //             CTA item % grid; the V chunk arrives as a ring stage, the K chunk
-//             is read straight from memory (the producer requests it into L2
-//             first), so that all of a CTA's items are in flight at once; the
+//             is read straight from memory with plain loads, so that all of a
+//             CTA's items are in flight at once; the
 //             row of the current position comes from this step's Q/K/V phase;
 //             each item writes its split's (o_s, m_s, l_s);
 //   TK_ACOMB  after the grid barrier, the outputs (h, d) spread over the CTAs,
@@ -311,20 +311,15 @@ __device__ __forceinline__ int tk_attn_items(const AttnParams& a, int n, int& ns
     return a.H * nsplit;
 }
 
-// producer side: the K chunks of this CTA's items are requested into L2 (the
-// consumers read them with plain loads), then one ring stage per item carries
-// its V chunk, so that every item's V is in flight at once
+// producer side: one ring stage per item carries its V chunk, so that every
+// item's V is in flight at once (the consumers read the K chunks with plain
+// loads; requesting them into L2 first measured no faster)
 __device__ __forceinline__ bool tk_attn_produce(const AttnParams& a, int n, int cta, int ncta,
                                                 unsigned char* ring, int NS, uint64_t* full, uint64_t* empty,
                                                 int& j, int inflight) {
     int nsplit;
     const int items = tk_attn_items(a, n, nsplit);
     const int G = a.H / a.KVH, dh = a.dh;
-    for (int it = cta; it < items; it += ncta) {
-        const int h = it / nsplit, s = it % nsplit, kvh = h / G;
-        const int j0 = s * kAttnChunk, len = min(kAttnChunk, n - j0);
-        bulk_prefetch_l2(a.K + ((size_t)kvh * a.max_seq + j0) * dh, (uint32_t)len * dh * 4);
-    }
     for (int it = cta; it < items; it += ncta) {
         const int h = it / nsplit, s = it % nsplit, kvh = h / G;
         const int j0 = s * kAttnChunk, len = min(kAttnChunk, n - j0);
@@ -360,7 +355,7 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
     float* ml = scr + 64;             // m, l
     bool tagbad = false;
     // item k of this CTA: its V chunk is ring stage j, taken by group j & 1 (as in
-    // the GEMV phases); its K chunk is read from global memory (L2, prefetched)
+    // the GEMV phases); its K chunk is read from global memory
     for (int it = cta; it < items; it += ncta, ++j) {
         const int slotv = j % NS;
         if ((j & 1) != group) continue;
@@ -870,6 +865,7 @@ __device__ __forceinline__ bool tk_gemv(const GemvParams& p, int unit, int rs, i
         ok = tk_load_tagged(p.tx, n, itag, vec, tid);
         gemv_epi_store(er, r1 - r0, tid, epi);
         consumer_bar();                                 // vec[0, n) and epi[] complete
+        tk_stamp(tr, 8, tid);                           // timeline: every input word present
         if (bulk) {
             ok = mbar_wait_bounded(vbar, vphase & 1) && ok;
             ++vphase;

@@ -3,6 +3,7 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdio>
 #include <cstdlib>
 #include <mutex>
@@ -65,13 +66,21 @@ cudaError_t launch_nm(const void* A0, const void* A1, const unsigned char* plane
     auto k = prefill_gemm_kernel<NM>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, Sh::SmemBytes);
     if (e != cudaSuccess) return e;
-    const dim3 grid((unsigned)((p.M + kPfRows - 1) / kPfRows), (unsigned)((p.T + Sh::N - 1) / Sh::N));
+    dim3 grid((unsigned)((p.M + kPfRows - 1) / kPfRows), (unsigned)((p.T + Sh::N - 1) / Sh::N));
+    // few tiles (few tokens, few rows): split K over up to 8 CTAs a tile so that most
+    // SMs take part; the splits' integer plane sums add exactly in any order
+    static int sms = 0;
+    if (!sms && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0) != cudaSuccess) sms = 148;
+    const unsigned tiles = grid.x * grid.y;
+    const int kb = (p.K + kPfKBlock - 1) / kPfKBlock;
+    if (p.acc && p.cnt && tiles <= (unsigned)kPfSplitTiles && NM * 4 * Sh::N <= kPfSplitCols)
+        grid.z = (unsigned)std::max(1, std::min({sms / (int)tiles, kb / 4, 8}));
     if (!trace_path()) {
         k<<<grid, kPfThreads, Sh::SmemBytes, s>>>(a0, a1, b, p);
         return cudaGetLastError();
     }
     PfGemmParams q = p;
-    const size_t n = (size_t)grid.x * grid.y * 8;
+    const size_t n = (size_t)grid.x * grid.y * grid.z * 8;
     if ((e = cudaMalloc(&q.trace, n * 8)) != cudaSuccess) return e;
     cudaMemsetAsync(q.trace, 0, n * 8, s);
     k<<<grid, kPfThreads, Sh::SmemBytes, s>>>(a0, a1, b, q);
@@ -80,7 +89,7 @@ cudaError_t launch_nm(const void* A0, const void* A1, const unsigned char* plane
     if (e == cudaSuccess) e = cudaMemcpy(h.data(), q.trace, n * 8, cudaMemcpyDeviceToHost);
     cudaFree(q.trace);
     if (FILE* f = std::fopen(trace_path(), "ab")) {
-        const unsigned hdr[4] = {grid.x, grid.y, (unsigned)p.K, (unsigned)NM};
+        const unsigned hdr[4] = {grid.x, grid.y, (unsigned)p.K, (unsigned)NM | (grid.z << 8)};
         std::fwrite(hdr, 4, 4, f);
         std::fwrite(h.data(), 8, n, f);
         std::fclose(f);

@@ -34,6 +34,8 @@
 namespace b2 {
 
 constexpr int kPfRows = 128;           // weight rows per tile (MMA M)
+constexpr int kPfSplitTiles = 80;      // split-K totals: tiles of a launch the accumulator holds
+constexpr int kPfSplitCols = 1024;     // columns per tile it holds (NM * 4 planes * N)
 constexpr int kPfKBlock = 128;         // bytes of K per stage (one 128-byte swizzle row)
 constexpr int kPfEpiWarps = 8;         // epilogue warps: TMEM lane quarter w % 4, column half w / 4
 constexpr int kPfThreads = (kPfEpiWarps + 3) * 32;   // + weight copies, MMAs, plane copies
@@ -65,6 +67,12 @@ struct PfGemmParams {
     const int* tok_pos;
     long long cache_seq;
     int* err;
+    // split K (grid z > 1): CTA z takes K blocks [z KB / Z, (z + 1) KB / Z); each adds
+    // its int32 plane sums into acc (exact, any order) and the last of a tile's Z
+    // CTAs (counter cnt[tile]) runs the epilogue from the totals, then clears both
+    // for the next launch. acc: per tile [NM * 4 * N columns][128 rows] int32.
+    int* acc;
+    unsigned* cnt;
     // optional timeline (B2_PF_TRACE): per CTA 8 global-timer values: start, MMA
     // thread's waits on weight / plane tiles (total ns), MMA loop end, weight and
     // plane copy threads' waits for free slots (total ns), epilogue start and end
@@ -246,7 +254,10 @@ prefill_gemm_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_cons
     volatile int* fail = reinterpret_cast<volatile int*>(tmem_slot + 1);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int m0 = blockIdx.x * kPfRows, n0 = blockIdx.y * N;
-    const int KB = (p.K + kPfKBlock - 1) / kPfKBlock;
+    const int KBall = (p.K + kPfKBlock - 1) / kPfKBlock;
+    const int kb0 = (int)(blockIdx.z * (unsigned)KBall / gridDim.z);
+    const int KB = (int)((blockIdx.z + 1) * (unsigned)KBall / gridDim.z) - kb0;   // this CTA's K blocks
+    const bool split = gridDim.z > 1;
 
     if (tid == 0) {
         for (int s = 0; s < NSA; ++s) { mbar_init(&fullA[s], 1); mbar_init(&emptyA[s], 1); }
@@ -264,7 +275,8 @@ prefill_gemm_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_cons
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    unsigned long long* tr = p.trace ? p.trace + ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 8 : nullptr;
+    unsigned long long* tr =
+        p.trace ? p.trace + (((size_t)blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) * 8 : nullptr;
     if (tr && tid == 0) tr[0] = globaltimer_ns();
 
     if (warp == kPfEpiWarps) {
@@ -278,8 +290,8 @@ prefill_gemm_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_cons
                 if (tr) waited += globaltimer_ns() - tw;
                 unsigned char* st = ringA + (size_t)s * Sh::AStage;
                 mbar_arrive_expect_tx(&fullA[s], (uint32_t)Sh::AStage);
-                tma_load_2d(st, &mapA0, kb * kPfKBlock, m0, &fullA[s]);
-                if constexpr (NM == 2) tma_load_2d(st + Sh::ABytes, &mapA1, kb * kPfKBlock, m0, &fullA[s]);
+                tma_load_2d(st, &mapA0, (kb0 + kb) * kPfKBlock, m0, &fullA[s]);
+                if constexpr (NM == 2) tma_load_2d(st + Sh::ABytes, &mapA1, (kb0 + kb) * kPfKBlock, m0, &fullA[s]);
             }
             if (tr) tr[4] = waited;
         }
@@ -296,7 +308,7 @@ prefill_gemm_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_cons
                 mbar_arrive_expect_tx(&fullB[s], (uint32_t)Sh::BStage);
 #pragma unroll
                 for (int pl = 0; pl < 4; ++pl)
-                    tma_load_2d(st + pl * Sh::BBytes, &mapB, kb * kPfKBlock, pl * p.Tpad + n0, &fullB[s]);
+                    tma_load_2d(st + pl * Sh::BBytes, &mapB, (kb0 + kb) * kPfKBlock, pl * p.Tpad + n0, &fullB[s]);
             }
             if (tr) tr[5] = waited;
         }
@@ -336,7 +348,8 @@ prefill_gemm_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_cons
         }
     } else {
         // ---- epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 = weight rows
-        // m0 + 32 (w % 4) + lane, token columns of half w / 4. Per 16-token chunk
+        // m0 + 32 (w % 4) + lane, the 16-token chunks w / 4, w / 4 + 2, ... that hold
+        // tokens (interleaved, so that a short tile keeps both halves busy). Per chunk
         // every global input (the residual, the RoPE rows) is requested before the
         // TMEM reads, so their latencies overlap; the tokens' shifts were staged in
         // shared memory while the MMAs ran.
@@ -358,11 +371,42 @@ prefill_gemm_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_cons
         const bool rope = (p.epi == PF_Q || p.epi == PF_K) && p.rope;
         const int hd = rope ? (m & ~1) % p.dh : 0;
         asm volatile("bar.sync 2, %0;" ::"n"(kPfEpiWarps * 32) : "memory");   // sS complete
-        const bool ok = mbar_wait_bounded(done, 0);
+        bool ok = mbar_wait_bounded(done, 0);
         tc_fence_after();
         if (tr && tid == 0) tr[6] = globaltimer_ns();
-        constexpr int NH = N / (kPfEpiWarps / 4);                   // columns per warp
-        for (int c0 = half * NH; c0 < (half + 1) * NH; c0 += 16) {
+        const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+        int* acc = split ? p.acc + (size_t)tile * (NM * 4 * N) * kPfRows + 32 * quarter + lane : nullptr;
+        bool last = true;
+        if (split) {
+            // this CTA's plane sums into the tile's totals (exact integer adds)
+            for (int c0 = 16 * half; c0 < N && n0 + c0 < p.T; c0 += 32) {
+#pragma unroll
+                for (int mt = 0; mt < NM; ++mt) {
+                    uint32_t r[4][16];
+#pragma unroll
+                    for (int pl = 0; pl < 4; ++pl) tmem_ld16(trow + (uint32_t)((mt * 4 + pl) * N + c0), r[pl]);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int pl = 0; pl < 4; ++pl)
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            if (ok && n0 + c0 + j < p.T && m < p.M)
+                                atomicAdd(acc + (size_t)((mt * 4 + pl) * N + c0 + j) * kPfRows, (int)r[pl][j]);
+                }
+            }
+            __threadfence();
+            volatile int* lastf = const_cast<int*>(fail) + 1 + 2 * N;
+            asm volatile("bar.sync 2, %0;" ::"n"(kPfEpiWarps * 32) : "memory");
+            if (tid == 0) {
+                const unsigned t = atomicAdd(p.cnt + tile, 1u);
+                *lastf = t == gridDim.z - 1;
+                if (t == gridDim.z - 1) p.cnt[tile] = 0u;      // for the next launch
+            }
+            asm volatile("bar.sync 2, %0;" ::"n"(kPfEpiWarps * 32) : "memory");
+            last = *lastf != 0;
+            if (last) __threadfence();
+        }
+        for (int c0 = 16 * half; last && c0 < N && n0 + c0 < p.T; c0 += 32) {
             float in0[16], in1[16];
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
@@ -382,9 +426,25 @@ prefill_gemm_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_cons
 #pragma unroll
             for (int mt = 0; mt < NM; ++mt) {
                 uint32_t r[4][16];
+                if (split) {
+                    // the totals of every split, then zeros for the next launch
 #pragma unroll
-                for (int pl = 0; pl < 4; ++pl) tmem_ld16(trow + (uint32_t)((mt * 4 + pl) * N + c0), r[pl]);
-                tmem_wait_ld();
+                    for (int pl = 0; pl < 4; ++pl)
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) {
+                            int* a = acc + (size_t)((mt * 4 + pl) * N + c0 + j) * kPfRows;
+                            r[pl][j] = (n0 + c0 + j < p.T && m < p.M) ? (uint32_t)__ldcg(a) : 0u;
+                        }
+#pragma unroll
+                    for (int pl = 0; pl < 4; ++pl)
+#pragma unroll
+                        for (int j = 0; j < 16; ++j)
+                            if (n0 + c0 + j < p.T && m < p.M) acc[(size_t)((mt * 4 + pl) * N + c0 + j) * kPfRows] = 0;
+                } else {
+#pragma unroll
+                    for (int pl = 0; pl < 4; ++pl) tmem_ld16(trow + (uint32_t)((mt * 4 + pl) * N + c0), r[pl]);
+                    tmem_wait_ld();
+                }
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {
                     const int pls[4] = {(int)r[0][j], (int)r[1][j], (int)r[2][j], (int)r[3][j]};

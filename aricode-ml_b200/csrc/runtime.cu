@@ -208,6 +208,8 @@ struct b2_ctx {
     unsigned char* pf_planes = nullptr;
     int* pf_S = nullptr;
     float *pf_x = nullptr, *pf_q = nullptr, *pf_att = nullptr, *pf_f = nullptr, *pf_part = nullptr;
+    int* pf_acc = nullptr;          // split-K plane-sum totals of the tensor-core GEMM (zero between launches)
+    unsigned* pf_cnt = nullptr;     // its per-tile arrival counters
     // batched decode (b2_batch_init): bt_n sequences, each with its own KV cache
     int bt_n = 0, bt_max_steps = 0;
     void* bt_base = nullptr;
@@ -1049,7 +1051,8 @@ void prefill_workspace(b2_ctx* c) {
     const size_t b_planes = al(4 * T * c->pf_ldp), b_S = al(T * 4), b_x = al(T * c->d * 4),
                  b_q = al(T * qd * 4), b_f = al(T * ffn * 4),
                  b_part = al(T * H * (size_t)c->attn_nsplit_max * (dh + 2) * 4);
-    const size_t total = b_planes + b_S + b_x + 2 * b_q + b_f + b_part;
+    const size_t b_acc = al((size_t)kPfSplitTiles * kPfSplitCols * kPfRows * 4), b_cnt = al(kPfSplitTiles * 4);
+    const size_t total = b_planes + b_S + b_x + 2 * b_q + b_f + b_part + b_acc + b_cnt;
     if (cudaMalloc(&c->pf_base, total) != cudaSuccess) throw Err(B2_E_OOM, "prefill workspace allocation failed");
     char* w = static_cast<char*>(c->pf_base);
     c->pf_planes = reinterpret_cast<unsigned char*>(w); w += b_planes;
@@ -1058,9 +1061,13 @@ void prefill_workspace(b2_ctx* c) {
     c->pf_q = reinterpret_cast<float*>(w); w += b_q;
     c->pf_att = reinterpret_cast<float*>(w); w += b_q;
     c->pf_f = reinterpret_cast<float*>(w); w += b_f;
-    c->pf_part = reinterpret_cast<float*>(w);
-    // plane rows past the chunk's tokens must read as zeros
+    c->pf_part = reinterpret_cast<float*>(w); w += b_part;
+    c->pf_acc = reinterpret_cast<int*>(w); w += b_acc;
+    c->pf_cnt = reinterpret_cast<unsigned*>(w);
+    // plane rows past the chunk's tokens must read as zeros; the split-K totals and
+    // counters start (and are left by every launch) at zero
     CK(cudaMemsetAsync(c->pf_planes, 0, b_planes, c->stream));
+    CK(cudaMemsetAsync(c->pf_acc, 0, b_acc + b_cnt, c->stream));
 }
 
 // Tokens [p0, p0 + T) of the device id buffer `ids` through every sub-block, no LM
@@ -1085,6 +1092,7 @@ void enqueue_prefill_chunk(b2_ctx* c, int p0, int T, cudaStream_t s, const int* 
         g.out = out; g.ldo = ldo; g.err = err; g.pos0 = p0; g.max_seq = c->max_seq;
         if (B) { g.rope = B->rope; g.rope_tab = c->rope_tab; g.dh = B->dh; g.qscale = (float)(1.0 / std::sqrt((double)B->dh)); }
         g.cache = cache;
+        g.acc = c->pf_acc; g.cnt = c->pf_cnt;
         CK(launch_prefill_gemm(nm, A.w, A1 ? A1->w : nullptr, c->pf_planes, c->pf_ldp, g, s));
     };
     CK(launch_prefill_embed(static_cast<const int8_t*>(c->emb.w), c->emb.s, c->emb.ld, ids, p0, c->vocab,
@@ -1155,6 +1163,7 @@ void enqueue_batch_step(b2_ctx* c, cudaStream_t s) {
         g.tok_pos = c->bt_pos; g.cache_seq = c->bt_seq_stride;
         if (B) { g.rope = B->rope; g.rope_tab = c->rope_tab; g.dh = B->dh; g.qscale = (float)(1.0 / std::sqrt((double)B->dh)); }
         g.cache = cache;
+        g.acc = c->pf_acc; g.cnt = c->pf_cnt;
         CK(launch_prefill_gemm(nm, A.w, A1 ? A1->w : nullptr, c->pf_planes, c->pf_ldp, g, s));
     };
     CK(launch_prefill_embed(static_cast<const int8_t*>(c->emb.w), c->emb.s, c->emb.ld, c->bt_tok, 0, c->vocab, c->d,

@@ -357,12 +357,18 @@ __device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
     return d;
 }
 
+// the exact dot D from its four plane sums
+__device__ __forceinline__ long long xfix_dot(int p0, int p1, int p2, int p3) {
+    return (long long)p0 + (long long)p1 * 256ll + (long long)p2 * 65536ll + (long long)p3 * 16777216ll;
+}
+// one row's value from its exact dot: f32(D 2^-S), one rounding
+__device__ __forceinline__ float xfix_value(long long D, int S) {
+    if (S == kXfixBad) return __uint_as_float(0x7fc00000u);
+    return __double2float_rn(__dmul_rn(__ll2double_rn(D), pow2d(-S)));
+}
 // one row's value from its four plane sums
 __device__ __forceinline__ float xfix_row(const int* pl, int S) {
-    if (S == kXfixBad) return __uint_as_float(0x7fc00000u);
-    const long long D = (long long)pl[0] + (long long)pl[1] * 256ll + (long long)pl[2] * 65536ll +
-                        (long long)pl[3] * 16777216ll;
-    return __double2float_rn(__dmul_rn(__ll2double_rn(D), pow2d(-S)));
+    return xfix_value(xfix_dot(pl[0], pl[1], pl[2], pl[3]), S);
 }
 
 // Block-wide S: every consumer thread passes the largest |x| bits it has seen;

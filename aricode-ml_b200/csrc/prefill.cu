@@ -68,12 +68,12 @@ cudaError_t launch_nm(const void* A0, const void* A1, const unsigned char* plane
     if (e != cudaSuccess) return e;
     dim3 grid((unsigned)((p.M + kPfRows - 1) / kPfRows), (unsigned)((p.T + Sh::N - 1) / Sh::N));
     // few tiles (few tokens, few rows): split K over up to 8 CTAs a tile so that most
-    // SMs take part; the splits' integer plane sums add exactly in any order
+    // SMs take part; the splits' integer dots add exactly in any order
     static int sms = 0;
     if (!sms && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0) != cudaSuccess) sms = 148;
     const unsigned tiles = grid.x * grid.y;
     const int kb = (p.K + kPfKBlock - 1) / kPfKBlock;
-    if (p.acc && p.cnt && tiles <= (unsigned)kPfSplitTiles && NM * 4 * Sh::N <= kPfSplitCols)
+    if (p.acc && p.cnt && tiles <= (unsigned)kPfSplitTiles && NM * Sh::N <= kPfSplitCols)
         grid.z = (unsigned)std::max(1, std::min({sms / (int)tiles, kb / 4, 8}));
     if (!trace_path()) {
         k<<<grid, kPfThreads, Sh::SmemBytes, s>>>(a0, a1, b, p);

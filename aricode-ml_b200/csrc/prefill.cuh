@@ -35,7 +35,7 @@ namespace b2 {
 
 constexpr int kPfRows = 128;           // weight rows per tile (MMA M)
 constexpr int kPfSplitTiles = 80;      // split-K totals: tiles of a launch the accumulator holds
-constexpr int kPfSplitCols = 1024;     // columns per tile it holds (NM * 4 planes * N)
+constexpr int kPfSplitCols = 256;      // columns per tile it holds (NM * N, one int64 total each)
 constexpr int kPfKBlock = 128;         // bytes of K per stage (one 128-byte swizzle row)
 constexpr int kPfEpiWarps = 8;         // epilogue warps: TMEM lane quarter w % 4, column half w / 4
 constexpr int kPfThreads = (kPfEpiWarps + 3) * 32;   // + weight copies, MMAs, plane copies
@@ -68,10 +68,11 @@ struct PfGemmParams {
     long long cache_seq;
     int* err;
     // split K (grid z > 1): CTA z takes K blocks [z KB / Z, (z + 1) KB / Z); each adds
-    // its int32 plane sums into acc (exact, any order) and the last of a tile's Z
-    // CTAs (counter cnt[tile]) runs the epilogue from the totals, then clears both
-    // for the next launch. acc: per tile [NM * 4 * N columns][128 rows] int32.
-    int* acc;
+    // its exact dot D = P0 + 2^8 P1 + 2^16 P2 + 2^24 P3 of every (row, token) into acc
+    // (64-bit integer adds: exact in any order) and the last of a tile's Z CTAs
+    // (counter cnt[tile]) runs the epilogue from the totals, then clears both for the
+    // next launch. acc: per tile [NM * N columns][128 rows] int64.
+    unsigned long long* acc;
     unsigned* cnt;
     // optional timeline (B2_PF_TRACE): per CTA 8 global-timer values: start, MMA
     // thread's waits on weight / plane tiles (total ns), MMA loop end, weight and
@@ -375,7 +376,7 @@ prefill_gemm_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_cons
         tc_fence_after();
         if (tr && tid == 0) tr[6] = globaltimer_ns();
         const int tile = blockIdx.y * gridDim.x + blockIdx.x;
-        int* acc = split ? p.acc + (size_t)tile * (NM * 4 * N) * kPfRows + 32 * quarter + lane : nullptr;
+        unsigned long long* acc = split ? p.acc + (size_t)tile * (NM * N) * kPfRows + 32 * quarter + lane : nullptr;
         bool last = true;
         if (split) {
             // this CTA's plane sums into the tile's totals (exact integer adds)
@@ -387,11 +388,10 @@ prefill_gemm_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_cons
                     for (int pl = 0; pl < 4; ++pl) tmem_ld16(trow + (uint32_t)((mt * 4 + pl) * N + c0), r[pl]);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int pl = 0; pl < 4; ++pl)
-#pragma unroll
-                        for (int j = 0; j < 16; ++j)
-                            if (ok && n0 + c0 + j < p.T && m < p.M)
-                                atomicAdd(acc + (size_t)((mt * 4 + pl) * N + c0 + j) * kPfRows, (int)r[pl][j]);
+                    for (int j = 0; j < 16; ++j)
+                        if (ok && n0 + c0 + j < p.T && m < p.M)
+                            atomicAdd(acc + (size_t)(mt * N + c0 + j) * kPfRows,
+                                      (unsigned long long)xfix_dot((int)r[0][j], (int)r[1][j], (int)r[2][j], (int)r[3][j]));
                 }
             }
             __threadfence();
@@ -425,30 +425,29 @@ prefill_gemm_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_cons
             float v[NM][16];
 #pragma unroll
             for (int mt = 0; mt < NM; ++mt) {
-                uint32_t r[4][16];
                 if (split) {
                     // the totals of every split, then zeros for the next launch
+                    long long D[16];
 #pragma unroll
-                    for (int pl = 0; pl < 4; ++pl)
+                    for (int j = 0; j < 16; ++j) {
+                        unsigned long long* a = acc + (size_t)(mt * N + c0 + j) * kPfRows;
+                        D[j] = (n0 + c0 + j < p.T && m < p.M) ? (long long)__ldcg(a) : 0ll;
+                    }
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) {
-                            int* a = acc + (size_t)((mt * 4 + pl) * N + c0 + j) * kPfRows;
-                            r[pl][j] = (n0 + c0 + j < p.T && m < p.M) ? (uint32_t)__ldcg(a) : 0u;
-                        }
-#pragma unroll
-                    for (int pl = 0; pl < 4; ++pl)
-#pragma unroll
-                        for (int j = 0; j < 16; ++j)
-                            if (n0 + c0 + j < p.T && m < p.M) acc[(size_t)((mt * 4 + pl) * N + c0 + j) * kPfRows] = 0;
+                    for (int j = 0; j < 16; ++j) {
+                        if (n0 + c0 + j < p.T && m < p.M) acc[(size_t)(mt * N + c0 + j) * kPfRows] = 0ull;
+                        v[mt][j] = xfix_value(D[j], sS[c0 + j]);
+                    }
                 } else {
+                    uint32_t r[4][16];
 #pragma unroll
                     for (int pl = 0; pl < 4; ++pl) tmem_ld16(trow + (uint32_t)((mt * 4 + pl) * N + c0), r[pl]);
                     tmem_wait_ld();
-                }
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int pls[4] = {(int)r[0][j], (int)r[1][j], (int)r[2][j], (int)r[3][j]};
-                    v[mt][j] = xfix_row(pls, sS[c0 + j]);
+                    for (int j = 0; j < 16; ++j) {
+                        const int pls[4] = {(int)r[0][j], (int)r[1][j], (int)r[2][j], (int)r[3][j]};
+                        v[mt][j] = xfix_row(pls, sS[c0 + j]);
+                    }
                 }
             }
 #pragma unroll

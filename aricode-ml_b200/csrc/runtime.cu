@@ -208,7 +208,7 @@ struct b2_ctx {
     unsigned char* pf_planes = nullptr;
     int* pf_S = nullptr;
     float *pf_x = nullptr, *pf_q = nullptr, *pf_att = nullptr, *pf_f = nullptr, *pf_part = nullptr;
-    int* pf_acc = nullptr;          // split-K plane-sum totals of the tensor-core GEMM (zero between launches)
+    unsigned long long* pf_acc = nullptr;   // split-K dot totals of the tensor-core GEMM (zero between launches)
     unsigned* pf_cnt = nullptr;     // its per-tile arrival counters
     // batched decode (b2_batch_init): bt_n sequences, each with its own KV cache
     int bt_n = 0, bt_max_steps = 0;
@@ -1051,7 +1051,7 @@ void prefill_workspace(b2_ctx* c) {
     const size_t b_planes = al(4 * T * c->pf_ldp), b_S = al(T * 4), b_x = al(T * c->d * 4),
                  b_q = al(T * qd * 4), b_f = al(T * ffn * 4),
                  b_part = al(T * H * (size_t)c->attn_nsplit_max * (dh + 2) * 4);
-    const size_t b_acc = al((size_t)kPfSplitTiles * kPfSplitCols * kPfRows * 4), b_cnt = al(kPfSplitTiles * 4);
+    const size_t b_acc = al((size_t)kPfSplitTiles * kPfSplitCols * kPfRows * 8), b_cnt = al(kPfSplitTiles * 4);
     const size_t total = b_planes + b_S + b_x + 2 * b_q + b_f + b_part + b_acc + b_cnt;
     if (cudaMalloc(&c->pf_base, total) != cudaSuccess) throw Err(B2_E_OOM, "prefill workspace allocation failed");
     char* w = static_cast<char*>(c->pf_base);
@@ -1062,7 +1062,7 @@ void prefill_workspace(b2_ctx* c) {
     c->pf_att = reinterpret_cast<float*>(w); w += b_q;
     c->pf_f = reinterpret_cast<float*>(w); w += b_f;
     c->pf_part = reinterpret_cast<float*>(w); w += b_part;
-    c->pf_acc = reinterpret_cast<int*>(w); w += b_acc;
+    c->pf_acc = reinterpret_cast<unsigned long long*>(w); w += b_acc;
     c->pf_cnt = reinterpret_cast<unsigned*>(w);
     // plane rows past the chunk's tokens must read as zeros; the split-K totals and
     // counters start (and are left by every launch) at zero

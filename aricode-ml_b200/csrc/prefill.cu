@@ -71,10 +71,13 @@ cudaError_t launch_nm(const void* A0, const void* A1, const unsigned char* plane
     // SMs take part; the splits' integer dots add exactly in any order
     static int sms = 0;
     if (!sms && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0) != cudaSuccess) sms = 148;
-    const unsigned tiles = grid.x * grid.y;
+    const int tiles = (int)(grid.x * grid.y);
     const int kb = (p.K + kPfKBlock - 1) / kPfKBlock;
-    if (p.acc && p.cnt && tiles <= (unsigned)kPfSplitTiles && NM * Sh::N <= kPfSplitCols)
-        grid.z = (unsigned)std::max(1, std::min({sms / (int)tiles, kb / 4, 8}));
+    if (p.acc && p.cnt && tiles <= kPfSplitCounters && (long long)tiles * NM * Sh::N <= (long long)kPfSplitTiles * kPfSplitCols) {
+        // one wave (a CTA per SM): a second wave of CTAs costs more than their shorter
+        // K ranges save (measured: 86 tiles split 8 ways, 67 -> 93 us)
+        grid.z = (unsigned)std::max(1, std::min({sms / tiles, kb / 4, 8}));
+    }
     if (!trace_path()) {
         k<<<grid, kPfThreads, Sh::SmemBytes, s>>>(a0, a1, b, p);
         return cudaGetLastError();

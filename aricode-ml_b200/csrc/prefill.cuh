@@ -34,8 +34,9 @@
 namespace b2 {
 
 constexpr int kPfRows = 128;           // weight rows per tile (MMA M)
-constexpr int kPfSplitTiles = 80;      // split-K totals: tiles of a launch the accumulator holds
-constexpr int kPfSplitCols = 256;      // columns per tile it holds (NM * N, one int64 total each)
+constexpr int kPfSplitTiles = 80;      // split-K totals: the accumulator holds kPfSplitTiles x
+constexpr int kPfSplitCols = 256;      // kPfSplitCols columns of 128 rows (NM * N a tile, int64 each)
+constexpr int kPfSplitCounters = 512;  // tiles of a split launch (arrival counters)
 constexpr int kPfKBlock = 128;         // bytes of K per stage (one 128-byte swizzle row)
 constexpr int kPfEpiWarps = 8;         // epilogue warps: TMEM lane quarter w % 4, column half w / 4
 constexpr int kPfThreads = (kPfEpiWarps + 3) * 32;   // + weight copies, MMAs, plane copies

@@ -1051,7 +1051,7 @@ void prefill_workspace(b2_ctx* c) {
     const size_t b_planes = al(4 * T * c->pf_ldp), b_S = al(T * 4), b_x = al(T * c->d * 4),
                  b_q = al(T * qd * 4), b_f = al(T * ffn * 4),
                  b_part = al(T * H * (size_t)c->attn_nsplit_max * (dh + 2) * 4);
-    const size_t b_acc = al((size_t)kPfSplitTiles * kPfSplitCols * kPfRows * 8), b_cnt = al(kPfSplitTiles * 4);
+    const size_t b_acc = al((size_t)kPfSplitTiles * kPfSplitCols * kPfRows * 8), b_cnt = al(kPfSplitCounters * 4);
     const size_t total = b_planes + b_S + b_x + 2 * b_q + b_f + b_part + b_acc + b_cnt;
     if (cudaMalloc(&c->pf_base, total) != cudaSuccess) throw Err(B2_E_OOM, "prefill workspace allocation failed");
     char* w = static_cast<char*>(c->pf_base);

@@ -161,6 +161,19 @@ cudaError_t launch_batch_tail(const float* logits, int vocab, const BatchState& 
     return cudaGetLastError();
 }
 
+// One thread: the previous launches on this stream are complete, so their peer
+// stores are performed; the flag exchange (system-scope release and acquire) then
+// orders them before every rank's next launch.
+static __global__ void tp_sync_kernel(unsigned* flags, Mirror mir, int rank, int nranks, unsigned e, int* err) {
+    if (threadIdx.x == 0 && !tp_flag_exchange(flags, rank, nranks, mir, e)) set_err(err, B2_DEV_ERR_TIMEOUT);
+}
+
+cudaError_t launch_tp_sync(unsigned* flags, const Mirror& mir, int rank, int nranks, unsigned e, int* err,
+                           cudaStream_t s) {
+    tp_sync_kernel<<<1, 32, 0, s>>>(flags, mir, rank, nranks, e, err);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_batch_check(const BatchState& b, int B, cudaStream_t s) {
     batch_check_kernel<<<(B + 127) / 128, 128, 0, s>>>(b, B);
     return cudaGetLastError();

@@ -75,6 +75,8 @@ struct PfGemmParams {
     // next launch. acc: per tile [NM * N columns][128 rows] int64.
     unsigned long long* acc;
     unsigned* cnt;
+    // tensor parallelism: out rows also written into every peer's copy of out
+    Mirror mir;
     // optional timeline (B2_PF_TRACE): per CTA 8 global-timer values: start, MMA
     // thread's waits on weight / plane tiles (total ns), MMA loop end, weight and
     // plane copy threads' waits for free slots (total ns), epilogue start and end
@@ -91,6 +93,9 @@ struct PfAttnParams {
     int T, pos0;
     int* err;
     const int* n_of;         // combine only: token t sees n_of[t] + 1 keys (nullptr: pos0 + t + 1)
+    int ldo;                 // out row stride (0: H * dh); tensor parallelism: this rank's heads
+                             // at their columns of the whole attention output
+    Mirror mir;              // and written into every peer's copy of it
 };
 
 // ------------------------------------------------------------------ PTX wrappers
@@ -457,7 +462,7 @@ prefill_gemm_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_cons
                 float y = fmul(v[0][j], sc[0]);
                 if (p.epi == PF_SWIGLU) {
                     const float u = fmul(v[NM - 1][j], sc[NM - 1]);
-                    if (ok && t < p.T && m < p.M) p.out[(size_t)t * p.ldo + m] = fmul(silu_f(y), u);
+                    if (ok && t < p.T && m < p.M) mirror_store(p.mir, p.out + (size_t)t * p.ldo + m, fmul(silu_f(y), u));
                     continue;
                 }
                 if (p.bias) y = fadd(y, bi);
@@ -479,7 +484,7 @@ prefill_gemm_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_cons
                         p.cache[t * p.cache_seq + ((size_t)kvh * p.max_seq + pos) * p.dh + hdv] = y;
                     else set_err(p.err, B2_DEV_ERR_KV_OVERFLOW);
                 } else if (p.epi == PF_RESID) {
-                    p.out[(size_t)t * p.ldo + m] = fadd(y, in0[j]);
+                    mirror_store(p.mir, p.out + (size_t)t * p.ldo + m, fadd(y, in0[j]));
                 } else {
                     p.out[(size_t)t * p.ldo + m] = y;
                 }
@@ -660,7 +665,7 @@ static __global__ void __launch_bounds__(256) prefill_attn_combine_kernel(const 
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const int d = lane + 32 * i;
-        if (d < dh) p.out[(size_t)t * p.H * dh + (size_t)h * dh + d] = fdiv(o[i], l);
+        if (d < dh) mirror_store(p.mir, p.out + (size_t)t * (p.ldo ? p.ldo : p.H * dh) + (size_t)h * dh + d, fdiv(o[i], l));
     }
 }
 
@@ -859,6 +864,10 @@ cudaError_t launch_prefill_planes(const PfPlanesParams& p, int T, cudaStream_t s
 cudaError_t launch_prefill_attn(const PfAttnParams& p, cudaStream_t s);
 cudaError_t launch_batch_attn(const AttnParams& a, int nseq, cudaStream_t s);
 cudaError_t launch_batch_tail(const float* logits, int vocab, const BatchState& b, int B, cudaStream_t s);
+// tensor parallelism, between two prefill launches whose outputs the ranks mirror:
+// epoch e published to every rank and awaited from every rank (bounded)
+cudaError_t launch_tp_sync(unsigned* flags, const Mirror& mir, int rank, int nranks, unsigned e, int* err,
+                           cudaStream_t s);
 cudaError_t launch_batch_check(const BatchState& b, int B, cudaStream_t s);
 cudaError_t launch_prefill_embed(const int8_t* emb, const float* emb_s, long long ld, const int* ids, int pos0,
                                  int vocab, int d, float* x, int T, int* err, cudaStream_t s);

@@ -208,6 +208,13 @@ struct b2_ctx {
     unsigned char* pf_planes = nullptr;
     int* pf_S = nullptr;
     float *pf_x = nullptr, *pf_q = nullptr, *pf_att = nullptr, *pf_f = nullptr, *pf_part = nullptr;
+    // tensor parallelism: the prefill's x, attention output and FFN hidden rows of every
+    // rank, in the exchange buffer (the peers write their rows), and the flags and
+    // epoch of the barriers between its launches
+    float *pfx_x = nullptr, *pfx_att = nullptr, *pfx_f = nullptr;
+    unsigned* tp_pflag = nullptr;
+    unsigned tp_pepoch = 0;
+    int pfx_tmax = 0;
     unsigned long long* pf_acc = nullptr;   // split-K dot totals of the tensor-core GEMM (zero between launches)
     unsigned* pf_cnt = nullptr;     // its per-tile arrival counters
     // batched decode (b2_batch_init): bt_n sequences, each with its own KV cache
@@ -559,6 +566,12 @@ void assemble(b2_ctx* c, const b2json::Value& plan) {
                      o_cv = xadd(kMaxRanks * 4), o_ci = xadd(kMaxRanks * 4), o_cn = xadd(kMaxRanks * 4),
                      o_tx = xadd((size_t)c->d * 8), o_tatt = xadd((size_t)max_q_all * 8),
                      o_tf = xadd((size_t)max_ffn * 8);
+        // tensor parallelism: the batched prefill's exchanged activations
+        const size_t pfT = c->tp_size > 1
+                               ? (size_t)std::min(512, (c->max_seq + kPfTokenTile - 1) / kPfTokenTile * kPfTokenTile)
+                               : 0;
+        const size_t o_pfx = xadd(pfT * c->d * 4), o_pfa = xadd(pfT * max_q_all * 4), o_pff = xadd(pfT * max_ffn * 4),
+                     o_pfl = xadd(kMaxRanks * 4);
         c->xch_bytes = xo;
         if (cudaMalloc(&c->d_xch, c->xch_bytes) != cudaSuccess) throw Err(B2_E_OOM, "exchange buffer allocation failed");
         CK(cudaMemsetAsync(c->d_xch, 0, c->xch_bytes, c->stream));
@@ -576,6 +589,13 @@ void assemble(b2_ctx* c, const b2json::Value& plan) {
         c->tx = reinterpret_cast<unsigned long long*>(xb + o_tx);
         c->tatt = reinterpret_cast<unsigned long long*>(xb + o_tatt);
         c->tf = reinterpret_cast<unsigned long long*>(xb + o_tf);
+        if (pfT) {
+            c->pfx_tmax = (int)pfT;
+            c->pfx_x = reinterpret_cast<float*>(xb + o_pfx);
+            c->pfx_att = reinterpret_cast<float*>(xb + o_pfa);
+            c->pfx_f = reinterpret_cast<float*>(xb + o_pff);
+            c->tp_pflag = reinterpret_cast<unsigned*>(xb + o_pfl);
+        }
     }
     c->logits = reinterpret_cast<float*>(w + offs[i_logits]);
     c->attn_part = reinterpret_cast<float*>(w + offs[i_part]);
@@ -618,7 +638,6 @@ void assemble(b2_ctx* c, const b2json::Value& plan) {
     c->pf_ok = false;
     const char* pe = std::getenv("B2_PREFILL_BATCHED");
     if (pe && pe[0] == '0') c->pf_why = "batched prefill disabled (B2_PREFILL_BATCHED=0)";
-    else if (c->tp_size > 1) c->pf_why = "tensor parallelism";
     else if (c->pos_tab) c->pf_why = "learned positional embedding";
     else if (c->emb.i4 || c->lm.i4) c->pf_why = "int4 weights";
     else {
@@ -1036,12 +1055,12 @@ void prefill_workspace(b2_ctx* c) {
     for (const Block& B : c->blocks) {
         if (B.attn) {
             ld_max = std::max({ld_max, B.q.ld, B.o.ld});
-            qd = std::max(qd, B.H * B.dh);
+            qd = std::max(qd, B.H_all * B.dh);
             H = std::max(H, B.H);
             dh = std::max(dh, B.dh);
         } else {
             ld_max = std::max({ld_max, B.w1.ld, B.w2.ld});
-            ffn = std::max(ffn, B.ffn_local);
+            ffn = std::max(ffn, B.d_ffn);
         }
     }
     c->pf_ldp = (ld_max + 127) / 128 * 128;
@@ -1061,6 +1080,10 @@ void prefill_workspace(b2_ctx* c) {
     c->pf_q = reinterpret_cast<float*>(w); w += b_q;
     c->pf_att = reinterpret_cast<float*>(w); w += b_q;
     c->pf_f = reinterpret_cast<float*>(w); w += b_f;
+    if (c->tp_size > 1) {                       // the exchanged ones: in the exchange buffer
+        if (c->pfx_tmax < c->pf_tmax) throw Err(B2_E_INVALID, "prefill exchange region too small");
+        c->pf_x = c->pfx_x; c->pf_att = c->pfx_att; c->pf_f = c->pfx_f;
+    }
     c->pf_part = reinterpret_cast<float*>(w); w += b_part;
     c->pf_acc = reinterpret_cast<unsigned long long*>(w); w += b_acc;
     c->pf_cnt = reinterpret_cast<unsigned*>(w);
@@ -1084,9 +1107,20 @@ void enqueue_prefill_chunk(b2_ctx* c, int p0, int T, cudaStream_t s, const int* 
         pp.planes = c->pf_planes; pp.ldp = c->pf_ldp; pp.kp = c->pf_ldp; pp.Tpad = Tpad; pp.S = c->pf_S;
         CK(launch_prefill_planes(pp, T, s));
     };
+    // tensor parallelism: a rank's rows of x, its heads of the attention output and its
+    // columns of the FFN hidden go to every rank's copy (mirrored stores), and a flag
+    // barrier follows each such launch before any rank reads the whole row
+    const bool tp = c->tp_size > 1;
+    const Mirror nomir{};
+    const Mirror& mir = tp ? c->mir : nomir;
+    const int d0 = c->tp_rank * (c->d / c->tp_size);
+    auto sync = [&]() {
+        if (tp) CK(launch_tp_sync(c->tp_pflag, c->mir, c->tp_rank, c->tp_size, ++c->tp_pepoch, err, s));
+    };
     auto gemm = [&](int nm, const DevMat& A, const DevMat* A1, int epi, float* out, int ldo, const float* bias,
                     const Block* B, float* cache) {
         PfGemmParams g{};
+        g.mir = (epi == PF_RESID || epi == PF_SWIGLU) ? mir : nomir;
         g.M = A.rows; g.K = A.ld; g.T = T; g.Tpad = Tpad; g.epi = epi; g.S = c->pf_S;
         g.scale[0] = A.s; g.scale[1] = A1 ? A1->s : A.s; g.bias = bias;
         g.out = out; g.ldo = ldo; g.err = err; g.pos0 = p0; g.max_seq = c->max_seq;
@@ -1108,16 +1142,22 @@ void enqueue_prefill_chunk(b2_ctx* c, int p0, int T, cudaStream_t s, const int* 
             gemm(1, B.k, nullptr, PF_K, nullptr, 0, B.bias[1], &B, Kc);
             gemm(1, B.v, nullptr, PF_V, nullptr, 0, B.bias[2], &B, Vc);
             PfAttnParams a{};
-            a.q = c->pf_q; a.K = Kc; a.V = Vc; a.out = c->pf_att; a.part = c->pf_part;
+            const int qall = B.H_all * B.dh;
+            a.q = c->pf_q; a.K = Kc; a.V = Vc; a.out = c->pf_att + (size_t)B.head0 * B.dh; a.ldo = qall;
+            a.mir = mir; a.part = c->pf_part;
             a.H = B.H; a.KVH = B.KVH; a.dh = B.dh; a.max_seq = c->max_seq; a.nsplit_max = c->attn_nsplit_max;
             a.T = T; a.pos0 = p0; a.err = err;
             CK(launch_prefill_attn(a, s));
-            planes(c->pf_att, qd, qd, nullptr);
-            gemm(1, B.o, nullptr, PF_RESID, c->pf_x, c->d, B.bias[3], nullptr, nullptr);
+            sync();
+            planes(c->pf_att, qall, qall, nullptr);
+            gemm(1, B.o, nullptr, PF_RESID, c->pf_x + d0, c->d, B.bias[3], nullptr, nullptr);
+            sync();
         } else {
-            gemm(2, B.w1, &B.w3, PF_SWIGLU, c->pf_f, B.ffn_local, nullptr, nullptr, nullptr);
-            planes(c->pf_f, B.ffn_local, B.ffn_local, nullptr);
-            gemm(1, B.w2, nullptr, PF_RESID, c->pf_x, c->d, nullptr, nullptr, nullptr);
+            gemm(2, B.w1, &B.w3, PF_SWIGLU, c->pf_f + B.ffn0, B.d_ffn, nullptr, nullptr, nullptr);
+            sync();
+            planes(c->pf_f, B.d_ffn, B.d_ffn, nullptr);
+            gemm(1, B.w2, nullptr, PF_RESID, c->pf_x + d0, c->d, nullptr, nullptr, nullptr);
+            sync();
         }
     }
 }
@@ -1154,9 +1194,20 @@ void enqueue_batch_step(b2_ctx* c, cudaStream_t s) {
         pp.planes = c->pf_planes; pp.ldp = c->pf_ldp; pp.kp = c->pf_ldp; pp.Tpad = Tpad; pp.S = c->pf_S;
         CK(launch_prefill_planes(pp, Bn, s));
     };
+    // tensor parallelism: a rank's rows of x, its heads of the attention output and its
+    // columns of the FFN hidden go to every rank's copy (mirrored stores), and a flag
+    // barrier follows each such launch before any rank reads the whole row
+    const bool tp = c->tp_size > 1;
+    const Mirror nomir{};
+    const Mirror& mir = tp ? c->mir : nomir;
+    const int d0 = c->tp_rank * (c->d / c->tp_size);
+    auto sync = [&]() {
+        if (tp) CK(launch_tp_sync(c->tp_pflag, c->mir, c->tp_rank, c->tp_size, ++c->tp_pepoch, err, s));
+    };
     auto gemm = [&](int nm, const DevMat& A, const DevMat* A1, int epi, float* out, int ldo, const float* bias,
                     const Block* B, float* cache) {
         PfGemmParams g{};
+        g.mir = (epi == PF_RESID || epi == PF_SWIGLU) ? mir : nomir;
         g.M = A.rows; g.K = A.ld; g.T = Bn; g.Tpad = Tpad; g.epi = epi; g.S = c->pf_S;
         g.scale[0] = A.s; g.scale[1] = A1 ? A1->s : A.s; g.bias = bias;
         g.out = out; g.ldo = ldo; g.err = err; g.pos0 = 0; g.max_seq = c->max_seq;
@@ -1198,6 +1249,7 @@ void enqueue_batch_step(b2_ctx* c, cudaStream_t s) {
 
 void batch_init(b2_ctx* c, int n, int max_steps) {
     if (!c->pf_ok) throw Err(B2_E_UNSUPPORTED, "batched decode needs a plan the tensor-core path covers: " + c->pf_why);
+    if (c->tp_size > 1) throw Err(B2_E_UNSUPPORTED, "batched decode runs on one GPU");
     if (n < 1 || n > 512 || max_steps < 1) throw Err(B2_E_INVALID, "batch size 1..512 and max_steps >= 1");
     if (c->bt_base) throw Err(B2_E_INVALID, "batched state already initialised");
     prefill_workspace(c);

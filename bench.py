@@ -547,8 +547,8 @@ def time_e2e(torch, dec, prompt, new, stream, dist=None, reps=2):
     return {"value": new / (ms / 1000.0), "unit": "tokens/s",
             "h2d_bytes_per_step": 4 * P + 64, "d2h_bytes_per_step": 4 * new + 64,
             "ms_per_generate": ms,
-            "includes": "prefill of the prompt (batched on the tensor cores on one GPU, token at a time "
-                        "with tensor parallelism) + 256 decode steps"}
+            "includes": "prefill of the prompt (batched on the tensor cores, each rank its rows with tensor "
+                        "parallelism) + 256 decode steps"}
 
 
 if __name__ == "__main__":

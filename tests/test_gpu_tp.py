@@ -1,5 +1,6 @@
 """Tensor parallelism: WORLD processes, one GPU each (tests/tp_worker.py), against
-one GPU over the same synthetic weights. Every rank computes exactly its rows of
+one GPU over the same synthetic weights; the prompt goes through the batched
+(tensor-core) prefill on both sides. Every rank computes exactly its rows of
 the one-GPU step, so greedy ids and each rank's logit rows must be bit-identical.
 Needs WORLD GPUs; skipped otherwise."""
 import os
@@ -61,14 +62,16 @@ def test_tensor_parallel_matches_one_gpu(pkg, tmp_path, world, name, layers, max
     ids = one.generate(prompt, 20)
     one.reset()
     logits = [one.step(t, want_logits=True)[1] for t in prompt[:6]]
+    assert one.query("prefill_batched") == 1
     one.close()
-    _check(res, ids, logits, plan, world)
+    _check(res, ids, logits, plan, world, 1)
 
 
-def _check(res, ids, logits, plan, world):
+def _check(res, ids, logits, plan, world, pf):
     rows = plan["vocab"] // world
     for r, got in enumerate(res):
         assert int(got["tk"][0]) == 1
+        assert int(got["pf"][0]) == pf           # the same prefill path as one GPU
         assert got["ids"].tolist() == list(ids), f"rank {r}"
         ref = np.stack([lg[r * rows:(r + 1) * rows] for lg in logits])
         assert np.array_equal(got["logits"].view(np.uint32), ref.view(np.uint32)), f"rank {r}"
@@ -92,5 +95,6 @@ def test_tensor_parallel_from_a_packed_blob(pkg, tmp_path):
     ids = one.generate(prompt, 20)
     one.reset()
     logits = [one.step(t, want_logits=True)[1] for t in prompt[:6]]
+    pf = one.query("prefill_batched")
     one.close()
-    _check(res, ids, logits, plan, 2)
+    _check(res, ids, logits, plan, 2, pf)

@@ -56,7 +56,7 @@ def main(argv):
         _, lg = dec.step(t, want_logits=True)
         logits.append(lg[rank * rows:(rank + 1) * rows])
     np.savez(out, ids=np.asarray(ids, np.int64), logits=np.stack(logits),
-             tk=np.asarray([dec.query("token_kernel")]))
+             tk=np.asarray([dec.query("token_kernel")]), pf=np.asarray([dec.query("prefill_batched")]))
     dist.barrier()
     dec.close()
     dist.destroy_process_group()

@@ -138,7 +138,7 @@ cudaError_t launch_prefill_attn(const PfAttnParams& p, cudaStream_t s) {
     return cudaGetLastError();
 }
 
-cudaError_t launch_batch_attn(const AttnParams& a, int nseq, cudaStream_t s) {
+cudaError_t launch_batch_attn(const AttnParams& a, int nseq, int ldo, cudaStream_t s) {
     const int kd = (a.dh + 31) / 32;
     auto k = kd <= 1 ? attn_batch_part_kernel<1> : kd == 2 ? attn_batch_part_kernel<2>
                                                   : kd <= 4 ? attn_batch_part_kernel<4> : attn_batch_part_kernel<8>;
@@ -150,6 +150,7 @@ cudaError_t launch_batch_attn(const AttnParams& a, int nseq, cudaStream_t s) {
     PfAttnParams c{};
     c.out = a.out; c.part = a.part; c.H = a.H; c.KVH = a.KVH; c.dh = a.dh; c.max_seq = a.max_seq;
     c.nsplit_max = a.nsplit_max; c.T = nseq; c.pos0 = 0; c.err = a.err; c.n_of = a.n_of;
+    c.ldo = ldo; c.mir = a.mir;
     const long long items = (long long)nseq * a.H;
     prefill_attn_combine_kernel<<<(unsigned)((items + 7) / 8), 256, 0, s>>>(c);
     return cudaGetLastError();
@@ -163,14 +164,19 @@ cudaError_t launch_batch_tail(const float* logits, int vocab, const BatchState& 
 
 // One thread: the previous launches on this stream are complete, so their peer
 // stores are performed; the flag exchange (system-scope release and acquire) then
-// orders them before every rank's next launch.
-static __global__ void tp_sync_kernel(unsigned* flags, Mirror mir, int rank, int nranks, unsigned e, int* err) {
-    if (threadIdx.x == 0 && !tp_flag_exchange(flags, rank, nranks, mir, e)) set_err(err, B2_DEV_ERR_TIMEOUT);
+// orders them before every rank's next launch. The epoch is a counter in this
+// rank's memory (every rank takes the same barriers in the same order), so a
+// captured graph that replays the launch takes a new epoch each time.
+static __global__ void tp_sync_kernel(unsigned* flags, Mirror mir, int rank, int nranks, unsigned* epoch, int* err) {
+    if (threadIdx.x != 0) return;
+    const unsigned e = *epoch + 1u;
+    *epoch = e;
+    if (!tp_flag_exchange(flags, rank, nranks, mir, e)) set_err(err, B2_DEV_ERR_TIMEOUT);
 }
 
-cudaError_t launch_tp_sync(unsigned* flags, const Mirror& mir, int rank, int nranks, unsigned e, int* err,
+cudaError_t launch_tp_sync(unsigned* flags, const Mirror& mir, int rank, int nranks, unsigned* epoch, int* err,
                            cudaStream_t s) {
-    tp_sync_kernel<<<1, 32, 0, s>>>(flags, mir, rank, nranks, e, err);
+    tp_sync_kernel<<<1, 32, 0, s>>>(flags, mir, rank, nranks, epoch, err);
     return cudaGetLastError();
 }
 

@@ -486,7 +486,7 @@ prefill_gemm_kernel(const __grid_constant__ CUtensorMap mapA0, const __grid_cons
                 } else if (p.epi == PF_RESID) {
                     mirror_store(p.mir, p.out + (size_t)t * p.ldo + m, fadd(y, in0[j]));
                 } else {
-                    p.out[(size_t)t * p.ldo + m] = y;
+                    mirror_store(p.mir, p.out + (size_t)t * p.ldo + m, y);
                 }
             }
         }
@@ -862,11 +862,11 @@ cudaError_t launch_prefill_gemm(int nm, const void* A0, const void* A1, const un
                                 const PfGemmParams& p, cudaStream_t s);
 cudaError_t launch_prefill_planes(const PfPlanesParams& p, int T, cudaStream_t s);
 cudaError_t launch_prefill_attn(const PfAttnParams& p, cudaStream_t s);
-cudaError_t launch_batch_attn(const AttnParams& a, int nseq, cudaStream_t s);
+cudaError_t launch_batch_attn(const AttnParams& a, int nseq, int ldo, cudaStream_t s);
 cudaError_t launch_batch_tail(const float* logits, int vocab, const BatchState& b, int B, cudaStream_t s);
 // tensor parallelism, between two prefill launches whose outputs the ranks mirror:
 // epoch e published to every rank and awaited from every rank (bounded)
-cudaError_t launch_tp_sync(unsigned* flags, const Mirror& mir, int rank, int nranks, unsigned e, int* err,
+cudaError_t launch_tp_sync(unsigned* flags, const Mirror& mir, int rank, int nranks, unsigned* epoch, int* err,
                            cudaStream_t s);
 cudaError_t launch_batch_check(const BatchState& b, int B, cudaStream_t s);
 cudaError_t launch_prefill_embed(const int8_t* emb, const float* emb_s, long long ld, const int* ids, int pos0,

@@ -213,7 +213,8 @@ struct b2_ctx {
     // epoch of the barriers between its launches
     float *pfx_x = nullptr, *pfx_att = nullptr, *pfx_f = nullptr;
     unsigned* tp_pflag = nullptr;
-    unsigned tp_pepoch = 0;
+    unsigned* tp_pepoch = nullptr;     // this rank's count of those barriers (device)
+    float* pfx_logits = nullptr;       // batched decode's logits [pf_tmax][vocab]
     int pfx_tmax = 0;
     unsigned long long* pf_acc = nullptr;   // split-K dot totals of the tensor-core GEMM (zero between launches)
     unsigned* pf_cnt = nullptr;     // its per-tile arrival counters
@@ -571,7 +572,7 @@ void assemble(b2_ctx* c, const b2json::Value& plan) {
                                ? (size_t)std::min(512, (c->max_seq + kPfTokenTile - 1) / kPfTokenTile * kPfTokenTile)
                                : 0;
         const size_t o_pfx = xadd(pfT * c->d * 4), o_pfa = xadd(pfT * max_q_all * 4), o_pff = xadd(pfT * max_ffn * 4),
-                     o_pfl = xadd(kMaxRanks * 4);
+                     o_pfl = xadd(kMaxRanks * 4), o_pep = xadd(4), o_plg = xadd(pfT * c->vocab * 4);
         c->xch_bytes = xo;
         if (cudaMalloc(&c->d_xch, c->xch_bytes) != cudaSuccess) throw Err(B2_E_OOM, "exchange buffer allocation failed");
         CK(cudaMemsetAsync(c->d_xch, 0, c->xch_bytes, c->stream));
@@ -595,6 +596,8 @@ void assemble(b2_ctx* c, const b2json::Value& plan) {
             c->pfx_att = reinterpret_cast<float*>(xb + o_pfa);
             c->pfx_f = reinterpret_cast<float*>(xb + o_pff);
             c->tp_pflag = reinterpret_cast<unsigned*>(xb + o_pfl);
+            c->tp_pepoch = reinterpret_cast<unsigned*>(xb + o_pep);
+            c->pfx_logits = reinterpret_cast<float*>(xb + o_plg);
         }
     }
     c->logits = reinterpret_cast<float*>(w + offs[i_logits]);
@@ -1115,12 +1118,12 @@ void enqueue_prefill_chunk(b2_ctx* c, int p0, int T, cudaStream_t s, const int* 
     const Mirror& mir = tp ? c->mir : nomir;
     const int d0 = c->tp_rank * (c->d / c->tp_size);
     auto sync = [&]() {
-        if (tp) CK(launch_tp_sync(c->tp_pflag, c->mir, c->tp_rank, c->tp_size, ++c->tp_pepoch, err, s));
+        if (tp) CK(launch_tp_sync(c->tp_pflag, c->mir, c->tp_rank, c->tp_size, c->tp_pepoch, err, s));
     };
     auto gemm = [&](int nm, const DevMat& A, const DevMat* A1, int epi, float* out, int ldo, const float* bias,
                     const Block* B, float* cache) {
         PfGemmParams g{};
-        g.mir = (epi == PF_RESID || epi == PF_SWIGLU) ? mir : nomir;
+        g.mir = (epi == PF_RESID || epi == PF_SWIGLU || epi == PF_STORE) ? mir : nomir;
         g.M = A.rows; g.K = A.ld; g.T = T; g.Tpad = Tpad; g.epi = epi; g.S = c->pf_S;
         g.scale[0] = A.s; g.scale[1] = A1 ? A1->s : A.s; g.bias = bias;
         g.out = out; g.ldo = ldo; g.err = err; g.pos0 = p0; g.max_seq = c->max_seq;
@@ -1202,12 +1205,12 @@ void enqueue_batch_step(b2_ctx* c, cudaStream_t s) {
     const Mirror& mir = tp ? c->mir : nomir;
     const int d0 = c->tp_rank * (c->d / c->tp_size);
     auto sync = [&]() {
-        if (tp) CK(launch_tp_sync(c->tp_pflag, c->mir, c->tp_rank, c->tp_size, ++c->tp_pepoch, err, s));
+        if (tp) CK(launch_tp_sync(c->tp_pflag, c->mir, c->tp_rank, c->tp_size, c->tp_pepoch, err, s));
     };
     auto gemm = [&](int nm, const DevMat& A, const DevMat* A1, int epi, float* out, int ldo, const float* bias,
                     const Block* B, float* cache) {
         PfGemmParams g{};
-        g.mir = (epi == PF_RESID || epi == PF_SWIGLU) ? mir : nomir;
+        g.mir = (epi == PF_RESID || epi == PF_SWIGLU || epi == PF_STORE) ? mir : nomir;
         g.M = A.rows; g.K = A.ld; g.T = Bn; g.Tpad = Tpad; g.epi = epi; g.S = c->pf_S;
         g.scale[0] = A.s; g.scale[1] = A1 ? A1->s : A.s; g.bias = bias;
         g.out = out; g.ldo = ldo; g.err = err; g.pos0 = 0; g.max_seq = c->max_seq;
@@ -1227,29 +1230,37 @@ void enqueue_batch_step(b2_ctx* c, cudaStream_t s) {
             gemm(1, B.q, nullptr, PF_Q, c->pf_q, qd, B.bias[0], &B, nullptr);
             gemm(1, B.k, nullptr, PF_K, nullptr, 0, B.bias[1], &B, c->bt_K[bi]);
             gemm(1, B.v, nullptr, PF_V, nullptr, 0, B.bias[2], &B, c->bt_V[bi]);
+            const int qall = B.H_all * B.dh;
             AttnParams a{};
-            a.q = c->pf_q; a.K = c->bt_K[bi]; a.V = c->bt_V[bi]; a.out = c->pf_att;
-            a.part = c->bt_part; a.counters = c->bt_cnt;
+            a.q = c->pf_q; a.K = c->bt_K[bi]; a.V = c->bt_V[bi]; a.out = c->pf_att + (size_t)B.head0 * B.dh;
+            a.mir = mir; a.part = c->bt_part; a.counters = c->bt_cnt;
             a.H = B.H; a.KVH = B.KVH; a.dh = B.dh; a.max_seq = c->max_seq; a.nsplit_max = c->attn_nsplit_max;
             a.st = nullptr; a.err = err; a.n_of = c->bt_pos;
             a.sq = qd; a.skv = c->bt_seq_stride; a.spart = (long long)B.H * c->attn_nsplit_max * (B.dh + 2);
-            CK(launch_batch_attn(a, Bn, s));
-            planes(c->pf_att, qd, qd, nullptr);
-            gemm(1, B.o, nullptr, PF_RESID, c->pf_x, c->d, B.bias[3], nullptr, nullptr);
+            CK(launch_batch_attn(a, Bn, qall, s));
+            sync();
+            planes(c->pf_att, qall, qall, nullptr);
+            gemm(1, B.o, nullptr, PF_RESID, c->pf_x + d0, c->d, B.bias[3], nullptr, nullptr);
+            sync();
         } else {
-            gemm(2, B.w1, &B.w3, PF_SWIGLU, c->pf_f, B.ffn_local, nullptr, nullptr, nullptr);
-            planes(c->pf_f, B.ffn_local, B.ffn_local, nullptr);
-            gemm(1, B.w2, nullptr, PF_RESID, c->pf_x, c->d, nullptr, nullptr, nullptr);
+            gemm(2, B.w1, &B.w3, PF_SWIGLU, c->pf_f + B.ffn0, B.d_ffn, nullptr, nullptr, nullptr);
+            sync();
+            planes(c->pf_f, B.d_ffn, B.d_ffn, nullptr);
+            gemm(1, B.w2, nullptr, PF_RESID, c->pf_x + d0, c->d, nullptr, nullptr, nullptr);
+            sync();
         }
     }
+    // the LM head: each rank its vocabulary rows, into every rank's logits; every
+    // rank then takes the same greedy ids from the whole rows
     planes(c->pf_x, c->d, c->d, &c->fnorm);
-    gemm(1, c->lm, nullptr, PF_STORE, c->bt_logits, c->vocab, c->lm_b, nullptr, nullptr);
+    gemm(1, c->lm, nullptr, PF_STORE, c->bt_logits + (size_t)c->tp_rank * c->lm.rows, c->vocab, c->lm_b, nullptr,
+         nullptr);
+    sync();
     CK(launch_batch_tail(c->bt_logits, c->vocab, bs, Bn, s));
 }
 
 void batch_init(b2_ctx* c, int n, int max_steps) {
     if (!c->pf_ok) throw Err(B2_E_UNSUPPORTED, "batched decode needs a plan the tensor-core path covers: " + c->pf_why);
-    if (c->tp_size > 1) throw Err(B2_E_UNSUPPORTED, "batched decode runs on one GPU");
     if (n < 1 || n > 512 || max_steps < 1) throw Err(B2_E_INVALID, "batch size 1..512 and max_steps >= 1");
     if (c->bt_base) throw Err(B2_E_INVALID, "batched state already initialised");
     prefill_workspace(c);
@@ -1264,7 +1275,7 @@ void batch_init(b2_ctx* c, int n, int max_steps) {
         }
     auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
     const size_t b_kv = al(kv * 4), b_i = al((size_t)n * 4), b_out = al((size_t)max_steps * n * 4),
-                 b_ids = al((size_t)c->max_seq * 4), b_log = al((size_t)n * c->vocab * 4),
+                 b_ids = al((size_t)c->max_seq * 4), b_log = c->tp_size > 1 ? 0 : al((size_t)n * c->vocab * 4),
                  b_part = al((size_t)n * H * c->attn_nsplit_max * (dh + 2) * 4), b_cnt = al((size_t)n * H * 4);
     const size_t total = b_kv + 2 * b_i + b_out + 256 + b_ids + b_log + b_part + b_cnt;
     if (cudaMalloc(&c->bt_base, total) != cudaSuccess) throw Err(B2_E_OOM, "batched state allocation failed");
@@ -1276,6 +1287,7 @@ void batch_init(b2_ctx* c, int n, int max_steps) {
     c->bt_nsteps = reinterpret_cast<int*>(w); w += 256;
     c->bt_ids = reinterpret_cast<int*>(w); w += b_ids;
     c->bt_logits = reinterpret_cast<float*>(w); w += b_log;
+    if (c->tp_size > 1) c->bt_logits = c->pfx_logits;   // every rank writes its rows into every copy
     c->bt_part = reinterpret_cast<float*>(w); w += b_part;
     c->bt_cnt = reinterpret_cast<unsigned*>(w);
     c->bt_K.assign(c->blocks.size(), nullptr);

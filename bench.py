@@ -357,10 +357,10 @@ def main():
     if dist:
         dist.barrier()              # no rank frees its exchange buffer while a peer may still use it
     dec.close()
-    if world == 1 and not args.no_batched and args.layers is None:
-        # the batched configuration (64 sequences x (1024 + 128)) on the same GPU
+    if not args.no_batched and args.layers is None:
+        # the batched configuration (64 sequences x (1024 + 128)) on the same GPUs
         torch.cuda.empty_cache()
-        out["batched"] = time_batched(torch, pkg, local_rank, peaks)
+        out["batched"] = time_batched(torch, pkg, local_rank, peaks, dist=dist, rank=rank, world=world)
     if dist:
         dist.barrier()
         dist.destroy_process_group()
@@ -401,23 +401,41 @@ def time_prefill(torch, dec, prompt, stream, plan, reps=3):
             "what": "b2_prefill of the prompt minus its last token (no LM head), best of 3"}
 
 
-def time_batched(torch, pkg, local_rank, peaks, layers=None):
+def time_batched(torch, pkg, local_rank, peaks, layers=None, dist=None, rank=0, world=1):
     """The batched configuration: 64 sequences of Llama-2-7B, each a 1024-token
-    random prompt then 128 greedy tokens, all on one GPU. Decode: the 127 steps
+    random prompt then 128 greedy tokens, on one GPU or tensor-parallel over the
+    world's GPUs (each rank its rows and heads, strong scaling). Decode: the 127 steps
     after the first generated token, every sequence one token per step, timed with
     CUDA events on the device (device-resident: each step feeds its greedy ids to
-    the next); value = aggregate generated tokens/s. e2e: b2_batch_generate from
-    host prompts (64 prefills + 128 steps), ids back to the host."""
+    the next), the max over ranks; value = aggregate generated tokens/s. e2e:
+    b2_batch_generate from host prompts (64 prefills + 128 steps), ids back to the
+    host."""
     name = "llama2-7b-b64"
     c = pkg.synth.CONFIGS[name]
     plan = pkg.synth.config_plan(name, n_layers=layers)
     B, P, NEW = c["batch"], c["prompt"], c["new"]
     rng = np.random.default_rng(2)
     prompts = rng.integers(0, plan["vocab"], (B, P)).astype(np.int32)
-    dec = pkg.runtime.Decoder.synthetic(plan, seed=0, device=local_rank)
+    if world > 1:
+        def exchange(handle):
+            got = [None] * world
+            dist.all_gather_object(got, handle)
+            return got
+        dec = pkg.runtime.Decoder.synthetic_tp(plan, rank, world, exchange, seed=0, device=local_rank)
+    else:
+        dec = pkg.runtime.Decoder.synthetic(plan, seed=0, device=local_rank)
     stream = torch.cuda.current_stream()
     dec.set_stream(stream.cuda_stream)
     dec.batch_init(B, max_steps=NEW)
+    if dist:
+        dist.barrier()              # every rank's caches allocated before the first exchange
+
+    def max_over_ranks(ms):
+        if dist:
+            t = torch.tensor([ms], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
     t0 = time.time()
     for z in range(B):
         dec.batch_prefill(z, prompts[z, :-1].tolist())
@@ -430,7 +448,7 @@ def time_batched(torch, pkg, local_rank, peaks, layers=None):
     dec.batch_decode_async(NEW - 1)
     e1.record(stream)
     torch.cuda.synchronize()
-    dec_ms = e0.elapsed_time(e1)
+    dec_ms = max_over_ranks(e0.elapsed_time(e1))
     rec = dec.batch_read_output(NEW)
     toks = B * (NEW - 1)
     value = toks / (dec_ms / 1000.0)
@@ -440,7 +458,7 @@ def time_batched(torch, pkg, local_rank, peaks, layers=None):
     per_step = [w + B * kv_row * (P + i + 2) for i in range(NEW - 1)]
     step_bytes = sum(per_step) / len(per_step)
     gbs = step_bytes / (dec_ms / 1000.0 / (NEW - 1)) / 1e9
-    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    hbm = float(peaks.get("hbm_gbs", 6650.0)) * world
     # e2e through b2_batch_generate (host prompts in, host ids out)
     hp = torch.from_numpy(prompts).pin_memory()
     t0 = time.time()
@@ -448,15 +466,19 @@ def time_batched(torch, pkg, local_rank, peaks, layers=None):
     out = dec.batch_generate(hp.numpy(), NEW)
     e1.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
     same = bool(out[:, 0].tolist() == first and (out.T == rec[:NEW]).all())
+    if dist:
+        dist.barrier()              # no rank frees its exchange buffer while a peer may still use it
     dec.close()
     return {"workload": f"{name}: {B} sequences x ({P} prompt + {NEW} greedy tokens), batch decode",
+            "parallelism": f"tp{world}" if world > 1 else "one GPU",
             "value": value, "unit": "tokens/s (aggregate)", "decode_steps": NEW - 1,
             "ms_per_step": dec_ms / (NEW - 1),
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
                          "bytes_per_step": step_bytes,
-                         "what": "weights once + every sequence's KV rows per step, over the step time"},
+                         "what": "weights once + every sequence's KV rows per step, over the step time"
+                                 + (f" (peak: {world} GPUs)" if world > 1 else "")},
             "prefill_s": prefill_s, "prefill_tokens_per_s": B * (P - 1) / prefill_s,
             "e2e": {"value": B * NEW / (e2e_ms / 1000.0), "unit": "tokens/s", "ms_per_generate": e2e_ms,
                     "h2d_bytes_per_step": int(prompts.nbytes), "d2h_bytes_per_step": B * NEW * 4,

@@ -124,8 +124,14 @@ int b2_set_position(b2_ctx* ctx, int pos, int32_t next_tok);
  * rows equal the one-sequence GEMV bit for bit; attention runs per sequence over
  * its own cache; the LM head covers every sequence and the greedy token of each
  * is fed to its next step. So every sequence's ids and logits are those it would
- * get decoded alone. Needs a plan the batched prefill covers (Llama family, one
- * GPU) and n_seq <= 512.
+ * get decoded alone. Needs a plan the batched prefill covers (Llama family) and
+ * n_seq <= 512. With tensor parallelism (b2_create_tp / b2_create_synthetic_tp)
+ * every rank makes the same calls with the same arguments: each runs its rows of
+ * every GEMM, its heads and its vocabulary rows, writes them into every rank's
+ * copy and waits (bounded) for the others after each exchange, so ids and logits
+ * are the one-GPU ones on every rank. A rank more than about 1 s behind the
+ * others at an exchange makes their waits time out (B2_E_DEVICE): synchronise the
+ * ranks on the host after b2_batch_init.
  *   b2_batch_init       allocate the caches and an output record of max_steps steps
  *   b2_batch_reset      every sequence back to position 0, record emptied
  *   b2_batch_prefill    prompt tokens of one sequence (no LM head), batched

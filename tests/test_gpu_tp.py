@@ -23,7 +23,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _run_ranks(tmp_path, world, name, layers, max_seq):
+def _run_ranks(tmp_path, world, name, layers, max_seq, mode=None):
     port = str(_free_port())
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     procs, outs = [], []
@@ -31,7 +31,7 @@ def _run_ranks(tmp_path, world, name, layers, max_seq):
         out = tmp_path / f"rank{r}.npz"
         outs.append(out)
         procs.append(subprocess.Popen([sys.executable, str(HERE / "tp_worker.py"), str(r), str(world), port, name,
-                                       str(layers or 0), str(max_seq or 0), str(out)],
+                                       str(layers or 0), str(max_seq or 0), str(out)] + ([mode] if mode else []),
                                       env=env, stdout=subprocess.PIPE, stderr=subprocess.STDOUT))
     logs = []
     for p in procs:
@@ -98,3 +98,27 @@ def test_tensor_parallel_from_a_packed_blob(pkg, tmp_path):
     pf = one.query("prefill_batched")
     one.close()
     _check(res, ids, logits, plan, 2, pf)
+
+
+@pytest.mark.parametrize("world,name,layers,max_seq", [
+    (2, "llama2-7b", 2, 160),
+    (2, "tinyllama-1.1b", 2, 200),
+])
+def test_tensor_parallel_batched_decode_matches_one_gpu(pkg, tmp_path, world, name, layers, max_seq):
+    """Batched decode over WORLD ranks (each its rows of every GEMM, its heads, its
+    vocabulary rows mirrored to every rank) equals the one-GPU batched decode bit for
+    bit: ids of every call and the whole logits on every rank."""
+    import torch
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    sys.path.insert(0, str(HERE))
+    from tp_worker import batched_calls
+    res = _run_ranks(tmp_path, world, name, layers, max_seq, mode="batch")
+    plan = pkg.synth.config_plan(name, n_layers=layers, max_seq=max_seq)
+    one = pkg.runtime.Decoder.synthetic(plan, seed=0)
+    ref = batched_calls(one, plan)
+    one.close()
+    for r, got in enumerate(res):
+        for k in ("ids", "rec", "gen"):
+            assert np.array_equal(got[k], ref[k]), (r, k)
+        assert np.array_equal(got["logits"].view(np.uint32), ref["logits"].view(np.uint32)), f"rank {r}"

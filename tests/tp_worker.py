@@ -1,14 +1,15 @@
 """One rank of a tensor-parallel decode, run as its own process by
 tests/test_gpu_tp.py (and usable by hand):
 
-    python tests/tp_worker.py RANK WORLD PORT CONFIG LAYERS MAX_SEQ OUT.npz
+    python tests/tp_worker.py RANK WORLD PORT CONFIG LAYERS MAX_SEQ OUT.npz [batch]
 
 Creates rank RANK of a WORLD-GPU decoder over the synthetic CONFIG model
 (LAYERS, MAX_SEQ: 0 = the config's own), or over a packed model when CONFIG is
 blob:<path>, exchanges the buffer handles through a
 gloo process group on 127.0.0.1:PORT, then makes the same calls on every rank:
 one greedy generation, then a few steps with logits. Writes ids and this rank's
-logit rows to OUT.npz.
+logit rows to OUT.npz. With `batch`: the batched decode instead (batched_calls,
+also run on one GPU by the test), its ids and whole logits.
 """
 import datetime
 import importlib
@@ -47,6 +48,13 @@ def main(argv):
         dec = pkg.runtime.Decoder.from_blob_tp(blob, rank, world, exchange, device=rank)
     else:
         dec = pkg.runtime.Decoder.synthetic_tp(plan, rank, world, exchange, seed=0, device=rank)
+    if len(argv) > 7 and argv[7] == "batch":
+        dist.barrier()                      # every rank set up before the first exchange
+        np.savez(out, **batched_calls(dec, plan, dist.barrier))
+        dist.barrier()
+        dec.close()
+        dist.destroy_process_group()
+        return 0
     prompt = [int(t) for t in np.random.default_rng(5).integers(0, plan["vocab"], 12)]
     ids = dec.generate(prompt, 20)
     dec.reset()
@@ -61,6 +69,30 @@ def main(argv):
     dec.close()
     dist.destroy_process_group()
     return 0
+
+
+def batched_calls(dec, plan, barrier=lambda: None):
+    """Four sequences of different prompt lengths: batched prefills, six steps with
+    logits, four device-resident steps, then b2_batch_generate over equal-length
+    prompts. Returns the ids and logits."""
+    B = 4
+    rng = np.random.default_rng(3)
+    lens = [int(x) for x in rng.integers(2, min(plan["max_seq"] // 2, 60), B)]
+    prompts = [rng.integers(0, plan["vocab"], n).tolist() for n in lens]
+    dec.batch_init(B, max_steps=16)
+    barrier()                               # the caches are allocated on every rank
+    for z, pr in enumerate(prompts):
+        dec.batch_prefill(z, pr[:-1])
+    toks, ids, logits = [pr[-1] for pr in prompts], [], []
+    for _ in range(6):
+        toks, lg = dec.batch_step(toks, want_logits=True)
+        ids.append(toks)
+        logits.append(lg)
+    dec.batch_decode_async(4)
+    rec = dec.batch_read_output(16)
+    dec.batch_reset()
+    gen = dec.batch_generate(rng.integers(0, plan["vocab"], (B, 20)), 8)
+    return {"ids": np.asarray(ids, np.int64), "logits": np.stack(logits), "rec": rec, "gen": gen}
 
 
 if __name__ == "__main__":

@@ -69,6 +69,28 @@ def test_token_kernel_generate_and_async_decode(pkg, oracle):
     dec.close()
 
 
+def test_token_kernel_long_context_equals_per_layer_kernels(pkg):
+    """Positions near 3000 (47 splits x 32 heads: about ten attention items per CTA,
+    so each of a CTA's attention groups takes several in turn, and a ragged last
+    split): the token kernel and the per-layer kernels give the same bits."""
+    plan = pkg.synth.config_plan("llama2-7b", n_layers=2, max_seq=3072)
+    tk, pl = _pair(pkg, plan, seed=0)
+    assert tk.query("token_kernel") == 1
+    outs = []
+    for dec in (tk, pl):
+        dec.reset()
+        dec.fill_kv_synthetic(2990, seed=4)
+        logs = []
+        tok = 17
+        for _ in range(4):
+            tok, lg = dec.step(tok, want_logits=True)
+            logs.append(lg)
+        outs.append(logs)
+        dec.close()
+    for a, b in zip(*outs):
+        assert np.array_equal(a, b)
+
+
 def test_token_kernel_full_size_llama2_7b_equals_per_layer_kernels(pkg):
     """All 32 layers at the bench's positions: the two paths give the same bits."""
     plan = pkg.synth.config_plan("llama2-7b")

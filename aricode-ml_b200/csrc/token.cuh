@@ -364,6 +364,21 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
         const int jnew = pos - j0;                      // this step's row, if in the chunk
         const float* knew = a.K + ((size_t)kvh * a.max_seq + pos) * dh;
         const float* vnew = a.V + ((size_t)kvh * a.max_seq + pos) * dh;
+        // the chunk's earlier rows, written by earlier steps, straight from memory,
+        // issued first: their latency overlaps the wait for this step's words below.
+        // Scores: warp gwarp takes keys gwarp + 8 i; lane L sums d = L, L + 32, ...
+        // (this step's row from the Q/K/V phase's words)
+        const float* Kg = a.K + ((size_t)kvh * a.max_seq + j0) * dh;
+        float kk[8][4];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int jj = gwarp + 8 * i;
+#pragma unroll
+            for (int ii = 0; ii < 4; ++ii) {
+                const int d = lane + 32 * ii;
+                kk[i][ii] = (jj < len && jj != jnew && d < dh) ? __ldcg(Kg + (size_t)jj * dh + d) : 0.0f;
+            }
+        }
         // loads that do not need the ring: q, and this step's K/V row when it falls
         // in the chunk (issued before the waits, so their latency overlaps them)
         const bool has_new = jnew >= 0 && jnew < len;
@@ -421,20 +436,6 @@ __device__ __forceinline__ bool tk_attn_consume(const AttnParams& a, int pos, in
                 kn[i] = (has_new && d < dh) ? __ldcg(knew + d) : 0.0f;
             }
             vn = (has_new && gt < dh) ? __ldcg(vnew + gt) : 0.0f;
-        }
-        // scores: warp gwarp takes keys gwarp + 8 i; lane L sums d = L, L + 32, ...
-        // (the chunk's earlier rows, written by earlier steps, straight from memory;
-        // this step's row from the Q/K/V phase's words)
-        const float* Kg = a.K + ((size_t)kvh * a.max_seq + j0) * dh;
-        float kk[8][4];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int jj = gwarp + 8 * i;
-#pragma unroll
-            for (int ii = 0; ii < 4; ++ii) {
-                const int d = lane + 32 * ii;
-                kk[i][ii] = (jj < len && jj != jnew && d < dh) ? __ldcg(Kg + (size_t)jj * dh + d) : 0.0f;
-            }
         }
         float v[8];
 #pragma unroll

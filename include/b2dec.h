@@ -117,7 +117,7 @@ int b2_generate(b2_ctx* ctx, const int32_t* prompt, int n_prompt, int max_new, i
  * step. Both only enqueue work on the context's stream. */
 int b2_set_position(b2_ctx* ctx, int pos, int32_t next_tok);
 
-/* Batched decode: n_seq independent sequences on one GPU, each with its own KV
+/* Batched decode: n_seq independent sequences, each with its own KV
  * cache (n_seq x max_seq positions), advanced one token each per step. Every
  * projection of a step is one tensor-core GEMM over the n_seq tokens (tcgen05
  * kind::i8 over the byte planes of each token's fixed-point activations), whose

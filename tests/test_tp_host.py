@@ -146,3 +146,73 @@ def test_row_split_gemv_and_argmax_equal_one_rank():
         p.join(timeout=60)
         assert p.exitcode == 0
     assert got == {0: True, 1: True}
+
+
+def _batched_split_rank(rank, world, port, q):
+    """The tensor-parallel batched prefill / batched decode exchange over T tokens:
+    each rank computes its FFN hidden columns (gate / up rows ffn0 ..), writes them
+    into every rank's copy (here an all_gather standing in for the mirrored
+    stores and the flag barrier after them), then its rows of x (down rows d0 ..,
+    residual added) and its vocabulary rows of the LM head the same way. Every
+    rank's whole x and logits must equal the one-rank computation, and the greedy
+    ids taken from the whole rows on each rank must be the one-rank ids."""
+    sys.path.insert(0, str(ROOT))
+    sys.path.insert(0, str(ROOT / "oracle"))
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import oracle as O
+    pkg = importlib.import_module("aricode-ml_b200")
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    plan = pkg.synth.config_plan("tiny-llama")
+    t = O.synth_tensors(plan, seed=0)
+    ffn = next(b for b in plan["blocks"] if b["type"] == "ffn")
+    d, dff, vocab = plan["d_model"], ffn["d_ffn"], plan["vocab"]
+    d0, f0, v0 = rank * d // world, rank * dff // world, rank * vocab // world
+    dl, fl, vl = d // world, dff // world, vocab // world
+
+    def rows(name, lo, n, x):
+        return O.gemv_i8(t[name][lo:lo + n], t[name + "_scales"][lo:lo + n], x)
+
+    def silu_mul(g, u):                   # any elementwise map, the same on both sides
+        return (g / (1.0 + np.exp(-g.astype(np.float64)))).astype(np.float32) * u
+
+    def exchange(mine, total):            # every rank's copy of the whole row
+        parts = [torch.empty(total // world) for _ in range(world)]
+        dist.all_gather(parts, torch.from_numpy(np.ascontiguousarray(mine)))
+        return torch.cat(parts).numpy()
+
+    rng = np.random.default_rng(11)
+    ok = True
+    for tok in range(5):                  # the tokens of a chunk (or the sequences of a step)
+        x = rng.standard_normal(d).astype(np.float32)
+        f = exchange(silu_mul(rows(ffn["gate"], f0, fl, x), rows(ffn["up"], f0, fl, x)), dff)
+        xn = exchange(x[d0:d0 + dl] + rows(ffn["down"], d0, dl, f), d)
+        lg = exchange(rows(plan["lm_head"]["W"], v0, vl, xn), vocab)
+        f1 = silu_mul(O.gemv_i8(t[ffn["gate"]], t[ffn["gate"] + "_scales"], x),
+                      O.gemv_i8(t[ffn["up"]], t[ffn["up"] + "_scales"], x))
+        x1 = x + O.gemv_i8(t[ffn["down"]], t[ffn["down"] + "_scales"], f1)
+        lg1 = O.gemv_i8(t[plan["lm_head"]["W"]], t[plan["lm_head"]["W"] + "_scales"], x1)
+        ok = ok and np.array_equal(f.view(np.uint32), f1.view(np.uint32))
+        ok = ok and np.array_equal(xn.view(np.uint32), x1.view(np.uint32))
+        ok = ok and np.array_equal(lg.view(np.uint32), lg1.view(np.uint32)) and O.argmax(lg) == O.argmax(lg1)
+    dist.barrier()
+    dist.destroy_process_group()
+    q.put((rank, ok))
+
+
+def test_batched_row_split_exchange_equals_one_rank():
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_batched_split_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert got == {0: True, 1: True}

@@ -158,7 +158,11 @@ def main():
         if (dest / "ref_staging").exists():
             shutil.rmtree(dest / "ref_staging")
         collect_staging(work, "cfgT", dest / "ref_staging")
-        manifest["fixtures"]["cfgT"] = {"pack_flags": cmd[3:]}
+        # the flags as run, with this checkout's and the scratch folder's paths
+        # written relative to the repository / as <work>
+        root = str(HERE.parents[1]) + "/"
+        manifest["fixtures"]["cfgT"] = {"pack_flags": [a.replace(str(td), "<work>").replace(root, "")
+                                                       for a in map(str, cmd[3:])]}
 
         # ---------------- reference decoder examples
         for ex, (i8attn, max_new) in EXAMPLES.items():
